@@ -1,0 +1,275 @@
+"""AR decode benchmark (BASELINE config 2 per GPU): YuE2-3B dims, BF16, synthetic seeded
+weights, prompt of 512 random ids, 400 sampled semantic tokens (T 1.0, top-k 50,
+top-p 0.93, reference defaults elsewhere; min_tokens = max_tokens so every run decodes
+exactly 400 tokens). One bench step = one generate_tokens call through the C ABI.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank an independent song (data
+parallel, no collective on the data path; NCCL only for the barrier and the max-reduce
+of the timings). Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT, DECODE = 512, 400
+SAMPLING = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50,
+                min_tokens=DECODE, max_tokens=DECODE)
+LAYER_BYTES = 50_331_648 * 2          # q,k,v,o,gate,up,down of one layer, BF16
+NORM_BYTES = 28 * (2 * 2048 + 2 * 128) * 2 + 2048 * 2
+HEAD_BYTES = 32769 * 2048 * 2         # semantic LM-head rows
+KV_BYTES_PER_POS = 28 * 2 * 8 * 128 * 2
+EMBED_BYTES = 2048 * 2
+
+
+def step_bytes(L: int) -> int:
+    """Algorithmic HBM bytes of one decode step at L visible positions (B = 1)."""
+    return 28 * LAYER_BYTES + NORM_BYTES + HEAD_BYTES + EMBED_BYTES + KV_BYTES_PER_POS * (L + 1)
+
+
+def load_module(name, path, pkg=None):
+    import importlib.util
+    if name in sys.modules:
+        return sys.modules[name]
+    kw = {"submodule_search_locations": [pkg]} if pkg else {}
+    spec = importlib.util.spec_from_file_location(name, path, **kw)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.proc = None
+        self.index = index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.summary = None
+        if not self.proc:
+            return
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 7]
+        if not rows:
+            return
+        sm = [float(r[0]) for r in rows if r[0].strip().replace(".", "").isdigit()]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[3:7]):
+                if v.strip() == "Active":
+                    reasons.add(name)
+        self.summary = {"sm_mhz": float(np.median(sm)) if sm else None,
+                        "sm_max_mhz": float(rows[0][1]) if rows[0][1].strip().replace(".", "").isdigit() else None,
+                        "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def ensure_weights(rank: int, world: int, barrier) -> str:
+    synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
+    d = os.environ.get("YAR_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "yar_bench_3b_seed0"))
+    marker = os.path.join(d, ".complete")
+    if rank == 0 and not os.path.exists(marker):
+        synth.write_converted(d, synth.PINNED, seed=0)
+        open(marker, "w").write("ok")
+    barrier()
+    return d
+
+
+def cpu_decode_sample(seconds_budget: float = 20.0, layers_timed: int = 2):
+    """Oracle (numpy) decode tok/s at config-2 positions on this host, bounded: a prefix
+    of `layers_timed` decoder layers plus the semantic head is run for real (512-token
+    prefill, then decode steps), and the per-token time is scaled to 28 layers."""
+    import dataclasses
+    synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
+    from oracle import ar_oracle as ora
+    dims = dataclasses.replace(synth.PINNED, layers=layers_timed)
+    specs = synth.tensor_specs(synth.PINNED)
+    keep = {n for n, _ in synth.tensor_specs(dims)}
+    tensors = {}
+    for i, (name, shape) in enumerate(specs):
+        if name not in keep:
+            continue
+        if name in ("model.embed_tokens.weight", "lm_head.weight"):
+            tensors[name] = synth.tensor_bits(shape, i, 0, 0.02, 0.0)
+        else:
+            tensors[name] = synth.tensor_bits(shape, i, 0, 0.02, 0.0)
+    model = ora.OracleAR(tensors, dims, bf16=True)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, 184704, PROMPT).tolist()
+    cache = model.new_cache(PROMPT + 64)
+    model.forward(prompt, cache)
+    t_layers, t_head, n = 0.0, 0.0, 0
+    tok = 151853
+    start = time.perf_counter()
+    while n < 64 and time.perf_counter() - start < seconds_budget:
+        t0 = time.perf_counter()
+        h = model.forward([tok], cache)
+        t1 = time.perf_counter()
+        model.project(h[-1], "semantic")
+        t2 = time.perf_counter()
+        t_layers += t1 - t0
+        t_head += t2 - t1
+        n += 1
+    per_token = (t_layers / n) * (28 / layers_timed) + t_head / n
+    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy oracle, {n} decode steps at positions {PROMPT}..{PROMPT + n}, "
+                      f"{layers_timed} of 28 layers timed and scaled to 28, semantic head, float32 BLAS "
+                      f"on {os.cpu_count()} host threads"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": "config2: YuE2-3B dims (28L, H2048, 16/8 heads, FFN 6144, vocab 184704), bs1 per GPU, "
+                          "prompt 512 random ids, 400 semantic tokens, T1.0 top-k50 top-p0.93",
+              "batch_per_gpu": 1, "prompt": PROMPT, "decode": DECODE, "phase": "semantic",
+              "parallelism": f"dp{args.gpus}", "l2": "inputs larger than L2 (2.95 GB of weights per step)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        s = cpu_decode_sample()
+        vals = [cpu_decode_sample(seconds_budget=10.0)["value"] for _ in range(max(1, args.steps))]
+        v = float(np.median(vals))
+        print(json.dumps({"impl": "reference", "metric": "AR decode tok/s", "value": v, "unit": "tok/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "dtype": "bf16 storage, f32 math", "data": "synthetic",
+                          "config": config,
+                          "cpu_baseline": {"value": v, "unit": "tok/s", "cores": s["cores"], "kind": "port",
+                                           "sample": s["sample"]},
+                          "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        barrier = lambda: (torch.cuda.synchronize(), dist.barrier(device_ids=[local]))
+
+        def maxall(v):
+            t = torch.tensor([v], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+    else:
+        barrier = lambda: torch.cuda.synchronize()
+        maxall = lambda v: v
+
+    weights = ensure_weights(rank, world, barrier)
+    yar = load_module("yue2_mlx_b200", os.path.join(ROOT, "yue2-mlx_b200", "__init__.py"),
+                      os.path.join(ROOT, "yue2-mlx_b200"))
+    model = yar.ARModel(weights, device=local)
+    session = model.session(max_rows=1, max_ctx=PROMPT + DECODE)
+    smp = yar.Sampling(**SAMPLING)
+    rng = np.random.default_rng(1000 + rank)
+    prompts = [rng.integers(0, 184704, PROMPT).astype(np.int32) for _ in range(args.warmup + args.steps)]
+
+    for i in range(args.warmup):
+        session.generate(prompts[i], smp, seed=i, phase="semantic")
+    barrier()
+    decode_ms, wall, prefill_s, tokens = 0.0, 0.0, 0.0, 0
+    with Clocks(local) as clk:
+        t_start = time.perf_counter()
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            toks, timing, _ = session.generate(prompts[args.warmup + i], smp, seed=args.warmup + i, phase="semantic")
+            wall += time.perf_counter() - t0
+            decode_ms += timing["decode_device_ms"]
+            prefill_s += timing["prefill_seconds"]
+            tokens += len(toks)
+        torch.cuda.synchronize()
+        t_total = time.perf_counter() - t_start
+    barrier()
+    decode_s = maxall(decode_ms / 1000.0)
+    wall_s = maxall(wall)
+    total_tokens = tokens * world
+    value = total_tokens / decode_s
+    e2e = total_tokens / wall_s
+    per_token_s = decode_s / (tokens)
+    avg_L = PROMPT + DECODE / 2
+    bytes_per_step = step_bytes(int(avg_L))
+    peak, peak_kind = peaks()
+    achieved = bytes_per_step / per_token_s / 1e9
+    layers = 28
+    launches_per_token = 2 + 5 * layers + 1
+    prefill_launches = 1 + 8 * layers + 1
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_decode_sample()
+        except Exception as e:  # reported, not fatal
+            cpu = {"error": str(e)}
+    if rank == 0:
+        out = {
+            "metric": "AR decode tok/s (bs1/GPU) and % of HBM roofline", "value": value, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * decode_s / args.steps, "ms_per_token": 1000 * per_token_s,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, random prompt ids)", "config": config,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
+                    "d2h_bytes_per_step": DECODE * 4 + 20 * ((DECODE + 15) // 16),
+                    "prefill_s_per_step": prefill_s / args.steps},
+            "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph of 143 kernels)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": peak_kind, "bytes_per_step": bytes_per_step, "traffic": None},
+            "gpu_launches": args.steps * (DECODE * launches_per_token + prefill_launches),
+            "clocks": clk.summary,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out))
+    session.close()
+    model.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,133 @@
+/*
+ * yue2ar.h — C ABI of the B200 (sm_100a) YuE2 AR engine (libyue2ar_cuda.so).
+ *
+ * This is the drop-in boundary for the reference's AR engine interface
+ * (native/include/lyra/ar.hpp:20-48): model load, prefill, per-step decode with the
+ * sampler, the KV cache, and the whole generate_tokens loop. Plain C types only; no
+ * exception crosses it. Every function returns a status with the reference's codes
+ * (native/include/CLyraCore/lyra.h:18-23): YAR_OK 0, YAR_FAILURE 1, YAR_INVALID_INPUT 2,
+ * YAR_CANCELLED 130. The message and the reference's error type name ("ValueError",
+ * "FileNotFoundError", "InterruptedError", "RuntimeError"; native/include/lyra/types.hpp:70-74)
+ * of the last failure on the calling thread are read with yar_last_error() and
+ * yar_last_error_type().
+ *
+ * Threading: one call at a time per session; callbacks run on the calling thread and
+ * must not re-enter the library (native/include/lyra/runtime.hpp:6-9).
+ */
+#ifndef YUE2AR_H
+#define YUE2AR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  YAR_OK = 0,
+  YAR_FAILURE = 1,
+  YAR_INVALID_INPUT = 2,
+  YAR_CANCELLED = 130
+};
+
+/* Protocol phases (native/src/sampling.cpp:8-18). YAR_PHASE_FULL projects every
+ * vocabulary row; it exists for models whose vocabulary is smaller than the protocol's
+ * codec range (the tiny parity model) and is rejected for the pinned checkpoint. */
+enum { YAR_PHASE_ABC = 0, YAR_PHASE_SEMANTIC = 1, YAR_PHASE_FULL = 2 };
+
+/* yar_model_load_ex flags. */
+enum {
+  /* Accept any self-consistent dims instead of the pinned YuE2-3B config
+   * (native/src/ar.cpp:164-179 pins them); used by the tiny parity model. */
+  YAR_LOAD_ANY_DIMS = 1u << 0
+};
+
+/* lyra::Sampling (native/include/lyra/types.hpp:78-87), same field meaning and the same
+ * validation as upstream protocol.py:31-41. */
+typedef struct yar_sampling {
+  double temperature;
+  double top_p;
+  int32_t top_k;
+  double repetition_penalty;
+  int32_t penalty_window;
+  int32_t min_tokens;
+  int32_t max_tokens;
+} yar_sampling;
+
+typedef struct yar_model yar_model;
+typedef struct yar_session yar_session;
+
+/* Cooperative cancellation (lyra::Cancelled): return nonzero to cancel. Checked before
+ * prefill, between prefill chunks and between decode chunks; never inside a kernel. */
+typedef int (*yar_cancel_fn)(void *ctx);
+/* Token callback (lyra::TokenCallback): phase id and native token id, in order. */
+typedef void (*yar_token_fn)(void *ctx, int phase, int32_t token);
+
+const char *yar_last_error(void);
+const char *yar_last_error_type(void);
+const char *yar_version(void);
+
+/* ARModel::ARModel(dir, "bf16", verify=false) — native/src/ar.cpp:133-238: reads
+ * conversion.json (schema 1, precisions.bf16 record), config.json (pinned dims),
+ * ar-bf16.safetensors (exact key/shape/dtype set), and uploads the weights to `device`
+ * in the engine's layout (fused QKV, gate/up interleaved rows). */
+int yar_model_load(const char *dir, int device, yar_model **out);
+int yar_model_load_ex(const char *dir, int device, uint32_t flags, yar_model **out);
+int yar_model_free(yar_model *model);
+/* dims[10] = {hidden, layers, heads, kv_heads, head_dim, ffn, vocab, context,
+ * device bytes of weights (low 31 bits in MiB), sm count}. */
+int yar_model_dims(const yar_model *model, int64_t *dims10);
+
+/* Device memory for up to `max_rows` decode rows (a CFG request takes two rows) with
+ * `max_ctx` positions each, in pages of `page_tokens` (256 by default when 0): the
+ * paged BF16 KV cache (KVCache, native/src/ar.cpp:98-132, one page table per row),
+ * activations, logits, sampler state and the captured decode-step graph. */
+int yar_session_create(yar_model *model, int max_rows, int max_ctx, int page_tokens,
+                       yar_session **out);
+int yar_session_free(yar_session *session);
+
+/* generate_tokens — native/src/sampling.cpp:185-288 (upstream sampling.py:57-154): prefill
+ * of `prefix` (and of `negative` when cfg_scale != 1), then up to max_tokens sampled
+ * tokens. `out_tokens` receives native ids without the end token (capacity max_tokens);
+ * `*n_out` their count, `*truncated` 1 when no end token was sampled. `timing_json`
+ * (optional) receives the reference's timing dict. Host buffers in and out. */
+int yar_generate(yar_session *session, const int32_t *prefix, int n_prefix,
+                 const yar_sampling *sampling, uint64_t seed, int phase,
+                 const int32_t *negative, int n_negative, double cfg_scale, int legacy_off,
+                 yar_cancel_fn cancel, void *cancel_ctx, yar_token_fn on_token, void *token_ctx,
+                 int32_t *out_tokens, int *n_out, int *truncated, char *timing_json,
+                 size_t timing_cap);
+
+/* Row-level API (ARModel::hidden/project + KVCache, ar.cpp:246-323), used by batched
+ * serving and by parity tests. A row owns a page table and a position. */
+int yar_row_reset(yar_session *session, int row, int capacity);
+/* Prefill `n` ids into `row` at its current position (chunks of `chunk` tokens, 1024 if
+ * 0; native/src/sampling.cpp:152-183) and project the last hidden state onto `phase`. */
+int yar_row_prefill(yar_session *session, int row, const int32_t *ids, int n, int phase,
+                    int chunk);
+/* One decode forward of the given token per listed row (the token is written at each
+ * row's position), then the phase projection. */
+int yar_rows_step(yar_session *session, const int *rows, const int32_t *tokens, int n_rows,
+                  int phase);
+/* Copy the last projected logits of `row` (BF16 bits, phase-local width) to host. */
+int yar_row_logits(yar_session *session, int row, uint16_t *out, int n);
+/* Copy `count` positions starting at `start` of layer `layer` K and V (BF16 bits,
+ * [kv_heads][count][head_dim]) of `row` to host. */
+int yar_row_kv(yar_session *session, int row, int layer, int start, int count, uint16_t *k,
+               uint16_t *v);
+int yar_row_position(yar_session *session, int row, int *pos);
+
+/* The device sampler on host logits (one step), exposed for parity tests of the filter
+ * chain and the draw contract. cond/uncond are phase-local BF16 bits of width n
+ * (uncond may be NULL). history holds native ids. Returns the local token and, when
+ * scores is non-NULL, the FP32 filtered scores (removed rows -inf). */
+int yar_sample_host(yar_model *model, const uint16_t *cond, const uint16_t *uncond, int n,
+                    double cfg_scale, const yar_sampling *sampling, const int32_t *history,
+                    int n_history, int step, int phase, uint64_t seed, int legacy_off,
+                    int32_t *token, float *scores);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* YUE2AR_H */

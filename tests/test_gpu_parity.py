@@ -1,0 +1,300 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle and the golden vectors.
+
+Tolerances (BF16 storage at the reference's rounding points, FP32 accumulation):
+* operator level, identical inputs: BF16 outputs equal up to last-bit flips where FP32
+  accumulation order differs;
+* whole tiny model (2 layers): logits max-abs <= 2e-2 and rel-L2 <= 2e-2 — twice the
+  radius between the oracle and the upstream PyTorch path on the same weights
+  (max-abs 0.0117, rel-L2 0.0077; tools/limits.py:1-79 sets bounds the same way);
+* greedy tokens equal wherever the reference's top-1/top-2 margin exceeds 0.05;
+* sampler: tokens and filtered scores bit-exact against the oracle given the same
+  logits, seed and step (the build's Philox/yexp draw contract).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import ar_oracle as ora
+from oracle import sampler_oracle as so
+from tests.conftest import load_package
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def yar():
+    return load_package()
+
+
+@pytest.fixture(scope="module")
+def tiny(yar, tiny_dir):
+    return yar.ARModel(tiny_dir, any_dims=True)
+
+
+@pytest.fixture(scope="module")
+def tiny_oracle(tiny_dir, synth):
+    return ora.OracleAR(synth.read_safetensors(os.path.join(tiny_dir, "ar-bf16.safetensors")), synth.TINY, bf16=True)
+
+
+def bits(x):
+    return ora.bits_from_bf16(x)
+
+
+def f(b):
+    return ora.bf16_from_bits(b)
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def test_tiny_prefill_and_teacher_forced_decode(yar, tiny, tiny_oracle, golden):
+    g = golden("tiny_bf16.npz")
+    prompt, forced = g["prompt"].tolist(), g["tokens"].tolist()
+    s = tiny.session(max_rows=1, max_ctx=96)
+    s.reset(0, 96)
+    s.prefill(0, prompt, phase=None)
+    gpu = [f(s.logits(0, None))]
+    for t in forced[:63]:
+        s.step([0], [t], phase=None)
+        gpu.append(f(s.logits(0, None)))
+    gpu = np.stack(gpu)
+    logits, cache = tiny_oracle.prefill(prompt, 96, None)
+    orc = [logits] + [tiny_oracle.step(t, cache, None) for t in forced[:63]]
+    orc = np.stack(orc)
+    ref = f(g["logits"])
+    for other in (orc, ref):
+        assert np.abs(gpu - other).max() <= 2e-2
+        assert rel_l2(gpu, other) <= 2e-2
+    srt = np.sort(ref, axis=1)
+    sure = srt[:, -1] - srt[:, -2] > 0.05
+    assert (np.argmax(gpu, 1)[sure] == g["tokens"][sure]).all()
+    # Layer-0 cache after prefill+decode: only the QKV accumulation order differs.
+    k, v = s.kv(0, 0, 0, 95)
+    for name, mine in (("k", f(k)), ("v", f(v))):
+        theirs = cache[name][0][:, :95]
+        assert np.mean(mine != theirs) < 0.02, name
+        assert rel_l2(mine, theirs) < 2e-3, name
+    assert s.position(0) == 95
+
+
+def test_chunked_prefill_matches_one_shot(yar, tiny):
+    rng = np.random.default_rng(3)
+    ids = rng.integers(0, 4096, 300).tolist()
+    s = tiny.session(max_rows=2, max_ctx=512)
+    s.reset(0, 512)
+    s.prefill(0, ids, phase=None)
+    s.reset(1, 512)
+    s.prefill(1, ids, phase=None, chunk=37)
+    a, b = f(s.logits(0, None)), f(s.logits(1, None))
+    assert np.abs(a - b).max() <= 2e-2 and rel_l2(a, b) <= 1e-2
+    k0, _ = s.kv(0, 1, 0, 300)
+    k1, _ = s.kv(1, 1, 0, 300)
+    assert np.mean(k0 != k1) < 0.05
+
+
+def test_decode_rows_are_independent(yar, tiny):
+    """Two rows with different histories stepped together equal each row stepped alone
+    (the reference's cross-branch visibility test, test_cuda_graph.py:62-79)."""
+    rng = np.random.default_rng(5)
+    p0, p1 = rng.integers(0, 4096, 40).tolist(), rng.integers(0, 4096, 9).tolist()
+    s = tiny.session(max_rows=2, max_ctx=128)
+    for r, p in ((0, p0), (1, p1)):
+        s.reset(r, 128)
+        s.prefill(r, p, phase=None)
+    s.step([0, 1], [7, 11], phase=None)
+    both = [s.logits(0, None), s.logits(1, None)]
+    for r, p, t in ((0, p0, 7), (1, p1, 11)):
+        s.reset(r, 128)
+        s.prefill(r, p, phase=None)
+        s.step([r], [t], phase=None)
+        np.testing.assert_array_equal(s.logits(r, None), both[r])
+
+
+def test_capacity_overflow_is_an_error(yar, tiny):
+    s = tiny.session(max_rows=1, max_ctx=64)
+    s.reset(0, 10)
+    s.prefill(0, list(range(10)), phase=None)
+    with pytest.raises(yar.YarError) as e:
+        s.step([0], [1], phase=None)
+    assert e.value.kind == "ValueError" and "capacity" in e.value.message
+    with pytest.raises(yar.YarError):
+        s.prefill(0, [1], phase=None)
+
+
+SAMPLERS = [
+    dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50, min_tokens=400, max_tokens=400),
+    dict(temperature=1.0, top_p=0.95, top_k=100, repetition_penalty=1.2, penalty_window=50, min_tokens=200, max_tokens=9000),
+    dict(temperature=0.7, top_p=0.9, top_k=30, repetition_penalty=1.005, penalty_window=100, min_tokens=32, max_tokens=4096),
+    dict(temperature=1.3, top_p=1.0, top_k=7, repetition_penalty=0.9, penalty_window=10, min_tokens=0, max_tokens=100),
+    dict(temperature=0.0, top_p=0.5, top_k=5, repetition_penalty=1.2, penalty_window=50, min_tokens=0, max_tokens=100),
+]
+
+
+def test_sampler_bit_exact_on_golden_cases(yar, tiny, golden):
+    g = golden("sampler_cases.npz")
+    cases = json.loads(str(g["cases"]))
+    for i, c in enumerate(cases):
+        logits_bits = g[f"c{i}_logits"]
+        smp = yar.Sampling(**c["sampling"])
+        for seed in (0, 12345):
+            tok, scores = tiny.sample(logits_bits, smp, c["history"], c["step"], c["phase"], seed)
+            want_tok, want_scores = so.sample(f(logits_bits), c["sampling"], c["history"], c["step"], c["phase"], seed)
+            assert tok == want_tok, (c["name"], seed)
+            if c["sampling"]["temperature"] != 0:
+                np.testing.assert_array_equal(np.isfinite(scores), np.isfinite(want_scores), err_msg=c["name"])
+                fin = np.isfinite(want_scores)
+                np.testing.assert_array_equal(scores[fin], want_scores[fin], err_msg=c["name"])
+
+
+@pytest.mark.parametrize("cfg_scale", [1.0, 1.5])
+def test_sampler_bit_exact_random(yar, tiny, cfg_scale):
+    rng = np.random.default_rng(11)
+    for trial in range(24):
+        smp = SAMPLERS[trial % len(SAMPLERS)]
+        cond = bits((rng.standard_normal(32769) * 2.5).astype(np.float32))
+        unc = bits((rng.standard_normal(32769) * 2.5).astype(np.float32)) if cfg_scale != 1 else None
+        hist = (151853 + rng.integers(0, 200, int(rng.integers(0, 150)))).tolist()
+        step = int(rng.integers(0, 500))
+        seed = int(rng.integers(0, 2**62))
+        tok, scores = tiny.sample(cond, yar.Sampling(**smp), hist, step, "semantic", seed, uncond_bits=unc,
+                                  cfg_scale=cfg_scale)
+        want, want_scores = so.sample(f(cond), smp, hist, step, "semantic", seed,
+                                      unconditional=None if unc is None else f(unc), cfg_scale=cfg_scale)
+        assert tok == want, trial
+        if smp["temperature"] != 0:
+            fin = np.isfinite(want_scores)
+            np.testing.assert_array_equal(np.isfinite(scores), fin)
+            np.testing.assert_array_equal(scores[fin], want_scores[fin])
+
+
+def replay_generation(yar, model, prefix, tokens, smp, seed, phase, negative=None, cfg_scale=1.0):
+    """Re-derive every sampled token from the GPU's own teacher-forced logits with the
+    CPU sampler; the draw contract makes this bit-exact."""
+    s = model.session(max_rows=2, max_ctx=len(prefix) + smp["max_tokens"] + 8)
+    rows = [0] if negative is None else [0, 1]
+    s.reset(0, len(prefix) + smp["max_tokens"])
+    s.prefill(0, prefix, phase=phase)
+    if negative is not None:
+        s.reset(1, len(negative) + smp["max_tokens"])
+        s.prefill(1, negative, phase=phase)
+    history = []
+    for step, tok in enumerate(tokens):
+        cond = f(s.logits(0, phase))
+        unc = f(s.logits(1, phase)) if negative is not None else None
+        want, _ = so.sample(cond, smp, history, step, phase, seed, unconditional=unc, cfg_scale=cfg_scale)
+        assert so.local_to_native(want, phase) == tok, step
+        history.append(tok)
+        if step + 1 < len(tokens):
+            s.step(rows, [tok] * len(rows), phase=phase)
+
+
+def test_generate_sampled_replays_exactly(yar, tiny):
+    rng = np.random.default_rng(21)
+    prefix = rng.integers(0, 4096, 32).tolist()
+    smp = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50, min_tokens=40,
+               max_tokens=40)
+    s = tiny.session(max_rows=2, max_ctx=128)
+    tokens, timing, truncated = s.generate(prefix, yar.Sampling(**smp), seed=77, phase=None)
+    assert len(tokens) == 40 and truncated
+    assert timing["execution"] == "cuda_graph" and timing["output_tokens"] == 40
+    again, _, _ = s.generate(prefix, yar.Sampling(**smp), seed=77, phase=None)
+    assert again == tokens
+    other, _, _ = s.generate(prefix, yar.Sampling(**smp), seed=78, phase=None)
+    assert other != tokens
+    replay_generation(yar, tiny, prefix, tokens, smp, 77, None)
+
+
+def test_generate_cfg_replays_exactly(yar, tiny):
+    rng = np.random.default_rng(22)
+    prefix, negative = rng.integers(0, 4096, 48).tolist(), rng.integers(0, 4096, 6).tolist()
+    smp = dict(temperature=1.0, top_p=0.95, top_k=100, repetition_penalty=1.2, penalty_window=50, min_tokens=24,
+               max_tokens=24)
+    s = tiny.session(max_rows=2, max_ctx=128)
+    tokens, timing, _ = s.generate(prefix, yar.Sampling(**smp), seed=5, phase=None, negative=negative, cfg_scale=1.5)
+    assert timing["cfg_branches"] == 2 and len(tokens) == 24
+    replay_generation(yar, tiny, prefix, tokens, smp, 5, None, negative=negative, cfg_scale=1.5)
+
+
+def test_generate_greedy_follows_oracle(yar, tiny, tiny_oracle, golden):
+    g = golden("tiny_bf16.npz")
+    prompt = g["prompt"].tolist()
+    smp = yar.Sampling(temperature=0.0, top_p=1.0, top_k=1, repetition_penalty=1.0, penalty_window=1, min_tokens=0,
+                       max_tokens=64)
+    tokens, _, _ = tiny.session(max_rows=1, max_ctx=96).generate(prompt, smp, seed=0, phase=None)
+    logits, cache = tiny_oracle.prefill(prompt, 96, None)
+    for i, t in enumerate(tokens):
+        srt = np.sort(logits)
+        if srt[-1] - srt[-2] <= 0.05:
+            break  # below the margin the two valid BF16 paths may pick differently
+        assert t == int(np.argmax(logits)), i
+        logits = tiny_oracle.step(t, cache, None)
+
+
+def test_generate_validation_and_cancel(yar, tiny):
+    s = tiny.session(max_rows=2, max_ctx=64)
+    smp = yar.Sampling(temperature=1.0, top_p=0.9, top_k=10, repetition_penalty=1.0, penalty_window=1, min_tokens=0,
+                       max_tokens=32)
+    with pytest.raises(yar.YarError, match="capacity"):
+        s.generate(list(range(40)), smp, seed=1, phase=None)
+    with pytest.raises(yar.YarError, match="negative prefix"):
+        s.generate([1, 2], smp, seed=1, phase=None, cfg_scale=2.0)
+    with pytest.raises(yar.YarError) as e:
+        s.generate([1, 2], smp, seed=1, phase=None, cancelled=lambda: True)
+    assert e.value.status == yar.CANCELLED
+    calls = []
+    with pytest.raises(yar.YarError) as e:
+        s.generate([1, 2], smp, seed=1, phase=None, cancelled=lambda: len(calls) > 0,
+                   on_token=lambda ph, t: calls.append(t))
+    assert e.value.status == yar.CANCELLED and 0 < len(calls) < 32
+    with pytest.raises(yar.YarError, match="seed"):
+        s.generate([1, 2], smp, seed=2**63, phase=None)
+    toks, _, _ = s.generate([1, 2], smp, seed=1, phase=None)
+    assert len(toks) == 32
+
+
+@pytest.fixture(scope="module")
+def pinned(yar, synth, tmp_path_factory):
+    d = str(tmp_path_factory.mktemp("pinned"))
+    synth.write_converted(d, synth.PINNED, seed=0)
+    return yar.ARModel(d)
+
+
+def test_pinned_3b_prefill_decode_vs_upstream(yar, pinned, golden):
+    """YuE2-3B dims, 28 layers: GPU vs the upstream PyTorch golden (same weights)."""
+    g = golden("pinned_bf16.npz")
+    prompt = g["prompt"].tolist()
+    s = pinned.session(max_rows=1, max_ctx=256)
+    s.reset(0, 256)
+    s.prefill(0, prompt[:124], phase="semantic")
+    rows = [f(s.logits(0, "semantic"))]
+    for t in prompt[124:]:
+        s.step([0], [t], phase="semantic")
+        rows.append(f(s.logits(0, "semantic")))
+    ours, ref = np.stack(rows), f(g["semantic_logits"])
+    # Radius between two valid BF16 implementations at 28 layers: max-abs 0.141, rel-L2 0.035.
+    assert np.abs(ours - ref).max() <= 0.3
+    assert rel_l2(ours, ref) <= 0.07
+    srt = np.sort(ref, axis=1)
+    sure = srt[:, -1] - srt[:, -2] > 0.05
+    assert (np.argmax(ours, 1)[sure] == np.argmax(ref, 1)[sure]).all()
+    sel = g["kv_positions"]
+    k, v = s.kv(0, 0, 0, 128)
+    for name, mine in (("k_layer0", f(k)[:, sel]), ("v_layer0", f(v)[:, sel])):
+        theirs = f(g[name])
+        assert np.mean(mine != theirs) < 0.02, name
+        assert np.abs(mine - theirs).max() <= 0.0625, name
+
+
+def test_pinned_3b_generate_semantic(yar, pinned):
+    rng = np.random.default_rng(1)
+    prefix = rng.integers(0, 184704, 512).tolist()
+    smp = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50, min_tokens=16,
+               max_tokens=16)
+    s = pinned.session(max_rows=2, max_ctx=1024)
+    tokens, timing, truncated = s.generate(prefix, yar.Sampling(**smp), seed=3, phase="semantic")
+    assert len(tokens) == 16 and truncated
+    assert all(151853 <= t < 151853 + 32768 for t in tokens)
+    replay_generation(yar, pinned, prefix, tokens, smp, 3, "semantic")

@@ -1,0 +1,222 @@
+// api.cpp — the C ABI (include/yue2ar.h). Exceptions never cross it: every entry point
+// maps lyra-style typed errors to the lyra_status codes (native/include/CLyraCore/lyra.h:18-23)
+// and keeps the message for yar_last_error() on the calling thread.
+#include <cstring>
+#include <string>
+
+#include "engine.h"
+#include "yue2ar.h"
+
+namespace yar {
+Model *load_model(const std::string &dir, int device, uint32_t flags);
+void free_model(Model *m);
+Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens);
+void free_session(Session *s);
+void row_reset(Session &s, int row, int capacity);
+void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int chunk, int (*cancel)(void *),
+                 void *cancel_ctx);
+void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int phase);
+std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::yar_sampling &smp, uint64_t seed,
+                     int phase, const int32_t *negative, int n_negative, double cfg_scale, int legacy_off,
+                     int (*cancel)(void *), void *cancel_ctx, void (*on_token)(void *, int, int32_t),
+                     void *token_ctx, int32_t *out_tokens, int *n_out, int *truncated);
+void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
+                 const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
+                 uint64_t seed, int32_t *token, float *scores);
+}  // namespace yar
+
+struct yar_model {
+  yar::Model *m;
+};
+struct yar_session {
+  yar::Session *s;
+};
+
+namespace {
+thread_local std::string g_error, g_type;
+
+int status_for(const std::string &type) {
+  if (type == "ValueError" || type == "FileNotFoundError") return YAR_INVALID_INPUT;
+  if (type == "InterruptedError") return YAR_CANCELLED;
+  return YAR_FAILURE;
+}
+
+template <typename F>
+int guarded(F &&f) {
+  try {
+    f();
+    g_error.clear();
+    g_type.clear();
+    return YAR_OK;
+  } catch (const yar::Error &e) {
+    g_error = e.what();
+    g_type = e.type;
+    return status_for(e.type);
+  } catch (const std::bad_alloc &) {
+    g_error = "host out of memory";
+    g_type = "RuntimeError";
+    return YAR_FAILURE;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    g_type = "RuntimeError";
+    return YAR_FAILURE;
+  } catch (...) {
+    g_error = "unknown error";
+    g_type = "RuntimeError";
+    return YAR_FAILURE;
+  }
+}
+
+void need(bool ok, const char *msg) {
+  if (!ok) throw yar::Error("ValueError", msg);
+}
+}  // namespace
+
+#pragma GCC visibility push(default)
+extern "C" {
+
+const char *yar_last_error(void) { return g_error.c_str(); }
+const char *yar_last_error_type(void) { return g_type.c_str(); }
+const char *yar_version(void) { return "yue2ar-cuda 0.1 sm_100a"; }
+
+int yar_model_load_ex(const char *dir, int device, uint32_t flags, yar_model **out) {
+  return guarded([&] {
+    need(dir && out, "dir and out are required");
+    *out = nullptr;
+    auto *h = new yar_model{yar::load_model(dir, device, flags)};
+    *out = h;
+  });
+}
+
+int yar_model_load(const char *dir, int device, yar_model **out) { return yar_model_load_ex(dir, device, 0, out); }
+
+int yar_model_free(yar_model *model) {
+  return guarded([&] {
+    if (!model) return;
+    yar::free_model(model->m);
+    delete model;
+  });
+}
+
+int yar_model_dims(const yar_model *model, int64_t *dims) {
+  return guarded([&] {
+    need(model && dims, "model and dims are required");
+    const auto &d = model->m->d;
+    const int64_t v[10] = {d.hidden, d.layers, d.heads, d.kv_heads, d.head_dim, d.ffn,
+                           d.vocab,  d.context, int64_t(model->m->arena_bytes >> 20), model->m->sm_count};
+    std::memcpy(dims, v, sizeof(v));
+  });
+}
+
+int yar_session_create(yar_model *model, int max_rows, int max_ctx, int page_tokens, yar_session **out) {
+  return guarded([&] {
+    need(model && out, "model and out are required");
+    *out = nullptr;
+    *out = new yar_session{yar::create_session(model->m, max_rows, max_ctx, page_tokens)};
+  });
+}
+
+int yar_session_free(yar_session *session) {
+  return guarded([&] {
+    if (!session) return;
+    yar::free_session(session->s);
+    delete session;
+  });
+}
+
+int yar_generate(yar_session *session, const int32_t *prefix, int n_prefix, const yar_sampling *sampling,
+                 uint64_t seed, int phase, const int32_t *negative, int n_negative, double cfg_scale,
+                 int legacy_off, yar_cancel_fn cancel, void *cancel_ctx, yar_token_fn on_token, void *token_ctx,
+                 int32_t *out_tokens, int *n_out, int *truncated, char *timing_json, size_t timing_cap) {
+  return guarded([&] {
+    need(session && prefix && sampling && out_tokens && n_out && truncated, "missing argument");
+    need(n_negative == 0 || negative, "negative prefix pointer missing");
+    const std::string timing = yar::generate(*session->s, prefix, n_prefix, *sampling, seed, phase, negative,
+                                             n_negative, cfg_scale, legacy_off, cancel, cancel_ctx, on_token,
+                                             token_ctx, out_tokens, n_out, truncated);
+    if (timing_json && timing_cap > 0) {
+      const size_t n = timing.size() < timing_cap - 1 ? timing.size() : timing_cap - 1;
+      std::memcpy(timing_json, timing.data(), n);
+      timing_json[n] = '\0';
+    }
+  });
+}
+
+int yar_row_reset(yar_session *session, int row, int capacity) {
+  return guarded([&] {
+    need(session, "session is required");
+    yar::row_reset(*session->s, row, capacity);
+  });
+}
+
+int yar_row_prefill(yar_session *session, int row, const int32_t *ids, int n, int phase, int chunk) {
+  return guarded([&] {
+    need(session && ids, "session and ids are required");
+    yar::row_prefill(*session->s, row, ids, n, phase, chunk, nullptr, nullptr);
+  });
+}
+
+int yar_rows_step(yar_session *session, const int *rows, const int32_t *tokens, int n_rows, int phase) {
+  return guarded([&] {
+    need(session && rows && tokens, "session, rows and tokens are required");
+    yar::rows_step(*session->s, rows, tokens, n_rows, phase);
+  });
+}
+
+int yar_row_logits(yar_session *session, int row, uint16_t *out, int n) {
+  return guarded([&] {
+    need(session && out, "session and out are required");
+    auto &s = *session->s;
+    need(row >= 0 && row < s.max_rows && n >= 0 && n <= s.logit_stride, "row or width outside the session");
+    YAR_CUDA(cudaSetDevice(s.m->device));
+    YAR_CUDA(cudaStreamSynchronize(s.stream));
+    YAR_CUDA(cudaMemcpy(out, s.logits + size_t(row) * s.logit_stride, size_t(n) * 2, cudaMemcpyDeviceToHost));
+  });
+}
+
+int yar_row_kv(yar_session *session, int row, int layer, int start, int count, uint16_t *k, uint16_t *v) {
+  return guarded([&] {
+    need(session && k && v, "session, k and v are required");
+    auto &s = *session->s;
+    const auto &d = s.m->d;
+    need(row >= 0 && row < s.max_rows && layer >= 0 && layer < d.layers, "row or layer outside the session");
+    need(start >= 0 && count >= 0 && start + count <= s.pos[row], "positions outside the row's cache");
+    YAR_CUDA(cudaSetDevice(s.m->device));
+    YAR_CUDA(cudaStreamSynchronize(s.stream));
+    std::vector<int> table(s.pages_per_row);
+    YAR_CUDA(cudaMemcpy(table.data(), s.d_page_table + size_t(row) * s.pages_per_row,
+                        table.size() * sizeof(int), cudaMemcpyDeviceToHost));
+    for (int kv = 0; kv < 2; ++kv)
+      for (int h = 0; h < d.kv_heads; ++h)
+        for (int i = 0; i < count; ++i) {
+          const int pos = start + i, page = table[pos / s.page_tokens], slot = pos % s.page_tokens;
+          const size_t blk = (size_t(layer) * s.num_pages + page) * 2 + kv;
+          const yar::bf16 *src = s.kv + blk * s.kv_page_elems + (size_t(h) * s.page_tokens + slot) * d.head_dim;
+          uint16_t *dst = (kv ? v : k) + (size_t(h) * count + i) * d.head_dim;
+          YAR_CUDA(cudaMemcpy(dst, src, size_t(d.head_dim) * 2, cudaMemcpyDeviceToHost));
+        }
+  });
+}
+
+int yar_row_position(yar_session *session, int row, int *pos) {
+  return guarded([&] {
+    need(session && pos, "session and pos are required");
+    need(row >= 0 && row < session->s->max_rows, "row outside the session");
+    *pos = session->s->pos[row];
+  });
+}
+
+int yar_sample_host(yar_model *model, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
+                    const yar_sampling *sampling, const int32_t *history, int n_history, int step, int phase,
+                    uint64_t seed, int legacy_off, int32_t *token, float *scores) {
+  return guarded([&] {
+    need(model && cond && sampling && token, "missing argument");
+    need(n_history == 0 || history, "history pointer missing");
+    need(!legacy_off, "legacy_off (BF16 historical sampling) is not implemented");
+    yar::sample_host(*model->m, cond, uncond, n, cfg_scale, *sampling, history, n_history, step, phase, seed,
+                     token, scores);
+  });
+}
+
+}  // extern "C"
+#pragma GCC visibility pop

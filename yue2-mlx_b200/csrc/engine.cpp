@@ -1,0 +1,497 @@
+// engine.cpp — sessions (paged KV cache, activations, sampler state), chunked prefill,
+// the decode step (captured once as a CUDA graph and replayed per token) and the
+// generate_tokens loop (native/src/sampling.cpp:185-288; upstream sampling.py:57-154).
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <sstream>
+
+#include "engine.h"
+#include "exact_math.cuh"
+#include "nlohmann/json.hpp"
+#include "yue2ar.h"
+
+namespace yar {
+
+void launch_sampler_ex(RequestState *req, const bf16 *logits, int logit_stride, float *scores, int *token,
+                       int *active, int32_t *out_tokens, int out_cap, int write_scores, int32_t *picked,
+                       int n_requests, cudaStream_t st);
+
+static double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+template <typename T>
+static T *dmalloc(size_t n) {
+  T *p = nullptr;
+  YAR_CUDA(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+  return p;
+}
+
+Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
+  if (max_rows < 1 || max_rows > 256) throw Error("ValueError", "max_rows must be in [1, 256]");
+  if (max_ctx < 1 || max_ctx > m->d.context)
+    throw Error("ValueError", "KV cache capacity must be in [1, " + std::to_string(m->d.context) + "]");
+  if (page_tokens == 0) page_tokens = 256;
+  if (page_tokens < 16 || page_tokens > 4096 || (page_tokens & (page_tokens - 1)))
+    throw Error("ValueError", "page_tokens must be a power of two in [16, 4096]");
+  YAR_CUDA(cudaSetDevice(m->device));
+  auto *s = new Session();
+  try {
+    const Dims &d = m->d;
+    s->m = m;
+    s->max_rows = max_rows;
+    s->max_ctx = max_ctx;
+    s->page_tokens = page_tokens;
+    s->pages_per_row = (max_ctx + page_tokens - 1) / page_tokens;
+    s->num_pages = s->pages_per_row * max_rows;
+    s->kv_page_elems = size_t(d.kv_heads) * page_tokens * d.head_dim;
+    YAR_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    s->kv = dmalloc<bf16>(size_t(d.layers) * s->num_pages * 2 * s->kv_page_elems);
+    s->row_pages.assign(max_rows, {});
+    for (int p = s->num_pages - 1; p >= 0; --p) s->free_pages.push_back(p);
+    s->d_page_table = dmalloc<int>(size_t(max_rows) * s->pages_per_row);
+    YAR_CUDA(cudaMemset(s->d_page_table, 0, size_t(max_rows) * s->pages_per_row * sizeof(int)));
+    s->d_pos = dmalloc<int>(max_rows);
+    s->d_cur_pos = dmalloc<int>(max_rows);
+    s->d_capacity = dmalloc<int>(max_rows);
+    s->d_token = dmalloc<int>(max_rows);
+    s->d_active = dmalloc<int>(max_rows);
+    s->d_error = dmalloc<int>(1);
+    for (int *p : {s->d_pos, s->d_cur_pos, s->d_capacity, s->d_token, s->d_active})
+      YAR_CUDA(cudaMemset(p, 0, max_rows * sizeof(int)));
+    YAR_CUDA(cudaMemset(s->d_error, 0, sizeof(int)));
+    s->capacity.assign(max_rows, 0);
+    s->pos.assign(max_rows, 0);
+    s->x = dmalloc<bf16>(size_t(max_rows) * d.hidden);
+    s->qkv = dmalloc<bf16>(size_t(max_rows) * d.qkv_rows());
+    s->attn = dmalloc<bf16>(size_t(max_rows) * d.qdim());
+    s->mlp = dmalloc<bf16>(size_t(max_rows) * d.ffn);
+    int widest = d.vocab;
+    if (d.vocab == 184704) widest = std::max(phase_rows(d, kPhaseAbc).width(), phase_rows(d, kPhaseSemantic).width());
+    s->logit_stride = (widest + 7) & ~7;
+    s->logits = dmalloc<bf16>(size_t(max_rows) * s->logit_stride);
+    YAR_CUDA(cudaMemset(s->logits, 0, size_t(max_rows) * s->logit_stride * sizeof(bf16)));
+    s->max_splits = 32;
+    s->attn_part = dmalloc<float>(size_t(max_rows) * d.heads * s->max_splits * (d.head_dim + 2));
+    s->attn_count = dmalloc<int>(size_t(max_rows) * d.kv_heads);
+    YAR_CUDA(cudaMemset(s->attn_count, 0, size_t(max_rows) * d.kv_heads * sizeof(int)));
+    const int T = s->prefill_chunk;
+    s->px = dmalloc<bf16>(size_t(T) * d.hidden);
+    s->ph = dmalloc<bf16>(size_t(T) * d.hidden);
+    s->pqkv = dmalloc<bf16>(size_t(T) * d.qkv_rows());
+    s->pq = dmalloc<bf16>(size_t(T) * d.qdim());
+    s->pattn = dmalloc<bf16>(size_t(T) * d.qdim());
+    s->pmlp = dmalloc<bf16>(size_t(T) * d.ffn);
+    s->pids = dmalloc<int>(T);
+    s->max_requests = max_rows;
+    s->d_req = dmalloc<RequestState>(max_rows);
+    YAR_CUDA(cudaMemset(s->d_req, 0, max_rows * sizeof(RequestState)));
+    s->out_cap = max_ctx;
+    s->d_out_tokens = dmalloc<int32_t>(size_t(max_rows) * s->out_cap);
+    s->d_scores = dmalloc<float>(size_t(max_rows) * s->logit_stride);
+    YAR_CUDA(cudaMallocHost(&s->h_pinned, 1 << 20));
+    YAR_CUDA(cudaStreamSynchronize(s->stream));
+  } catch (...) {
+    delete s;
+    throw;
+  }
+  return s;
+}
+
+void free_session(Session *s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  cudaStreamSynchronize(s->stream);
+  for (auto &g : s->graphs) cudaGraphExecDestroy(g.exec);
+  for (void *p : std::initializer_list<void *>{s->kv, s->d_page_table, s->d_pos, s->d_cur_pos, s->d_capacity,
+                                               s->d_token, s->d_active, s->d_error, s->x, s->qkv, s->attn,
+                                               s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
+                                               s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
+                                               s->d_out_tokens, s->d_scores})
+    if (p) cudaFree(p);
+  if (s->h_pinned) cudaFreeHost(s->h_pinned);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+}
+
+static void check_row(const Session &s, int row) {
+  if (row < 0 || row >= s.max_rows) throw Error("ValueError", "row outside the session");
+}
+
+void row_reset(Session &s, int row, int capacity) {
+  check_row(s, row);
+  if (capacity < 1 || capacity > s.max_ctx)
+    throw Error("ValueError", "KV cache capacity must be in [1, " + std::to_string(s.max_ctx) + "]");
+  YAR_CUDA(cudaStreamSynchronize(s.stream));
+  for (int p : s.row_pages[row]) s.free_pages.push_back(p);
+  s.row_pages[row].clear();
+  const int need = (capacity + s.page_tokens - 1) / s.page_tokens;
+  if (int(s.free_pages.size()) < need) throw Error("ValueError", "KV page pool exhausted; generation was not shortened");
+  std::vector<int> table(s.pages_per_row, 0);
+  for (int i = 0; i < need; ++i) {
+    table[i] = s.free_pages.back();
+    s.row_pages[row].push_back(table[i]);
+    s.free_pages.pop_back();
+  }
+  YAR_CUDA(cudaMemcpyAsync(s.d_page_table + size_t(row) * s.pages_per_row, table.data(),
+                           table.size() * sizeof(int), cudaMemcpyHostToDevice, s.stream));
+  const int zero = 0;
+  YAR_CUDA(cudaMemcpyAsync(s.d_pos + row, &zero, sizeof(int), cudaMemcpyHostToDevice, s.stream));
+  YAR_CUDA(cudaMemcpyAsync(s.d_capacity + row, &capacity, sizeof(int), cudaMemcpyHostToDevice, s.stream));
+  YAR_CUDA(cudaMemcpyAsync(s.d_active + row, &zero, sizeof(int), cudaMemcpyHostToDevice, s.stream));
+  YAR_CUDA(cudaStreamSynchronize(s.stream));
+  s.capacity[row] = capacity;
+  s.pos[row] = 0;
+}
+
+// LM head over the phase rows for `n_rows` input rows (norm fused), into logits rows.
+static void project(const Model &m, Session &s, const bf16 *in, int in_stride, int n_rows, int phase,
+                    bf16 *out) {
+  const PhaseRows pr = phase_rows(m.d, phase);
+  launch_gemv(m.lm_head + size_t(pr.row0) * m.d.hidden, pr.n_main, m.d.hidden, in, in_stride, m.final_norm,
+              m.d.eps, out, s.logit_stride, kEpiStore, n_rows, nullptr, m.sm_count, s.stream);
+  if (pr.extra >= 0)
+    launch_gemv(m.lm_head + size_t(pr.extra) * m.d.hidden, 1, m.d.hidden, in, in_stride, m.final_norm, m.d.eps,
+                out + pr.n_main, s.logit_stride, kEpiStore, n_rows, nullptr, m.sm_count, s.stream);
+}
+
+void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int chunk,
+                 int (*cancel)(void *), void *cancel_ctx) {
+  check_row(s, row);
+  const Model &m = *s.m;
+  const Dims &d = m.d;
+  if (n < 1) throw Error("ValueError", "AR prefix must contain at least one token");
+  for (int i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= d.vocab)
+      throw Error("ValueError", "Token IDs must be in [0, " + std::to_string(d.vocab) + ")");
+  phase_rows(d, phase);
+  if (chunk <= 0) chunk = 1024;
+  chunk = std::min(chunk, s.prefill_chunk);
+  const int start0 = s.pos[row];
+  if (start0 + n > s.capacity[row]) throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
+  cudaStream_t st = s.stream;
+  const int H = d.hidden, QKV = d.qkv_rows();
+  for (int c0 = 0; c0 < n; c0 += chunk) {
+    if (cancel && cancel(cancel_ctx)) throw Error("InterruptedError", "Cancelled during prefill");
+    const int T = std::min(chunk, n - c0), start = start0 + c0;
+    YAR_CUDA(cudaMemcpyAsync(s.pids, ids + c0, T * sizeof(int), cudaMemcpyHostToDevice, st));
+    launch_embed_tokens(m.embed, s.pids, T, H, s.px, st);
+    for (int l = 0; l < d.layers; ++l) {
+      const LayerWeights &w = m.layers[l];
+      launch_rmsnorm_rows(s.px, w.ln1, T, H, d.eps, s.ph, st);
+      launch_gemm(s.ph, T, H, w.qkv, QKV, s.pqkv, QKV, kEpiStore, st);
+      launch_qkv_post_prefill(m, s, l, row, start, T, st);
+      launch_attn_prefill(m, s, l, row, start, T, st);
+      launch_gemm(s.pattn, T, d.qdim(), w.o, H, s.px, H, kEpiResidual, st);
+      launch_rmsnorm_rows(s.px, w.ln2, T, H, d.eps, s.ph, st);
+      launch_gemm(s.ph, T, H, w.gu, 2 * d.ffn, s.pmlp, d.ffn, kEpiSwiGLU, st);
+      launch_gemm(s.pmlp, T, d.ffn, w.down, H, s.px, H, kEpiResidual, st);
+    }
+    if (c0 + T == n)
+      project(m, s, s.px + size_t(T - 1) * H, H, 1, phase, s.logits + size_t(row) * s.logit_stride);
+    YAR_CUDA(cudaStreamSynchronize(st));
+  }
+  s.pos[row] = start0 + n;
+  YAR_CUDA(cudaMemcpyAsync(s.d_pos + row, &s.pos[row], sizeof(int), cudaMemcpyHostToDevice, st));
+  YAR_CUDA(cudaStreamSynchronize(st));
+}
+
+// One decode forward of rows [0, n_rows): embed -> 28 x (QKV, attention, O, gate/up, down)
+// -> LM head. Inactive rows are skipped by the embed/attention kernels.
+static void decode_forward(Session &s, int n_rows, int phase) {
+  const Model &m = *s.m;
+  const Dims &d = m.d;
+  cudaStream_t st = s.stream;
+  launch_embed_rows(m, s, n_rows, st);
+  for (int l = 0; l < d.layers; ++l) {
+    const LayerWeights &w = m.layers[l];
+    launch_gemv(w.qkv, d.qkv_rows(), d.hidden, s.x, d.hidden, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows,
+                nullptr, m.sm_count, st);
+    launch_attn_decode(m, s, l, n_rows, st);
+    launch_gemv(w.o, d.hidden, d.qdim(), s.attn, d.qdim(), nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows,
+                nullptr, m.sm_count, st);
+    launch_gemv(w.gu, 2 * d.ffn, d.hidden, s.x, d.hidden, w.ln2, d.eps, s.mlp, d.ffn, kEpiSwiGLU, n_rows, nullptr,
+                m.sm_count, st);
+    launch_gemv(w.down, d.hidden, d.ffn, s.mlp, d.ffn, nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows, nullptr,
+                m.sm_count, st);
+  }
+  project(m, s, s.x, d.hidden, n_rows, phase, s.logits);
+}
+
+void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int phase) {
+  if (n < 1) throw Error("ValueError", "rows_step needs at least one row");
+  int hi = 0;
+  for (int i = 0; i < n; ++i) {
+    check_row(s, rows[i]);
+    hi = std::max(hi, rows[i] + 1);
+    if (tokens[i] < 0 || tokens[i] >= s.m->d.vocab) throw Error("ValueError", "Token is outside the model vocabulary");
+    if (s.pos[rows[i]] + 1 > s.capacity[rows[i]])
+      throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
+  }
+  phase_rows(s.m->d, phase);
+  std::vector<int> active(hi, 0), tok(hi, 0);
+  for (int i = 0; i < n; ++i) {
+    active[rows[i]] = 1;
+    tok[rows[i]] = tokens[i];
+  }
+  cudaStream_t st = s.stream;
+  YAR_CUDA(cudaMemcpyAsync(s.d_active, active.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
+  YAR_CUDA(cudaMemcpyAsync(s.d_token, tok.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
+  decode_forward(s, hi, phase);
+  YAR_CUDA(cudaStreamSynchronize(st));
+  int err = 0;
+  YAR_CUDA(cudaMemcpy(&err, s.d_error, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) throw Error("RuntimeError", "device error flags " + std::to_string(err));
+  for (int i = 0; i < n; ++i) s.pos[rows[i]] += 1;
+}
+
+// The per-token step (sampler, then the forward of the sampled token), captured once
+// per (rows, requests, phase) and replayed.
+static cudaGraphExec_t step_graph(Session &s, int n_rows, int n_requests, int phase) {
+  for (auto &g : s.graphs)
+    if (g.rows == n_rows && g.requests == n_requests && g.phase == phase) return g.exec;
+  cudaStream_t st = s.stream;
+  YAR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  cudaGraph_t graph;
+  try {
+    launch_sampler(*s.m, s, n_requests, st);
+    decode_forward(s, n_rows, phase);
+  } catch (...) {
+    cudaStreamEndCapture(st, &graph);
+    throw;
+  }
+  YAR_CUDA(cudaStreamEndCapture(st, &graph));
+  cudaGraphExec_t exec;
+  YAR_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+  YAR_CUDA(cudaGraphDestroy(graph));
+  s.graphs.push_back({n_rows, n_requests, phase, exec});
+  return exec;
+}
+
+static RequestState make_request(const Model &m, const Session &s, int row_c, int row_u, int phase,
+                                 const ::yar_sampling &smp, double cfg_scale, uint64_t seed, uint32_t stream) {
+  RequestState r;
+  std::memset(&r, 0, sizeof(r));
+  r.row_c = row_c;
+  r.row_u = row_u;
+  r.phase = phase;
+  r.width = phase_rows(m.d, phase).width();
+  r.end_local = phase == kPhaseAbc ? kEOD : phase == kPhaseSemantic ? 0 : -1;
+  r.temperature = float(smp.temperature);
+  r.top_p = float(smp.top_p);
+  r.cfg_scale = float(cfg_scale);
+  r.top_k = smp.top_k;
+  r.window = smp.penalty_window;
+  r.min_tokens = smp.min_tokens;
+  r.max_tokens = smp.max_tokens;
+  r.penalty_on = smp.repetition_penalty != 1.0;
+  for (int i = 0; i <= kMaxPenaltyWindow; ++i)
+    r.alpha[i] = float(std::pow(double(float(smp.repetition_penalty)), double(i)));
+  r.seed_lo = uint32_t(seed);
+  r.seed_hi = uint32_t(seed >> 32);
+  r.stream = stream;
+  (void)s;
+  return r;
+}
+
+void validate_sampling(const ::yar_sampling &s) {
+  auto finite = [](double v) { return std::isfinite(v); };
+  if (!finite(s.temperature) || !finite(s.top_p) || !finite(s.repetition_penalty))
+    throw Error("ValueError", "Sampling numbers must be finite");
+  if (!(s.temperature >= 0 && s.temperature <= 5) || !(s.top_p > 0 && s.top_p <= 1) || s.top_k < 1)
+    throw Error("ValueError", "Invalid sampling temperature/top_p/top_k");
+  if (s.repetition_penalty <= 0 || s.penalty_window < 1 || s.penalty_window > 100)
+    throw Error("ValueError", "Invalid repetition penalty/window");
+  if (!(0 <= s.min_tokens && s.min_tokens <= s.max_tokens) || s.max_tokens < 1)
+    throw Error("ValueError", "Require 0 <= min_tokens <= max_tokens");
+  if (s.temperature > 0 && s.top_k > kCandCap)
+    throw Error("ValueError", "top_k above 2048 is not supported by the device sampler");
+}
+
+std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::yar_sampling &smp, uint64_t seed,
+                     int phase, const int32_t *negative, int n_negative, double cfg_scale, int legacy_off,
+                     int (*cancel)(void *), void *cancel_ctx, void (*on_token)(void *, int, int32_t),
+                     void *token_ctx, int32_t *out_tokens, int *n_out, int *truncated) {
+  const Model &m = *s.m;
+  phase_rows(m.d, phase);
+  validate_sampling(smp);
+  if (legacy_off) throw Error("ValueError", "legacy_off (BF16 historical sampling) is not implemented");
+  if (seed >= (uint64_t(1) << 63)) throw Error("ValueError", "seed must be an integer in [0, 2**63)");
+  if (n_prefix < 1) throw Error("ValueError", "AR prefix must contain at least one token");
+  if (size_t(n_prefix) + size_t(smp.max_tokens) > size_t(m.d.context))
+    throw Error("ValueError", "Prefix + requested generation budget exceeds 24576; no implicit truncation");
+  const bool cfg = cfg_scale != 1.0;
+  if (cfg && n_negative < 1) throw Error("ValueError", "CFG requires a negative prefix");
+  if (n_negative > 0 && size_t(n_negative) + size_t(smp.max_tokens) > size_t(m.d.context))
+    throw Error("ValueError", "Negative prefix + generation budget exceeds context");
+  const int rows = cfg ? 2 : 1;
+  if (rows > s.max_rows) throw Error("ValueError", "CFG needs a session with at least two rows");
+  if (n_prefix + smp.max_tokens > s.max_ctx || (cfg && n_negative + smp.max_tokens > s.max_ctx))
+    throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
+  if (smp.max_tokens > s.out_cap) throw Error("ValueError", "max_tokens exceeds the session output capacity");
+  if (cancel && cancel(cancel_ctx)) throw Error("InterruptedError", "Cancelled before prefill");
+
+  YAR_CUDA(cudaSetDevice(m.device));
+  YAR_CUDA(cudaStreamSynchronize(s.stream));
+  const double t0 = now_s();
+  row_reset(s, 0, n_prefix + smp.max_tokens);
+  row_prefill(s, 0, prefix, n_prefix, phase, 0, cancel, cancel_ctx);
+  if (cfg) {
+    row_reset(s, 1, n_negative + smp.max_tokens);
+    row_prefill(s, 1, negative, n_negative, phase, 0, cancel, cancel_ctx);
+  }
+  const double prefill_seconds = now_s() - t0;
+
+  const RequestState req = make_request(m, s, 0, cfg ? 1 : -1, phase, smp, cfg_scale, seed, 0);
+  cudaStream_t st = s.stream;
+  YAR_CUDA(cudaMemcpyAsync(s.d_req, &req, sizeof(req), cudaMemcpyHostToDevice, st));
+  std::vector<int> act(rows, 1);
+  YAR_CUDA(cudaMemcpyAsync(s.d_active, act.data(), rows * sizeof(int), cudaMemcpyHostToDevice, st));
+  YAR_CUDA(cudaMemsetAsync(s.d_error, 0, sizeof(int), st));
+  YAR_CUDA(cudaStreamSynchronize(st));
+  cudaGraphExec_t exec = step_graph(s, rows, 1, phase);
+
+  // Replay in chunks; after each chunk read the request's progress (done, tokens).
+  const int kChunk = 16;
+  int steps = 0, reported = 0;
+  bool done = false, eos = false;
+  double ttft = -1;
+  std::vector<int32_t> toks;
+  struct Progress {
+    int done, n_out, error, step;
+  };
+  auto *hp = reinterpret_cast<int *>(s.h_pinned);
+  // Device time of the decode loop (graph replays only), on the engine's stream.
+  cudaEvent_t ev0, ev1;
+  YAR_CUDA(cudaEventCreate(&ev0));
+  YAR_CUDA(cudaEventCreate(&ev1));
+  YAR_CUDA(cudaEventRecord(ev0, st));
+  float decode_ms = 0.f;
+  while (steps < smp.max_tokens && !done) {
+    if (cancel && cancel(cancel_ctx)) throw Error("InterruptedError", std::string("Cancelled during ") +
+                                                                          (phase == kPhaseAbc ? "abc" : "semantic"));
+    const int k = std::min(kChunk, smp.max_tokens - steps);
+    YAR_CUDA(cudaEventRecord(ev0, st));
+    for (int i = 0; i < k; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
+    YAR_CUDA(cudaEventRecord(ev1, st));
+    steps += k;
+    YAR_CUDA(cudaMemcpyAsync(hp, &s.d_req[0].step, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
+    YAR_CUDA(cudaMemcpyAsync(hp + 4, s.d_error, sizeof(int), cudaMemcpyDeviceToHost, st));
+    YAR_CUDA(cudaStreamSynchronize(st));
+    {
+      float ms = 0.f;
+      YAR_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+      decode_ms += ms;
+    }
+    if (ttft < 0) ttft = now_s() - t0;
+    const int dstep = hp[0], ddone = hp[1], dn = hp[2], derr = hp[3];
+    if (derr || hp[4]) throw Error("RuntimeError", "device sampler/forward error " + std::to_string(derr) + "/" +
+                                                       std::to_string(hp[4]));
+    if (dn > reported) {
+      toks.resize(dn);
+      YAR_CUDA(cudaMemcpy(toks.data() + reported, s.d_out_tokens + reported, (dn - reported) * sizeof(int32_t),
+                          cudaMemcpyDeviceToHost));
+      if (on_token)
+        for (int i = reported; i < dn; ++i) on_token(token_ctx, phase, toks[i]);
+      reported = dn;
+    }
+    if (ddone) {
+      done = true;
+      eos = dstep > dn;  // the end token was sampled (it is not stored)
+    }
+    if (dstep >= smp.max_tokens) done = true;
+  }
+  if (eos && on_token) {
+    const int end_native = phase == kPhaseAbc ? kAbcEnd : phase == kPhaseSemantic ? kMusicEnd : -1;
+    on_token(token_ctx, phase, end_native);
+  }
+  YAR_CUDA(cudaStreamSynchronize(st));
+  YAR_CUDA(cudaEventDestroy(ev0));
+  YAR_CUDA(cudaEventDestroy(ev1));
+  const double seconds = now_s() - t0;
+  std::copy(toks.begin(), toks.end(), out_tokens);
+  *n_out = int(toks.size());
+  *truncated = eos ? 0 : 1;
+  // Release the request's pages (caches are request-local, sampling.cpp:208-210).
+  for (int r = 0; r < rows; ++r) {
+    for (int p : s.row_pages[r]) s.free_pages.push_back(p);
+    s.row_pages[r].clear();
+    s.capacity[r] = 0;
+  }
+  nlohmann::json timing = {{"seconds", seconds},
+                           {"prefill_seconds", prefill_seconds},
+                           {"ttft_seconds", ttft},
+                           {"output_tokens", int(toks.size()) + int(eos)},
+                           {"content_tokens", int(toks.size())},
+                           {"output_tps", (toks.size() + int(eos)) / seconds},
+                           {"prefix_tokens", n_prefix},
+                           {"cfg_branches", cfg ? 2 : 1},
+                           {"execution", "cuda_graph"},
+                           {"attention", "split_kv"},
+                           {"backend", "cuda-sm100a"},
+                           {"decode_steps", steps},
+                           {"decode_device_ms", decode_ms}};
+  return timing.dump();
+}
+
+// Sampler on host logits (parity tests of the filter chain and the draw).
+void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
+                 const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
+                 uint64_t seed, int32_t *token, float *scores) {
+  validate_sampling(smp);
+  const int expected = phase == kPhaseAbc ? kEOD + 1 : phase == kPhaseSemantic ? kCodecSize + 1 : n;
+  if (phase != kPhaseAbc && phase != kPhaseSemantic && phase != kPhaseFull)
+    throw Error("ValueError", "phase must be 'abc' or 'semantic'");
+  if (n < 1 || n != expected) throw Error("ValueError", "Incorrect projected phase vocabulary size");
+  YAR_CUDA(cudaSetDevice(m.device));
+  const int stride = (n + 7) & ~7;
+  bf16 *logits = dmalloc<bf16>(size_t(2) * stride);
+  float *sc = dmalloc<float>(stride);
+  RequestState *req = dmalloc<RequestState>(1);
+  int *tok = dmalloc<int>(2), *act = dmalloc<int>(2);
+  int32_t *picked = dmalloc<int32_t>(1);
+  try {
+    YAR_CUDA(cudaMemcpy(logits, cond, size_t(n) * 2, cudaMemcpyHostToDevice));
+    const bool cfg = uncond && cfg_scale != 1.0;
+    if (cfg) YAR_CUDA(cudaMemcpy(logits + stride, uncond, size_t(n) * 2, cudaMemcpyHostToDevice));
+    RequestState r;
+    std::memset(&r, 0, sizeof(r));
+    r.row_c = 0;
+    r.row_u = cfg ? 1 : -1;
+    r.phase = phase;
+    r.width = n;
+    r.end_local = phase == kPhaseAbc ? kEOD : phase == kPhaseSemantic ? 0 : -1;
+    r.temperature = float(smp.temperature);
+    r.top_p = float(smp.top_p);
+    r.cfg_scale = float(cfg_scale);
+    r.top_k = smp.top_k;
+    r.window = smp.penalty_window;
+    r.min_tokens = smp.min_tokens;
+    r.max_tokens = step + 1;
+    r.penalty_on = smp.repetition_penalty != 1.0;
+    for (int i = 0; i <= kMaxPenaltyWindow; ++i)
+      r.alpha[i] = float(std::pow(double(float(smp.repetition_penalty)), double(i)));
+    r.seed_lo = uint32_t(seed);
+    r.seed_hi = uint32_t(seed >> 32);
+    r.step = step;
+    const int keep = std::min(n_history, kHistCap);
+    r.n_out = n_history;
+    for (int i = n_history - keep; i < n_history; ++i) r.hist[i % kHistCap] = history[i];
+    YAR_CUDA(cudaMemcpy(req, &r, sizeof(r), cudaMemcpyHostToDevice));
+    launch_sampler_ex(req, logits, stride, sc, tok, act, nullptr, 0, 1, picked, 1, nullptr);
+    YAR_CUDA(cudaDeviceSynchronize());
+    int err = 0;
+    YAR_CUDA(cudaMemcpy(&err, &req->error, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) throw Error("RuntimeError", err == 1 ? "sampler candidate set exceeds 2048 rows" : "no finite logits");
+    YAR_CUDA(cudaMemcpy(token, picked, sizeof(int32_t), cudaMemcpyDeviceToHost));
+    if (scores) YAR_CUDA(cudaMemcpy(scores, sc, size_t(n) * 4, cudaMemcpyDeviceToHost));
+  } catch (...) {
+    cudaFree(logits), cudaFree(sc), cudaFree(req), cudaFree(tok), cudaFree(act), cudaFree(picked);
+    throw;
+  }
+  cudaFree(logits), cudaFree(sc), cudaFree(req), cudaFree(tok), cudaFree(act), cudaFree(picked);
+}
+
+}  // namespace yar

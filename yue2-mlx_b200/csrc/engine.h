@@ -1,0 +1,157 @@
+// engine.h — internal types of the YuE2 AR engine (host C++20 + CUDA sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace yar {
+
+using bf16 = __nv_bfloat16;
+
+// Protocol ids (native/include/lyra/types.hpp:63-68).
+constexpr int kEOD = 151643, kAbcEnd = 151848, kMusicEnd = 151852;
+constexpr int kCodecOffset = 151853, kCodecSize = 32768, kContext = 24576;
+constexpr int kPhaseAbc = 0, kPhaseSemantic = 1, kPhaseFull = 2;
+
+// lyra::Error (types.hpp:70-74): a type name the C ABI maps to a status code.
+struct Error : std::runtime_error {
+  std::string type;
+  Error(std::string kind, const std::string &msg) : std::runtime_error(msg), type(std::move(kind)) {}
+};
+[[noreturn]] void throw_cuda(cudaError_t e, const char *what, const char *file, int line);
+#define YAR_CUDA(x)                                                        \
+  do {                                                                     \
+    cudaError_t _e = (x);                                                  \
+    if (_e != cudaSuccess) ::yar::throw_cuda(_e, #x, __FILE__, __LINE__);  \
+  } while (0)
+
+struct Dims {
+  int hidden = 2048, layers = 28, heads = 16, kv_heads = 8, head_dim = 128, ffn = 6144;
+  int vocab = 184704, context = kContext;
+  float eps = 1e-6f;
+  double theta = 1e6;
+  int qdim() const { return heads * head_dim; }
+  int kvdim() const { return kv_heads * head_dim; }
+  int qkv_rows() const { return qdim() + 2 * kvdim(); }
+};
+
+// Device weights of one decoder layer in the engine layout.
+struct LayerWeights {
+  const bf16 *qkv;   // [q + k + v rows][hidden]: q_proj, k_proj, v_proj rows stacked
+  const bf16 *o;     // [hidden][qdim]
+  const bf16 *gu;    // [2*ffn][hidden]: row 2j = gate_proj row j, row 2j+1 = up_proj row j
+  const bf16 *down;  // [hidden][ffn]
+  const bf16 *ln1, *ln2, *qn, *kn;
+};
+
+struct Model {
+  Dims d;
+  int device = 0, sm_count = 148;
+  void *arena = nullptr;
+  size_t arena_bytes = 0;
+  const bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
+  std::vector<LayerWeights> layers;
+  const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
+};
+
+// Phase projection of the LM head: rows [row0, row0 + n_main) and, optionally, one extra
+// row mapped to local index n_main (native/src/ar.cpp:302-323).
+struct PhaseRows {
+  int row0 = 0, n_main = 0, extra = -1;
+  int width() const { return n_main + (extra >= 0 ? 1 : 0); }
+};
+PhaseRows phase_rows(const Dims &d, int phase);
+
+// Per-request sampler state in device memory (one CFG request spans two rows).
+constexpr int kHistCap = 128;
+constexpr int kMaxPenaltyWindow = 100;
+struct RequestState {
+  int row_c, row_u;  // conditional row, unconditional row (-1: no CFG)
+  int phase, width, end_local;
+  float temperature, top_p, cfg_scale;
+  int top_k, window, min_tokens, max_tokens, penalty_on;
+  float alpha[kMaxPenaltyWindow + 1];  // penalty ** count in FP32
+  uint32_t seed_lo, seed_hi, stream;
+  int step, done, n_out, error;
+  int hist[kHistCap];  // ring of native ids (the last kHistCap sampled tokens)
+};
+
+struct Session;
+
+// Kernel launchers (kernels_*.cu). All run on `stream`.
+void launch_embed_rows(const Model &m, Session &s, int n_rows, cudaStream_t st);
+void launch_gemv(const bf16 *W, int N, int K, const bf16 *in, int in_stride, const bf16 *norm_w,
+                 float eps, bf16 *out, int out_stride, int epilogue, int n_rows,
+                 const int *row_active, int sm_count, cudaStream_t st);
+void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st);
+void launch_sampler(const Model &m, Session &s, int n_requests, cudaStream_t st);
+// Prefill (T tokens of one row).
+void launch_embed_tokens(const bf16 *embed, const int *ids, int T, int H, bf16 *x, cudaStream_t st);
+void launch_rmsnorm_rows(const bf16 *x, const bf16 *w, int T, int H, float eps, bf16 *out,
+                         cudaStream_t st);
+void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue,
+                 cudaStream_t st);
+void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
+                             cudaStream_t st);
+void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
+                         cudaStream_t st);
+
+void configure_gemv_kernels();
+void configure_gemm_kernels();
+void configure_attn_kernels();
+
+enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
+
+struct Session {
+  Model *m = nullptr;
+  int max_rows = 0, max_ctx = 0, page_tokens = 256, pages_per_row = 0, num_pages = 0;
+  int prefill_chunk = 1024;
+  cudaStream_t stream = nullptr;
+  // Paged KV pool: [layer][page][k|v][kv_head][page_tokens][head_dim] BF16.
+  bf16 *kv = nullptr;
+  size_t kv_page_elems = 0;  // elements of one (layer, page, k|v) block: kv_heads*P*D
+  std::vector<std::vector<int>> row_pages;
+  std::vector<int> free_pages;
+  int *d_page_table = nullptr;  // [max_rows][pages_per_row]
+  int *d_pos = nullptr;         // [max_rows] next position (== tokens in cache)
+  int *d_cur_pos = nullptr;     // [max_rows] position of the token being forwarded
+  int *d_capacity = nullptr;    // [max_rows]
+  int *d_token = nullptr;       // [max_rows]
+  int *d_active = nullptr;      // [max_rows]
+  int *d_error = nullptr;       // sticky device error flags
+  std::vector<int> capacity;    // host mirror
+  std::vector<int> pos;         // host mirror
+  // Decode activations.
+  bf16 *x = nullptr, *qkv = nullptr, *attn = nullptr, *mlp = nullptr;
+  bf16 *logits = nullptr;  // [max_rows][logit_stride]
+  int logit_stride = 0;
+  // Split-KV attention scratch.
+  float *attn_part = nullptr;  // [max_rows][heads][max_splits][head_dim + 2]
+  int *attn_count = nullptr;   // [max_rows][kv_heads]
+  int max_splits = 0;
+  // Prefill activations (prefill_chunk rows).
+  bf16 *px = nullptr, *ph = nullptr, *pqkv = nullptr, *pq = nullptr, *pattn = nullptr, *pmlp = nullptr;
+  int *pids = nullptr;
+  // Sampler.
+  RequestState *d_req = nullptr;
+  int max_requests = 0;
+  int32_t *d_out_tokens = nullptr;  // [max_requests][out_cap]
+  int out_cap = 0;
+  float *d_scores = nullptr;  // [max_requests][logit_stride] sampler scratch
+  uint64_t *d_cand = nullptr;  // [max_requests][kCandCap]
+  // Captured decode steps keyed by (rows, requests, phase).
+  struct Graph {
+    int rows, requests, phase;
+    cudaGraphExec_t exec;
+  };
+  std::vector<Graph> graphs;
+  int *h_pinned = nullptr;  // pinned staging for small D2H reads
+};
+
+constexpr int kCandCap = 2048;
+
+}  // namespace yar

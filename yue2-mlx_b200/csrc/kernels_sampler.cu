@@ -1,0 +1,321 @@
+// kernels_sampler.cu — one sampler step per request on phase-local BF16 logits.
+//
+// Filter chain = upstream distribution (vendor/yue/src/yue2/sampling.py:16-53) on the
+// phase rows (native/src/sampling.cpp:38-99), after the CFG mix (sampling.cpp:100-115):
+//   s = f32(bf16(u + bf16(bf16(c - u) * f32(scale))))          (CFG, when two rows)
+//   s[end] = -inf while step < min_tokens
+//   s[t] = s < 0 ? s * alpha[n] : s / alpha[n] for the n-times-repeated ids of the window
+//   greedy: first argmax                       (temperature == 0)
+//   s /= f32(T); s < kth-largest(s) -> -inf    (top-k by value, ties kept)
+//   shifted nucleus over survivors sorted by (score desc, index asc)
+// Draw: u = Philox uniform(seed, step); e_i = yexp(s_i - s_0); first survivor whose
+// sequential FP32 running sum of e exceeds u * sum(e). All of it is exact-FP32 code
+// (exact_math.cuh), so the CPU restatement reproduces the token bit for bit.
+#include "common.cuh"
+
+namespace yar {
+
+constexpr int kSampThreads = 1024;
+
+struct SamplerParams {
+  RequestState *req;
+  const bf16 *logits;
+  int logit_stride;
+  float *scores;      // [requests][logit_stride] scratch
+  int *token;         // [rows]
+  int *active;        // [rows]
+  int32_t *out_tokens;
+  int out_cap;
+  int write_scores;   // also leave the filtered FP32 scores in `scores` (tests)
+  int32_t *picked;    // optional [requests] local token of this step
+};
+
+__device__ __forceinline__ int native_to_local(int tok, int phase, int width) {
+  if (phase == kPhaseAbc) {
+    if (tok >= 0 && tok < kEOD) return tok;
+    return tok == kAbcEnd ? kEOD : -1;
+  }
+  if (phase == kPhaseSemantic) {
+    if (tok == kMusicEnd) return 0;
+    if (tok >= kCodecOffset && tok < kCodecOffset + kCodecSize) return tok - kMusicEnd;
+    return -1;
+  }
+  return (tok >= 0 && tok < width) ? tok : -1;
+}
+__device__ __forceinline__ int local_to_native(int loc, int phase) {
+  if (phase == kPhaseAbc) return loc < kEOD ? loc : kAbcEnd;
+  if (phase == kPhaseSemantic) return kMusicEnd + loc;
+  return loc;
+}
+
+__global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
+  __shared__ uint64_t cand[kCandCap];
+  __shared__ float ev[kCandCap];
+  __shared__ int hist256[256];
+  __shared__ int ncand, sel_bin, kth_rem, result;
+  __shared__ float red_v[32];
+  __shared__ int red_i[32];
+  __shared__ uint32_t prefix_s;
+
+  pdl_launch_dependents();
+  pdl_wait();
+  RequestState &st = p.req[blockIdx.x];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (st.done || st.step >= st.max_tokens) return;
+  const int n = st.width, step = st.step;
+  const bf16 *lc = p.logits + size_t(st.row_c) * p.logit_stride;
+  const bf16 *lu = st.row_u >= 0 ? p.logits + size_t(st.row_u) * p.logit_stride : nullptr;
+  float *s = p.scores + size_t(blockIdx.x) * p.logit_stride;
+
+  // CFG mix and FP32 upcast.
+  const float scale = st.cfg_scale;
+  for (int i = tid; i < n; i += kSampThreads) {
+    float v = bf2f(lc[i]);
+    if (lu) {
+      const float u = bf2f(lu[i]);
+      const float delta = round_bf16(f_sub(v, u));
+      const float scaled = round_bf16(f_mul(delta, scale));
+      v = round_bf16(f_add(u, scaled));
+    }
+    s[i] = v;
+  }
+  __syncthreads();
+  if (tid == 0 && step < st.min_tokens && st.end_local >= 0) s[st.end_local] = -INFINITY;
+  __syncthreads();
+  // Window penalty: thread t < W owns history entry t; the first occurrence of each id
+  // applies alpha[count of that id in the window].
+  if (st.penalty_on && st.n_out > 0) {
+    const int W = min(st.window, st.n_out);
+    __shared__ int loc_s[kMaxPenaltyWindow];
+    if (tid < W) loc_s[tid] = native_to_local(st.hist[(st.n_out - W + tid) % kHistCap], st.phase, n);
+    __syncthreads();
+    if (tid < W) {
+      const int me = loc_s[tid];
+      bool first = me >= 0;
+      int count = 0;
+      for (int j = 0; j < W; ++j) {
+        if (loc_s[j] == me) {
+          ++count;
+          if (j < tid) first = false;
+        }
+      }
+      if (first) {
+        const float a = st.alpha[count], v = s[me];
+        s[me] = v < 0.f ? f_mul(v, a) : f_div(v, a);
+      }
+    }
+    __syncthreads();
+  }
+
+  int local = -1;
+  if (st.temperature == 0.f) {
+    // Greedy: first index of the maximum.
+    float bv = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    for (int i = tid; i < n; i += kSampThreads) {
+      const float v = s[i];
+      if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      red_v[warp] = bv;
+      red_i[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float v = red_v[0];
+      int i0 = red_i[0];
+      for (int w = 1; w < kSampThreads / 32; ++w)
+        if (red_v[w] > v || (red_v[w] == v && red_i[w] < i0)) {
+          v = red_v[w];
+          i0 = red_i[w];
+        }
+      result = i0 < n ? i0 : 0;
+    }
+    __syncthreads();
+    local = result;
+  } else {
+    if (st.temperature != 1.f) {
+      for (int i = tid; i < n; i += kSampThreads) s[i] = f_div(s[i], st.temperature);
+      __syncthreads();
+    }
+    // k-th largest value by 8-bit radix select on order-preserving keys.
+    const int k = min(st.top_k, n);
+    if (tid == 0) {
+      prefix_s = 0;
+      kth_rem = k;
+    }
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += kSampThreads) hist256[b] = 0;
+      __syncthreads();
+      const uint32_t pre = prefix_s;
+      const uint32_t hmask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int i = tid; i < n; i += kSampThreads) {
+        const uint32_t key = f32_order_key(s[i]);
+        if ((key & hmask) == (pre & hmask)) atomicAdd(&hist256[(key >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int rem = kth_rem, b = 255;
+        for (; b > 0; --b) {
+          if (hist256[b] >= rem) break;
+          rem -= hist256[b];
+        }
+        kth_rem = rem;
+        prefix_s = pre | (uint32_t(b) << shift);
+      }
+      __syncthreads();
+    }
+    const float thr = f32_from_order_key(prefix_s);
+    if (tid == 0) ncand = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += kSampThreads) {
+      const float v = s[i];
+      if (v >= thr && v > -INFINITY) {
+        const int slot = atomicAdd(&ncand, 1);
+        if (slot < kCandCap) cand[slot] = (uint64_t(~f32_order_key(v)) << 32) | uint32_t(i);
+      } else if (p.write_scores && v < thr) {
+        s[i] = -INFINITY;
+      }
+    }
+    __syncthreads();
+    const int nc = ncand;
+    if (nc > kCandCap || nc == 0) {
+      if (tid == 0) {
+        st.error = nc == 0 ? 2 : 1;
+        result = 0;
+      }
+      __syncthreads();
+      local = -1;
+    } else {
+      int np2 = 1;
+      while (np2 < nc) np2 <<= 1;
+      for (int i = nc + tid; i < np2; i += kSampThreads) cand[i] = ~0ull;
+      __syncthreads();
+      // Bitonic sort, ascending keys = (score desc, index asc).
+      for (int size = 2; size <= np2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          for (int i = tid; i < np2; i += kSampThreads) {
+            const int j = i ^ stride;
+            if (j > i) {
+              const bool up = (i & size) == 0;
+              const uint64_t a = cand[i], b = cand[j];
+              if ((a > b) == up) {
+                cand[i] = b;
+                cand[j] = a;
+              }
+            }
+          }
+          __syncthreads();
+        }
+      }
+      const float s0 = s[uint32_t(cand[0])];
+      for (int i = tid; i < nc; i += kSampThreads) ev[i] = yexp(f_sub(s[uint32_t(cand[i])], s0));
+      __syncthreads();
+      if (tid == 0) {
+        int kept = nc;
+        if (st.top_p < 1.f) {
+          float total = 0.f;
+          for (int i = 0; i < nc; ++i) total = f_add(total, ev[i]);
+          float c = 0.f;
+          kept = 0;
+          for (int i = 0; i < nc; ++i) {
+            const float pi = f_div(ev[i], total);
+            c = f_add(c, pi);
+            const bool removed = i >= 1 && f_sub(c, pi) > st.top_p;
+            if (removed) {
+              ev[i] = -1.f;  // marks a removed survivor
+            } else {
+              ++kept;
+            }
+          }
+        }
+        const float u = step_uniform((uint64_t(st.seed_hi) << 32) | st.seed_lo, uint32_t(step), st.stream);
+        float total = 0.f;
+        for (int i = 0; i < nc; ++i)
+          if (ev[i] >= 0.f) total = f_add(total, ev[i]);
+        const float target = f_mul(u, total);
+        float acc = 0.f;
+        int pick = -1, last = -1;
+        for (int i = 0; i < nc; ++i) {
+          if (ev[i] < 0.f) continue;
+          last = i;
+          acc = f_add(acc, ev[i]);
+          if (target < acc) {
+            pick = i;
+            break;
+          }
+        }
+        if (pick < 0) pick = last;
+        result = int(uint32_t(cand[pick]));
+        (void)kept;
+      }
+      __syncthreads();
+      if (p.write_scores)
+        for (int i = tid; i < nc; i += kSampThreads)
+          if (ev[i] < 0.f) s[uint32_t(cand[i])] = -INFINITY;
+      local = result;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    if (p.picked) p.picked[blockIdx.x] = local;
+    if (local < 0) {
+      st.done = 1;
+      p.active[st.row_c] = 0;
+      if (st.row_u >= 0) p.active[st.row_u] = 0;
+      return;
+    }
+    const int native = local_to_native(local, st.phase);
+    st.step = step + 1;
+    if (local == st.end_local) {
+      st.done = 1;
+    } else {
+      if (p.out_tokens && st.n_out < p.out_cap) p.out_tokens[size_t(blockIdx.x) * p.out_cap + st.n_out] = native;
+      st.hist[st.n_out % kHistCap] = native;
+      st.n_out += 1;
+    }
+    p.token[st.row_c] = native;
+    if (st.row_u >= 0) p.token[st.row_u] = native;
+    if (st.done || st.step >= st.max_tokens) {
+      // The reference forwards no token after the end token or the last step.
+      p.active[st.row_c] = 0;
+      if (st.row_u >= 0) p.active[st.row_u] = 0;
+    }
+  }
+}
+
+void launch_sampler_ex(RequestState *req, const bf16 *logits, int logit_stride, float *scores, int *token,
+                       int *active, int32_t *out_tokens, int out_cap, int write_scores, int32_t *picked,
+                       int n_requests, cudaStream_t st) {
+  SamplerParams p{req, logits, logit_stride, scores, token, active, out_tokens, out_cap, write_scores, picked};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_requests);
+  cfg.blockDim = dim3(kSampThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  YAR_CUDA(cudaLaunchKernelEx(&cfg, k_sampler, p));
+}
+
+void launch_sampler(const Model &m, Session &s, int n_requests, cudaStream_t st) {
+  (void)m;
+  launch_sampler_ex(s.d_req, s.logits, s.logit_stride, s.d_scores, s.d_token, s.d_active, s.d_out_tokens,
+                    s.out_cap, 0, nullptr, n_requests, st);
+}
+
+}  // namespace yar

@@ -1,0 +1,371 @@
+// loader.cpp — the converted AR checkpoint into HBM (ARModel::ARModel,
+// native/src/ar.cpp:133-238, with verify=false as Pipeline::load_ar calls it,
+// native/src/pipeline.cpp:131-176).
+//
+// Checks, in the reference's order and with its error types:
+//   1. conversion.json is a schema-1 manifest with a precisions.bf16 record naming
+//      ar-bf16.safetensors and dtype bfloat16                      (ar.cpp:137-154)
+//   2. config.json matches the pinned generator config             (ar.cpp:161-192)
+//   3. ar-bf16.safetensors holds exactly the AR tensor set, BF16, with the pinned shapes
+//                                                                   (ar.cpp:193-236)
+// Device layout (one allocation): per layer the q/k/v rows stacked into one [q+2kv][H]
+// matrix, gate/up rows interleaved (row 2j gate j, row 2j+1 up j) so a SwiGLU output
+// comes from one row pair, and everything else as stored (row-major [out][in]).
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <set>
+#include <sstream>
+
+#include "engine.h"
+#include "exact_math.cuh"
+#include "nlohmann/json.hpp"
+
+namespace yar {
+
+using Json = nlohmann::json;
+
+void throw_cuda(cudaError_t e, const char *what, const char *file, int line) {
+  std::ostringstream os;
+  os << "CUDA error " << cudaGetErrorName(e) << " (" << cudaGetErrorString(e) << ") at " << file << ":"
+     << line << ": " << what;
+  throw Error("RuntimeError", os.str());
+}
+
+static Json read_json(const std::string &path) {
+  std::ifstream in(path);
+  if (!in) throw Error("FileNotFoundError", "Missing file: " + path);
+  std::stringstream ss;
+  ss << in.rdbuf();
+  try {
+    return Json::parse(ss.str());
+  } catch (const std::exception &e) {
+    throw Error("ValueError", "Invalid JSON in " + path + ": " + e.what());
+  }
+}
+
+PhaseRows phase_rows(const Dims &d, int phase) {
+  PhaseRows r;
+  if (phase == kPhaseFull) {
+    r.row0 = 0;
+    r.n_main = d.vocab;
+    return r;
+  }
+  if (d.vocab != 184704) throw Error("ValueError", "Protocol phases need the 184704-row vocabulary");
+  if (phase == kPhaseAbc) {
+    r.row0 = 0;
+    r.n_main = kEOD;
+    r.extra = kAbcEnd;
+  } else if (phase == kPhaseSemantic) {
+    r.row0 = kMusicEnd;
+    r.n_main = kCodecOffset + kCodecSize - kMusicEnd;
+  } else {
+    throw Error("ValueError", "phase must be 'abc' or 'semantic'");
+  }
+  return r;
+}
+
+static Dims config_dims(const Json &config, bool any_dims) {
+  if (!config.is_object()) throw Error("ValueError", "config.json must contain a JSON object");
+  const std::vector<std::pair<std::string, Json>> pinned = {
+      {"hidden_size", 2048},      {"intermediate_size", 6144},        {"num_hidden_layers", 28},
+      {"num_attention_heads", 16}, {"num_key_value_heads", 8},         {"head_dim", 128},
+      {"vocab_size", 184704},     {"max_position_embeddings", kContext}, {"rope_theta", 1000000.0}};
+  for (const auto &[key, expected] : pinned) {
+    Json actual = config.contains(key) ? config[key]
+                                        : (key == "max_position_embeddings" ? Json(kContext) : Json());
+    if (!any_dims && actual != expected) throw Error("ValueError", "Incompatible YuE2 config: " + key);
+    if (key != "rope_theta" && !(actual.is_number_integer() && actual.get<long long>() > 0))
+      throw Error("ValueError", "Generator config field " + key + " must be a positive integer");
+    if (key == "rope_theta" && !(actual.is_number() && actual.get<double>() > 0))
+      throw Error("ValueError", "rope_theta must be a positive number");
+  }
+  if (config.value("tie_word_embeddings", Json(false)) != Json(false))
+    throw Error("ValueError", "YuE2 requires untied input and output embeddings");
+  if (config.contains("rope_scaling") && !config["rope_scaling"].is_null() &&
+      config["rope_scaling"] != Json::object())
+    throw Error("ValueError", "YuE2 uses fixed base RoPE without scaling");
+  if (config.value("hidden_act", std::string("silu")) != "silu")
+    throw Error("ValueError", "Incompatible YuE2 config: hidden_act must be silu");
+  if (!config.contains("rms_norm_eps") || !config["rms_norm_eps"].is_number() ||
+      !std::isfinite(config["rms_norm_eps"].get<double>()) || config["rms_norm_eps"].get<double>() <= 0)
+    throw Error("ValueError", "rms_norm_eps must be finite and positive");
+  Dims d;
+  d.hidden = config["hidden_size"];
+  d.ffn = config["intermediate_size"];
+  d.layers = config["num_hidden_layers"];
+  d.heads = config["num_attention_heads"];
+  d.kv_heads = config["num_key_value_heads"];
+  d.head_dim = config["head_dim"];
+  d.vocab = config["vocab_size"];
+  d.context = config.value("max_position_embeddings", kContext);
+  d.theta = config["rope_theta"].get<double>();
+  d.eps = float(config["rms_norm_eps"].get<double>());
+  if (d.heads % d.kv_heads != 0) throw Error("ValueError", "num_attention_heads must be a multiple of num_key_value_heads");
+  if (d.head_dim != 64 && d.head_dim != 128) throw Error("ValueError", "head_dim must be 64 or 128");
+  if (d.hidden % 8 || d.ffn % 8) throw Error("ValueError", "hidden_size and intermediate_size must be multiples of 8");
+  if (d.context > kContext) throw Error("ValueError", "max_position_embeddings above 24576");
+  return d;
+}
+
+struct TensorRec {
+  std::vector<int64_t> shape;
+  uint64_t begin, end;
+};
+
+static std::map<std::string, TensorRec> read_safetensors_header(const std::string &path, uint64_t &data_start) {
+  std::ifstream in(path, std::ios::binary);
+  if (!in) throw Error("FileNotFoundError", "Converted artifact does not contain bf16 AR weights: " + path);
+  in.seekg(0, std::ios::end);
+  const uint64_t size = uint64_t(in.tellg());
+  in.seekg(0);
+  uint64_t len = 0;
+  if (size < 10) throw Error("ValueError", "Invalid safetensors file: " + path);
+  in.read(reinterpret_cast<char *>(&len), 8);
+  if (!in || len < 2 || len > 64ull * 1024 * 1024 || len > size - 8)
+    throw Error("ValueError", "Invalid safetensors header size");
+  std::string raw(len, '\0');
+  in.read(raw.data(), std::streamsize(len));
+  if (!in) throw Error("ValueError", "Truncated safetensors header");
+  Json h;
+  try {
+    h = Json::parse(raw);
+  } catch (const std::exception &e) {
+    throw Error("ValueError", std::string("Invalid safetensors header: ") + e.what());
+  }
+  if (!h.is_object()) throw Error("ValueError", "Invalid safetensors header");
+  data_start = 8 + len;
+  std::map<std::string, TensorRec> out;
+  for (auto it = h.begin(); it != h.end(); ++it) {
+    if (it.key() == "__metadata__") continue;
+    const Json &r = it.value();
+    if (!r.is_object() || !r.contains("dtype") || !r.contains("shape") || !r.contains("data_offsets"))
+      throw Error("ValueError", "Invalid safetensors entry: " + it.key());
+    if (r["dtype"] != "BF16") throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + it.key());
+    TensorRec t;
+    for (const auto &v : r["shape"]) t.shape.push_back(v.get<int64_t>());
+    t.begin = r["data_offsets"][0].get<uint64_t>();
+    t.end = r["data_offsets"][1].get<uint64_t>();
+    uint64_t n = 2;
+    for (auto v : t.shape) n *= uint64_t(v);
+    if (t.end < t.begin || t.end - t.begin != n || data_start + t.end > size)
+      throw Error("ValueError", "Truncated or inconsistent safetensors tensor: " + it.key());
+    out.emplace(it.key(), std::move(t));
+  }
+  return out;
+}
+
+Model *load_model(const std::string &dir, int device, uint32_t flags) {
+  const bool any_dims = flags & 1u;
+  // 1. Manifest.
+  Json manifest = read_json(dir + "/conversion.json");
+  if (!manifest.is_object() || manifest.value("schema", 0) != 1)
+    throw Error("ValueError", "conversion.json must be a schema-1 manifest");
+  if (!manifest.contains("precisions") || !manifest["precisions"].is_object() ||
+      !manifest["precisions"].contains("bf16") || !manifest["precisions"]["bf16"].is_object())
+    throw Error("FileNotFoundError", "Converted artifact does not contain bf16 AR weights");
+  const Json &entry = manifest["precisions"]["bf16"];
+  if (entry.value("ar", std::string()) != "ar-bf16.safetensors")
+    throw Error("ValueError", "Manifest AR filename does not match precision");
+  if (entry.value("dtype", std::string()) != "bfloat16")
+    throw Error("ValueError", "BF16 manifest entry must declare dtype='bfloat16'");
+  // 2. Config.
+  const Dims d = config_dims(read_json(dir + "/config.json"), any_dims);
+  // 3. Tensors.
+  const std::string path = dir + "/ar-bf16.safetensors";
+  uint64_t data_start = 0;
+  auto recs = read_safetensors_header(path, data_start);
+  std::set<std::string> expected;
+  auto require = [&](const std::string &name, std::vector<int64_t> shape) {
+    expected.insert(name);
+    auto it = recs.find(name);
+    if (it == recs.end()) throw Error("ValueError", "Missing AR tensor: " + name);
+    if (it->second.shape != shape) throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + name);
+  };
+  const int H = d.hidden, Q = d.qdim(), KV = d.kvdim(), F = d.ffn, V = d.vocab, D = d.head_dim;
+  require("model.embed_tokens.weight", {V, H});
+  require("model.norm.weight", {H});
+  require("lm_head.weight", {V, H});
+  for (int i = 0; i < d.layers; ++i) {
+    const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
+    require(n + ".input_layernorm.weight", {H});
+    require(n + ".post_attention_layernorm.weight", {H});
+    require(a + ".q_norm.weight", {D});
+    require(a + ".k_norm.weight", {D});
+    require(a + ".q_proj.weight", {Q, H});
+    require(a + ".k_proj.weight", {KV, H});
+    require(a + ".v_proj.weight", {KV, H});
+    require(a + ".o_proj.weight", {H, Q});
+    require(n + ".mlp.gate_proj.weight", {F, H});
+    require(n + ".mlp.up_proj.weight", {F, H});
+    require(n + ".mlp.down_proj.weight", {H, F});
+  }
+  for (const auto &[name, rec] : recs)
+    if (!expected.count(name)) throw Error("ValueError", "Unexpected AR tensor: " + name);
+
+  // Arena layout (256-byte aligned pieces).
+  auto *m = new Model();
+  try {
+    m->d = d;
+    m->device = device;
+    YAR_CUDA(cudaSetDevice(device));
+    YAR_CUDA(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device));
+    configure_gemv_kernels();
+    configure_gemm_kernels();
+    configure_attn_kernels();
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+      const size_t o = off;
+      off = (off + bytes + 255) & ~size_t(255);
+      return o;
+    };
+    const size_t e2 = sizeof(uint16_t);
+    const size_t o_embed = take(size_t(V) * H * e2), o_head = take(size_t(V) * H * e2), o_norm = take(size_t(H) * e2);
+    struct LO { size_t qkv, o, gu, down, ln1, ln2, qn, kn; };
+    std::vector<LO> lo(d.layers);
+    for (int i = 0; i < d.layers; ++i) {
+      lo[i].qkv = take(size_t(Q + 2 * KV) * H * e2);
+      lo[i].o = take(size_t(H) * Q * e2);
+      lo[i].gu = take(size_t(2 * F) * H * e2);
+      lo[i].down = take(size_t(H) * F * e2);
+      lo[i].ln1 = take(H * e2);
+      lo[i].ln2 = take(H * e2);
+      lo[i].qn = take(D * e2);
+      lo[i].kn = take(D * e2);
+    }
+    const size_t o_cos = take(size_t(d.context) * (D / 2) * 4), o_sin = take(size_t(d.context) * (D / 2) * 4);
+    m->arena_bytes = off;
+    YAR_CUDA(cudaMalloc(&m->arena, off));
+    char *base = static_cast<char *>(m->arena);
+    auto at = [&](size_t o) { return reinterpret_cast<bf16 *>(base + o); };
+
+    // Stream the file through a pinned staging buffer.
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) throw Error("FileNotFoundError", "Cannot open " + path);
+    const size_t stage_bytes = 64ull << 20;
+    void *stage = nullptr;
+    YAR_CUDA(cudaMallocHost(&stage, 2 * stage_bytes));
+    cudaStream_t st;
+    YAR_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    cudaEvent_t done[2];
+    YAR_CUDA(cudaEventCreate(&done[0]));
+    YAR_CUDA(cudaEventCreate(&done[1]));
+    int buf = 0;
+    bool pending[2] = {false, false};
+    auto pread_all = [&](char *dst, uint64_t file_off, size_t n) {
+      size_t got = 0;
+      while (got < n) {
+        const ssize_t r = ::pread(fd, dst + got, n - got, off_t(file_off + got));
+        if (r <= 0) throw Error("ValueError", "Truncated safetensors data in " + path);
+        got += size_t(r);
+      }
+    };
+    // Copy bytes [src_off, src_off+n) of a tensor to device address dst (row-chunked).
+    auto upload = [&](const std::string &name, char *dst) {
+      const TensorRec &r = recs.at(name);
+      const uint64_t n = r.end - r.begin;
+      for (uint64_t done_b = 0; done_b < n; done_b += stage_bytes) {
+        const size_t len = size_t(std::min<uint64_t>(stage_bytes, n - done_b));
+        if (pending[buf]) YAR_CUDA(cudaEventSynchronize(done[buf]));
+        char *sb = static_cast<char *>(stage) + buf * stage_bytes;
+        pread_all(sb, data_start + r.begin + done_b, len);
+        YAR_CUDA(cudaMemcpyAsync(dst + done_b, sb, len, cudaMemcpyHostToDevice, st));
+        YAR_CUDA(cudaEventRecord(done[buf], st));
+        pending[buf] = true;
+        buf ^= 1;
+      }
+    };
+    // Interleave gate/up rows into dst: rows 2j (gate j) and 2j+1 (up j).
+    auto upload_gate_up = [&](const std::string &gate, const std::string &up, char *dst) {
+      const size_t row_bytes = size_t(H) * e2;
+      const size_t rows_per = stage_bytes / (2 * row_bytes);
+      for (int r0 = 0; r0 < F; r0 += int(rows_per)) {
+        const int nr = int(std::min<size_t>(rows_per, size_t(F - r0)));
+        if (pending[buf]) YAR_CUDA(cudaEventSynchronize(done[buf]));
+        char *sb = static_cast<char *>(stage) + buf * stage_bytes;
+        std::vector<char> g(nr * row_bytes), u(nr * row_bytes);
+        pread_all(g.data(), data_start + recs.at(gate).begin + size_t(r0) * row_bytes, g.size());
+        pread_all(u.data(), data_start + recs.at(up).begin + size_t(r0) * row_bytes, u.size());
+        for (int j = 0; j < nr; ++j) {
+          std::memcpy(sb + (2 * size_t(j)) * row_bytes, g.data() + size_t(j) * row_bytes, row_bytes);
+          std::memcpy(sb + (2 * size_t(j) + 1) * row_bytes, u.data() + size_t(j) * row_bytes, row_bytes);
+        }
+        YAR_CUDA(cudaMemcpyAsync(dst + 2 * size_t(r0) * row_bytes, sb, 2 * size_t(nr) * row_bytes,
+                                 cudaMemcpyHostToDevice, st));
+        YAR_CUDA(cudaEventRecord(done[buf], st));
+        pending[buf] = true;
+        buf ^= 1;
+      }
+    };
+    upload("model.embed_tokens.weight", base + o_embed);
+    upload("lm_head.weight", base + o_head);
+    upload("model.norm.weight", base + o_norm);
+    m->layers.resize(d.layers);
+    for (int i = 0; i < d.layers; ++i) {
+      const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
+      upload(a + ".q_proj.weight", base + lo[i].qkv);
+      upload(a + ".k_proj.weight", base + lo[i].qkv + size_t(Q) * H * e2);
+      upload(a + ".v_proj.weight", base + lo[i].qkv + size_t(Q + KV) * H * e2);
+      upload(a + ".o_proj.weight", base + lo[i].o);
+      upload_gate_up(n + ".mlp.gate_proj.weight", n + ".mlp.up_proj.weight", base + lo[i].gu);
+      upload(n + ".mlp.down_proj.weight", base + lo[i].down);
+      upload(n + ".input_layernorm.weight", base + lo[i].ln1);
+      upload(n + ".post_attention_layernorm.weight", base + lo[i].ln2);
+      upload(a + ".q_norm.weight", base + lo[i].qn);
+      upload(a + ".k_norm.weight", base + lo[i].kn);
+      m->layers[i] = LayerWeights{at(lo[i].qkv), at(lo[i].o), at(lo[i].gu), at(lo[i].down),
+                                  at(lo[i].ln1), at(lo[i].ln2), at(lo[i].qn), at(lo[i].kn)};
+    }
+    m->embed = at(o_embed);
+    m->lm_head = at(o_head);
+    m->final_norm = at(o_norm);
+    // RoPE tables (modeling_yue2.py:142-156): FP32 inv_freq = 1 / float(theta ** (2i/d)),
+    // FP32 angle = pos * inv_freq, cos/sin evaluated in double, rounded to FP32, then
+    // to BF16 (the activation dtype they are cast to before use).
+    {
+      const int half = D / 2;
+      std::vector<float> inv(half), c(size_t(d.context) * half), s(size_t(d.context) * half);
+      for (int i = 0; i < half; ++i) {
+        const float e = f_div(float(2 * i), float(D));
+        const float pw = float(std::pow(double(float(d.theta)), double(e)));
+        inv[i] = f_div(1.0f, pw);
+      }
+      for (int pos = 0; pos < d.context; ++pos)
+        for (int i = 0; i < half; ++i) {
+          const float ang = f_mul(float(pos), inv[i]);
+          c[size_t(pos) * half + i] = round_bf16(float(std::cos(double(ang))));
+          s[size_t(pos) * half + i] = round_bf16(float(std::sin(double(ang))));
+        }
+      YAR_CUDA(cudaStreamSynchronize(st));
+      YAR_CUDA(cudaMemcpy(base + o_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+      YAR_CUDA(cudaMemcpy(base + o_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+      m->rope_cos = reinterpret_cast<const float *>(base + o_cos);
+      m->rope_sin = reinterpret_cast<const float *>(base + o_sin);
+    }
+    YAR_CUDA(cudaStreamSynchronize(st));
+    YAR_CUDA(cudaEventDestroy(done[0]));
+    YAR_CUDA(cudaEventDestroy(done[1]));
+    YAR_CUDA(cudaStreamDestroy(st));
+    YAR_CUDA(cudaFreeHost(stage));
+    ::close(fd);
+  } catch (...) {
+    if (m->arena) cudaFree(m->arena);
+    delete m;
+    throw;
+  }
+  return m;
+}
+
+void free_model(Model *m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->arena) cudaFree(m->arena);
+  delete m;
+}
+
+}  // namespace yar

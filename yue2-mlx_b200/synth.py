@@ -1,0 +1,227 @@
+"""Seeded synthetic checkpoints in the converted AR layout.
+
+There is no real YuE2 checkpoint on these machines, so every test, the bench and the
+CPU baseline run on weights drawn here. The directory this module writes has exactly
+the layout ``lyra prepare`` produces for the AR partition and which ``ARModel`` loads
+(native/src/ar.cpp:133-238, native/src/conversion.cpp:203-275, :383-389, :552-565):
+
+* ``config.json``      — the generator config (conversion.cpp:203-221);
+* ``conversion.json``  — schema-1 manifest with a ``precisions.bf16`` record;
+* ``ar-bf16.safetensors`` — the AR tensors only, BF16, row-major ``[out, in]``.
+
+Weights: every matrix (embedding and LM head included) is N(0, std) with std 0.02,
+drawn with numpy's PCG64 ``standard_normal`` in float32, multiplied by float32(std) and
+rounded to BF16 (round to nearest even). Draws are made in row blocks of at most
+``BLOCK_ELEMS`` elements, each block seeded by ``[seed, tensor_index, block_index]``, so
+any tensor or row range can be regenerated alone and blocks can be drawn in parallel
+with identical bits on any machine running the same numpy. Norm weights are 1.0 unless
+``norm_std`` > 0, in which case they are ``1 + N(0, norm_std)`` (tests use that so the
+norm-weight rounding point is exercised).
+"""
+from __future__ import annotations
+
+import json
+import multiprocessing as mp
+import os
+from dataclasses import asdict, dataclass
+
+import numpy as np
+
+BLOCK_ELEMS = 1 << 22
+
+
+@dataclass(frozen=True)
+class Dims:
+    hidden: int = 2048
+    layers: int = 28
+    heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 6144
+    vocab: int = 184704
+    eps: float = 1e-6
+    theta: float = 1e6
+    context: int = 24576
+
+
+PINNED = Dims()
+"""The YuE2-3B AR dims the reference pins (native/src/ar.cpp:164-169)."""
+
+TINY = Dims(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=688,
+            vocab=4096, eps=1e-6, theta=1e4, context=2048)
+"""BASELINE config 1: the tiny LLaMA-style decoder used for fast parity checks."""
+
+
+def tensor_specs(d: Dims) -> list[tuple[str, tuple[int, ...]]]:
+    """AR tensors in canonical order; the index in this list seeds each tensor."""
+    specs = [("model.embed_tokens.weight", (d.vocab, d.hidden)),
+             ("lm_head.weight", (d.vocab, d.hidden)),
+             ("model.norm.weight", (d.hidden,))]
+    q, kv = d.heads * d.head_dim, d.kv_heads * d.head_dim
+    for i in range(d.layers):
+        p = f"model.layers.{i}."
+        specs += [(p + "input_layernorm.weight", (d.hidden,)),
+                  (p + "post_attention_layernorm.weight", (d.hidden,)),
+                  (p + "self_attn.q_proj.weight", (q, d.hidden)),
+                  (p + "self_attn.k_proj.weight", (kv, d.hidden)),
+                  (p + "self_attn.v_proj.weight", (kv, d.hidden)),
+                  (p + "self_attn.o_proj.weight", (d.hidden, q)),
+                  (p + "self_attn.q_norm.weight", (d.head_dim,)),
+                  (p + "self_attn.k_norm.weight", (d.head_dim,)),
+                  (p + "mlp.gate_proj.weight", (d.ffn, d.hidden)),
+                  (p + "mlp.up_proj.weight", (d.ffn, d.hidden)),
+                  (p + "mlp.down_proj.weight", (d.hidden, d.ffn))]
+    return specs
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round float32 to BF16 (nearest, ties to even) and return the uint16 bit pattern."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).copy()
+    u += np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))
+    return (u >> np.uint32(16)).astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def _blocks(shape: tuple[int, ...]):
+    rows = shape[0]
+    cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
+    per = max(1, BLOCK_ELEMS // cols)
+    for b, r0 in enumerate(range(0, rows, per)):
+        yield b, r0, min(rows, r0 + per), cols
+
+
+def draw_block(seed: int, tidx: int, block: int, n: int, std: float) -> np.ndarray:
+    rng = np.random.default_rng([seed, tidx, block])
+    a = rng.standard_normal(n, dtype=np.float32)
+    a *= np.float32(std)
+    return a
+
+
+def tensor_f32(shape, tidx: int, seed: int, std: float, norm_std: float,
+               rows: tuple[int, int] | None = None) -> np.ndarray:
+    """Float32 draws of one tensor (or rows [r0, r1) of it) before BF16 rounding."""
+    if len(shape) == 1:
+        if norm_std > 0:
+            return np.float32(1.0) + draw_block(seed, tidx, 0, shape[0], norm_std)
+        return np.ones(shape[0], dtype=np.float32)
+    r0, r1 = rows if rows is not None else (0, shape[0])
+    out = np.empty((r1 - r0,) + tuple(shape[1:]), dtype=np.float32)
+    for b, b0, b1, cols in _blocks(tuple(shape)):
+        if b1 <= r0 or b0 >= r1:
+            continue
+        vals = draw_block(seed, tidx, b, (b1 - b0) * cols, std).reshape((b1 - b0,) + tuple(shape[1:]))
+        s0, s1 = max(b0, r0), min(b1, r1)
+        out[s0 - r0:s1 - r0] = vals[s0 - b0:s1 - b0]
+    return out
+
+
+def tensor_bits(shape, tidx: int, seed: int, std: float, norm_std: float,
+                rows: tuple[int, int] | None = None) -> np.ndarray:
+    """BF16 bits of one tensor (or of rows [r0, r1) of it), as the writer produces them."""
+    return f32_to_bf16_bits(tensor_f32(shape, tidx, seed, std, norm_std, rows))
+
+
+def f32_tensors(dims: Dims, seed: int = 0, std: float = 0.02, norm_std: float = 0.0) -> dict:
+    """All AR tensors as unrounded float32 (BASELINE config 1 runs the tiny model in FP32)."""
+    return {name: tensor_f32(shape, i, seed, std, norm_std)
+            for i, (name, shape) in enumerate(tensor_specs(dims))}
+
+
+def config_json(d: Dims) -> dict:
+    """Generator config in the shape conversion.cpp:203-221 pins."""
+    return {"model_type": "yue2", "architectures": ["YuE2ForCausalLM"],
+            "hidden_size": d.hidden, "num_hidden_layers": d.layers,
+            "num_attention_heads": d.heads, "num_key_value_heads": d.kv_heads,
+            "head_dim": d.head_dim, "intermediate_size": d.ffn, "vocab_size": d.vocab,
+            "rms_norm_eps": d.eps, "rope_theta": d.theta,
+            "max_position_embeddings": d.context, "tie_word_embeddings": False,
+            "latent_type": "vae", "latent_dim": 64, "max_latent_frames": d.context,
+            "timestep_shift": 1.0, "hidden_act": "silu", "dtype": "bfloat16"}
+
+
+def _layout(d: Dims):
+    specs = tensor_specs(d)
+    header, off = {}, 0
+    for name, shape in specs:
+        n = int(np.prod(shape)) * 2
+        header[name] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [off, off + n]}
+        off += n
+    header["__metadata__"] = {"format": "mlx", "partition": "ar", "precision": "bfloat16"}
+    raw = json.dumps(header, separators=(",", ":")).encode()
+    raw += b" " * ((8 - (len(raw) % 8)) % 8)
+    return specs, header, raw
+
+
+def _fill_job(args):
+    path, data_start, offset, shape, tidx, seed, std, norm_std, r0, r1 = args
+    bits = tensor_bits(shape, tidx, seed, std, norm_std, rows=(r0, r1) if len(shape) > 1 else None)
+    cols = int(np.prod(shape[1:])) if len(shape) > 1 else 1
+    mm = np.memmap(path, dtype=np.uint16, mode="r+")
+    start = (data_start + offset) // 2 + (r0 * cols if len(shape) > 1 else 0)
+    mm[start:start + bits.size] = bits.reshape(-1)
+    mm.flush()
+    del mm
+    return bits.size
+
+
+def write_converted(directory: str, dims: Dims = PINNED, seed: int = 0, std: float = 0.02,
+                    norm_std: float = 0.0, workers: int | None = None) -> str:
+    """Write config.json, conversion.json and ar-bf16.safetensors under ``directory``."""
+    os.makedirs(directory, exist_ok=True)
+    specs, header, raw = _layout(dims)
+    path = os.path.join(directory, "ar-bf16.safetensors")
+    data_start = 8 + len(raw)
+    total = data_start + max(v["data_offsets"][1] for k, v in header.items() if k != "__metadata__")
+    with open(path, "wb") as f:
+        f.write(np.uint64(len(raw)).tobytes())
+        f.write(raw)
+        f.truncate(total)
+    jobs = []
+    for tidx, (name, shape) in enumerate(specs):
+        off = header[name]["data_offsets"][0]
+        if len(shape) == 1:
+            jobs.append((path, data_start, off, shape, tidx, seed, std, norm_std, 0, 1))
+            continue
+        # One job per group of blocks (~64 MB) keeps the pool busy on the big tables.
+        per = max(1, BLOCK_ELEMS // int(np.prod(shape[1:])))
+        step = per * 8
+        for r0 in range(0, shape[0], step):
+            jobs.append((path, data_start, off, shape, tidx, seed, std, norm_std, r0, min(shape[0], r0 + step)))
+    workers = workers or min(32, os.cpu_count() or 1)
+    if workers > 1 and len(jobs) > 1:
+        with mp.get_context("spawn").Pool(workers) as pool:
+            for _ in pool.imap_unordered(_fill_job, jobs, chunksize=1):
+                pass
+    else:
+        for j in jobs:
+            _fill_job(j)
+    with open(os.path.join(directory, "config.json"), "w") as f:
+        json.dump(config_json(dims), f, indent=1)
+    manifest = {"schema": 1, "format": "lyra-yue2-mlx",
+                "source": {"synthetic": True, "seed": seed, "std": std, "norm_std": norm_std,
+                           "dims": asdict(dims)},
+                "upstream": "synthetic", "conversion": "synthetic",
+                "precisions": {"bf16": {"ar": "ar-bf16.safetensors", "nar": "nar-bf16.safetensors",
+                                        "dtype": "bfloat16"}},
+                "files": {}}
+    with open(os.path.join(directory, "conversion.json"), "w") as f:
+        json.dump(manifest, f, indent=1)
+    return directory
+
+
+def read_safetensors(path: str) -> dict[str, np.ndarray]:
+    """Read a BF16 safetensors file into {name: uint16 array} (memory-mapped)."""
+    with open(path, "rb") as f:
+        n = int(np.frombuffer(f.read(8), dtype=np.uint64)[0])
+        header = json.loads(f.read(n))
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    out = {}
+    for name, rec in header.items():
+        if name == "__metadata__":
+            continue
+        b, e = rec["data_offsets"]
+        out[name] = mm[8 + n + b:8 + n + e].view(np.uint16).reshape(rec["shape"])
+    return out
