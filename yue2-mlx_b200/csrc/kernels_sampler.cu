@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   __shared__ uint64_t cand[kCandCap];
   __shared__ float ev[kCandCap];
   __shared__ int hist256[256];
-  __shared__ int ncand, sel_bin, kth_rem, result;
+  __shared__ int ncand, sel_bin, kth_rem, result, tie_total;
   __shared__ float red_v[32];
   __shared__ int red_i[32];
   __shared__ uint32_t prefix_s;
@@ -178,30 +178,61 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       __syncthreads();
     }
     const float thr = f32_from_order_key(prefix_s);
+    // Survivors in (score desc, index asc) order are the rows strictly above the k-th
+    // value (at most k-1 of them, sorted here) followed by every row equal to it (a tie
+    // group of any size, already in index order, walked implicitly). When the k-th value
+    // is -inf the tie group is empty: only finite rows survive.
+    const bool ties_live = thr > -INFINITY;
+    const int chunk = (n + kSampThreads - 1) / kSampThreads;
+    const int c0 = min(n, tid * chunk), c1 = min(n, c0 + chunk);
     if (tid == 0) ncand = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += kSampThreads) {
+    int my_ties = 0;
+    for (int i = c0; i < c1; ++i) {
       const float v = s[i];
-      if (v >= thr && v > -INFINITY) {
+      if (v > thr) {
         const int slot = atomicAdd(&ncand, 1);
         if (slot < kCandCap) cand[slot] = (uint64_t(~f32_order_key(v)) << 32) | uint32_t(i);
-      } else if (p.write_scores && v < thr) {
+      } else if (v == thr && ties_live) {
+        ++my_ties;
+      } else if (p.write_scores) {
         s[i] = -INFINITY;
       }
     }
+    // Exclusive scan of the per-thread tie counts (tie rank = index order).
+    int incl = my_ties;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) red_i[warp] = incl;
     __syncthreads();
-    const int nc = ncand;
-    if (nc > kCandCap || nc == 0) {
+    if (warp == 0) {
+      int w = red_i[lane];
+      int wi = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+        if (lane >= o) wi += y;
+      }
+      red_i[lane] = wi - w;  // exclusive warp offsets
+      if (lane == 31) tie_total = wi;
+    }
+    __syncthreads();
+    const int tie_before = red_i[warp] + incl - my_ties;
+    const int na = ncand, nt = tie_total;
+    if (na > kCandCap || na + nt == 0) {
       if (tid == 0) {
-        st.error = nc == 0 ? 2 : 1;
-        result = 0;
+        st.error = na + nt == 0 ? 2 : 1;
+        result = -1;
       }
       __syncthreads();
       local = -1;
     } else {
       int np2 = 1;
-      while (np2 < nc) np2 <<= 1;
-      for (int i = nc + tid; i < np2; i += kSampThreads) cand[i] = ~0ull;
+      while (np2 < na) np2 <<= 1;
+      for (int i = na + tid; i < np2; i += kSampThreads) cand[i] = ~0ull;
       __syncthreads();
       // Bitonic sort, ascending keys = (score desc, index asc).
       for (int size = 2; size <= np2; size <<= 1) {
@@ -220,51 +251,85 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
           __syncthreads();
         }
       }
-      const float s0 = s[uint32_t(cand[0])];
-      for (int i = tid; i < nc; i += kSampThreads) ev[i] = yexp(f_sub(s[uint32_t(cand[i])], s0));
+      const float s0 = na > 0 ? s[uint32_t(cand[0])] : thr;
+      for (int i = tid; i < na; i += kSampThreads) ev[i] = yexp(f_sub(s[uint32_t(cand[i])], s0));
       __syncthreads();
       if (tid == 0) {
-        int kept = nc;
+        const float et = yexp(f_sub(thr, s0));
+        int keep_ties = nt;
         if (st.top_p < 1.f) {
           float total = 0.f;
-          for (int i = 0; i < nc; ++i) total = f_add(total, ev[i]);
+          for (int i = 0; i < na; ++i) total = f_add(total, ev[i]);
+          for (int j = 0; j < nt; ++j) total = f_add(total, et);
           float c = 0.f;
-          kept = 0;
-          for (int i = 0; i < nc; ++i) {
+          for (int i = 0; i < na; ++i) {
             const float pi = f_div(ev[i], total);
             c = f_add(c, pi);
-            const bool removed = i >= 1 && f_sub(c, pi) > st.top_p;
-            if (removed) {
-              ev[i] = -1.f;  // marks a removed survivor
-            } else {
-              ++kept;
-            }
+            if (i >= 1 && f_sub(c, pi) > st.top_p) ev[i] = -1.f;  // removed
+          }
+          // Within the tie group p is constant and c - p never decreases, so the kept
+          // ties are a prefix of the group.
+          const float pt = f_div(et, total);
+          keep_ties = 0;
+          for (int j = 0; j < nt; ++j) {
+            c = f_add(c, pt);
+            if (na + j >= 1 && f_sub(c, pt) > st.top_p) break;
+            ++keep_ties;
           }
         }
         const float u = step_uniform((uint64_t(st.seed_hi) << 32) | st.seed_lo, uint32_t(step), st.stream);
         float total = 0.f;
-        for (int i = 0; i < nc; ++i)
+        for (int i = 0; i < na; ++i)
           if (ev[i] >= 0.f) total = f_add(total, ev[i]);
+        for (int j = 0; j < keep_ties; ++j) total = f_add(total, et);
         const float target = f_mul(u, total);
         float acc = 0.f;
-        int pick = -1, last = -1;
-        for (int i = 0; i < nc; ++i) {
+        int pick = -1, last = -1;  // >= 0: candidate slot; <= -2: tie rank -(pick+2)
+        for (int i = 0; i < na && pick == -1; ++i) {
           if (ev[i] < 0.f) continue;
           last = i;
           acc = f_add(acc, ev[i]);
-          if (target < acc) {
-            pick = i;
-            break;
-          }
+          if (target < acc) pick = i;
         }
-        if (pick < 0) pick = last;
-        result = int(uint32_t(cand[pick]));
-        (void)kept;
+        for (int j = 0; j < keep_ties && pick == -1; ++j) {
+          last = -(j + 2);
+          acc = f_add(acc, et);
+          if (target < acc) pick = -(j + 2);
+        }
+        if (pick == -1) pick = last;
+        sel_bin = pick;
+        kth_rem = keep_ties;
+        result = pick >= 0 ? int(uint32_t(cand[pick])) : -1;
       }
       __syncthreads();
-      if (p.write_scores)
-        for (int i = tid; i < nc; i += kSampThreads)
+      const int pick = sel_bin, keep_ties = kth_rem;
+      if (pick <= -2) {
+        // The chosen tie has rank -(pick+2) in index order: the thread whose chunk holds
+        // that rank finds it.
+        const int rank = -(pick + 2);
+        if (rank >= tie_before && rank < tie_before + my_ties) {
+          int r = tie_before;
+          for (int i = c0; i < c1; ++i)
+            if (s[i] == thr) {
+              if (r == rank) result = i;
+              ++r;
+            }
+        }
+      }
+      if (p.write_scores) {
+        for (int i = tid; i < na; i += kSampThreads)
           if (ev[i] < 0.f) s[uint32_t(cand[i])] = -INFINITY;
+        __syncthreads();
+        if (keep_ties < nt) {
+          int r = tie_before;
+          for (int i = c0; i < c1; ++i)
+            if (s[i] == thr) {
+              if (r >= keep_ties) s[i] = -INFINITY;
+              ++r;
+            }
+        }
+      }
+      __syncthreads();
       local = result;
     }
   }

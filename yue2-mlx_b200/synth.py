@@ -21,7 +21,7 @@ norm-weight rounding point is exercised).
 from __future__ import annotations
 
 import json
-import multiprocessing as mp
+from concurrent.futures import ThreadPoolExecutor
 import os
 from dataclasses import asdict, dataclass
 
@@ -190,10 +190,12 @@ def write_converted(directory: str, dims: Dims = PINNED, seed: int = 0, std: flo
         step = per * 8
         for r0 in range(0, shape[0], step):
             jobs.append((path, data_start, off, shape, tidx, seed, std, norm_std, r0, min(shape[0], r0 + step)))
+    # Threads, not processes: numpy's generators and ufunc loops release the GIL, and a
+    # thread pool needs no importable worker module (callers load this file by path).
     workers = workers or min(32, os.cpu_count() or 1)
     if workers > 1 and len(jobs) > 1:
-        with mp.get_context("spawn").Pool(workers) as pool:
-            for _ in pool.imap_unordered(_fill_job, jobs, chunksize=1):
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            for _ in pool.map(_fill_job, jobs):
                 pass
     else:
         for j in jobs:
