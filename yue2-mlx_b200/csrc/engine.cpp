@@ -151,10 +151,10 @@ static void project(const Model &m, Session &s, const bf16 *in, int in_stride, i
                     bf16 *out) {
   const PhaseRows pr = phase_rows(m.d, phase);
   launch_gemv(m.lm_head + size_t(pr.row0) * m.d.hidden, pr.n_main, m.d.hidden, in, in_stride, m.final_norm,
-              m.d.eps, out, s.logit_stride, kEpiStore, n_rows, nullptr, m.sm_count, s.stream);
+              m.d.eps, out, s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, s.stream);
   if (pr.extra >= 0)
     launch_gemv(m.lm_head + size_t(pr.extra) * m.d.hidden, 1, m.d.hidden, in, in_stride, m.final_norm, m.d.eps,
-                out + pr.n_main, s.logit_stride, kEpiStore, n_rows, nullptr, m.sm_count, s.stream);
+                out + pr.n_main, s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, s.stream);
 }
 
 void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int chunk,
@@ -208,13 +208,13 @@ static void decode_forward(Session &s, int n_rows, int phase) {
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
     launch_gemv(w.qkv, d.qkv_rows(), d.hidden, s.x, d.hidden, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows,
-                nullptr, m.sm_count, st);
+                s.d_error, m.sm_count, st);
     launch_attn_decode(m, s, l, n_rows, st);
     launch_gemv(w.o, d.hidden, d.qdim(), s.attn, d.qdim(), nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows,
-                nullptr, m.sm_count, st);
-    launch_gemv(w.gu, 2 * d.ffn, d.hidden, s.x, d.hidden, w.ln2, d.eps, s.mlp, d.ffn, kEpiSwiGLU, n_rows, nullptr,
+                s.d_error, m.sm_count, st);
+    launch_gemv(w.gu, 2 * d.ffn, d.hidden, s.x, d.hidden, w.ln2, d.eps, s.mlp, d.ffn, kEpiSwiGLU, n_rows, s.d_error,
                 m.sm_count, st);
-    launch_gemv(w.down, d.hidden, d.ffn, s.mlp, d.ffn, nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows, nullptr,
+    launch_gemv(w.down, d.hidden, d.ffn, s.mlp, d.ffn, nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows, s.d_error,
                 m.sm_count, st);
   }
   project(m, s, s.x, d.hidden, n_rows, phase, s.logits);

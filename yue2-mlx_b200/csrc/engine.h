@@ -84,9 +84,10 @@ struct Session;
 
 // Kernel launchers (kernels_*.cu). All run on `stream`.
 void launch_embed_rows(const Model &m, Session &s, int n_rows, cudaStream_t st);
+// `error` (device int) enables the bulk-copy kernel, which reports expired waits there.
 void launch_gemv(const bf16 *W, int N, int K, const bf16 *in, int in_stride, const bf16 *norm_w,
                  float eps, bf16 *out, int out_stride, int epilogue, int n_rows,
-                 const int *row_active, int sm_count, cudaStream_t st);
+                 int *error, int sm_count, cudaStream_t st);
 void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st);
 void launch_sampler(const Model &m, Session &s, int n_requests, cudaStream_t st);
 // Prefill (T tokens of one row).
@@ -103,6 +104,7 @@ void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int sta
 void configure_gemv_kernels();
 void configure_gemm_kernels();
 void configure_attn_kernels();
+void configure_gemv_tma_kernels();
 
 enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
 

@@ -51,7 +51,7 @@ __device__ __forceinline__ int local_to_native(int loc, int phase) {
 __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   __shared__ uint64_t cand[kCandCap];
   __shared__ float ev[kCandCap];
-  __shared__ int hist256[256];
+  __shared__ int hist[4096];
   __shared__ int ncand, sel_bin, kth_rem, result, tie_total;
   __shared__ float red_v[32];
   __shared__ int red_i[32];
@@ -150,29 +150,69 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       for (int i = tid; i < n; i += kSampThreads) s[i] = f_div(s[i], st.temperature);
       __syncthreads();
     }
-    // k-th largest value by 8-bit radix select on order-preserving keys.
+    // k-th largest value: radix select on order-preserving keys, digits of 12, 12 and 8
+    // bits from the top; histogram updates are aggregated per warp (lanes with the same
+    // bin add once) and the bin holding the k-th key is found by a block-wide scan.
     const int k = min(st.top_k, n);
     if (tid == 0) {
       prefix_s = 0;
       kth_rem = k;
     }
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += kSampThreads) hist256[b] = 0;
+    __syncthreads();
+    const int shifts[3] = {20, 8, 0}, widths[3] = {12, 12, 8};
+    for (int pass = 0; pass < 3; ++pass) {
+      const int shift = shifts[pass], nb = 1 << widths[pass];
+      for (int b = tid; b < nb; b += kSampThreads) hist[b] = 0;
       __syncthreads();
       const uint32_t pre = prefix_s;
-      const uint32_t hmask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      for (int i = tid; i < n; i += kSampThreads) {
-        const uint32_t key = f32_order_key(s[i]);
-        if ((key & hmask) == (pre & hmask)) atomicAdd(&hist256[(key >> shift) & 255], 1);
+      const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + widths[pass]));
+      for (int base = warp * 32; base < n; base += kSampThreads) {
+        const int i = base + lane;
+        uint32_t bin = 0xFFFFFFFFu;
+        if (i < n) {
+          const uint32_t key = f32_order_key(s[i]);
+          if ((key & hmask) == (pre & hmask)) bin = (key >> shift) & uint32_t(nb - 1);
+        }
+        const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
+        if (bin != 0xFFFFFFFFu && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
       }
       __syncthreads();
-      if (tid == 0) {
-        int rem = kth_rem, b = 255;
-        for (; b > 0; --b) {
-          if (hist256[b] >= rem) break;
-          rem -= hist256[b];
+      // Counts from the top bin down: thread t owns bins [nb-1-per*(t+1)+1, nb-1-per*t].
+      const int per = (nb + kSampThreads - 1) / kSampThreads;
+      const int hi = nb - 1 - per * tid;
+      int mine = 0;
+      for (int j = 0; j < per; ++j)
+        if (hi - j >= 0) mine += hist[hi - j];
+      int incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (lane == 31) red_i[warp] = incl;
+      __syncthreads();
+      if (warp == 0) {
+        const int w = red_i[lane];
+        int wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+          if (lane >= o) wi += y;
         }
-        kth_rem = rem;
+        red_i[lane] = wi - w;
+      }
+      __syncthreads();
+      const int before = red_i[warp] + incl - mine;  // keys in bins above this thread's bins
+      const int rem = kth_rem;
+      __syncthreads();
+      if (before < rem && before + mine >= rem) {
+        int acc = before, b = hi;
+        for (int j = 0; j < per && hi - j >= 0; ++j) {
+          b = hi - j;
+          if (acc + hist[b] >= rem) break;
+          acc += hist[b];
+        }
+        kth_rem = rem - acc;
         prefix_s = pre | (uint32_t(b) << shift);
       }
       __syncthreads();

@@ -218,6 +218,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     configure_gemv_kernels();
     configure_gemm_kernels();
     configure_attn_kernels();
+    configure_gemv_tma_kernels();
     size_t off = 0;
     auto take = [&](size_t bytes) {
       const size_t o = off;
