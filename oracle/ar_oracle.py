@@ -82,12 +82,15 @@ def rope_cos_sin(positions, head_dim: int, theta: float):
 class OracleAR:
     """The AR decoder on float32 arrays, with BF16 rounding points when ``bf16``."""
 
-    def __init__(self, tensors: dict, dims, bf16: bool = True):
+    def __init__(self, tensors: dict, dims, bf16: bool = True, prerounded: bool = False):
         self.d = dims
         self.bf16 = bf16
         self.w = {}
         for name, value in tensors.items():
             a = np.asarray(value)
+            if prerounded:  # float32 arrays already holding BF16 values (kept as given)
+                self.w[name] = a
+                continue
             if a.dtype == np.uint16:
                 self.w[name] = bf16_from_bits(a)  # already BF16 values
                 continue
