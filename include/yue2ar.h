@@ -87,6 +87,12 @@ int yar_session_create(yar_model *model, int max_rows, int max_ctx, int page_tok
                        yar_session **out);
 int yar_session_free(yar_session *session);
 
+/* Session options. YAR_OPT_PERSISTENT (default 1): run each decode forward of one or two
+ * rows as the single persistent kernel when the model's shapes allow it; 0 selects one
+ * kernel per operation (same arithmetic, identical results). */
+enum { YAR_OPT_PERSISTENT = 1 };
+int yar_session_set_option(yar_session *session, int option, int value);
+
 /* generate_tokens — native/src/sampling.cpp:185-288 (upstream sampling.py:57-154): prefill
  * of `prefix` (and of `negative` when cfg_scale != 1), then up to max_tokens sampled
  * tokens. `out_tokens` receives native ids without the end token (capacity max_tokens);

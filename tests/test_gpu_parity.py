@@ -340,3 +340,34 @@ def test_pinned_width_two_layers_vs_oracle(yar, wide2):
             assert np.mean(mine != theirs) <= 0.005, name
             assert rel_l2(mine, theirs) <= 1e-4, name
         s.close()
+
+
+def _trace(model, rows, prompt, forced, persistent):
+    s = model.session(max_rows=2, max_ctx=400)
+    s.set_persistent(persistent)
+    for r in range(rows):
+        s.reset(r, 400)
+        s.prefill(r, prompt[r], phase=None)
+    out = [[s.logits(r, None)] for r in range(rows)]
+    for t in forced:
+        s.step(list(range(rows)), [t] * rows, phase=None)
+        for r in range(rows):
+            out[r].append(s.logits(r, None))
+    kv = s.kv(0, 1, 0, len(prompt[0]) + len(forced))
+    s.close()
+    return np.array(out), kv
+
+
+@pytest.mark.parametrize("rows", [1, 2])
+def test_persistent_decode_matches_per_operation_kernels(yar, wide2, rows):
+    """The single persistent decode kernel and the one-kernel-per-operation path run the
+    same device code: logits and caches must be identical bits."""
+    model, _ = wide2
+    rng = np.random.default_rng(9)
+    prompt = [rng.integers(0, 4096, 200).tolist(), rng.integers(0, 4096, 37).tolist()]
+    forced = rng.integers(0, 4096, 12).tolist()
+    a, kva = _trace(model, rows, prompt, forced, persistent=True)
+    b, kvb = _trace(model, rows, prompt, forced, persistent=False)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(kva[0], kvb[0])
+    np.testing.assert_array_equal(kva[1], kvb[1])

@@ -71,6 +71,7 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_model_dims": (I, [P, ctypes.POINTER(ctypes.c_int64)]),
         "yar_session_create": (I, [P, I, I, I, ctypes.POINTER(P)]),
         "yar_session_free": (I, [P]),
+        "yar_session_set_option": (I, [P, I, I]),
         "yar_generate": (I, [P, i32p, I, ctypes.POINTER(_Sampling), U64, I, i32p, I, D, I, CANCEL_FN, P,
                              TOKEN_FN, P, i32p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.c_char_p,
                              ctypes.c_size_t]),
@@ -195,6 +196,10 @@ class Session:
             self.close()
         except Exception:
             pass
+
+    def set_persistent(self, on: bool):
+        """Decode forward as one persistent kernel (default) or one kernel per operation."""
+        _check(lib.yar_session_set_option(self._h, 1, int(bool(on))))
 
     def reset(self, row: int, capacity: int):
         _check(lib.yar_row_reset(self._h, row, capacity))

@@ -124,6 +124,16 @@ int yar_session_free(yar_session *session) {
   });
 }
 
+int yar_session_set_option(yar_session *session, int option, int value) {
+  return guarded([&] {
+    need(session, "session is required");
+    if (option == YAR_OPT_PERSISTENT)
+      session->s->use_persistent = value != 0;
+    else
+      throw yar::Error("ValueError", "unknown session option");
+  });
+}
+
 int yar_generate(yar_session *session, const int32_t *prefix, int n_prefix, const yar_sampling *sampling,
                  uint64_t seed, int phase, const int32_t *negative, int n_negative, double cfg_scale,
                  int legacy_off, yar_cancel_fn cancel, void *cancel_ctx, yar_token_fn on_token, void *token_ctx,

@@ -92,6 +92,11 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     s->d_out_tokens = dmalloc<int32_t>(size_t(max_rows) * s->out_cap);
     s->d_scores = dmalloc<float>(size_t(max_rows) * s->logit_stride);
     YAR_CUDA(cudaMallocHost(&s->h_pinned, 1 << 20));
+    s->n_ctr = 2 + 5 * d.layers;
+    s->d_ctr = dmalloc<int>(s->n_ctr);
+    s->d_epoch = dmalloc<int>(1);
+    YAR_CUDA(cudaMemset(s->d_ctr, 0, s->n_ctr * sizeof(int)));
+    YAR_CUDA(cudaMemset(s->d_epoch, 0, sizeof(int)));
     YAR_CUDA(cudaStreamSynchronize(s->stream));
   } catch (...) {
     delete s;
@@ -109,7 +114,7 @@ void free_session(Session *s) {
                                                s->d_token, s->d_active, s->d_error, s->x, s->qkv, s->attn,
                                                s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
                                                s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
-                                               s->d_out_tokens, s->d_scores})
+                                               s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -200,10 +205,28 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
 
 // One decode forward of rows [0, n_rows): embed -> 28 x (QKV, attention, O, gate/up, down)
 // -> LM head. Inactive rows are skipped by the embed/attention kernels.
+static bool use_persistent(Session &s, int n_rows) {
+  if (!s.use_persistent || n_rows < 1 || n_rows > 2) return false;
+  if (s.persistent_ok[n_rows] < 0) s.persistent_ok[n_rows] = persistent_supported(*s.m, n_rows) ? 1 : 0;
+  return s.persistent_ok[n_rows] == 1;
+}
+
+// Zero the persistent kernel's operation counters and step epoch (and the split-KV
+// arrival counts) before a sequence of decode steps.
+static void reset_step_sync(Session &s) {
+  YAR_CUDA(cudaMemsetAsync(s.d_ctr, 0, s.n_ctr * sizeof(int), s.stream));
+  YAR_CUDA(cudaMemsetAsync(s.d_epoch, 0, sizeof(int), s.stream));
+  YAR_CUDA(cudaMemsetAsync(s.attn_count, 0, size_t(s.max_rows) * s.m->d.kv_heads * sizeof(int), s.stream));
+}
+
 static void decode_forward(Session &s, int n_rows, int phase) {
   const Model &m = *s.m;
   const Dims &d = m.d;
   cudaStream_t st = s.stream;
+  if (use_persistent(s, n_rows)) {
+    launch_decode_persistent(m, s, n_rows, phase, st);
+    return;
+  }
   launch_embed_rows(m, s, n_rows, st);
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
@@ -239,6 +262,7 @@ void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int ph
   cudaStream_t st = s.stream;
   YAR_CUDA(cudaMemcpyAsync(s.d_active, active.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
   YAR_CUDA(cudaMemcpyAsync(s.d_token, tok.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
+  reset_step_sync(s);
   decode_forward(s, hi, phase);
   YAR_CUDA(cudaStreamSynchronize(st));
   int err = 0;
@@ -250,8 +274,9 @@ void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int ph
 // The per-token step (sampler, then the forward of the sampled token), captured once
 // per (rows, requests, phase) and replayed.
 static cudaGraphExec_t step_graph(Session &s, int n_rows, int n_requests, int phase) {
+  const int pers = use_persistent(s, n_rows) ? 1 : 0;
   for (auto &g : s.graphs)
-    if (g.rows == n_rows && g.requests == n_requests && g.phase == phase) return g.exec;
+    if (g.rows == n_rows && g.requests == n_requests && g.phase == phase && g.persistent == pers) return g.exec;
   cudaStream_t st = s.stream;
   YAR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
   cudaGraph_t graph;
@@ -266,7 +291,7 @@ static cudaGraphExec_t step_graph(Session &s, int n_rows, int n_requests, int ph
   cudaGraphExec_t exec;
   YAR_CUDA(cudaGraphInstantiate(&exec, graph, 0));
   YAR_CUDA(cudaGraphDestroy(graph));
-  s.graphs.push_back({n_rows, n_requests, phase, exec});
+  s.graphs.push_back({n_rows, n_requests, phase, pers, exec});
   return exec;
 }
 
@@ -350,6 +375,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
   std::vector<int> act(rows, 1);
   YAR_CUDA(cudaMemcpyAsync(s.d_active, act.data(), rows * sizeof(int), cudaMemcpyHostToDevice, st));
   YAR_CUDA(cudaMemsetAsync(s.d_error, 0, sizeof(int), st));
+  reset_step_sync(s);
   YAR_CUDA(cudaStreamSynchronize(st));
   cudaGraphExec_t exec = step_graph(s, rows, 1, phase);
 

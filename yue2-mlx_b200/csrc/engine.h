@@ -55,6 +55,7 @@ struct Model {
   size_t arena_bytes = 0;
   const bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
   std::vector<LayerWeights> layers;
+  LayerWeights *d_layers = nullptr;  // device copy of `layers` (persistent decode kernel)
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
 };
 
@@ -105,6 +106,9 @@ void configure_gemv_kernels();
 void configure_gemm_kernels();
 void configure_attn_kernels();
 void configure_gemv_tma_kernels();
+void configure_persistent_kernels();
+bool persistent_supported(const Model &m, int n_rows);
+void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
 
 enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
 
@@ -147,11 +151,17 @@ struct Session {
   uint64_t *d_cand = nullptr;  // [max_requests][kCandCap]
   // Captured decode steps keyed by (rows, requests, phase).
   struct Graph {
-    int rows, requests, phase;
+    int rows, requests, phase, persistent;
     cudaGraphExec_t exec;
   };
   std::vector<Graph> graphs;
   int *h_pinned = nullptr;  // pinned staging for small D2H reads
+  // Persistent decode kernel: operation counters and the completed-step epoch.
+  bool use_persistent = true;
+  int persistent_ok[3] = {-1, -1, -1};  // per row count: unknown / no / yes
+  int *d_ctr = nullptr;
+  int *d_epoch = nullptr;
+  int n_ctr = 0;
 };
 
 constexpr int kCandCap = 2048;

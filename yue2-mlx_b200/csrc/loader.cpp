@@ -219,6 +219,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     configure_gemm_kernels();
     configure_attn_kernels();
     configure_gemv_tma_kernels();
+    configure_persistent_kernels();
     size_t off = 0;
     auto take = [&](size_t bytes) {
       const size_t o = off;
@@ -322,6 +323,8 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
       m->layers[i] = LayerWeights{at(lo[i].qkv), at(lo[i].o), at(lo[i].gu), at(lo[i].down),
                                   at(lo[i].ln1), at(lo[i].ln2), at(lo[i].qn), at(lo[i].kn)};
     }
+    YAR_CUDA(cudaMalloc(&m->d_layers, sizeof(LayerWeights) * d.layers));
+    YAR_CUDA(cudaMemcpy(m->d_layers, m->layers.data(), sizeof(LayerWeights) * d.layers, cudaMemcpyHostToDevice));
     m->embed = at(o_embed);
     m->lm_head = at(o_head);
     m->final_norm = at(o_norm);
@@ -356,6 +359,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     ::close(fd);
   } catch (...) {
     if (m->arena) cudaFree(m->arena);
+    if (m->d_layers) cudaFree(m->d_layers);
     delete m;
     throw;
   }
@@ -366,6 +370,7 @@ void free_model(Model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
   if (m->arena) cudaFree(m->arena);
+  if (m->d_layers) cudaFree(m->d_layers);
   delete m;
 }
 
