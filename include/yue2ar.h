@@ -89,9 +89,14 @@ int yar_session_free(yar_session *session);
 
 /* Session options. YAR_OPT_PERSISTENT (default 1): run each decode forward of one or two
  * rows as the single persistent kernel when the model's shapes allow it; 0 selects one
- * kernel per operation (same arithmetic, identical results). */
-enum { YAR_OPT_PERSISTENT = 1 };
+ * kernel per operation (same arithmetic, identical results). YAR_OPT_TRACE (default 0):
+ * record the persistent kernel's timeline (per CTA and operation, 8 globaltimer stamps
+ * in ns: wait done, activations staged, stages consumed, signalled, producer first/last
+ * issue), overwritten by every step; read it with yar_session_trace. */
+enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2 };
 int yar_session_set_option(yar_session *session, int option, int value);
+/* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64) to host. */
+int yar_session_trace(yar_session *session, uint64_t *out, size_t n, size_t *n_written);
 
 /* generate_tokens — native/src/sampling.cpp:185-288 (upstream sampling.py:57-154): prefill
  * of `prefix` (and of `negative` when cfg_scale != 1), then up to max_tokens sampled

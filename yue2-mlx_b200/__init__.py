@@ -72,6 +72,7 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_session_create": (I, [P, I, I, I, ctypes.POINTER(P)]),
         "yar_session_free": (I, [P]),
         "yar_session_set_option": (I, [P, I, I]),
+        "yar_session_trace": (I, [P, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
         "yar_generate": (I, [P, i32p, I, ctypes.POINTER(_Sampling), U64, I, i32p, I, D, I, CANCEL_FN, P,
                              TOKEN_FN, P, i32p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.c_char_p,
                              ctypes.c_size_t]),
@@ -200,6 +201,18 @@ class Session:
     def set_persistent(self, on: bool):
         """Decode forward as one persistent kernel (default) or one kernel per operation."""
         _check(lib.yar_session_set_option(self._h, 1, int(bool(on))))
+
+    def set_trace(self, on: bool):
+        """Record the persistent decode kernel's per-CTA timeline (see ``trace``)."""
+        _check(lib.yar_session_set_option(self._h, 2, int(bool(on))))
+
+    def trace(self) -> np.ndarray:
+        """Last step's timeline: [sm][5 * layers + 1][8] globaltimer stamps in ns."""
+        d = self.model.dims
+        out = np.zeros(d["sms"] * (5 * d["layers"] + 1) * 8, np.uint64)
+        n = ctypes.c_size_t()
+        _check(lib.yar_session_trace(self._h, _ptr(out, ctypes.c_uint64), out.size, ctypes.byref(n)))
+        return out.reshape(d["sms"], 5 * d["layers"] + 1, 8)
 
     def reset(self, row: int, capacity: int):
         _check(lib.yar_row_reset(self._h, row, capacity))

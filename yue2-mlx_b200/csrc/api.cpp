@@ -127,10 +127,39 @@ int yar_session_free(yar_session *session) {
 int yar_session_set_option(yar_session *session, int option, int value) {
   return guarded([&] {
     need(session, "session is required");
-    if (option == YAR_OPT_PERSISTENT)
-      session->s->use_persistent = value != 0;
-    else
+    auto &s = *session->s;
+    if (option == YAR_OPT_PERSISTENT) {
+      s.use_persistent = value != 0;
+    } else if (option == YAR_OPT_TRACE) {
+      YAR_CUDA(cudaSetDevice(s.m->device));
+      YAR_CUDA(cudaStreamSynchronize(s.stream));
+      if (s.d_trace) cudaFree(s.d_trace);
+      s.d_trace = nullptr;
+      s.trace_elems = 0;
+      for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old pointer
+      s.graphs.clear();
+      if (value) {
+        s.trace_elems = size_t(s.m->sm_count) * (5 * s.m->d.layers + 1) * 8;
+        YAR_CUDA(cudaMalloc(&s.d_trace, s.trace_elems * sizeof(unsigned long long)));
+        YAR_CUDA(cudaMemset(s.d_trace, 0, s.trace_elems * sizeof(unsigned long long)));
+      }
+    } else {
       throw yar::Error("ValueError", "unknown session option");
+    }
+  });
+}
+
+int yar_session_trace(yar_session *session, uint64_t *out, size_t n, size_t *n_written) {
+  return guarded([&] {
+    need(session && out && n_written, "missing argument");
+    auto &s = *session->s;
+    *n_written = 0;
+    if (!s.d_trace) return;
+    YAR_CUDA(cudaSetDevice(s.m->device));
+    YAR_CUDA(cudaStreamSynchronize(s.stream));
+    const size_t k = n < s.trace_elems ? n : s.trace_elems;
+    YAR_CUDA(cudaMemcpy(out, s.d_trace, k * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    *n_written = k;
   });
 }
 

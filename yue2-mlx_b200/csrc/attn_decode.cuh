@@ -117,17 +117,83 @@ struct DecodeAttnParams {
 
 template <int D, int G>
 struct AttnSmem {
-  static constexpr int NW = kAttnThreads / 32, LPP = D / 8, PPW = 32 / LPP, kMaxPages = 128, MS = 64;
+  static constexpr int NW = kAttnThreads / 32, LPP = D / 8, PPW = 32 / LPP, MS = 64;
   float q_s[G][D];
   float knew[D], vnew[D];
   float m_s[NW][PPW][G], l_s[NW][PPW][G];
   float o_s[NW * PPW][G][D];
-  float qn_s[D], kn_s[D];
-  int ptab_s[kMaxPages];
   float wsplit[G][MS];
   float inv_l[G];
   int last_flag;
 };
+
+// Per-step state of one row, staged in shared memory once: activity, the position being
+// decoded, its RoPE cos/sin, and the page table.
+template <int D>
+struct AttnRow {
+  static constexpr int kMaxPages = 128;
+  int active, pos;
+  float cosr[D / 2], sinr[D / 2];
+  int ptab[kMaxPages];
+};
+
+// Fill `rs` for `row` with `nthreads` threads starting at thread `tid`; the caller
+// synchronizes afterwards. Tables longer than kMaxPages stay in global memory.
+template <int D>
+__device__ void attn_row_load(AttnRow<D> &rs, const DecodeAttnParams &p, int row, int tid, int nthreads) {
+  const int pos = __ldcg(p.cur_pos + row);
+  if (tid == 0) {
+    rs.active = __ldcg(p.active + row);
+    rs.pos = pos;
+  }
+  for (int i = tid; i < D / 2; i += nthreads) {
+    rs.cosr[i] = p.cos_tab[size_t(pos) * (D / 2) + i];
+    rs.sinr[i] = p.sin_tab[size_t(pos) * (D / 2) + i];
+  }
+  const int n = p.g.pages_per_row < AttnRow<D>::kMaxPages ? p.g.pages_per_row : AttnRow<D>::kMaxPages;
+  for (int i = tid; i < n; i += nthreads) rs.ptab[i] = p.page_table[size_t(row) * p.g.pages_per_row + i];
+}
+
+// The split geometry every unit of a row computes identically.
+struct SplitRange {
+  int chunk, n_active, p0, p1;
+};
+__device__ __forceinline__ SplitRange split_range(int L, int max_splits, int split) {
+  SplitRange r;
+  r.chunk = (L + max_splits - 1) / max_splits;
+  r.chunk = max(64, (r.chunk + 15) & ~15);
+  r.n_active = (L + r.chunk - 1) / r.chunk;
+  r.p0 = split * r.chunk;
+  r.p1 = min(L, r.p0 + r.chunk);
+  return r;
+}
+
+template <int D>
+__device__ __forceinline__ bf16 *kv_row_ptr(const DecodeAttnParams &p, const AttnRow<D> &rs, int row, int layer,
+                                           int kv, int kvh, int q) {
+  const AttnGeom &g = p.g;
+  const int lp = q / g.page_tokens;
+  const int page = lp < AttnRow<D>::kMaxPages ? rs.ptab[lp] : p.page_table[size_t(row) * g.pages_per_row + lp];
+  const size_t blk = (size_t(layer) * g.num_pages + page) * 2 + kv;
+  return p.pool + blk * g.page_elems + (size_t(kvh) * g.page_tokens + q % g.page_tokens) * D;
+}
+
+// Ask L2 to fetch the cached K/V lines a unit will read (positions before the new one),
+// so the unit's loads hit L2 instead of queueing behind the weight stream.
+template <int D>
+__device__ void attn_prefetch_kv(const DecodeAttnParams &p, const AttnRow<D> &rs, int row, int layer, int kvh,
+                                 int split, int tid, int nthreads) {
+  if (!rs.active) return;
+  const SplitRange r = split_range(rs.pos + 1, p.max_splits, split);
+  if (split >= r.n_active) return;
+  const int pend = min(r.p1, rs.pos);
+  constexpr int LINES = D * 2 / 128;  // 128-byte lines per position and tensor
+  for (int i = tid; i < (pend - r.p0) * 2 * LINES; i += nthreads) {
+    const int q = r.p0 + i / (2 * LINES), kv = (i / LINES) & 1, ln = i % LINES;
+    const char *a = reinterpret_cast<const char *>(kv_row_ptr<D>(p, rs, row, layer, kv, kvh, q)) + ln * 128;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+  }
+}
 
 __device__ __forceinline__ void team_sync(int bar_id) {
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "n"(kAttnThreads) : "memory");
@@ -175,57 +241,64 @@ __device__ void attn_merge(const DecodeAttnParams &p, AttnSmem<D, G> &sm, const 
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
 }
 
+// q/k RMSNorm (modeling_yue2.py:185) then half-split RoPE (:152-156) of one head held
+// in registers, lane l owning dims l, l+32, ...: the RoPE pairs (d, d + D/2) are in the
+// same lane. Same arithmetic and order as norm_rope_head_s.
+template <int D>
+__device__ __forceinline__ void norm_rope_regs(float (&v)[D / 32], const float (&w)[D / 32], const float *cosr,
+                                               const float *sinr, float eps, int lane) {
+  constexpr int NPL = D / 32, HALF = NPL / 2;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) ss += v[i] * v[i];
+  ss = warp_sum(ss);
+  const float scale = rms_scale_bf16(ss, D, eps);
+  float nv[NPL];
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) nv[i] = rbf(rbf(v[i] * scale) * w[i]);
+#pragma unroll
+  for (int i = 0; i < HALF; ++i) {
+    const int d = lane + 32 * i;
+    const float c = cosr[d], sn = sinr[d];
+    v[i] = rbf(rbf(nv[i] * c) - rbf(nv[i + HALF] * sn));
+    v[i + HALF] = rbf(rbf(nv[i + HALF] * c) + rbf(nv[i] * sn));
+  }
+}
+
+__device__ __forceinline__ void attn_stamp(unsigned long long *st, int k, int tid) {
+  if (st && tid == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    st[k] = t;
+  }
+}
+
 // One unit. Returns true when this unit merged (row, kvh) (its outputs are written).
+// Dependent memory round trips: (1) the first K/V round (L2 hits when prefetched)
+// together with the raw q/k/v and the q/k norm weights; (2) partial + arrival count;
+// (3) for the last of the n_active units, the split partials for the merge.
+// `st` (optional) receives globaltimer stamps at the unit's checkpoints (slots 3..6).
 template <int D, int G>
-__device__ bool attn_unit(const DecodeAttnParams &p, AttnSmem<D, G> &sm, int row, int kvh, int split, int nsplit,
-                          int tid, int bar_id) {
+__device__ bool attn_unit(const DecodeAttnParams &p, AttnSmem<D, G> &sm, const AttnRow<D> &rs, int row, int kvh,
+                          int split, int tid, int bar_id, unsigned long long *st = nullptr) {
   using S = AttnSmem<D, G>;
-  constexpr int LPP = S::LPP, PPW = S::PPW, NW = S::NW;
+  constexpr int LPP = S::LPP, PPW = S::PPW, NW = S::NW, NPL = D / 32;
+  static_assert(G < NW, "one warp per q head plus one for the new k");
   constexpr int UN = 8;  // positions per lane group per round
   const AttnGeom &g = p.g;
   const int lane = tid & 31, warp = tid >> 5;
   const int grp = lane / LPP, sub = lane % LPP;
 
-  if (!__ldcg(p.active + row)) return false;
-  const int *ptab_g = p.page_table + size_t(row) * g.pages_per_row;
-  const bool ptab_in_smem = g.pages_per_row <= S::kMaxPages;
-  if (ptab_in_smem)
-    for (int i = tid; i < g.pages_per_row; i += kAttnThreads) sm.ptab_s[i] = ptab_g[i];
-  for (int d = tid; d < D; d += kAttnThreads) {
-    sm.qn_s[d] = bf2f(p.qn[d]);
-    sm.kn_s[d] = bf2f(p.kn[d]);
-  }
-  const int pos = __ldcg(p.cur_pos + row);
-  const int L = pos + 1;
-  int chunk = (L + nsplit - 1) / nsplit;
-  chunk = max(64, (chunk + 15) & ~15);
-  const int n_active = (L + chunk - 1) / chunk;
-  const int p0 = split * chunk, p1 = min(L, p0 + chunk);
+  if (!rs.active) return false;
+  const int pos = rs.pos;
+  const SplitRange sr = split_range(pos + 1, p.max_splits, split);
+  const int n_active = sr.n_active;
+  if (split >= n_active) return false;  // beyond the context: no work, no arrival
+  const int p0 = sr.p0, p1 = sr.p1;
   const bool holds_new = p0 <= pos && pos < p1;
   float *part_base = p.part + (size_t(row) * g.heads) * p.max_splits * (D + 2);
-  if (split >= n_active) {
-    // Beyond the context: nothing to read, and the merge never looks at this split.
-    // Only take part in the arrival count.
-    team_sync(bar_id);
-    if (tid == 0) {
-      __threadfence();
-      const int prev = atomicAdd(p.count + row * g.kv_heads + kvh, 1);
-      sm.last_flag = prev == nsplit - 1;
-    }
-    team_sync(bar_id);
-    if (!sm.last_flag) return false;
-    __threadfence();
-    attn_merge<D, G>(p, sm, part_base, kvh, row, n_active, tid, bar_id);
-    return true;
-  }
-  team_sync(bar_id);  // page table and norm weights staged
-  const int *ptab = ptab_in_smem ? sm.ptab_s : ptab_g;
-  auto kv_ptr = [&](int kv, int q) {
-    const int page = ptab[q / g.page_tokens], slot = q % g.page_tokens;
-    const size_t blk = (size_t(p.layer) * g.num_pages + page) * 2 + kv;
-    return p.pool + blk * g.page_elems + (size_t(kvh) * g.page_tokens + slot) * D;
-  };
-  // Issue the first round of K/V loads now; q-norm and RoPE run while they are in flight.
+  auto kv_ptr = [&](int kv, int q) { return kv_row_ptr<D>(p, rs, row, p.layer, kv, kvh, q); };
+  // (1) First K/V round, raw q (and new k, v) and the norm weights.
   const int pend = holds_new ? pos : p1;
   uint4 kr[UN], vr[UN];
   int pp[UN];
@@ -245,29 +318,36 @@ __device__ bool attn_unit(const DecodeAttnParams &p, AttnSmem<D, G> &sm, int row
   };
   int base = p0 + warp * PPW;
   load_round(base);
-
   const bf16 *qkv = p.qkv + size_t(row) * (g.qdim + 2 * g.kvdim);
-  const float *cosr = p.cos_tab + size_t(pos) * (D / 2);
-  const float *sinr = p.sin_tab + size_t(pos) * (D / 2);
-  for (int h = warp; h < G + (holds_new ? 1 : 0); h += NW) {
-    const bool is_k = h == G;
-    const bf16 *src = is_k ? qkv + g.qdim + kvh * D : qkv + (kvh * G + h) * D;
-    float *dst = is_k ? sm.knew : sm.q_s[h];
-    for (int d = lane; d < D; d += 32) dst[d] = bf2f(__ldcg(src + d));
-    __syncwarp();
-    norm_rope_head_s<D>(dst, is_k ? sm.kn_s : sm.qn_s, cosr, sinr, g.eps, lane);
-  }
-  if (holds_new)
-    for (int d = tid; d < D; d += kAttnThreads) sm.vnew[d] = bf2f(__ldcg(qkv + g.qdim + g.kvdim + kvh * D + d));
-  team_sync(bar_id);
-  if (holds_new) {
-    bf16 *kd = kv_ptr(0, pos);
-    bf16 *vd = kv_ptr(1, pos);
-    for (int d = tid; d < D; d += kAttnThreads) {
-      kd[d] = f2bf(sm.knew[d]);
-      vd[d] = f2bf(sm.vnew[d]);
+  const int my_head = warp;  // warps 0..G-1: q heads; warp G: the new k (when held)
+  const bool does_head = my_head < G || (my_head == G && holds_new);
+  if (does_head) {
+    const bool is_k = my_head == G;
+    const bf16 *src = is_k ? qkv + g.qdim + kvh * D : qkv + (kvh * G + my_head) * D;
+    const bf16 *wn = is_k ? p.kn : p.qn;
+    float hv[NPL], vv[NPL], wv[NPL];
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      hv[i] = bf2f(__ldcg(src + lane + 32 * i));
+      wv[i] = bf2f(wn[lane + 32 * i]);
+      if (is_k) vv[i] = bf2f(__ldcg(qkv + g.qdim + g.kvdim + kvh * D + lane + 32 * i));
+    }
+    norm_rope_regs<D>(hv, wv, rs.cosr, rs.sinr, g.eps, lane);
+    float *dst = is_k ? sm.knew : sm.q_s[my_head];
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) dst[lane + 32 * i] = hv[i];
+    if (is_k) {
+      bf16 *kd = kv_ptr(0, pos), *vd = kv_ptr(1, pos);
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        sm.vnew[lane + 32 * i] = vv[i];
+        kd[lane + 32 * i] = f2bf(hv[i]);
+        vd[lane + 32 * i] = f2bf(vv[i]);
+      }
     }
   }
+  team_sync(bar_id);
+  attn_stamp(st, 3, tid);
 
   // Per-lane state: its group's running max/sum per q head and 8 output dims.
   float m[G], l[G], acc[G][8];
@@ -327,6 +407,7 @@ __device__ bool attn_unit(const DecodeAttnParams &p, AttnSmem<D, G> &sm, int row
     consume(grp == 0 ? pos : -1, kf, vf);
   }
 
+  attn_stamp(st, 4, tid);
   // Merge lane groups and warps of this unit.
   const int slot = warp * PPW + grp;
 #pragma unroll
@@ -362,16 +443,20 @@ __device__ bool attn_unit(const DecodeAttnParams &p, AttnSmem<D, G> &sm, int row
       pr[1] = Ls;
     }
   }
-  __threadfence();
+  // (3) Arrival: one release fence after the team barrier covers the team's partial.
   team_sync(bar_id);
   if (tid == 0) {
+    __threadfence();
     const int prev = atomicAdd(p.count + row * g.kv_heads + kvh, 1);
-    sm.last_flag = prev == nsplit - 1;
+    sm.last_flag = prev == n_active - 1;
   }
   team_sync(bar_id);
+  attn_stamp(st, 5, tid);
   if (!sm.last_flag) return false;
   __threadfence();
+  // (4) The last of the n_active units merges them.
   attn_merge<D, G>(p, sm, part_base, kvh, row, n_active, tid, bar_id);
+  attn_stamp(st, 6, tid);
   return true;
 }
 

@@ -114,7 +114,7 @@ void free_session(Session *s) {
                                                s->d_token, s->d_active, s->d_error, s->x, s->qkv, s->attn,
                                                s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
                                                s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
-                                               s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch})
+                                               s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch, s->d_trace})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);

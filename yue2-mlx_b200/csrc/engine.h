@@ -162,6 +162,8 @@ struct Session {
   int *d_ctr = nullptr;
   int *d_epoch = nullptr;
   int n_ctr = 0;
+  unsigned long long *d_trace = nullptr;  // persistent-kernel timeline (when enabled)
+  size_t trace_elems = 0;
 };
 
 constexpr int kCandCap = 2048;

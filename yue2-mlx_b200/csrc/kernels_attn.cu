@@ -32,9 +32,12 @@ static AttnGeom geom(const Model &m, const Session &s) {
 template <int D, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p) {
   __shared__ AttnSmem<D, G> sm;
+  __shared__ AttnRow<D> rs;
   pdl_launch_dependents();
   pdl_wait();
-  attn_unit<D, G>(p, sm, blockIdx.z, blockIdx.x, blockIdx.y, gridDim.y, threadIdx.x, 1);
+  attn_row_load<D>(rs, p, blockIdx.z, threadIdx.x, kAttnThreads);
+  __syncthreads();
+  attn_unit<D, G>(p, sm, rs, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x, 1);
 }
 
 void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st) {
@@ -68,16 +71,12 @@ void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaS
     YAR_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<128, 2>, p));
   else if (m.d.head_dim == 128 && G == 1)
     YAR_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<128, 1>, p));
-  else if (m.d.head_dim == 128 && G == 4)
-    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<128, 4>, p));
   else if (m.d.head_dim == 64 && G == 2)
     YAR_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<64, 2>, p));
   else if (m.d.head_dim == 64 && G == 1)
     YAR_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<64, 1>, p));
-  else if (m.d.head_dim == 64 && G == 4)
-    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<64, 4>, p));
   else
-    throw Error("ValueError", "head_dim must be 64 or 128 and the GQA group 1, 2 or 4");
+    throw Error("ValueError", "head_dim must be 64 or 128 and the GQA group 1 or 2");
 }
 
 // ---------------------------------------------------------------------------------------

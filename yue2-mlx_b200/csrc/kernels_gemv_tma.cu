@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) k_gemv_tma(TmaGemvParams p) {
   bf16 *act = reinterpret_cast<bf16 *>(smem_raw + kTmaStages * kRingStageBytes);  // [NB][K]
   __shared__ __align__(8) uint64_t full[kTmaStages], empty[kTmaStages];
   __shared__ float red[NB * kRingConsumers];
-  __shared__ float rowres[NB * 8];
+  float *gred = reinterpret_cast<float *>(smem_raw + kTmaStages * kRingStageBytes + size_t(NB) * p.t.K * 2);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int g0, g1;
   task_groups(p.t.N, blockIdx.x, gridDim.x, g0, g1);
@@ -64,10 +64,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) k_gemv_tma(TmaGemvParams p) {
   ring_stage_act<NB>(p.t, act, red, threadIdx.x);
   long long it = 0;
   bool bad = false;
-  ring_consume<NB, kTmaStages>(p.t, g0, g1, ring, act, full, empty, it, rowres, p.error, bad, threadIdx.x);
+  ring_consume<NB, kTmaStages>(p.t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, threadIdx.x);
 }
 
-size_t gemv_tma_smem(int NB, int K) { return size_t(kTmaStages) * kRingStageBytes + size_t(NB) * K * 2; }
+size_t gemv_tma_smem(int NB, int K) {
+  return size_t(kTmaStages) * kRingStageBytes + size_t(NB) * K * 2 + size_t(ring_gred_floats(NB)) * 4;
+}
 
 template <int NB, int EPI>
 static void tma_launch(const TmaGemvParams &p, int sm_count, cudaStream_t st) {

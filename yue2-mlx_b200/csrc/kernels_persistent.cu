@@ -43,7 +43,14 @@ struct PersistParams {
   DecodeAttnParams ap;
   int *token, *pos, *cur_pos, *capacity, *active, *error;
   int *ctr, *epoch;
+  unsigned long long *trace;  // optional [cta][op][8] globaltimer stamps (ns), op = 5*layer + k
 };
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
   int v;
@@ -56,11 +63,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int NS = kPersistStages;
   using ASm = AttnSmem<128, 2>;
+  // Layout: ring | act (GEMV activations) aliased with the attention teams' scratch (the
+  // two are never live at once) | group partials.
+  constexpr size_t kActBytes = size_t(NB) * kPersistMaxK * 2;
+  constexpr size_t kUnion = kActBytes > 2 * sizeof(ASm) ? kActBytes : 2 * sizeof(ASm);
   bf16 *ring = reinterpret_cast<bf16 *>(smem_raw);
   bf16 *act = reinterpret_cast<bf16 *>(smem_raw + NS * kRingStageBytes);
-  ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kRingStageBytes + NB * kPersistMaxK * 2);
+  ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kRingStageBytes);
+  float *gred = reinterpret_cast<float *>(smem_raw + NS * kRingStageBytes + kUnion);
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
-  __shared__ float red[NB * kRingConsumers], rowres[NB * 8];
+  __shared__ float red[NB * kRingConsumers];
+  __shared__ AttnRow<128> rowst[NB];
   __shared__ int s_epoch, s_bad;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -94,15 +107,23 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       long long it = 0;
       bool ok = true;
       int g0, g1;
+      const int kop[4] = {0, 2, 3, 4};
+      auto pstamp = [&](int o, int k) {
+        if (p.trace) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = globaltimer();
+      };
       for (int l = 0; l < nL && ok; ++l)
         for (int k = 0; k < 4 && ok; ++k) {
           const GemvTask t = task(l, k);
           task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
+          pstamp(5 * l + kop[k], 4);
           ok = ring_produce<NS>(t, g0, g1, ring, full, empty, it, p.error);
+          pstamp(5 * l + kop[k], 5);
         }
       if (ok) {
         task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
+        pstamp(5 * nL, 4);
         ring_produce<NS>(head, g0, g1, ring, full, empty, it, p.error);
+        pstamp(5 * nL, 5);
       }
       ring_drain<NS>(full, it);
     }
@@ -113,15 +134,22 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   const int ctid = threadIdx.x;
   bool bad = false;
   long long it = 0;
+  auto stamp = [&](int o, int k) {
+    if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = globaltimer();
+  };
   auto unify_bad = [&]() {
     if (bad) s_bad = 1;
     consumer_sync();
     bad = s_bad != 0;
   };
+  // All consumer threads' writes are ordered before thread 0's release fence by the
+  // barrier; one fence + one atomic publishes the CTA's share.
   auto signal = [&](int idx) {
-    __threadfence();
     consumer_sync();
-    if (ctid == 0) atomicAdd(p.ctr + idx, 1);
+    if (ctid == 0) {
+      __threadfence();
+      atomicAdd(p.ctr + idx, 1);
+    }
   };
   // Wait until counter idx reaches target; gives up on expiry or once any CTA failed.
   auto wait_for = [&](int idx, int target) {
@@ -175,78 +203,112 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     signal(c_embed);
   }
   wait_for(c_embed, epoch + 1);
+  // This step's row state (activity, position, cos/sin, page table) for the attention units.
+  for (int b = 0; b < NB; ++b) attn_row_load<128>(rowst[b], p.ap, b, ctid, kRingConsumers * 32);
+  consumer_sync();
 
   const int team = warp / 4, ttid = ctid % kAttnThreads;
+  const int n_units = NB * kvh_n * nsplit;
   for (int l = 0; l < nL; ++l) {
     int g0, g1;
+    // Prefetch into L2 the cached K/V this CTA's attention units will read in this layer.
+    for (int u = blockIdx.x * 2; u < n_units; u += 2 * gridDim.x)
+      for (int tm = 0; tm < 2 && u + tm < n_units; ++tm) {
+        const int uu = u + tm, row = uu / (kvh_n * nsplit), kvh = (uu / nsplit) % kvh_n, split = uu % nsplit;
+        attn_prefetch_kv<128>(p.ap, rowst[row], row, l, kvh, split, ctid, kRingConsumers * 32);
+      }
     // QKV (RMSNorm of x fused).
     {
+      stamp(5 * l, 0);
       const GemvTask t = task(l, 0);
       task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
       ring_stage_act<NB>(t, act, red, ctid);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, rowres, p.error, bad, ctid);
+      stamp(5 * l, 1);
+      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+      stamp(5 * l, 2);
       unify_bad();
       signal(c_op(l, 0));
+      stamp(5 * l, 3);
     }
     // Attention: two 4-warp teams per CTA, units (row, kv head, split) round-robin.
     wait_for(c_op(l, 0), (epoch + 1) * all);
+    stamp(5 * l + 1, 0);
     {
       DecodeAttnParams ap = p.ap;
       ap.layer = l;
       ap.qn = p.layers[l].qn;
       ap.kn = p.layers[l].kn;
-      const int n_units = NB * kvh_n * nsplit;
       for (int u = blockIdx.x * 2 + team; u < n_units; u += 2 * gridDim.x) {
         const int row = u / (kvh_n * nsplit), kvh = (u / nsplit) % kvh_n, split = u % nsplit;
         bool merged = false;
-        if (!bad) merged = attn_unit<128, 2>(ap, team_sm[team], row, kvh, split, nsplit, ttid, 2 + team);
+        unsigned long long *st =
+            (p.trace && team == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
+        if (!bad) merged = attn_unit<128, 2>(ap, team_sm[team], rowst[row], row, kvh, split, ttid, 2 + team, st);
         // An inactive row contributes its kv heads' counts without work (split 0 stands in).
-        const bool count = merged || (split == 0 && (bad || !__ldcg(p.active + row)));
+        const bool count = merged || (split == 0 && (bad || !rowst[row].active));
         if (count) {
-          __threadfence();
           team_sync(2 + team);
-          if (ttid == 0) atomicAdd(p.ctr + c_op(l, 1), 1);
+          if (ttid == 0) {
+            __threadfence();
+            atomicAdd(p.ctr + c_op(l, 1), 1);
+          }
         }
       }
     }
+    stamp(5 * l + 1, 2);
     // O (+ residual).
     wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB);
     {
+      stamp(5 * l + 2, 0);
       const GemvTask t = task(l, 1);
       task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
       ring_stage_act<NB>(t, act, red, ctid);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, rowres, p.error, bad, ctid);
+      stamp(5 * l + 2, 1);
+      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+      stamp(5 * l + 2, 2);
       unify_bad();
       signal(c_op(l, 2));
+      stamp(5 * l + 2, 3);
     }
     // gate/up (RMSNorm of x fused, SwiGLU epilogue).
     wait_for(c_op(l, 2), (epoch + 1) * all);
     {
+      stamp(5 * l + 3, 0);
       const GemvTask t = task(l, 2);
       task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
       ring_stage_act<NB>(t, act, red, ctid);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, rowres, p.error, bad, ctid);
+      stamp(5 * l + 3, 1);
+      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+      stamp(5 * l + 3, 2);
       unify_bad();
       signal(c_op(l, 3));
+      stamp(5 * l + 3, 3);
     }
     // down (+ residual).
     wait_for(c_op(l, 3), (epoch + 1) * all);
     {
+      stamp(5 * l + 4, 0);
       const GemvTask t = task(l, 3);
       task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
       ring_stage_act<NB>(t, act, red, ctid);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, rowres, p.error, bad, ctid);
+      stamp(5 * l + 4, 1);
+      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+      stamp(5 * l + 4, 2);
       unify_bad();
       signal(c_op(l, 4));
+      stamp(5 * l + 4, 3);
     }
     wait_for(c_op(l, 4), (epoch + 1) * all);
   }
   // Final RMSNorm + phase rows of the LM head.
   {
     int g0, g1;
+    stamp(5 * nL, 0);
     task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
     ring_stage_act<NB>(head, act, red, ctid);
-    ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, rowres, p.error, bad, ctid);
+    stamp(5 * nL, 1);
+    ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+    stamp(5 * nL, 2);
     if (p.extra_row >= 0 && blockIdx.x == gridDim.x - 1 && warp < NB && !bad) {
       // The ABC phase's extra row (ABC_END), from the normalized activations in `act`.
       const bf16 *wr = p.head + size_t(p.extra_row - 0) * H;
@@ -278,7 +340,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
 }
 
 size_t persistent_smem(int NB) {
-  return size_t(kPersistStages) * kRingStageBytes + size_t(NB) * kPersistMaxK * 2 + 2 * sizeof(AttnSmem<128, 2>);
+  const size_t act = size_t(NB) * kPersistMaxK * 2, teams = 2 * sizeof(AttnSmem<128, 2>);
+  return size_t(kPersistStages) * kRingStageBytes + (act > teams ? act : teams) + size_t(ring_gred_floats(NB)) * 4;
 }
 
 void configure_persistent_kernels() {
@@ -359,6 +422,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.error = s.d_error;
   p.ctr = s.d_ctr;
   p.epoch = s.d_epoch;
+  p.trace = s.d_trace;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.sm_count);

@@ -14,8 +14,9 @@
 namespace yar {
 
 constexpr int kRingConsumers = 8;
-constexpr int kRingPiece = 2048;                    // BF16 elements per row piece
-constexpr int kRingStageBytes = 8 * kRingPiece * 2;  // 32 KB
+constexpr int kRingPiece = 2048;                      // BF16 elements per row piece
+constexpr int kRingRowPitch = kRingPiece + 8;         // +16 bytes: ldmatrix rows hit distinct banks
+constexpr int kRingStageBytes = 8 * kRingRowPitch * 2;  // 32,896 bytes
 constexpr long long kRingWaitLimit = 1ll << 22;      // try_wait polls before giving up (seconds)
 
 struct GemvTask {
@@ -91,7 +92,7 @@ __device__ bool ring_produce(const GemvTask &t, int g0, int g1, bf16 *ring, uint
       const int r0 = g * 8, nrows = min(8, t.N - r0);
       mbar_arrive_expect_tx(&full[s], unsigned(nrows) * kRingPiece * 2);
       for (int r = 0; r < nrows; ++r)
-        bulk_g2s(ring + (size_t(s) * 8 + r) * kRingPiece, t.W + size_t(r0 + r) * t.K + size_t(ks) * kRingPiece,
+        bulk_g2s(ring + (size_t(s) * 8 + r) * kRingRowPitch, t.W + size_t(r0 + r) * t.K + size_t(ks) * kRingPiece,
                  kRingPiece * 2, &full[s]);
     }
   return true;
@@ -105,21 +106,28 @@ __device__ void ring_drain(uint64_t *full, long long issued) {
 }
 
 // Consumers: the task's activation rows into `act` ([NB][K] BF16), RMSNorm applied when the
-// task has a norm weight (modeling_yue2.py:131-132). `red` holds NB x 8 floats.
+// task has a norm weight (modeling_yue2.py:131-132): x is read once into registers (up to
+// 4 chunks of 8 per thread, K <= 8192), reduced, normalized. `red` holds NB x 8 floats.
 template <int NB>
 __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int ctid) {
+  constexpr int T = kRingConsumers * 32;
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K;
   if (t.norm_w) {
+    uint4 xv[NB][4];
     for (int b = 0; b < NB; ++b) {
       const bf16 *x = t.in + size_t(b) * t.in_stride;
       float ss = 0.f;
-      for (int k = ctid * 8; k < K; k += kRingConsumers * 32 * 8) {
-        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(x + k));
-        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = bf_lo(w4[j]), c = bf_hi(w4[j]);
-          ss += a * a + c * c;
+      for (int j = 0; j < 4; ++j) {
+        const int k = (ctid + j * T) * 8;
+        if (k < K) {
+          xv[b][j] = __ldcg(reinterpret_cast<const uint4 *>(x + k));
+          const uint32_t w4[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a = bf_lo(w4[q]), c = bf_hi(w4[q]);
+            ss += a * a + c * c;
+          }
         }
       }
       ss = warp_sum(ss);
@@ -131,17 +139,18 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
 #pragma unroll
       for (int i = 0; i < kRingConsumers; ++i) tot += red[b * kRingConsumers + i];
       const float scale = rms_scale_bf16(tot, K, t.eps);
-      const bf16 *x = t.in + size_t(b) * t.in_stride;
-      for (int k = ctid * 8; k < K; k += kRingConsumers * 32 * 8) {
-        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(x + k));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int k = (ctid + j * T) * 8;
+        if (k >= K) continue;
         const uint4 wn = ldg16(t.norm_w + k);
-        const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, wv[4] = {wn.x, wn.y, wn.z, wn.w};
+        const uint32_t xq[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w}, wq[4] = {wn.x, wn.y, wn.z, wn.w};
         uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float lo = rbf(rbf(bf_lo(xv[j]) * scale) * bf_lo(wv[j]));
-          const float hi = rbf(rbf(bf_hi(xv[j]) * scale) * bf_hi(wv[j]));
-          o[j] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
+        for (int q = 0; q < 4; ++q) {
+          const float lo = rbf(rbf(bf_lo(xq[q]) * scale) * bf_lo(wq[q]));
+          const float hi = rbf(rbf(bf_hi(xq[q]) * scale) * bf_hi(wq[q]));
+          o[q] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
         }
         *reinterpret_cast<uint4 *>(act + b * K + k) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -149,87 +158,123 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
   } else {
     for (int b = 0; b < NB; ++b) {
       const bf16 *x = t.in + size_t(b) * t.in_stride;
-      for (int c = ctid; c < K / 8; c += kRingConsumers * 32)
+      for (int c = ctid; c < K / 8; c += T)
         *reinterpret_cast<uint4 *>(act + b * K + c * 8) = __ldcg(reinterpret_cast<const uint4 *>(x + c * 8));
     }
   }
   consumer_sync();
 }
 
-// Consumers: consume the task's stages (continuing `it`), apply the epilogue per 8-row
-// group. After a wait expires (`bad`), stages are still released and barriers still
-// taken, without computing. `rowres` holds NB x 8 floats.
+__device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  // A rows 8..15 are zero (a1 = a3 = 0): rows 0..NB-1 carry the activation rows.
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+constexpr int kRingMaxGroups = 32;  // 8-row groups whose partial sums wait for one epilogue
+
+// Bytes of the group-partials buffer ring_consume needs.
+__host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGroups * kRingConsumers * NB * 8; }
+
+// Consumers: consume the task's stages (continuing `it`) and apply the epilogue. Each
+// stage is 8 weight rows x 2048; warp w owns the k range [256w, 256w+256) of every stage
+// and runs tensor-core MMAs with the 8 weight rows as the B operand (n = 8, read by
+// ldmatrix straight from the ring) and the activation rows as rows 0..NB-1 of A,
+// accumulating in FP32 across the stages of a group. Warps park their per-group partial
+// sums in `gred`; one barrier per up to kRingMaxGroups groups, then the 8 partials of
+// each output are added in warp order and the epilogue is applied. After a wait expires
+// (`bad`), stages are still released and barriers still taken, without computing.
 template <int NB, int NS>
 __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring, const bf16 *act, uint64_t *full,
-                             uint64_t *empty, long long &it, float *rowres, int *error, bool &bad, int ctid) {
+                             uint64_t *empty, long long &it, float *gred, int *error, bool &bad, int ctid) {
+  static_assert(NB >= 1 && NB <= 8, "activation rows must fit the MMA's first 8 rows");
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K, KS = K / kRingPiece;
-  float acc[NB];
+  const int grow = lane >> 2, gcol = (lane & 3) * 2;  // fragment row / column pair of this lane
+  // ldmatrix x4 addresses: matrices (k, k+8, k+16, k+24) of rows 0..7.
+  const int lrow = lane & 7, lk = (lane >> 3) * 8;
+  for (int gb = g0; gb < g1; gb += kRingMaxGroups) {
+    const int ge = min(g1, gb + kRingMaxGroups);
+    for (int g = gb; g < ge; ++g) {
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ks = 0; ks < KS; ++ks, ++it) {
+        const int s = int(it % NS);
+        if (!bad && !mbar_wait(&full[s], unsigned(it / NS) & 1u)) {
+          if (lane == 0) atomicOr(error, 8);
+          bad = true;
+        }
+        if (!bad) {
+          const bf16 *wst = ring + size_t(s) * 8 * kRingRowPitch;
+          const bf16 *ar = act + size_t(ks) * kRingPiece;
 #pragma unroll
-  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
-  for (int g = g0; g < g1; ++g) {
-    for (int ks = 0; ks < KS; ++ks, ++it) {
-      const int s = int(it % NS);
-      if (!bad && !mbar_wait(&full[s], unsigned(it / NS) & 1u)) {
-        if (lane == 0) atomicOr(error, 8);
-        bad = true;
-      }
-      const int row = g * 8 + warp;
-      if (!bad && row < t.N) {
-        const bf16 *wr = ring + (size_t(s) * 8 + warp) * kRingPiece;
-        const bf16 *ar = act + size_t(ks) * kRingPiece;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int c = lane + 32 * q;
-          const uint4 wq = *reinterpret_cast<const uint4 *>(wr + c * 8);
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const uint4 av = *reinterpret_cast<const uint4 *>(ar + size_t(b) * K + c * 8);
-            float v = acc[b];
-            v = fmaf(bf_lo(wq.x), bf_lo(av.x), v);
-            v = fmaf(bf_hi(wq.x), bf_hi(av.x), v);
-            v = fmaf(bf_lo(wq.y), bf_lo(av.y), v);
-            v = fmaf(bf_hi(wq.y), bf_hi(av.y), v);
-            v = fmaf(bf_lo(wq.z), bf_lo(av.z), v);
-            v = fmaf(bf_hi(wq.z), bf_hi(av.z), v);
-            v = fmaf(bf_lo(wq.w), bf_lo(av.w), v);
-            v = fmaf(bf_hi(wq.w), bf_hi(av.w), v);
-            acc[b] = v;
+          for (int kt = 0; kt < 16; kt += 2) {
+            const int k0 = warp * 256 + kt * 16;  // two k-tiles of 16: [k0, k0 + 32)
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(b0, b1, b2, b3, wst + lrow * kRingRowPitch + k0 + lk);
+            uint32_t a0 = 0, a2 = 0, a0n = 0, a2n = 0;
+            if (grow < NB) {
+              const bf16 *ap = ar + size_t(grow) * K + k0 + gcol;
+              a0 = *reinterpret_cast<const uint32_t *>(ap);
+              a2 = *reinterpret_cast<const uint32_t *>(ap + 8);
+              a0n = *reinterpret_cast<const uint32_t *>(ap + 16);
+              a2n = *reinterpret_cast<const uint32_t *>(ap + 24);
+            }
+            mma_16816(c, a0, a2, b0, b1);
+            mma_16816(c, a0n, a2n, b2, b3);
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // End of an 8-row group: reduce each warp's row, then the group's epilogue.
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      const float v = warp_sum(acc[b]);
-      if (lane == 0) rowres[b * 8 + warp] = v;
-      acc[b] = 0.f;
+      // c[0], c[1] of lane (b, j): activation row b's partial dot with weight rows
+      // 2j, 2j+1 over this warp's k range.
+      if (grow < NB) {
+        float *dst = gred + (size_t(g - gb) * kRingConsumers + warp) * NB * 8 + grow * 8 + gcol;
+        dst[0] = c[0];
+        dst[1] = c[1];
+      }
     }
     consumer_sync();
-    const int r0 = g * 8;
     if (!bad) {
-      if (t.epi == kEpiSwiGLU) {
-        if (ctid < 4 * NB) {
-          const int b = ctid / 4, j = ctid % 4;  // pair j of the group: rows 2j (gate), 2j+1 (up)
-          if (r0 + 2 * j + 1 < t.N) {
-            const float gate = rbf(rowres[b * 8 + 2 * j]), up = rbf(rowres[b * 8 + 2 * j + 1]);
-            t.out[size_t(b) * t.out_stride + (r0 >> 1) + j] = f2bf(rbf(silu_f32(gate)) * up);
+      const bool swiglu = t.epi == kEpiSwiGLU;
+      const int per_group = NB * (swiglu ? 4 : 8);
+      for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {
+        const int gi = u / per_group, rem = u % per_group;
+        const float *src = gred + size_t(gi) * kRingConsumers * NB * 8;
+        const int r0 = (gb + gi) * 8;
+        if (swiglu) {
+          const int b = rem / 4, j = rem % 4;  // pair j of the group: rows 2j (gate), 2j+1 (up)
+          if (r0 + 2 * j + 1 >= t.N) continue;
+          float gs = 0.f, us = 0.f;
+#pragma unroll
+          for (int w = 0; w < kRingConsumers; ++w) {
+            gs += src[w * NB * 8 + b * 8 + 2 * j];
+            us += src[w * NB * 8 + b * 8 + 2 * j + 1];
           }
-        }
-      } else if (ctid < 8 * NB) {
-        const int b = ctid / 8, r = ctid % 8;
-        if (r0 + r < t.N) {
+          const float gate = rbf(gs), up = rbf(us);
+          t.out[size_t(b) * t.out_stride + (r0 >> 1) + j] = f2bf(rbf(silu_f32(gate)) * up);
+        } else {
+          const int b = rem / 8, r = rem % 8;
+          if (r0 + r >= t.N) continue;
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < kRingConsumers; ++w) v += src[w * NB * 8 + b * 8 + r];
           bf16 *o = t.out + size_t(b) * t.out_stride + r0 + r;
           if (t.epi == kEpiResidual)
-            *o = f2bf(bf2f(__ldcg(o)) + rbf(rowres[b * 8 + r]));
+            *o = f2bf(bf2f(__ldcg(o)) + rbf(v));
           else
-            *o = f2bf(rowres[b * 8 + r]);
+            *o = f2bf(v);
         }
       }
     }
-    consumer_sync();
+    if (ge < g1) consumer_sync();  // the next batch reuses gred
   }
 }
 
