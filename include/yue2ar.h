@@ -138,6 +138,25 @@ int yar_sample_host(yar_model *model, const uint16_t *cond, const uint16_t *unco
                     int n_history, int step, int phase, uint64_t seed, int legacy_off,
                     int32_t *token, float *scores);
 
+/* No counterpart in the reference. The sampler step of yar_sample_host for callers that
+ * can't allocate device memory: a process whose caching allocator (PyTorch's, for one)
+ * already holds the GPU's free memory, and real-time loops that can't afford the
+ * device-wide synchronisation cudaFree implies. It calls no cudaMalloc or cudaFree.
+ * Inputs and outputs are the caller's DEVICE memory: `logits` holds `rows` BF16 rows of
+ * width n (row 0 conditional; row 1, at logits + row_stride elements, unconditional and
+ * used when cfg_scale != 1), `token` one int32 (the phase-local token), `scores` (may be
+ * NULL) n FP32 filtered scores. `sampling`, `history` and the rest are host values with
+ * yar_sample_host's meaning. Runs on `stream` (a cudaStream_t; NULL = default stream) and
+ * returns once the step has finished there. Its working memory is one static device array
+ * of 769 KiB that every GPU loading the library holds until exit, so n is at most 196608
+ * (larger n returns YAR_INVALID_INPUT). The first call for a device looks up that array's
+ * address on the device; make it before any stream capture there. Calls share the array:
+ * the library serialises its own calls, and calls whose kernels overlapped would race. */
+int yar_sample_device_noalloc(yar_model *model, const uint16_t *logits, int64_t row_stride,
+                              int rows, int n, double cfg_scale, const yar_sampling *sampling,
+                              const int32_t *history, int n_history, int step, int phase,
+                              uint64_t seed, int32_t *token, float *scores, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

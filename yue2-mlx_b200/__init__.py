@@ -84,6 +84,8 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_row_position": (I, [P, I, ctypes.POINTER(I)]),
         "yar_sample_host": (I, [P, u16p, u16p, I, D, ctypes.POINTER(_Sampling), i32p, I, I, I, U64, I, i32p,
                                 ctypes.POINTER(ctypes.c_float)]),
+        "yar_sample_device_noalloc": (I, [P, P, ctypes.c_int64, I, I, D, ctypes.POINTER(_Sampling), i32p, I, I, I,
+                                          U64, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

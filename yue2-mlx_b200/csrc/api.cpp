@@ -23,6 +23,10 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
 void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
                  const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
                  uint64_t seed, int32_t *token, float *scores);
+void sample_device_noalloc(Model &m, const uint16_t *logits, long long row_stride, int rows, int n,
+                           double cfg_scale, const ::yar_sampling &smp, const int32_t *history, int n_history,
+                           int step, int phase, uint64_t seed, int32_t *token, float *scores,
+                           cudaStream_t st);
 }  // namespace yar
 
 struct yar_model {
@@ -254,6 +258,18 @@ int yar_sample_host(yar_model *model, const uint16_t *cond, const uint16_t *unco
     need(!legacy_off, "legacy_off (BF16 historical sampling) is not implemented");
     yar::sample_host(*model->m, cond, uncond, n, cfg_scale, *sampling, history, n_history, step, phase, seed,
                      token, scores);
+  });
+}
+
+int yar_sample_device_noalloc(yar_model *model, const uint16_t *logits, int64_t row_stride, int rows, int n,
+                              double cfg_scale, const yar_sampling *sampling, const int32_t *history,
+                              int n_history, int step, int phase, uint64_t seed, int32_t *token, float *scores,
+                              void *stream) {
+  return guarded([&] {
+    need(model && logits && sampling && token, "missing argument");
+    need(n_history == 0 || history, "history pointer missing");
+    yar::sample_device_noalloc(*model->m, logits, row_stride, rows, n, cfg_scale, *sampling, history, n_history,
+                               step, phase, seed, token, scores, static_cast<cudaStream_t>(stream));
   });
 }
 
