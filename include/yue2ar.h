@@ -90,9 +90,11 @@ int yar_session_free(yar_session *session);
 /* Session options. YAR_OPT_PERSISTENT (default 1): run each decode forward of one or two
  * rows as the single persistent kernel when the model's shapes allow it; 0 selects one
  * kernel per operation (same arithmetic, identical results). YAR_OPT_TRACE (default 0):
- * record the persistent kernel's timeline (per CTA and operation, 8 globaltimer stamps
- * in ns: wait done, activations staged, stages consumed, signalled, producer first/last
- * issue), overwritten by every step; read it with yar_session_trace. */
+ * record the persistent kernel's timeline (per CTA and operation, 8 SM-clock (clock64)
+ * stamps: wait done, activations staged, stages consumed, signalled, producer first/last
+ * issue; slots 6/7 of operation 0 and of the head hold globaltimer ns and the SM clock
+ * at the step's start and end, for converting cycles to time), overwritten by every
+ * step; read it with yar_session_trace. */
 enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2 };
 int yar_session_set_option(yar_session *session, int option, int value);
 /* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64) to host. */

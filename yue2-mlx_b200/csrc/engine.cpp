@@ -206,7 +206,9 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
 // One decode forward of rows [0, n_rows): embed -> 28 x (QKV, attention, O, gate/up, down)
 // -> LM head. Inactive rows are skipped by the embed/attention kernels.
 static bool use_persistent(Session &s, int n_rows) {
-  if (!s.use_persistent || n_rows < 1 || n_rows > 2) return false;
+  // The persistent kernel streams each 64-position KV chunk as one contiguous copy, so a
+  // chunk must not straddle pages.
+  if (!s.use_persistent || n_rows < 1 || n_rows > 2 || s.page_tokens < 64) return false;
   if (s.persistent_ok[n_rows] < 0) s.persistent_ok[n_rows] = persistent_supported(*s.m, n_rows) ? 1 : 0;
   return s.persistent_ok[n_rows] == 1;
 }

@@ -107,6 +107,7 @@ void configure_gemm_kernels();
 void configure_attn_kernels();
 void configure_gemv_tma_kernels();
 void configure_persistent_kernels();
+void configure_sampler_kernels();
 bool persistent_supported(const Model &m, int n_rows);
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
 

@@ -18,6 +18,8 @@ static AttnGeom geom(const Model &m, const Session &s) {
   g.qdim = m.d.qdim();
   g.kvdim = m.d.kvdim();
   g.page_tokens = s.page_tokens;
+  g.page_shift = 0;
+  while ((1 << g.page_shift) < s.page_tokens) ++g.page_shift;
   g.pages_per_row = s.pages_per_row;
   g.num_pages = s.num_pages;
   g.page_elems = s.kv_page_elems;
@@ -28,16 +30,42 @@ static AttnGeom geom(const Model &m, const Session &s) {
 
 // ---------------------------------------------------------------------------------------
 // Decode: grid (kv_head, split, row), 128 threads = one attention unit per CTA
-// (attn_decode.cuh). The page table and norm weights are staged inside the unit.
+// (attn_decode.cuh); each chunk's cached rows are loaded into shared memory with 16-byte
+// loads (any page size), then processed by the same code as the persistent kernel.
 template <int D, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p) {
-  __shared__ AttnSmem<D, G> sm;
+  __shared__ AttnTeamSmem<D, G> sm;
   __shared__ AttnRow<D> rs;
+  __shared__ __align__(16) bf16 kbuf[kKvChunk * D];
+  __shared__ __align__(16) bf16 vbuf[kKvChunk * D];
+  const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z, tid = threadIdx.x;
+  float wv[D / 32];
+  attn_load_norm_w<D, G>(p.qn, p.kn, wv, tid);
   pdl_launch_dependents();
   pdl_wait();
-  attn_row_load<D>(rs, p, blockIdx.z, threadIdx.x, kAttnThreads);
+  attn_row_load<D>(rs, p, row, tid, kAttnThreads);
   __syncthreads();
-  attn_unit<D, G>(p, sm, rs, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x, 1);
+  if (!rs.active) return;
+  const int pos = rs.pos;
+  const SplitPlan sp = split_plan(pos + 1, p.max_splits);
+  if (split >= sp.n_splits) return;  // beyond the context: no work, no arrival
+  attn_qk<D, G>(p, sm, rs, row, kvh, split == sp.n_splits - 1, wv, tid, 1);
+  AttnAcc<D> acc;
+  attn_acc_init(acc);
+  const int c1 = min((split + 1) * sp.cps, sp.nchunks);
+  for (int c = split * sp.cps; c < c1; ++c) {
+    const int base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
+    for (int idx = tid; idx < n_main * (D / 8); idx += kAttnThreads) {
+      const int r = idx / (D / 8), cc = idx % (D / 8);
+      const uint4 kq = ldg16(kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, base + r) + cc * 8);
+      const uint4 vq = ldg16(kv_row_ptr<D>(p, rs, row, p.layer, 1, kvh, base + r) + cc * 8);
+      *reinterpret_cast<uint4 *>(kbuf + r * D + cc * 8) = kq;
+      *reinterpret_cast<uint4 *>(vbuf + r * D + cc * 8) = vq;
+    }
+    team_sync(1);
+    attn_chunk<D, G>(sm, kbuf, vbuf, n_main, pos - base < kKvChunk, p.g.scale, acc, tid, 1);
+  }
+  attn_finish<D, G>(p, sm, acc, row, kvh, split, sp.n_splits, tid, 1);
 }
 
 void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st) {

@@ -43,26 +43,119 @@ struct PersistParams {
   DecodeAttnParams ap;
   int *token, *pos, *cur_pos, *capacity, *active, *error;
   int *ctr, *epoch;
-  unsigned long long *trace;  // optional [cta][op][8] globaltimer stamps (ns), op = 5*layer + k
+  unsigned long long *trace;  // optional [cta][op][8] SM-clock stamps (clock64), op = 5*layer + k
 };
 
+__device__ __forceinline__ unsigned long long sm_clock() { return (unsigned long long)clock64(); }
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 
+// Release-add at GPU scope: orders this thread's earlier writes, and those of the CTA made
+// visible to it by a preceding barrier, before the count.
+__device__ __forceinline__ void red_release_add(int *p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ int ld_acquire(const int *p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
+// True on every thread of the team when `v` is true on any of its threads.
+__device__ __forceinline__ bool team_any(int bar_id, bool v) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(int(v)), "r"(bar_id), "n"(kAttnThreads)
+      : "memory");
+  return r != 0;
+}
+
+// The attention units of one step: rows in order; an active row has kv_heads x n_splits
+// units (kv head major), an inactive row kv_heads units without work, each standing in for
+// its kv head's arrival. Unit u runs on CTA u % grid; the CTA's k-th unit on team k % 2.
+// Its chunks travel through the CTA's weight ring as stages (K rows, then V rows),
+// issued right after the layer's QKV stages.
+template <int NB>
+struct StepRows {
+  int active[NB], pos[NB];
+};
+struct UnitInfo {
+  int row, kvh, split, n_splits, c0, c1;
+  bool active;
+};
+template <int NB>
+__device__ __forceinline__ int step_units(const StepRows<NB> &r, int kvh_n, int max_splits) {
+  int U = 0;
+  for (int b = 0; b < NB; ++b) U += kvh_n * (r.active[b] ? split_plan(r.pos[b] + 1, max_splits).n_splits : 1);
+  return U;
+}
+template <int NB>
+__device__ __forceinline__ UnitInfo step_unit(const StepRows<NB> &r, int kvh_n, int max_splits, int u) {
+  UnitInfo ui{};
+  for (int b = 0; b < NB; ++b) {
+    const bool act = r.active[b] != 0;
+    const SplitPlan sp = act ? split_plan(r.pos[b] + 1, max_splits) : SplitPlan{0, 1, 1};
+    const int ub = kvh_n * sp.n_splits;
+    if (u < ub || b == NB - 1) {
+      ui.row = b;
+      ui.active = act;
+      ui.kvh = u / sp.n_splits;
+      ui.split = u % sp.n_splits;
+      ui.n_splits = sp.n_splits;
+      ui.c0 = act ? ui.split * sp.cps : 0;
+      ui.c1 = act ? min(ui.c0 + sp.cps, sp.nchunks) : 0;
+      return ui;
+    }
+    u -= ub;
+  }
+  return ui;
+}
+
+constexpr int kMaxCtaChunks = 64;  // chunks whose page the producer caches per step
+
+// Producer: this CTA's KV chunk stages of one layer. A chunk's cached rows are those
+// before the row's position; the new position's k/v come from the projection instead.
+template <int NS, int NB>
+__device__ bool kv_produce(const PersistParams &p, const StepRows<NB> &rows, const int *pages, int U, int layer,
+                           bf16 *ring, uint64_t *full, uint64_t *empty, long long &it) {
+  const AttnGeom &g = p.ap.g;
+  int pi = 0;
+  for (int u = blockIdx.x; u < U; u += gridDim.x) {
+    const UnitInfo ui = step_unit(rows, g.kv_heads, p.ap.max_splits, u);
+    for (int c = ui.c0; c < ui.c1; ++c, ++it, ++pi) {
+      const int s = int(it % NS);
+      if (it >= NS && !mbar_wait(&empty[s], unsigned((it / NS) - 1) & 1u)) {
+        atomicOr(p.error, 4);
+        return false;
+      }
+      const int base = c * kKvChunk, n_main = min(kKvChunk, rows.pos[ui.row] - base);
+      const unsigned bytes = unsigned(n_main) * 128 * 2;
+      mbar_arrive_expect_tx(&full[s], 2 * bytes);
+      if (n_main > 0) {
+        const int page = pi < kMaxCtaChunks
+                             ? pages[pi]
+                             : __ldcg(p.ap.page_table + size_t(ui.row) * g.pages_per_row + (base >> g.page_shift));
+        const size_t blk = (size_t(layer) * g.num_pages + page) * 2;
+        const size_t off = (size_t(ui.kvh) * g.page_tokens + (base & (g.page_tokens - 1))) * 128;
+        bf16 *dst = ring + size_t(s) * 8 * kRingRowPitch;
+        bulk_g2s(dst, p.ap.pool + blk * g.page_elems + off, bytes, &full[s]);
+        bulk_g2s(dst + kKvChunk * 128, p.ap.pool + (blk + 1) * g.page_elems + off, bytes, &full[s]);
+      }
+    }
+  }
+  return true;
+}
+
 template <int NB>
 __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(PersistParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   constexpr int NS = kPersistStages;
-  using ASm = AttnSmem<128, 2>;
+  using ASm = AttnTeamSmem<128, 2>;
   // Layout: ring | act (GEMV activations) aliased with the attention teams' scratch (the
   // two are never live at once) | group partials.
   constexpr size_t kActBytes = size_t(NB) * kPersistMaxK * 2;
@@ -109,8 +202,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       int g0, g1;
       const int kop[4] = {0, 2, 3, 4};
       auto pstamp = [&](int o, int k) {
-        if (p.trace) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = globaltimer();
+        if (p.trace) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
       };
+      StepRows<NB> rows;
+      int pages[kMaxCtaChunks];
+      int U = 0;
       for (int l = 0; l < nL && ok; ++l)
         for (int k = 0; k < 4 && ok; ++k) {
           const GemvTask t = task(l, k);
@@ -118,6 +214,37 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
           pstamp(5 * l + kop[k], 4);
           ok = ring_produce<NS>(t, g0, g1, ring, full, empty, it, p.error);
           pstamp(5 * l + kop[k], 5);
+          if (k != 0 || !ok) continue;
+          if (l == 0) {
+            // The step's rows are known once CTA 0 has latched the positions (bounded wait).
+            long long i = 0;
+            for (; i < kCounterWaitLimit; ++i) {
+              if (ld_acquire(p.ctr) >= epoch + 1) break;
+              if (ld_acquire(p.error) != 0) {
+                i = kCounterWaitLimit;
+                break;
+              }
+              __nanosleep(64);
+            }
+            if (i >= kCounterWaitLimit) {
+              atomicOr(p.error, 16);
+              ok = false;
+              continue;
+            }
+            for (int b = 0; b < NB; ++b) {
+              rows.active[b] = __ldcg(p.active + b);
+              rows.pos[b] = __ldcg(p.cur_pos + b);
+            }
+            U = step_units(rows, p.ap.g.kv_heads, p.ap.max_splits);
+            int pi = 0;
+            for (int u = blockIdx.x; u < U; u += gridDim.x) {
+              const UnitInfo ui = step_unit(rows, p.ap.g.kv_heads, p.ap.max_splits, u);
+              for (int c = ui.c0; c < ui.c1 && pi < kMaxCtaChunks; ++c, ++pi)
+                pages[pi] = __ldcg(p.ap.page_table + size_t(ui.row) * p.ap.g.pages_per_row +
+                                   ((c * kKvChunk) >> p.ap.g.page_shift));
+            }
+          }
+          ok = kv_produce<NS, NB>(p, rows, pages, U, l, ring, full, empty, it);
         }
       if (ok) {
         task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
@@ -135,21 +262,15 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   bool bad = false;
   long long it = 0;
   auto stamp = [&](int o, int k) {
-    if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = globaltimer();
+    if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
   };
-  auto unify_bad = [&]() {
+  // One barrier orders every consumer thread's writes before thread 0's release-add, which
+  // publishes the CTA's share; the same barrier makes a recorded failure CTA-wide.
+  auto signal = [&](int idx) {
     if (bad) s_bad = 1;
     consumer_sync();
     bad = s_bad != 0;
-  };
-  // All consumer threads' writes are ordered before thread 0's release fence by the
-  // barrier; one fence + one atomic publishes the CTA's share.
-  auto signal = [&](int idx) {
-    consumer_sync();
-    if (ctid == 0) {
-      __threadfence();
-      atomicAdd(p.ctr + idx, 1);
-    }
+    if (ctid == 0) red_release_add(p.ctr + idx, 1);
   };
   // Wait until counter idx reaches target; gives up on expiry or once any CTA failed.
   auto wait_for = [&](int idx, int target) {
@@ -202,21 +323,28 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       }
     signal(c_embed);
   }
+  // Trace calibration: globaltimer (ns) and the SM clock at the step's start and end.
+  auto calib = [&](int o) {
+    if (p.trace && ctid == 0) {
+      p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 6] = globaltimer();
+      p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 7] = sm_clock();
+    }
+  };
+  calib(0);
   wait_for(c_embed, epoch + 1);
   // This step's row state (activity, position, cos/sin, page table) for the attention units.
   for (int b = 0; b < NB; ++b) attn_row_load<128>(rowst[b], p.ap, b, ctid, kRingConsumers * 32);
   consumer_sync();
+  StepRows<NB> srows;
+  for (int b = 0; b < NB; ++b) {
+    srows.active[b] = rowst[b].active;
+    srows.pos[b] = rowst[b].pos;
+  }
+  const int U = step_units(srows, kvh_n, nsplit);
 
   const int team = warp / 4, ttid = ctid % kAttnThreads;
-  const int n_units = NB * kvh_n * nsplit;
   for (int l = 0; l < nL; ++l) {
     int g0, g1;
-    // Prefetch into L2 the cached K/V this CTA's attention units will read in this layer.
-    for (int u = blockIdx.x * 2; u < n_units; u += 2 * gridDim.x)
-      for (int tm = 0; tm < 2 && u + tm < n_units; ++tm) {
-        const int uu = u + tm, row = uu / (kvh_n * nsplit), kvh = (uu / nsplit) % kvh_n, split = uu % nsplit;
-        attn_prefetch_kv<128>(p.ap, rowst[row], row, l, kvh, split, ctid, kRingConsumers * 32);
-      }
     // QKV (RMSNorm of x fused).
     {
       stamp(5 * l, 0);
@@ -226,34 +354,62 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l, 2);
-      unify_bad();
       signal(c_op(l, 0));
       stamp(5 * l, 3);
     }
-    // Attention: two 4-warp teams per CTA, units (row, kv head, split) round-robin.
+    // Attention: the CTA's units alternate between its two 4-warp teams; each unit's KV
+    // chunks are ring stages (owned by that team: its 4 warps release each with count 2).
+    float wv[4];
+    if (int(blockIdx.x) + team * int(gridDim.x) < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ttid);
     wait_for(c_op(l, 0), (epoch + 1) * all);
     stamp(5 * l + 1, 0);
     {
       DecodeAttnParams ap = p.ap;
       ap.layer = l;
-      ap.qn = p.layers[l].qn;
-      ap.kn = p.layers[l].kn;
-      for (int u = blockIdx.x * 2 + team; u < n_units; u += 2 * gridDim.x) {
-        const int row = u / (kvh_n * nsplit), kvh = (u / nsplit) % kvh_n, split = u % nsplit;
-        bool merged = false;
-        unsigned long long *st =
-            (p.trace && team == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
-        if (!bad) merged = attn_unit<128, 2>(ap, team_sm[team], rowst[row], row, kvh, split, ttid, 2 + team, st);
-        // An inactive row contributes its kv heads' counts without work (split 0 stands in).
-        const bool count = merged || (split == 0 && (bad || !rowst[row].active));
-        if (count) {
-          team_sync(2 + team);
-          if (ttid == 0) {
-            __threadfence();
-            atomicAdd(p.ctr + c_op(l, 1), 1);
+      long long itk = it;
+      for (int k = 0, u = blockIdx.x; u < U; ++k, u += gridDim.x) {
+        const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
+        const int nch = ui.c1 - ui.c0;
+        if ((k & 1) == team) {
+          unsigned long long *st =
+              (p.trace && team == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
+          ASm &tsm = team_sm[team];
+          const AttnRow<128> &rs = rowst[ui.row];
+          if (ui.active && !bad) attn_qk<128, 2>(ap, tsm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ttid, 2 + team);
+          attn_stamp(st, 3, ttid);
+          AttnAcc<128> acc;
+          attn_acc_init(acc);
+          for (int j = 0; j < nch; ++j) {
+            const long long ij = itk + j;
+            const int sidx = int(ij % NS);
+            bool failed = false;
+            if (!bad) failed = !mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
+            if (team_any(2 + team, failed)) {
+              if (ttid == 0 && !bad) atomicOr(p.error, 8);
+              bad = true;
+            }
+            if (!bad) {
+              const bf16 *ks = ring + size_t(sidx) * 8 * kRingRowPitch;
+              const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
+              attn_chunk<128, 2>(tsm, ks, ks + kKvChunk * 128, n_main, rs.pos - base < kKvChunk, ap.g.scale, acc,
+                                 ttid, 2 + team);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cnt(&empty[sidx], 2);
+          }
+          attn_stamp(st, 4, ttid);
+          bool merged = false;
+          if (ui.active && !bad) merged = attn_finish<128, 2>(ap, tsm, acc, ui.row, ui.kvh, ui.split, ui.n_splits, ttid, 2 + team);
+          attn_stamp(st, 5, ttid);
+          // An inactive row (or a failed step) counts each kv head once, from split 0.
+          if (merged || (ui.split == 0 && (bad || !ui.active))) {
+            team_sync(2 + team);
+            if (ttid == 0) red_release_add(p.ctr + c_op(l, 1), 1);
           }
         }
+        itk += nch;
       }
+      it = itk;
     }
     stamp(5 * l + 1, 2);
     // O (+ residual).
@@ -266,7 +422,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 2, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 2, 2);
-      unify_bad();
       signal(c_op(l, 2));
       stamp(5 * l + 2, 3);
     }
@@ -280,7 +435,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 3, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 3, 2);
-      unify_bad();
       signal(c_op(l, 3));
       stamp(5 * l + 3, 3);
     }
@@ -294,7 +448,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 4, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 4, 2);
-      unify_bad();
       signal(c_op(l, 4));
       stamp(5 * l + 4, 3);
     }
@@ -327,8 +480,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       v = warp_sum(v);
       if (lane == 0) p.logits[size_t(warp) * p.logit_stride + p.head_rows] = f2bf(v);
     }
-    unify_bad();
     signal(c_head);
+    calib(5 * nL);
   }
   if (blockIdx.x == 0) {
     wait_for(c_head, (epoch + 1) * all);
@@ -340,7 +493,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
 }
 
 size_t persistent_smem(int NB) {
-  const size_t act = size_t(NB) * kPersistMaxK * 2, teams = 2 * sizeof(AttnSmem<128, 2>);
+  const size_t act = size_t(NB) * kPersistMaxK * 2, teams = 2 * sizeof(AttnTeamSmem<128, 2>);
   return size_t(kPersistStages) * kRingStageBytes + (act > teams ? act : teams) + size_t(ring_gred_floats(NB)) * 4;
 }
 
@@ -396,6 +549,10 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   a.g.qdim = d.qdim();
   a.g.kvdim = d.kvdim();
   a.g.page_tokens = s.page_tokens;
+  a.g.page_shift = 0;
+  while ((1 << a.g.page_shift) < s.page_tokens) ++a.g.page_shift;
+  if ((1 << a.g.page_shift) != s.page_tokens || s.page_tokens < kKvChunk)
+    throw Error("RuntimeError", "persistent decode needs power-of-two pages of at least 64 positions");
   a.g.pages_per_row = s.pages_per_row;
   a.g.num_pages = s.num_pages;
   a.g.page_elems = s.kv_page_elems;

@@ -16,6 +16,9 @@
 namespace yar {
 
 constexpr int kSampThreads = 1024;
+// Phase widths up to this many columns keep the FP32 score row in shared memory (the
+// semantic phase's 32,769 do); wider rows (ABC) work in the global scratch row.
+constexpr int kSampSmemScores = 36864;
 
 struct SamplerParams {
   RequestState *req;
@@ -65,11 +68,13 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   const int n = st.width, step = st.step;
   const bf16 *lc = p.logits + size_t(st.row_c) * p.logit_stride;
   const bf16 *lu = st.row_u >= 0 ? p.logits + size_t(st.row_u) * p.logit_stride : nullptr;
-  float *s = p.scores + size_t(blockIdx.x) * p.logit_stride;
+  extern __shared__ float s_row[];
+  const bool in_smem = n <= kSampSmemScores;
+  float *s = in_smem ? s_row : p.scores + size_t(blockIdx.x) * p.logit_stride;
 
-  // CFG mix and FP32 upcast.
+  // CFG mix and FP32 upcast (independent loads, several in flight per thread).
   const float scale = st.cfg_scale;
-  for (int i = tid; i < n; i += kSampThreads) {
+  auto mix = [&](int i) {
     float v = bf2f(lc[i]);
     if (lu) {
       const float u = bf2f(lu[i]);
@@ -78,6 +83,30 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       v = round_bf16(f_add(u, scaled));
     }
     s[i] = v;
+  };
+  {
+    constexpr int U = 8;
+    int i = tid;
+    for (; i + (U - 1) * kSampThreads < n; i += U * kSampThreads) {
+      bf16 c[U], uu[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        c[j] = lc[i + j * kSampThreads];
+        uu[j] = lu ? lu[i + j * kSampThreads] : c[j];
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        float v = bf2f(c[j]);
+        if (lu) {
+          const float u = bf2f(uu[j]);
+          const float delta = round_bf16(f_sub(v, u));
+          const float scaled = round_bf16(f_mul(delta, scale));
+          v = round_bf16(f_add(u, scaled));
+        }
+        s[i + j * kSampThreads] = v;
+      }
+    }
+    for (; i < n; i += kSampThreads) mix(i);
   }
   __syncthreads();
   if (tid == 0 && step < st.min_tokens && st.end_local >= 0) s[st.end_local] = -INFINITY;
@@ -374,6 +403,10 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     }
   }
   __syncthreads();
+  if (in_smem && p.write_scores) {
+    float *g = p.scores + size_t(blockIdx.x) * p.logit_stride;
+    for (int i = tid; i < n; i += kSampThreads) g[i] = s[i];
+  }
   if (tid == 0) {
     if (p.picked) p.picked[blockIdx.x] = local;
     if (local < 0) {
@@ -408,6 +441,7 @@ void launch_sampler_ex(RequestState *req, const bf16 *logits, int logit_stride, 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_requests);
   cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = kSampSmemScores * sizeof(float);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -415,6 +449,11 @@ void launch_sampler_ex(RequestState *req, const bf16 *logits, int logit_stride, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   YAR_CUDA(cudaLaunchKernelEx(&cfg, k_sampler, p));
+}
+
+void configure_sampler_kernels() {
+  YAR_CUDA(cudaFuncSetAttribute(k_sampler, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kSampSmemScores * sizeof(float))));
 }
 
 void launch_sampler(const Model &m, Session &s, int n_requests, cudaStream_t st) {

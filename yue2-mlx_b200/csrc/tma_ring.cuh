@@ -44,6 +44,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned by
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
 // Bounded wait for the phase with the given parity to complete; false on expiry.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
   const uint32_t a = smem_u32(bar);
@@ -65,6 +68,22 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// The same copy with an L2 eviction-priority policy (createpolicy).
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+// Weights are read once per token and 3 GB pass through L2 between two reads of the same
+// row, so they are marked evict-first: L2 keeps the KV cache and the activations instead.
+__device__ __forceinline__ uint64_t weight_stream_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
 // Barrier 1 among the 256 consumer threads (the producer warp never joins it).
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kRingConsumers * 32) : "memory");
@@ -82,6 +101,7 @@ template <int NS>
 __device__ bool ring_produce(const GemvTask &t, int g0, int g1, bf16 *ring, uint64_t *full, uint64_t *empty,
                              long long &it, int *error) {
   const int KS = t.K / kRingPiece;
+  const uint64_t pol = weight_stream_policy();
   for (int g = g0; g < g1; ++g)
     for (int ks = 0; ks < KS; ++ks, ++it) {
       const int s = int(it % NS);
@@ -92,8 +112,8 @@ __device__ bool ring_produce(const GemvTask &t, int g0, int g1, bf16 *ring, uint
       const int r0 = g * 8, nrows = min(8, t.N - r0);
       mbar_arrive_expect_tx(&full[s], unsigned(nrows) * kRingPiece * 2);
       for (int r = 0; r < nrows; ++r)
-        bulk_g2s(ring + (size_t(s) * 8 + r) * kRingRowPitch, t.W + size_t(r0 + r) * t.K + size_t(ks) * kRingPiece,
-                 kRingPiece * 2, &full[s]);
+        bulk_g2s_hint(ring + (size_t(s) * 8 + r) * kRingRowPitch,
+                      t.W + size_t(r0 + r) * t.K + size_t(ks) * kRingPiece, kRingPiece * 2, &full[s], pol);
     }
   return true;
 }
@@ -113,6 +133,13 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
   constexpr int T = kRingConsumers * 32;
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K;
   if (t.norm_w) {
+    // The norm weight and x in one round trip.
+    uint4 wn[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = (ctid + j * T) * 8;
+      if (k < K) wn[j] = ldg16(t.norm_w + k);
+    }
     uint4 xv[NB][4];
     for (int b = 0; b < NB; ++b) {
       const bf16 *x = t.in + size_t(b) * t.in_stride;
@@ -143,8 +170,8 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
       for (int j = 0; j < 4; ++j) {
         const int k = (ctid + j * T) * 8;
         if (k >= K) continue;
-        const uint4 wn = ldg16(t.norm_w + k);
-        const uint32_t xq[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w}, wq[4] = {wn.x, wn.y, wn.z, wn.w};
+        const uint32_t xq[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w};
+        const uint32_t wq[4] = {wn[j].x, wn[j].y, wn[j].z, wn[j].w};
         uint32_t o[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
