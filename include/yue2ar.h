@@ -94,8 +94,10 @@ int yar_session_free(yar_session *session);
  * stamps: wait done, activations staged, stages consumed, signalled, producer first/last
  * issue; slots 6/7 of operation 0 and of the head hold globaltimer ns and the SM clock
  * at the step's start and end, for converting cycles to time), overwritten by every
- * step; read it with yar_session_trace. */
-enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2 };
+ * step; read it with yar_session_trace. YAR_OPT_PREFETCH_STAGES (default 6, 0..64): how many
+ * 32 KB stages per SM the persistent kernel pulls into L2 ahead of its shared-memory ring
+ * (its lookahead while the step waits at operation boundaries). */
+enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3 };
 int yar_session_set_option(yar_session *session, int option, int value);
 /* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64) to host. */
 int yar_session_trace(yar_session *session, uint64_t *out, size_t n, size_t *n_written);

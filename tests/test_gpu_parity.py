@@ -345,6 +345,7 @@ def test_pinned_width_two_layers_vs_oracle(yar, wide2):
 def _trace(model, rows, prompt, forced, persistent):
     s = model.session(max_rows=2, max_ctx=400)
     s.set_persistent(persistent)
+    s.set_trace(persistent)  # the persistent kernel stamps its timeline: proof that it ran
     for r in range(rows):
         s.reset(r, 400)
         s.prefill(r, prompt[r], phase=None)
@@ -354,8 +355,9 @@ def _trace(model, rows, prompt, forced, persistent):
         for r in range(rows):
             out[r].append(s.logits(r, None))
     kv = s.kv(0, 1, 0, len(prompt[0]) + len(forced))
+    ran = persistent and bool(np.any(s.trace()))
     s.close()
-    return np.array(out), kv
+    return np.array(out), kv, ran
 
 
 @pytest.mark.parametrize("rows", [1, 2])
@@ -366,8 +368,9 @@ def test_persistent_decode_matches_per_operation_kernels(yar, wide2, rows):
     rng = np.random.default_rng(9)
     prompt = [rng.integers(0, 4096, 200).tolist(), rng.integers(0, 4096, 37).tolist()]
     forced = rng.integers(0, 4096, 12).tolist()
-    a, kva = _trace(model, rows, prompt, forced, persistent=True)
-    b, kvb = _trace(model, rows, prompt, forced, persistent=False)
+    a, kva, ran = _trace(model, rows, prompt, forced, persistent=True)
+    assert ran, "the persistent decode kernel did not run (unsupported shape or occupancy)"
+    b, kvb, _ = _trace(model, rows, prompt, forced, persistent=False)
     np.testing.assert_array_equal(a, b)
     np.testing.assert_array_equal(kva[0], kvb[0])
     np.testing.assert_array_equal(kva[1], kvb[1])

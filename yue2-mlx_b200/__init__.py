@@ -204,6 +204,10 @@ class Session:
         """Decode forward as one persistent kernel (default) or one kernel per operation."""
         _check(lib.yar_session_set_option(self._h, 1, int(bool(on))))
 
+    def set_prefetch_stages(self, n: int):
+        """L2 prefetch distance of the persistent decode kernel, in 32 KB stages per SM."""
+        _check(lib.yar_session_set_option(self._h, 3, int(n)))
+
     def set_trace(self, on: bool):
         """Record the persistent decode kernel's per-CTA timeline (see ``trace``)."""
         _check(lib.yar_session_set_option(self._h, 2, int(bool(on))))

@@ -147,6 +147,13 @@ int yar_session_set_option(yar_session *session, int option, int value) {
         YAR_CUDA(cudaMalloc(&s.d_trace, s.trace_elems * sizeof(unsigned long long)));
         YAR_CUDA(cudaMemset(s.d_trace, 0, s.trace_elems * sizeof(unsigned long long)));
       }
+    } else if (option == YAR_OPT_PREFETCH_STAGES) {
+      need(value >= 0 && value <= 64, "prefetch stages must be in [0, 64]");
+      YAR_CUDA(cudaSetDevice(s.m->device));
+      YAR_CUDA(cudaStreamSynchronize(s.stream));
+      for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old value
+      s.graphs.clear();
+      s.prefetch_stages = value;
     } else {
       throw yar::Error("ValueError", "unknown session option");
     }

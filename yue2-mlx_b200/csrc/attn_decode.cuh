@@ -89,7 +89,6 @@ struct DecodeAttnParams {
 };
 
 constexpr int kKvChunk = 64;  // positions per KV chunk
-constexpr int kMaxSplits = 64;
 
 // The split plan of a row whose context holds L positions (the new one included): split s
 // covers chunks [s * cps, min((s + 1) * cps, nchunks)); the last split holds the new position.
@@ -111,8 +110,6 @@ struct __align__(16) AttnTeamSmem {
   bf16 knew[D], vnew[D];       // the new position's k (normed, roped) and v, as cached
   float p_s[G][kKvChunk];      // exp(score - chunk max)
   float red[2][kAttnThreads / 32];
-  float wsplit[G][kMaxSplits];  // merge weights
-  float inv_l[G];
   int last_flag;
 };
 
@@ -317,44 +314,53 @@ __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *V
   team_sync(bar_id);
 }
 
-// Merge the n_active split partials of the G heads of (row, kv_head): per-split weights
-// exp(m_s - M) are formed once in shared memory, then every output dim sums its splits
-// with independent (pipelined) L2 loads. The merging unit resets the arrival counter.
+// Merge the n_active split partials of the G heads of (row, kv_head) into the BF16 head
+// outputs. Thread t owns output dims (t % 64) * D/64 of head t / 64 and reads those dims
+// plus (m, l) of up to 8 splits in one round trip; batches fold into the running (M, L,
+// O) with exp rescaling, in split order. The merging unit resets the arrival counter.
 template <int D, int G>
-__device__ void attn_merge(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const float *part_base, int kvh,
-                           int row, int n_active, int tid, int bar_id) {
-  constexpr int MS = kMaxSplits;
-  const int lane = tid & 31, warp = tid >> 5;
-  for (int h = warp; h < G; h += kAttnThreads / 32) {
-    const float *pr0 = part_base + size_t(kvh * G + h) * p.max_splits * (D + 2);
-    float mv[MS / 32], lv[MS / 32];
-    float M = -INFINITY;
+__device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, int kvh, int row, int n_active,
+                           int tid) {
+  constexpr int DPT = D / 64, MB = 8;
+  const int hd = tid >> 6, i = tid & 63;
+  if (hd < G) {
+    const float *pr0 = part_base + size_t(kvh * G + hd) * p.max_splits * (D + 2);
+    float M = -INFINITY, Ls = 0.f, O[DPT] = {};
+    for (int s0 = 0; s0 < n_active; s0 += MB) {
+      float mv[MB], lv[MB], ov[MB][DPT];
 #pragma unroll
-    for (int i = 0; i < MS / 32; ++i) {
-      const int s = lane + 32 * i;
-      mv[i] = s < n_active ? __ldcg(pr0 + s * (D + 2)) : -INFINITY;
-      lv[i] = s < n_active ? __ldcg(pr0 + s * (D + 2) + 1) : 0.f;
-      M = fmaxf(M, mv[i]);
-    }
-    M = warp_max(M);
-    float Ls = 0.f;
+      for (int j = 0; j < MB; ++j) {
+        mv[j] = -INFINITY;
+        if (s0 + j < n_active) {
+          const float *pr = pr0 + size_t(s0 + j) * (D + 2);
+          mv[j] = __ldcg(pr);
+          lv[j] = __ldcg(pr + 1);
 #pragma unroll
-    for (int i = 0; i < MS / 32; ++i) {
-      const float c = mv[i] == -INFINITY ? 0.f : expf(mv[i] - M);
-      sm.wsplit[h][lane + 32 * i] = c;
-      Ls += lv[i] * c;
+          for (int e = 0; e < DPT; ++e) ov[j][e] = __ldcg(pr + 2 + i * DPT + e);
+        }
+      }
+      float Mb = M;
+#pragma unroll
+      for (int j = 0; j < MB; ++j) Mb = fmaxf(Mb, mv[j]);
+      if (Mb == -INFINITY) continue;
+      const float r = M == -INFINITY ? 0.f : expf(M - Mb);
+      Ls *= r;
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) O[e] *= r;
+#pragma unroll
+      for (int j = 0; j < MB; ++j) {
+        if (mv[j] == -INFINITY) continue;
+        const float c = expf(mv[j] - Mb);
+        Ls += lv[j] * c;
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) O[e] += ov[j][e] * c;
+      }
+      M = Mb;
     }
-    Ls = warp_sum(Ls);
-    if (lane == 0) sm.inv_l[h] = 1.0f / Ls;
-  }
-  team_sync(bar_id);
-  for (int idx = tid; idx < G * D; idx += kAttnThreads) {
-    const int h = idx / D, d = idx % D;
-    const float *pr0 = part_base + size_t(kvh * G + h) * p.max_splits * (D + 2) + 2 + d;
-    float O = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < n_active; ++s) O += __ldcg(pr0 + s * (D + 2)) * sm.wsplit[h][s];
-    p.out[size_t(row) * p.g.qdim + (kvh * G + h) * D + d] = f2bf(O * sm.inv_l[h]);
+    const float inv = 1.0f / Ls;
+#pragma unroll
+    for (int e = 0; e < DPT; ++e)
+      p.out[size_t(row) * p.g.qdim + (kvh * G + hd) * D + i * DPT + e] = f2bf(O[e] * inv);
   }
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
 }
@@ -389,7 +395,7 @@ __device__ bool attn_finish(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, c
   }
   team_sync(bar_id);
   if (!sm.last_flag) return false;
-  attn_merge<D, G>(p, sm, part_base, kvh, row, n_splits, tid, bar_id);
+  attn_merge<D, G>(p, part_base, kvh, row, n_splits, tid);
   return true;
 }
 

@@ -163,6 +163,7 @@ struct Session {
   int *d_ctr = nullptr;
   int *d_epoch = nullptr;
   int n_ctr = 0;
+  int prefetch_stages = 6;  // persistent kernel: L2 prefetch distance beyond the ring
   unsigned long long *d_trace = nullptr;  // persistent-kernel timeline (when enabled)
   size_t trace_elems = 0;
 };

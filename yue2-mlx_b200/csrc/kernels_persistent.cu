@@ -43,6 +43,7 @@ struct PersistParams {
   DecodeAttnParams ap;
   int *token, *pos, *cur_pos, *capacity, *active, *error;
   int *ctr, *epoch;
+  int prefetch_stages;        // L2 prefetch distance beyond the ring, in stages
   unsigned long long *trace;  // optional [cta][op][8] SM-clock stamps (clock64), op = 5*layer + k
 };
 
@@ -116,40 +117,193 @@ __device__ __forceinline__ UnitInfo step_unit(const StepRows<NB> &r, int kvh_n, 
   return ui;
 }
 
-constexpr int kMaxCtaChunks = 64;  // chunks whose page the producer caches per step
+constexpr int kMaxCtaChunks = 64;  // KV chunks of one CTA in one layer
 
-// Producer: this CTA's KV chunk stages of one layer. A chunk's cached rows are those
-// before the row's position; the new position's k/v come from the projection instead.
-template <int NS, int NB>
-__device__ bool kv_produce(const PersistParams &p, const StepRows<NB> &rows, const int *pages, int U, int layer,
-                           bf16 *ring, uint64_t *full, uint64_t *empty, long long &it) {
-  const AttnGeom &g = p.ap.g;
-  int pi = 0;
-  for (int u = blockIdx.x; u < U; u += gridDim.x) {
-    const UnitInfo ui = step_unit(rows, g.kv_heads, p.ap.max_splits, u);
-    for (int c = ui.c0; c < ui.c1; ++c, ++it, ++pi) {
-      const int s = int(it % NS);
-      if (it >= NS && !mbar_wait(&empty[s], unsigned((it / NS) - 1) & 1u)) {
-        atomicOr(p.error, 4);
-        return false;
+__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ GemvTask layer_task(const PersistParams &p, int l, int k) {
+  const LayerWeights &w = p.layers[l];
+  const int H = p.H;
+  switch (k) {
+    case 0: return GemvTask{w.qkv, p.QKV, H, p.x, H, w.ln1, p.eps, p.qkv, p.QKV, kEpiStore};
+    case 1: return GemvTask{w.o, H, p.QD, p.attn, p.QD, nullptr, p.eps, p.x, H, kEpiResidual};
+    case 2: return GemvTask{w.gu, 2 * p.F, H, p.x, H, w.ln2, p.eps, p.mlp, p.F, kEpiSwiGLU};
+    default: return GemvTask{w.down, H, p.F, p.mlp, p.F, nullptr, p.eps, p.x, H, kEpiResidual};
+  }
+}
+__device__ __forceinline__ GemvTask head_task(const PersistParams &p) {
+  return GemvTask{p.head, p.head_rows, p.H, p.x, p.H, p.final_norm, p.eps, p.logits, p.logit_stride, kEpiStore};
+}
+
+struct KvChunkRef {
+  int page, kvh, base, n_main;
+};
+// A stage of the producer's sequence: stage i of operation o (0 QKV, 1 this CTA's KV
+// chunks, 2 O, 3 gate/up, 4 down) of layer l; layer n_layers is the LM head (o = 0). The
+// operation's constants are loaded once on entering it.
+struct ProdCursor {
+  int l, o, i, len;
+  const bf16 *W;  // GEMV operations: weight, K, this CTA's first group, stages per group
+  int K, N, g, ks, KS;
+};
+
+// The producer lane's view of one step. It walks the stage sequence twice: once to copy
+// stages into the ring, and `prefetch_stages` stages ahead of that to pull the same
+// bytes into L2 (cp.async.bulk.prefetch), so HBM keeps streaming while the consumers wait
+// at operation boundaries and the ring copies of those stages then hit L2.
+template <int NB>
+struct Producer {
+  const LayerWeights *layers;
+  const bf16 *head;
+  int head_rows, H, QKV, QD, F, nL, epoch;
+  bf16 *pool;
+  AttnGeom g;
+  int max_splits;
+  const int *page_table, *ctr, *active, *cur_pos;
+  int *error;
+  int nkv;
+  bool planned, failed;
+  KvChunkRef *kv;  // this CTA's chunk list (shared memory, kMaxCtaChunks entries)
+
+  __device__ Producer(const PersistParams &p, int ep, KvChunkRef *kv_smem)
+      : layers(p.layers), head(p.head), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F),
+        nL(p.n_layers), epoch(ep), pool(p.ap.pool), g(p.ap.g), max_splits(p.ap.max_splits),
+        page_table(p.ap.page_table), ctr(p.ctr), active(p.active), cur_pos(p.cur_pos), error(p.error), nkv(0),
+        planned(false), failed(false), kv(kv_smem) {}
+
+  // This CTA's KV chunks, once CTA 0 has latched the step's positions (bounded wait).
+  __device__ bool plan() {
+    long long i = 0;
+    for (; i < kCounterWaitLimit; ++i) {
+      if (ld_acquire(ctr) >= epoch + 1) break;
+      if (ld_acquire(error) != 0) {
+        i = kCounterWaitLimit;
+        break;
       }
-      const int base = c * kKvChunk, n_main = min(kKvChunk, rows.pos[ui.row] - base);
-      const unsigned bytes = unsigned(n_main) * 128 * 2;
-      mbar_arrive_expect_tx(&full[s], 2 * bytes);
-      if (n_main > 0) {
-        const int page = pi < kMaxCtaChunks
-                             ? pages[pi]
-                             : __ldcg(p.ap.page_table + size_t(ui.row) * g.pages_per_row + (base >> g.page_shift));
-        const size_t blk = (size_t(layer) * g.num_pages + page) * 2;
-        const size_t off = (size_t(ui.kvh) * g.page_tokens + (base & (g.page_tokens - 1))) * 128;
-        bf16 *dst = ring + size_t(s) * 8 * kRingRowPitch;
-        bulk_g2s(dst, p.ap.pool + blk * g.page_elems + off, bytes, &full[s]);
-        bulk_g2s(dst + kKvChunk * 128, p.ap.pool + (blk + 1) * g.page_elems + off, bytes, &full[s]);
+      __nanosleep(64);
+    }
+    if (i >= kCounterWaitLimit) {
+      atomicOr(error, 16);
+      return false;
+    }
+    StepRows<NB> rows;
+    for (int b = 0; b < NB; ++b) {
+      rows.active[b] = __ldcg(active + b);
+      rows.pos[b] = __ldcg(cur_pos + b);
+    }
+    const int U = step_units(rows, g.kv_heads, max_splits);
+    for (int u = blockIdx.x; u < U; u += gridDim.x) {
+      const UnitInfo ui = step_unit(rows, g.kv_heads, max_splits, u);
+      for (int c = ui.c0; c < ui.c1; ++c) {
+        if (nkv == kMaxCtaChunks) {
+          atomicOr(error, 32);
+          return false;
+        }
+        const int base = c * kKvChunk;
+        kv[nkv++] = KvChunkRef{__ldcg(page_table + size_t(ui.row) * g.pages_per_row + (base >> g.page_shift)),
+                               ui.kvh, base, min(kKvChunk, rows.pos[ui.row] - base)};
       }
     }
+    return true;
   }
-  return true;
-}
+
+  // Load operation (c.l, c.o)'s constants and stage count into the cursor.
+  __device__ void enter(ProdCursor &c) {
+    c.i = 0;
+    if (c.l < nL && c.o == 1) {
+      if (!planned) {
+        planned = true;
+        failed = !plan();
+      }
+      c.len = failed ? 0 : nkv;
+      return;
+    }
+    if (c.l == nL) {
+      c.W = head, c.N = head_rows, c.K = H;
+    } else {
+      const LayerWeights &w = layers[c.l];
+      switch (c.o) {
+        case 0: c.W = w.qkv, c.N = QKV, c.K = H; break;
+        case 2: c.W = w.o, c.N = H, c.K = QD; break;
+        case 3: c.W = w.gu, c.N = 2 * F, c.K = H; break;
+        default: c.W = w.down, c.N = H, c.K = F; break;
+      }
+    }
+    const int groups = (c.N + 7) / 8;
+    const int g0 = int(blockIdx.x) * groups / int(gridDim.x), g1 = (int(blockIdx.x) + 1) * groups / int(gridDim.x);
+    c.KS = c.K / kRingPiece;
+    c.g = g0;
+    c.ks = 0;
+    c.len = (g1 - g0) * c.KS;
+  }
+  __device__ bool valid(const ProdCursor &c) const { return c.l < nL || (c.l == nL && c.o == 0); }
+  __device__ void begin(ProdCursor &c) {
+    c.l = 0;
+    c.o = 0;
+    enter(c);
+    skip_empty(c);
+  }
+  __device__ void skip_empty(ProdCursor &c) {
+    while (!failed && valid(c) && c.i >= c.len) {
+      if (c.l == nL) {
+        c.o = 1;  // past the head
+        return;
+      }
+      if (++c.o == 5) {
+        c.o = 0;
+        ++c.l;
+      }
+      enter(c);
+    }
+  }
+  // Advance to the next stage; false past the last stage.
+  __device__ bool next(ProdCursor &c) {
+    ++c.i;
+    if (++c.ks == c.KS) {
+      c.ks = 0;
+      ++c.g;
+    }
+    skip_empty(c);
+    return !failed && valid(c);
+  }
+  // Copy the stage into ring slot `dst`, completing on `bar`.
+  __device__ void issue(const ProdCursor &c, bf16 *dst, uint64_t *bar, uint64_t pol) const {
+    if (c.l < nL && c.o == 1) {
+      const KvChunkRef r = kv[c.i];
+      const unsigned bytes = r.n_main > 0 ? unsigned(r.n_main) * 128 * 2 : 0u;
+      mbar_arrive_expect_tx(bar, 2 * bytes);
+      if (bytes) {
+        const size_t blk = (size_t(c.l) * g.num_pages + r.page) * 2;
+        const size_t off = (size_t(r.kvh) * g.page_tokens + (r.base & (g.page_tokens - 1))) * 128;
+        bulk_g2s(dst, pool + blk * g.page_elems + off, bytes, bar);
+        bulk_g2s(dst + kKvChunk * 128, pool + (blk + 1) * g.page_elems + off, bytes, bar);
+      }
+      return;
+    }
+    const int r0 = c.g * 8, nrows = min(8, c.N - r0);
+    const bf16 *src = c.W + size_t(r0) * c.K + size_t(c.ks) * kRingPiece;
+    mbar_arrive_expect_tx(bar, unsigned(nrows) * kRingPiece * 2);
+    for (int r = 0; r < nrows; ++r)
+      bulk_g2s_hint(dst + r * kRingRowPitch, src + size_t(r) * c.K, kRingPiece * 2, bar, pol);
+  }
+  // Pull the stage's bytes into L2.
+  __device__ void prefetch(const ProdCursor &c) const {
+    if (c.l < nL && c.o == 1) {
+      const KvChunkRef r = kv[c.i];
+      if (r.n_main <= 0) return;
+      const size_t blk = (size_t(c.l) * g.num_pages + r.page) * 2;
+      const size_t off = (size_t(r.kvh) * g.page_tokens + (r.base & (g.page_tokens - 1))) * 128;
+      prefetch_l2(pool + blk * g.page_elems + off, unsigned(r.n_main) * 256);
+      prefetch_l2(pool + (blk + 1) * g.page_elems + off, unsigned(r.n_main) * 256);
+      return;
+    }
+    const int r0 = c.g * 8, nrows = min(8, c.N - r0);
+    const bf16 *src = c.W + size_t(r0) * c.K + size_t(c.ks) * kRingPiece;
+    for (int r = 0; r < nrows; ++r) prefetch_l2(src + size_t(r) * c.K, kRingPiece * 2);
+  }
+};
 
 template <int NB>
 __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(PersistParams p) {
@@ -168,19 +322,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   __shared__ float red[NB * kRingConsumers];
   __shared__ AttnRow<128> rowst[NB];
   __shared__ int s_epoch, s_bad;
+  __shared__ KvChunkRef kv_chunks[kMaxCtaChunks];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nL = p.n_layers, H = p.H;
-  auto task = [&](int l, int k) {
-    const LayerWeights &w = p.layers[l];
-    switch (k) {
-      case 0: return GemvTask{w.qkv, p.QKV, H, p.x, H, w.ln1, p.eps, p.qkv, p.QKV, kEpiStore};
-      case 1: return GemvTask{w.o, H, p.QD, p.attn, p.QD, nullptr, p.eps, p.x, H, kEpiResidual};
-      case 2: return GemvTask{w.gu, 2 * p.F, H, p.x, H, w.ln2, p.eps, p.mlp, p.F, kEpiSwiGLU};
-      default: return GemvTask{w.down, H, p.F, p.mlp, p.F, nullptr, p.eps, p.x, H, kEpiResidual};
-    }
-  };
-  const GemvTask head{p.head, p.head_rows, H, p.x, H, p.final_norm, p.eps, p.logits, p.logit_stride, kEpiStore};
+  auto task = [&](int l, int k) { return layer_task(p, l, k); };
+  const GemvTask head = head_task(p);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -197,60 +344,34 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
 
   if (warp == kRingConsumers) {
     if (lane == 0) {
-      long long it = 0;
-      bool ok = true;
-      int g0, g1;
-      const int kop[4] = {0, 2, 3, 4};
       auto pstamp = [&](int o, int k) {
         if (p.trace) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
       };
-      StepRows<NB> rows;
-      int pages[kMaxCtaChunks];
-      int U = 0;
-      for (int l = 0; l < nL && ok; ++l)
-        for (int k = 0; k < 4 && ok; ++k) {
-          const GemvTask t = task(l, k);
-          task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-          pstamp(5 * l + kop[k], 4);
-          ok = ring_produce<NS>(t, g0, g1, ring, full, empty, it, p.error);
-          pstamp(5 * l + kop[k], 5);
-          if (k != 0 || !ok) continue;
-          if (l == 0) {
-            // The step's rows are known once CTA 0 has latched the positions (bounded wait).
-            long long i = 0;
-            for (; i < kCounterWaitLimit; ++i) {
-              if (ld_acquire(p.ctr) >= epoch + 1) break;
-              if (ld_acquire(p.error) != 0) {
-                i = kCounterWaitLimit;
-                break;
-              }
-              __nanosleep(64);
-            }
-            if (i >= kCounterWaitLimit) {
-              atomicOr(p.error, 16);
-              ok = false;
-              continue;
-            }
-            for (int b = 0; b < NB; ++b) {
-              rows.active[b] = __ldcg(p.active + b);
-              rows.pos[b] = __ldcg(p.cur_pos + b);
-            }
-            U = step_units(rows, p.ap.g.kv_heads, p.ap.max_splits);
-            int pi = 0;
-            for (int u = blockIdx.x; u < U; u += gridDim.x) {
-              const UnitInfo ui = step_unit(rows, p.ap.g.kv_heads, p.ap.max_splits, u);
-              for (int c = ui.c0; c < ui.c1 && pi < kMaxCtaChunks; ++c, ++pi)
-                pages[pi] = __ldcg(p.ap.page_table + size_t(ui.row) * p.ap.g.pages_per_row +
-                                   ((c * kKvChunk) >> p.ap.g.page_shift));
-            }
-          }
-          ok = kv_produce<NS, NB>(p, rows, pages, U, l, ring, full, empty, it);
+      Producer<NB> pr(p, epoch, kv_chunks);
+      ProdCursor ic, pc;
+      pr.begin(ic);
+      pc = ic;
+      bool iv = !pr.failed && pr.valid(ic), pv = iv;
+      long long it = 0, pf = 0;
+      const uint64_t pol = weight_stream_policy();
+      const int ahead = p.prefetch_stages;
+      while (iv) {
+        while (pv && pf < it + ahead) {
+          pr.prefetch(pc);
+          pv = pr.next(pc);
+          ++pf;
         }
-      if (ok) {
-        task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
-        pstamp(5 * nL, 4);
-        ring_produce<NS>(head, g0, g1, ring, full, empty, it, p.error);
-        pstamp(5 * nL, 5);
+        const int s = int(it % NS);
+        if (it >= NS && !mbar_wait(&empty[s], unsigned((it / NS) - 1) & 1u)) {
+          atomicOr(p.error, 4);
+          break;
+        }
+        const int op = 5 * ic.l + ic.o, so = ic.o == 1 ? 6 : 4;  // attention op slots 4/5 hold unit stamps
+        if (ic.i == 0) pstamp(op, so);
+        pr.issue(ic, ring + size_t(s) * 8 * kRingRowPitch, &full[s], pol);
+        ++it;
+        iv = pr.next(ic);
+        if (!iv || 5 * ic.l + ic.o != op) pstamp(op, so + 1);
       }
       ring_drain<NS>(full, it);
     }
@@ -580,6 +701,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.ctr = s.d_ctr;
   p.epoch = s.d_epoch;
   p.trace = s.d_trace;
+  p.prefetch_stages = s.prefetch_stages;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.sm_count);

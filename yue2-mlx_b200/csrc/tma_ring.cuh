@@ -230,7 +230,9 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
   for (int gb = g0; gb < g1; gb += kRingMaxGroups) {
     const int ge = min(g1, gb + kRingMaxGroups);
     for (int g = gb; g < ge; ++g) {
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      // Two independent accumulator chains (even / odd k-tile pairs) halve the MMAs that
+      // serialize on one accumulator; they are added at the end.
+      float c2[2][4] = {};
       for (int ks = 0; ks < KS; ++ks, ++it) {
         const int s = int(it % NS);
         if (!bad && !mbar_wait(&full[s], unsigned(it / NS) & 1u)) {
@@ -253,13 +255,16 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
               a0n = *reinterpret_cast<const uint32_t *>(ap + 16);
               a2n = *reinterpret_cast<const uint32_t *>(ap + 24);
             }
-            mma_16816(c, a0, a2, b0, b1);
-            mma_16816(c, a0n, a2n, b2, b3);
+            mma_16816(c2[0], a0, a2, b0, b1);
+            mma_16816(c2[1], a0n, a2n, b2, b3);
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
+      float c[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) c[q] = c2[0][q] + c2[1][q];
       // c[0], c[1] of lane (b, j): activation row b's partial dot with weight rows
       // 2j, 2j+1 over this warp's k range.
       if (grow < NB) {
