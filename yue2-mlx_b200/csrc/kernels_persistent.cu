@@ -464,6 +464,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   const int U = step_units(srows, kvh_n, nsplit);
 
   const int team = warp / 4, ttid = ctid % kAttnThreads;
+  uint4 wn_next[4];  // RMSNorm weight chunks of the next norm-prologue GEMV, loaded before its wait
+  ring_norm_w_load(task(0, 0), wn_next, ctid);
   for (int l = 0; l < nL; ++l) {
     int g0, g1;
     // QKV (RMSNorm of x fused).
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l, 0);
       const GemvTask t = task(l, 0);
       task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-      ring_stage_act<NB>(t, act, red, ctid);
+      ring_stage_act<NB>(t, act, red, ctid, &wn_next);
       stamp(5 * l, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l, 2);
@@ -534,6 +536,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     }
     stamp(5 * l + 1, 2);
     // O (+ residual).
+    stamp(5 * l + 2, 6);  // wait began
     wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB);
     {
       stamp(5 * l + 2, 0);
@@ -547,12 +550,14 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 2, 3);
     }
     // gate/up (RMSNorm of x fused, SwiGLU epilogue).
+    stamp(5 * l + 3, 6);  // wait began
+    ring_norm_w_load(task(l, 2), wn_next, ctid);
     wait_for(c_op(l, 2), (epoch + 1) * all);
     {
       stamp(5 * l + 3, 0);
       const GemvTask t = task(l, 2);
       task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-      ring_stage_act<NB>(t, act, red, ctid);
+      ring_stage_act<NB>(t, act, red, ctid, &wn_next);
       stamp(5 * l + 3, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 3, 2);
@@ -560,6 +565,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 3, 3);
     }
     // down (+ residual).
+    stamp(5 * l + 4, 6);  // wait began
     wait_for(c_op(l, 3), (epoch + 1) * all);
     {
       stamp(5 * l + 4, 0);
@@ -571,6 +577,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 4, 2);
       signal(c_op(l, 4));
       stamp(5 * l + 4, 3);
+    }
+    if (l + 1 < nL) {
+      stamp(5 * (l + 1), 6);  // the next QKV's wait began
+      ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
     }
     wait_for(c_op(l, 4), (epoch + 1) * all);
   }
@@ -588,7 +598,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       const bf16 *wr = p.head + size_t(p.extra_row - 0) * H;
       float v = 0.f;
       for (int c = lane; c < H / 8; c += 32) {
-        const uint4 wq = ldg16(wr + c * 8), av = *reinterpret_cast<const uint4 *>(act + warp * H + c * 8);
+        const uint4 wq = ldg16(wr + c * 8), av = act_load_chunk(act + warp * H, c * 8);
         v = fmaf(bf_lo(wq.x), bf_lo(av.x), v);
         v = fmaf(bf_hi(wq.x), bf_hi(av.x), v);
         v = fmaf(bf_lo(wq.y), bf_lo(av.y), v);

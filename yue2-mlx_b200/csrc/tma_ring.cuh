@@ -128,17 +128,47 @@ __device__ void ring_drain(uint64_t *full, long long issued) {
 // Consumers: the task's activation rows into `act` ([NB][K] BF16), RMSNorm applied when the
 // task has a norm weight (modeling_yue2.py:131-132): x is read once into registers (up to
 // 4 chunks of 8 per thread, K <= 8192), reduced, normalized. `red` holds NB x 8 floats.
+// Activation rows are kept in shared memory in MMA-fragment order: within every block of
+// 32 elements (16 two-element words), word w sits at position (w % 4) * 4 + w / 4, so the
+// four words a lane needs for two k-tiles (w = q, q + 4, q + 8, q + 12) are one 16-byte
+// load. A 16-byte chunk of 8 consecutive elements (words w0..w0+3, w0 % 4 == 0) scatters to
+// positions w0 / 4, + 4, + 8, + 12.
+__device__ __forceinline__ void act_store_chunk(bf16 *row, int k, uint4 v) {
+  uint32_t *blk = reinterpret_cast<uint32_t *>(row + (k & ~31));
+  const int w0 = (k & 31) >> 1;
+  blk[w0 >> 2] = v.x;
+  blk[4 + (w0 >> 2)] = v.y;
+  blk[8 + (w0 >> 2)] = v.z;
+  blk[12 + (w0 >> 2)] = v.w;
+}
+__device__ __forceinline__ uint4 act_load_chunk(const bf16 *row, int k) {
+  const uint32_t *blk = reinterpret_cast<const uint32_t *>(row + (k & ~31));
+  const int w0 = (k & 31) >> 1;
+  return make_uint4(blk[w0 >> 2], blk[4 + (w0 >> 2)], blk[8 + (w0 >> 2)], blk[12 + (w0 >> 2)]);
+}
+
+// The task's RMSNorm weight chunks of this thread (a layer constant: callers may load it
+// before waiting for the activations).
+__device__ __forceinline__ void ring_norm_w_load(const GemvTask &t, uint4 (&wn)[4], int ctid) {
+  constexpr int T = kRingConsumers * 32;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = (ctid + j * T) * 8;
+    if (t.norm_w && k < t.K) wn[j] = ldg16(t.norm_w + k);
+  }
+}
+
 template <int NB>
-__device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int ctid) {
+__device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int ctid, const uint4 (*wn_pre)[4] = nullptr) {
   constexpr int T = kRingConsumers * 32;
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K;
   if (t.norm_w) {
-    // The norm weight and x in one round trip.
     uint4 wn[4];
+    if (wn_pre) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int k = (ctid + j * T) * 8;
-      if (k < K) wn[j] = ldg16(t.norm_w + k);
+      for (int j = 0; j < 4; ++j) wn[j] = (*wn_pre)[j];
+    } else {
+      ring_norm_w_load(t, wn, ctid);  // with x below: one round trip
     }
     uint4 xv[NB][4];
     for (int b = 0; b < NB; ++b) {
@@ -179,14 +209,14 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
           const float hi = rbf(rbf(bf_hi(xq[q]) * scale) * bf_hi(wq[q]));
           o[q] = (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
         }
-        *reinterpret_cast<uint4 *>(act + b * K + k) = make_uint4(o[0], o[1], o[2], o[3]);
+        act_store_chunk(act + b * K, k, make_uint4(o[0], o[1], o[2], o[3]));
       }
     }
   } else {
     for (int b = 0; b < NB; ++b) {
       const bf16 *x = t.in + size_t(b) * t.in_stride;
       for (int c = ctid; c < K / 8; c += T)
-        *reinterpret_cast<uint4 *>(act + b * K + c * 8) = __ldcg(reinterpret_cast<const uint4 *>(x + c * 8));
+        act_store_chunk(act + b * K, c * 8, __ldcg(reinterpret_cast<const uint4 *>(x + c * 8)));
     }
   }
   consumer_sync();
@@ -247,14 +277,9 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
             const int k0 = warp * 256 + kt * 16;  // two k-tiles of 16: [k0, k0 + 32)
             uint32_t b0, b1, b2, b3;
             ldsm_x4(b0, b1, b2, b3, wst + lrow * kRingRowPitch + k0 + lk);
-            uint32_t a0 = 0, a2 = 0, a0n = 0, a2n = 0;
-            if (grow < NB) {
-              const bf16 *ap = ar + size_t(grow) * K + k0 + gcol;
-              a0 = *reinterpret_cast<const uint32_t *>(ap);
-              a2 = *reinterpret_cast<const uint32_t *>(ap + 8);
-              a0n = *reinterpret_cast<const uint32_t *>(ap + 16);
-              a2n = *reinterpret_cast<const uint32_t *>(ap + 24);
-            }
+            uint4 a4 = make_uint4(0, 0, 0, 0);  // (a0, a2) of k-tile kt, then of kt + 1
+            if (grow < NB) a4 = *reinterpret_cast<const uint4 *>(ar + size_t(grow) * K + k0 + gcol * 4);
+            const uint32_t a0 = a4.x, a2 = a4.y, a0n = a4.z, a2n = a4.w;
             mma_16816(c2[0], a0, a2, b0, b1);
             mma_16816(c2[1], a0n, a2n, b2, b3);
           }
