@@ -99,7 +99,9 @@ int yar_session_free(yar_session *session);
  * (its lookahead while the step waits at operation boundaries). */
 enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3 };
 int yar_session_set_option(yar_session *session, int option, int value);
-/* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64) to host. */
+/* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64, then 16 sampler stamps:
+ * SM clocks at its phase ends, and globaltimer ns at its start and end in slots 12/13)
+ * to host. */
 int yar_session_trace(yar_session *session, uint64_t *out, size_t n, size_t *n_written);
 
 /* generate_tokens — native/src/sampling.cpp:185-288 (upstream sampling.py:57-154): prefill

@@ -215,10 +215,20 @@ class Session:
     def trace(self) -> np.ndarray:
         """Last step's timeline: [sm][5 * layers + 1][8] globaltimer stamps in ns."""
         d = self.model.dims
-        out = np.zeros(d["sms"] * (5 * d["layers"] + 1) * 8, np.uint64)
+        k = d["sms"] * (5 * d["layers"] + 1) * 8
+        out = np.zeros(k + 16, np.uint64)
         n = ctypes.c_size_t()
         _check(lib.yar_session_trace(self._h, _ptr(out, ctypes.c_uint64), out.size, ctypes.byref(n)))
-        return out.reshape(d["sms"], 5 * d["layers"] + 1, 8)
+        return out[:k].reshape(d["sms"], 5 * d["layers"] + 1, 8)
+
+    def sampler_trace(self) -> np.ndarray:
+        """The last sampler launch's phase stamps (16 uint64, see yar_session_trace)."""
+        d = self.model.dims
+        k = d["sms"] * (5 * d["layers"] + 1) * 8
+        out = np.zeros(k + 16, np.uint64)
+        n = ctypes.c_size_t()
+        _check(lib.yar_session_trace(self._h, _ptr(out, ctypes.c_uint64), out.size, ctypes.byref(n)))
+        return out[k:]
 
     def reset(self, row: int, capacity: int):
         _check(lib.yar_row_reset(self._h, row, capacity))

@@ -143,7 +143,7 @@ int yar_session_set_option(yar_session *session, int option, int value) {
       for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old pointer
       s.graphs.clear();
       if (value) {
-        s.trace_elems = size_t(s.m->sm_count) * (5 * s.m->d.layers + 1) * 8;
+        s.trace_elems = size_t(s.m->sm_count) * (5 * s.m->d.layers + 1) * 8 + 16;  // + sampler phases
         YAR_CUDA(cudaMalloc(&s.d_trace, s.trace_elems * sizeof(unsigned long long)));
         YAR_CUDA(cudaMemset(s.d_trace, 0, s.trace_elems * sizeof(unsigned long long)));
       }

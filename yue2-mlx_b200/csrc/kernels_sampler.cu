@@ -19,6 +19,8 @@ constexpr int kSampThreads = 1024;
 // Phase widths up to this many columns keep the FP32 score row in shared memory (the
 // semantic phase's 32,769 do); wider rows (ABC) work in the global scratch row.
 constexpr int kSampSmemScores = 36864;
+// Dynamic shared memory: the score row, then the radix histograms (32 warps x 256 bins).
+constexpr size_t kSampSmemBytes = kSampSmemScores * sizeof(float) + 32 * 256 * sizeof(int);
 
 struct SamplerParams {
   RequestState *req;
@@ -31,6 +33,7 @@ struct SamplerParams {
   int out_cap;
   int write_scores;   // also leave the filtered FP32 scores in `scores` (tests)
   int32_t *picked;    // optional [requests] local token of this step
+  unsigned long long *trace;  // optional: SM-clock stamps of request 0's phases (16 slots)
 };
 
 __device__ __forceinline__ int native_to_local(int tok, int phase, int width) {
@@ -54,7 +57,8 @@ __device__ __forceinline__ int local_to_native(int loc, int phase) {
 __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   __shared__ uint64_t cand[kCandCap];
   __shared__ float ev[kCandCap];
-  __shared__ int hist[4096];
+  __shared__ int tot[256];
+  __shared__ float pv[kCandCap];
   __shared__ int ncand, sel_bin, kth_rem, result, tie_total;
   __shared__ float red_v[32];
   __shared__ int red_i[32];
@@ -62,6 +66,21 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
 
   pdl_launch_dependents();
   pdl_wait();
+  // Phase stamps (tracing only): 0 start, 1 CFG mix, 2 penalty, 3 temperature, 4-6 radix
+  // passes, 7 candidates, 8 sort, 9 exp, 10 nucleus + draw, 11 done; 12/13 globaltimer ns
+  // at start / end.
+  auto stamp = [&](int k) {
+    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[k] = (unsigned long long)clock64();
+  };
+  auto stamp_ns = [&](int k) {
+    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      p.trace[k] = t;
+    }
+  };
+  stamp_ns(12);
+  stamp(0);
   RequestState &st = p.req[blockIdx.x];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (st.done || st.step >= st.max_tokens) return;
@@ -69,6 +88,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   const bf16 *lc = p.logits + size_t(st.row_c) * p.logit_stride;
   const bf16 *lu = st.row_u >= 0 ? p.logits + size_t(st.row_u) * p.logit_stride : nullptr;
   extern __shared__ float s_row[];
+  int *hist = reinterpret_cast<int *>(s_row + kSampSmemScores);  // [32 warps][256 bins]
   const bool in_smem = n <= kSampSmemScores;
   float *s = in_smem ? s_row : p.scores + size_t(blockIdx.x) * p.logit_stride;
 
@@ -84,7 +104,28 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     }
     s[i] = v;
   };
-  {
+  const bool vec = (reinterpret_cast<uintptr_t>(lc) & 15) == 0 && (!lu || (reinterpret_cast<uintptr_t>(lu) & 15) == 0);
+  if (vec) {
+    // 16-byte loads: 8 logits per load, every load of a thread in flight at once.
+    const int nv = n / 8;
+    for (int c = tid; c < nv; c += kSampThreads) {
+      const uint4 cq = *reinterpret_cast<const uint4 *>(lc + size_t(c) * 8);
+      const uint4 uq = lu ? *reinterpret_cast<const uint4 *>(lu + size_t(c) * 8) : cq;
+      const uint32_t cw[4] = {cq.x, cq.y, cq.z, cq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = (e & 1) ? bf_hi(cw[e >> 1]) : bf_lo(cw[e >> 1]);
+        if (lu) {
+          const float u = (e & 1) ? bf_hi(uw[e >> 1]) : bf_lo(uw[e >> 1]);
+          const float delta = round_bf16(f_sub(v, u));
+          const float scaled = round_bf16(f_mul(delta, scale));
+          v = round_bf16(f_add(u, scaled));
+        }
+        s[c * 8 + e] = v;
+      }
+    }
+    for (int i = nv * 8 + tid; i < n; i += kSampThreads) mix(i);
+  } else {
     constexpr int U = 8;
     int i = tid;
     for (; i + (U - 1) * kSampThreads < n; i += U * kSampThreads) {
@@ -109,6 +150,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     for (; i < n; i += kSampThreads) mix(i);
   }
   __syncthreads();
+  stamp(1);
   if (tid == 0 && step < st.min_tokens && st.end_local >= 0) s[st.end_local] = -INFINITY;
   __syncthreads();
   // Window penalty: thread t < W owns history entry t; the first occurrence of each id
@@ -136,6 +178,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     __syncthreads();
   }
 
+  stamp(2);
   int local = -1;
   if (st.temperature == 0.f) {
     // Greedy: first index of the maximum.
@@ -179,72 +222,70 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       for (int i = tid; i < n; i += kSampThreads) s[i] = f_div(s[i], st.temperature);
       __syncthreads();
     }
-    // k-th largest value: radix select on order-preserving keys, digits of 12, 12 and 8
-    // bits from the top; histogram updates are aggregated per warp (lanes with the same
-    // bin add once) and the bin holding the k-th key is found by a block-wide scan.
+    stamp(3);
+    // k-th largest value: radix select on order-preserving keys, four 8-bit digits from
+    // the top. Each warp counts into its own 256-bin histogram (lanes with the same bin add
+    // once), so warps never contend when the logits crowd a few bins; the 32 histograms are
+    // summed per bin and warp 0 finds the bin holding the k-th key by a scan from the top.
     const int k = min(st.top_k, n);
-    if (tid == 0) {
-      prefix_s = 0;
-      kth_rem = k;
-    }
-    __syncthreads();
-    const int shifts[3] = {20, 8, 0}, widths[3] = {12, 12, 8};
-    for (int pass = 0; pass < 3; ++pass) {
-      const int shift = shifts[pass], nb = 1 << widths[pass];
-      for (int b = tid; b < nb; b += kSampThreads) hist[b] = 0;
-      __syncthreads();
-      const uint32_t pre = prefix_s;
-      const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + widths[pass]));
+    uint32_t pre = 0;
+    int rem = k;
+    int *wh = hist + warp * 256;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int b = lane; b < 256; b += 32) wh[b] = 0;
+      __syncwarp();
+      const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
       for (int base = warp * 32; base < n; base += kSampThreads) {
         const int i = base + lane;
         uint32_t bin = 0xFFFFFFFFu;
         if (i < n) {
           const uint32_t key = f32_order_key(s[i]);
-          if ((key & hmask) == (pre & hmask)) bin = (key >> shift) & uint32_t(nb - 1);
+          if ((key & hmask) == (pre & hmask)) bin = (key >> shift) & 255u;
         }
         const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
-        if (bin != 0xFFFFFFFFu && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
+        if (bin != 0xFFFFFFFFu && lane == __ffs(peers) - 1) wh[bin] += __popc(peers);
+        __syncwarp();
       }
       __syncthreads();
-      // Counts from the top bin down: thread t owns bins [nb-1-per*(t+1)+1, nb-1-per*t].
-      const int per = (nb + kSampThreads - 1) / kSampThreads;
-      const int hi = nb - 1 - per * tid;
-      int mine = 0;
-      for (int j = 0; j < per; ++j)
-        if (hi - j >= 0) mine += hist[hi - j];
-      int incl = mine;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
+      if (tid < 256) {
+        int c = 0;
+#pragma unroll 8
+        for (int w = 0; w < kSampThreads / 32; ++w) c += hist[w * 256 + tid];
+        tot[tid] = c;
       }
-      if (lane == 31) red_i[warp] = incl;
       __syncthreads();
       if (warp == 0) {
-        const int w = red_i[lane];
-        int wi = w;
+        // Lane l owns bins 255 - 8l - j (j < 8), counted from the top.
+        int cnt[8], mine = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          cnt[j] = tot[255 - 8 * lane - j];
+          mine += cnt[j];
+        }
+        int incl = mine;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xFFFFFFFFu, wi, o);
-          if (lane >= o) wi += y;
+          const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += y;
         }
-        red_i[lane] = wi - w;
+        const int before = incl - mine;
+        if (before < rem && before + mine >= rem) {
+          int acc = before, b = 255 - 8 * lane;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            b = 255 - 8 * lane - j;
+            if (acc + cnt[j] >= rem) break;
+            acc += cnt[j];
+          }
+          kth_rem = rem - acc;
+          prefix_s = pre | (uint32_t(b) << shift);
+        }
       }
       __syncthreads();
-      const int before = red_i[warp] + incl - mine;  // keys in bins above this thread's bins
-      const int rem = kth_rem;
-      __syncthreads();
-      if (before < rem && before + mine >= rem) {
-        int acc = before, b = hi;
-        for (int j = 0; j < per && hi - j >= 0; ++j) {
-          b = hi - j;
-          if (acc + hist[b] >= rem) break;
-          acc += hist[b];
-        }
-        kth_rem = rem - acc;
-        prefix_s = pre | (uint32_t(b) << shift);
-      }
-      __syncthreads();
+      pre = prefix_s;
+      rem = kth_rem;
+      stamp(4 + (pass < 2 ? pass : 2));
     }
     const float thr = f32_from_order_key(prefix_s);
     // Survivors in (score desc, index asc) order are the rows strictly above the k-th
@@ -291,6 +332,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     __syncthreads();
     const int tie_before = red_i[warp] + incl - my_ties;
     const int na = ncand, nt = tie_total;
+    stamp(7);
     if (na > kCandCap || na + nt == 0) {
       if (tid == 0) {
         st.error = na + nt == 0 ? 2 : 1;
@@ -301,6 +343,32 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     } else {
       int np2 = 1;
       while (np2 < na) np2 <<= 1;
+      if (np2 <= 64) {
+        // Bitonic sort of up to 64 keys in warp 0's registers (element lane + 32 h).
+        if (warp == 0) {
+          uint64_t e[2] = {lane < na ? cand[lane] : ~0ull, lane + 32 < na ? cand[lane + 32] : ~0ull};
+          for (int size = 2; size <= 64; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+              if (stride == 32) {
+                const uint64_t lo = e[0] < e[1] ? e[0] : e[1], hi = e[0] < e[1] ? e[1] : e[0];
+                e[0] = lo;
+                e[1] = hi;
+              } else {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int i = lane + 32 * h;
+                  const uint64_t y = __shfl_xor_sync(0xFFFFFFFFu, e[h], stride);
+                  const bool up = (i & size) == 0, lower = (i & stride) == 0;
+                  const uint64_t mn = e[h] < y ? e[h] : y, mx = e[h] < y ? y : e[h];
+                  e[h] = lower == up ? mn : mx;
+                }
+              }
+            }
+          if (lane < na) cand[lane] = e[0];
+          if (lane + 32 < na) cand[lane + 32] = e[1];
+        }
+        __syncthreads();
+      } else {
       for (int i = na + tid; i < np2; i += kSampThreads) cand[i] = ~0ull;
       __syncthreads();
       // Bitonic sort, ascending keys = (score desc, index asc).
@@ -320,19 +388,34 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
           __syncthreads();
         }
       }
+      }
+      stamp(8);
       const float s0 = na > 0 ? s[uint32_t(cand[0])] : thr;
       for (int i = tid; i < na; i += kSampThreads) ev[i] = yexp(f_sub(s[uint32_t(cand[i])], s0));
       __syncthreads();
-      if (tid == 0) {
-        const float et = yexp(f_sub(thr, s0));
-        int keep_ties = nt;
-        if (st.top_p < 1.f) {
+      stamp(9);
+      // Nucleus: the normalizer is a sequential FP32 sum (thread 0); the divisions
+      // p_i = e_i / total are independent (all threads); the running sum is sequential.
+      const float et = yexp(f_sub(thr, s0));
+      if (st.top_p < 1.f) {
+        if (tid == 0) {
           float total = 0.f;
           for (int i = 0; i < na; ++i) total = f_add(total, ev[i]);
           for (int j = 0; j < nt; ++j) total = f_add(total, et);
+          red_v[0] = total;
+        }
+        __syncthreads();
+        const float total = red_v[0];
+        for (int i = tid; i < na; i += kSampThreads) pv[i] = f_div(ev[i], total);
+        __syncthreads();
+      }
+      if (tid == 0) {
+        int keep_ties = nt;
+        if (st.top_p < 1.f) {
+          const float total = red_v[0];
           float c = 0.f;
           for (int i = 0; i < na; ++i) {
-            const float pi = f_div(ev[i], total);
+            const float pi = pv[i];
             c = f_add(c, pi);
             if (i >= 1 && f_sub(c, pi) > st.top_p) ev[i] = -1.f;  // removed
           }
@@ -399,10 +482,12 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
         }
       }
       __syncthreads();
+      stamp(10);
       local = result;
     }
   }
   __syncthreads();
+  stamp(11);
   if (in_smem && p.write_scores) {
     float *g = p.scores + size_t(blockIdx.x) * p.logit_stride;
     for (int i = tid; i < n; i += kSampThreads) g[i] = s[i];
@@ -431,17 +516,29 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       p.active[st.row_c] = 0;
       if (st.row_u >= 0) p.active[st.row_u] = 0;
     }
+    stamp_ns(13);
   }
 }
+
+static void launch_sampler_impl(RequestState *req, const bf16 *logits, int logit_stride, float *scores, int *token,
+                                int *active, int32_t *out_tokens, int out_cap, int write_scores, int32_t *picked,
+                                int n_requests, cudaStream_t st, unsigned long long *trace);
 
 void launch_sampler_ex(RequestState *req, const bf16 *logits, int logit_stride, float *scores, int *token,
                        int *active, int32_t *out_tokens, int out_cap, int write_scores, int32_t *picked,
                        int n_requests, cudaStream_t st) {
-  SamplerParams p{req, logits, logit_stride, scores, token, active, out_tokens, out_cap, write_scores, picked};
+  launch_sampler_impl(req, logits, logit_stride, scores, token, active, out_tokens, out_cap, write_scores, picked,
+                      n_requests, st, nullptr);
+}
+
+static void launch_sampler_impl(RequestState *req, const bf16 *logits, int logit_stride, float *scores, int *token,
+                                int *active, int32_t *out_tokens, int out_cap, int write_scores, int32_t *picked,
+                                int n_requests, cudaStream_t st, unsigned long long *trace) {
+  SamplerParams p{req, logits, logit_stride, scores, token, active, out_tokens, out_cap, write_scores, picked, trace};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_requests);
   cfg.blockDim = dim3(kSampThreads);
-  cfg.dynamicSmemBytes = kSampSmemScores * sizeof(float);
+  cfg.dynamicSmemBytes = kSampSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -452,14 +549,15 @@ void launch_sampler_ex(RequestState *req, const bf16 *logits, int logit_stride, 
 }
 
 void configure_sampler_kernels() {
-  YAR_CUDA(cudaFuncSetAttribute(k_sampler, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(kSampSmemScores * sizeof(float))));
+  YAR_CUDA(cudaFuncSetAttribute(k_sampler, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSampSmemBytes)));
 }
 
 void launch_sampler(const Model &m, Session &s, int n_requests, cudaStream_t st) {
-  (void)m;
-  launch_sampler_ex(s.d_req, s.logits, s.logit_stride, s.d_scores, s.d_token, s.d_active, s.d_out_tokens,
-                    s.out_cap, 0, nullptr, n_requests, st);
+  // With tracing on, the sampler's phase stamps follow the persistent kernel's timeline.
+  unsigned long long *trace =
+      s.d_trace ? s.d_trace + size_t(m.sm_count) * (5 * m.d.layers + 1) * 8 : nullptr;
+  launch_sampler_impl(s.d_req, s.logits, s.logit_stride, s.d_scores, s.d_token, s.d_active, s.d_out_tokens,
+                      s.out_cap, 0, nullptr, n_requests, st, trace);
 }
 
 }  // namespace yar
