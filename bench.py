@@ -101,6 +101,18 @@ class Clocks:
                         "reasons": sorted(reasons), "samples": len(rows)}
 
 
+def measured_traffic(avg_L: float):
+    """DRAM bytes (read + write) of one persistent decode launch from the committed ncu
+    capture, moved from the captured position to `avg_L` by the KV bytes per position
+    (weights and head rows are position-independent)."""
+    path = os.path.join(ROOT, "profiles", "decode_persistent_config2.txt")
+    try:
+        kv = dict(line.split(":", 1) for line in open(path) if line.startswith("traffic_"))
+        return int(int(kv["traffic_bytes_per_launch"]) + KV_BYTES_PER_POS * (avg_L - int(kv["traffic_position"])))
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def ensure_weights(rank: int, world: int, barrier) -> str:
     synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
     d = os.environ.get("YAR_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "yar_bench_3b_seed0"))
@@ -246,8 +258,11 @@ def main():
     peak, peak_kind = peaks()
     achieved = bytes_per_step / per_token_s / 1e9
     layers = 28
-    launches_per_token = 2 + 5 * layers + 1
+    # Per decoded token: the persistent decode kernel (embedding, 28 layers, LM head) and
+    # the sampler. Per song: the prefill's embedding, 8 kernels per layer, the head GEMV.
+    launches_per_token = 2
     prefill_launches = 1 + 8 * layers + 1
+    traffic = measured_traffic(avg_L)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -264,9 +279,11 @@ def main():
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                     "d2h_bytes_per_step": DECODE * 4 + 20 * ((DECODE + 15) // 16),
                     "prefill_s_per_step": prefill_s / args.steps},
-            "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph of 143 kernels)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "k_decode_persistent (whole decode forward, one CTA per SM) + k_sampler; "
+                                   "achieved = algorithmic bytes / device time per decoded token (both kernels)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": peak_kind, "bytes_per_step": bytes_per_step, "traffic": None},
+                         "peak_source": peak_kind, "bytes_per_step": bytes_per_step, "traffic": traffic},
             "gpu_launches": args.steps * (DECODE * launches_per_token + prefill_launches),
             "clocks": clk.summary,
             "cpu_baseline": cpu,
