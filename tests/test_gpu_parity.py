@@ -312,6 +312,22 @@ def wide2(yar, synth, tmp_path_factory):
     return yar.ARModel(d, any_dims=True), oracle
 
 
+def test_pinned_3b_generate_abc(yar, pinned):
+    """The ABC planning phase on the same kernels: the 151,644-row head (text rows plus
+    ABC_END), the reference's ABC sampling defaults (native/include/lyra/types.hpp:40),
+    tokens replayed bit-exactly by the CPU sampler."""
+    rng = np.random.default_rng(4)
+    prefix = rng.integers(0, 184704, 300).tolist()
+    smp = dict(temperature=0.7, top_p=0.9, top_k=30, repetition_penalty=1.005, penalty_window=100, min_tokens=12,
+               max_tokens=12)
+    s = pinned.session(max_rows=1, max_ctx=512)
+    tokens, timing, truncated = s.generate(prefix, yar.Sampling(**smp), seed=11, phase="abc")
+    assert len(tokens) == 12 and truncated
+    assert all(0 <= t < 151643 for t in tokens)
+    assert s.logits(0, "abc").shape == (151644,)
+    replay_generation(yar, pinned, prefix, tokens, smp, 11, "abc")
+
+
 def test_pinned_width_two_layers_vs_oracle(yar, wide2):
     """Radius here (oracle with FP32 vs FP64 accumulation): logits max-abs 0.031, rel-L2
     0.0073; layer-0 K at decode positions: 0.006% of values flip, rel-L2 1.3e-5."""

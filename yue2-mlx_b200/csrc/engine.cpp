@@ -178,6 +178,14 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
   if (start0 + n > s.capacity[row]) throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
   cudaStream_t st = s.stream;
   const int H = d.hidden, QKV = d.qkv_rows();
+  // Linears on the tcgen05 tensor-core GEMM where the shape allows (K % 64, N % 128);
+  // otherwise the mma.sync GEMM.
+  auto gemm = [&](const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epi) {
+    if (gemm_tc_supported(A, M, K, W, N, C, ldc))
+      launch_gemm_tc(A, M, K, W, N, C, ldc, epi, s.d_error, st);
+    else
+      launch_gemm(A, M, K, W, N, C, ldc, epi, st);
+  };
   for (int c0 = 0; c0 < n; c0 += chunk) {
     if (cancel && cancel(cancel_ctx)) throw Error("InterruptedError", "Cancelled during prefill");
     const int T = std::min(chunk, n - c0), start = start0 + c0;
@@ -186,18 +194,21 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
     for (int l = 0; l < d.layers; ++l) {
       const LayerWeights &w = m.layers[l];
       launch_rmsnorm_rows(s.px, w.ln1, T, H, d.eps, s.ph, st);
-      launch_gemm(s.ph, T, H, w.qkv, QKV, s.pqkv, QKV, kEpiStore, st);
+      gemm(s.ph, T, H, w.qkv, QKV, s.pqkv, QKV, kEpiStore);
       launch_qkv_post_prefill(m, s, l, row, start, T, st);
       launch_attn_prefill(m, s, l, row, start, T, st);
-      launch_gemm(s.pattn, T, d.qdim(), w.o, H, s.px, H, kEpiResidual, st);
+      gemm(s.pattn, T, d.qdim(), w.o, H, s.px, H, kEpiResidual);
       launch_rmsnorm_rows(s.px, w.ln2, T, H, d.eps, s.ph, st);
-      launch_gemm(s.ph, T, H, w.gu, 2 * d.ffn, s.pmlp, d.ffn, kEpiSwiGLU, st);
-      launch_gemm(s.pmlp, T, d.ffn, w.down, H, s.px, H, kEpiResidual, st);
+      gemm(s.ph, T, H, w.gu, 2 * d.ffn, s.pmlp, d.ffn, kEpiSwiGLU);
+      gemm(s.pmlp, T, d.ffn, w.down, H, s.px, H, kEpiResidual);
     }
     if (c0 + T == n)
       project(m, s, s.px + size_t(T - 1) * H, H, 1, phase, s.logits + size_t(row) * s.logit_stride);
     YAR_CUDA(cudaStreamSynchronize(st));
   }
+  int err = 0;
+  YAR_CUDA(cudaMemcpy(&err, s.d_error, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) throw Error("RuntimeError", "device error flags " + std::to_string(err));
   s.pos[row] = start0 + n;
   YAR_CUDA(cudaMemcpyAsync(s.d_pos + row, &s.pos[row], sizeof(int), cudaMemcpyHostToDevice, st));
   YAR_CUDA(cudaStreamSynchronize(st));

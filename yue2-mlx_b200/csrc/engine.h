@@ -97,6 +97,11 @@ void launch_rmsnorm_rows(const bf16 *x, const bf16 *w, int T, int H, float eps, 
                          cudaStream_t st);
 void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue,
                  cudaStream_t st);
+// Prefill linears on tcgen05 (kernels_gemm_tc.cu); `error` receives expired-wait flags.
+bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const bf16 *C, int ldc);
+void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
+                    cudaStream_t st);
+void configure_gemm_tc_kernels();
 void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
                              cudaStream_t st);
 void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int start, int T,

@@ -221,6 +221,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     configure_gemv_tma_kernels();
     configure_persistent_kernels();
     configure_sampler_kernels();
+    configure_gemm_tc_kernels();
     size_t off = 0;
     auto take = [&](size_t bytes) {
       const size_t o = off;
