@@ -4,12 +4,13 @@
 // The cached positions of a row are cut into chunks of 64 (one chunk never straddles a
 // page of >= 64 positions, so its K rows and its V rows are each one contiguous 16 KB
 // block for head_dim 128). A split is a run of consecutive chunks; a unit = (row, kv head,
-// split) is processed by a team of 128 threads (4 warps):
+// split) is processed by 256 threads (8 warps):
 //   1. q-norm + RoPE of the group's G q heads; the unit holding the new position also
 //      norms and ropes the new k and appends k, v to the paged cache;
-//   2. per chunk (rows staged in shared memory): FP32 scores with one (head, position)
-//      per thread, the chunk's max and exp-sum, P.V with two dims per thread, folded into
-//      the running (max, sum, o) with exp rescaling;
+//   2. per chunk (rows staged in shared memory): FP32 scores with 2-4 threads per (head,
+//      position), the chunk's max and exp-sum, P.V with one output dim per thread (or a
+//      fixed split of the positions when G x D < 256), folded into the running (max, sum,
+//      o) with exp rescaling;
 //   3. a partial (max, sum, o[D]) per q head; the last of the row's splits to arrive merges
 //      them into the BF16 head outputs (native/src/ar.cpp:88-96, :276-291;
 //      oracle/port/lyra/ar.py:131-145).
@@ -71,7 +72,7 @@ __device__ __forceinline__ void norm_rope_head(float *v, const bf16 *w, const fl
   __syncwarp();
 }
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;  // one unit at a time on all 8 warps
 
 struct DecodeAttnParams {
   AttnGeom g;
@@ -233,35 +234,42 @@ __device__ void attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const
   team_sync(bar_id);
 }
 
-// Running state of one thread: q head tid / 64 (when < G), output dims (tid % 64) * D/64.
+// Running state of one thread: output o = tid / PS (q head o / D, dim o % D), where
+// PS = 256 / (G x D) threads share an output (1 for the pinned GQA pair of 128-dim heads).
 template <int D>
 struct AttnAcc {
-  float m, l, o[D / 64];
+  float m, l, o;
 };
 template <int D>
 __device__ __forceinline__ void attn_acc_init(AttnAcc<D> &a) {
   a.m = -INFINITY;
   a.l = 0.f;
-#pragma unroll
-  for (int e = 0; e < D / 64; ++e) a.o[e] = 0.f;
+  a.o = 0.f;
 }
 
 // Step 2, one chunk: rows [0, n_main) of Ks/Vs (shared memory, row pitch D) and, when
-// `extra`, the new position (sm.knew/vnew) as row n_main. Ends with a team barrier.
+// `extra`, the new position (sm.knew/vnew) as row n_main. Ends with a barrier.
 template <int D, int G>
 __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *Vs, int n_main, bool extra, float scale,
                            AttnAcc<D> &acc, int tid, int bar_id) {
-  constexpr int NC = D / 8, DPT = D / 64;
-  const int hd = tid >> 6, i = tid & 63, lane = tid & 31, warp = tid >> 5;
+  constexpr int NC = D / 8;                             // 16-byte chunks per row
+  constexpr int TP = kAttnThreads / (G * kKvChunk);     // threads per (head, position)
+  constexpr int CPT = NC / TP;                          // chunks per thread
+  constexpr int PS = kAttnThreads / (G * D);            // threads per output dim
+  constexpr int WPH = kAttnThreads / 32 / G;            // warps per head in the score phase
+  static_assert(TP >= 1 && CPT >= 1 && PS >= 1 && (CPT & (CPT - 1)) == 0, "unsupported attention shape");
+  const int lane = tid & 31, warp = tid >> 5;
+  const int pair = tid / TP, part = tid % TP, hd = pair / kKvChunk, i = pair % kKvChunk;
   const int n = n_main + (extra ? 1 : 0);
-  float sc = -INFINITY;
-  if (hd < G && i < n) {
+  // Scores: thread part p of (hd, i) covers chunks [p * CPT, p * CPT + CPT) of row i, in an
+  // order rotated by the row so that the rows of a quarter-warp hit distinct banks.
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if (i < n) {
     const bf16 *kr = i < n_main ? Ks + size_t(i) * D : sm.knew;
     const float *qh = sm.q_s[hd];
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-    for (int j = 0; j < NC; ++j) {
-      const int c = (j + i) & (NC - 1);  // rotated: the 8 rows of a quarter-warp hit distinct banks
+    for (int j = 0; j < CPT; ++j) {
+      const int c = part * CPT + ((j + 2 * i + part) & (CPT - 1));
       const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + c * 8);
       const float4 q0 = *reinterpret_cast<const float4 *>(qh + c * 8);
       const float4 q1 = *reinterpret_cast<const float4 *>(qh + c * 8 + 4);
@@ -274,60 +282,64 @@ __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *V
       a2 = fmaf(q1.z, bf_lo(k8.w), a2);
       a3 = fmaf(q1.w, bf_hi(k8.w), a3);
     }
-    sc = ((a0 + a1) + (a2 + a3)) * scale;
   }
+  float dot = (a0 + a1) + (a2 + a3);
+#pragma unroll
+  for (int o = 1; o < TP; o <<= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
+  const float sc = i < n ? dot * scale : -INFINITY;
   const float mx = warp_max(sc);
   if (lane == 0) sm.red[0][warp] = mx;
   team_sync(bar_id);
-  const float mc = hd < G ? fmaxf(sm.red[0][2 * hd], sm.red[0][2 * hd + 1]) : -INFINITY;
-  const float pe = (hd < G && i < n) ? expf(sc - mc) : 0.f;
-  if (hd < G) sm.p_s[hd][i] = pe;
-  const float ps = warp_sum(pe);
+  float mc = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < WPH; ++w) mc = fmaxf(mc, sm.red[0][hd * WPH + w]);
+  const float pe = i < n ? expf(sc - mc) : 0.f;
+  if (part == 0) sm.p_s[hd][i] = pe;
+  const float ps = warp_sum(part == 0 ? pe : 0.f);
   if (lane == 0) sm.red[1][warp] = ps;
   team_sync(bar_id);
-  if (hd < G) {
-    const float lc = sm.red[1][2 * hd] + sm.red[1][2 * hd + 1];
-    const float *pr = sm.p_s[hd];
-    const int d0 = i * DPT;
-    float oc[DPT];
+  // P.V: output o = tid / PS (head oh, dim od); its PS threads take positions r = q (mod PS).
+  const int o = tid / PS, q = tid % PS, oh = o / D, od = o % D;
+  float lcv = 0.f;
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) oc[e] = 0.f;
-    auto add_row = [&](float pv, const bf16 *vr) {
-      if constexpr (DPT == 2) {
-        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vr + d0);
-        oc[0] = fmaf(pv, bf_lo(v2), oc[0]);
-        oc[1] = fmaf(pv, bf_hi(v2), oc[1]);
-      } else {
-        oc[0] = fmaf(pv, bf2f(vr[d0]), oc[0]);
-      }
-    };
-#pragma unroll 4
-    for (int r = 0; r < n_main; ++r) add_row(pr[r], Vs + size_t(r) * D);
-    if (extra) add_row(pr[n_main], sm.vnew);
-    const float mn = fmaxf(acc.m, mc);
-    const float ca = expf(acc.m - mn), cb = expf(mc - mn);
-    acc.l = acc.l * ca + lc * cb;
+  for (int w = 0; w < WPH; ++w) lcv += sm.red[1][oh * WPH + w];
+  float mcv = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) acc.o[e] = acc.o[e] * ca + oc[e] * cb;
-    acc.m = mn;
+  for (int w = 0; w < WPH; ++w) mcv = fmaxf(mcv, sm.red[0][oh * WPH + w]);
+  const float *pr = sm.p_s[oh];
+  float e0 = 0.f, e1 = 0.f;
+  int r = q;
+  for (; r + PS < n_main; r += 2 * PS) {
+    e0 = fmaf(pr[r], bf2f(Vs[size_t(r) * D + od]), e0);
+    e1 = fmaf(pr[r + PS], bf2f(Vs[size_t(r + PS) * D + od]), e1);
   }
+  if (r < n_main) e0 = fmaf(pr[r], bf2f(Vs[size_t(r) * D + od]), e0);
+  if (extra && (n_main % PS) == q) e1 = fmaf(pr[n_main], bf2f(sm.vnew[od]), e1);
+  float oc = e0 + e1;
+#pragma unroll
+  for (int w = 1; w < PS; w <<= 1) oc += __shfl_xor_sync(0xFFFFFFFFu, oc, w);
+  const float mn = fmaxf(acc.m, mcv);
+  const float ca = expf(acc.m - mn), cb = expf(mcv - mn);
+  acc.l = acc.l * ca + lcv * cb;
+  acc.o = acc.o * ca + oc * cb;
+  acc.m = mn;
   team_sync(bar_id);
 }
 
 // Merge the n_active split partials of the G heads of (row, kv_head) into the BF16 head
-// outputs. Thread t owns output dims (t % 64) * D/64 of head t / 64 and reads those dims
-// plus (m, l) of up to 8 splits in one round trip; batches fold into the running (M, L,
-// O) with exp rescaling, in split order. The merging unit resets the arrival counter.
+// outputs. Thread t < G x D owns output t (head t / D, dim t % D) and reads that dim plus
+// (m, l) of up to 8 splits in one round trip; batches fold into the running (M, L, O)
+// with exp rescaling, in split order. The merging unit resets the arrival counter.
 template <int D, int G>
 __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, int kvh, int row, int n_active,
                            int tid) {
-  constexpr int DPT = D / 64, MB = 8;
-  const int hd = tid >> 6, i = tid & 63;
-  if (hd < G) {
+  constexpr int MB = 8;
+  if (tid < G * D) {
+    const int hd = tid / D, d = tid % D;
     const float *pr0 = part_base + size_t(kvh * G + hd) * p.max_splits * (D + 2);
-    float M = -INFINITY, Ls = 0.f, O[DPT] = {};
+    float M = -INFINITY, Ls = 0.f, O = 0.f;
     for (int s0 = 0; s0 < n_active; s0 += MB) {
-      float mv[MB], lv[MB], ov[MB][DPT];
+      float mv[MB], lv[MB], ov[MB];
 #pragma unroll
       for (int j = 0; j < MB; ++j) {
         mv[j] = -INFINITY;
@@ -335,8 +347,7 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
           const float *pr = pr0 + size_t(s0 + j) * (D + 2);
           mv[j] = __ldcg(pr);
           lv[j] = __ldcg(pr + 1);
-#pragma unroll
-          for (int e = 0; e < DPT; ++e) ov[j][e] = __ldcg(pr + 2 + i * DPT + e);
+          ov[j] = __ldcg(pr + 2 + d);
         }
       }
       float Mb = M;
@@ -345,22 +356,17 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
       if (Mb == -INFINITY) continue;
       const float r = M == -INFINITY ? 0.f : expf(M - Mb);
       Ls *= r;
-#pragma unroll
-      for (int e = 0; e < DPT; ++e) O[e] *= r;
+      O *= r;
 #pragma unroll
       for (int j = 0; j < MB; ++j) {
         if (mv[j] == -INFINITY) continue;
         const float c = expf(mv[j] - Mb);
         Ls += lv[j] * c;
-#pragma unroll
-        for (int e = 0; e < DPT; ++e) O[e] += ov[j][e] * c;
+        O += ov[j] * c;
       }
       M = Mb;
     }
-    const float inv = 1.0f / Ls;
-#pragma unroll
-    for (int e = 0; e < DPT; ++e)
-      p.out[size_t(row) * p.g.qdim + (kvh * G + hd) * D + i * DPT + e] = f2bf(O[e] * inv);
+    p.out[size_t(row) * p.g.qdim + (kvh * G + hd) * D + d] = f2bf(O * (1.0f / Ls));
   }
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
 }
@@ -370,14 +376,13 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
 template <int D, int G>
 __device__ bool attn_finish(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const AttnAcc<D> &acc, int row,
                             int kvh, int split, int n_splits, int tid, int bar_id) {
-  constexpr int DPT = D / 64;
-  const int hd = tid >> 6, i = tid & 63;
+  constexpr int PS = kAttnThreads / (G * D);
+  const int o = tid / PS, hd = o / D, d = o % D;
   float *part_base = p.part + (size_t(row) * p.g.heads) * p.max_splits * (D + 2);
-  if (hd < G) {
+  if (tid % PS == 0) {
     float *pr = part_base + (size_t(kvh * G + hd) * p.max_splits + split) * (D + 2);
-#pragma unroll
-    for (int e = 0; e < DPT; ++e) pr[2 + i * DPT + e] = acc.o[e];
-    if (i == 0) {
+    pr[2 + d] = acc.o;
+    if (d == 0) {
       pr[0] = acc.m;
       pr[1] = acc.l;
     }

@@ -4,7 +4,7 @@
 // matrix, both row-major ("K-major") BF16; FP32 accumulation in tensor memory. One CTA per
 // 128 x 128 output tile, 128 threads:
 //   * lane 0 of warp 0 streams 64-wide K slices of the A and W tiles with TMA
-//     (cp.async.bulk.tensor, SWIZZLE_128B) into a 4-stage shared-memory ring;
+//     (cp.async.bulk.tensor, SWIZZLE_128B) into a 6-stage shared-memory ring;
 //   * lane 0 of warp 1 issues tcgen05.mma (kind::f16, BF16 x BF16 -> FP32, M = N = 128,
 //     K = 16 per instruction) on each slice and releases the slice with tcgen05.commit;
 //   * after the last slice all four warps read their 32 TMEM lanes (= tile rows) with
@@ -19,7 +19,7 @@
 
 namespace yar {
 
-constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 64, kTcStages = 4, kTcThreads = 128;
+constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 64, kTcStages = 6, kTcThreads = 128;
 constexpr int kTcTileA = kTcBM * kTcBK * 2;  // 16 KB
 constexpr int kTcTileB = kTcBN * kTcBK * 2;  // 16 KB
 constexpr int kTcSmem = kTcStages * (kTcTileA + kTcTileB) + 1024;  // + alignment slack

@@ -65,7 +65,7 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
   return v;
 }
 
-// True on every thread of the team when `v` is true on any of its threads.
+// True on every consumer thread when `v` is true on any of them (barrier `bar_id`).
 __device__ __forceinline__ bool team_any(int bar_id, bool v) {
   int r;
   asm volatile(
@@ -78,7 +78,7 @@ __device__ __forceinline__ bool team_any(int bar_id, bool v) {
 
 // The attention units of one step: rows in order; an active row has kv_heads x n_splits
 // units (kv head major), an inactive row kv_heads units without work, each standing in for
-// its kv head's arrival. Unit u runs on CTA u % grid; the CTA's k-th unit on team k % 2.
+// its kv head's arrival. Unit u runs on CTA u % grid, on all its consumer warps.
 // Its chunks travel through the CTA's weight ring as stages (K rows, then V rows),
 // issued right after the layer's QKV stages.
 template <int NB>
@@ -313,10 +313,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   // Layout: ring | act (GEMV activations) aliased with the attention teams' scratch (the
   // two are never live at once) | group partials.
   constexpr size_t kActBytes = size_t(NB) * kPersistMaxK * 2;
-  constexpr size_t kUnion = kActBytes > 2 * sizeof(ASm) ? kActBytes : 2 * sizeof(ASm);
+  constexpr size_t kUnion = kActBytes > sizeof(ASm) ? kActBytes : sizeof(ASm);
   bf16 *ring = reinterpret_cast<bf16 *>(smem_raw);
   bf16 *act = reinterpret_cast<bf16 *>(smem_raw + NS * kRingStageBytes);
-  ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kRingStageBytes);
+  ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kRingStageBytes);  // attention scratch
   float *gred = reinterpret_cast<float *>(smem_raw + NS * kRingStageBytes + kUnion);
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
   __shared__ float red[NB * kRingConsumers];
@@ -463,7 +463,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   }
   const int U = step_units(srows, kvh_n, nsplit);
 
-  const int team = warp / 4, ttid = ctid % kAttnThreads;
   uint4 wn_next[4];  // RMSNorm weight chunks of the next norm-prologue GEMV, loaded before its wait
   ring_norm_w_load(task(0, 0), wn_next, ctid);
   for (int l = 0; l < nL; ++l) {
@@ -480,10 +479,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       signal(c_op(l, 0));
       stamp(5 * l, 3);
     }
-    // Attention: the CTA's units alternate between its two 4-warp teams; each unit's KV
-    // chunks are ring stages (owned by that team: its 4 warps release each with count 2).
+    // Attention: the CTA's units, one after another on all consumer warps; each unit's KV
+    // chunks are ring stages (every consumer warp releases each once).
     float wv[4];
-    if (int(blockIdx.x) + team * int(gridDim.x) < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ttid);
+    if (int(blockIdx.x) < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
     wait_for(c_op(l, 0), (epoch + 1) * all);
     stamp(5 * l + 1, 0);
     {
@@ -493,42 +492,39 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       for (int k = 0, u = blockIdx.x; u < U; ++k, u += gridDim.x) {
         const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
         const int nch = ui.c1 - ui.c0;
-        if ((k & 1) == team) {
-          unsigned long long *st =
-              (p.trace && team == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
-          ASm &tsm = team_sm[team];
-          const AttnRow<128> &rs = rowst[ui.row];
-          if (ui.active && !bad) attn_qk<128, 2>(ap, tsm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ttid, 2 + team);
-          attn_stamp(st, 3, ttid);
-          AttnAcc<128> acc;
-          attn_acc_init(acc);
-          for (int j = 0; j < nch; ++j) {
-            const long long ij = itk + j;
-            const int sidx = int(ij % NS);
-            bool failed = false;
-            if (!bad) failed = !mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
-            if (team_any(2 + team, failed)) {
-              if (ttid == 0 && !bad) atomicOr(p.error, 8);
-              bad = true;
-            }
-            if (!bad) {
-              const bf16 *ks = ring + size_t(sidx) * 8 * kRingRowPitch;
-              const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
-              attn_chunk<128, 2>(tsm, ks, ks + kKvChunk * 128, n_main, rs.pos - base < kKvChunk, ap.g.scale, acc,
-                                 ttid, 2 + team);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cnt(&empty[sidx], 2);
+        unsigned long long *st =
+            (p.trace && k == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
+        const AttnRow<128> &rs = rowst[ui.row];
+        if (ui.active && !bad) attn_qk<128, 2>(ap, *team_sm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ctid, 1);
+        attn_stamp(st, 3, ctid);
+        AttnAcc<128> acc;
+        attn_acc_init(acc);
+        for (int j = 0; j < nch; ++j) {
+          const long long ij = itk + j;
+          const int sidx = int(ij % NS);
+          bool failed = false;
+          if (!bad) failed = !mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
+          if (team_any(1, failed)) {
+            if (ctid == 0 && !bad) atomicOr(p.error, 8);
+            bad = true;
           }
-          attn_stamp(st, 4, ttid);
-          bool merged = false;
-          if (ui.active && !bad) merged = attn_finish<128, 2>(ap, tsm, acc, ui.row, ui.kvh, ui.split, ui.n_splits, ttid, 2 + team);
-          attn_stamp(st, 5, ttid);
-          // An inactive row (or a failed step) counts each kv head once, from split 0.
-          if (merged || (ui.split == 0 && (bad || !ui.active))) {
-            team_sync(2 + team);
-            if (ttid == 0) red_release_add(p.ctr + c_op(l, 1), 1);
+          if (!bad) {
+            const bf16 *ks = ring + size_t(sidx) * 8 * kRingRowPitch;
+            const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
+            attn_chunk<128, 2>(*team_sm, ks, ks + kKvChunk * 128, n_main, rs.pos - base < kKvChunk, ap.g.scale, acc,
+                               ctid, 1);
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[sidx]);
+        }
+        attn_stamp(st, 4, ctid);
+        bool merged = false;
+        if (ui.active && !bad) merged = attn_finish<128, 2>(ap, *team_sm, acc, ui.row, ui.kvh, ui.split, ui.n_splits, ctid, 1);
+        attn_stamp(st, 5, ctid);
+        // An inactive row (or a failed step) counts each kv head once, from split 0.
+        if (merged || (ui.split == 0 && (bad || !ui.active))) {
+          consumer_sync();
+          if (ctid == 0) red_release_add(p.ctr + c_op(l, 1), 1);
         }
         itk += nch;
       }
@@ -624,7 +620,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
 }
 
 size_t persistent_smem(int NB) {
-  const size_t act = size_t(NB) * kPersistMaxK * 2, teams = 2 * sizeof(AttnTeamSmem<128, 2>);
+  const size_t act = size_t(NB) * kPersistMaxK * 2, teams = sizeof(AttnTeamSmem<128, 2>);
   return size_t(kPersistStages) * kRingStageBytes + (act > teams ? act : teams) + size_t(ring_gred_floats(NB)) * 4;
 }
 
