@@ -107,10 +107,11 @@ __host__ __device__ __forceinline__ SplitPlan split_plan(int L, int max_splits) 
 // Shared memory of one team.
 template <int D, int G>
 struct __align__(16) AttnTeamSmem {
-  float q_s[G][D];             // normed, roped q (BF16 values)
+  bf16 q_b[G][D];              // normed, roped q (BF16-exact values)
   bf16 knew[D], vnew[D];       // the new position's k (normed, roped) and v, as cached
   float p_s[G][kKvChunk];      // exp(score - chunk max)
   float red[2][kAttnThreads / 32];
+  float pvp[kAttnThreads / G / (D / 8)][G * D];  // P.V partials per position phase
   int last_flag;
 };
 
@@ -217,7 +218,7 @@ __device__ void attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const
     norm_rope_regs<D>(hv, wv, rs.cosr, rs.sinr, g.eps, lane);
     if (!is_k) {
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) sm.q_s[warp][lane + 32 * i] = hv[i];
+      for (int i = 0; i < NPL; ++i) sm.q_b[warp][lane + 32 * i] = f2bf(hv[i]);
     } else {
       bf16 *kd = kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, rs.pos);
       bf16 *vd = kv_row_ptr<D>(p, rs, row, p.layer, 1, kvh, rs.pos);
@@ -234,8 +235,7 @@ __device__ void attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const
   team_sync(bar_id);
 }
 
-// Running state of one thread: output o = tid / PS (q head o / D, dim o % D), where
-// PS = 256 / (G x D) threads share an output (1 for the pinned GQA pair of 128-dim heads).
+// Running state of one thread: output tid (q head tid / D, dim tid % D) when tid < G x D.
 template <int D>
 struct AttnAcc {
   float m, l, o;
@@ -249,80 +249,119 @@ __device__ __forceinline__ void attn_acc_init(AttnAcc<D> &a) {
 
 // Step 2, one chunk: rows [0, n_main) of Ks/Vs (shared memory, row pitch D) and, when
 // `extra`, the new position (sm.knew/vnew) as row n_main. Ends with a barrier.
+//   Scores: the threads of head hd (256 / G of them) form 4-thread groups; part p of a
+//   group holds its quarter of q in registers and dots it with that quarter of rows ps,
+//   ps + slots, ... (16-byte K loads in an order rotated by row and part, so a
+//   quarter-warp never hits one bank group twice); the 4 parts are added by shuffles.
+//   P.V: thread (head hd, dim group dg of 8 dims, phase q) sums p_r * V[r][8 dg .. +7]
+//   over the rows r = q (mod phases) with 16-byte V loads; the phases are added in order
+//   through shared memory, one output per thread.
 template <int D, int G>
 __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *Vs, int n_main, bool extra, float scale,
                            AttnAcc<D> &acc, int tid, int bar_id) {
-  constexpr int NC = D / 8;                             // 16-byte chunks per row
-  constexpr int TP = kAttnThreads / (G * kKvChunk);     // threads per (head, position)
-  constexpr int CPT = NC / TP;                          // chunks per thread
-  constexpr int PS = kAttnThreads / (G * D);            // threads per output dim
-  constexpr int WPH = kAttnThreads / 32 / G;            // warps per head in the score phase
-  static_assert(TP >= 1 && CPT >= 1 && PS >= 1 && (CPT & (CPT - 1)) == 0, "unsupported attention shape");
+  constexpr int NC = D / 8;                  // 16-byte chunks per row
+  constexpr int THD = kAttnThreads / G;      // threads per head
+  constexpr int CP = NC / 4;                 // chunks per part
+  constexpr int SLOTS = THD / 4;             // position slots per head
+  constexpr int PPT = kKvChunk / SLOTS;      // positions per thread
+  constexpr int WPH = THD / 32;              // warps per head
+  constexpr int NPH = THD / NC;              // P.V position phases
+  static_assert(CP >= 1 && (CP & (CP - 1)) == 0 && PPT >= 1 && NPH >= 1, "unsupported attention shape");
   const int lane = tid & 31, warp = tid >> 5;
-  const int pair = tid / TP, part = tid % TP, hd = pair / kKvChunk, i = pair % kKvChunk;
+  const int hd = tid / THD, u = tid % THD, part = u % 4, ps = u / 4;
   const int n = n_main + (extra ? 1 : 0);
-  // Scores: thread part p of (hd, i) covers chunks [p * CPT, p * CPT + CPT) of row i, in an
-  // order rotated by the row so that the rows of a quarter-warp hit distinct banks.
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  if (i < n) {
-    const bf16 *kr = i < n_main ? Ks + size_t(i) * D : sm.knew;
-    const float *qh = sm.q_s[hd];
+  // q quarter of this part, BF16 pairs.
+  uint4 qv[CP];
 #pragma unroll
-    for (int j = 0; j < CPT; ++j) {
-      const int c = part * CPT + ((j + 2 * i + part) & (CPT - 1));
-      const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + c * 8);
-      const float4 q0 = *reinterpret_cast<const float4 *>(qh + c * 8);
-      const float4 q1 = *reinterpret_cast<const float4 *>(qh + c * 8 + 4);
-      a0 = fmaf(q0.x, bf_lo(k8.x), a0);
-      a1 = fmaf(q0.y, bf_hi(k8.x), a1);
-      a2 = fmaf(q0.z, bf_lo(k8.y), a2);
-      a3 = fmaf(q0.w, bf_hi(k8.y), a3);
-      a0 = fmaf(q1.x, bf_lo(k8.z), a0);
-      a1 = fmaf(q1.y, bf_hi(k8.z), a1);
-      a2 = fmaf(q1.z, bf_lo(k8.w), a2);
-      a3 = fmaf(q1.w, bf_hi(k8.w), a3);
+  for (int c = 0; c < CP; ++c) qv[c] = *reinterpret_cast<const uint4 *>(&sm.q_b[hd][(part * CP + c) * 8]);
+  float sc[PPT];
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    const int i = ps + k * SLOTS;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (i < n) {
+      const bf16 *kr = i < n_main ? Ks + size_t(i) * D : sm.knew;
+#pragma unroll
+      for (int j = 0; j < CP; ++j) {
+        const int cj = (j + ps * (CP > 1 ? CP / 2 : 1) + (part >> 1)) & (CP - 1);
+        const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + (part * CP + cj) * 8);
+        uint4 q8 = qv[0];
+#pragma unroll
+        for (int c = 1; c < CP; ++c)
+          if (c == cj) q8 = qv[c];
+        a0 = fmaf(bf_lo(q8.x), bf_lo(k8.x), a0);
+        a1 = fmaf(bf_hi(q8.x), bf_hi(k8.x), a1);
+        a2 = fmaf(bf_lo(q8.y), bf_lo(k8.y), a2);
+        a3 = fmaf(bf_hi(q8.y), bf_hi(k8.y), a3);
+        a0 = fmaf(bf_lo(q8.z), bf_lo(k8.z), a0);
+        a1 = fmaf(bf_hi(q8.z), bf_hi(k8.z), a1);
+        a2 = fmaf(bf_lo(q8.w), bf_lo(k8.w), a2);
+        a3 = fmaf(bf_hi(q8.w), bf_hi(k8.w), a3);
+      }
     }
+    float dot = (a0 + a1) + (a2 + a3);
+    dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
+    dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
+    sc[k] = i < n ? dot * scale : -INFINITY;
   }
-  float dot = (a0 + a1) + (a2 + a3);
+  float mx = sc[0];
 #pragma unroll
-  for (int o = 1; o < TP; o <<= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
-  const float sc = i < n ? dot * scale : -INFINITY;
-  const float mx = warp_max(sc);
+  for (int k = 1; k < PPT; ++k) mx = fmaxf(mx, sc[k]);
+  mx = warp_max(mx);
   if (lane == 0) sm.red[0][warp] = mx;
   team_sync(bar_id);
   float mc = -INFINITY;
 #pragma unroll
   for (int w = 0; w < WPH; ++w) mc = fmaxf(mc, sm.red[0][hd * WPH + w]);
-  const float pe = i < n ? expf(sc - mc) : 0.f;
-  if (part == 0) sm.p_s[hd][i] = pe;
-  const float ps = warp_sum(part == 0 ? pe : 0.f);
-  if (lane == 0) sm.red[1][warp] = ps;
-  team_sync(bar_id);
-  // P.V: output o = tid / PS (head oh, dim od); its PS threads take positions r = q (mod PS).
-  const int o = tid / PS, q = tid % PS, oh = o / D, od = o % D;
-  float lcv = 0.f;
+  float pt = 0.f;
 #pragma unroll
-  for (int w = 0; w < WPH; ++w) lcv += sm.red[1][oh * WPH + w];
-  float mcv = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < WPH; ++w) mcv = fmaxf(mcv, sm.red[0][oh * WPH + w]);
-  const float *pr = sm.p_s[oh];
-  float e0 = 0.f, e1 = 0.f;
-  int r = q;
-  for (; r + PS < n_main; r += 2 * PS) {
-    e0 = fmaf(pr[r], bf2f(Vs[size_t(r) * D + od]), e0);
-    e1 = fmaf(pr[r + PS], bf2f(Vs[size_t(r + PS) * D + od]), e1);
+  for (int k = 0; k < PPT; ++k) {
+    const int i = ps + k * SLOTS;
+    const float pe = i < n ? expf(sc[k] - mc) : 0.f;
+    if (part == 0) sm.p_s[hd][i] = pe;
+    pt += pe;
   }
-  if (r < n_main) e0 = fmaf(pr[r], bf2f(Vs[size_t(r) * D + od]), e0);
-  if (extra && (n_main % PS) == q) e1 = fmaf(pr[n_main], bf2f(sm.vnew[od]), e1);
-  float oc = e0 + e1;
+  const float psum = warp_sum(part == 0 ? pt : 0.f);
+  if (lane == 0) sm.red[1][warp] = psum;
+  team_sync(bar_id);
+  // P.V partials.
+  {
+    const int dg = u % NC, q = u / NC;
+    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = q; r < n; r += NPH) {
+      const float pr = sm.p_s[hd][r];
+      const uint4 v8 = *reinterpret_cast<const uint4 *>((r < n_main ? Vs + size_t(r) * D : sm.vnew) + dg * 8);
+      o8[0] = fmaf(pr, bf_lo(v8.x), o8[0]);
+      o8[1] = fmaf(pr, bf_hi(v8.x), o8[1]);
+      o8[2] = fmaf(pr, bf_lo(v8.y), o8[2]);
+      o8[3] = fmaf(pr, bf_hi(v8.y), o8[3]);
+      o8[4] = fmaf(pr, bf_lo(v8.z), o8[4]);
+      o8[5] = fmaf(pr, bf_hi(v8.z), o8[5]);
+      o8[6] = fmaf(pr, bf_lo(v8.w), o8[6]);
+      o8[7] = fmaf(pr, bf_hi(v8.w), o8[7]);
+    }
+    float *dst = &sm.pvp[q][hd * D + dg * 8];
+    *reinterpret_cast<float4 *>(dst) = make_float4(o8[0], o8[1], o8[2], o8[3]);
+    *reinterpret_cast<float4 *>(dst + 4) = make_float4(o8[4], o8[5], o8[6], o8[7]);
+  }
+  team_sync(bar_id);
+  if (tid < G * D) {
+    const int oh = tid / D;
+    float oc = 0.f;
 #pragma unroll
-  for (int w = 1; w < PS; w <<= 1) oc += __shfl_xor_sync(0xFFFFFFFFu, oc, w);
-  const float mn = fmaxf(acc.m, mcv);
-  const float ca = expf(acc.m - mn), cb = expf(mcv - mn);
-  acc.l = acc.l * ca + lcv * cb;
-  acc.o = acc.o * ca + oc * cb;
-  acc.m = mn;
+    for (int q = 0; q < NPH; ++q) oc += sm.pvp[q][tid];
+    float lcv = 0.f, mcv = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < WPH; ++w) {
+      lcv += sm.red[1][oh * WPH + w];
+      mcv = fmaxf(mcv, sm.red[0][oh * WPH + w]);
+    }
+    const float mn = fmaxf(acc.m, mcv);
+    const float ca = expf(acc.m - mn), cb = expf(mcv - mn);
+    acc.l = acc.l * ca + lcv * cb;
+    acc.o = acc.o * ca + oc * cb;
+    acc.m = mn;
+  }
   team_sync(bar_id);
 }
 
@@ -376,10 +415,9 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
 template <int D, int G>
 __device__ bool attn_finish(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const AttnAcc<D> &acc, int row,
                             int kvh, int split, int n_splits, int tid, int bar_id) {
-  constexpr int PS = kAttnThreads / (G * D);
-  const int o = tid / PS, hd = o / D, d = o % D;
+  const int hd = tid / D, d = tid % D;
   float *part_base = p.part + (size_t(row) * p.g.heads) * p.max_splits * (D + 2);
-  if (tid % PS == 0) {
+  if (tid < G * D) {
     float *pr = part_base + (size_t(kvh * G + hd) * p.max_splits + split) * (D + 2);
     pr[2 + d] = acc.o;
     if (d == 0) {
