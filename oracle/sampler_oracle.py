@@ -27,6 +27,14 @@ Two layers:
 
 Top-p uses the same ``e_i``: ``p_i = e_i / S`` (IEEE division), a sequential FP32
 running sum ``c_i`` and ``removed_i = i >= 1 and (c_i - p_i) > f32(top_p)``.
+
+``legacy_off`` (historical BF16 sampling, sampling.py:27 with ``legacy_off=True``) keeps
+the scores in BF16 as torch does: the penalty power has its base rounded to BF16 first
+(``bf16(penalty) ** count``, rounded to BF16), the penalty multiply / divide and the
+temperature division (by the FP32 temperature) round to BF16, the nucleus probabilities
+are ``bf16(e_i / S)``, the cumulative sum is an FP32 running sum rounded to BF16 at each
+row, ``preceding = bf16(cum_i - p_i)`` is compared against ``bf16(top_p)``, and the
+first three rows are always kept (sampling.py:50).
 """
 from __future__ import annotations
 
@@ -142,8 +150,14 @@ def guided(conditional, unconditional, scale: float) -> np.ndarray:
     return bf16_round(u + scaled)
 
 
+def legacy_alpha(penalty: float, count: int) -> np.float32:
+    """BF16 ``penalty ** count`` of the BF16 path: base rounded to BF16, result to BF16."""
+    base = float(bf16_round(np.array([penalty], F32))[0])
+    return bf16_round(np.array([F32(base ** int(count))], F32))[0]
+
+
 def filter_scores(logits, sampling: dict, history, step: int, phase: str | None,
-                  vocab: int | None = None):
+                  vocab: int | None = None, legacy_off: bool = False):
     """Upstream ``distribution`` on phase-local rows; returns (scores, sorted survivors).
 
     ``scores`` is the FP32 filtered vector (removed rows are -inf), as the upstream
@@ -165,14 +179,18 @@ def filter_scores(logits, sampling: dict, history, step: int, phase: str | None,
             if loc is not None and 0 <= loc < n:
                 counts[loc] = counts.get(loc, 0) + 1
         for loc, c in counts.items():
-            a = penalty_alpha(penalty, c)
+            a = legacy_alpha(penalty, c) if legacy_off else penalty_alpha(penalty, c)
             v = s[loc]
             s[loc] = F32(v * a) if v < 0 else F32(v / a)
+            if legacy_off:
+                s[loc] = bf16_round(np.array([s[loc]], F32))[0]
     t = sampling["temperature"]
     if t == 0:
         return s, None
     if t != 1:
         s = (s / F32(t)).astype(F32)
+        if legacy_off:
+            s = bf16_round(s)
     k = min(int(sampling["top_k"]), n)
     threshold = np.sort(s)[::-1][k - 1]
     s = np.where(s < threshold, F32(-np.inf), s).astype(F32)
@@ -187,10 +205,20 @@ def filter_scores(logits, sampling: dict, history, step: int, phase: str | None,
         c = F32(0.0)
         top_p = F32(sampling["top_p"])
         keep = np.ones(len(order), dtype=bool)
-        for i in range(len(order)):
-            c = F32(c + p[i])
-            if i >= 1 and F32(c - p[i]) > top_p:
-                keep[i] = False
+        if legacy_off:
+            p = bf16_round(p)
+            top_p = bf16_round(np.array([top_p], F32))[0]
+            for i in range(len(order)):
+                c = F32(c + p[i])
+                cum = bf16_round(np.array([c], F32))[0]
+                preceding = bf16_round(np.array([F32(cum - p[i])], F32))[0]
+                if i >= 3 and preceding > top_p:
+                    keep[i] = False
+        else:
+            for i in range(len(order)):
+                c = F32(c + p[i])
+                if i >= 1 and F32(c - p[i]) > top_p:
+                    keep[i] = False
         s[order[~keep]] = -np.inf
         order = order[keep]
     return s, order
@@ -212,10 +240,11 @@ def draw(scores, order, u) -> int:
 
 
 def sample(logits, sampling: dict, history, step: int, phase: str | None, seed: int,
-           stream: int = 0, unconditional=None, cfg_scale: float = 1.0, vocab: int | None = None):
+           stream: int = 0, unconditional=None, cfg_scale: float = 1.0, vocab: int | None = None,
+           legacy_off: bool = False):
     """One sampler step on phase-local BF16 logits; returns (local token, filtered scores)."""
     mixed = guided(logits, unconditional if cfg_scale != 1.0 else None, cfg_scale)
-    scores, order = filter_scores(mixed, sampling, history, step, phase, vocab)
+    scores, order = filter_scores(mixed, sampling, history, step, phase, vocab, legacy_off)
     if order is None:
         return int(np.argmax(scores)), scores
     return draw(scores, order, uniform(seed, step, stream)), scores

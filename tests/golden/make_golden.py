@@ -226,6 +226,21 @@ def make_sampler(out_dir):
             s = Sampling(temperature=.7, top_p=.9, top_k=30, repetition_penalty=1.005, penalty_window=100,
                          min_tokens=32, max_tokens=4096)
         add(f"random_{i}", v, s, hist, int(rng.integers(0, 300)), phase)
+    # legacy_off (historical BF16 sampling): the chain in BF16, nucleus keeping >= 3 rows.
+    rng_legacy = np.random.default_rng(17)
+    v = base.copy(); v[CODEC_OFFSET:CODEC_OFFSET + 5] = [5, 4, 3, 2, 1]
+    add("legacy_nucleus_keep3", v, Sampling(top_k=5, top_p=.01, min_tokens=0, repetition_penalty=1), [], 0,
+        "semantic", legacy=True)
+    for i in range(6):
+        v = (rng_legacy.standard_normal(VOCAB_SIZE) * 2.0).astype(np.float32)
+        phase = "semantic" if i < 4 else "abc"
+        hist = list(rng_legacy.integers(CODEC_OFFSET, CODEC_OFFSET + 64, size=int(rng_legacy.integers(0, 120))))
+        for t in range(len(hist)):
+            v[hist[t]] += 1.5
+        s = (Sampling(temperature=1.0, top_k=50, top_p=0.93, min_tokens=400, max_tokens=400) if i % 2 == 0 else
+             Sampling(temperature=.7, top_p=.9, top_k=30, repetition_penalty=1.005, penalty_window=100,
+                      min_tokens=32, max_tokens=4096))
+        add(f"legacy_random_{i}", v, s, hist, int(rng_legacy.integers(0, 300)), phase, legacy=True)
     # Greedy with penalty.
     v = (rng.standard_normal(VOCAB_SIZE) * 2.0).astype(np.float32)
     hist = list(rng.integers(CODEC_OFFSET, CODEC_OFFSET + 32, size=60))

@@ -139,9 +139,11 @@ def test_sampler_bit_exact_on_golden_cases(yar, tiny, golden):
     for i, c in enumerate(cases):
         logits_bits = g[f"c{i}_logits"]
         smp = yar.Sampling(**c["sampling"])
+        lg = c.get("legacy", False)
         for seed in (0, 12345):
-            tok, scores = tiny.sample(logits_bits, smp, c["history"], c["step"], c["phase"], seed)
-            want_tok, want_scores = so.sample(f(logits_bits), c["sampling"], c["history"], c["step"], c["phase"], seed)
+            tok, scores = tiny.sample(logits_bits, smp, c["history"], c["step"], c["phase"], seed, legacy_off=lg)
+            want_tok, want_scores = so.sample(f(logits_bits), c["sampling"], c["history"], c["step"], c["phase"], seed,
+                                              legacy_off=lg)
             assert tok == want_tok, (c["name"], seed)
             if c["sampling"]["temperature"] != 0:
                 np.testing.assert_array_equal(np.isfinite(scores), np.isfinite(want_scores), err_msg=c["name"])
@@ -149,8 +151,8 @@ def test_sampler_bit_exact_on_golden_cases(yar, tiny, golden):
                 np.testing.assert_array_equal(scores[fin], want_scores[fin], err_msg=c["name"])
 
 
-@pytest.mark.parametrize("cfg_scale", [1.0, 1.5])
-def test_sampler_bit_exact_random(yar, tiny, cfg_scale):
+@pytest.mark.parametrize("cfg_scale,legacy", [(1.0, False), (1.5, False), (1.0, True), (1.5, True)])
+def test_sampler_bit_exact_random(yar, tiny, cfg_scale, legacy):
     rng = np.random.default_rng(11)
     for trial in range(24):
         smp = SAMPLERS[trial % len(SAMPLERS)]
@@ -160,9 +162,10 @@ def test_sampler_bit_exact_random(yar, tiny, cfg_scale):
         step = int(rng.integers(0, 500))
         seed = int(rng.integers(0, 2**62))
         tok, scores = tiny.sample(cond, yar.Sampling(**smp), hist, step, "semantic", seed, uncond_bits=unc,
-                                  cfg_scale=cfg_scale)
+                                  cfg_scale=cfg_scale, legacy_off=legacy)
         want, want_scores = so.sample(f(cond), smp, hist, step, "semantic", seed,
-                                      unconditional=None if unc is None else f(unc), cfg_scale=cfg_scale)
+                                      unconditional=None if unc is None else f(unc), cfg_scale=cfg_scale,
+                                      legacy_off=legacy)
         assert tok == want, trial
         if smp["temperature"] != 0:
             fin = np.isfinite(want_scores)
@@ -170,7 +173,7 @@ def test_sampler_bit_exact_random(yar, tiny, cfg_scale):
             np.testing.assert_array_equal(scores[fin], want_scores[fin])
 
 
-def replay_generation(yar, model, prefix, tokens, smp, seed, phase, negative=None, cfg_scale=1.0):
+def replay_generation(yar, model, prefix, tokens, smp, seed, phase, negative=None, cfg_scale=1.0, legacy_off=False):
     """Re-derive every sampled token from the GPU's own teacher-forced logits with the
     CPU sampler; the draw contract makes this bit-exact."""
     s = model.session(max_rows=2, max_ctx=len(prefix) + smp["max_tokens"] + 8)
@@ -184,7 +187,8 @@ def replay_generation(yar, model, prefix, tokens, smp, seed, phase, negative=Non
     for step, tok in enumerate(tokens):
         cond = f(s.logits(0, phase))
         unc = f(s.logits(1, phase)) if negative is not None else None
-        want, _ = so.sample(cond, smp, history, step, phase, seed, unconditional=unc, cfg_scale=cfg_scale)
+        want, _ = so.sample(cond, smp, history, step, phase, seed, unconditional=unc, cfg_scale=cfg_scale,
+                            legacy_off=legacy_off)
         assert so.local_to_native(want, phase) == tok, step
         history.append(tok)
         if step + 1 < len(tokens):
@@ -205,6 +209,20 @@ def test_generate_sampled_replays_exactly(yar, tiny):
     other, _, _ = s.generate(prefix, yar.Sampling(**smp), seed=78, phase=None)
     assert other != tokens
     replay_generation(yar, tiny, prefix, tokens, smp, 77, None)
+
+
+def test_generate_legacy_off_replays_exactly(yar, tiny):
+    """legacy_off (historical BF16 sampling, the reference's cot=off path): the filter
+    chain in BF16 with a nucleus that keeps >= 3 rows, replayed bit-exactly by the CPU
+    restatement; it differs from the FP32 chain on the same seed."""
+    rng = np.random.default_rng(23)
+    prefix = rng.integers(0, 4096, 40).tolist()
+    smp = dict(temperature=0.7, top_p=0.9, top_k=30, repetition_penalty=1.005, penalty_window=100, min_tokens=30,
+               max_tokens=30)
+    s = tiny.session(max_rows=1, max_ctx=128)
+    tokens, _, _ = s.generate(prefix, yar.Sampling(**smp), seed=9, phase=None, legacy_off=True)
+    assert len(tokens) == 30
+    replay_generation(yar, tiny, prefix, tokens, smp, 9, None, legacy_off=True)
 
 
 def test_generate_cfg_replays_exactly(yar, tiny):
@@ -358,12 +376,12 @@ def test_pinned_width_two_layers_vs_oracle(yar, wide2):
         s.close()
 
 
-def _trace(model, rows, prompt, forced, persistent):
-    s = model.session(max_rows=2, max_ctx=400)
+def _trace(model, rows, prompt, forced, persistent, ctx=400):
+    s = model.session(max_rows=2, max_ctx=ctx)
     s.set_persistent(persistent)
     s.set_trace(persistent)  # the persistent kernel stamps its timeline: proof that it ran
     for r in range(rows):
-        s.reset(r, 400)
+        s.reset(r, ctx)
         s.prefill(r, prompt[r], phase=None)
     out = [[s.logits(r, None)] for r in range(rows)]
     for t in forced:
@@ -390,3 +408,17 @@ def test_persistent_decode_matches_per_operation_kernels(yar, wide2, rows):
     np.testing.assert_array_equal(a, b)
     np.testing.assert_array_equal(kva[0], kvb[0])
     np.testing.assert_array_equal(kva[1], kvb[1])
+
+
+def test_persistent_matches_per_operation_at_long_context(yar, wide2):
+    """~3000 cached positions: 47 chunks per kv head, so splits hold two chunks each and
+    the running (max, sum, o) is rescaled across chunks on both paths."""
+    model, _ = wide2
+    rng = np.random.default_rng(13)
+    prompt = [rng.integers(0, 4096, 2980).tolist(), rng.integers(0, 4096, 1500).tolist()]
+    forced = rng.integers(0, 4096, 6).tolist()
+    a, kva, ran = _trace(model, 2, prompt, forced, persistent=True, ctx=3072)
+    assert ran
+    b, kvb, _ = _trace(model, 2, prompt, forced, persistent=False, ctx=3072)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(kva[0], kvb[0])

@@ -150,10 +150,11 @@ def test_filter_chain_matches_upstream_distribution(golden):
     independent there, so rows may differ only among ties at the boundary score."""
     g = golden("sampler_cases.npz")
     cases = json.loads(str(g["cases"]))
-    assert len(cases) >= 15
+    assert len(cases) >= 22 and sum(c.get("legacy", False) for c in cases) >= 7
     for i, c in enumerate(cases):
         logits = ora.bf16_from_bits(g[f"c{i}_logits"])
-        scores, order = so.filter_scores(logits, c["sampling"], c["history"], c["step"], c["phase"])
+        scores, order = so.filter_scores(logits, c["sampling"], c["history"], c["step"], c["phase"],
+                                         legacy_off=c.get("legacy", False))
         finite = np.flatnonzero(np.isfinite(scores))
         ref_idx, ref_val = g[f"c{i}_idx"], g[f"c{i}_val"]
         assert len(finite) == len(ref_idx), c["name"]

@@ -164,7 +164,7 @@ class ARModel:
         return self.dims["vocab"]
 
     def sample(self, cond_bits, sampling: Sampling, history=(), step: int = 0, phase="semantic", seed: int = 0,
-               uncond_bits=None, cfg_scale: float = 1.0, want_scores: bool = True):
+               uncond_bits=None, cfg_scale: float = 1.0, want_scores: bool = True, legacy_off: bool = False):
         """The device sampler on host BF16 logits: returns (local token, FP32 scores)."""
         cond = np.ascontiguousarray(np.asarray(cond_bits, dtype=np.uint16))
         n = cond.size
@@ -175,7 +175,7 @@ class ARModel:
         _check(lib.yar_sample_host(self._h, _ptr(cond, ctypes.c_uint16),
                                    None if unc is None else _ptr(unc, ctypes.c_uint16), n, cfg_scale,
                                    ctypes.byref(sampling._c()), _ptr(hist, ctypes.c_int32), len(history), step,
-                                   PHASES[phase], seed, 0, ctypes.byref(tok),
+                                   PHASES[phase], seed, int(legacy_off), ctypes.byref(tok),
                                    None if scores is None else _ptr(scores, ctypes.c_float)))
         return tok.value, scores
 

@@ -22,7 +22,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
                      void *token_ctx, int32_t *out_tokens, int *n_out, int *truncated);
 void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
                  const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
-                 uint64_t seed, int32_t *token, float *scores);
+                 uint64_t seed, int legacy_off, int32_t *token, float *scores);
 void sample_device_noalloc(Model &m, const uint16_t *logits, long long row_stride, int rows, int n,
                            double cfg_scale, const ::yar_sampling &smp, const int32_t *history, int n_history,
                            int step, int phase, uint64_t seed, int32_t *token, float *scores,
@@ -262,9 +262,8 @@ int yar_sample_host(yar_model *model, const uint16_t *cond, const uint16_t *unco
   return guarded([&] {
     need(model && cond && sampling && token, "missing argument");
     need(n_history == 0 || history, "history pointer missing");
-    need(!legacy_off, "legacy_off (BF16 historical sampling) is not implemented");
     yar::sample_host(*model->m, cond, uncond, n, cfg_scale, *sampling, history, n_history, step, phase, seed,
-                     token, scores);
+                     legacy_off, token, scores);
   });
 }
 

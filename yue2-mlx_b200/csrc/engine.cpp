@@ -308,8 +308,17 @@ static cudaGraphExec_t step_graph(Session &s, int n_rows, int n_requests, int ph
   return exec;
 }
 
+void fill_penalty_alpha(RequestState &r, double penalty, bool legacy) {
+  const double base = legacy ? double(round_bf16(float(penalty))) : double(float(penalty));
+  for (int i = 0; i <= kMaxPenaltyWindow; ++i) {
+    const float a = float(std::pow(base, double(i)));
+    r.alpha[i] = legacy ? round_bf16(a) : a;
+  }
+}
+
 static RequestState make_request(const Model &m, const Session &s, int row_c, int row_u, int phase,
-                                 const ::yar_sampling &smp, double cfg_scale, uint64_t seed, uint32_t stream) {
+                                 const ::yar_sampling &smp, double cfg_scale, uint64_t seed, uint32_t stream,
+                                 bool legacy) {
   RequestState r;
   std::memset(&r, 0, sizeof(r));
   r.row_c = row_c;
@@ -325,8 +334,8 @@ static RequestState make_request(const Model &m, const Session &s, int row_c, in
   r.min_tokens = smp.min_tokens;
   r.max_tokens = smp.max_tokens;
   r.penalty_on = smp.repetition_penalty != 1.0;
-  for (int i = 0; i <= kMaxPenaltyWindow; ++i)
-    r.alpha[i] = float(std::pow(double(float(smp.repetition_penalty)), double(i)));
+  r.legacy = legacy ? 1 : 0;
+  fill_penalty_alpha(r, smp.repetition_penalty, legacy);
   r.seed_lo = uint32_t(seed);
   r.seed_hi = uint32_t(seed >> 32);
   r.stream = stream;
@@ -355,7 +364,6 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
   const Model &m = *s.m;
   phase_rows(m.d, phase);
   validate_sampling(smp);
-  if (legacy_off) throw Error("ValueError", "legacy_off (BF16 historical sampling) is not implemented");
   if (seed >= (uint64_t(1) << 63)) throw Error("ValueError", "seed must be an integer in [0, 2**63)");
   if (n_prefix < 1) throw Error("ValueError", "AR prefix must contain at least one token");
   if (size_t(n_prefix) + size_t(smp.max_tokens) > size_t(m.d.context))
@@ -382,7 +390,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
   }
   const double prefill_seconds = now_s() - t0;
 
-  const RequestState req = make_request(m, s, 0, cfg ? 1 : -1, phase, smp, cfg_scale, seed, 0);
+  const RequestState req = make_request(m, s, 0, cfg ? 1 : -1, phase, smp, cfg_scale, seed, 0, legacy_off != 0);
   cudaStream_t st = s.stream;
   YAR_CUDA(cudaMemcpyAsync(s.d_req, &req, sizeof(req), cudaMemcpyHostToDevice, st));
   std::vector<int> act(rows, 1);
@@ -478,7 +486,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
 // Sampler on host logits (parity tests of the filter chain and the draw).
 void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
                  const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
-                 uint64_t seed, int32_t *token, float *scores) {
+                 uint64_t seed, int legacy_off, int32_t *token, float *scores) {
   validate_sampling(smp);
   const int expected = phase == kPhaseAbc ? kEOD + 1 : phase == kPhaseSemantic ? kCodecSize + 1 : n;
   if (phase != kPhaseAbc && phase != kPhaseSemantic && phase != kPhaseFull)
@@ -510,8 +518,8 @@ void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, 
     r.min_tokens = smp.min_tokens;
     r.max_tokens = step + 1;
     r.penalty_on = smp.repetition_penalty != 1.0;
-    for (int i = 0; i <= kMaxPenaltyWindow; ++i)
-      r.alpha[i] = float(std::pow(double(float(smp.repetition_penalty)), double(i)));
+    r.legacy = legacy_off ? 1 : 0;
+    fill_penalty_alpha(r, smp.repetition_penalty, legacy_off != 0);
     r.seed_lo = uint32_t(seed);
     r.seed_hi = uint32_t(seed >> 32);
     r.step = step;

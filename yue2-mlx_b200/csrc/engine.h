@@ -75,7 +75,8 @@ struct RequestState {
   int phase, width, end_local;
   float temperature, top_p, cfg_scale;
   int top_k, window, min_tokens, max_tokens, penalty_on;
-  float alpha[kMaxPenaltyWindow + 1];  // penalty ** count in FP32
+  int legacy;  // legacy_off: the filter chain in BF16, nucleus keeps >= 3 rows
+  float alpha[kMaxPenaltyWindow + 1];  // penalty ** count (FP32; BF16 values when legacy)
   uint32_t seed_lo, seed_hi, stream;
   int step, done, n_out, error;
   int hist[kHistCap];  // ring of native ids (the last kHistCap sampled tokens)
@@ -107,6 +108,9 @@ void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int
 void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
                          cudaStream_t st);
 
+// penalty ** count per window count: FP32 (power in double of the FP32 penalty, rounded
+// once), or for legacy_off the BF16 path's BF16(BF16(penalty) ** count).
+void fill_penalty_alpha(RequestState &r, double penalty, bool legacy);
 void configure_gemv_kernels();
 void configure_gemm_kernels();
 void configure_attn_kernels();

@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       }
       if (first) {
         const float a = st.alpha[count], v = s[me];
-        s[me] = v < 0.f ? f_mul(v, a) : f_div(v, a);
+        const float r = v < 0.f ? f_mul(v, a) : f_div(v, a);
+        s[me] = st.legacy ? round_bf16(r) : r;  // legacy_off: BF16 scores
       }
     }
     __syncthreads();
@@ -219,7 +220,10 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     local = result;
   } else {
     if (st.temperature != 1.f) {
-      for (int i = tid; i < n; i += kSampThreads) s[i] = f_div(s[i], st.temperature);
+      if (st.legacy)
+        for (int i = tid; i < n; i += kSampThreads) s[i] = round_bf16(f_div(s[i], st.temperature));
+      else
+        for (int i = tid; i < n; i += kSampThreads) s[i] = f_div(s[i], st.temperature);
       __syncthreads();
     }
     stamp(3);
@@ -406,26 +410,34 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
         }
         __syncthreads();
         const float total = red_v[0];
-        for (int i = tid; i < na; i += kSampThreads) pv[i] = f_div(ev[i], total);
+        for (int i = tid; i < na; i += kSampThreads) pv[i] = st.legacy ? round_bf16(f_div(ev[i], total)) : f_div(ev[i], total);
         __syncthreads();
       }
       if (tid == 0) {
         int keep_ties = nt;
         if (st.top_p < 1.f) {
           const float total = red_v[0];
+          // Row i is removed when the mass before it exceeds top_p (from row 1 on). The
+          // legacy_off path (BF16 scores) rounds p, the running sum and the preceding mass
+          // to BF16, compares with bf16(top_p) and keeps the first three rows
+          // (vendor/yue/src/yue2/sampling.py:46-50).
+          const bool lg = st.legacy != 0;
+          const float top_p = lg ? round_bf16(st.top_p) : st.top_p;
+          const int keep_min = lg ? 3 : 1;
+          auto preceding = [&](float c, float p) { return lg ? round_bf16(f_sub(round_bf16(c), p)) : f_sub(c, p); };
           float c = 0.f;
           for (int i = 0; i < na; ++i) {
             const float pi = pv[i];
             c = f_add(c, pi);
-            if (i >= 1 && f_sub(c, pi) > st.top_p) ev[i] = -1.f;  // removed
+            if (i >= keep_min && preceding(c, pi) > top_p) ev[i] = -1.f;  // removed
           }
-          // Within the tie group p is constant and c - p never decreases, so the kept
-          // ties are a prefix of the group.
-          const float pt = f_div(et, total);
+          // Within the tie group p is constant and the preceding mass never decreases, so
+          // the kept ties are a prefix of the group.
+          const float pt = lg ? round_bf16(f_div(et, total)) : f_div(et, total);
           keep_ties = 0;
           for (int j = 0; j < nt; ++j) {
             c = f_add(c, pt);
-            if (na + j >= 1 && f_sub(c, pt) > st.top_p) break;
+            if (na + j >= keep_min && preceding(c, pt) > top_p) break;
             ++keep_ties;
           }
         }

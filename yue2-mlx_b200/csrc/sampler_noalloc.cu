@@ -106,8 +106,7 @@ void sample_device_noalloc(Model &m, const uint16_t *logits, long long row_strid
   r.min_tokens = smp.min_tokens;
   r.max_tokens = step + 1;
   r.penalty_on = smp.repetition_penalty != 1.0;
-  for (int i = 0; i <= kMaxPenaltyWindow; ++i)
-    r.alpha[i] = float(std::pow(double(float(smp.repetition_penalty)), double(i)));
+  fill_penalty_alpha(r, smp.repetition_penalty, false);
   r.seed_lo = uint32_t(seed);
   r.seed_hi = uint32_t(seed >> 32);
   r.step = step;
