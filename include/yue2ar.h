@@ -116,6 +116,18 @@ int yar_generate(yar_session *session, const int32_t *prefix, int n_prefix,
                  int32_t *out_tokens, int *n_out, int *truncated, char *timing_json,
                  size_t timing_cap);
 
+/* Many independent requests (the reference's per-song generate_tokens, sampling.cpp:185-288,
+ * run for n_requests songs at once; no CFG): request r's prefix is prefixes[sum of earlier
+ * lengths ..][prefix_lens[r]], it decodes on row r with seed seeds[r], and its native
+ * tokens (end token excluded) land in out_tokens[r * max_tokens ..], n_out[r] of them;
+ * truncated[r] is 1 when no end token was sampled. All requests step together (from 16
+ * rows on, one batched forward reads each weight once per step for every row); a finished
+ * request's row is skipped. Needs n_requests <= the session's rows. */
+int yar_generate_batch(yar_session *session, int n_requests, const int32_t *prefixes,
+                       const int32_t *prefix_lens, const yar_sampling *sampling,
+                       const uint64_t *seeds, int phase, int legacy_off, int32_t *out_tokens,
+                       int *n_out, int *truncated, char *timing_json, size_t timing_cap);
+
 /* Row-level API (ARModel::hidden/project + KVCache, ar.cpp:246-323), used by batched
  * serving and by parity tests. A row owns a page table and a position. */
 int yar_row_reset(yar_session *session, int row, int capacity);

@@ -422,3 +422,42 @@ def test_persistent_matches_per_operation_at_long_context(yar, wide2):
     b, kvb, _ = _trace(model, 2, prompt, forced, persistent=False, ctx=3072)
     np.testing.assert_array_equal(a, b)
     np.testing.assert_array_equal(kva[0], kvb[0])
+
+
+def test_generate_batch_replays_exactly(yar, wide2):
+    """18 independent requests (the batched tcgen05 forward, one weight read per step for
+    all rows): every request's tokens replay bit-exactly from teacher-forced batched steps
+    through the CPU sampler, and a batched step agrees with the rows stepped one at a time
+    within the BF16 radius."""
+    model, _ = wide2
+    rng = np.random.default_rng(31)
+    n = 18
+    prefixes = [rng.integers(0, 4096, int(rng.integers(20, 200))).tolist() for _ in range(n)]
+    seeds = [int(x) for x in rng.integers(0, 2**62, n)]
+    smp = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50, min_tokens=8,
+               max_tokens=8)
+    s = model.session(max_rows=n, max_ctx=256)
+    tokens, timing, truncated = s.generate_batch(prefixes, yar.Sampling(**smp), seeds, phase=None)
+    assert timing["forward"] == "batched_tcgen05" and timing["requests"] == n
+    assert all(len(t) == 8 for t in tokens) and all(truncated)
+    for r in range(n):
+        s.reset(r, 256)
+        s.prefill(r, prefixes[r], phase=None)
+    hist = [[] for _ in range(n)]
+    for step in range(8):
+        for r in range(n):
+            want, _ = so.sample(f(s.logits(r, None)), smp, hist[r], step, None, seeds[r])
+            assert so.local_to_native(want, None) == tokens[r][step], (r, step)
+            hist[r].append(tokens[r][step])
+        if step + 1 < 8:
+            s.step(list(range(n)), [tokens[r][step] for r in range(n)], phase=None)
+    batched = [f(s.logits(r, None)) for r in range(n)]
+    # The same last step, one row at a time (persistent kernel).
+    for r in range(n):
+        s.reset(r, 256)
+        s.prefill(r, prefixes[r] + tokens[r][:6], phase=None)
+        s.step([r], [tokens[r][6]], phase=None)
+        single = f(s.logits(r, None))
+        assert np.abs(single - batched[r]).max() <= 0.0625, r
+        assert rel_l2(single, batched[r]) <= 2e-2, r
+    s.close()

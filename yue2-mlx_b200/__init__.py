@@ -76,6 +76,8 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_generate": (I, [P, i32p, I, ctypes.POINTER(_Sampling), U64, I, i32p, I, D, I, CANCEL_FN, P,
                              TOKEN_FN, P, i32p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.c_char_p,
                              ctypes.c_size_t]),
+        "yar_generate_batch": (I, [P, I, i32p, i32p, ctypes.POINTER(_Sampling), ctypes.POINTER(ctypes.c_uint64), I, I,
+                                   i32p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.c_char_p, ctypes.c_size_t]),
         "yar_row_reset": (I, [P, I, I]),
         "yar_row_prefill": (I, [P, I, i32p, I, I, I]),
         "yar_rows_step": (I, [P, ctypes.POINTER(I), i32p, I, I]),
@@ -204,6 +206,10 @@ class Session:
         """Decode forward as one persistent kernel (default) or one kernel per operation."""
         _check(lib.yar_session_set_option(self._h, 1, int(bool(on))))
 
+    def generate_batch(self, prefixes, sampling: Sampling, seeds, phase="semantic", legacy_off: bool = False):
+        """Independent requests decoded together on rows 0..n-1: (token lists, timing, truncated)."""
+        return _generate_batch(self, prefixes, sampling, seeds, phase, legacy_off)
+
     def set_prefetch_stages(self, n: int):
         """L2 prefetch distance of the persistent decode kernel, in 32 KB stages per SM."""
         _check(lib.yar_session_set_option(self._h, 3, int(n)))
@@ -278,6 +284,23 @@ class Session:
                                 cancel_cb, None, token_cb, None, _ptr(out, ctypes.c_int32), ctypes.byref(n_out),
                                 ctypes.byref(trunc), timing, len(timing)))
         return out[:n_out.value].tolist(), json.loads(timing.value.decode()), bool(trunc.value)
+
+
+def _generate_batch(session, prefixes, sampling: Sampling, seeds, phase="semantic", legacy_off: bool = False):
+    n = len(prefixes)
+    lens = np.array([len(p) for p in prefixes], np.int32)
+    flat = _i32(np.concatenate([np.asarray(p, np.int32) for p in prefixes]))
+    sd = np.ascontiguousarray(np.asarray(seeds, np.uint64))
+    out = np.zeros(n * max(1, sampling.max_tokens), np.int32)
+    n_out, trunc = np.zeros(n, np.int32), np.zeros(n, np.int32)
+    timing = ctypes.create_string_buffer(4096)
+    _check(lib.yar_generate_batch(session._h, n, _ptr(flat, ctypes.c_int32), _ptr(lens, ctypes.c_int32),
+                                  ctypes.byref(sampling._c()), _ptr(sd, ctypes.c_uint64), PHASES[phase],
+                                  int(legacy_off), _ptr(out, ctypes.c_int32), _ptr(n_out, ctypes.c_int),
+                                  _ptr(trunc, ctypes.c_int), timing, len(timing)))
+    m = max(1, sampling.max_tokens)
+    tokens = [out[r * m:r * m + n_out[r]].tolist() for r in range(n)]
+    return tokens, json.loads(timing.value.decode()), [bool(t) for t in trunc]
 
 
 def generate_tokens(model: ARModel, prefix, sampling: Sampling, seed: int, phase: str = "semantic", negative=None,

@@ -23,6 +23,9 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
 void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
                  const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
                  uint64_t seed, int legacy_off, int32_t *token, float *scores);
+std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const int32_t *prefix_lens,
+                           const ::yar_sampling &smp, const uint64_t *seeds, int phase, int legacy_off,
+                           int32_t *out_tokens, int *n_out, int *truncated);
 void sample_device_noalloc(Model &m, const uint16_t *logits, long long row_stride, int rows, int n,
                            double cfg_scale, const ::yar_sampling &smp, const int32_t *history, int n_history,
                            int step, int phase, uint64_t seed, int32_t *token, float *scores,
@@ -184,6 +187,22 @@ int yar_generate(yar_session *session, const int32_t *prefix, int n_prefix, cons
     const std::string timing = yar::generate(*session->s, prefix, n_prefix, *sampling, seed, phase, negative,
                                              n_negative, cfg_scale, legacy_off, cancel, cancel_ctx, on_token,
                                              token_ctx, out_tokens, n_out, truncated);
+    if (timing_json && timing_cap > 0) {
+      const size_t n = timing.size() < timing_cap - 1 ? timing.size() : timing_cap - 1;
+      std::memcpy(timing_json, timing.data(), n);
+      timing_json[n] = '\0';
+    }
+  });
+}
+
+int yar_generate_batch(yar_session *session, int n_requests, const int32_t *prefixes, const int32_t *prefix_lens,
+                       const yar_sampling *sampling, const uint64_t *seeds, int phase, int legacy_off,
+                       int32_t *out_tokens, int *n_out, int *truncated, char *timing_json, size_t timing_cap) {
+  return guarded([&] {
+    need(session && prefixes && prefix_lens && sampling && seeds && out_tokens && n_out && truncated,
+         "missing argument");
+    const std::string timing = yar::generate_batch(*session->s, n_requests, prefixes, prefix_lens, *sampling, seeds,
+                                                   phase, legacy_off, out_tokens, n_out, truncated);
     if (timing_json && timing_cap > 0) {
       const size_t n = timing.size() < timing_cap - 1 ? timing.size() : timing_cap - 1;
       std::memcpy(timing_json, timing.data(), n);

@@ -232,12 +232,53 @@ static void reset_step_sync(Session &s) {
   YAR_CUDA(cudaMemsetAsync(s.attn_count, 0, size_t(s.max_rows) * s.m->d.kv_heads * sizeof(int), s.stream));
 }
 
+// Batches of at least this many rows run the decode linears as tcgen05 GEMMs: the weights
+// are read once per step for all rows instead of once per 8 rows.
+constexpr int kBatchedRows = 16;
+
+// One decode forward of many rows: RMSNorm rows -> tcgen05 GEMM (QKV, O + residual,
+// gate/up + SwiGLU, down + residual), the split-KV decode attention per row, and the
+// phase head as a GEMM over the normalized rows.
+static void decode_forward_batched(Session &s, int n_rows, int phase) {
+  const Model &m = *s.m;
+  const Dims &d = m.d;
+  cudaStream_t st = s.stream;
+  const int H = d.hidden;
+  auto gemm = [&](const bf16 *A, int K, const bf16 *W, int N, bf16 *C, int ldc, int epi) {
+    if (gemm_tc_supported(A, n_rows, K, W, N, C, ldc))
+      launch_gemm_tc(A, n_rows, K, W, N, C, ldc, epi, s.d_error, st);
+    else
+      launch_gemm(A, n_rows, K, W, N, C, ldc, epi, st);
+  };
+  launch_embed_rows(m, s, n_rows, st);
+  for (int l = 0; l < d.layers; ++l) {
+    const LayerWeights &w = m.layers[l];
+    launch_rmsnorm_rows(s.x, w.ln1, n_rows, H, d.eps, s.ph, st);
+    gemm(s.ph, H, w.qkv, d.qkv_rows(), s.qkv, d.qkv_rows(), kEpiStore);
+    launch_attn_decode(m, s, l, n_rows, st);
+    gemm(s.attn, d.qdim(), w.o, H, s.x, H, kEpiResidual);
+    launch_rmsnorm_rows(s.x, w.ln2, n_rows, H, d.eps, s.ph, st);
+    gemm(s.ph, H, w.gu, 2 * d.ffn, s.mlp, d.ffn, kEpiSwiGLU);
+    gemm(s.mlp, d.ffn, w.down, H, s.x, H, kEpiResidual);
+  }
+  launch_rmsnorm_rows(s.x, m.final_norm, n_rows, H, d.eps, s.ph, st);
+  const PhaseRows pr = phase_rows(d, phase);
+  launch_gemm(s.ph, n_rows, H, m.lm_head + size_t(pr.row0) * H, pr.n_main, s.logits, s.logit_stride, kEpiStore, st);
+  if (pr.extra >= 0)
+    launch_gemv(m.lm_head + size_t(pr.extra) * H, 1, H, s.ph, H, nullptr, d.eps, s.logits + pr.n_main,
+                s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, st);
+}
+
 static void decode_forward(Session &s, int n_rows, int phase) {
   const Model &m = *s.m;
   const Dims &d = m.d;
   cudaStream_t st = s.stream;
   if (use_persistent(s, n_rows)) {
     launch_decode_persistent(m, s, n_rows, phase, st);
+    return;
+  }
+  if (n_rows >= kBatchedRows && n_rows <= s.prefill_chunk) {
+    decode_forward_batched(s, n_rows, phase);
     return;
   }
   launch_embed_rows(m, s, n_rows, st);
@@ -539,6 +580,109 @@ void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, 
     throw;
   }
   cudaFree(logits), cudaFree(sc), cudaFree(req), cudaFree(tok), cudaFree(act), cudaFree(picked);
+}
+
+
+// Many independent requests decoded in lockstep on rows 0..n-1 (no CFG): each is prefilled
+// on its own row, then every step samples all unfinished requests (one sampler CTA each,
+// own seed) and forwards all rows at once (rows >= 16 use the batched tcgen05 forward).
+// A request stops at its end token or after max_tokens; finished rows are skipped by the
+// sampler, embedding and attention.
+std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const int32_t *prefix_lens,
+                           const ::yar_sampling &smp, const uint64_t *seeds, int phase, int legacy_off,
+                           int32_t *out_tokens, int *n_out, int *truncated) {
+  const Model &m = *s.m;
+  phase_rows(m.d, phase);
+  validate_sampling(smp);
+  if (n_req < 1 || n_req > s.max_rows) throw Error("ValueError", "request count must be in [1, session rows]");
+  if (smp.max_tokens > s.out_cap) throw Error("ValueError", "max_tokens exceeds the session output capacity");
+  size_t off = 0;
+  std::vector<size_t> starts(n_req);
+  for (int r = 0; r < n_req; ++r) {
+    const int n = prefix_lens[r];
+    if (n < 1) throw Error("ValueError", "AR prefix must contain at least one token");
+    if (size_t(n) + size_t(smp.max_tokens) > size_t(m.d.context))
+      throw Error("ValueError", "Prefix + requested generation budget exceeds 24576; no implicit truncation");
+    if (n + smp.max_tokens > s.max_ctx)
+      throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
+    if (seeds[r] >= (uint64_t(1) << 63)) throw Error("ValueError", "seed must be an integer in [0, 2**63)");
+    starts[r] = off;
+    off += size_t(n);
+  }
+  YAR_CUDA(cudaSetDevice(m.device));
+  YAR_CUDA(cudaStreamSynchronize(s.stream));
+  const double t0 = now_s();
+  for (int r = 0; r < n_req; ++r) {
+    row_reset(s, r, prefix_lens[r] + smp.max_tokens);
+    row_prefill(s, r, prefixes + starts[r], prefix_lens[r], phase, 0, nullptr, nullptr);
+  }
+  const double prefill_seconds = now_s() - t0;
+  std::vector<RequestState> reqs(n_req);
+  for (int r = 0; r < n_req; ++r) reqs[r] = make_request(m, s, r, -1, phase, smp, 1.0, seeds[r], 0, legacy_off != 0);
+  cudaStream_t st = s.stream;
+  YAR_CUDA(cudaMemcpyAsync(s.d_req, reqs.data(), n_req * sizeof(RequestState), cudaMemcpyHostToDevice, st));
+  std::vector<int> act(n_req, 1);
+  YAR_CUDA(cudaMemcpyAsync(s.d_active, act.data(), n_req * sizeof(int), cudaMemcpyHostToDevice, st));
+  YAR_CUDA(cudaMemsetAsync(s.d_error, 0, sizeof(int), st));
+  reset_step_sync(s);
+  YAR_CUDA(cudaStreamSynchronize(st));
+  cudaGraphExec_t exec = step_graph(s, n_req, n_req, phase);
+
+  const int kChunk = 16;
+  int steps = 0;
+  float decode_ms = 0.f;
+  cudaEvent_t ev0, ev1;
+  YAR_CUDA(cudaEventCreate(&ev0));
+  YAR_CUDA(cudaEventCreate(&ev1));
+  std::vector<int> prog(size_t(n_req) * 4);  // (step, done, n_out, error) per request
+  bool all_done = false;
+  while (steps < smp.max_tokens && !all_done) {
+    const int k = std::min(kChunk, smp.max_tokens - steps);
+    YAR_CUDA(cudaEventRecord(ev0, st));
+    for (int i = 0; i < k; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
+    YAR_CUDA(cudaEventRecord(ev1, st));
+    steps += k;
+    YAR_CUDA(cudaMemcpy2DAsync(prog.data(), 4 * sizeof(int), &s.d_req[0].step, sizeof(RequestState), 4 * sizeof(int),
+                               n_req, cudaMemcpyDeviceToHost, st));
+    int derr = 0;
+    YAR_CUDA(cudaMemcpyAsync(&derr, s.d_error, sizeof(int), cudaMemcpyDeviceToHost, st));
+    YAR_CUDA(cudaStreamSynchronize(st));
+    float ms = 0.f;
+    YAR_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+    decode_ms += ms;
+    all_done = true;
+    for (int r = 0; r < n_req; ++r) {
+      if (prog[4 * r + 3] || derr)
+        throw Error("RuntimeError", "device sampler/forward error " + std::to_string(prog[4 * r + 3]) + "/" +
+                                        std::to_string(derr));
+      if (!prog[4 * r + 1] && prog[4 * r] < smp.max_tokens) all_done = false;
+    }
+  }
+  YAR_CUDA(cudaEventDestroy(ev0));
+  YAR_CUDA(cudaEventDestroy(ev1));
+  long long total = 0;
+  for (int r = 0; r < n_req; ++r) {
+    const int dn = prog[4 * r + 2];
+    YAR_CUDA(cudaMemcpy(out_tokens + size_t(r) * smp.max_tokens, s.d_out_tokens + size_t(r) * s.out_cap,
+                        size_t(dn) * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    n_out[r] = dn;
+    truncated[r] = prog[4 * r] > dn ? 0 : 1;  // a sampled end token is counted in step, not stored
+    total += dn;
+    for (int p : s.row_pages[r]) s.free_pages.push_back(p);
+    s.row_pages[r].clear();
+    s.capacity[r] = 0;
+  }
+  const double seconds = now_s() - t0;
+  nlohmann::json timing = {{"seconds", seconds},
+                           {"prefill_seconds", prefill_seconds},
+                           {"requests", n_req},
+                           {"content_tokens", total},
+                           {"decode_steps", steps},
+                           {"decode_device_ms", decode_ms},
+                           {"execution", "cuda_graph"},
+                           {"forward", n_req >= kBatchedRows ? "batched_tcgen05" : "per_row"},
+                           {"backend", "cuda-sm100a"}};
+  return timing.dump();
 }
 
 }  // namespace yar
