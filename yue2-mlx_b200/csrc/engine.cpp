@@ -92,6 +92,8 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     s->d_out_tokens = dmalloc<int32_t>(size_t(max_rows) * s->out_cap);
     s->d_scores = dmalloc<float>(size_t(max_rows) * s->logit_stride);
     YAR_CUDA(cudaMallocHost(&s->h_pinned, 1 << 20));
+    s->gemm_ws_floats = size_t(4) << 20;
+    s->gemm_ws = dmalloc<float>(s->gemm_ws_floats);
     s->n_ctr = 2 + 5 * d.layers;
     s->d_ctr = dmalloc<int>(s->n_ctr);
     s->d_epoch = dmalloc<int>(1);
@@ -114,7 +116,8 @@ void free_session(Session *s) {
                                                s->d_token, s->d_active, s->d_error, s->x, s->qkv, s->attn,
                                                s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
                                                s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
-                                               s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch, s->d_trace})
+                                               s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch, s->d_trace,
+                                               s->gemm_ws})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -182,7 +185,7 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
   // otherwise the mma.sync GEMM.
   auto gemm = [&](const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epi) {
     if (gemm_tc_supported(A, M, K, W, N, C, ldc))
-      launch_gemm_tc(A, M, K, W, N, C, ldc, epi, s.d_error, st);
+      launch_gemm_tc(A, M, K, W, N, C, ldc, epi, s.d_error, s.gemm_ws, s.gemm_ws_floats, st);
     else
       launch_gemm(A, M, K, W, N, C, ldc, epi, st);
   };
@@ -246,24 +249,34 @@ static void decode_forward_batched(Session &s, int n_rows, int phase) {
   const int H = d.hidden;
   auto gemm = [&](const bf16 *A, int K, const bf16 *W, int N, bf16 *C, int ldc, int epi) {
     if (gemm_tc_supported(A, n_rows, K, W, N, C, ldc))
-      launch_gemm_tc(A, n_rows, K, W, N, C, ldc, epi, s.d_error, st);
+      launch_gemm_tc(A, n_rows, K, W, N, C, ldc, epi, s.d_error, s.gemm_ws, s.gemm_ws_floats, st);
     else
       launch_gemm(A, n_rows, K, W, N, C, ldc, epi, st);
   };
+  // About two waves of attention CTAs (5 resident per SM): fewer, longer splits per row
+  // than the one-row path, so each CTA streams several chunks.
+  const int splits = std::max(1, (2 * 5 * m.sm_count + n_rows * d.kv_heads - 1) / (n_rows * d.kv_heads));
   launch_embed_rows(m, s, n_rows, st);
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
     launch_rmsnorm_rows(s.x, w.ln1, n_rows, H, d.eps, s.ph, st);
     gemm(s.ph, H, w.qkv, d.qkv_rows(), s.qkv, d.qkv_rows(), kEpiStore);
-    launch_attn_decode(m, s, l, n_rows, st);
+    launch_attn_decode(m, s, l, n_rows, st, splits);
     gemm(s.attn, d.qdim(), w.o, H, s.x, H, kEpiResidual);
     launch_rmsnorm_rows(s.x, w.ln2, n_rows, H, d.eps, s.ph, st);
     gemm(s.ph, H, w.gu, 2 * d.ffn, s.mlp, d.ffn, kEpiSwiGLU);
     gemm(s.mlp, d.ffn, w.down, H, s.x, H, kEpiResidual);
   }
   launch_rmsnorm_rows(s.x, m.final_norm, n_rows, H, d.eps, s.ph, st);
+  // Head: an even number of rows as a GEMM; an odd last phase row and the ABC extra row as
+  // GEMVs over the normalized rows.
   const PhaseRows pr = phase_rows(d, phase);
-  launch_gemm(s.ph, n_rows, H, m.lm_head + size_t(pr.row0) * H, pr.n_main, s.logits, s.logit_stride, kEpiStore, st);
+  const int n_even = pr.n_main & ~1;
+  const bf16 *head = m.lm_head + size_t(pr.row0) * H;
+  launch_gemm(s.ph, n_rows, H, head, n_even, s.logits, s.logit_stride, kEpiStore, st);
+  if (n_even < pr.n_main)
+    launch_gemv(head + size_t(n_even) * H, 1, H, s.ph, H, nullptr, d.eps, s.logits + n_even, s.logit_stride,
+                kEpiStore, n_rows, s.d_error, m.sm_count, st);
   if (pr.extra >= 0)
     launch_gemv(m.lm_head + size_t(pr.extra) * H, 1, H, s.ph, H, nullptr, d.eps, s.logits + pr.n_main,
                 s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, st);

@@ -90,7 +90,9 @@ void launch_embed_rows(const Model &m, Session &s, int n_rows, cudaStream_t st);
 void launch_gemv(const bf16 *W, int N, int K, const bf16 *in, int in_stride, const bf16 *norm_w,
                  float eps, bf16 *out, int out_stride, int epilogue, int n_rows,
                  int *error, int sm_count, cudaStream_t st);
-void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st);
+// `max_splits` (0: the session's) caps the splits per (row, kv head); fewer, longer splits
+// suit large batches.
+void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st, int max_splits = 0);
 void launch_sampler(const Model &m, Session &s, int n_requests, cudaStream_t st);
 // Prefill (T tokens of one row).
 void launch_embed_tokens(const bf16 *embed, const int *ids, int T, int H, bf16 *x, cudaStream_t st);
@@ -100,8 +102,9 @@ void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int
                  cudaStream_t st);
 // Prefill linears on tcgen05 (kernels_gemm_tc.cu); `error` receives expired-wait flags.
 bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const bf16 *C, int ldc);
+// `ws` (ws_floats FP32 values, may be null) lets small-M shapes split K across CTAs.
 void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
-                    cudaStream_t st);
+                    float *ws, size_t ws_floats, cudaStream_t st);
 void configure_gemm_tc_kernels();
 void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
                              cudaStream_t st);
@@ -172,6 +175,8 @@ struct Session {
   int *d_ctr = nullptr;
   int *d_epoch = nullptr;
   int n_ctr = 0;
+  float *gemm_ws = nullptr;  // split-K partials of the tcgen05 GEMM
+  size_t gemm_ws_floats = 0;
   int prefetch_stages = 6;  // persistent kernel: L2 prefetch distance beyond the ring
   unsigned long long *d_trace = nullptr;  // persistent-kernel timeline (when enabled)
   size_t trace_elems = 0;

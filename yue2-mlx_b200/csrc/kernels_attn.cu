@@ -55,24 +55,33 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p
   const int c1 = min((split + 1) * sp.cps, sp.nchunks);
   for (int c = split * sp.cps; c < c1; ++c) {
     const int base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
+    // Every 16-byte piece of the chunk's cached K and V rows in flight at once (cp.async,
+    // any page size), one wait.
     for (int idx = tid; idx < n_main * (D / 8); idx += kAttnThreads) {
       const int r = idx / (D / 8), cc = idx % (D / 8);
-      const uint4 kq = ldg16(kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, base + r) + cc * 8);
-      const uint4 vq = ldg16(kv_row_ptr<D>(p, rs, row, p.layer, 1, kvh, base + r) + cc * 8);
-      *reinterpret_cast<uint4 *>(kbuf + r * D + cc * 8) = kq;
-      *reinterpret_cast<uint4 *>(vbuf + r * D + cc * 8) = vq;
+      const bf16 *ks = kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, base + r) + cc * 8;
+      const bf16 *vs = kv_row_ptr<D>(p, rs, row, p.layer, 1, kvh, base + r) + cc * 8;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                       __cvta_generic_to_shared(kbuf + r * D + cc * 8))),
+                   "l"(ks)
+                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                       __cvta_generic_to_shared(vbuf + r * D + cc * 8))),
+                   "l"(vs)
+                   : "memory");
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     team_sync(1);
     attn_chunk<D, G>(sm, kbuf, vbuf, n_main, pos - base < kKvChunk, p.g.scale, acc, tid, 1);
   }
   attn_finish<D, G>(p, sm, acc, row, kvh, split, sp.n_splits, tid, 1);
 }
 
-void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st) {
+void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaStream_t st, int max_splits) {
   DecodeAttnParams p;
   p.g = geom(m, s);
   p.layer = layer;
-  p.max_splits = s.max_splits;
+  p.max_splits = max_splits > 0 && max_splits < s.max_splits ? max_splits : s.max_splits;
   p.pool = s.kv;
   p.page_table = s.d_page_table;
   p.cur_pos = s.d_cur_pos;
@@ -86,7 +95,7 @@ void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaS
   p.count = s.attn_count;
   p.out = s.attn;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(m.d.kv_heads, s.max_splits, n_rows);
+  cfg.gridDim = dim3(m.d.kv_heads, p.max_splits, n_rows);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -34,6 +34,8 @@ struct TcParams {
   bf16 *C;
   int M, N, K, ldc;
   int *error;
+  float *ws;   // split-K: FP32 partials [splits][M][N] instead of the epilogue (null: none)
+  int kb_per;  // 64-wide K slices per CTA (blockIdx.z picks the CTA's range)
 };
 
 __device__ __forceinline__ uint32_t tc_smem(const void *p) {
@@ -70,7 +72,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int s_fail;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTcBN, m0 = blockIdx.y * kTcBM, KB = p.K / kTcBK;
+  const int n0 = blockIdx.x * kTcBN, m0 = blockIdx.y * kTcBM, KB = p.kb_per, kb0 = blockIdx.z * p.kb_per;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
@@ -107,12 +109,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       asm volatile(
           "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
           "[%2];" ::"r"(tc_smem(sa + s * kTcTileA)),
-          "l"(&tma_a), "r"(tc_smem(&full[s])), "r"(kb * kTcBK), "r"(m0)
+          "l"(&tma_a), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(m0)
           : "memory");
       asm volatile(
           "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
           "[%2];" ::"r"(tc_smem(sb + s * kTcTileB)),
-          "l"(&tma_b), "r"(tc_smem(&full[s])), "r"(kb * kTcBK), "r"(n0)
+          "l"(&tma_b), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(n0)
           : "memory");
       issued = kb + 1;
     }
@@ -173,6 +175,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       if (row >= p.M) continue;
       const int col = n0 + c;
+      if (p.ws) {  // split-K partial: FP32 values, the epilogue runs after the reduction
+        uint4 *dst = reinterpret_cast<uint4 *>(p.ws + (size_t(blockIdx.z) * p.M + row) * p.N + col);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        continue;
+      }
       if (EPI == kEpiSwiGLU) {
         uint32_t o[8];
 #pragma unroll
@@ -213,6 +221,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcBN));
+}
+
+// Split-K: out = epilogue(sum over splits of the FP32 partials, in split order). One thread
+// per 8 consecutive columns of a row.
+template <int EPI>
+__global__ void __launch_bounds__(256) k_splitk_reduce(const float *ws, int splits, int M, int N, bf16 *C, int ldc) {
+  const long long idx = blockIdx.x * 256ll + threadIdx.x, groups = N / 8;
+  if (idx >= (long long)M * groups) return;
+  const int row = int(idx / groups), col = int(idx % groups) * 8;
+  float v[8];
+  for (int s = 0; s < splits; ++s) {
+    const float4 *src = reinterpret_cast<const float4 *>(ws + (size_t(s) * M + row) * N + col);
+    const float4 a = src[0], b = src[1];
+    const float w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = s == 0 ? w[j] : v[j] + w[j];
+  }
+  if (EPI == kEpiSwiGLU) {
+    uint32_t o[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float r2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float gate = rbf(v[4 * j + 2 * h]), up = rbf(v[4 * j + 2 * h + 1]);
+        r2[h] = rbf(silu_f32(gate)) * up;
+      }
+      o[j] = (__float_as_uint(rbf(r2[0])) >> 16) | (__float_as_uint(rbf(r2[1])) & 0xFFFF0000u);
+    }
+    *reinterpret_cast<uint2 *>(C + size_t(row) * ldc + (col >> 1)) = make_uint2(o[0], o[1]);
+  } else {
+    uint4 *dst = reinterpret_cast<uint4 *>(C + size_t(row) * ldc + col);
+    uint4 old = make_uint4(0, 0, 0, 0);
+    if (EPI == kEpiResidual) old = *dst;
+    const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float lo = v[2 * j], hi = v[2 * j + 1];
+      if (EPI == kEpiResidual) {
+        lo = bf_lo(ow[j]) + rbf(lo);
+        hi = bf_hi(ow[j]) + rbf(hi);
+      }
+      o[j] = (__float_as_uint(rbf(lo)) >> 16) | (__float_as_uint(rbf(hi)) & 0xFFFF0000u);
+    }
+    *dst = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // ------------------------------------------------------------------------------- host
@@ -260,10 +315,16 @@ bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const 
 }
 
 void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
-                    cudaStream_t st) {
+                    float *ws, size_t ws_floats, cudaStream_t st) {
   const CUtensorMap ma = kmajor_map(A, M, K, kTcBM), mb = kmajor_map(W, N, K, kTcBN);
-  TcParams p{C, M, N, K, ldc, error};
-  const dim3 grid(N / kTcBN, (M + kTcBM - 1) / kTcBM);
+  // Split K across CTAs while the tile grid leaves SMs idle (small M: batched decode).
+  const int tiles = (N / kTcBN) * ((M + kTcBM - 1) / kTcBM), KB = K / kTcBK;
+  int splits = 1;
+  while (ws && splits < 8 && tiles * splits < 120 && KB % (splits * 2) == 0 &&
+         size_t(splits * 2) * M * N <= ws_floats)
+    splits *= 2;
+  TcParams p{C, M, N, K, ldc, error, splits > 1 ? ws : nullptr, KB / splits};
+  const dim3 grid(N / kTcBN, (M + kTcBM - 1) / kTcBM, splits);
   if (epilogue == kEpiSwiGLU)
     k_gemm_tc<kEpiSwiGLU><<<grid, kTcThreads, kTcSmem, st>>>(ma, mb, p);
   else if (epilogue == kEpiResidual)
@@ -271,6 +332,17 @@ void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, 
   else
     k_gemm_tc<kEpiStore><<<grid, kTcThreads, kTcSmem, st>>>(ma, mb, p);
   YAR_CUDA(cudaGetLastError());
+  if (splits > 1) {
+    const long long threads = (long long)M * (N / 8);
+    const unsigned blocks = unsigned((threads + 255) / 256);
+    if (epilogue == kEpiSwiGLU)
+      k_splitk_reduce<kEpiSwiGLU><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
+    else if (epilogue == kEpiResidual)
+      k_splitk_reduce<kEpiResidual><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
+    else
+      k_splitk_reduce<kEpiStore><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
+    YAR_CUDA(cudaGetLastError());
+  }
 }
 
 }  // namespace yar
