@@ -1,0 +1,213 @@
+"""Tensor parallelism: the split plan on CPU (gloo ranks) and the NCCL path on 2 GPUs.
+
+CPU tests (no GPU; they call the library's host-only split functions):
+* the plan covers every q/k/v row, O column, gate/up row and down column exactly once
+  across ranks, and a rank's query heads are exactly those of its KV heads (GQA groups
+  stay whole);
+* the head slices cover every phase column exactly once;
+* on two gloo ranks, a decoder layer computed from each rank's share of the weights
+  (rank-partial O and down sums, all-reduced) and the LM head computed by slices
+  (all-gathered) equal the whole model's layer and head in FP64.
+
+GPU test (two GPUs, torchrun): the tensor-parallel model against the one-GPU model on the
+same weights — logits within the BF16 radius (the FP32 partial sums are added in another
+order, so last-bit flips of BF16 values propagate), tokens identical on every rank.
+"""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from tests.conftest import ROOT, load_package
+
+
+@pytest.fixture(scope="module")
+def yar():
+    return load_package()
+
+
+@pytest.mark.parametrize("dims", [(16, 8, 128, 6144), (4, 2, 64, 688)])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_plan_covers_every_row_once(yar, dims, world):
+    heads, kv, hd, ffn = dims
+    if kv % world or (ffn // world) % 8 or ffn % world:
+        with pytest.raises(yar.YarError):
+            yar.tp_plan(heads, kv, hd, ffn, 0, world)
+        return
+    q_seen, kv_seen, f_seen = np.zeros(heads * hd, int), np.zeros(kv * hd, int), np.zeros(ffn, int)
+    group = heads // kv
+    for r in range(world):
+        p = yar.tp_plan(heads, kv, hd, ffn, r, world)
+        q_seen[p["q_row0"]:p["q_row0"] + p["q_rows"]] += 1
+        kv_seen[p["kv_row0"]:p["kv_row0"] + p["kv_rows"]] += 1
+        f_seen[p["ffn_row0"]:p["ffn_row0"] + p["ffn_rows"]] += 1
+        q_heads = set(range(p["q_row0"] // hd, (p["q_row0"] + p["q_rows"]) // hd))
+        kv_heads = set(range(p["kv_row0"] // hd, (p["kv_row0"] + p["kv_rows"]) // hd))
+        assert {h // group for h in q_heads} == kv_heads
+        assert p["q_rows"] % hd == 0 and p["kv_rows"] % hd == 0
+    assert (q_seen == 1).all() and (kv_seen == 1).all() and (f_seen == 1).all()
+
+
+@pytest.mark.parametrize("width", [32769, 151644, 4096, 5, 8])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_head_slices_cover_every_column_once(yar, width, world):
+    seen = np.zeros(width, int)
+    for r in range(world):
+        b, e = yar.tp_head_slice(width, r, world)
+        assert 0 <= b <= e <= width
+        seen[b:e] += 1
+    assert (seen == 1).all()
+
+
+def test_plan_rejects_bad_ranks(yar):
+    for rank, world in ((2, 2), (-1, 2), (0, 0)):
+        with pytest.raises(yar.YarError):
+            yar.tp_plan(16, 8, 128, 6144, rank, world)
+
+
+# --- gloo decomposition (two CPU ranks) -------------------------------------------------
+
+def _rms(x, w, eps=1e-6):
+    return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps) * w
+
+
+def _rope(x, pos, theta=1e6):
+    d = x.shape[-1]
+    inv = 1.0 / theta ** (np.arange(0, d, 2) / d)
+    ang = pos[:, None] * inv[None, :]
+    c, s = np.cos(ang), np.sin(ang)
+    x1, x2 = x[..., : d // 2], x[..., d // 2:]
+    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
+
+
+def _layer_parts(x, w, hd, group, q_sl, kv_sl, f_sl):
+    """One decoder layer's two rank-partial sums (before the all-reduce) over the heads
+    and FFN columns in the slices; FP64, causal attention over the T rows of x."""
+    T = x.shape[0]
+    h = _rms(x, w["ln1"])
+    q = (h @ w["q"][q_sl].T).reshape(T, -1, hd)
+    k = (h @ w["k"][kv_sl].T).reshape(T, -1, hd)
+    v = (h @ w["v"][kv_sl].T).reshape(T, -1, hd)
+    pos = np.arange(T, dtype=np.float64)
+    q = np.stack([_rope(_rms(q[:, i], w["qn"]), pos) for i in range(q.shape[1])], 1)
+    k = np.stack([_rope(_rms(k[:, i], w["kn"]), pos) for i in range(k.shape[1])], 1)
+    mask = np.triu(np.full((T, T), -np.inf), 1)
+    outs = []
+    for i in range(q.shape[1]):
+        sc = q[:, i] @ k[:, i // group].T / np.sqrt(hd) + mask
+        p = np.exp(sc - sc.max(-1, keepdims=True))
+        outs.append((p / p.sum(-1, keepdims=True)) @ v[:, i // group])
+    attn = np.concatenate(outs, -1)
+    o_part = attn @ w["o"][:, q_sl].T
+    return o_part, h
+
+
+def _mlp_part(x, w, f_sl):
+    h = _rms(x, w["ln2"])
+    g, u = h @ w["gate"][f_sl].T, h @ w["up"][f_sl].T
+    return (g / (1 + np.exp(-g)) * u) @ w["down"][:, f_sl].T
+
+
+def _weights(heads, kv, hd, ffn, H, V, seed=0):
+    rng = np.random.default_rng(seed)
+    n = lambda *s: rng.normal(0, 0.05, s)  # noqa: E731
+    return {"ln1": 1 + n(H), "ln2": 1 + n(H), "qn": 1 + n(hd), "kn": 1 + n(hd), "q": n(heads * hd, H),
+            "k": n(kv * hd, H), "v": n(kv * hd, H), "o": n(H, heads * hd), "gate": n(ffn, H), "up": n(ffn, H),
+            "down": n(H, ffn), "head": n(V, H), "norm": 1 + n(H)}
+
+
+def _gloo_rank(rank, world, port, out_dir):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    sys.path.insert(0, ROOT)
+    from tests.conftest import load_package as lp
+    yar = lp()
+    heads, kv, hd, ffn, H, V, T = 4, 2, 64, 688, 256, 301, 7
+    w = _weights(heads, kv, hd, ffn, H, V)
+    x = np.random.default_rng(1).normal(0, 1, (T, H))
+    p = yar.tp_plan(heads, kv, hd, ffn, rank, world)
+    q_sl = slice(p["q_row0"], p["q_row0"] + p["q_rows"])
+    kv_sl = slice(p["kv_row0"], p["kv_row0"] + p["kv_rows"])
+    f_sl = slice(p["ffn_row0"], p["ffn_row0"] + p["ffn_rows"])
+    o_part, _ = _layer_parts(x, w, hd, heads // kv, q_sl, kv_sl, f_sl)
+    t = torch.from_numpy(o_part.copy())
+    dist.all_reduce(t)
+    x1 = x + t.numpy()
+    t = torch.from_numpy(_mlp_part(x1, w, f_sl).copy())
+    dist.all_reduce(t)
+    x2 = x1 + t.numpy()
+    hn = _rms(x2, w["norm"])
+    b, e = yar.tp_head_slice(V, rank, world)
+    mine = np.zeros((T, max(e - b, 0)))
+    if e > b:
+        mine = hn @ w["head"][b:e].T
+    parts = [None] * world
+    dist.all_gather_object(parts, (b, e, mine))
+    if rank == 0:
+        logits = np.zeros((T, V))
+        for b2, e2, m in parts:
+            logits[:, b2:e2] = m
+        full = slice(None)
+        o_full, _ = _layer_parts(x, w, hd, heads // kv, full, full, full)
+        y1 = x + o_full
+        y2 = y1 + _mlp_part(y1, w, full)
+        ref = _rms(y2, w["norm"]) @ w["head"].T
+        np.save(os.path.join(out_dir, "err.npy"), np.array([np.abs(x2 - y2).max(), np.abs(logits - ref).max()]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_two_gloo_ranks_reassemble_the_whole_layer(tmp_path):
+    import torch.multiprocessing as mp
+    mp.start_processes(_gloo_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    err = np.load(tmp_path / "err.npy")
+    assert err[0] < 1e-10 and err[1] < 1e-10, err
+
+
+# --- two GPUs ---------------------------------------------------------------------------
+
+@pytest.mark.gpu
+def test_tensor_parallel_two_gpus_match_one_gpu(synth, tmp_path):
+    """Run on a box with at least two GPUs (skipped on one): TP=2 against TP=1."""
+    import dataclasses
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    small = str(tmp_path / "wide2")
+    synth.write_converted(small, dataclasses.replace(synth.PINNED, layers=2, vocab=4096, context=4096), seed=3,
+                          norm_std=0.1)
+    big = str(tmp_path / "vocab")
+    synth.write_converted(big, dataclasses.replace(synth.PINNED, layers=2, context=4096), seed=4, norm_std=0.1)
+    out = str(tmp_path / "tp.json")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "tp_worker.py"), small, big, out]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    if r.returncode != 0:
+        print(r.stdout[-20000:])
+        print(r.stderr[-20000:])
+    assert r.returncode == 0, "the tensor-parallel ranks failed (their output is printed above)"
+    res = json.load(open(out))
+    assert res["dims_tp"]["heads"] == 8 and res["dims_tp"]["kv_heads"] == 4 and res["dims_tp"]["ffn"] == 3072
+    for key in ("full_rows1", "full_rows2", "semantic", "abc"):
+        assert res[key]["same_on_all_ranks"], key
+        assert res[key]["max_abs"] <= 0.0625 and res[key]["rel_l2"] <= 2e-2, (key, res[key])
+    assert res["semantic"]["width"] == 32769 and res["abc"]["width"] == 151644
+    assert res["generate"]["ranks_agree"] and res["generate"]["tensor_parallel"] == 2
+    assert len(res["generate"]["tokens"]) == 24
+    assert res["batch"]["ranks_agree"] and res["batch"]["forward"] == "batched_tcgen05"
+    assert res["batch"]["max_abs"] <= 0.0625 and res["batch"]["rel_l2"] <= 2e-2, res["batch"]

@@ -67,6 +67,10 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_version": (ctypes.c_char_p, []),
         "yar_model_load": (I, [ctypes.c_char_p, I, ctypes.POINTER(P)]),
         "yar_model_load_ex": (I, [ctypes.c_char_p, I, ctypes.c_uint32, ctypes.POINTER(P)]),
+        "yar_tp_unique_id": (I, [ctypes.c_char_p]),
+        "yar_tp_plan": (I, [I, I, I, I, I, I, ctypes.POINTER(ctypes.c_int64)]),
+        "yar_tp_head_slice": (I, [I, I, I, ctypes.POINTER(I), ctypes.POINTER(I)]),
+        "yar_model_load_tp": (I, [ctypes.c_char_p, I, I, I, ctypes.c_char_p, ctypes.c_uint32, ctypes.POINTER(P)]),
         "yar_model_free": (I, [P]),
         "yar_model_dims": (I, [P, ctypes.POINTER(ctypes.c_int64)]),
         "yar_session_create": (I, [P, I, I, I, ctypes.POINTER(P)]),
@@ -131,12 +135,50 @@ ABC_SAMPLING = Sampling(.7, .9, 30, 1.005, 100, 32, 4096)
 """GenerationConfig.abc defaults (types.hpp:89)."""
 
 
-class ARModel:
-    """Converted BF16 AR weights resident on one GPU (ARModel, ar.cpp:133-238)."""
+def tp_unique_id() -> bytes:
+    """128 opaque bytes naming a new tensor-parallel group (ncclGetUniqueId); one rank
+    makes it and every rank passes it to ``ARModel(..., tp=(rank, world, id))``."""
+    buf = ctypes.create_string_buffer(128)
+    _check(lib.yar_tp_unique_id(buf))
+    return buf.raw
 
-    def __init__(self, path: str, device: int = 0, any_dims: bool = False):
+
+def tp_plan(heads: int, kv_heads: int, head_dim: int, ffn: int, rank: int, world: int) -> dict:
+    """The loader's tensor-parallel split for one rank, in rows of the whole model's
+    tensors (q_proj rows = o_proj columns, gate/up rows = down_proj columns)."""
+    out = (ctypes.c_int64 * 6)()
+    _check(lib.yar_tp_plan(heads, kv_heads, head_dim, ffn, rank, world, out))
+    keys = ("q_row0", "q_rows", "kv_row0", "kv_rows", "ffn_row0", "ffn_rows")
+    return dict(zip(keys, [int(v) for v in out]))
+
+
+def tp_head_slice(width: int, rank: int, world: int) -> tuple[int, int]:
+    """Columns [begin, end) of a phase projection this rank computes under tensor parallelism."""
+    b, e = ctypes.c_int(), ctypes.c_int()
+    _check(lib.yar_tp_head_slice(width, rank, world, ctypes.byref(b), ctypes.byref(e)))
+    return b.value, e.value
+
+
+class ARModel:
+    """Converted BF16 AR weights resident on one GPU (ARModel, ar.cpp:133-238).
+
+    ``tp=(rank, world, nccl_id)`` loads this rank's tensor-parallel share instead: its
+    KV-head groups and FFN column block, with NCCL exchanges inside every forward. All
+    ranks must then make the same calls with the same arguments."""
+
+    def __init__(self, path: str, device: int = 0, any_dims: bool = False, tp=None):
         h = ctypes.c_void_p()
-        _check(lib.yar_model_load_ex(os.fsencode(path), device, LOAD_ANY_DIMS if any_dims else 0, ctypes.byref(h)))
+        flags = LOAD_ANY_DIMS if any_dims else 0
+        if tp is None:
+            _check(lib.yar_model_load_ex(os.fsencode(path), device, flags, ctypes.byref(h)))
+            self.tp_rank, self.tp_world = 0, 1
+        else:
+            rank, world, nccl_id = tp
+            if len(nccl_id) != 128:
+                raise ValueError("nccl_id must be the 128 bytes of tp_unique_id()")
+            _check(lib.yar_model_load_tp(os.fsencode(path), device, rank, world, bytes(nccl_id), flags,
+                                         ctypes.byref(h)))
+            self.tp_rank, self.tp_world = rank, world
         self._h = h
         dims = (ctypes.c_int64 * 10)()
         _check(lib.yar_model_dims(h, dims))

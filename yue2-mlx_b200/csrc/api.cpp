@@ -1,6 +1,7 @@
 // api.cpp — the C ABI (include/yue2ar.h). Exceptions never cross it: every entry point
 // maps lyra-style typed errors to the lyra_status codes (native/include/CLyraCore/lyra.h:18-23)
 // and keeps the message for yar_last_error() on the calling thread.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -8,7 +9,8 @@
 #include "yue2ar.h"
 
 namespace yar {
-Model *load_model(const std::string &dir, int device, uint32_t flags);
+Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_rank = 0, int tp_world = 1,
+                  const uint8_t *nccl_id = nullptr);
 void free_model(Model *m);
 Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens);
 void free_session(Session *s);
@@ -96,6 +98,48 @@ int yar_model_load_ex(const char *dir, int device, uint32_t flags, yar_model **o
 }
 
 int yar_model_load(const char *dir, int device, yar_model **out) { return yar_model_load_ex(dir, device, 0, out); }
+
+int yar_tp_unique_id(uint8_t *out) {
+  return guarded([&] {
+    need(out, "out is required");
+    yar::tp_unique_id(out);
+  });
+}
+
+int yar_tp_plan(int heads, int kv_heads, int head_dim, int ffn, int rank, int world, int64_t *plan) {
+  return guarded([&] {
+    need(plan && heads > 0 && kv_heads > 0 && head_dim > 0 && ffn > 0 && heads % kv_heads == 0,
+         "positive dims with heads a multiple of kv_heads are required");
+    yar::Dims d;
+    d.heads = heads;
+    d.kv_heads = kv_heads;
+    d.head_dim = head_dim;
+    d.ffn = ffn;
+    const yar::TpPlan p = yar::tp_plan(d, rank, world);
+    const int64_t v[6] = {p.q_row0, p.q_rows, p.kv_row0, p.kv_rows, p.ffn_row0, p.ffn_rows};
+    std::memcpy(plan, v, sizeof(v));
+  });
+}
+
+int yar_tp_head_slice(int width, int rank, int world, int *begin, int *end) {
+  return guarded([&] {
+    need(begin && end && width > 0 && world >= 1 && rank >= 0 && rank < world, "width > 0, rank in [0, world)");
+    const int slice = yar::tp_head_slice(width, world);
+    *begin = std::min(width, rank * slice);
+    *end = std::min(width, (rank + 1) * slice);
+  });
+}
+
+int yar_model_load_tp(const char *dir, int device, int rank, int world, const uint8_t *nccl_id, uint32_t flags,
+                      yar_model **out) {
+  return guarded([&] {
+    need(dir && out && nccl_id, "dir, nccl_id and out are required");
+    need(world >= 1 && rank >= 0 && rank < world, "rank must be in [0, world)");
+    *out = nullptr;
+    auto *h = new yar_model{yar::load_model(dir, device, flags, rank, world, nccl_id)};
+    *out = h;
+  });
+}
 
 int yar_model_free(yar_model *model) {
   return guarded([&] {

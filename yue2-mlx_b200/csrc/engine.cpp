@@ -94,6 +94,12 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     YAR_CUDA(cudaMallocHost(&s->h_pinned, 1 << 20));
     s->gemm_ws_floats = size_t(4) << 20;
     s->gemm_ws = dmalloc<float>(s->gemm_ws_floats);
+    if (m->tp_world > 1) {
+      const int slice = tp_head_slice(widest, m->tp_world);
+      s->tp_part = dmalloc<float>(size_t(std::max(T, max_rows)) * d.hidden);
+      s->tp_send = dmalloc<bf16>(size_t(max_rows) * slice);
+      s->tp_recv = dmalloc<bf16>(size_t(m->tp_world) * max_rows * slice);
+    }
     s->n_ctr = 2 + 5 * d.layers;
     s->d_ctr = dmalloc<int>(s->n_ctr);
     s->d_epoch = dmalloc<int>(1);
@@ -117,7 +123,7 @@ void free_session(Session *s) {
                                                s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
                                                s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
                                                s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch, s->d_trace,
-                                               s->gemm_ws})
+                                               s->gemm_ws, s->tp_part, s->tp_send, s->tp_recv})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -154,9 +160,47 @@ void row_reset(Session &s, int row, int capacity) {
   s.pos[row] = 0;
 }
 
+// Under tensor parallelism the phase head is split by columns: rank r projects phase
+// columns [r*slice, (r+1)*slice) (its share of the main rows and, where it falls in the
+// slice, the ABC extra row) into [n_rows][slice], the slices are all-gathered and laid
+// out as full logits rows on every rank. `in` is normalized already when norm_w is null.
+static void project_tp(const Model &m, Session &s, const bf16 *in, int in_stride, const bf16 *norm_w,
+                       int n_rows, int phase, bf16 *out) {
+  const PhaseRows pr = phase_rows(m.d, phase);
+  const int width = pr.width(), slice = tp_head_slice(width, m.tp_world);
+  const int a = m.tp_rank * slice, b = std::min(width, a + slice);
+  const int H = m.d.hidden;
+  cudaStream_t st = s.stream;
+  const int main_end = std::min(b, pr.n_main);
+  if (main_end > a)
+    launch_gemv(m.lm_head + size_t(pr.row0 + a) * H, main_end - a, H, in, in_stride, norm_w, m.d.eps, s.tp_send,
+                slice, kEpiStore, n_rows, s.d_error, m.sm_count, st);
+  if (pr.extra >= 0 && a <= pr.n_main && pr.n_main < b)
+    launch_gemv(m.lm_head + size_t(pr.extra) * H, 1, H, in, in_stride, norm_w, m.d.eps, s.tp_send + (pr.n_main - a),
+                slice, kEpiStore, n_rows, s.d_error, m.sm_count, st);
+  tp_allgather_bf16(m, s.tp_send, s.tp_recv, size_t(n_rows) * slice, st);
+  launch_gather_logits(s.tp_recv, n_rows, slice, width, out, s.logit_stride, st);
+}
+
+// A linear whose input is split across tensor-parallel ranks (O over heads, down over FFN
+// columns), added to the residual x: on one GPU the residual epilogue; under tensor
+// parallelism the rank-partial FP32 product, all-reduced, rounded once and added.
+template <class Linear>
+static void linear_residual(const Model &m, Session &s, bf16 *x, int n_rows, Linear &&linear) {
+  if (m.tp_world == 1) {
+    linear(x, kEpiResidual);
+    return;
+  }
+  const int H = m.d.hidden;
+  linear(reinterpret_cast<bf16 *>(s.tp_part), kEpiF32);
+  tp_allreduce_f32(m, s.tp_part, size_t(n_rows) * H, s.stream);
+  launch_residual_f32(x, s.tp_part, n_rows, H, s.stream);
+}
+
 // LM head over the phase rows for `n_rows` input rows (norm fused), into logits rows.
 static void project(const Model &m, Session &s, const bf16 *in, int in_stride, int n_rows, int phase,
                     bf16 *out) {
+  if (m.tp_world > 1) return project_tp(m, s, in, in_stride, m.final_norm, n_rows, phase, out);
   const PhaseRows pr = phase_rows(m.d, phase);
   launch_gemv(m.lm_head + size_t(pr.row0) * m.d.hidden, pr.n_main, m.d.hidden, in, in_stride, m.final_norm,
               m.d.eps, out, s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, s.stream);
@@ -200,10 +244,10 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
       gemm(s.ph, T, H, w.qkv, QKV, s.pqkv, QKV, kEpiStore);
       launch_qkv_post_prefill(m, s, l, row, start, T, st);
       launch_attn_prefill(m, s, l, row, start, T, st);
-      gemm(s.pattn, T, d.qdim(), w.o, H, s.px, H, kEpiResidual);
+      linear_residual(m, s, s.px, T, [&](bf16 *out, int epi) { gemm(s.pattn, T, d.qdim(), w.o, H, out, H, epi); });
       launch_rmsnorm_rows(s.px, w.ln2, T, H, d.eps, s.ph, st);
       gemm(s.ph, T, H, w.gu, 2 * d.ffn, s.pmlp, d.ffn, kEpiSwiGLU);
-      gemm(s.pmlp, T, d.ffn, w.down, H, s.px, H, kEpiResidual);
+      linear_residual(m, s, s.px, T, [&](bf16 *out, int epi) { gemm(s.pmlp, T, d.ffn, w.down, H, out, H, epi); });
     }
     if (c0 + T == n)
       project(m, s, s.px + size_t(T - 1) * H, H, 1, phase, s.logits + size_t(row) * s.logit_stride);
@@ -222,7 +266,8 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
 static bool use_persistent(Session &s, int n_rows) {
   // The persistent kernel streams each 64-position KV chunk as one contiguous copy, so a
   // chunk must not straddle pages.
-  if (!s.use_persistent || n_rows < 1 || n_rows > 2 || s.page_tokens < 64) return false;
+  // Under tensor parallelism the exchange steps run between per-operation launches.
+  if (!s.use_persistent || n_rows < 1 || n_rows > 2 || s.page_tokens < 64 || s.m->tp_world > 1) return false;
   if (s.persistent_ok[n_rows] < 0) s.persistent_ok[n_rows] = persistent_supported(*s.m, n_rows) ? 1 : 0;
   return s.persistent_ok[n_rows] == 1;
 }
@@ -262,12 +307,13 @@ static void decode_forward_batched(Session &s, int n_rows, int phase) {
     launch_rmsnorm_rows(s.x, w.ln1, n_rows, H, d.eps, s.ph, st);
     gemm(s.ph, H, w.qkv, d.qkv_rows(), s.qkv, d.qkv_rows(), kEpiStore);
     launch_attn_decode(m, s, l, n_rows, st, splits);
-    gemm(s.attn, d.qdim(), w.o, H, s.x, H, kEpiResidual);
+    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) { gemm(s.attn, d.qdim(), w.o, H, out, H, epi); });
     launch_rmsnorm_rows(s.x, w.ln2, n_rows, H, d.eps, s.ph, st);
     gemm(s.ph, H, w.gu, 2 * d.ffn, s.mlp, d.ffn, kEpiSwiGLU);
-    gemm(s.mlp, d.ffn, w.down, H, s.x, H, kEpiResidual);
+    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) { gemm(s.mlp, d.ffn, w.down, H, out, H, epi); });
   }
   launch_rmsnorm_rows(s.x, m.final_norm, n_rows, H, d.eps, s.ph, st);
+  if (m.tp_world > 1) return project_tp(m, s, s.ph, H, nullptr, n_rows, phase, s.logits);
   // Head: an even number of rows as a GEMM; an odd last phase row and the ABC extra row as
   // GEMVs over the normalized rows.
   const PhaseRows pr = phase_rows(d, phase);
@@ -300,12 +346,16 @@ static void decode_forward(Session &s, int n_rows, int phase) {
     launch_gemv(w.qkv, d.qkv_rows(), d.hidden, s.x, d.hidden, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows,
                 s.d_error, m.sm_count, st);
     launch_attn_decode(m, s, l, n_rows, st);
-    launch_gemv(w.o, d.hidden, d.qdim(), s.attn, d.qdim(), nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows,
-                s.d_error, m.sm_count, st);
+    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) {
+      launch_gemv(w.o, d.hidden, d.qdim(), s.attn, d.qdim(), nullptr, d.eps, out, d.hidden, epi, n_rows, s.d_error,
+                  m.sm_count, st);
+    });
     launch_gemv(w.gu, 2 * d.ffn, d.hidden, s.x, d.hidden, w.ln2, d.eps, s.mlp, d.ffn, kEpiSwiGLU, n_rows, s.d_error,
                 m.sm_count, st);
-    launch_gemv(w.down, d.hidden, d.ffn, s.mlp, d.ffn, nullptr, d.eps, s.x, d.hidden, kEpiResidual, n_rows, s.d_error,
-                m.sm_count, st);
+    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) {
+      launch_gemv(w.down, d.hidden, d.ffn, s.mlp, d.ffn, nullptr, d.eps, out, d.hidden, epi, n_rows, s.d_error,
+                  m.sm_count, st);
+    });
   }
   project(m, s, s.x, d.hidden, n_rows, phase, s.logits);
 }
@@ -531,6 +581,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
                            {"cfg_branches", cfg ? 2 : 1},
                            {"execution", "cuda_graph"},
                            {"attention", "split_kv"},
+                           {"tensor_parallel", s.m->tp_world},
                            {"backend", "cuda-sm100a"},
                            {"decode_steps", steps},
                            {"decode_device_ms", decode_ms}};
@@ -694,6 +745,7 @@ std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const
                            {"decode_device_ms", decode_ms},
                            {"execution", "cuda_graph"},
                            {"forward", n_req >= kBatchedRows ? "batched_tcgen05" : "per_row"},
+                           {"tensor_parallel", s.m->tp_world},
                            {"backend", "cuda-sm100a"}};
   return timing.dump();
 }

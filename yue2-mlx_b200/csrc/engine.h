@@ -57,7 +57,34 @@ struct Model {
   std::vector<LayerWeights> layers;
   LayerWeights *d_layers = nullptr;  // device copy of `layers` (persistent decode kernel)
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
+  // Tensor parallelism: this rank's share of the heads, KV heads and FFN columns is in `d`
+  // (the whole model's dims in `full`); `tp_comm` is the NCCL communicator (null: one GPU).
+  Dims full;
+  int tp_rank = 0, tp_world = 1;
+  void *tp_comm = nullptr;
 };
+
+// Tensor-parallel share of one rank, in rows/columns of the whole model's tensors: query
+// rows [q_row0, +q_rows) of q_proj (= columns of o_proj), rows [kv_row0, +kv_rows) of
+// k_proj and v_proj, rows [ffn_row0, +ffn_rows) of gate_proj and up_proj (= columns of
+// down_proj). KV heads are split into equal groups and each keeps its query heads.
+struct TpPlan {
+  int q_row0 = 0, q_rows = 0, kv_row0 = 0, kv_rows = 0, ffn_row0 = 0, ffn_rows = 0;
+};
+TpPlan tp_plan(const Dims &full, int rank, int world);
+
+// Tensor-parallel exchange steps (tp.cpp) and the element-wise kernels around them.
+void tp_unique_id(uint8_t *out128);
+void tp_init(Model &m, int rank, int world, const uint8_t *id128);
+void tp_destroy(Model &m);
+void tp_allreduce_f32(const Model &m, float *buf, size_t n, cudaStream_t st);
+void tp_allgather_bf16(const Model &m, const bf16 *send, bf16 *recv, size_t n, cudaStream_t st);
+void launch_residual_f32(bf16 *x, const float *sum, int n_rows, int H, cudaStream_t st);
+void launch_gather_logits(const bf16 *recv, int n_rows, int slice, int width, bf16 *logits, int logit_stride,
+                          cudaStream_t st);
+// LM-head columns per rank under tensor parallelism: the phase width split evenly, rounded
+// up to 8 columns.
+inline int tp_head_slice(int width, int world) { return ((width + world - 1) / world + 7) / 8 * 8; }
 
 // Phase projection of the LM head: rows [row0, row0 + n_main) and, optionally, one extra
 // row mapped to local index n_main (native/src/ar.cpp:302-323).
@@ -123,7 +150,10 @@ void configure_sampler_kernels();
 bool persistent_supported(const Model &m, int n_rows);
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
 
-enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
+// kEpiF32: the FP32 accumulator itself (the output pointer is a float array and its
+// stride counts floats) — a tensor-parallel rank's partial sum of O or down, all-reduced
+// before the one BF16 rounding and residual add.
+enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3 };
 
 struct Session {
   Model *m = nullptr;
@@ -179,6 +209,11 @@ struct Session {
   size_t gemm_ws_floats = 0;
   int prefetch_stages = 6;  // persistent kernel: L2 prefetch distance beyond the ring
   unsigned long long *d_trace = nullptr;  // persistent-kernel timeline (when enabled)
+  // Tensor parallelism: the rank-partial FP32 sums of O and down
+  // ([max(prefill_chunk, max_rows)][hidden]) and the LM-head slices before
+  // ([max_rows][slice]) and after ([world][max_rows][slice]) the all-gather.
+  float *tp_part = nullptr;
+  bf16 *tp_send = nullptr, *tp_recv = nullptr;
   size_t trace_elems = 0;
 };
 

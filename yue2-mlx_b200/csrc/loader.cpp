@@ -160,8 +160,25 @@ static std::map<std::string, TensorRec> read_safetensors_header(const std::strin
   return out;
 }
 
-Model *load_model(const std::string &dir, int device, uint32_t flags) {
+TpPlan tp_plan(const Dims &d, int rank, int world) {
+  if (world < 1 || rank < 0 || rank >= world) throw Error("ValueError", "tensor-parallel rank outside [0, world)");
+  if (d.kv_heads % world || d.ffn % world || (d.ffn / world) % 8)
+    throw Error("ValueError", "tensor-parallel world must divide num_key_value_heads and intermediate_size / 8");
+  const int group = d.heads / d.kv_heads;  // query heads per KV head stay together
+  TpPlan p;
+  p.kv_rows = d.kv_heads / world * d.head_dim;
+  p.kv_row0 = rank * p.kv_rows;
+  p.q_rows = p.kv_rows * group;
+  p.q_row0 = rank * p.q_rows;
+  p.ffn_rows = d.ffn / world;
+  p.ffn_row0 = rank * p.ffn_rows;
+  return p;
+}
+
+Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_rank, int tp_world,
+                  const uint8_t *nccl_id) {
   const bool any_dims = flags & 1u;
+  if (tp_world > 1 && !nccl_id) throw Error("ValueError", "tensor parallelism needs an NCCL unique id");
   // 1. Manifest.
   Json manifest = read_json(dir + "/conversion.json");
   if (!manifest.is_object() || manifest.value("schema", 0) != 1)
@@ -207,11 +224,21 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
   }
   for (const auto &[name, rec] : recs)
     if (!expected.count(name)) throw Error("ValueError", "Unexpected AR tensor: " + name);
+  // Tensor-parallel share of this rank (the tensors keep their full shapes on disk).
+  const TpPlan plan = tp_plan(d, tp_rank, tp_world);
+  Dims dl = d;
+  dl.heads = plan.q_rows / d.head_dim;
+  dl.kv_heads = plan.kv_rows / d.head_dim;
+  dl.ffn = plan.ffn_rows;
+  const int Ql = dl.qdim(), KVl = dl.kvdim(), Fl = dl.ffn;
 
   // Arena layout (256-byte aligned pieces).
   auto *m = new Model();
   try {
-    m->d = d;
+    m->d = dl;
+    m->full = d;
+    m->tp_rank = tp_rank;
+    m->tp_world = tp_world;
     m->device = device;
     YAR_CUDA(cudaSetDevice(device));
     YAR_CUDA(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device));
@@ -233,10 +260,10 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     struct LO { size_t qkv, o, gu, down, ln1, ln2, qn, kn; };
     std::vector<LO> lo(d.layers);
     for (int i = 0; i < d.layers; ++i) {
-      lo[i].qkv = take(size_t(Q + 2 * KV) * H * e2);
-      lo[i].o = take(size_t(H) * Q * e2);
-      lo[i].gu = take(size_t(2 * F) * H * e2);
-      lo[i].down = take(size_t(H) * F * e2);
+      lo[i].qkv = take(size_t(Ql + 2 * KVl) * H * e2);
+      lo[i].o = take(size_t(H) * Ql * e2);
+      lo[i].gu = take(size_t(2 * Fl) * H * e2);
+      lo[i].down = take(size_t(H) * Fl * e2);
       lo[i].ln1 = take(H * e2);
       lo[i].ln2 = take(H * e2);
       lo[i].qn = take(D * e2);
@@ -269,32 +296,51 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
         got += size_t(r);
       }
     };
-    // Copy bytes [src_off, src_off+n) of a tensor to device address dst (row-chunked).
-    auto upload = [&](const std::string &name, char *dst) {
+    // Copy the block rows [row0, row0+nrows) x columns [col0, col0+ncols) of a 2-D tensor
+    // (a 1-D tensor is one row) to dst, packed [nrows][ncols]; the whole tensor by default.
+    auto upload_block = [&](const std::string &name, char *dst, int64_t row0, int64_t nrows, int64_t col0,
+                            int64_t ncols) {
       const TensorRec &r = recs.at(name);
-      const uint64_t n = r.end - r.begin;
-      for (uint64_t done_b = 0; done_b < n; done_b += stage_bytes) {
-        const size_t len = size_t(std::min<uint64_t>(stage_bytes, n - done_b));
+      const int64_t cols = r.shape.size() == 2 ? r.shape[1] : r.shape[0];
+      const size_t src_row = size_t(cols) * e2, dst_row = size_t(ncols) * e2;
+      const bool whole_rows = col0 == 0 && ncols == cols;
+      const int64_t rows_per = int64_t(stage_bytes / src_row);
+      std::vector<char> tmp(whole_rows ? 0 : size_t(rows_per) * src_row);
+      for (int64_t r0 = 0; r0 < nrows; r0 += rows_per) {
+        const int64_t nr = std::min(rows_per, nrows - r0);
         if (pending[buf]) YAR_CUDA(cudaEventSynchronize(done[buf]));
         char *sb = static_cast<char *>(stage) + buf * stage_bytes;
-        pread_all(sb, data_start + r.begin + done_b, len);
-        YAR_CUDA(cudaMemcpyAsync(dst + done_b, sb, len, cudaMemcpyHostToDevice, st));
+        const uint64_t src = data_start + r.begin + uint64_t(row0 + r0) * src_row;
+        if (whole_rows) {
+          pread_all(sb, src, size_t(nr) * src_row);
+        } else {
+          pread_all(tmp.data(), src, size_t(nr) * src_row);
+          for (int64_t j = 0; j < nr; ++j)
+            std::memcpy(sb + size_t(j) * dst_row, tmp.data() + size_t(j) * src_row + size_t(col0) * e2, dst_row);
+        }
+        YAR_CUDA(cudaMemcpyAsync(dst + size_t(r0) * dst_row, sb, size_t(nr) * dst_row, cudaMemcpyHostToDevice, st));
         YAR_CUDA(cudaEventRecord(done[buf], st));
         pending[buf] = true;
         buf ^= 1;
       }
     };
+    auto upload = [&](const std::string &name, char *dst) {
+      const TensorRec &r = recs.at(name);
+      const int64_t rows = r.shape.size() == 2 ? r.shape[0] : 1, cols = r.shape.size() == 2 ? r.shape[1] : r.shape[0];
+      upload_block(name, dst, 0, rows, 0, cols);
+    };
     // Interleave gate/up rows into dst: rows 2j (gate j) and 2j+1 (up j).
-    auto upload_gate_up = [&](const std::string &gate, const std::string &up, char *dst) {
+    // Rows [f0, f0 + nf) of gate_proj and up_proj (this rank's FFN block).
+    auto upload_gate_up = [&](const std::string &gate, const std::string &up, char *dst, int f0, int nf) {
       const size_t row_bytes = size_t(H) * e2;
       const size_t rows_per = stage_bytes / (2 * row_bytes);
-      for (int r0 = 0; r0 < F; r0 += int(rows_per)) {
-        const int nr = int(std::min<size_t>(rows_per, size_t(F - r0)));
+      for (int r0 = 0; r0 < nf; r0 += int(rows_per)) {
+        const int nr = int(std::min<size_t>(rows_per, size_t(nf - r0)));
         if (pending[buf]) YAR_CUDA(cudaEventSynchronize(done[buf]));
         char *sb = static_cast<char *>(stage) + buf * stage_bytes;
         std::vector<char> g(nr * row_bytes), u(nr * row_bytes);
-        pread_all(g.data(), data_start + recs.at(gate).begin + size_t(r0) * row_bytes, g.size());
-        pread_all(u.data(), data_start + recs.at(up).begin + size_t(r0) * row_bytes, u.size());
+        pread_all(g.data(), data_start + recs.at(gate).begin + size_t(f0 + r0) * row_bytes, g.size());
+        pread_all(u.data(), data_start + recs.at(up).begin + size_t(f0 + r0) * row_bytes, u.size());
         for (int j = 0; j < nr; ++j) {
           std::memcpy(sb + (2 * size_t(j)) * row_bytes, g.data() + size_t(j) * row_bytes, row_bytes);
           std::memcpy(sb + (2 * size_t(j) + 1) * row_bytes, u.data() + size_t(j) * row_bytes, row_bytes);
@@ -312,12 +358,14 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     m->layers.resize(d.layers);
     for (int i = 0; i < d.layers; ++i) {
       const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
-      upload(a + ".q_proj.weight", base + lo[i].qkv);
-      upload(a + ".k_proj.weight", base + lo[i].qkv + size_t(Q) * H * e2);
-      upload(a + ".v_proj.weight", base + lo[i].qkv + size_t(Q + KV) * H * e2);
-      upload(a + ".o_proj.weight", base + lo[i].o);
-      upload_gate_up(n + ".mlp.gate_proj.weight", n + ".mlp.up_proj.weight", base + lo[i].gu);
-      upload(n + ".mlp.down_proj.weight", base + lo[i].down);
+      // Rank r: q rows of its heads, k/v rows of its KV heads, the matching O columns, its
+      // FFN block of gate/up rows and down columns (all of them when tp_world == 1).
+      upload_block(a + ".q_proj.weight", base + lo[i].qkv, plan.q_row0, Ql, 0, H);
+      upload_block(a + ".k_proj.weight", base + lo[i].qkv + size_t(Ql) * H * e2, plan.kv_row0, KVl, 0, H);
+      upload_block(a + ".v_proj.weight", base + lo[i].qkv + size_t(Ql + KVl) * H * e2, plan.kv_row0, KVl, 0, H);
+      upload_block(a + ".o_proj.weight", base + lo[i].o, 0, H, plan.q_row0, Ql);
+      upload_gate_up(n + ".mlp.gate_proj.weight", n + ".mlp.up_proj.weight", base + lo[i].gu, plan.ffn_row0, Fl);
+      upload_block(n + ".mlp.down_proj.weight", base + lo[i].down, 0, H, plan.ffn_row0, Fl);
       upload(n + ".input_layernorm.weight", base + lo[i].ln1);
       upload(n + ".post_attention_layernorm.weight", base + lo[i].ln2);
       upload(a + ".q_norm.weight", base + lo[i].qn);
@@ -359,7 +407,9 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
     YAR_CUDA(cudaStreamDestroy(st));
     YAR_CUDA(cudaFreeHost(stage));
     ::close(fd);
+    if (tp_world > 1) tp_init(*m, tp_rank, tp_world, nccl_id);
   } catch (...) {
+    tp_destroy(*m);
     if (m->arena) cudaFree(m->arena);
     if (m->d_layers) cudaFree(m->d_layers);
     delete m;
@@ -371,6 +421,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags) {
 void free_model(Model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  tp_destroy(*m);
   if (m->arena) cudaFree(m->arena);
   if (m->d_layers) cudaFree(m->d_layers);
   delete m;
