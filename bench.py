@@ -8,6 +8,10 @@ exactly 400 tokens). One bench step = one generate_tokens call through the C ABI
 N > 1 runs under torchrun, one rank per GPU, each rank an independent song (data
 parallel, no collective on the data path; NCCL only for the barrier and the max-reduce
 of the timings). Prints one JSON line on rank 0.
+
+Two more workloads are reported under their own keys of the same line: "bs64" (config
+5: 64 independent requests per GPU, data parallel) and "long_context" (config 4: one
+9000-position song, tensor-parallel across all N ranks with the NCCL exchange steps).
 """
 from __future__ import annotations
 
@@ -137,6 +141,49 @@ def batched_throughput(yar, model, rank, barrier, maxall):
             "frac_of_hbm": achieved / peak, "forward": timing["forward"]}
 
 
+LONG_PROMPT, LONG_TOTAL = 2048, 9000
+
+
+def long_context(yar, model_one, weights, rank, world, local, barrier, maxall):
+    """Config 4: one song — prompt of 2048 random ids decoded to 9000 positions (6952
+    sampled semantic tokens, fixed length), 256-token pages — tensor-parallel over all
+    ranks (TP = N; N = 1 runs the one-GPU model, persistent kernel). Value = decoded tokens
+    over the decode loop's device time, max over ranks; e2e = tokens over the wall time of
+    the generate call (prefill, host copies and the token read-back included)."""
+    if world > 1:
+        import torch.distributed as dist
+        ids = [yar.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        model = yar.ARModel(weights, device=local, tp=(rank, world, ids[0]))
+    else:
+        model = model_one
+    n_dec = LONG_TOTAL - LONG_PROMPT
+    rng = np.random.default_rng(7000)  # the same song on every rank
+    prompt = rng.integers(0, 184704, LONG_PROMPT).astype(np.int32)
+    s = model.session(max_rows=1, max_ctx=LONG_TOTAL, page_tokens=256)
+    s.generate(prompt[:256], yar.Sampling(**dict(SAMPLING, min_tokens=32, max_tokens=32)), seed=1, phase="semantic")
+    barrier()
+    t0 = time.perf_counter()
+    toks, timing, _ = s.generate(prompt, yar.Sampling(**dict(SAMPLING, min_tokens=n_dec, max_tokens=n_dec)), seed=2,
+                                 phase="semantic")
+    wall = time.perf_counter() - t0
+    s.close()
+    if model is not model_one:
+        model.close()
+    dec, wall = maxall(timing["decode_device_ms"] / 1000.0), maxall(wall)
+    avg_L = LONG_PROMPT + n_dec / 2
+    # Per GPU and token: its share of the layers, the head and the KV cache, plus the
+    # replicated norms and embedding row.
+    per_gpu = (28 * LAYER_BYTES + HEAD_BYTES + KV_BYTES_PER_POS * (avg_L + 1)) / world + NORM_BYTES + EMBED_BYTES
+    peak, _ = peaks()
+    achieved = per_gpu / (dec / len(toks)) / 1e9
+    return {"workload": "config4: one song, prompt 2048, decoded to 9000 positions, 256-token pages",
+            "parallelism": f"tp{world}", "value": len(toks) / dec, "unit": "tok/s", "e2e": len(toks) / wall,
+            "tokens": len(toks), "ms_per_token": 1000 * dec / len(toks), "prefill_s": timing["prefill_seconds"],
+            "bytes_per_token_per_gpu": int(per_gpu), "achieved_gbs_per_gpu": achieved, "frac_of_hbm": achieved / peak,
+            "tensor_parallel": timing["tensor_parallel"]}
+
+
 def measured_traffic(avg_L: float):
     """DRAM bytes (read + write) of one persistent decode launch from the committed ncu
     capture, moved from the captured position to `avg_L` by the KV bytes per position
@@ -218,6 +265,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bs64", action="store_true", help="skip the config-5 batched throughput measurement")
+    ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context tensor-parallel song")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -301,6 +349,7 @@ def main():
     prefill_launches = 1 + 8 * layers + 1
     traffic = measured_traffic(avg_L)
     bs64 = None if args.no_bs64 else batched_throughput(yar, model, rank, barrier, maxall)
+    long = None if args.no_long else long_context(yar, model, weights, rank, world, local, barrier, maxall)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -326,6 +375,7 @@ def main():
             "clocks": clk.summary,
             "cpu_baseline": cpu,
             "bs64": bs64,
+            "long_context": long,
         }
         print(json.dumps(out))
     session.close()
