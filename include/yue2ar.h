@@ -76,21 +76,23 @@ int yar_model_load(const char *dir, int device, yar_model **out);
 int yar_model_load_ex(const char *dir, int device, uint32_t flags, yar_model **out);
 int yar_model_free(yar_model *model);
 /* Tensor parallelism over `world` GPUs, one process per GPU (no reference counterpart:
- * the reference runs one device; this is the column/row split of ARModel's layers).
- * Rank r holds KV heads [r*kv/world, (r+1)*kv/world) with their query heads (q/k/v rows,
- * O columns), FFN columns [r*ffn/world, (r+1)*ffn/world) (gate/up rows, down columns),
- * and the embedding, norms and LM head whole. Each layer all-reduces the FP32 partial
- * sums of O and down over NCCL and rounds them once into the residual; the phase head is
- * split by columns and its BF16 logits all-gathered, so every rank samples the same
- * tokens. Every rank makes the same calls in the same order with the same arguments.
+ * the reference runs one device; this splits ARModel's layers across GPUs). Every linear
+ * is split by output rows with its whole input width: rank r holds KV heads
+ * [r*kv/world, (r+1)*kv/world) with their query heads (q/k/v rows), FFN rows
+ * [r*ffn/world, (r+1)*ffn/world) of gate/up, hidden rows [r*hidden/world, ...) of O and
+ * down, and the embedding, norms and LM head whole (it projects its share of each phase's
+ * columns). After each operation the ranks' BF16 outputs are all-gathered over NCCL, so
+ * every value is computed by one rank with the one-GPU arithmetic: logits and tokens are
+ * those of one GPU, on every rank. Every rank makes the same calls in the same order with
+ * the same arguments.
  * `nccl_id` is 128 bytes from yar_tp_unique_id on one rank, passed to all of them.
  * NCCL is opened at run time (libnccl.so.2). With a TP model yar_model_dims reports this
  * rank's heads, kv_heads and ffn. */
 int yar_tp_unique_id(uint8_t *nccl_id128);
-/* The split itself, without a GPU: plan6 = {q_row0, q_rows, kv_row0, kv_rows, ffn_row0,
- * ffn_rows} — this rank's rows of q_proj (= columns of o_proj), of k_proj and v_proj, and
- * of gate_proj and up_proj (= columns of down_proj) in the whole model's tensors. */
-int yar_tp_plan(int heads, int kv_heads, int head_dim, int ffn, int rank, int world, int64_t *plan6);
+/* The split itself, without a GPU: plan8 = {q_row0, q_rows, kv_row0, kv_rows, ffn_row0,
+ * ffn_rows, h_row0, h_rows} — this rank's rows of q_proj, of k_proj and v_proj, of
+ * gate_proj and up_proj, and of o_proj and down_proj, in the whole model's tensors. */
+int yar_tp_plan(int hidden, int heads, int kv_heads, int head_dim, int ffn, int rank, int world, int64_t *plan8);
 /* This rank's LM-head columns [begin, end) of a `width`-column phase projection. */
 int yar_tp_head_slice(int width, int rank, int world, int *begin, int *end);
 int yar_model_load_tp(const char *dir, int device, int rank, int world, const uint8_t *nccl_id128,

@@ -68,7 +68,7 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_model_load": (I, [ctypes.c_char_p, I, ctypes.POINTER(P)]),
         "yar_model_load_ex": (I, [ctypes.c_char_p, I, ctypes.c_uint32, ctypes.POINTER(P)]),
         "yar_tp_unique_id": (I, [ctypes.c_char_p]),
-        "yar_tp_plan": (I, [I, I, I, I, I, I, ctypes.POINTER(ctypes.c_int64)]),
+        "yar_tp_plan": (I, [I, I, I, I, I, I, I, ctypes.POINTER(ctypes.c_int64)]),
         "yar_tp_head_slice": (I, [I, I, I, ctypes.POINTER(I), ctypes.POINTER(I)]),
         "yar_model_load_tp": (I, [ctypes.c_char_p, I, I, I, ctypes.c_char_p, ctypes.c_uint32, ctypes.POINTER(P)]),
         "yar_model_free": (I, [P]),
@@ -143,12 +143,12 @@ def tp_unique_id() -> bytes:
     return buf.raw
 
 
-def tp_plan(heads: int, kv_heads: int, head_dim: int, ffn: int, rank: int, world: int) -> dict:
+def tp_plan(hidden: int, heads: int, kv_heads: int, head_dim: int, ffn: int, rank: int, world: int) -> dict:
     """The loader's tensor-parallel split for one rank, in rows of the whole model's
-    tensors (q_proj rows = o_proj columns, gate/up rows = down_proj columns)."""
-    out = (ctypes.c_int64 * 6)()
-    _check(lib.yar_tp_plan(heads, kv_heads, head_dim, ffn, rank, world, out))
-    keys = ("q_row0", "q_rows", "kv_row0", "kv_rows", "ffn_row0", "ffn_rows")
+    tensors: q_proj, k/v_proj, gate/up_proj and o/down_proj ("h") rows."""
+    out = (ctypes.c_int64 * 8)()
+    _check(lib.yar_tp_plan(hidden, heads, kv_heads, head_dim, ffn, rank, world, out))
+    keys = ("q_row0", "q_rows", "kv_row0", "kv_rows", "ffn_row0", "ffn_rows", "h_row0", "h_rows")
     return dict(zip(keys, [int(v) for v in out]))
 
 

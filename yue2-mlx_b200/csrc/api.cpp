@@ -106,17 +106,18 @@ int yar_tp_unique_id(uint8_t *out) {
   });
 }
 
-int yar_tp_plan(int heads, int kv_heads, int head_dim, int ffn, int rank, int world, int64_t *plan) {
+int yar_tp_plan(int hidden, int heads, int kv_heads, int head_dim, int ffn, int rank, int world, int64_t *plan) {
   return guarded([&] {
-    need(plan && heads > 0 && kv_heads > 0 && head_dim > 0 && ffn > 0 && heads % kv_heads == 0,
+    need(plan && hidden > 0 && heads > 0 && kv_heads > 0 && head_dim > 0 && ffn > 0 && heads % kv_heads == 0,
          "positive dims with heads a multiple of kv_heads are required");
     yar::Dims d;
+    d.hidden = hidden;
     d.heads = heads;
     d.kv_heads = kv_heads;
     d.head_dim = head_dim;
     d.ffn = ffn;
     const yar::TpPlan p = yar::tp_plan(d, rank, world);
-    const int64_t v[6] = {p.q_row0, p.q_rows, p.kv_row0, p.kv_rows, p.ffn_row0, p.ffn_rows};
+    const int64_t v[8] = {p.q_row0, p.q_rows, p.kv_row0, p.kv_rows, p.ffn_row0, p.ffn_rows, p.h_row0, p.h_rows};
     std::memcpy(plan, v, sizeof(v));
   });
 }

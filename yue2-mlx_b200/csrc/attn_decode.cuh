@@ -86,7 +86,8 @@ struct DecodeAttnParams {
   const float *cos_tab, *sin_tab;
   float *part;   // [rows][heads][max_splits][D + 2]
   int *count;    // [rows][kv_heads]
-  bf16 *out;     // [rows][qdim]
+  bf16 *out;     // row r, head h at out[r * out_stride + h * D]
+  int out_stride;
 };
 
 constexpr int kKvChunk = 64;  // positions per KV chunk
@@ -405,7 +406,7 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
       }
       M = Mb;
     }
-    p.out[size_t(row) * p.g.qdim + (kvh * G + hd) * D + d] = f2bf(O * (1.0f / Ls));
+    p.out[size_t(row) * p.out_stride + (kvh * G + hd) * D + d] = f2bf(O * (1.0f / Ls));
   }
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
 }

@@ -66,8 +66,11 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     s->pos.assign(max_rows, 0);
     s->x = dmalloc<bf16>(size_t(max_rows) * d.hidden);
     s->qkv = dmalloc<bf16>(size_t(max_rows) * d.qkv_rows());
-    s->attn = dmalloc<bf16>(size_t(max_rows) * d.qdim());
-    s->mlp = dmalloc<bf16>(size_t(max_rows) * d.ffn);
+    // Attention and FFN activations at the whole model's width: under tensor parallelism
+    // each rank writes its block and the all-gather fills in the others.
+    const Dims &f = m->full;
+    s->attn = dmalloc<bf16>(size_t(max_rows) * f.qdim());
+    s->mlp = dmalloc<bf16>(size_t(max_rows) * f.ffn);
     int widest = d.vocab;
     if (d.vocab == 184704) widest = std::max(phase_rows(d, kPhaseAbc).width(), phase_rows(d, kPhaseSemantic).width());
     s->logit_stride = (widest + 7) & ~7;
@@ -82,8 +85,8 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     s->ph = dmalloc<bf16>(size_t(T) * d.hidden);
     s->pqkv = dmalloc<bf16>(size_t(T) * d.qkv_rows());
     s->pq = dmalloc<bf16>(size_t(T) * d.qdim());
-    s->pattn = dmalloc<bf16>(size_t(T) * d.qdim());
-    s->pmlp = dmalloc<bf16>(size_t(T) * d.ffn);
+    s->pattn = dmalloc<bf16>(size_t(T) * f.qdim());
+    s->pmlp = dmalloc<bf16>(size_t(T) * f.ffn);
     s->pids = dmalloc<int>(T);
     s->max_requests = max_rows;
     s->d_req = dmalloc<RequestState>(max_rows);
@@ -95,10 +98,10 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     s->gemm_ws_floats = size_t(4) << 20;
     s->gemm_ws = dmalloc<float>(s->gemm_ws_floats);
     if (m->tp_world > 1) {
-      const int slice = tp_head_slice(widest, m->tp_world);
-      s->tp_part = dmalloc<float>(size_t(std::max(T, max_rows)) * d.hidden);
-      s->tp_send = dmalloc<bf16>(size_t(max_rows) * slice);
-      s->tp_recv = dmalloc<bf16>(size_t(m->tp_world) * max_rows * slice);
+      const size_t block = std::max({size_t(std::max(T, max_rows)) * std::max({d.qdim(), d.ffn, m->tp.h_rows}),
+                                     size_t(max_rows) * tp_head_slice(widest, m->tp_world)});
+      s->tp_send = dmalloc<bf16>(block);
+      s->tp_recv = dmalloc<bf16>(size_t(m->tp_world) * block);
     }
     s->n_ctr = 2 + 5 * d.layers;
     s->d_ctr = dmalloc<int>(s->n_ctr);
@@ -123,7 +126,7 @@ void free_session(Session *s) {
                                                s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
                                                s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
                                                s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch, s->d_trace,
-                                               s->gemm_ws, s->tp_part, s->tp_send, s->tp_recv})
+                                               s->gemm_ws, s->tp_send, s->tp_recv})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -160,53 +163,74 @@ void row_reset(Session &s, int row, int capacity) {
   s.pos[row] = 0;
 }
 
-// Under tensor parallelism the phase head is split by columns: rank r projects phase
-// columns [r*slice, (r+1)*slice) (its share of the main rows and, where it falls in the
-// slice, the ABC extra row) into [n_rows][slice], the slices are all-gathered and laid
-// out as full logits rows on every rank. `in` is normalized already when norm_w is null.
-static void project_tp(const Model &m, Session &s, const bf16 *in, int in_stride, const bf16 *norm_w,
-                       int n_rows, int phase, bf16 *out) {
+// Phase columns [c0, c1) of the LM head for `n_rows` input rows into out ([n_rows][stride],
+// column c at out[c - c0]). `normed`: `in` holds the final-normed rows and the main rows
+// go through the GEMM (an even number of them) with the GEMV for an odd last one; else
+// the GEMVs apply the final RMSNorm themselves. Each column's value depends only on its
+// weight row, so any column range gives the bits of the whole projection.
+static void project_cols(const Model &m, Session &s, const bf16 *in, int in_stride, bool normed, int n_rows,
+                         int phase, int c0, int c1, bf16 *out, int stride) {
   const PhaseRows pr = phase_rows(m.d, phase);
-  const int width = pr.width(), slice = tp_head_slice(width, m.tp_world);
-  const int a = m.tp_rank * slice, b = std::min(width, a + slice);
   const int H = m.d.hidden;
   cudaStream_t st = s.stream;
-  const int main_end = std::min(b, pr.n_main);
-  if (main_end > a)
-    launch_gemv(m.lm_head + size_t(pr.row0 + a) * H, main_end - a, H, in, in_stride, norm_w, m.d.eps, s.tp_send,
-                slice, kEpiStore, n_rows, s.d_error, m.sm_count, st);
-  if (pr.extra >= 0 && a <= pr.n_main && pr.n_main < b)
-    launch_gemv(m.lm_head + size_t(pr.extra) * H, 1, H, in, in_stride, norm_w, m.d.eps, s.tp_send + (pr.n_main - a),
-                slice, kEpiStore, n_rows, s.d_error, m.sm_count, st);
-  tp_allgather_bf16(m, s.tp_send, s.tp_recv, size_t(n_rows) * slice, st);
-  launch_gather_logits(s.tp_recv, n_rows, slice, width, out, s.logit_stride, st);
+  const bf16 *norm_w = normed ? nullptr : m.final_norm;
+  const int main_end = std::min(c1, pr.n_main);
+  const bf16 *head = m.lm_head + size_t(pr.row0) * H;
+  if (main_end > c0) {
+    if (normed) {
+      const int n_even = pr.n_main & ~1, g_end = std::min(main_end, n_even);
+      if (g_end > c0) launch_gemm(in, n_rows, H, head + size_t(c0) * H, g_end - c0, out, stride, kEpiStore, st);
+      if (n_even < main_end)
+        launch_gemv(head + size_t(n_even) * H, 1, H, in, in_stride, nullptr, m.d.eps, out + (n_even - c0), stride,
+                    kEpiStore, n_rows, s.d_error, m.sm_count, st);
+    } else {
+      launch_gemv(head + size_t(c0) * H, main_end - c0, H, in, in_stride, norm_w, m.d.eps, out, stride, kEpiStore,
+                  n_rows, s.d_error, m.sm_count, st);
+    }
+  }
+  if (pr.extra >= 0 && c0 <= pr.n_main && pr.n_main < c1)
+    launch_gemv(m.lm_head + size_t(pr.extra) * H, 1, H, in, in_stride, norm_w, m.d.eps, out + (pr.n_main - c0),
+                stride, kEpiStore, n_rows, s.d_error, m.sm_count, st);
 }
 
-// A linear whose input is split across tensor-parallel ranks (O over heads, down over FFN
-// columns), added to the residual x: on one GPU the residual epilogue; under tensor
-// parallelism the rank-partial FP32 product, all-reduced, rounded once and added.
-template <class Linear>
-static void linear_residual(const Model &m, Session &s, bf16 *x, int n_rows, Linear &&linear) {
-  if (m.tp_world == 1) {
-    linear(x, kEpiResidual);
+// LM head over the phase columns for `n_rows` input rows into logits rows (stride
+// logit_stride). Under tensor parallelism rank r projects columns [r*slice, (r+1)*slice)
+// into its send block, the blocks are all-gathered and laid out as whole logits rows on
+// every rank.
+static void project(const Model &m, Session &s, const bf16 *in, int in_stride, bool normed, int n_rows, int phase,
+                    bf16 *out) {
+  const int width = phase_rows(m.d, phase).width();
+  if (m.tp_world == 1) return project_cols(m, s, in, in_stride, normed, n_rows, phase, 0, width, out, s.logit_stride);
+  const int slice = tp_head_slice(width, m.tp_world);
+  const int a = std::min(width, m.tp_rank * slice), b = std::min(width, a + slice);
+  project_cols(m, s, in, in_stride, normed, n_rows, phase, a, b, s.tp_send, slice);
+  tp_allgather_bf16(m, s.tp_send, s.tp_recv, size_t(n_rows) * slice, s.stream);
+  launch_tp_unpack(s.tp_recv, m.tp_world, n_rows, slice, width, out, s.logit_stride, s.stream);
+}
+
+// Under tensor parallelism: every rank's block of columns [k*n, k*n + n) of the activation
+// rows buf ([n_rows][stride]) into every rank's buf. One row whose blocks tile it is
+// gathered in place; otherwise through the pack / all-gather / unpack steps.
+static void tp_gather(const Model &m, Session &s, bf16 *buf, int n_rows, int stride, int n) {
+  if (m.tp_world == 1) return;
+  const int W = m.tp_world;
+  if (n_rows == 1 && stride == W * n) {
+    tp_allgather_bf16(m, buf + size_t(m.tp_rank) * n, buf, size_t(n), s.stream);
     return;
   }
-  const int H = m.d.hidden;
-  linear(reinterpret_cast<bf16 *>(s.tp_part), kEpiF32);
-  tp_allreduce_f32(m, s.tp_part, size_t(n_rows) * H, s.stream);
-  launch_residual_f32(x, s.tp_part, n_rows, H, s.stream);
+  launch_tp_pack(buf, stride, m.tp_rank * n, n, n_rows, s.tp_send, s.stream);
+  tp_allgather_bf16(m, s.tp_send, s.tp_recv, size_t(n_rows) * n, s.stream);
+  launch_tp_unpack(s.tp_recv, W, n_rows, n, W * n, buf, stride, s.stream);
 }
 
-// LM head over the phase rows for `n_rows` input rows (norm fused), into logits rows.
-static void project(const Model &m, Session &s, const bf16 *in, int in_stride, int n_rows, int phase,
-                    bf16 *out) {
-  if (m.tp_world > 1) return project_tp(m, s, in, in_stride, m.final_norm, n_rows, phase, out);
-  const PhaseRows pr = phase_rows(m.d, phase);
-  launch_gemv(m.lm_head + size_t(pr.row0) * m.d.hidden, pr.n_main, m.d.hidden, in, in_stride, m.final_norm,
-              m.d.eps, out, s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, s.stream);
-  if (pr.extra >= 0)
-    launch_gemv(m.lm_head + size_t(pr.extra) * m.d.hidden, 1, m.d.hidden, in, in_stride, m.final_norm, m.d.eps,
-                out + pr.n_main, s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, s.stream);
+// The shapes of one layer's linears on this rank (the whole layer on one GPU): hidden
+// width, query width of the model / of this rank, FFN width of the model / of this rank,
+// and this rank's block of hidden rows of O and down.
+struct LayerShape {
+  int H, Qf, Ql, Ff, Fl, Hs, h0;
+};
+static LayerShape layer_shape(const Model &m) {
+  return {m.d.hidden, m.full.qdim(), m.d.qdim(), m.full.ffn, m.d.ffn, m.tp.h_rows, m.tp.h_row0};
 }
 
 void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int chunk,
@@ -227,12 +251,15 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
   const int H = d.hidden, QKV = d.qkv_rows();
   // Linears on the tcgen05 tensor-core GEMM where the shape allows (K % 64, N % 128);
   // otherwise the mma.sync GEMM.
+  // Linears are split by output rows under tensor parallelism: the K split follows the
+  // whole model's N (tp_world x this rank's).
   auto gemm = [&](const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epi) {
     if (gemm_tc_supported(A, M, K, W, N, C, ldc))
-      launch_gemm_tc(A, M, K, W, N, C, ldc, epi, s.d_error, s.gemm_ws, s.gemm_ws_floats, st);
+      launch_gemm_tc(A, M, K, W, N, C, ldc, epi, s.d_error, s.gemm_ws, s.gemm_ws_floats, st, N * m.tp_world);
     else
       launch_gemm(A, M, K, W, N, C, ldc, epi, st);
   };
+  const LayerShape ls = layer_shape(m);
   for (int c0 = 0; c0 < n; c0 += chunk) {
     if (cancel && cancel(cancel_ctx)) throw Error("InterruptedError", "Cancelled during prefill");
     const int T = std::min(chunk, n - c0), start = start0 + c0;
@@ -244,13 +271,17 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
       gemm(s.ph, T, H, w.qkv, QKV, s.pqkv, QKV, kEpiStore);
       launch_qkv_post_prefill(m, s, l, row, start, T, st);
       launch_attn_prefill(m, s, l, row, start, T, st);
-      linear_residual(m, s, s.px, T, [&](bf16 *out, int epi) { gemm(s.pattn, T, d.qdim(), w.o, H, out, H, epi); });
+      tp_gather(m, s, s.pattn, T, ls.Qf, ls.Ql);
+      gemm(s.pattn, T, ls.Qf, w.o, ls.Hs, s.px + ls.h0, H, kEpiResidual);
+      tp_gather(m, s, s.px, T, H, ls.Hs);
       launch_rmsnorm_rows(s.px, w.ln2, T, H, d.eps, s.ph, st);
-      gemm(s.ph, T, H, w.gu, 2 * d.ffn, s.pmlp, d.ffn, kEpiSwiGLU);
-      linear_residual(m, s, s.px, T, [&](bf16 *out, int epi) { gemm(s.pmlp, T, d.ffn, w.down, H, out, H, epi); });
+      gemm(s.ph, T, H, w.gu, 2 * ls.Fl, s.pmlp + size_t(m.tp_rank) * ls.Fl, ls.Ff, kEpiSwiGLU);
+      tp_gather(m, s, s.pmlp, T, ls.Ff, ls.Fl);
+      gemm(s.pmlp, T, ls.Ff, w.down, ls.Hs, s.px + ls.h0, H, kEpiResidual);
+      tp_gather(m, s, s.px, T, H, ls.Hs);
     }
     if (c0 + T == n)
-      project(m, s, s.px + size_t(T - 1) * H, H, 1, phase, s.logits + size_t(row) * s.logit_stride);
+      project(m, s, s.px + size_t(T - 1) * H, H, false, 1, phase, s.logits + size_t(row) * s.logit_stride);
     YAR_CUDA(cudaStreamSynchronize(st));
   }
   int err = 0;
@@ -294,38 +325,34 @@ static void decode_forward_batched(Session &s, int n_rows, int phase) {
   const int H = d.hidden;
   auto gemm = [&](const bf16 *A, int K, const bf16 *W, int N, bf16 *C, int ldc, int epi) {
     if (gemm_tc_supported(A, n_rows, K, W, N, C, ldc))
-      launch_gemm_tc(A, n_rows, K, W, N, C, ldc, epi, s.d_error, s.gemm_ws, s.gemm_ws_floats, st);
+      launch_gemm_tc(A, n_rows, K, W, N, C, ldc, epi, s.d_error, s.gemm_ws, s.gemm_ws_floats, st, N * m.tp_world);
     else
       launch_gemm(A, n_rows, K, W, N, C, ldc, epi, st);
   };
   // About two waves of attention CTAs (5 resident per SM): fewer, longer splits per row
-  // than the one-row path, so each CTA streams several chunks.
-  const int splits = std::max(1, (2 * 5 * m.sm_count + n_rows * d.kv_heads - 1) / (n_rows * d.kv_heads));
+  // than the one-row path, so each CTA streams several chunks. (Counted with the whole
+  // model's KV heads, so tensor-parallel ranks split each head's positions the same way.)
+  const int kvh = m.full.kv_heads;
+  const int splits = std::max(1, (2 * 5 * m.sm_count + n_rows * kvh - 1) / (n_rows * kvh));
+  const LayerShape ls = layer_shape(m);
   launch_embed_rows(m, s, n_rows, st);
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
     launch_rmsnorm_rows(s.x, w.ln1, n_rows, H, d.eps, s.ph, st);
     gemm(s.ph, H, w.qkv, d.qkv_rows(), s.qkv, d.qkv_rows(), kEpiStore);
     launch_attn_decode(m, s, l, n_rows, st, splits);
-    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) { gemm(s.attn, d.qdim(), w.o, H, out, H, epi); });
+    tp_gather(m, s, s.attn, n_rows, ls.Qf, ls.Ql);
+    gemm(s.attn, ls.Qf, w.o, ls.Hs, s.x + ls.h0, H, kEpiResidual);
+    tp_gather(m, s, s.x, n_rows, H, ls.Hs);
     launch_rmsnorm_rows(s.x, w.ln2, n_rows, H, d.eps, s.ph, st);
-    gemm(s.ph, H, w.gu, 2 * d.ffn, s.mlp, d.ffn, kEpiSwiGLU);
-    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) { gemm(s.mlp, d.ffn, w.down, H, out, H, epi); });
+    gemm(s.ph, H, w.gu, 2 * ls.Fl, s.mlp + size_t(m.tp_rank) * ls.Fl, ls.Ff, kEpiSwiGLU);
+    tp_gather(m, s, s.mlp, n_rows, ls.Ff, ls.Fl);
+    gemm(s.mlp, ls.Ff, w.down, ls.Hs, s.x + ls.h0, H, kEpiResidual);
+    tp_gather(m, s, s.x, n_rows, H, ls.Hs);
   }
+  // Head: GEMM over the normalized rows (odd last phase row and ABC extra row as GEMVs).
   launch_rmsnorm_rows(s.x, m.final_norm, n_rows, H, d.eps, s.ph, st);
-  if (m.tp_world > 1) return project_tp(m, s, s.ph, H, nullptr, n_rows, phase, s.logits);
-  // Head: an even number of rows as a GEMM; an odd last phase row and the ABC extra row as
-  // GEMVs over the normalized rows.
-  const PhaseRows pr = phase_rows(d, phase);
-  const int n_even = pr.n_main & ~1;
-  const bf16 *head = m.lm_head + size_t(pr.row0) * H;
-  launch_gemm(s.ph, n_rows, H, head, n_even, s.logits, s.logit_stride, kEpiStore, st);
-  if (n_even < pr.n_main)
-    launch_gemv(head + size_t(n_even) * H, 1, H, s.ph, H, nullptr, d.eps, s.logits + n_even, s.logit_stride,
-                kEpiStore, n_rows, s.d_error, m.sm_count, st);
-  if (pr.extra >= 0)
-    launch_gemv(m.lm_head + size_t(pr.extra) * H, 1, H, s.ph, H, nullptr, d.eps, s.logits + pr.n_main,
-                s.logit_stride, kEpiStore, n_rows, s.d_error, m.sm_count, st);
+  project(m, s, s.ph, H, true, n_rows, phase, s.logits);
 }
 
 static void decode_forward(Session &s, int n_rows, int phase) {
@@ -340,24 +367,26 @@ static void decode_forward(Session &s, int n_rows, int phase) {
     decode_forward_batched(s, n_rows, phase);
     return;
   }
+  const LayerShape ls = layer_shape(m);
+  const int H = d.hidden;
   launch_embed_rows(m, s, n_rows, st);
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
-    launch_gemv(w.qkv, d.qkv_rows(), d.hidden, s.x, d.hidden, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows,
-                s.d_error, m.sm_count, st);
-    launch_attn_decode(m, s, l, n_rows, st);
-    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) {
-      launch_gemv(w.o, d.hidden, d.qdim(), s.attn, d.qdim(), nullptr, d.eps, out, d.hidden, epi, n_rows, s.d_error,
-                  m.sm_count, st);
-    });
-    launch_gemv(w.gu, 2 * d.ffn, d.hidden, s.x, d.hidden, w.ln2, d.eps, s.mlp, d.ffn, kEpiSwiGLU, n_rows, s.d_error,
+    launch_gemv(w.qkv, d.qkv_rows(), H, s.x, H, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows, s.d_error,
                 m.sm_count, st);
-    linear_residual(m, s, s.x, n_rows, [&](bf16 *out, int epi) {
-      launch_gemv(w.down, d.hidden, d.ffn, s.mlp, d.ffn, nullptr, d.eps, out, d.hidden, epi, n_rows, s.d_error,
-                  m.sm_count, st);
-    });
+    launch_attn_decode(m, s, l, n_rows, st);
+    tp_gather(m, s, s.attn, n_rows, ls.Qf, ls.Ql);
+    launch_gemv(w.o, ls.Hs, ls.Qf, s.attn, ls.Qf, nullptr, d.eps, s.x + ls.h0, H, kEpiResidual, n_rows, s.d_error,
+                m.sm_count, st);
+    tp_gather(m, s, s.x, n_rows, H, ls.Hs);
+    launch_gemv(w.gu, 2 * ls.Fl, H, s.x, H, w.ln2, d.eps, s.mlp + size_t(m.tp_rank) * ls.Fl, ls.Ff, kEpiSwiGLU,
+                n_rows, s.d_error, m.sm_count, st);
+    tp_gather(m, s, s.mlp, n_rows, ls.Ff, ls.Fl);
+    launch_gemv(w.down, ls.Hs, ls.Ff, s.mlp, ls.Ff, nullptr, d.eps, s.x + ls.h0, H, kEpiResidual, n_rows, s.d_error,
+                m.sm_count, st);
+    tp_gather(m, s, s.x, n_rows, H, ls.Hs);
   }
-  project(m, s, s.x, d.hidden, n_rows, phase, s.logits);
+  project(m, s, s.x, H, false, n_rows, phase, s.logits);
 }
 
 void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int phase) {

@@ -39,12 +39,13 @@ struct Dims {
   int qkv_rows() const { return qdim() + 2 * kvdim(); }
 };
 
-// Device weights of one decoder layer in the engine layout.
+// Device weights of one decoder layer in the engine layout (under tensor parallelism the
+// rank's rows of each, with the whole model's input width).
 struct LayerWeights {
   const bf16 *qkv;   // [q + k + v rows][hidden]: q_proj, k_proj, v_proj rows stacked
-  const bf16 *o;     // [hidden][qdim]
+  const bf16 *o;     // [hidden rows][qdim of the whole model]
   const bf16 *gu;    // [2*ffn][hidden]: row 2j = gate_proj row j, row 2j+1 = up_proj row j
-  const bf16 *down;  // [hidden][ffn]
+  const bf16 *down;  // [hidden rows][ffn of the whole model]
   const bf16 *ln1, *ln2, *qn, *kn;
 };
 
@@ -58,30 +59,37 @@ struct Model {
   LayerWeights *d_layers = nullptr;  // device copy of `layers` (persistent decode kernel)
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
   // Tensor parallelism: this rank's share of the heads, KV heads and FFN columns is in `d`
-  // (the whole model's dims in `full`); `tp_comm` is the NCCL communicator (null: one GPU).
+  // (the whole model's dims in `full`, the rank's rows in `tp`); `tp_comm` is the NCCL
+  // communicator (null: one GPU).
   Dims full;
   int tp_rank = 0, tp_world = 1;
   void *tp_comm = nullptr;
+  struct TpRows {
+    int q_row0 = 0, q_rows = 0, kv_row0 = 0, kv_rows = 0, ffn_row0 = 0, ffn_rows = 0, h_row0 = 0, h_rows = 0;
+  } tp;
 };
+using TpPlan = Model::TpRows;
 
-// Tensor-parallel share of one rank, in rows/columns of the whole model's tensors: query
-// rows [q_row0, +q_rows) of q_proj (= columns of o_proj), rows [kv_row0, +kv_rows) of
-// k_proj and v_proj, rows [ffn_row0, +ffn_rows) of gate_proj and up_proj (= columns of
-// down_proj). KV heads are split into equal groups and each keeps its query heads.
-struct TpPlan {
-  int q_row0 = 0, q_rows = 0, kv_row0 = 0, kv_rows = 0, ffn_row0 = 0, ffn_rows = 0;
-};
+// Tensor-parallel share of one rank, in rows of the whole model's tensors. Every linear is
+// split by output rows and keeps its whole input width: query rows [q_row0, +q_rows) of
+// q_proj, rows [kv_row0, +kv_rows) of k_proj and v_proj (KV heads in equal groups, each
+// with its query heads), rows [ffn_row0, +ffn_rows) of gate_proj and up_proj, and rows
+// [h_row0, +h_rows) of o_proj and down_proj. Each rank's outputs (attention heads, hidden
+// rows, FFN columns) are all-gathered after their operation, so every output value is
+// computed by one rank exactly as on one GPU.
 TpPlan tp_plan(const Dims &full, int rank, int world);
 
 // Tensor-parallel exchange steps (tp.cpp) and the element-wise kernels around them.
 void tp_unique_id(uint8_t *out128);
 void tp_init(Model &m, int rank, int world, const uint8_t *id128);
 void tp_destroy(Model &m);
-void tp_allreduce_f32(const Model &m, float *buf, size_t n, cudaStream_t st);
 void tp_allgather_bf16(const Model &m, const bf16 *send, bf16 *recv, size_t n, cudaStream_t st);
-void launch_residual_f32(bf16 *x, const float *sum, int n_rows, int H, cudaStream_t st);
-void launch_gather_logits(const bf16 *recv, int n_rows, int slice, int width, bf16 *logits, int logit_stride,
-                          cudaStream_t st);
+// send[r][j] = buf[r * stride + col0 + j] for r < n_rows, j < n.
+void launch_tp_pack(const bf16 *buf, int stride, int col0, int n, int n_rows, bf16 *send, cudaStream_t st);
+// buf[r * stride + k * n + j] = recv[(k * n_rows + r) * n + j] for every rank k, where
+// k * n + j < width.
+void launch_tp_unpack(const bf16 *recv, int world, int n_rows, int n, int width, bf16 *buf, int stride,
+                      cudaStream_t st);
 // LM-head columns per rank under tensor parallelism: the phase width split evenly, rounded
 // up to 8 columns.
 inline int tp_head_slice(int width, int world) { return ((width + world - 1) / world + 7) / 8 * 8; }
@@ -129,9 +137,11 @@ void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int
                  cudaStream_t st);
 // Prefill linears on tcgen05 (kernels_gemm_tc.cu); `error` receives expired-wait flags.
 bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const bf16 *C, int ldc);
-// `ws` (ws_floats FP32 values, may be null) lets small-M shapes split K across CTAs.
+// `ws` (ws_floats FP32 values, may be null) lets small-M shapes split K across CTAs; the
+// split count is chosen for `split_n` columns (0: N), so a tensor-parallel rank's block of
+// N / world columns splits K, and adds its partial sums, as the whole N does on one GPU.
 void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
-                    float *ws, size_t ws_floats, cudaStream_t st);
+                    float *ws, size_t ws_floats, cudaStream_t st, int split_n = 0);
 void configure_gemm_tc_kernels();
 void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
                              cudaStream_t st);
@@ -150,10 +160,7 @@ void configure_sampler_kernels();
 bool persistent_supported(const Model &m, int n_rows);
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
 
-// kEpiF32: the FP32 accumulator itself (the output pointer is a float array and its
-// stride counts floats) — a tensor-parallel rank's partial sum of O or down, all-reduced
-// before the one BF16 rounding and residual add.
-enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3 };
+enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
 
 struct Session {
   Model *m = nullptr;
@@ -209,10 +216,8 @@ struct Session {
   size_t gemm_ws_floats = 0;
   int prefetch_stages = 6;  // persistent kernel: L2 prefetch distance beyond the ring
   unsigned long long *d_trace = nullptr;  // persistent-kernel timeline (when enabled)
-  // Tensor parallelism: the rank-partial FP32 sums of O and down
-  // ([max(prefill_chunk, max_rows)][hidden]) and the LM-head slices before
-  // ([max_rows][slice]) and after ([world][max_rows][slice]) the all-gather.
-  float *tp_part = nullptr;
+  // Tensor parallelism: a rank's block of rows before ([rows][n]) and after
+  // ([world][rows][n]) the all-gather.
   bf16 *tp_send = nullptr, *tp_recv = nullptr;
   size_t trace_elems = 0;
 };

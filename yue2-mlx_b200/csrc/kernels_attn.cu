@@ -93,7 +93,9 @@ void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaS
   p.sin_tab = m.rope_sin;
   p.part = s.attn_part;
   p.count = s.attn_count;
-  p.out = s.attn;
+  // Under tensor parallelism this rank's heads sit at their place in the whole model's rows.
+  p.out = s.attn + m.tp.q_row0;
+  p.out_stride = m.full.qdim();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.d.kv_heads, p.max_splits, n_rows);
   cfg.blockDim = dim3(kAttnThreads);
@@ -192,7 +194,8 @@ struct PrefillAttnParams {
   bf16 *pool;
   const int *ptab;
   const bf16 *q;  // [T][heads][D]
-  bf16 *out;      // [T][qdim]
+  bf16 *out;      // token t, head h at out[t * out_stride + h * D]
+  int out_stride;
 };
 
 template <int D>
@@ -305,7 +308,7 @@ __global__ void __launch_bounds__(256) k_attn_prefill(PrefillAttnParams p) {
     const float inv = 1.0f / l[i];
 #pragma unroll
     for (int dd = 0; dd < DT; ++dd)
-      p.out[size_t(qi) * g.qdim + h * D + kj * DT + dd] = f2bf(o[i][dd] * inv);
+      p.out[size_t(qi) * p.out_stride + h * D + kj * DT + dd] = f2bf(o[i][dd] * inv);
   }
 }
 
@@ -328,7 +331,8 @@ void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int sta
   p.pool = s.kv;
   p.ptab = s.d_page_table + size_t(row) * s.pages_per_row;
   p.q = s.pq;
-  p.out = s.pattn;
+  p.out = s.pattn + m.tp.q_row0;
+  p.out_stride = m.full.qdim();
   const int D = m.d.head_dim;
   const size_t smem = prefill_attn_smem(D);
   dim3 grid((T + 63) / 64, m.d.heads);

@@ -124,10 +124,6 @@ __global__ void __launch_bounds__(256) k_gemm(const bf16 *__restrict__ A, int M,
           bf16 *o = C + size_t(r) * ldc + c;
           o[0] = f2bf(bf2f(o[0]) + rbf(v0));
           o[1] = f2bf(bf2f(o[1]) + rbf(v1));
-        } else if (EPI == kEpiF32) {
-          float *o = reinterpret_cast<float *>(C) + size_t(r) * ldc + c;
-          o[0] = v0;
-          o[1] = v1;
         } else {
           bf16 *o = C + size_t(r) * ldc + c;
           o[0] = f2bf(v0);
@@ -151,7 +147,6 @@ void configure_gemm_kernels() {
   YAR_CUDA(cudaFuncSetAttribute(k_gemm<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   YAR_CUDA(cudaFuncSetAttribute(k_gemm<kEpiResidual>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   YAR_CUDA(cudaFuncSetAttribute(k_gemm<kEpiSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  YAR_CUDA(cudaFuncSetAttribute(k_gemm<kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
 }
 
 void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue,
@@ -159,7 +154,6 @@ void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int
   if (K % 8 != 0 || N % 2 != 0) throw Error("ValueError", "GEMM needs K % 8 == 0 and even N");
   if (epilogue == kEpiSwiGLU) return gemm_launch<kEpiSwiGLU>(A, M, K, W, N, C, ldc, st);
   if (epilogue == kEpiResidual) return gemm_launch<kEpiResidual>(A, M, K, W, N, C, ldc, st);
-  if (epilogue == kEpiF32) return gemm_launch<kEpiF32>(A, M, K, W, N, C, ldc, st);
   return gemm_launch<kEpiStore>(A, M, K, W, N, C, ldc, st);
 }
 

@@ -238,11 +238,7 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const float *ws, int spli
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = s == 0 ? w[j] : v[j] + w[j];
   }
-  if (EPI == kEpiF32) {
-    float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(C) + size_t(row) * ldc + col);
-    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-  } else if (EPI == kEpiSwiGLU) {
+  if (EPI == kEpiSwiGLU) {
     uint32_t o[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -319,19 +315,17 @@ bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const 
 }
 
 void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
-                    float *ws, size_t ws_floats, cudaStream_t st) {
+                    float *ws, size_t ws_floats, cudaStream_t st, int split_n) {
   const CUtensorMap ma = kmajor_map(A, M, K, kTcBM), mb = kmajor_map(W, N, K, kTcBN);
   // Split K across CTAs while the tile grid leaves SMs idle (small M: batched decode).
-  const int tiles = (N / kTcBN) * ((M + kTcBM - 1) / kTcBM), KB = K / kTcBK;
+  const int NS = split_n > 0 ? split_n : N;
+  if (NS < N) throw Error("ValueError", "split_n below N");
+  const int tiles = (NS / kTcBN) * ((M + kTcBM - 1) / kTcBM), KB = K / kTcBK;
   int splits = 1;
   while (ws && splits < 8 && tiles * splits < 120 && KB % (splits * 2) == 0 &&
-         size_t(splits * 2) * M * N <= ws_floats)
+         size_t(splits * 2) * M * NS <= ws_floats)
     splits *= 2;
-  // FP32 output: one split writes its accumulators straight into C (the split-K partial
-  // store with C as the workspace); several are summed by the reduction kernel.
-  if (epilogue == kEpiF32 && ldc != N) throw Error("ValueError", "FP32 GEMM output must be dense (ldc == N)");
-  float *partials = splits > 1 ? ws : epilogue == kEpiF32 ? reinterpret_cast<float *>(C) : nullptr;
-  TcParams p{C, M, N, K, ldc, error, partials, KB / splits};
+  TcParams p{C, M, N, K, ldc, error, splits > 1 ? ws : nullptr, KB / splits};
   const dim3 grid(N / kTcBN, (M + kTcBM - 1) / kTcBM, splits);
   if (epilogue == kEpiSwiGLU)
     k_gemm_tc<kEpiSwiGLU><<<grid, kTcThreads, kTcSmem, st>>>(ma, mb, p);
@@ -343,9 +337,7 @@ void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, 
   if (splits > 1) {
     const long long threads = (long long)M * (N / 8);
     const unsigned blocks = unsigned((threads + 255) / 256);
-    if (epilogue == kEpiF32)
-      k_splitk_reduce<kEpiF32><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
-    else if (epilogue == kEpiSwiGLU)
+    if (epilogue == kEpiSwiGLU)
       k_splitk_reduce<kEpiSwiGLU><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
     else if (epilogue == kEpiResidual)
       k_splitk_reduce<kEpiResidual><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);

@@ -182,9 +182,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(GemvParams p) {
             if (rr == r && bb == b) v = acc[rr][bb];
         if (row < p.N) {
           bf16 *o = p.out + size_t(b) * p.out_stride + row;
-          if (EPI == kEpiF32)
-            reinterpret_cast<float *>(p.out)[size_t(b) * p.out_stride + row] = v;
-          else if (EPI == kEpiResidual)
+          if (EPI == kEpiResidual)
             *o = f2bf(bf2f(*o) + rbf(v));
           else
             *o = f2bf(v);
@@ -403,8 +401,6 @@ static void gemv_configure_nb() {
   YAR_CUDA(cudaFuncSetAttribute(k_gemv<NB, 2, kEpiResidual>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   YAR_CUDA(cudaFuncSetAttribute(k_gemv<NB, 1, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   YAR_CUDA(cudaFuncSetAttribute(k_gemv<NB, 2, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  YAR_CUDA(cudaFuncSetAttribute(k_gemv<NB, 1, kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  YAR_CUDA(cudaFuncSetAttribute(k_gemv<NB, 2, kEpiF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   if constexpr (NB <= 2) {
     gemv_stream_configure<NB, 1>();
     gemv_stream_configure<NB, 3>();
@@ -428,16 +424,13 @@ template <int NB>
 static void gemv_dispatch_epi(const GemvParams &p, int epi, int sm_count, cudaStream_t st) {
   // One or two rows (bs1, a CFG pair): the streaming kernel; more rows keep the
   // register-lighter kernel below (the streaming kernel would spill).
-  // The FP32-partial epilogue (tensor parallelism) only exists in the kernel below.
   if constexpr (NB <= 2) {
-    if (epi != kEpiF32 && p.K == 2048) return gemv_stream_dispatch<NB, 1>(p, epi, sm_count, st);
-    if (epi != kEpiF32 && p.K == 6144) return gemv_stream_dispatch<NB, 3>(p, epi, sm_count, st);
+    if (p.K == 2048) return gemv_stream_dispatch<NB, 1>(p, epi, sm_count, st);
+    if (p.K == 6144) return gemv_stream_dispatch<NB, 3>(p, epi, sm_count, st);
   }
   if (epi == kEpiSwiGLU) return gemv_launch<NB, 2, kEpiSwiGLU>(p, sm_count, st);
   // Two rows per warp when there are enough rows to fill the machine, else one.
   const bool wide = p.N / 2 >= 2 * sm_count * kGemvWarps;
-  if (epi == kEpiF32)
-    return wide ? gemv_launch<NB, 2, kEpiF32>(p, sm_count, st) : gemv_launch<NB, 1, kEpiF32>(p, sm_count, st);
   if (epi == kEpiResidual)
     return wide ? gemv_launch<NB, 2, kEpiResidual>(p, sm_count, st)
                 : gemv_launch<NB, 1, kEpiResidual>(p, sm_count, st);
@@ -453,7 +446,7 @@ void launch_gemv(const bf16 *W, int N, int K, const bf16 *in, int in_stride, con
                  float eps, bf16 *out, int out_stride, int epilogue, int n_rows,
                  int *error, int sm_count, cudaStream_t st) {
   if (K % 8 != 0) throw Error("ValueError", "GEMV inner dimension must be a multiple of 8");
-  if (error && epilogue != kEpiF32 && launch_gemv_tma(W, N, K, in, in_stride, norm_w, eps, out, out_stride, epilogue, n_rows, error,
+  if (error && launch_gemv_tma(W, N, K, in, in_stride, norm_w, eps, out, out_stride, epilogue, n_rows, error,
                                sm_count, st))
     return;
   // Rows beyond 8 are processed in groups of up to 8 (the weights are re-streamed).

@@ -698,6 +698,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   a.part = s.attn_part;
   a.count = s.attn_count;
   a.out = s.attn;
+  a.out_stride = m.d.qdim();
   p.token = s.d_token;
   p.pos = s.d_pos;
   p.cur_pos = s.d_cur_pos;

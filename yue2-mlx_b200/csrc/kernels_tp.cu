@@ -1,47 +1,42 @@
-// kernels_tp.cu — the two element-wise steps around the tensor-parallel exchanges.
+// kernels_tp.cu — the layout steps around the tensor-parallel all-gathers.
 //
-//   k_residual_f32   x[r][i] = bf16(x[r][i] + bf16(sum[r][i])): the all-reduced FP32 sum
-//                    of O (or down) rounded once and added to the BF16 residual, the same
-//                    rounding points as the single-GPU residual epilogue
-//                    (native/src/ar.cpp:292-298).
-//   k_gather_logits  the all-gathered head slices, laid out [rank][row][slice], into the
-//                    [row][logit_stride] logits rows the sampler reads.
+// Each rank computes a block of columns of an activation ([rows][stride], block k at
+// columns [k*n, k*n + n)); the all-gather moves whole contiguous buffers, laid out
+// [rank][rows][n]. k_tp_pack copies this rank's block out of the activation rows;
+// k_tp_unpack writes every rank's block back into them (for the LM head, the phase
+// columns of the logits rows the sampler reads). With one row the blocks are contiguous
+// already and the engine gathers in place, without either kernel.
 #include "common.cuh"
 
 namespace yar {
 
-__global__ void __launch_bounds__(256) k_residual_f32(bf16 *x, const float *sum, int n) {
-  const int i = (blockIdx.x * 256 + threadIdx.x) * 4;
-  if (i >= n) return;
-  const float4 s = *reinterpret_cast<const float4 *>(sum + i);
-  uint2 *xp = reinterpret_cast<uint2 *>(x + i);
-  const uint2 old = *xp;
-  const float a = bf_lo(old.x) + rbf(s.x), b = bf_hi(old.x) + rbf(s.y);
-  const float c = bf_lo(old.y) + rbf(s.z), d = bf_hi(old.y) + rbf(s.w);
-  *xp = make_uint2((__float_as_uint(rbf(a)) >> 16) | (__float_as_uint(rbf(b)) & 0xFFFF0000u),
-                   (__float_as_uint(rbf(c)) >> 16) | (__float_as_uint(rbf(d)) & 0xFFFF0000u));
+__global__ void __launch_bounds__(256) k_tp_pack(const bf16 *buf, int stride, int col0, int n, int n_rows,
+                                                 bf16 *send) {
+  const int r = blockIdx.y;
+  for (int j = blockIdx.x * 256 + threadIdx.x; j < n; j += gridDim.x * 256)
+    send[size_t(r) * n + j] = buf[size_t(r) * stride + col0 + j];
 }
 
-void launch_residual_f32(bf16 *x, const float *sum, int n_rows, int H, cudaStream_t st) {
-  if (H % 4) throw Error("ValueError", "residual width must be a multiple of 4");
-  const int n = n_rows * H;
-  k_residual_f32<<<(n / 4 + 255) / 256, 256, 0, st>>>(x, sum, n);
-  YAR_CUDA(cudaGetLastError());
-}
-
-__global__ void __launch_bounds__(256) k_gather_logits(const bf16 *recv, int n_rows, int slice, int width,
-                                                       bf16 *logits, int logit_stride) {
-  const int row = blockIdx.y;
-  for (int j = blockIdx.x * 256 + threadIdx.x; j < width; j += gridDim.x * 256) {
-    const int rank = j / slice, col = j - rank * slice;
-    logits[size_t(row) * logit_stride + j] = recv[(size_t(rank) * n_rows + row) * slice + col];
+__global__ void __launch_bounds__(256) k_tp_unpack(const bf16 *recv, int n_rows, int n, int width, bf16 *buf,
+                                                   int stride) {
+  const int r = blockIdx.y;
+  for (int c = blockIdx.x * 256 + threadIdx.x; c < width; c += gridDim.x * 256) {
+    const int k = c / n, j = c - k * n;
+    buf[size_t(r) * stride + c] = recv[(size_t(k) * n_rows + r) * n + j];
   }
 }
 
-void launch_gather_logits(const bf16 *recv, int n_rows, int slice, int width, bf16 *logits, int logit_stride,
-                          cudaStream_t st) {
-  const int blocks = (width + 255) / 256 < 148 ? (width + 255) / 256 : 148;
-  k_gather_logits<<<dim3(blocks, n_rows), 256, 0, st>>>(recv, n_rows, slice, width, logits, logit_stride);
+static int blocks_for(int n) { return (n + 255) / 256 < 148 ? (n + 255) / 256 : 148; }
+
+void launch_tp_pack(const bf16 *buf, int stride, int col0, int n, int n_rows, bf16 *send, cudaStream_t st) {
+  k_tp_pack<<<dim3(blocks_for(n), n_rows), 256, 0, st>>>(buf, stride, col0, n, n_rows, send);
+  YAR_CUDA(cudaGetLastError());
+}
+
+void launch_tp_unpack(const bf16 *recv, int world, int n_rows, int n, int width, bf16 *buf, int stride,
+                      cudaStream_t st) {
+  if (width > world * n) throw Error("ValueError", "unpack width exceeds the gathered blocks");
+  k_tp_unpack<<<dim3(blocks_for(width), n_rows), 256, 0, st>>>(recv, n_rows, n, width, buf, stride);
   YAR_CUDA(cudaGetLastError());
 }
 

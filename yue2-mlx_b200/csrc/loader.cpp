@@ -162,8 +162,9 @@ static std::map<std::string, TensorRec> read_safetensors_header(const std::strin
 
 TpPlan tp_plan(const Dims &d, int rank, int world) {
   if (world < 1 || rank < 0 || rank >= world) throw Error("ValueError", "tensor-parallel rank outside [0, world)");
-  if (d.kv_heads % world || d.ffn % world || (d.ffn / world) % 8)
-    throw Error("ValueError", "tensor-parallel world must divide num_key_value_heads and intermediate_size / 8");
+  if (d.kv_heads % world || d.ffn % world || (d.ffn / world) % 8 || d.hidden % (8 * world))
+    throw Error("ValueError",
+                "tensor-parallel world must divide num_key_value_heads, intermediate_size / 8 and hidden_size / 8");
   const int group = d.heads / d.kv_heads;  // query heads per KV head stay together
   TpPlan p;
   p.kv_rows = d.kv_heads / world * d.head_dim;
@@ -172,6 +173,8 @@ TpPlan tp_plan(const Dims &d, int rank, int world) {
   p.q_row0 = rank * p.q_rows;
   p.ffn_rows = d.ffn / world;
   p.ffn_row0 = rank * p.ffn_rows;
+  p.h_rows = d.hidden / world;
+  p.h_row0 = rank * p.h_rows;
   return p;
 }
 
@@ -230,7 +233,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
   dl.heads = plan.q_rows / d.head_dim;
   dl.kv_heads = plan.kv_rows / d.head_dim;
   dl.ffn = plan.ffn_rows;
-  const int Ql = dl.qdim(), KVl = dl.kvdim(), Fl = dl.ffn;
+  const int Ql = dl.qdim(), KVl = dl.kvdim(), Fl = dl.ffn, Hs = plan.h_rows;
 
   // Arena layout (256-byte aligned pieces).
   auto *m = new Model();
@@ -239,6 +242,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     m->full = d;
     m->tp_rank = tp_rank;
     m->tp_world = tp_world;
+    m->tp = plan;
     m->device = device;
     YAR_CUDA(cudaSetDevice(device));
     YAR_CUDA(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device));
@@ -261,9 +265,9 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     std::vector<LO> lo(d.layers);
     for (int i = 0; i < d.layers; ++i) {
       lo[i].qkv = take(size_t(Ql + 2 * KVl) * H * e2);
-      lo[i].o = take(size_t(H) * Ql * e2);
+      lo[i].o = take(size_t(Hs) * Q * e2);
       lo[i].gu = take(size_t(2 * Fl) * H * e2);
-      lo[i].down = take(size_t(H) * Fl * e2);
+      lo[i].down = take(size_t(Hs) * F * e2);
       lo[i].ln1 = take(H * e2);
       lo[i].ln2 = take(H * e2);
       lo[i].qn = take(D * e2);
@@ -358,14 +362,14 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     m->layers.resize(d.layers);
     for (int i = 0; i < d.layers; ++i) {
       const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
-      // Rank r: q rows of its heads, k/v rows of its KV heads, the matching O columns, its
-      // FFN block of gate/up rows and down columns (all of them when tp_world == 1).
+      // Rank r: q rows of its heads, k/v rows of its KV heads, its FFN block of gate/up rows,
+      // its hidden rows of O and down (all of them when tp_world == 1).
       upload_block(a + ".q_proj.weight", base + lo[i].qkv, plan.q_row0, Ql, 0, H);
       upload_block(a + ".k_proj.weight", base + lo[i].qkv + size_t(Ql) * H * e2, plan.kv_row0, KVl, 0, H);
       upload_block(a + ".v_proj.weight", base + lo[i].qkv + size_t(Ql + KVl) * H * e2, plan.kv_row0, KVl, 0, H);
-      upload_block(a + ".o_proj.weight", base + lo[i].o, 0, H, plan.q_row0, Ql);
+      upload_block(a + ".o_proj.weight", base + lo[i].o, plan.h_row0, Hs, 0, Q);
       upload_gate_up(n + ".mlp.gate_proj.weight", n + ".mlp.up_proj.weight", base + lo[i].gu, plan.ffn_row0, Fl);
-      upload_block(n + ".mlp.down_proj.weight", base + lo[i].down, 0, H, plan.ffn_row0, Fl);
+      upload_block(n + ".mlp.down_proj.weight", base + lo[i].down, plan.h_row0, Hs, 0, F);
       upload(n + ".input_layernorm.weight", base + lo[i].ln1);
       upload(n + ".post_attention_layernorm.weight", base + lo[i].ln2);
       upload(a + ".q_norm.weight", base + lo[i].qn);

@@ -1,13 +1,13 @@
 // tp.cpp — the tensor-parallel exchange steps over NCCL.
 //
-// Tensor parallelism (one process per GPU, `world` ranks): attention is split by KV-head
-// group and the MLP by FFN column block, so each decoder layer has two exchange steps —
-// the O projection and the down projection each produce a rank-partial FP32 sum that is
-// all-reduced, then rounded once to BF16 and added to the residual (the single rounding
-// point of model_ops::linear + residual, native/src/ar.cpp:20-28,292-298). The LM head
-// is split by vocabulary rows: each rank projects its slice and the BF16 logits are
-// all-gathered, so every rank samples the same token from identical logits with the same
-// Philox key and no further exchange.
+// Tensor parallelism (one process per GPU, `world` ranks) splits every linear of a layer
+// by output rows — q/k/v by KV-head group, O and down by hidden rows, gate/up by FFN
+// columns, the LM head by phase columns — and keeps its whole input width, so each output
+// value is computed by one rank with exactly the one-GPU arithmetic. After each operation
+// the ranks' output blocks are all-gathered (BF16), leaving every rank with the whole
+// activation: attention heads before O, the residual rows after O and after down, the FFN
+// activations before down, the logits before sampling. Every rank then samples the same
+// token from identical logits with the same Philox key.
 //
 // NCCL is opened at run time (dlopen of libnccl.so.2: the copy already in the process —
 // PyTorch's, when it is loaded — else the system one), so the library itself has no
@@ -29,8 +29,6 @@ struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
   ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
-  ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
-                             cudaStream_t) = nullptr;
   ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char *(*error_string)(ncclResult_t) = nullptr;
   std::string failure;
@@ -55,7 +53,6 @@ const NcclApi &nccl() {
     api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
-    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
   });
@@ -90,11 +87,6 @@ void tp_destroy(Model &m) {
   if (!m.tp_comm) return;
   nccl().comm_destroy(static_cast<ncclComm_t>(m.tp_comm));
   m.tp_comm = nullptr;
-}
-
-void tp_allreduce_f32(const Model &m, float *buf, size_t n, cudaStream_t st) {
-  check(nccl().all_reduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(m.tp_comm), st),
-        "ncclAllReduce");
 }
 
 void tp_allgather_bf16(const Model &m, const bf16 *send, bf16 *recv, size_t n, cudaStream_t st) {
