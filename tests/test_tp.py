@@ -201,11 +201,12 @@ def test_tensor_parallel_two_gpus_match_one_gpu(synth, tmp_path):
     res = json.load(open(out))
     assert res["dims_tp"]["heads"] == 8 and res["dims_tp"]["kv_heads"] == 4 and res["dims_tp"]["ffn"] == 3072
     print(json.dumps(res))
-    for key in ("full_rows1", "full_rows2", "semantic", "abc", "batch"):
+    for key in ("full_rows1", "full_rows2", "full_rows1_per_op", "full_rows2_per_op", "semantic", "abc", "batch"):
         assert res[key]["bit_identical"], (key, res[key])
         assert res[key].get("same_on_all_ranks", True), key
     assert res["semantic"]["width"] == 32769 and res["abc"]["width"] == 151644
     assert res["generate"]["ranks_agree"] and res["generate"]["equal_to_one_gpu"]
     assert res["generate"]["tensor_parallel"] == 2 and len(res["generate"]["tokens"]) == 24
+    assert res["generate"]["tp_exchange"] == "peer_stores"
     assert res["batch"]["ranks_agree"] and res["batch"]["equal_to_one_gpu"]
     assert res["batch"]["forward"] == "batched_tcgen05"

@@ -37,8 +37,9 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def forced_logits(model, prompt, forced, rows, phase, ctx):
+def forced_logits(model, prompt, forced, rows, phase, ctx, persistent=True):
     s = model.session(max_rows=2, max_ctx=ctx)
+    s.set_persistent(persistent)
     for r in range(rows):
         s.reset(r, ctx)
         s.prefill(r, prompt, phase=phase)
@@ -74,12 +75,15 @@ def main():
     res["dims_tp"], res["dims_one"] = tp.dims, one.dims
     rng = np.random.default_rng(5)
     prompt, forced = rng.integers(0, 4096, 300).tolist(), rng.integers(0, 4096, 12).tolist()
+    # Decode steps of one row and of a row pair: the persistent kernel (exchanging through
+    # stores into the peers' buffers) and the per-operation kernels (exchanging through NCCL).
     for rows in (1, 2):
-        a = forced_logits(tp, prompt, forced, rows, None, 400)
         b = forced_logits(one, prompt, forced, rows, None, 400)
-        res[f"full_rows{rows}"] = {"max_abs": float(np.abs(a - b).max()), "rel_l2": rel_l2(a, b),
-                                   "bit_identical": bool(np.array_equal(a, b)),
-                                   "same_on_all_ranks": len({x.tobytes() for x in gather(a)}) == 1}
+        for mode, persistent in (("", True), ("_per_op", False)):
+            a = forced_logits(tp, prompt, forced, rows, None, 400, persistent)
+            res[f"full_rows{rows}{mode}"] = {"max_abs": float(np.abs(a - b).max()), "rel_l2": rel_l2(a, b),
+                                             "bit_identical": bool(np.array_equal(a, b)),
+                                             "same_on_all_ranks": len({x.tobytes() for x in gather(a)}) == 1}
 
     smp = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50, min_tokens=24,
                max_tokens=24)
@@ -90,7 +94,8 @@ def main():
     toks_one, _, _ = s.generate(prompt, yar.Sampling(**smp), seed=7, phase=None)
     s.close()
     res["generate"] = {"tokens": toks, "ranks_agree": all(t == toks for t in gather(toks)),
-                       "equal_to_one_gpu": toks == toks_one, "tensor_parallel": timing["tensor_parallel"]}
+                       "equal_to_one_gpu": toks == toks_one, "tensor_parallel": timing["tensor_parallel"],
+                       "tp_exchange": timing["tp_exchange"]}
 
     n = 18
     prefixes = [rng.integers(0, 4096, int(rng.integers(20, 200))).tolist() for _ in range(n)]

@@ -88,6 +88,8 @@ struct DecodeAttnParams {
   int *count;    // [rows][kv_heads]
   bf16 *out;     // row r, head h at out[r * out_stride + h * D]
   int out_stride;
+  int out_ndst;  // tensor parallelism: also stored at out + out_dst[i] bytes (peer copies)
+  const long long *out_dst;
 };
 
 constexpr int kKvChunk = 64;  // positions per KV chunk
@@ -406,7 +408,10 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
       }
       M = Mb;
     }
-    p.out[size_t(row) * p.out_stride + (kvh * G + hd) * D + d] = f2bf(O * (1.0f / Ls));
+    bf16 *o = p.out + size_t(row) * p.out_stride + (kvh * G + hd) * D + d;
+    const bf16 v = f2bf(O * (1.0f / Ls));
+    *o = v;
+    for (int i = 0; i < p.out_ndst; ++i) *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(o) + p.out_dst[i]) = v;
   }
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
 }

@@ -64,18 +64,34 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
     YAR_CUDA(cudaMemset(s->d_error, 0, sizeof(int)));
     s->capacity.assign(max_rows, 0);
     s->pos.assign(max_rows, 0);
-    s->x = dmalloc<bf16>(size_t(max_rows) * d.hidden);
     s->qkv = dmalloc<bf16>(size_t(max_rows) * d.qkv_rows());
-    // Attention and FFN activations at the whole model's width: under tensor parallelism
-    // each rank writes its block and the all-gather fills in the others.
-    const Dims &f = m->full;
-    s->attn = dmalloc<bf16>(size_t(max_rows) * f.qdim());
-    s->mlp = dmalloc<bf16>(size_t(max_rows) * f.ffn);
     int widest = d.vocab;
     if (d.vocab == 184704) widest = std::max(phase_rows(d, kPhaseAbc).width(), phase_rows(d, kPhaseSemantic).width());
     s->logit_stride = (widest + 7) & ~7;
-    s->logits = dmalloc<bf16>(size_t(max_rows) * s->logit_stride);
-    YAR_CUDA(cudaMemset(s->logits, 0, size_t(max_rows) * s->logit_stride * sizeof(bf16)));
+    // The exchange region: residual rows, attention and FFN activations (at the whole
+    // model's width: under tensor parallelism each rank writes its block and the exchange
+    // fills in the others), logits rows and the persistent kernel's counters.
+    const Dims &f = m->full;
+    s->n_ctr = 2 + 5 * d.layers;
+    {
+      size_t off = 0;
+      auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off = (off + bytes + 255) & ~size_t(255);
+        return o;
+      };
+      const size_t ox = take(size_t(max_rows) * d.hidden * 2), oa = take(size_t(max_rows) * f.qdim() * 2),
+                   om = take(size_t(max_rows) * f.ffn * 2), ol = take(size_t(max_rows) * s->logit_stride * 2),
+                   oc = take(size_t(s->n_ctr) * 4);
+      s->xregion = dmalloc<char>(off);
+      s->xregion_bytes = off;
+      YAR_CUDA(cudaMemset(s->xregion, 0, off));
+      s->x = reinterpret_cast<bf16 *>(s->xregion + ox);
+      s->attn = reinterpret_cast<bf16 *>(s->xregion + oa);
+      s->mlp = reinterpret_cast<bf16 *>(s->xregion + om);
+      s->logits = reinterpret_cast<bf16 *>(s->xregion + ol);
+      s->d_ctr = reinterpret_cast<int *>(s->xregion + oc);
+    }
     s->max_splits = 32;
     s->attn_part = dmalloc<float>(size_t(max_rows) * d.heads * s->max_splits * (d.head_dim + 2));
     s->attn_count = dmalloc<int>(size_t(max_rows) * d.kv_heads);
@@ -103,12 +119,13 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
       s->tp_send = dmalloc<bf16>(block);
       s->tp_recv = dmalloc<bf16>(size_t(m->tp_world) * block);
     }
-    s->n_ctr = 2 + 5 * d.layers;
-    s->d_ctr = dmalloc<int>(s->n_ctr);
     s->d_epoch = dmalloc<int>(1);
-    YAR_CUDA(cudaMemset(s->d_ctr, 0, s->n_ctr * sizeof(int)));
     YAR_CUDA(cudaMemset(s->d_epoch, 0, sizeof(int)));
-    YAR_CUDA(cudaStreamSynchronize(s->stream));
+    YAR_CUDA(cudaDeviceSynchronize());
+    // Collective under tensor parallelism: map the peers' exchange regions (their counters
+    // are zero already: each rank zeroed its region before this exchange).
+    if (m->tp_world > 1)
+      s->tp_mapped = tp_map_peers(*m, s->xregion, s->xregion_bytes, s->tp_peer_regions, s->tp_dst, s->stream);
   } catch (...) {
     delete s;
     throw;
@@ -121,12 +138,13 @@ void free_session(Session *s) {
   cudaSetDevice(s->m->device);
   cudaStreamSynchronize(s->stream);
   for (auto &g : s->graphs) cudaGraphExecDestroy(g.exec);
+  tp_unmap_peers(s->tp_peer_regions);
   for (void *p : std::initializer_list<void *>{s->kv, s->d_page_table, s->d_pos, s->d_cur_pos, s->d_capacity,
-                                               s->d_token, s->d_active, s->d_error, s->x, s->qkv, s->attn,
-                                               s->mlp, s->logits, s->attn_part, s->attn_count, s->px, s->ph,
-                                               s->pqkv, s->pq, s->pattn, s->pmlp, s->pids, s->d_req,
-                                               s->d_out_tokens, s->d_scores, s->d_ctr, s->d_epoch, s->d_trace,
-                                               s->gemm_ws, s->tp_send, s->tp_recv})
+                                               s->d_token, s->d_active, s->d_error, s->xregion, s->qkv,
+                                               s->attn_part, s->attn_count, s->px, s->ph, s->pqkv, s->pq,
+                                               s->pattn, s->pmlp, s->pids, s->d_req, s->d_out_tokens,
+                                               s->d_scores, s->d_epoch, s->d_trace, s->gemm_ws, s->tp_send,
+                                               s->tp_recv})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -296,18 +314,32 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
 // -> LM head. Inactive rows are skipped by the embed/attention kernels.
 static bool use_persistent(Session &s, int n_rows) {
   // The persistent kernel streams each 64-position KV chunk as one contiguous copy, so a
-  // chunk must not straddle pages.
-  // Under tensor parallelism the exchange steps run between per-operation launches.
-  if (!s.use_persistent || n_rows < 1 || n_rows > 2 || s.page_tokens < 64 || s.m->tp_world > 1) return false;
+  // chunk must not straddle pages. Under tensor parallelism it needs the peers' exchange
+  // regions mapped (otherwise the per-operation path exchanges through NCCL).
+  if (!s.use_persistent || n_rows < 1 || n_rows > 2 || s.page_tokens < 64) return false;
+  if (s.m->tp_world > 1 && !s.tp_mapped) return false;
   if (s.persistent_ok[n_rows] < 0) s.persistent_ok[n_rows] = persistent_supported(*s.m, n_rows) ? 1 : 0;
   return s.persistent_ok[n_rows] == 1;
 }
 
 // Zero the persistent kernel's operation counters and step epoch (and the split-KV
 // arrival counts) before a sequence of decode steps.
+//
+// Under tensor parallelism peers add to this rank's counters, and a peer may already be in
+// its next step's first exchange while this rank is still on the host: the counters and the
+// epoch are never zeroed then (targets grow with the epoch), except every 2^20 steps, when
+// all ranks stop at a barrier, zero them, and meet again before any of them goes on.
 static void reset_step_sync(Session &s) {
-  YAR_CUDA(cudaMemsetAsync(s.d_ctr, 0, s.n_ctr * sizeof(int), s.stream));
-  YAR_CUDA(cudaMemsetAsync(s.d_epoch, 0, sizeof(int), s.stream));
+  if (s.m->tp_world == 1 || !s.tp_mapped) {
+    YAR_CUDA(cudaMemsetAsync(s.d_ctr, 0, s.n_ctr * sizeof(int), s.stream));
+    YAR_CUDA(cudaMemsetAsync(s.d_epoch, 0, sizeof(int), s.stream));
+  } else if (s.tp_epoch_steps >= (1ll << 20)) {
+    tp_barrier(*s.m, s.tp_send, s.stream);
+    YAR_CUDA(cudaMemsetAsync(s.d_ctr, 0, s.n_ctr * sizeof(int), s.stream));
+    YAR_CUDA(cudaMemsetAsync(s.d_epoch, 0, sizeof(int), s.stream));
+    tp_barrier(*s.m, s.tp_send, s.stream);
+    s.tp_epoch_steps = 0;
+  }
   YAR_CUDA(cudaMemsetAsync(s.attn_count, 0, size_t(s.max_rows) * s.m->d.kv_heads * sizeof(int), s.stream));
 }
 
@@ -410,6 +442,7 @@ void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int ph
   YAR_CUDA(cudaMemcpyAsync(s.d_token, tok.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
   reset_step_sync(s);
   decode_forward(s, hi, phase);
+  s.tp_epoch_steps += 1;
   YAR_CUDA(cudaStreamSynchronize(st));
   int err = 0;
   YAR_CUDA(cudaMemcpy(&err, s.d_error, sizeof(int), cudaMemcpyDeviceToHost));
@@ -555,6 +588,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
     const int k = std::min(kChunk, smp.max_tokens - steps);
     YAR_CUDA(cudaEventRecord(ev0, st));
     for (int i = 0; i < k; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
+    s.tp_epoch_steps += k;
     YAR_CUDA(cudaEventRecord(ev1, st));
     steps += k;
     YAR_CUDA(cudaMemcpyAsync(hp, &s.d_req[0].step, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -611,6 +645,7 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
                            {"execution", "cuda_graph"},
                            {"attention", "split_kv"},
                            {"tensor_parallel", s.m->tp_world},
+                           {"tp_exchange", s.m->tp_world == 1 ? "none" : s.tp_mapped ? "peer_stores" : "nccl"},
                            {"backend", "cuda-sm100a"},
                            {"decode_steps", steps},
                            {"decode_device_ms", decode_ms}};
@@ -733,6 +768,7 @@ std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const
     const int k = std::min(kChunk, smp.max_tokens - steps);
     YAR_CUDA(cudaEventRecord(ev0, st));
     for (int i = 0; i < k; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
+    s.tp_epoch_steps += k;
     YAR_CUDA(cudaEventRecord(ev1, st));
     steps += k;
     YAR_CUDA(cudaMemcpy2DAsync(prog.data(), 4 * sizeof(int), &s.d_req[0].step, sizeof(RequestState), 4 * sizeof(int),
@@ -775,6 +811,7 @@ std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const
                            {"execution", "cuda_graph"},
                            {"forward", n_req >= kBatchedRows ? "batched_tcgen05" : "per_row"},
                            {"tensor_parallel", s.m->tp_world},
+                           {"tp_exchange", s.m->tp_world == 1 ? "none" : s.tp_mapped ? "peer_stores" : "nccl"},
                            {"backend", "cuda-sm100a"}};
   return timing.dump();
 }

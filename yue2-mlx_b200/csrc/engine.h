@@ -84,6 +84,15 @@ void tp_unique_id(uint8_t *out128);
 void tp_init(Model &m, int rank, int world, const uint8_t *id128);
 void tp_destroy(Model &m);
 void tp_allgather_bf16(const Model &m, const bf16 *send, bf16 *recv, size_t n, cudaStream_t st);
+// Map every peer's exchange region (collective: every rank calls it for its session in the
+// same order). All ranks take the same outcome: true with the peers mapped and `dst`
+// filled, or false with nothing mapped (a peer without P2P loads/stores/atomics, or a
+// device of another size) — the engine then exchanges through NCCL only.
+bool tp_map_peers(const Model &m, void *region, size_t region_bytes, std::vector<void *> &peers, long long *dst,
+                  cudaStream_t st);
+void tp_unmap_peers(std::vector<void *> &peers);
+// Returns once every rank has reached it with its stream idle.
+void tp_barrier(const Model &m, void *scratch, cudaStream_t st);
 // send[r][j] = buf[r * stride + col0 + j] for r < n_rows, j < n.
 void launch_tp_pack(const bf16 *buf, int stride, int col0, int n, int n_rows, bf16 *send, cudaStream_t st);
 // buf[r * stride + k * n + j] = recv[(k * n_rows + r) * n + j] for every rank k, where
@@ -219,6 +228,16 @@ struct Session {
   // Tensor parallelism: a rank's block of rows before ([rows][n]) and after
   // ([world][rows][n]) the all-gather.
   bf16 *tp_send = nullptr, *tp_recv = nullptr;
+  // The exchange region (one allocation: x, attn, mlp, logits, the persistent kernel's
+  // counters). Under tensor parallelism every peer's region is mapped here (CUDA IPC) and
+  // tp_dst[i] is the byte offset from this region to peer i's (ranks in order, self left
+  // out), so the persistent kernel stores its outputs straight into the peers' buffers.
+  char *xregion = nullptr;
+  size_t xregion_bytes = 0;
+  bool tp_mapped = false;
+  long long tp_dst[7] = {};
+  std::vector<void *> tp_peer_regions;
+  long long tp_epoch_steps = 0;  // persistent steps since the counters were last zeroed
   size_t trace_elems = 0;
 };
 

@@ -96,6 +96,8 @@ void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaS
   // Under tensor parallelism this rank's heads sit at their place in the whole model's rows.
   p.out = s.attn + m.tp.q_row0;
   p.out_stride = m.full.qdim();
+  p.out_ndst = 0;
+  p.out_dst = nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.d.kv_heads, p.max_splits, n_rows);
   cfg.blockDim = dim3(kAttnThreads);

@@ -22,6 +22,15 @@
 // error; a CTA that gave up keeps releasing ring stages and taking every barrier (so its
 // producer finishes and no copy is left in flight) and keeps signalling counters (so
 // other CTAs do not wait for it), without computing.
+//
+// Tensor parallelism (tp_world ranks, one GPU each, every rank running this kernel for the
+// same step): each rank's operations compute its rows (its heads' attention, its hidden
+// rows of O and down, its FFN rows of gate/up, its columns of the head) and the epilogues
+// store every value both locally and into each peer's mapped copy of the buffer (x, attn,
+// mlp, logits: one exchange region per session, mapped by CUDA IPC). The counters of
+// attention, O, gate/up, down and the head are then released to every rank at system
+// scope, and their waits count all ranks' contributions — the all-gather is the
+// epilogue's stores, and the wait is the only synchronization. QKV stays rank-local.
 #include "attn_decode.cuh"
 #include "tma_ring.cuh"
 
@@ -32,9 +41,13 @@ constexpr int kPersistThreads = (kRingConsumers + 1) * 32;
 constexpr int kPersistMaxK = 6144;
 constexpr long long kCounterWaitLimit = 1ll << 22;  // polls of ~100 ns: under a second
 
+constexpr int kMaxTpWorld = 8;
+
 struct PersistParams {
   const LayerWeights *layers;  // device array, one entry per layer
-  int n_layers, H, QKV, QD, F, vocab;
+  // QKV: this rank's q/k/v rows; QD, F: the model's query and FFN widths (the K of O and
+  // down); HS, h0: this rank's hidden rows of O and down; FL, f0: its FFN rows.
+  int n_layers, H, QKV, QD, F, vocab, HS, h0, FL, f0;
   float eps;
   const bf16 *embed, *final_norm, *head;
   int head_rows, extra_row;  // phase rows [0, head_rows) of `head`, plus one extra row or -1
@@ -45,6 +58,10 @@ struct PersistParams {
   int *ctr, *epoch;
   int prefetch_stages;        // L2 prefetch distance beyond the ring, in stages
   unsigned long long *trace;  // optional [cta][op][8] SM-clock stamps (clock64), op = 5*layer + k
+  // Tensor parallelism: ranks, and the byte offsets from this rank's exchange region to
+  // each peer's (as mapped here).
+  int tp_world, tp_ndst;
+  long long tp_dst[kMaxTpWorld - 1];
 };
 
 __device__ __forceinline__ unsigned long long sm_clock() { return (unsigned long long)clock64(); }
@@ -62,6 +79,16 @@ __device__ __forceinline__ void red_release_add(int *p, int v) {
 __device__ __forceinline__ int ld_acquire(const int *p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// The same at system scope: counters that peer GPUs add to, ordering the data they
+// stored into this GPU's memory (over NVLink) before the count.
+__device__ __forceinline__ void red_release_add_sys(int *p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -123,18 +150,20 @@ __device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ GemvTask layer_task(const PersistParams &p, int l, int k) {
+// `dst`: the peer offsets (tp_ndst of them) the exchanged outputs are also stored at.
+__device__ __forceinline__ GemvTask layer_task(const PersistParams &p, int l, int k, const long long *dst) {
   const LayerWeights &w = p.layers[l];
-  const int H = p.H;
+  const int H = p.H, nd = p.tp_ndst;
   switch (k) {
-    case 0: return GemvTask{w.qkv, p.QKV, H, p.x, H, w.ln1, p.eps, p.qkv, p.QKV, kEpiStore};
-    case 1: return GemvTask{w.o, H, p.QD, p.attn, p.QD, nullptr, p.eps, p.x, H, kEpiResidual};
-    case 2: return GemvTask{w.gu, 2 * p.F, H, p.x, H, w.ln2, p.eps, p.mlp, p.F, kEpiSwiGLU};
-    default: return GemvTask{w.down, H, p.F, p.mlp, p.F, nullptr, p.eps, p.x, H, kEpiResidual};
+    case 0: return GemvTask{w.qkv, p.QKV, H, p.x, H, w.ln1, p.eps, p.qkv, p.QKV, kEpiStore, 0, nullptr};
+    case 1: return GemvTask{w.o, p.HS, p.QD, p.attn, p.QD, nullptr, p.eps, p.x + p.h0, H, kEpiResidual, nd, dst};
+    case 2: return GemvTask{w.gu, 2 * p.FL, H, p.x, H, w.ln2, p.eps, p.mlp + p.f0, p.F, kEpiSwiGLU, nd, dst};
+    default: return GemvTask{w.down, p.HS, p.F, p.mlp, p.F, nullptr, p.eps, p.x + p.h0, H, kEpiResidual, nd, dst};
   }
 }
-__device__ __forceinline__ GemvTask head_task(const PersistParams &p) {
-  return GemvTask{p.head, p.head_rows, p.H, p.x, p.H, p.final_norm, p.eps, p.logits, p.logit_stride, kEpiStore};
+__device__ __forceinline__ GemvTask head_task(const PersistParams &p, const long long *dst) {
+  return GemvTask{p.head,   p.head_rows, p.H, p.x, p.H, p.final_norm, p.eps, p.logits, p.logit_stride, kEpiStore,
+                  p.tp_ndst, dst};
 }
 
 struct KvChunkRef {
@@ -157,7 +186,7 @@ template <int NB>
 struct Producer {
   const LayerWeights *layers;
   const bf16 *head;
-  int head_rows, H, QKV, QD, F, nL, epoch;
+  int head_rows, H, QKV, QD, F, HS, FL, nL, epoch;
   bf16 *pool;
   AttnGeom g;
   int max_splits;
@@ -168,8 +197,8 @@ struct Producer {
   KvChunkRef *kv;  // this CTA's chunk list (shared memory, kMaxCtaChunks entries)
 
   __device__ Producer(const PersistParams &p, int ep, KvChunkRef *kv_smem)
-      : layers(p.layers), head(p.head), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F),
-        nL(p.n_layers), epoch(ep), pool(p.ap.pool), g(p.ap.g), max_splits(p.ap.max_splits),
+      : layers(p.layers), head(p.head), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F), HS(p.HS),
+        FL(p.FL), nL(p.n_layers), epoch(ep), pool(p.ap.pool), g(p.ap.g), max_splits(p.ap.max_splits),
         page_table(p.ap.page_table), ctr(p.ctr), active(p.active), cur_pos(p.cur_pos), error(p.error), nkv(0),
         planned(false), failed(false), kv(kv_smem) {}
 
@@ -226,9 +255,9 @@ struct Producer {
       const LayerWeights &w = layers[c.l];
       switch (c.o) {
         case 0: c.W = w.qkv, c.N = QKV, c.K = H; break;
-        case 2: c.W = w.o, c.N = H, c.K = QD; break;
-        case 3: c.W = w.gu, c.N = 2 * F, c.K = H; break;
-        default: c.W = w.down, c.N = H, c.K = F; break;
+        case 2: c.W = w.o, c.N = HS, c.K = QD; break;
+        case 3: c.W = w.gu, c.N = 2 * FL, c.K = H; break;
+        default: c.W = w.down, c.N = HS, c.K = F; break;
       }
     }
     const int groups = (c.N + 7) / 8;
@@ -323,11 +352,15 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   __shared__ AttnRow<128> rowst[NB];
   __shared__ int s_epoch, s_bad;
   __shared__ KvChunkRef kv_chunks[kMaxCtaChunks];
+  __shared__ long long s_dst[kMaxTpWorld - 1];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nL = p.n_layers, H = p.H;
-  auto task = [&](int l, int k) { return layer_task(p, l, k); };
-  const GemvTask head = head_task(p);
+  auto task = [&](int l, int k) { return layer_task(p, l, k, s_dst); };
+  const GemvTask head = head_task(p, s_dst);
+  const bool tp = p.tp_world > 1;
+  const int W = p.tp_world;
+  if (threadIdx.x < kMaxTpWorld - 1) s_dst[threadIdx.x] = threadIdx.x < p.tp_ndst ? p.tp_dst[threadIdx.x] : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -385,20 +418,32 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   auto stamp = [&](int o, int k) {
     if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
   };
+  // Thread 0 publishes one share of counter idx: to this rank only, or (exchanged
+  // operations under tensor parallelism) to every rank at system scope.
+  auto publish = [&](int idx, bool all_ranks) {
+    if (!tp) {
+      red_release_add(p.ctr + idx, 1);
+      return;
+    }
+    red_release_add_sys(p.ctr + idx, 1);
+    if (all_ranks)
+      for (int i = 0; i < p.tp_ndst; ++i)
+        red_release_add_sys(reinterpret_cast<int *>(reinterpret_cast<char *>(p.ctr + idx) + s_dst[i]), 1);
+  };
   // One barrier orders every consumer thread's writes before thread 0's release-add, which
   // publishes the CTA's share; the same barrier makes a recorded failure CTA-wide.
-  auto signal = [&](int idx) {
+  auto signal = [&](int idx, bool all_ranks) {
     if (bad) s_bad = 1;
     consumer_sync();
     bad = s_bad != 0;
-    if (ctid == 0) red_release_add(p.ctr + idx, 1);
+    if (ctid == 0) publish(idx, all_ranks);
   };
   // Wait until counter idx reaches target; gives up on expiry or once any CTA failed.
   auto wait_for = [&](int idx, int target) {
     if (ctid == 0 && !s_bad) {
       long long i = 0;
       for (; i < kCounterWaitLimit; ++i) {
-        if (ld_acquire(p.ctr + idx) >= target) break;
+        if ((tp ? ld_acquire_sys(p.ctr + idx) : ld_acquire(p.ctr + idx)) >= target) break;
         if (ld_acquire(p.error) != 0) {
           i = kCounterWaitLimit;
           break;
@@ -442,7 +487,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
           p.pos[b] = q + 1;
         }
       }
-    signal(c_embed);
+    signal(c_embed, false);
   }
   // Trace calibration: globaltimer (ns) and the SM clock at the step's start and end.
   auto calib = [&](int o) {
@@ -476,7 +521,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l, 2);
-      signal(c_op(l, 0));
+      signal(c_op(l, 0), false);
       stamp(5 * l, 3);
     }
     // Attention: the CTA's units, one after another on all consumer warps; each unit's KV
@@ -488,6 +533,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     {
       DecodeAttnParams ap = p.ap;
       ap.layer = l;
+      ap.out_ndst = p.tp_ndst;
+      ap.out_dst = s_dst;
       long long itk = it;
       for (int k = 0, u = blockIdx.x; u < U; ++k, u += gridDim.x) {
         const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
@@ -524,7 +571,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
         // An inactive row (or a failed step) counts each kv head once, from split 0.
         if (merged || (ui.split == 0 && (bad || !ui.active))) {
           consumer_sync();
-          if (ctid == 0) red_release_add(p.ctr + c_op(l, 1), 1);
+          if (ctid == 0) publish(c_op(l, 1), true);
         }
         itk += nch;
       }
@@ -533,7 +580,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     stamp(5 * l + 1, 2);
     // O (+ residual).
     stamp(5 * l + 2, 6);  // wait began
-    wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB);
+    wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB * W);
     {
       stamp(5 * l + 2, 0);
       const GemvTask t = task(l, 1);
@@ -542,13 +589,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 2, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 2, 2);
-      signal(c_op(l, 2));
+      signal(c_op(l, 2), true);
       stamp(5 * l + 2, 3);
     }
     // gate/up (RMSNorm of x fused, SwiGLU epilogue).
     stamp(5 * l + 3, 6);  // wait began
     ring_norm_w_load(task(l, 2), wn_next, ctid);
-    wait_for(c_op(l, 2), (epoch + 1) * all);
+    wait_for(c_op(l, 2), (epoch + 1) * all * W);
     {
       stamp(5 * l + 3, 0);
       const GemvTask t = task(l, 2);
@@ -557,12 +604,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 3, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 3, 2);
-      signal(c_op(l, 3));
+      signal(c_op(l, 3), true);
       stamp(5 * l + 3, 3);
     }
     // down (+ residual).
     stamp(5 * l + 4, 6);  // wait began
-    wait_for(c_op(l, 3), (epoch + 1) * all);
+    wait_for(c_op(l, 3), (epoch + 1) * all * W);
     {
       stamp(5 * l + 4, 0);
       const GemvTask t = task(l, 3);
@@ -571,14 +618,14 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * l + 4, 1);
       ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
       stamp(5 * l + 4, 2);
-      signal(c_op(l, 4));
+      signal(c_op(l, 4), true);
       stamp(5 * l + 4, 3);
     }
     if (l + 1 < nL) {
       stamp(5 * (l + 1), 6);  // the next QKV's wait began
       ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
     }
-    wait_for(c_op(l, 4), (epoch + 1) * all);
+    wait_for(c_op(l, 4), (epoch + 1) * all * W);
   }
   // Final RMSNorm + phase rows of the LM head.
   {
@@ -605,13 +652,15 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
         v = fmaf(bf_hi(wq.w), bf_hi(av.w), v);
       }
       v = warp_sum(v);
-      if (lane == 0) p.logits[size_t(warp) * p.logit_stride + p.head_rows] = f2bf(v);
+      if (lane == 0) store_all(p.logits + size_t(warp) * p.logit_stride + p.head_rows, f2bf(v), p.tp_ndst, s_dst);
     }
-    signal(c_head);
+    signal(c_head, true);
     calib(5 * nL);
   }
+  // CTA 0 ends the step once every rank's head columns are in (the sampler, launched after
+  // this kernel, reads the whole logits rows).
   if (blockIdx.x == 0) {
-    wait_for(c_head, (epoch + 1) * all);
+    wait_for(c_head, (epoch + 1) * all * W);
     if (ctid == 0) {
       __threadfence();
       atomicExch(p.epoch, epoch + 1);
@@ -633,11 +682,13 @@ void configure_persistent_kernels() {
 
 // True when the persistent kernel handles this model and row count.
 bool persistent_supported(const Model &m, int n_rows) {
-  const Dims &d = m.d;
-  if (n_rows < 1 || n_rows > 2) return false;
+  // The ring GEMVs need every K (hidden, and the model's query and FFN widths: O and down
+  // keep their whole input width under tensor parallelism) a multiple of 2048.
+  const Dims &d = m.d, &f = m.full;
+  if (n_rows < 1 || n_rows > 2 || m.tp_world > kMaxTpWorld) return false;
   if (d.head_dim != 128 || d.heads != 2 * d.kv_heads) return false;
-  if (d.hidden % kRingPiece || d.qdim() % kRingPiece || d.ffn % kRingPiece || d.ffn > kPersistMaxK ||
-      d.hidden > kPersistMaxK || d.qdim() > kPersistMaxK)
+  if (d.hidden % kRingPiece || f.qdim() % kRingPiece || f.ffn % kRingPiece || f.ffn > kPersistMaxK ||
+      d.hidden > kPersistMaxK || f.qdim() > kPersistMaxK)
     return false;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, n_rows == 1 ? k_decode_persistent<1> : k_decode_persistent<2>,
@@ -649,26 +700,38 @@ bool persistent_supported(const Model &m, int n_rows) {
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st) {
   const Dims &d = m.d;
   const PhaseRows pr = phase_rows(d, phase);
+  if (m.tp_world > 1 && !s.tp_mapped) throw Error("RuntimeError", "persistent tensor-parallel decode needs mapped peers");
   PersistParams p;
   p.layers = m.d_layers;
   p.n_layers = d.layers;
   p.H = d.hidden;
   p.QKV = d.qkv_rows();
-  p.QD = d.qdim();
-  p.F = d.ffn;
+  p.QD = m.full.qdim();
+  p.F = m.full.ffn;
+  p.HS = m.tp.h_rows;
+  p.h0 = m.tp.h_row0;
+  p.FL = d.ffn;
+  p.f0 = m.tp.ffn_row0;
   p.vocab = d.vocab;
   p.eps = d.eps;
   p.embed = m.embed;
   p.final_norm = m.final_norm;
-  p.head = m.lm_head + size_t(pr.row0) * d.hidden;
-  p.head_rows = pr.n_main;
-  p.extra_row = pr.extra >= 0 ? pr.extra - pr.row0 : -1;
+  // This rank's phase columns [c0, c1) of the head (all of them on one GPU): main rows
+  // [c0, min(c1, n_main)) and, when n_main falls in the range, the extra row.
+  const int width = pr.width(), slice = m.tp_world > 1 ? tp_head_slice(width, m.tp_world) : width;
+  const int c0 = std::min(width, m.tp_rank * slice), c1 = std::min(width, c0 + slice);
+  p.head = m.lm_head + size_t(pr.row0 + c0) * d.hidden;
+  p.head_rows = std::max(0, std::min(c1, pr.n_main) - c0);
+  p.extra_row = pr.extra >= 0 && c0 <= pr.n_main && pr.n_main < c1 ? pr.extra - pr.row0 - c0 : -1;
   p.x = s.x;
   p.qkv = s.qkv;
   p.attn = s.attn;
   p.mlp = s.mlp;
-  p.logits = s.logits;
+  p.logits = s.logits + c0;
   p.logit_stride = s.logit_stride;
+  p.tp_world = m.tp_world;
+  p.tp_ndst = m.tp_world > 1 ? m.tp_world - 1 : 0;
+  for (int i = 0; i < kMaxTpWorld - 1; ++i) p.tp_dst[i] = i < p.tp_ndst ? s.tp_dst[i] : 0;
   DecodeAttnParams &a = p.ap;
   a.g.heads = d.heads;
   a.g.kv_heads = d.kv_heads;
@@ -697,8 +760,10 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   a.sin_tab = m.rope_sin;
   a.part = s.attn_part;
   a.count = s.attn_count;
-  a.out = s.attn;
-  a.out_stride = m.d.qdim();
+  a.out = s.attn + m.tp.q_row0;
+  a.out_stride = m.full.qdim();
+  a.out_ndst = 0;  // set in the kernel (peer offsets in shared memory)
+  a.out_dst = nullptr;
   p.token = s.d_token;
   p.pos = s.d_pos;
   p.cur_pos = s.d_cur_pos;

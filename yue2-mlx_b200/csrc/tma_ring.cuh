@@ -29,7 +29,17 @@ struct GemvTask {
   bf16 *out;
   int out_stride;
   int epi;  // kEpiStore / kEpiResidual / kEpiSwiGLU
+  // Tensor parallelism: every output value is also stored at out + dst[i] bytes for
+  // i < n_dst — the same place in each peer rank's mapped copy of the buffer.
+  int n_dst;
+  const long long *dst;
 };
+
+// Store v at o and at its copies in the peers' mapped buffers.
+__device__ __forceinline__ void store_all(bf16 *o, bf16 v, int n_dst, const long long *dst) {
+  *o = v;
+  for (int i = 0; i < n_dst; ++i) *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(o) + dst[i]) = v;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -316,7 +326,7 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
             us += src[w * NB * 8 + b * 8 + 2 * j + 1];
           }
           const float gate = rbf(gs), up = rbf(us);
-          t.out[size_t(b) * t.out_stride + (r0 >> 1) + j] = f2bf(rbf(silu_f32(gate)) * up);
+          store_all(t.out + size_t(b) * t.out_stride + (r0 >> 1) + j, f2bf(rbf(silu_f32(gate)) * up), t.n_dst, t.dst);
         } else {
           const int b = rem / 8, r = rem % 8;
           if (r0 + r >= t.N) continue;
@@ -324,10 +334,7 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
 #pragma unroll
           for (int w = 0; w < kRingConsumers; ++w) v += src[w * NB * 8 + b * 8 + r];
           bf16 *o = t.out + size_t(b) * t.out_stride + r0 + r;
-          if (t.epi == kEpiResidual)
-            *o = f2bf(bf2f(__ldcg(o)) + rbf(v));
-          else
-            *o = f2bf(v);
+          store_all(o, t.epi == kEpiResidual ? f2bf(bf2f(__ldcg(o)) + rbf(v)) : f2bf(v), t.n_dst, t.dst);
         }
       }
     }

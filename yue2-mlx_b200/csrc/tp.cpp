@@ -19,6 +19,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "engine.h"
 
@@ -91,6 +92,100 @@ void tp_destroy(Model &m) {
 
 void tp_allgather_bf16(const Model &m, const bf16 *send, bf16 *recv, size_t n, cudaStream_t st) {
   check(nccl().all_gather(send, recv, n, ncclBfloat16, static_cast<ncclComm_t>(m.tp_comm), st), "ncclAllGather");
+}
+
+namespace {
+// Every rank's `bytes` of host data (rank order) through one all-gather.
+std::vector<char> allgather_host(const Model &m, const void *mine, size_t bytes, cudaStream_t st) {
+  const int W = m.tp_world;
+  char *d = nullptr;
+  YAR_CUDA(cudaMalloc(&d, bytes * (W + 1)));
+  std::vector<char> out(bytes * W);
+  try {
+    YAR_CUDA(cudaMemcpyAsync(d + bytes * W, mine, bytes, cudaMemcpyHostToDevice, st));
+    check(nccl().all_gather(d + bytes * W, d, bytes, ncclInt8, static_cast<ncclComm_t>(m.tp_comm), st),
+          "ncclAllGather");
+    YAR_CUDA(cudaMemcpyAsync(out.data(), d, bytes * W, cudaMemcpyDeviceToHost, st));
+    YAR_CUDA(cudaStreamSynchronize(st));
+  } catch (...) {
+    cudaFree(d);
+    throw;
+  }
+  cudaFree(d);
+  return out;
+}
+bool all_ranks_agree(const Model &m, bool ok, cudaStream_t st) {
+  const int mine = ok ? 1 : 0;
+  const std::vector<char> v = allgather_host(m, &mine, sizeof(int), st);
+  for (int k = 0; k < m.tp_world; ++k) {
+    int x;
+    std::memcpy(&x, v.data() + k * sizeof(int), sizeof(int));
+    if (!x) return false;
+  }
+  return true;
+}
+}  // namespace
+
+bool tp_map_peers(const Model &m, void *region, size_t region_bytes, std::vector<void *> &peers, long long *dst,
+                  cudaStream_t st) {
+  struct Entry {
+    cudaIpcMemHandle_t handle;
+    int device, sm_count;
+    unsigned long long bytes;
+  };
+  const int W = m.tp_world, rank = m.tp_rank;
+  if (W > 8) return false;  // dst holds at most 7 peers (the same answer on every rank)
+  Entry mine{};
+  const bool have_handle = cudaIpcGetMemHandle(&mine.handle, region) == cudaSuccess;
+  cudaGetLastError();
+  mine.device = m.device;
+  mine.sm_count = m.sm_count;
+  mine.bytes = region_bytes;
+  const std::vector<char> raw = allgather_host(m, &mine, sizeof(Entry), st);
+  std::vector<Entry> e(W);
+  std::memcpy(e.data(), raw.data(), raw.size());
+  // Direct loads, stores and atomics to every peer, the same grid everywhere (the
+  // persistent kernel's counter targets assume it) and regions of the same size (the same
+  // session shape, hence the same layout: outputs are stored at their own offset).
+  bool ok = have_handle;
+  for (int k = 0; k < W; ++k) ok = ok && e[k].bytes == region_bytes;
+  for (int k = 0; k < W && ok; ++k) {
+    if (k == rank) continue;
+    int access = 0, atomics = 0;
+    ok = cudaDeviceCanAccessPeer(&access, m.device, e[k].device) == cudaSuccess && access &&
+         cudaDeviceGetP2PAttribute(&atomics, cudaDevP2PAttrNativeAtomicSupported, m.device, e[k].device) ==
+             cudaSuccess &&
+         atomics && e[k].sm_count == m.sm_count;
+  }
+  cudaGetLastError();
+  if (!all_ranks_agree(m, ok, st)) return false;
+  peers.assign(W, nullptr);
+  bool opened = true;
+  for (int k = 0; k < W && opened; ++k) {
+    if (k == rank) continue;
+    opened = cudaIpcOpenMemHandle(&peers[k], e[k].handle, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+  }
+  cudaGetLastError();
+  if (!all_ranks_agree(m, opened, st)) {
+    tp_unmap_peers(peers);
+    return false;
+  }
+  for (int k = 0, i = 0; k < W; ++k)
+    if (k != rank) dst[i++] = static_cast<char *>(peers[k]) - static_cast<char *>(region);
+  return true;
+}
+
+void tp_unmap_peers(std::vector<void *> &peers) {
+  for (void *p : peers)
+    if (p) cudaIpcCloseMemHandle(p);
+  peers.clear();
+}
+
+void tp_barrier(const Model &m, void *scratch, cudaStream_t st) {
+  YAR_CUDA(cudaStreamSynchronize(st));
+  bf16 *b = static_cast<bf16 *>(scratch);
+  tp_allgather_bf16(m, b, b + 1, 1, st);
+  YAR_CUDA(cudaStreamSynchronize(st));
 }
 
 }  // namespace yar
