@@ -29,15 +29,21 @@ static AttnGeom geom(const Model &m, const Session &s) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Decode: grid (kv_head, split, row), 128 threads = one attention unit per CTA
+// Decode: grid (kv_head, split, row), 256 threads = one attention unit per CTA
 // (attn_decode.cuh); each chunk's cached rows are loaded into shared memory with 16-byte
-// loads (any page size), then processed by the same code as the persistent kernel.
+// cp.async copies (any page size), then processed by the same code as the persistent
+// kernel. Two chunk buffers (dynamic shared memory, [2][K | V][64][D]): chunk c + 1's
+// copies are in flight while chunk c is computed, and the first chunk's while q and k are
+// normalized and rotated.
+template <int D>
+__host__ __device__ constexpr size_t attn_decode_dyn_smem() { return size_t(2) * 2 * kKvChunk * D * sizeof(bf16); }
+
 template <int D, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p) {
   __shared__ AttnTeamSmem<D, G> sm;
   __shared__ AttnRow<D> rs;
-  __shared__ __align__(16) bf16 kbuf[kKvChunk * D];
-  __shared__ __align__(16) bf16 vbuf[kKvChunk * D];
+  extern __shared__ __align__(16) unsigned char attn_dyn[];
+  bf16 *kvbuf = reinterpret_cast<bf16 *>(attn_dyn);
   const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z, tid = threadIdx.x;
   float wv[D / 32];
   attn_load_norm_w<D, G>(p.qn, p.kn, wv, tid);
@@ -49,30 +55,44 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p
   const int pos = rs.pos;
   const SplitPlan sp = split_plan(pos + 1, p.max_splits);
   if (split >= sp.n_splits) return;  // beyond the context: no work, no arrival
-  attn_qk<D, G>(p, sm, rs, row, kvh, split == sp.n_splits - 1, wv, tid, 1);
-  AttnAcc<D> acc;
-  attn_acc_init(acc);
-  const int c1 = min((split + 1) * sp.cps, sp.nchunks);
-  for (int c = split * sp.cps; c < c1; ++c) {
+  const int c0 = split * sp.cps, c1 = min((split + 1) * sp.cps, sp.nchunks);
+  // Chunk c's cached K and V rows (positions < pos: the new one is appended by attn_qk and
+  // read from shared memory) into buffer `slot`, as one cp.async group.
+  auto issue = [&](int c, int slot) {
     const int base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
-    // Every 16-byte piece of the chunk's cached K and V rows in flight at once (cp.async,
-    // any page size), one wait.
+    bf16 *kb = kvbuf + size_t(slot) * 2 * kKvChunk * D, *vb = kb + kKvChunk * D;
     for (int idx = tid; idx < n_main * (D / 8); idx += kAttnThreads) {
       const int r = idx / (D / 8), cc = idx % (D / 8);
       const bf16 *ks = kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, base + r) + cc * 8;
       const bf16 *vs = kv_row_ptr<D>(p, rs, row, p.layer, 1, kvh, base + r) + cc * 8;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
-                       __cvta_generic_to_shared(kbuf + r * D + cc * 8))),
+                       __cvta_generic_to_shared(kb + r * D + cc * 8))),
                    "l"(ks)
                    : "memory");
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
-                       __cvta_generic_to_shared(vbuf + r * D + cc * 8))),
+                       __cvta_generic_to_shared(vb + r * D + cc * 8))),
                    "l"(vs)
                    : "memory");
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (c0 < c1) issue(c0, 0);
+  attn_qk<D, G>(p, sm, rs, row, kvh, split == sp.n_splits - 1, wv, tid, 1);
+  AttnAcc<D> acc;
+  attn_acc_init(acc);
+  for (int c = c0; c < c1; ++c) {
+    const int slot = (c - c0) & 1, base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
+    // The other buffer was last read by chunk c - 1, whose attn_chunk ended on a team
+    // barrier: it is free for chunk c + 1.
+    if (c + 1 < c1) {
+      issue(c + 1, slot ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
     team_sync(1);
-    attn_chunk<D, G>(sm, kbuf, vbuf, n_main, pos - base < kKvChunk, p.g.scale, acc, tid, 1);
+    const bf16 *kb = kvbuf + size_t(slot) * 2 * kKvChunk * D;
+    attn_chunk<D, G>(sm, kb, kb + kKvChunk * D, n_main, pos - base < kKvChunk, p.g.scale, acc, tid, 1);
   }
   attn_finish<D, G>(p, sm, acc, row, kvh, split, sp.n_splits, tid, 1);
 }
@@ -101,6 +121,7 @@ void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaS
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.d.kv_heads, p.max_splits, n_rows);
   cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = m.d.head_dim == 128 ? attn_decode_dyn_smem<128>() : attn_decode_dyn_smem<64>();
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -317,6 +338,14 @@ __global__ void __launch_bounds__(256) k_attn_prefill(PrefillAttnParams p) {
 static size_t prefill_attn_smem(int D) { return (64 * (D + 1) * 2 + 64 * D + 64 * 65) * sizeof(float); }
 
 void configure_attn_kernels() {
+  YAR_CUDA(cudaFuncSetAttribute(k_attn_decode<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(attn_decode_dyn_smem<128>())));
+  YAR_CUDA(cudaFuncSetAttribute(k_attn_decode<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(attn_decode_dyn_smem<128>())));
+  YAR_CUDA(cudaFuncSetAttribute(k_attn_decode<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(attn_decode_dyn_smem<64>())));
+  YAR_CUDA(cudaFuncSetAttribute(k_attn_decode<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(attn_decode_dyn_smem<64>())));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(prefill_attn_smem(128))));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
