@@ -334,7 +334,10 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
 #pragma unroll
           for (int w = 0; w < kRingConsumers; ++w) v += src[w * NB * 8 + b * 8 + r];
           bf16 *o = t.out + size_t(b) * t.out_stride + r0 + r;
-          store_all(o, t.epi == kEpiResidual ? f2bf(bf2f(__ldcg(o)) + rbf(v)) : f2bf(v), t.n_dst, t.dst);
+          if (t.epi == kEpiResidual)
+            store_all(o, f2bf(bf2f(__ldcg(o)) + rbf(v)), t.n_dst, t.dst);
+          else
+            store_all(o, f2bf(v), t.n_dst, t.dst);
         }
       }
     }
