@@ -90,6 +90,7 @@ struct DecodeAttnParams {
   int out_stride;
   int out_ndst;  // tensor parallelism: also stored at out + out_dst[i] bytes (peer copies)
   const long long *out_dst;
+  int *error;  // device error word: expired waits of the standalone kernel (may be null)
 };
 
 constexpr int kKvChunk = 64;  // positions per KV chunk
@@ -253,9 +254,10 @@ __device__ __forceinline__ void attn_acc_init(AttnAcc<D> &a) {
 // Step 2, one chunk: rows [0, n_main) of Ks/Vs (shared memory, row pitch D) and, when
 // `extra`, the new position (sm.knew/vnew) as row n_main. Ends with a barrier.
 //   Scores: the threads of head hd (256 / G of them) form 4-thread groups; part p of a
-//   group holds its quarter of q in registers and dots it with that quarter of rows ps,
-//   ps + slots, ... (16-byte K loads in an order rotated by row and part, so a
-//   quarter-warp never hits one bank group twice); the 4 parts are added by shuffles.
+//   group holds its quarter of q in registers (in the rotated order below) and dots it
+//   with that quarter of rows ps, ps + slots, ... (16-byte K loads in an order rotated by
+//   row and part, so a quarter-warp never hits one bank group twice); the 4 parts are
+//   added by shuffles.
 //   P.V: thread (head hd, dim group dg of 8 dims, phase q) sums p_r * V[r][8 dg .. +7]
 //   over the rows r = q (mod phases) with 16-byte V loads; the phases are added in order
 //   through shared memory, one output per thread.
@@ -273,10 +275,14 @@ __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *V
   const int lane = tid & 31, warp = tid >> 5;
   const int hd = tid / THD, u = tid % THD, part = u % 4, ps = u / 4;
   const int n = n_main + (extra ? 1 : 0);
-  // q quarter of this part, BF16 pairs.
-  uint4 qv[CP];
+  // This part's q chunks in the rotated order of the K loads (the rotation depends on the
+  // lane only), BF16 pairs.
+  uint4 qr[CP];
 #pragma unroll
-  for (int c = 0; c < CP; ++c) qv[c] = *reinterpret_cast<const uint4 *>(&sm.q_b[hd][(part * CP + c) * 8]);
+  for (int j = 0; j < CP; ++j) {
+    const int cj = (j + ps * (CP > 1 ? CP / 2 : 1) + (part >> 1)) & (CP - 1);
+    qr[j] = *reinterpret_cast<const uint4 *>(&sm.q_b[hd][(part * CP + cj) * 8]);
+  }
   float sc[PPT];
 #pragma unroll
   for (int k = 0; k < PPT; ++k) {
@@ -288,10 +294,7 @@ __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *V
       for (int j = 0; j < CP; ++j) {
         const int cj = (j + ps * (CP > 1 ? CP / 2 : 1) + (part >> 1)) & (CP - 1);
         const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + (part * CP + cj) * 8);
-        uint4 q8 = qv[0];
-#pragma unroll
-        for (int c = 1; c < CP; ++c)
-          if (c == cj) q8 = qv[c];
+        const uint4 q8 = qr[j];
         a0 = fmaf(bf_lo(q8.x), bf_lo(k8.x), a0);
         a1 = fmaf(bf_hi(q8.x), bf_hi(k8.x), a1);
         a2 = fmaf(bf_lo(q8.y), bf_lo(k8.y), a2);

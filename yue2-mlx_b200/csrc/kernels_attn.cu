@@ -7,6 +7,7 @@
 // table maps logical page i (positions i*P .. i*P+P-1) to a physical page. Physical slot
 // = RoPE position (modeling_yue2.py:383-393: StaticKVCache writes slot pos).
 #include "attn_decode.cuh"
+#include "tma_ring.cuh"
 
 namespace yar {
 
@@ -30,11 +31,13 @@ static AttnGeom geom(const Model &m, const Session &s) {
 
 // ---------------------------------------------------------------------------------------
 // Decode: grid (kv_head, split, row), 256 threads = one attention unit per CTA
-// (attn_decode.cuh); each chunk's cached rows are loaded into shared memory with 16-byte
-// cp.async copies (any page size), then processed by the same code as the persistent
-// kernel. Two chunk buffers (dynamic shared memory, [2][K | V][64][D]): chunk c + 1's
-// copies are in flight while chunk c is computed, and the first chunk's while q and k are
-// normalized and rotated.
+// (attn_decode.cuh); each chunk's cached rows are brought into shared memory, then
+// processed by the same code as the persistent kernel. With pages of at least 64
+// positions a chunk's K rows and its V rows are each one contiguous block (a chunk never
+// straddles a page): thread 0 moves them with two bulk copies on an mbarrier; smaller
+// pages take 16-byte cp.async copies, row by row. Two chunk buffers (dynamic shared
+// memory, [2][K | V][64][D]): chunk c + 1's copies are in flight while chunk c is
+// computed, and the first chunk's while q and k are normalized and rotated.
 template <int D>
 __host__ __device__ constexpr size_t attn_decode_dyn_smem() { return size_t(2) * 2 * kKvChunk * D * sizeof(bf16); }
 
@@ -42,11 +45,18 @@ template <int D, int G>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p) {
   __shared__ AttnTeamSmem<D, G> sm;
   __shared__ AttnRow<D> rs;
+  __shared__ __align__(8) uint64_t kv_full[2];
   extern __shared__ __align__(16) unsigned char attn_dyn[];
   bf16 *kvbuf = reinterpret_cast<bf16 *>(attn_dyn);
   const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z, tid = threadIdx.x;
+  const bool bulk = p.g.page_tokens >= kKvChunk;
   float wv[D / 32];
   attn_load_norm_w<D, G>(p.qn, p.kn, wv, tid);
+  if (tid == 0) {
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   pdl_launch_dependents();
   pdl_wait();
   attn_row_load<D>(rs, p, row, tid, kAttnThreads);
@@ -61,6 +71,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p
   auto issue = [&](int c, int slot) {
     const int base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
     bf16 *kb = kvbuf + size_t(slot) * 2 * kKvChunk * D, *vb = kb + kKvChunk * D;
+    if (bulk) {
+      if (tid == 0) {
+        const unsigned bytes = unsigned(n_main) * D * 2;
+        mbar_arrive_expect_tx(&kv_full[slot], 2 * bytes);
+        if (bytes) {
+          bulk_g2s(kb, kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, base), bytes, &kv_full[slot]);
+          bulk_g2s(vb, kv_row_ptr<D>(p, rs, row, p.layer, 1, kvh, base), bytes, &kv_full[slot]);
+        }
+      }
+      return;
+    }
     for (int idx = tid; idx < n_main * (D / 8); idx += kAttnThreads) {
       const int r = idx / (D / 8), cc = idx % (D / 8);
       const bf16 *ks = kv_row_ptr<D>(p, rs, row, p.layer, 0, kvh, base + r) + cc * 8;
@@ -84,8 +105,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p
     const int slot = (c - c0) & 1, base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
     // The other buffer was last read by chunk c - 1, whose attn_chunk ended on a team
     // barrier: it is free for chunk c + 1.
-    if (c + 1 < c1) {
-      issue(c + 1, slot ^ 1);
+    if (c + 1 < c1) issue(c + 1, slot ^ 1);
+    if (bulk) {
+      if (!mbar_wait(&kv_full[slot], unsigned((c - c0) >> 1) & 1u) && tid == 0 && p.error) atomicOr(p.error, 8);
+    } else if (c + 1 < c1) {
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -118,6 +141,7 @@ void launch_attn_decode(const Model &m, Session &s, int layer, int n_rows, cudaS
   p.out_stride = m.full.qdim();
   p.out_ndst = 0;
   p.out_dst = nullptr;
+  p.error = s.d_error;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.d.kv_heads, p.max_splits, n_rows);
   cfg.blockDim = dim3(kAttnThreads);

@@ -764,6 +764,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   a.out_stride = m.full.qdim();
   a.out_ndst = 0;  // set in the kernel (peer offsets in shared memory)
   a.out_dst = nullptr;
+  a.error = s.d_error;
   p.token = s.d_token;
   p.pos = s.d_pos;
   p.cur_pos = s.d_cur_pos;
