@@ -156,6 +156,17 @@ __device__ __forceinline__ bf16 *kv_row_ptr(const DecodeAttnParams &p, const Att
   return p.pool + blk * g.page_elems + (size_t(kvh) * g.page_tokens + (q & (g.page_tokens - 1))) * D;
 }
 
+// lo += a.lo * b.lo and hi += a.hi * b.hi for BF16 pairs a, b, FP32 accumulators: the
+// mixed-precision FMA takes the BF16 halves directly (their conversion to FP32 is exact,
+// so each result is fmaf of the converted values, rounded once) instead of unpacking
+// both operands with shifts and masks first.
+__device__ __forceinline__ void fma_bf16x2(float &lo, float &hi, uint32_t a, uint32_t b) {
+  asm("{\n .reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %2;\n mov.b32 {bl, bh}, %3;\n"
+      " fma.rn.f32.bf16 %0, al, bl, %0;\n fma.rn.f32.bf16 %1, ah, bh, %1;\n}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(a), "r"(b));
+}
+
 __device__ __forceinline__ void team_sync(int bar_id) {
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "n"(kAttnThreads) : "memory");
 }
@@ -295,14 +306,10 @@ __device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *V
         const int cj = (j + ps * (CP > 1 ? CP / 2 : 1) + (part >> 1)) & (CP - 1);
         const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + (part * CP + cj) * 8);
         const uint4 q8 = qr[j];
-        a0 = fmaf(bf_lo(q8.x), bf_lo(k8.x), a0);
-        a1 = fmaf(bf_hi(q8.x), bf_hi(k8.x), a1);
-        a2 = fmaf(bf_lo(q8.y), bf_lo(k8.y), a2);
-        a3 = fmaf(bf_hi(q8.y), bf_hi(k8.y), a3);
-        a0 = fmaf(bf_lo(q8.z), bf_lo(k8.z), a0);
-        a1 = fmaf(bf_hi(q8.z), bf_hi(k8.z), a1);
-        a2 = fmaf(bf_lo(q8.w), bf_lo(k8.w), a2);
-        a3 = fmaf(bf_hi(q8.w), bf_hi(k8.w), a3);
+        fma_bf16x2(a0, a1, q8.x, k8.x);
+        fma_bf16x2(a2, a3, q8.y, k8.y);
+        fma_bf16x2(a0, a1, q8.z, k8.z);
+        fma_bf16x2(a2, a3, q8.w, k8.w);
       }
     }
     float dot = (a0 + a1) + (a2 + a3);
