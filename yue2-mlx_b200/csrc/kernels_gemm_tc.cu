@@ -93,65 +93,73 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // Producer: TMA loads of the A and W slices.
-    int issued = 0;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kTcStages;
-      if (kb >= kTcStages && !tc_wait(&empty[s], unsigned((kb / kTcStages) - 1) & 1u)) {
-        atomicOr(p.error, 64);
-        s_fail = 1;
-        break;
-      }
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[s])),
-                   "r"(kTcTileA + kTcTileB)
-                   : "memory");
-      asm volatile(
-          "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-          "[%2];" ::"r"(tc_smem(sa + s * kTcTileA)),
-          "l"(&tma_a), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(m0)
-          : "memory");
-      asm volatile(
-          "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-          "[%2];" ::"r"(tc_smem(sb + s * kTcTileB)),
-          "l"(&tma_b), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(n0)
-          : "memory");
-      issued = kb + 1;
-    }
-    // Never leave with a copy in flight: wait (bounded) for the last stages issued.
-    for (int kb = issued > kTcStages ? issued - kTcStages : 0; kb < issued; ++kb)
-      tc_wait(&full[kb % kTcStages], unsigned(kb / kTcStages) & 1u);
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer.
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kTcStages;
-      if (!tc_wait(&full[s], unsigned(kb / kTcStages) & 1u)) {
-        atomicOr(p.error, 64);
-        s_fail = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t da = tc_desc(sa + s * kTcTileA), db = tc_desc(sb + s * kTcTileB);
-#pragma unroll
-      for (int k = 0; k < kTcBK / 16; ++k) {
-        const uint32_t acc = (kb | k) != 0;
+  // Lane 0 of warp 0 produces and lane 0 of warp 1 issues the MMAs; the other lanes of
+  // those warps wait for their lane 0 at __syncwarp (parked, not spinning on `done`, which
+  // would take the warp's issue slots from the one lane doing the work).
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer: TMA loads of the A and W slices.
+      int issued = 0;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % kTcStages;
+        if (kb >= kTcStages && !tc_wait(&empty[s], unsigned((kb / kTcStages) - 1) & 1u)) {
+          atomicOr(p.error, 64);
+          s_fail = 1;
+          break;
+        }
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[s])),
+                     "r"(kTcTileA + kTcTileB)
+                     : "memory");
         asm volatile(
-            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(tmem),
-            "l"(da + 2 * k), "l"(db + 2 * k), "r"(kTcIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+            "[%2];" ::"r"(tc_smem(sa + s * kTcTileA)),
+            "l"(&tma_a), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(m0)
             : "memory");
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+            "[%2];" ::"r"(tc_smem(sb + s * kTcTileB)),
+            "l"(&tma_b), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(n0)
+            : "memory");
+        issued = kb + 1;
       }
-      // The slice's smem is free once these MMAs have read it.
+      // Never leave with a copy in flight: wait (bounded) for the last stages issued.
+      for (int kb = issued > kTcStages ? issued - kTcStages : 0; kb < issued; ++kb)
+        tc_wait(&full[kb % kTcStages], unsigned(kb / kTcStages) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer.
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % kTcStages;
+        if (!tc_wait(&full[s], unsigned(kb / kTcStages) & 1u)) {
+          atomicOr(p.error, 64);
+          s_fail = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t da = tc_desc(sa + s * kTcTileA), db = tc_desc(sb + s * kTcTileB);
+  #pragma unroll
+        for (int k = 0; k < kTcBK / 16; ++k) {
+          const uint32_t acc = (kb | k) != 0;
+          asm volatile(
+              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+              " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(tmem),
+              "l"(da + 2 * k), "l"(db + 2 * k), "r"(kTcIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+              : "memory");
+        }
+        // The slice's smem is free once these MMAs have read it.
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         tc_smem(&empty[s]))
+                     : "memory");
+      }
+      // Completes when every MMA issued above has finished (also after a failure).
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       tc_smem(&empty[s]))
+                       tc_smem(&done))
                    : "memory");
     }
-    // Completes when every MMA issued above has finished (also after a failure).
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     tc_smem(&done))
-                 : "memory");
+    __syncwarp();
   }
-
   // Epilogue: warp w owns TMEM lanes (tile rows) 32w..32w+31.
   if (!tc_wait(&done, 0u)) {
     if (lane == 0) atomicOr(p.error, 64);
