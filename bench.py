@@ -181,7 +181,7 @@ def long_context(yar, model_one, weights, rank, world, local, barrier, maxall):
             "parallelism": f"tp{world}", "value": len(toks) / dec, "unit": "tok/s", "e2e": len(toks) / wall,
             "tokens": len(toks), "ms_per_token": 1000 * dec / len(toks), "prefill_s": timing["prefill_seconds"],
             "bytes_per_token_per_gpu": int(per_gpu), "achieved_gbs_per_gpu": achieved, "frac_of_hbm": achieved / peak,
-            "tensor_parallel": timing["tensor_parallel"]}
+            "tensor_parallel": timing["tensor_parallel"], "tp_exchange": timing["tp_exchange"]}
 
 
 def measured_traffic(avg_L: float):

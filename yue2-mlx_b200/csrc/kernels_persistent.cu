@@ -81,14 +81,18 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// The same at system scope: counters that peer GPUs add to, ordering the data they
-// stored into this GPU's memory (over NVLink) before the count.
-__device__ __forceinline__ void red_release_add_sys(int *p, int v) {
-  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// System scope, for the counters of exchanged operations (peer GPUs add to them after
+// storing into this GPU's memory over NVLink). A system-scope fence costs microseconds, so
+// the publisher takes one fence and then adds relaxed to every rank's counter (a release
+// pattern), and a waiter polls relaxed and fences once the count is reached (an acquire
+// pattern).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_relaxed_add_sys(int *p, int v) {
+  asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+__device__ __forceinline__ int ld_relaxed_sys(const int *p) {
   int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -418,17 +422,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   auto stamp = [&](int o, int k) {
     if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
   };
-  // Thread 0 publishes one share of counter idx: to this rank only, or (exchanged
-  // operations under tensor parallelism) to every rank at system scope.
+  // Thread 0 publishes one share of counter idx: to this rank only (GPU scope), or
+  // (exchanged operations under tensor parallelism) to every rank at system scope.
   auto publish = [&](int idx, bool all_ranks) {
-    if (!tp) {
+    if (!tp || !all_ranks) {
       red_release_add(p.ctr + idx, 1);
       return;
     }
-    red_release_add_sys(p.ctr + idx, 1);
-    if (all_ranks)
-      for (int i = 0; i < p.tp_ndst; ++i)
-        red_release_add_sys(reinterpret_cast<int *>(reinterpret_cast<char *>(p.ctr + idx) + s_dst[i]), 1);
+    fence_acq_rel_sys();
+    red_relaxed_add_sys(p.ctr + idx, 1);
+    for (int i = 0; i < p.tp_ndst; ++i)
+      red_relaxed_add_sys(reinterpret_cast<int *>(reinterpret_cast<char *>(p.ctr + idx) + s_dst[i]), 1);
   };
   // One barrier orders every consumer thread's writes before thread 0's release-add, which
   // publishes the CTA's share; the same barrier makes a recorded failure CTA-wide.
@@ -439,11 +443,16 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     if (ctid == 0) publish(idx, all_ranks);
   };
   // Wait until counter idx reaches target; gives up on expiry or once any CTA failed.
-  auto wait_for = [&](int idx, int target) {
+  // `exchanged`: a counter every rank adds to (system scope under tensor parallelism).
+  auto wait_for = [&](int idx, int target, bool exchanged) {
     if (ctid == 0 && !s_bad) {
+      const bool sys = tp && exchanged;
       long long i = 0;
       for (; i < kCounterWaitLimit; ++i) {
-        if ((tp ? ld_acquire_sys(p.ctr + idx) : ld_acquire(p.ctr + idx)) >= target) break;
+        if ((sys ? ld_relaxed_sys(p.ctr + idx) : ld_acquire(p.ctr + idx)) >= target) {
+          if (sys) fence_acq_rel_sys();
+          break;
+        }
         if (ld_acquire(p.error) != 0) {
           i = kCounterWaitLimit;
           break;
@@ -497,7 +506,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     }
   };
   calib(0);
-  wait_for(c_embed, epoch + 1);
+  wait_for(c_embed, epoch + 1, false);
   // This step's row state (activity, position, cos/sin, page table) for the attention units.
   for (int b = 0; b < NB; ++b) attn_row_load<128>(rowst[b], p.ap, b, ctid, kRingConsumers * 32);
   consumer_sync();
@@ -528,7 +537,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     // chunks are ring stages (every consumer warp releases each once).
     float wv[4];
     if (int(blockIdx.x) < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
-    wait_for(c_op(l, 0), (epoch + 1) * all);
+    wait_for(c_op(l, 0), (epoch + 1) * all, false);
     stamp(5 * l + 1, 0);
     {
       DecodeAttnParams ap = p.ap;
@@ -580,7 +589,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     stamp(5 * l + 1, 2);
     // O (+ residual).
     stamp(5 * l + 2, 6);  // wait began
-    wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB * W);
+    wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB * W, true);
     {
       stamp(5 * l + 2, 0);
       const GemvTask t = task(l, 1);
@@ -595,7 +604,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     // gate/up (RMSNorm of x fused, SwiGLU epilogue).
     stamp(5 * l + 3, 6);  // wait began
     ring_norm_w_load(task(l, 2), wn_next, ctid);
-    wait_for(c_op(l, 2), (epoch + 1) * all * W);
+    wait_for(c_op(l, 2), (epoch + 1) * all * W, true);
     {
       stamp(5 * l + 3, 0);
       const GemvTask t = task(l, 2);
@@ -609,7 +618,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     }
     // down (+ residual).
     stamp(5 * l + 4, 6);  // wait began
-    wait_for(c_op(l, 3), (epoch + 1) * all * W);
+    wait_for(c_op(l, 3), (epoch + 1) * all * W, true);
     {
       stamp(5 * l + 4, 0);
       const GemvTask t = task(l, 3);
@@ -625,7 +634,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       stamp(5 * (l + 1), 6);  // the next QKV's wait began
       ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
     }
-    wait_for(c_op(l, 4), (epoch + 1) * all * W);
+    wait_for(c_op(l, 4), (epoch + 1) * all * W, true);
   }
   // Final RMSNorm + phase rows of the LM head.
   {
@@ -660,7 +669,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   // CTA 0 ends the step once every rank's head columns are in (the sampler, launched after
   // this kernel, reads the whole logits rows).
   if (blockIdx.x == 0) {
-    wait_for(c_head, (epoch + 1) * all * W);
+    wait_for(c_head, (epoch + 1) * all * W, true);
     if (ctid == 0) {
       __threadfence();
       atomicExch(p.epoch, epoch + 1);
