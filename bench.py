@@ -349,7 +349,14 @@ def main():
     prefill_launches = 1 + 8 * layers + 1
     traffic = measured_traffic(avg_L)
     bs64 = None if args.no_bs64 else batched_throughput(yar, model, rank, barrier, maxall)
-    long = None if args.no_long else long_context(yar, model, weights, rank, world, local, barrier, maxall)
+    long = None
+    if not args.no_long:
+        # Every rank takes the same path, so a failure here is raised on every rank alike:
+        # it is reported in the line instead of losing the data-parallel measurement.
+        try:
+            long = long_context(yar, model, weights, rank, world, local, barrier, maxall)
+        except Exception as e:
+            long = {"error": f"{type(e).__name__}: {e}"[:300]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
