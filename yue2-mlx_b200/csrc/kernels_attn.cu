@@ -361,6 +361,218 @@ __global__ void __launch_bounds__(256) k_attn_prefill(PrefillAttnParams p) {
 
 static size_t prefill_attn_smem(int D) { return (64 * (D + 1) * 2 + 64 * D + 64 * 65) * sizeof(float); }
 
+// ---------------------------------------------------------------------------------------
+// Causal prefill attention on tensor cores (head_dim 128): the same queries, keys, causal
+// rule and FP32 softmax as k_attn_prefill, computed flash-attention style. Grid
+// (ceil(T/64), heads), 4 warps; warp w owns queries 16w..16w+15 of the tile, held in
+// registers as the A operand of mma.sync m16n8k16 (BF16 in, FP32 accumulate). Per tile of
+// 64 keys (cp.async into rows padded to 272 bytes, two tiles in flight):
+//   S = Q K^T (K rows as the B operand via ldmatrix), scaled and masked, folded into the
+//   running row max / sum (quad shuffles) with exp rescaling of O;
+//   O += P V with P taken from the S accumulators as the A operand, split into BF16 high
+//   and low parts (two MMAs: P keeps ~16 mantissa bits, products within 2^-17 of FP32 P)
+//   and V through ldmatrix.trans.
+// Key rows past the last visible key are zeroed (their scores are masked; V must stay
+// finite under P = 0).
+constexpr int kPfPitch = 128 + 8;                        // BF16 elements per K/V row
+constexpr int kPfTile = 64 * kPfPitch;                   // one K or V tile
+constexpr size_t kPfSmem = size_t(2) * 2 * kPfTile * 2;  // two stages of K and V tiles
+
+__device__ __forceinline__ void mma_bf16_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4_b16(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+__device__ __forceinline__ void ldsm_x4_trans_b16(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3,
+                                                  const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+// (x, y) as a BF16 pair (x in the low half), and the pair of what that rounding left.
+__device__ __forceinline__ void split_bf16_pair(float x, float y, uint32_t &hi, uint32_t &lo) {
+  const uint32_t xh = __float_as_uint(rbf(x)), yh = __float_as_uint(rbf(y));
+  hi = (xh >> 16) | (yh & 0xFFFF0000u);
+  const uint32_t xl = __float_as_uint(rbf(x - __uint_as_float(xh))), yl = __float_as_uint(rbf(y - __uint_as_float(yh)));
+  lo = (xl >> 16) | (yl & 0xFFFF0000u);
+}
+
+__global__ void __launch_bounds__(128) k_attn_prefill_mma(PrefillAttnParams p) {
+  constexpr int D = 128, BQ = 64, BK = 64;
+  extern __shared__ __align__(16) unsigned char pf_raw[];
+  bf16 *tiles = reinterpret_cast<bf16 *>(pf_raw);  // [stage][K | V][64][kPfPitch]
+  const AttnGeom &g = p.g;
+  const int qt = blockIdx.x, h = blockIdx.y, kvh = h / (g.heads / g.kv_heads);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gr = lane >> 2, tq = lane & 3;
+  const int q0 = qt * BQ;
+  const int qlast = min(p.T, q0 + BQ) - 1;
+  const int kend = p.start + qlast + 1;  // keys visible to the tile's last query
+  const int ntiles = (kend + BK - 1) / BK;
+
+  // K and V rows of key tile `kt` into stage `st` (one cp.async group).
+  auto load_tile = [&](int kt, int st) {
+    bf16 *kb = tiles + size_t(st) * 2 * kPfTile, *vb = kb + kPfTile;
+    const int k0 = kt * BK, cc = tid & 15;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = (tid >> 4) + 8 * j, kp = k0 + r;
+      bf16 *kd = kb + r * kPfPitch + cc * 8, *vd = vb + r * kPfPitch + cc * 8;
+      if (kp < kend) {
+        const bf16 *ks = kv_addr(p.pool, g, p.ptab, p.layer, 0, kvh, kp) + cc * 8;
+        const bf16 *vs = ks + g.page_elems;  // the V block follows the K block of the page
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                         __cvta_generic_to_shared(kd))),
+                     "l"(ks)
+                     : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(
+                         __cvta_generic_to_shared(vd))),
+                     "l"(vs)
+                     : "memory");
+      } else {
+        *reinterpret_cast<uint4 *>(kd) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(vd) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_tile(0, 0);
+
+  // This warp's 16 queries as A fragments (rows gr and gr + 8), 8 k-tiles of 16 dims.
+  uint32_t qa[8][4];
+  {
+    const int r0 = q0 + warp * 16 + gr, r1 = r0 + 8;
+    const bf16 *q0p = p.q + (size_t(r0) * g.heads + h) * D, *q1p = p.q + (size_t(r1) * g.heads + h) * D;
+#pragma unroll
+    for (int kt = 0; kt < 8; ++kt) {
+      const int d = kt * 16 + 2 * tq;
+      qa[kt][0] = r0 < p.T ? *reinterpret_cast<const uint32_t *>(q0p + d) : 0u;
+      qa[kt][1] = r1 < p.T ? *reinterpret_cast<const uint32_t *>(q1p + d) : 0u;
+      qa[kt][2] = r0 < p.T ? *reinterpret_cast<const uint32_t *>(q0p + d + 8) : 0u;
+      qa[kt][3] = r1 < p.T ? *reinterpret_cast<const uint32_t *>(q1p + d + 8) : 0u;
+    }
+  }
+  const int qpos0 = p.start + q0 + warp * 16 + gr, qpos1 = qpos0 + 8;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float oa[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) oa[n][0] = oa[n][1] = oa[n][2] = oa[n][3] = 0.f;
+
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int st = kt & 1;
+    // The other stage was last read before the previous tile's closing barrier.
+    if (kt + 1 < ntiles) {
+      load_tile(kt + 1, st ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const bf16 *kb = tiles + size_t(st) * 2 * kPfTile, *vb = kb + kPfTile;
+    const int k0 = kt * BK;
+    // S = Q K^T: 8 n-tiles of 8 keys.
+    float sa[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      sa[n][0] = sa[n][1] = sa[n][2] = sa[n][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {  // 32 dims per ldmatrix.x4
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_b16(b0, b1, b2, b3, kb + (n * 8 + (lane & 7)) * kPfPitch + kk * 32 + (lane >> 3) * 8);
+        mma_bf16_16816(sa[n], qa[2 * kk][0], qa[2 * kk][1], qa[2 * kk][2], qa[2 * kk][3], b0, b1);
+        mma_bf16_16816(sa[n], qa[2 * kk + 1][0], qa[2 * kk + 1][1], qa[2 * kk + 1][2], qa[2 * kk + 1][3], b2, b3);
+      }
+    }
+    // Scale, mask, and fold into the running max / sum of rows gr (0, 1) and gr + 8 (2, 3).
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int kp = k0 + n * 8 + 2 * tq;
+      sa[n][0] = kp <= qpos0 ? sa[n][0] * g.scale : -INFINITY;
+      sa[n][1] = kp + 1 <= qpos0 ? sa[n][1] * g.scale : -INFINITY;
+      sa[n][2] = kp <= qpos1 ? sa[n][2] * g.scale : -INFINITY;
+      sa[n][3] = kp + 1 <= qpos1 ? sa[n][3] * g.scale : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(sa[n][0], sa[n][1]));
+      mx1 = fmaxf(mx1, fmaxf(sa[n][2], sa[n][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = mn0 == -INFINITY ? 1.f : expf(m0 - mn0), c1 = mn1 == -INFINITY ? 1.f : expf(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      sa[n][0] = sa[n][0] == -INFINITY ? 0.f : expf(sa[n][0] - mn0);
+      sa[n][1] = sa[n][1] == -INFINITY ? 0.f : expf(sa[n][1] - mn0);
+      sa[n][2] = sa[n][2] == -INFINITY ? 0.f : expf(sa[n][2] - mn1);
+      sa[n][3] = sa[n][3] == -INFINITY ? 0.f : expf(sa[n][3] - mn1);
+      ps0 += sa[n][0] + sa[n][1];
+      ps1 += sa[n][2] + sa[n][3];
+    }
+    l0 = l0 * c0 + ps0;
+    l1 = l1 * c1 + ps1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      oa[n][0] *= c0;
+      oa[n][1] *= c0;
+      oa[n][2] *= c1;
+      oa[n][3] *= c1;
+    }
+    // O += P V: 4 k-tiles of 16 keys, 16 n-tiles of 8 dims (pairs via ldmatrix.x4.trans).
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t h0, l0b, h1, l1b, h2, l2b, h3, l3b;
+      split_bf16_pair(sa[2 * kk][0], sa[2 * kk][1], h0, l0b);
+      split_bf16_pair(sa[2 * kk][2], sa[2 * kk][3], h1, l1b);
+      split_bf16_pair(sa[2 * kk + 1][0], sa[2 * kk + 1][1], h2, l2b);
+      split_bf16_pair(sa[2 * kk + 1][2], sa[2 * kk + 1][3], h3, l3b);
+      const int vrow = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans_b16(b0, b1, b2, b3, vb + vrow * kPfPitch + np * 16 + (lane >> 4) * 8);
+        mma_bf16_16816(oa[2 * np], h0, h1, h2, h3, b0, b1);
+        mma_bf16_16816(oa[2 * np], l0b, l1b, l2b, l3b, b0, b1);
+        mma_bf16_16816(oa[2 * np + 1], h0, h1, h2, h3, b2, b3);
+        mma_bf16_16816(oa[2 * np + 1], l0b, l1b, l2b, l3b, b2, b3);
+      }
+    }
+    __syncthreads();  // every warp is done with this stage before it is refilled
+  }
+  // Row sums across the quad, then the BF16 outputs.
+  l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 1);
+  l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 2);
+  l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
+  l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 2);
+  const int r0 = q0 + warp * 16 + gr, r1 = r0 + 8;
+  const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int d = n * 8 + 2 * tq;
+    if (r0 < p.T) {
+      bf16 *o = p.out + size_t(r0) * p.out_stride + h * D + d;
+      o[0] = f2bf(oa[n][0] * i0);
+      o[1] = f2bf(oa[n][1] * i0);
+    }
+    if (r1 < p.T) {
+      bf16 *o = p.out + size_t(r1) * p.out_stride + h * D + d;
+      o[0] = f2bf(oa[n][2] * i1);
+      o[1] = f2bf(oa[n][3] * i1);
+    }
+  }
+}
+
 void configure_attn_kernels() {
   YAR_CUDA(cudaFuncSetAttribute(k_attn_decode<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(attn_decode_dyn_smem<128>())));
@@ -372,6 +584,7 @@ void configure_attn_kernels() {
                                 int(attn_decode_dyn_smem<64>())));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(prefill_attn_smem(128))));
+  YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmem)));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(prefill_attn_smem(64))));
 }
@@ -389,12 +602,11 @@ void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int sta
   p.out = s.pattn + m.tp.q_row0;
   p.out_stride = m.full.qdim();
   const int D = m.d.head_dim;
-  const size_t smem = prefill_attn_smem(D);
   dim3 grid((T + 63) / 64, m.d.heads);
   if (D == 128)
-    k_attn_prefill<128><<<grid, 256, smem, st>>>(p);
+    k_attn_prefill_mma<<<grid, 128, kPfSmem, st>>>(p);
   else
-    k_attn_prefill<64><<<grid, 256, smem, st>>>(p);
+    k_attn_prefill<64><<<grid, 256, prefill_attn_smem(D), st>>>(p);
   YAR_CUDA(cudaGetLastError());
 }
 
