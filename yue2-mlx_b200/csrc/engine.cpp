@@ -196,8 +196,19 @@ static void project_cols(const Model &m, Session &s, const bf16 *in, int in_stri
   const bf16 *head = m.lm_head + size_t(pr.row0) * H;
   if (main_end > c0) {
     if (normed) {
+      // Even rows as GEMMs: the whole 128-column blocks (aligned to absolute phase columns;
+      // tensor-parallel ranges start on such a block) on tcgen05, never split along K, and
+      // the last partial block on mma.sync — so a column's kernel, hence its bits, does not
+      // depend on which range (rank) holds it.
       const int n_even = pr.n_main & ~1, g_end = std::min(main_end, n_even);
-      if (g_end > c0) launch_gemm(in, n_rows, H, head + size_t(c0) * H, g_end - c0, out, stride, kEpiStore, st);
+      int t0 = (c0 + 127) / 128 * 128, t1 = g_end / 128 * 128;
+      if (t1 <= t0 || !gemm_tc_supported(in, n_rows, H, head + size_t(t0) * H, t1 - t0, out + (t0 - c0), stride))
+        t0 = t1 = g_end;
+      if (t0 > c0) launch_gemm(in, n_rows, H, head + size_t(c0) * H, t0 - c0, out, stride, kEpiStore, st);
+      if (t1 > t0)
+        launch_gemm_tc(in, n_rows, H, head + size_t(t0) * H, t1 - t0, out + (t0 - c0), stride, kEpiStore, s.d_error,
+                       nullptr, 0, st, -1);
+      if (g_end > t1) launch_gemm(in, n_rows, H, head + size_t(t1) * H, g_end - t1, out + (t1 - c0), stride, kEpiStore, st);
       if (n_even < main_end)
         launch_gemv(head + size_t(n_even) * H, 1, H, in, in_stride, nullptr, m.d.eps, out + (n_even - c0), stride,
                     kEpiStore, n_rows, s.d_error, m.sm_count, st);

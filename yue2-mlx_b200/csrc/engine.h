@@ -100,8 +100,9 @@ void launch_tp_pack(const bf16 *buf, int stride, int col0, int n, int n_rows, bf
 void launch_tp_unpack(const bf16 *recv, int world, int n_rows, int n, int width, bf16 *buf, int stride,
                       cudaStream_t st);
 // LM-head columns per rank under tensor parallelism: the phase width split evenly, rounded
-// up to 8 columns.
-inline int tp_head_slice(int width, int world) { return ((width + world - 1) / world + 7) / 8 * 8; }
+// up to 128 columns, so every 128-column block of the head (one tcgen05 tile in the batched
+// projection) lies within one rank's range and is computed as on one GPU.
+inline int tp_head_slice(int width, int world) { return ((width + world - 1) / world + 127) / 128 * 128; }
 
 // Phase projection of the LM head: rows [row0, row0 + n_main) and, optionally, one extra
 // row mapped to local index n_main (native/src/ar.cpp:302-323).
@@ -147,8 +148,9 @@ void launch_gemm(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int
 // Prefill linears on tcgen05 (kernels_gemm_tc.cu); `error` receives expired-wait flags.
 bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const bf16 *C, int ldc);
 // `ws` (ws_floats FP32 values, may be null) lets small-M shapes split K across CTAs; the
-// split count is chosen for `split_n` columns (0: N), so a tensor-parallel rank's block of
-// N / world columns splits K, and adds its partial sums, as the whole N does on one GPU.
+// split count is chosen for `split_n` columns (0: N; negative: never split), so a
+// tensor-parallel rank's block of N / world columns splits K, and adds its partial sums,
+// as the whole N does on one GPU.
 void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
                     float *ws, size_t ws_floats, cudaStream_t st, int split_n = 0);
 void configure_gemm_tc_kernels();

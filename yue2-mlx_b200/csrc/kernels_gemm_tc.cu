@@ -327,10 +327,10 @@ void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, 
   const CUtensorMap ma = kmajor_map(A, M, K, kTcBM), mb = kmajor_map(W, N, K, kTcBN);
   // Split K across CTAs while the tile grid leaves SMs idle (small M: batched decode).
   const int NS = split_n > 0 ? split_n : N;
-  if (NS < N) throw Error("ValueError", "split_n below N");
+  if (split_n > 0 && NS < N) throw Error("ValueError", "split_n below N");
   const int tiles = (NS / kTcBN) * ((M + kTcBM - 1) / kTcBM), KB = K / kTcBK;
   int splits = 1;
-  while (ws && splits < 8 && tiles * splits < 120 && KB % (splits * 2) == 0 &&
+  while (ws && split_n >= 0 && splits < 8 && tiles * splits < 120 && KB % (splits * 2) == 0 &&
          size_t(splits * 2) * M * NS <= ws_floats)
     splits *= 2;
   TcParams p{C, M, N, K, ldc, error, splits > 1 ? ws : nullptr, KB / splits};
