@@ -96,13 +96,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // Lane 0 of warp 0 produces and lane 0 of warp 1 issues the MMAs; the other lanes of
   // those warps wait for their lane 0 at __syncwarp (parked, not spinning on `done`, which
   // would take the warp's issue slots from the one lane doing the work).
+  pdl_launch_dependents();
   if (warp == 0) {
     if (lane == 0) {
-      // Producer: TMA loads of the A and W slices.
-      int issued = 0;
-      for (int kb = 0; kb < KB; ++kb) {
+      // Producer: TMA loads of the A and W slices. The first stages' weight slices are
+      // requested before waiting for the kernel that writes A (programmatic launch: the
+      // weights are constants); their A slices, and everything after, once it is done.
+      auto load_a = [&](int kb, int s) {
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+            "[%2];" ::"r"(tc_smem(sa + s * kTcTileA)),
+            "l"(&tma_a), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(m0)
+            : "memory");
+      };
+      auto load_b = [&](int kb, int s) {
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+            "[%2];" ::"r"(tc_smem(sb + s * kTcTileB)),
+            "l"(&tma_b), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(n0)
+            : "memory");
+      };
+      const int pre = KB < kTcStages ? KB : kTcStages;
+      for (int kb = 0; kb < pre; ++kb) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[kb])),
+                     "r"(kTcTileA + kTcTileB)
+                     : "memory");
+        load_b(kb, kb);
+      }
+      pdl_wait();
+      for (int kb = 0; kb < pre; ++kb) load_a(kb, kb);
+      int issued = pre;
+      for (int kb = pre; kb < KB; ++kb) {
         const int s = kb % kTcStages;
-        if (kb >= kTcStages && !tc_wait(&empty[s], unsigned((kb / kTcStages) - 1) & 1u)) {
+        if (!tc_wait(&empty[s], unsigned((kb / kTcStages) - 1) & 1u)) {
           atomicOr(p.error, 64);
           s_fail = 1;
           break;
@@ -110,16 +136,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(&full[s])),
                      "r"(kTcTileA + kTcTileB)
                      : "memory");
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-            "[%2];" ::"r"(tc_smem(sa + s * kTcTileA)),
-            "l"(&tma_a), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(m0)
-            : "memory");
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-            "[%2];" ::"r"(tc_smem(sb + s * kTcTileB)),
-            "l"(&tma_b), "r"(tc_smem(&full[s])), "r"((kb0 + kb) * kTcBK), "r"(n0)
-            : "memory");
+        load_a(kb, s);
+        load_b(kb, s);
         issued = kb + 1;
       }
       // Never leave with a copy in flight: wait (bounded) for the last stages issued.
@@ -160,7 +178,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
   }
-  // Epilogue: warp w owns TMEM lanes (tile rows) 32w..32w+31.
+  // Epilogue: warp w owns TMEM lanes (tile rows) 32w..32w+31. (Every thread has waited for
+  // the predecessor kernel before touching C.)
+  pdl_wait();
   if (!tc_wait(&done, 0u)) {
     if (lane == 0) atomicOr(p.error, 64);
     s_fail = 1;
@@ -235,6 +255,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // per 8 consecutive columns of a row.
 template <int EPI>
 __global__ void __launch_bounds__(256) k_splitk_reduce(const float *ws, int splits, int M, int N, bf16 *C, int ldc) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long idx = blockIdx.x * 256ll + threadIdx.x, groups = N / 8;
   if (idx >= (long long)M * groups) return;
   const int row = int(idx / groups), col = int(idx % groups) * 8;
@@ -334,24 +356,35 @@ void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, 
          size_t(splits * 2) * M * NS <= ws_floats)
     splits *= 2;
   TcParams p{C, M, N, K, ldc, error, splits > 1 ? ws : nullptr, KB / splits};
-  const dim3 grid(N / kTcBN, (M + kTcBM - 1) / kTcBM, splits);
+  // Programmatic launches: each kernel may start while its predecessor finishes and waits
+  // (griddepcontrol.wait) before reading its outputs or writing anything.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(N / kTcBN, (M + kTcBM - 1) / kTcBM, splits);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (epilogue == kEpiSwiGLU)
-    k_gemm_tc<kEpiSwiGLU><<<grid, kTcThreads, kTcSmem, st>>>(ma, mb, p);
+    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<kEpiSwiGLU>, ma, mb, p));
   else if (epilogue == kEpiResidual)
-    k_gemm_tc<kEpiResidual><<<grid, kTcThreads, kTcSmem, st>>>(ma, mb, p);
+    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<kEpiResidual>, ma, mb, p));
   else
-    k_gemm_tc<kEpiStore><<<grid, kTcThreads, kTcSmem, st>>>(ma, mb, p);
-  YAR_CUDA(cudaGetLastError());
+    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<kEpiStore>, ma, mb, p));
   if (splits > 1) {
     const long long threads = (long long)M * (N / 8);
-    const unsigned blocks = unsigned((threads + 255) / 256);
+    cfg.gridDim = dim3(unsigned((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
     if (epilogue == kEpiSwiGLU)
-      k_splitk_reduce<kEpiSwiGLU><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
+      YAR_CUDA(cudaLaunchKernelEx(&cfg, k_splitk_reduce<kEpiSwiGLU>, (const float *)ws, splits, M, N, C, ldc));
     else if (epilogue == kEpiResidual)
-      k_splitk_reduce<kEpiResidual><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
+      YAR_CUDA(cudaLaunchKernelEx(&cfg, k_splitk_reduce<kEpiResidual>, (const float *)ws, splits, M, N, C, ldc));
     else
-      k_splitk_reduce<kEpiStore><<<blocks, 256, 0, st>>>(ws, splits, M, N, C, ldc);
-    YAR_CUDA(cudaGetLastError());
+      YAR_CUDA(cudaLaunchKernelEx(&cfg, k_splitk_reduce<kEpiStore>, (const float *)ws, splits, M, N, C, ldc));
   }
 }
 

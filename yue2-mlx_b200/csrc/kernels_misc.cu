@@ -66,6 +66,8 @@ void launch_embed_tokens(const bf16 *embed, const int *ids, int T, int H, bf16 *
 __global__ void __launch_bounds__(256) k_rmsnorm_rows(const bf16 *x, const bf16 *w, int H, float eps,
                                                       bf16 *out) {
   __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();  // programmatic launch: x comes from the preceding kernel
   const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bf16 *xr = x + size_t(t) * H;
   float ss = 0.f;
@@ -86,8 +88,16 @@ __global__ void __launch_bounds__(256) k_rmsnorm_rows(const bf16 *x, const bf16 
 
 void launch_rmsnorm_rows(const bf16 *x, const bf16 *w, int T, int H, float eps, bf16 *out,
                          cudaStream_t st) {
-  k_rmsnorm_rows<<<T, 256, 0, st>>>(x, w, H, eps, out);
-  YAR_CUDA(cudaGetLastError());
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(T);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  YAR_CUDA(cudaLaunchKernelEx(&cfg, k_rmsnorm_rows, x, w, H, eps, out));
 }
 
 }  // namespace yar
