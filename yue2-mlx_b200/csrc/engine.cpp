@@ -417,7 +417,7 @@ static void decode_forward(Session &s, int n_rows, int phase) {
     const LayerWeights &w = m.layers[l];
     launch_gemv(w.qkv, d.qkv_rows(), H, s.x, H, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows, s.d_error,
                 m.sm_count, st);
-    launch_attn_decode(m, s, l, n_rows, st);
+    launch_attn_decode(m, s, l, n_rows, st, decode_max_splits(m, s, n_rows));
     tp_gather(m, s, s.attn, n_rows, ls.Qf, ls.Ql);
     launch_gemv(w.o, ls.Hs, ls.Qf, s.attn, ls.Qf, nullptr, d.eps, s.x + ls.h0, H, kEpiResidual, n_rows, s.d_error,
                 m.sm_count, st);

@@ -245,4 +245,13 @@ struct Session {
 
 constexpr int kCandCap = 2048;
 
+// Splits per (row, kv head) of the decode attention for one or two rows (the persistent
+// kernel and the per-operation path alike): about one unit per SM, so a long context runs
+// in one round of longer units instead of two rounds of short ones. Counted with the whole
+// model's KV heads, so tensor-parallel ranks split each head's positions as one GPU does.
+inline int decode_max_splits(const Model &m, const Session &s, int n_rows) {
+  const int per = m.sm_count / (m.full.kv_heads * (n_rows > 0 ? n_rows : 1));
+  return per < 1 ? 1 : per < s.max_splits ? per : s.max_splits;
+}
+
 }  // namespace yar

@@ -758,7 +758,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   a.g.eps = d.eps;
   a.g.scale = float(1.0 / std::sqrt(double(d.head_dim)));
   a.layer = 0;
-  a.max_splits = s.max_splits;
+  a.max_splits = decode_max_splits(m, s, n_rows);
   a.pool = s.kv;
   a.page_table = s.d_page_table;
   a.cur_pos = s.d_cur_pos;
