@@ -344,9 +344,11 @@ def main():
     achieved = bytes_per_step / per_token_s / 1e9
     layers = 28
     # Per decoded token: the persistent decode kernel (embedding, 28 layers, LM head) and
-    # the sampler. Per song: the prefill's embedding, 8 kernels per layer, the head GEMV.
+    # the sampler. Per song: the prefill's embedding, 10 kernels per layer, the head GEMV.
     launches_per_token = 2
-    prefill_launches = 1 + 8 * layers + 1
+    # Prefill of 512 tokens per layer: RMSNorm, QKV GEMM, q/k post, attention, O GEMM and
+    # its split-K reduction, RMSNorm, gate/up GEMM, down GEMM and its reduction.
+    prefill_launches = 1 + 10 * layers + 1
     traffic = measured_traffic(avg_L)
     bs64 = None if args.no_bs64 else batched_throughput(yar, model, rank, barrier, maxall)
     long = None
