@@ -56,6 +56,7 @@ __device__ __forceinline__ int local_to_native(int loc, int phase) {
 
 __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   __shared__ uint64_t cand[kCandCap];
+  __shared__ int list_n;
   __shared__ float ev[kCandCap];
   __shared__ int tot[256];
   __shared__ float pv[kCandCap];
@@ -235,16 +236,23 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     uint32_t pre = 0;
     int rem = k;
     int *wh = hist + warp * 256;
+    // After two digits only the rows sharing the found 16-bit prefix can hold the k-th key:
+    // their indices are listed (in `cand`, idle until the candidates are gathered) and the
+    // last two passes count that list instead of every row.
+    int *list = reinterpret_cast<int *>(cand);
+    constexpr int kListCap = kCandCap * 2;
+    int m = n;
+    bool listed = false;
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
       for (int b = lane; b < 256; b += 32) wh[b] = 0;
       __syncwarp();
       const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      for (int base = warp * 32; base < n; base += kSampThreads) {
-        const int i = base + lane;
+      for (int base = warp * 32; base < m; base += kSampThreads) {
+        const int j = base + lane;
         uint32_t bin = 0xFFFFFFFFu;
-        if (i < n) {
-          const uint32_t key = f32_order_key(s[i]);
+        if (j < m) {
+          const uint32_t key = f32_order_key(s[listed ? list[j] : j]);
           if ((key & hmask) == (pre & hmask)) bin = (key >> shift) & 255u;
         }
         const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
@@ -289,6 +297,18 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       __syncthreads();
       pre = prefix_s;
       rem = kth_rem;
+      if (pass == 1) {
+        if (tid == 0) list_n = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += kSampThreads)
+          if ((f32_order_key(s[i]) >> 16) == (pre >> 16)) {
+            const int slot = atomicAdd(&list_n, 1);
+            if (slot < kListCap) list[slot] = i;
+          }
+        __syncthreads();
+        listed = list_n <= kListCap;
+        m = listed ? list_n : n;
+      }
       stamp(4 + (pass < 2 ? pass : 2));
     }
     const float thr = f32_from_order_key(prefix_s);
