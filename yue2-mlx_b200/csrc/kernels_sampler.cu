@@ -56,7 +56,7 @@ __device__ __forceinline__ int local_to_native(int loc, int phase) {
 
 __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   __shared__ uint64_t cand[kCandCap];
-  __shared__ int list_n;
+  __shared__ int list_n, kth_cnt;
   __shared__ float ev[kCandCap];
   __shared__ int tot[256];
   __shared__ float pv[kCandCap];
@@ -236,13 +236,15 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     uint32_t pre = 0;
     int rem = k;
     int *wh = hist + warp * 256;
-    // After two digits only the rows sharing the found 16-bit prefix can hold the k-th key:
-    // their indices are listed (in `cand`, idle until the candidates are gathered) and the
-    // last two passes count that list instead of every row.
+    // Once the rows sharing the found prefix fit the list (their count is the selected
+    // bin's), only they can hold the k-th key: their indices are listed (in `cand`, idle
+    // until the candidates are gathered) and the remaining passes count the list instead of
+    // every row.
     int *list = reinterpret_cast<int *>(cand);
     constexpr int kListCap = kCandCap * 2;
     int m = n;
     bool listed = false;
+    if (tid == 0) kth_cnt = n;  // (set by every pass; read after its barriers)
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
       for (int b = lane; b < 256; b += 32) wh[b] = 0;
@@ -291,23 +293,21 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
             acc += cnt[j];
           }
           kth_rem = rem - acc;
+          kth_cnt = tot[b];
           prefix_s = pre | (uint32_t(b) << shift);
         }
       }
       __syncthreads();
       pre = prefix_s;
       rem = kth_rem;
-      if (pass == 1) {
+      if (!listed && pass < 3 && kth_cnt <= kListCap) {
         if (tid == 0) list_n = 0;
         __syncthreads();
         for (int i = tid; i < n; i += kSampThreads)
-          if ((f32_order_key(s[i]) >> 16) == (pre >> 16)) {
-            const int slot = atomicAdd(&list_n, 1);
-            if (slot < kListCap) list[slot] = i;
-          }
+          if ((f32_order_key(s[i]) >> shift) == (pre >> shift)) list[atomicAdd(&list_n, 1)] = i;
         __syncthreads();
-        listed = list_n <= kListCap;
-        m = listed ? list_n : n;
+        listed = true;
+        m = list_n;
       }
       stamp(4 + (pass < 2 ? pass : 2));
     }
