@@ -60,6 +60,9 @@ def test_head_slices_cover_every_column_once(yar, width, world):
     for r in range(world):
         b, e = yar.tp_head_slice(width, r, world)
         assert 0 <= b <= e <= width
+        # Ranges start on a 128-column block (a whole tcgen05 tile of the batched head stays
+        # within one rank, computed as on one GPU).
+        assert b % 128 == 0 or b == width
         seen[b:e] += 1
     assert (seen == 1).all()
 
