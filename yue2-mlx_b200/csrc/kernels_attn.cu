@@ -231,8 +231,9 @@ void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int
   YAR_CUDA(cudaGetLastError());
 }
 
-// Causal prefill attention over the row's cache positions [0, start + T): grid
-// (ceil(T/64), heads), 256 threads, FP32 tiles of 64 queries x 64 keys in shared memory.
+// Causal prefill attention over the row's cache positions [0, start + T) for head_dim 64
+// (head_dim 128 runs k_attn_prefill_mma below): grid (ceil(T/64), heads), 256 threads,
+// FP32 tiles of 64 queries x 64 keys in shared memory.
 // Thread t owns queries 4*(t/16) .. +3 and, for scores, keys 4*(t%16) .. +3; for the
 // output, dims (D/16)*(t%16) .. +D/16-1.
 struct PrefillAttnParams {
@@ -582,8 +583,6 @@ void configure_attn_kernels() {
                                 int(attn_decode_dyn_smem<64>())));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_decode<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(attn_decode_dyn_smem<64>())));
-  YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(prefill_attn_smem(128))));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmem)));
   YAR_CUDA(cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(prefill_attn_smem(64))));
