@@ -9,9 +9,15 @@ N > 1 runs under torchrun, one rank per GPU, each rank an independent song (data
 parallel, no collective on the data path; NCCL only for the barrier and the max-reduce
 of the timings). Prints one JSON line on rank 0.
 
-Two more workloads are reported under their own keys of the same line: "bs64" (config
-5: 64 independent requests per GPU, data parallel) and "long_context" (config 4: one
-9000-position song, tensor-parallel across all N ranks with the NCCL exchange steps).
+More workloads are reported under their own keys of the same line: "cfg" (config 3: one
+classifier-free-guidance song per GPU, conditional prompt 1024 / unconditional 64, scale
+1.5, 3000 tokens), "bs64" (config 5: 64 independent requests per GPU, data parallel) and
+"long_context" (config 4: one 9000-position song, tensor-parallel across all N ranks).
+
+`--impl reference` times the CPU restatement of the reference's AR path (oracle/, a numpy
+port: the reference's own AR engine is Apple-only MLX) decoding the same config-2 song on
+all host threads: the whole 28-layer model on the bench's own weights, the semantic head
+and the sampler, a bounded number of decode steps per bench step.
 """
 from __future__ import annotations
 
@@ -30,6 +36,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+METRIC = "AR decode tok/s (bs1/GPU; bs64 box-wide) and % of HBM roofline"
 PROMPT, DECODE = 512, 400
 SAMPLING = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50,
                 min_tokens=DECODE, max_tokens=DECODE)
@@ -108,37 +115,83 @@ class Clocks:
 BS64_REQUESTS, BS64_DECODE = 64, 1024
 
 
-def batched_throughput(yar, model, rank, barrier, maxall):
-    """Config 5 on each GPU: 64 independent requests, prompt lengths uniform in [256, 2048]
-    (seeded), 1024 sampled tokens each (top-k 50 with per-request seeds, fixed length), all
-    decoded together by ``generate_batch``. Value = decoded tokens over the device time of
-    the decode loop, max over ranks; e2e includes the 64 prefills."""
+def batched_throughput(yar, model, rank, barrier, maxall, per_gpu: int, label: str, rows: int = 0,
+                       n_requests: int = 0, lengths=None):
+    """Config 5 on each GPU: `n_requests` (default `per_gpu`) independent requests served by
+    continuous batching on `rows` rows (default: one row per request) — prompt lengths
+    uniform in [256, 2048] (seeded per rank), top-k 50 with per-request seeds, fixed lengths
+    (1024 tokens, or `lengths` = (lo, hi) drawn per request). Value = decoded tokens over
+    the device time of the decode loop (max over ranks) x ranks; e2e includes the prefills
+    (a refilled row's prefill runs between decode chunks)."""
     rng = np.random.default_rng(5000 + rank)
-    smp = yar.Sampling(**dict(SAMPLING, min_tokens=BS64_DECODE, max_tokens=BS64_DECODE))
-    warm = yar.Sampling(**dict(SAMPLING, min_tokens=16, max_tokens=16))
-    lens = rng.integers(256, 2049, BS64_REQUESTS)
+    n_req = n_requests or per_gpu
+    rows = rows or n_req
+    lens = rng.integers(256, 2049, n_req)
     prompts = [rng.integers(0, 184704, int(n)).astype(np.int32) for n in lens]
-    seeds = [int(x) for x in rng.integers(0, 2**62, BS64_REQUESTS)]
-    s = model.session(max_rows=BS64_REQUESTS, max_ctx=2048 + BS64_DECODE)
-    s.generate_batch([p[:256] for p in prompts], warm, seeds, phase="semantic")  # capture + first use
+    seeds = [int(x) for x in rng.integers(0, 2**62, n_req)]
+    outs = ([BS64_DECODE] * n_req if lengths is None else
+            [int(x) for x in rng.integers(lengths[0], lengths[1] + 1, n_req)])
+    smps = [yar.Sampling(**dict(SAMPLING, min_tokens=o, max_tokens=o)) for o in outs]
+    warm = yar.Sampling(**dict(SAMPLING, min_tokens=16, max_tokens=16))
+    s = model.session(max_rows=rows, max_ctx=2048 + max(outs))
+    s.generate_requests([p[:256] for p in prompts[:rows]], [warm] * rows, seeds[:rows], phase="semantic",
+                        slots=rows)  # capture + first use
     barrier()
     t0 = time.perf_counter()
-    toks, timing, _ = s.generate_batch(prompts, smp, seeds, phase="semantic")
+    toks, timing, _ = s.generate_requests(prompts, smps, seeds, phase="semantic", slots=rows)
     wall = time.perf_counter() - t0
     s.close()
     n = sum(len(t) for t in toks)
     dec = maxall(timing["decode_device_ms"] / 1000.0)
     wall = maxall(wall)
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    avg_L = float(np.mean(lens)) + BS64_DECODE / 2
-    step_bytes_b = 28 * LAYER_BYTES + NORM_BYTES + HEAD_BYTES + BS64_REQUESTS * (EMBED_BYTES + KV_BYTES_PER_POS * (avg_L + 1))
+    steps = timing["decode_steps"]
+    avg_L = float(np.mean(lens)) + float(np.mean(outs)) / 2
+    step_bytes_b = 28 * LAYER_BYTES + NORM_BYTES + HEAD_BYTES + rows * (EMBED_BYTES + KV_BYTES_PER_POS * (avg_L + 1))
     peak, _ = peaks()
-    achieved = step_bytes_b / (dec / BS64_DECODE) / 1e9
-    return {"workload": "config5: 64 requests per GPU, prompts U[256,2048], 1024 tokens each, top-k 50",
+    achieved = step_bytes_b / (dec / steps) / 1e9
+    return {"workload": label, "requests_per_gpu": n_req, "rows_per_gpu": rows,
             "value": n * world / dec, "unit": "tok/s", "e2e": n * world / wall,
-            "prefill_s": timing["prefill_seconds"], "ms_per_step": 1000 * dec / BS64_DECODE,
-            "tokens": n * world, "bytes_per_step": int(step_bytes_b), "achieved_gbs": achieved,
-            "frac_of_hbm": achieved / peak, "forward": timing["forward"]}
+            "prefill_s": timing["prefill_seconds"], "ms_per_step": 1000 * dec / steps, "decode_steps": steps,
+            "refills": timing["refills"], "tokens": n * world, "bytes_per_step": int(step_bytes_b),
+            "achieved_gbs": achieved, "frac_of_hbm": achieved / peak, "forward": timing["forward"]}
+
+
+CFG_COND, CFG_UNCOND, CFG_DECODE, CFG_SCALE = 1024, 64, 3000, 1.5
+
+
+def cfg_song(yar, model, rank, barrier, maxall):
+    """Config 3 on each GPU: one classifier-free-guidance song — conditional prompt of 1024
+    random ids, unconditional prompt of 64, guidance scale 1.5, 3000 sampled semantic tokens
+    (fixed length) — both branches decoded together as one two-row step per token (the
+    weights are read once for both rows). Value = song tokens over the decode loop's device
+    time, max over ranks; e2e = song tokens over the wall time of the generate call (both
+    prefills, host copies and the token read-back included)."""
+    rng = np.random.default_rng(3000 + rank)
+    cond = rng.integers(0, 184704, CFG_COND).astype(np.int32)
+    uncond = rng.integers(0, 184704, CFG_UNCOND).astype(np.int32)
+    s = model.session(max_rows=2, max_ctx=CFG_COND + CFG_DECODE + 8)
+    s.generate(cond[:256], yar.Sampling(**dict(SAMPLING, min_tokens=32, max_tokens=32)), seed=1, phase="semantic",
+               negative=uncond, cfg_scale=CFG_SCALE)
+    barrier()
+    smp = yar.Sampling(**dict(SAMPLING, min_tokens=CFG_DECODE, max_tokens=CFG_DECODE))
+    t0 = time.perf_counter()
+    toks, timing, _ = s.generate(cond, smp, seed=2, phase="semantic", negative=uncond, cfg_scale=CFG_SCALE)
+    wall = time.perf_counter() - t0
+    s.close()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    dec, wall = maxall(timing["decode_device_ms"] / 1000.0), maxall(wall)
+    # Per step: the weights once, both rows' KV (average visible lengths over the song).
+    kv_pos = (CFG_COND + CFG_DECODE / 2) + (CFG_UNCOND + CFG_DECODE / 2)
+    step_b = 28 * LAYER_BYTES + NORM_BYTES + HEAD_BYTES + 2 * EMBED_BYTES + KV_BYTES_PER_POS * (kv_pos + 2)
+    peak, _ = peaks()
+    achieved = step_b / (dec / len(toks)) / 1e9
+    return {"workload": "config3: one CFG song per GPU, cond prompt 1024 / uncond 64 random ids, scale 1.5, "
+                        "3000 semantic tokens, T1.0 top-k50 top-p0.93",
+            "value": len(toks) * world / dec, "unit": "tok/s", "e2e": len(toks) * world / wall,
+            "tokens": len(toks) * world, "ms_per_token": 1000 * dec / len(toks), "prefill_s": timing["prefill_seconds"],
+            "bytes_per_step": int(step_b), "achieved_gbs": achieved, "frac_of_hbm": achieved / peak,
+            "cfg_branches": timing.get("cfg_branches")}
 
 
 LONG_PROMPT, LONG_TOTAL = 2048, 9000
@@ -207,54 +260,84 @@ def ensure_weights(rank: int, world: int, barrier) -> str:
     return d
 
 
-def cpu_decode_sample(seconds_budget: float = 20.0, layers_timed: int = 2):
-    """Oracle (numpy) decode tok/s at config-2 positions on this host, bounded: a prefix
-    of `layers_timed` decoder layers plus the semantic head is run for real (512-token
-    prefill, then decode steps), and the per-token time is scaled to 28 layers. Only the
-    embedding rows the sample reads and the semantic LM-head rows are materialized."""
-    import dataclasses
-    synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
-    from oracle import ar_oracle as ora
-    dims = dataclasses.replace(synth.PINNED, layers=layers_timed)
-    # Token values do not change the timing; drawing them from two narrow id ranges keeps
-    # the embedding rows to synthesize to a few generator blocks.
-    rng = np.random.default_rng(0)
-    prompt = rng.integers(0, 4096, PROMPT).tolist()
-    decode_ids = rng.integers(151853, 151853 + 1024, 64).tolist()
-    tensors = {}
-    for i, (name, shape) in enumerate(synth.tensor_specs(synth.PINNED)):
-        if name not in {n for n, _ in synth.tensor_specs(dims)}:
-            continue
-        if name == "model.embed_tokens.weight":
-            t = np.zeros(shape, np.float32)  # untouched pages cost nothing
-            for r0, r1 in ((0, 4096), (151853, 151853 + 1024)):
-                t[r0:r1] = synth.bf16_bits_to_f32(synth.tensor_bits(shape, i, 0, 0.02, 0.0, rows=(r0, r1)))
-        elif name == "lm_head.weight":
-            t = np.zeros(shape, np.float32)
-            r0, r1 = 151852, 151853 + 32768
-            t[r0:r1] = synth.bf16_bits_to_f32(synth.tensor_bits(shape, i, 0, 0.02, 0.0, rows=(r0, r1)))
-        else:
-            t = synth.bf16_bits_to_f32(synth.tensor_bits(shape, i, 0, 0.02, 0.0))
-        tensors[name] = t
-    model = ora.OracleAR(tensors, dims, bf16=True, prerounded=True)
-    cache = model.new_cache(PROMPT + 64)
-    model.forward(prompt, cache)
-    t_layers, t_head, n = 0.0, 0.0, 0
-    start = time.perf_counter()
-    while n < 64 and time.perf_counter() - start < seconds_budget:
+class CpuDecoder:
+    """The CPU restatement of the reference's AR path (oracle/ar_oracle.py + the sampler
+    oracle) decoding config 2 on the host cores: every one of the 28 layers on the bench's
+    own weights (BF16 values held as float32, float32 BLAS on every host thread), the
+    semantic head rows and the sampler, after a 512-token prefill. The embedding rows are
+    formed from the BF16 bits as they are looked up."""
+
+    def __init__(self, weights_dir: str, threads: int):
+        import threadpoolctl
+        synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
+        from oracle import ar_oracle as ora
+        from oracle import sampler_oracle as so
+        self.ora, self.so = ora, so
+        self.limits = threadpoolctl.threadpool_limits(threads)  # torchrun sets OMP_NUM_THREADS=1
+        self.threads = threads
+        bits = synth.read_safetensors(os.path.join(weights_dir, "ar-bf16.safetensors"))
+
+        class EmbedRows:
+            def __init__(self, b):
+                self.b = b
+
+            def __getitem__(self, ids):
+                return ora.bf16_from_bits(self.b[ids])
+
+        tensors = {}
+        for name, arr in bits.items():
+            if name == "model.embed_tokens.weight":
+                tensors[name] = EmbedRows(arr)
+            elif name == "lm_head.weight":
+                t = np.zeros(arr.shape, np.float32)  # untouched pages are never materialized
+                r0, r1 = ora.MUSIC_END, ora.CODEC_OFFSET + ora.CODEC_SIZE
+                t[r0:r1] = ora.bf16_from_bits(arr[r0:r1])
+                tensors[name] = t
+            else:
+                tensors[name] = ora.bf16_from_bits(arr)
+        synth_dims = synth.PINNED
+        self.model = ora.OracleAR(tensors, synth_dims, bf16=True, prerounded=True)
+        rng = np.random.default_rng(1000)
+        self.prompt = rng.integers(0, 184704, PROMPT).tolist()
+        self.cache = self.model.new_cache(PROMPT + DECODE)
         t0 = time.perf_counter()
-        h = model.forward([decode_ids[n]], cache)
-        t1 = time.perf_counter()
-        model.project(h[-1], "semantic")
-        t2 = time.perf_counter()
-        t_layers += t1 - t0
-        t_head += t2 - t1
+        h = self.model.forward(self.prompt, self.cache)
+        self.prefill_s = time.perf_counter() - t0
+        self.logits = self.model.project(h[-1], "semantic")[0]
+        self.history: list[int] = []
+        self.decoded = 0
+
+    def decode(self, n: int) -> float:
+        """Sample and forward n tokens (the GPU arm's sampler settings); returns seconds."""
+        t0 = time.perf_counter()
+        for _ in range(n):
+            if self.cache["offset"] >= PROMPT + DECODE:  # keep the window at config-2 positions
+                self.cache["offset"] = PROMPT
+                self.history = []
+            tok, _ = self.so.sample(self.logits, SAMPLING, self.history, len(self.history), "semantic", 7)
+            native = self.so.local_to_native(tok, "semantic")
+            self.history.append(native)
+            h = self.model.forward([native], self.cache)
+            self.logits = self.model.project(h[-1], "semantic")[0]
+            self.decoded += 1
+        return time.perf_counter() - t0
+
+    def sample_desc(self, n: int) -> str:
+        return (f"numpy port of the reference AR path (oracle/), config-2 song: all 28 layers on the bench weights "
+                f"(float32 math on BF16 values), semantic head, sampler; {n} decode steps at positions "
+                f"{PROMPT}..{PROMPT + DECODE} after a {PROMPT}-token prefill ({self.prefill_s:.1f} s), float32 BLAS "
+                f"on {self.threads} host threads")
+
+
+def cpu_decode_sample(weights_dir: str, seconds_budget: float = 20.0):
+    """Bounded CPU baseline: decode steps of CpuDecoder until ~seconds_budget has passed."""
+    dec = CpuDecoder(weights_dir, os.cpu_count() or 1)
+    dec.decode(1)  # first touch of every weight page
+    spent, n = 0.0, 0
+    while spent < seconds_budget and n < 64:
+        spent += dec.decode(1)
         n += 1
-    per_token = (t_layers / n) * (28 / layers_timed) + t_head / n
-    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"numpy oracle, {n} decode steps at positions {PROMPT}..{PROMPT + n}, "
-                      f"{layers_timed} of 28 layers timed and scaled to 28, semantic head, float32 BLAS "
-                      f"on {os.cpu_count()} host threads"}
+    return {"value": n / spent, "unit": "tok/s", "cores": dec.threads, "kind": "port", "sample": dec.sample_desc(n)}
 
 
 def main():
@@ -266,6 +349,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bs64", action="store_true", help="skip the config-5 batched throughput measurement")
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context tensor-parallel song")
+    ap.add_argument("--no-cfg", action="store_true", help="skip the config-3 classifier-free-guidance song")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -278,16 +362,22 @@ def main():
 
     if args.impl == "reference":
         if rank != 0:
-            return
-        s = cpu_decode_sample()
-        vals = [cpu_decode_sample(seconds_budget=10.0)["value"] for _ in range(max(1, args.steps))]
-        v = float(np.median(vals))
-        print(json.dumps({"impl": "reference", "metric": "AR decode tok/s", "value": v, "unit": "tok/s",
+            return  # rank 0 alone times the CPU arm; the other ranks exit without work
+        weights = ensure_weights(0, 1, lambda: None)
+        dec = CpuDecoder(weights, os.cpu_count() or 1)
+        per_step = 4  # decode steps per bench step (a bounded sample of the config-2 song)
+        for _ in range(args.warmup):
+            dec.decode(per_step)
+        times = [dec.decode(per_step) for _ in range(args.steps)]
+        v = per_step * args.steps / sum(times)
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s",
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                          "higher_is_better": True, "dtype": "bf16 storage, f32 math", "data": "synthetic",
-                          "config": config,
-                          "cpu_baseline": {"value": v, "unit": "tok/s", "cores": s["cores"], "kind": "port",
-                                           "sample": s["sample"]},
+                          "ms_per_step": 1000 * sum(times) / args.steps, "ms_per_token": 1000 * sum(times) / (per_step * args.steps),
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "bf16 storage, f32 math", "data": "synthetic (the bench weights, random prompt ids)",
+                          "config": dict(config, bench_step=f"{per_step} decode tokens of the config-2 song"),
+                          "cpu_baseline": {"value": v, "unit": "tok/s", "cores": dec.threads, "kind": "port",
+                                           "sample": dec.sample_desc(per_step * args.steps)},
                           "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
 
@@ -350,7 +440,24 @@ def main():
     # its split-K reduction, RMSNorm, gate/up GEMM, down GEMM and its reduction.
     prefill_launches = 1 + 10 * layers + 1
     traffic = measured_traffic(avg_L)
-    bs64 = None if args.no_bs64 else batched_throughput(yar, model, rank, barrier, maxall)
+    cfg = None if args.no_cfg else cfg_song(yar, model, rank, barrier, maxall)
+    bs64 = bs64_weak = bs64_cont = None
+    if not args.no_bs64:
+        # Config 5 as BASELINE states it: 64 requests in all, sharded across the N GPUs.
+        per = max(1, BS64_REQUESTS // world)
+        bs64 = batched_throughput(yar, model, rank, barrier, maxall, per,
+                                  f"config5: 64 requests sharded across {world} GPU(s) ({per} per GPU, one row "
+                                  "each), prompts U[256,2048], 1024 tokens each, top-k 50")
+        if world > 1:  # weak-scaling variant: 64 requests on every GPU
+            bs64_weak = batched_throughput(yar, model, rank, barrier, maxall, BS64_REQUESTS,
+                                           "config5 weak variant: 64 requests per GPU, prompts U[256,2048], "
+                                           "1024 tokens each, top-k 50")
+        # Continuous batching: 96 requests per GPU with lengths U[512,1536] on 64 rows, finished
+        # rows refilled from the queue between decode chunks.
+        bs64_cont = batched_throughput(yar, model, rank, barrier, maxall, 96,
+                                       "config5 continuous batching: 96 requests per GPU on 64 rows, prompts "
+                                       "U[256,2048], U[512,1536] tokens each, top-k 50", rows=64,
+                                       n_requests=96, lengths=(512, 1536))
     long = None
     if not args.no_long:
         # Every rank takes the same path, so a failure here is raised on every rank alike:
@@ -362,12 +469,12 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_decode_sample()
+            cpu = cpu_decode_sample(weights)
         except Exception as e:  # reported, not fatal
             cpu = {"error": str(e)}
     if rank == 0:
         out = {
-            "metric": "AR decode tok/s (bs1/GPU) and % of HBM roofline", "value": value, "unit": "tok/s",
+            "metric": METRIC, "value": value, "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * decode_s / args.steps, "ms_per_token": 1000 * per_token_s,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -383,7 +490,10 @@ def main():
             "gpu_launches": args.steps * (DECODE * launches_per_token + prefill_launches),
             "clocks": clk.summary,
             "cpu_baseline": cpu,
+            "cfg": cfg,
             "bs64": bs64,
+            "bs64_per_gpu": bs64_weak,
+            "bs64_continuous": bs64_cont,
             "long_context": long,
         }
         print(json.dumps(out))

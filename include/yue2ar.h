@@ -119,11 +119,26 @@ int yar_session_free(yar_session *session);
  * step; read it with yar_session_trace. YAR_OPT_PREFETCH_STAGES (default 6, 0..64): how many
  * 32 KB stages per SM the persistent kernel pulls into L2 ahead of its shared-memory ring
  * (its lookahead while the step waits at operation boundaries). */
-enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3 };
+enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3, YAR_OPT_MAX_SPLITS = 4,
+       YAR_OPT_LAYER_DUMP = 5, YAR_OPT_FAULT_INJECT = 6 };
+/* YAR_OPT_MAX_SPLITS (default 0 = automatic, else 1..32): the number of splits each (row,
+ * kv head) of the decode attention is cut into at most — 1 puts a row's whole context in
+ * one unit (the longest chain of chunks), for parity tests of the split-KV rescaling.
+ * YAR_OPT_LAYER_DUMP (default 0): record, on every decode step, each row's residual stream
+ * after the embedding and after every layer (read with yar_row_hidden); used by per-layer
+ * parity tests (a teacher-forced layer: its input and cache from the engine, its output
+ * compared with the CPU oracle's).
+ * YAR_OPT_FAULT_INJECT (default 0; testing of the failure path): 1 + 5 * layer + k makes
+ * operation k (0 QKV, 1 attention, 2 O, 3 gate/up, 4 down) of that layer wait, in the
+ * persistent decode kernel, for a flag that no operation writes, with every wait of the
+ * step limited to ~65k polls: the wait expires, the kernel records the error and ends, and
+ * the call returns YAR_FAILURE ("RuntimeError"). No fault, trap or hang is involved; the
+ * session stays usable (the next call starts from cleared state). */
 int yar_session_set_option(yar_session *session, int option, int value);
 /* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64, then 16 sampler stamps:
- * SM clocks at its phase ends, and globaltimer ns at its start and end in slots 12/13)
- * to host. */
+ * SM clocks at its phase ends, and globaltimer ns at its start and end in slots 12/13,
+ * then a [64][4] step log indexed by decode step % 64: globaltimer ns of the sampler's
+ * start and end (request 0) and of the persistent kernel's start and end (CTA 0)) to host. */
 int yar_session_trace(yar_session *session, uint64_t *out, size_t n, size_t *n_written);
 
 /* generate_tokens — native/src/sampling.cpp:185-288 (upstream sampling.py:57-154): prefill
@@ -150,6 +165,21 @@ int yar_generate_batch(yar_session *session, int n_requests, const int32_t *pref
                        const uint64_t *seeds, int phase, int legacy_off, int32_t *out_tokens,
                        int *n_out, int *truncated, char *timing_json, size_t timing_cap);
 
+/* Continuous batching (no reference counterpart: the reference serves one song at a time,
+ * native/src/sampling.cpp:185-288): n_requests independent requests (no CFG) served from a
+ * queue on `slots` rows of the session (0: min(n_requests, rows)). Request i has its own
+ * prefix (prefixes[sum of earlier lengths ..][prefix_lens[i]]), sampling (samplings[i],
+ * its own max_tokens) and seed; it is prefilled on the first free row, and a row whose
+ * request ended (end token or max_tokens) takes the next waiting request between decode
+ * chunks. Request i's native tokens (end token excluded) land at out_tokens[sum of the
+ * earlier requests' max_tokens ..], n_out[i] of them; truncated[i] is 1 when no end token
+ * was sampled. Every step forwards all `slots` rows at once (from 16 rows on, one batched
+ * forward reads each weight once per step for every row). */
+int yar_generate_requests(yar_session *session, int n_requests, int slots, const int32_t *prefixes,
+                          const int32_t *prefix_lens, const yar_sampling *samplings, const uint64_t *seeds,
+                          int phase, int legacy_off, int32_t *out_tokens, int *n_out, int *truncated,
+                          char *timing_json, size_t timing_cap);
+
 /* Row-level API (ARModel::hidden/project + KVCache, ar.cpp:246-323), used by batched
  * serving and by parity tests. A row owns a page table and a position. */
 int yar_row_reset(yar_session *session, int row, int capacity);
@@ -168,6 +198,10 @@ int yar_row_logits(yar_session *session, int row, uint16_t *out, int n);
 int yar_row_kv(yar_session *session, int row, int layer, int start, int count, uint16_t *k,
                uint16_t *v);
 int yar_row_position(yar_session *session, int row, int *pos);
+/* With YAR_OPT_LAYER_DUMP on: the last decode step's residual rows of `row` (n = hidden
+ * BF16 values) at `slot` — 0 the embedding, l + 1 the output of layer l. The hidden state
+ * between layers of ARModel::hidden (native/src/ar.cpp:262-299), exposed for parity. */
+int yar_row_hidden(yar_session *session, int row, int slot, uint16_t *out, int n);
 
 /* The device sampler on host logits (one step), exposed for parity tests of the filter
  * chain and the draw contract. cond/uncond are phase-local BF16 bits of width n
@@ -191,7 +225,8 @@ int yar_sample_host(yar_model *model, const uint16_t *cond, const uint16_t *unco
  * of 769 KiB that every GPU loading the library holds until exit, so n is at most 196608
  * (larger n returns YAR_INVALID_INPUT). The first call for a device looks up that array's
  * address on the device; make it before any stream capture there. Calls share the array:
- * the library serialises its own calls, and calls whose kernels overlapped would race. */
+ * the library serialises its own calls, and calls whose kernels overlapped would race.
+ * The calling thread's current device is the same after the call as before it. */
 int yar_sample_device_noalloc(yar_model *model, const uint16_t *logits, int64_t row_stride,
                               int rows, int n, double cfg_scale, const yar_sampling *sampling,
                               const int32_t *history, int n_history, int step, int phase,

@@ -79,18 +79,33 @@ def rope_cos_sin(positions, head_dim: int, theta: float):
     return np.cos(angles.astype(np.float64)).astype(F32), np.sin(angles.astype(np.float64)).astype(F32)
 
 
+class LazyBf16Weights:
+    """BF16 bit arrays (e.g. memory-mapped safetensors) whose float32 values are formed on
+    each access and not kept: a 3B-parameter model then costs no resident float32 copy,
+    for tests that run one layer at a time."""
+
+    def __init__(self, bits: dict):
+        self.bits = bits
+
+    def __getitem__(self, name):
+        return bf16_from_bits(self.bits[name])
+
+
 class OracleAR:
     """The AR decoder on float32 arrays, with BF16 rounding points when ``bf16``."""
 
-    def __init__(self, tensors: dict, dims, bf16: bool = True, prerounded: bool = False):
+    def __init__(self, tensors: dict, dims, bf16: bool = True, prerounded: bool = False, lazy: bool = False):
         self.d = dims
         self.bf16 = bf16
+        if lazy:  # BF16 bits, converted per access
+            self.w = LazyBf16Weights(tensors)
+            return
         self.w = {}
         for name, value in tensors.items():
-            a = np.asarray(value)
-            if prerounded:  # float32 arrays already holding BF16 values (kept as given)
-                self.w[name] = a
+            if prerounded:  # float32 arrays (or row-indexable views) already holding BF16 values, kept as given
+                self.w[name] = value
                 continue
+            a = np.asarray(value)
             if a.dtype == np.uint16:
                 self.w[name] = bf16_from_bits(a)  # already BF16 values
                 continue
@@ -132,54 +147,74 @@ class OracleAR:
         return {"k": np.zeros(shape, F32), "v": np.zeros(shape, F32), "offset": 0, "capacity": capacity}
 
     # -- forward ----------------------------------------------------------------------------
-    def forward(self, ids, cache: dict) -> np.ndarray:
-        """Run ``ids`` at positions ``cache.offset ..``; return final-normed hidden [T, H]."""
+    def layer(self, i: int, x, cache: dict, start: int) -> np.ndarray:
+        """Decoder layer ``i`` (modeling_yue2.py:296-303) on residual rows ``x`` [T, H] at
+        positions ``start ..``: appends their K/V to ``cache`` layer ``i`` and returns the
+        layer's output rows. ``cache`` must already hold positions ``< start`` of layer ``i``."""
         d = self.d
-        ids = np.asarray(ids, dtype=np.int64)
-        T = len(ids)
-        start = cache["offset"]
-        if start + T > cache["capacity"]:
+        T = x.shape[0]
+        end = start + T
+        if end > cache["capacity"]:
             raise ValueError("KV cache capacity exceeded; generation was not shortened")
-        x = self.w["model.embed_tokens.weight"][ids].copy()
-        cos, sin = rope_cos_sin(np.arange(start, start + T), d.head_dim, d.theta)
+        cos, sin = rope_cos_sin(np.arange(start, end), d.head_dim, d.theta)
         group = d.heads // d.kv_heads
         scale = F32(float(d.head_dim) ** -0.5)
-        end = start + T
-        qpos = np.arange(start, end)[:, None]
-        kpos = np.arange(end)[None, :]
-        visible = kpos <= qpos
-        for i in range(d.layers):
-            p = f"model.layers.{i}."
-            h = self.rms_norm(x, self.w[p + "input_layernorm.weight"])
-            q = self.linear(h, p + "self_attn.q_proj.weight").reshape(T, d.heads, d.head_dim)
-            k = self.linear(h, p + "self_attn.k_proj.weight").reshape(T, d.kv_heads, d.head_dim)
-            v = self.linear(h, p + "self_attn.v_proj.weight").reshape(T, d.kv_heads, d.head_dim)
-            q = self.rms_norm(q, self.w[p + "self_attn.q_norm.weight"])
-            k = self.rms_norm(k, self.w[p + "self_attn.k_norm.weight"])
-            q = self.rope(q, cos, sin)
-            k = self.rope(k, cos, sin)
-            cache["k"][i, :, start:end] = k.transpose(1, 0, 2)
-            cache["v"][i, :, start:end] = v.transpose(1, 0, 2)
-            out = np.empty((T, d.heads, d.head_dim), F32)
-            for hq in range(d.heads):
-                kv = hq // group
-                K = cache["k"][i, kv, :end]
-                V = cache["v"][i, kv, :end]
-                s = (q[:, hq, :] @ K.T).astype(F32) * scale
-                s = np.where(visible, s, F32(-np.inf))
-                m = s.max(axis=-1, keepdims=True)
-                e = np.exp(s - m).astype(F32)
-                l = e.sum(axis=-1, keepdims=True, dtype=F32)
-                out[:, hq, :] = ((e @ V).astype(F32) / l).astype(F32)
-            attn = self.r(out).reshape(T, d.heads * d.head_dim)
-            x = self.r(x + self.linear(attn, p + "self_attn.o_proj.weight"))
-            h2 = self.rms_norm(x, self.w[p + "post_attention_layernorm.weight"])
-            g = self.linear(h2, p + "mlp.gate_proj.weight")
-            u = self.linear(h2, p + "mlp.up_proj.weight")
-            m = self.r(self.silu(g) * u)
-            x = self.r(x + self.linear(m, p + "mlp.down_proj.weight"))
-        cache["offset"] = end
+        visible = np.arange(end)[None, :] <= np.arange(start, end)[:, None]
+        p = f"model.layers.{i}."
+        h = self.rms_norm(x, self.w[p + "input_layernorm.weight"])
+        q = self.linear(h, p + "self_attn.q_proj.weight").reshape(T, d.heads, d.head_dim)
+        k = self.linear(h, p + "self_attn.k_proj.weight").reshape(T, d.kv_heads, d.head_dim)
+        v = self.linear(h, p + "self_attn.v_proj.weight").reshape(T, d.kv_heads, d.head_dim)
+        q = self.rms_norm(q, self.w[p + "self_attn.q_norm.weight"])
+        k = self.rms_norm(k, self.w[p + "self_attn.k_norm.weight"])
+        q = self.rope(q, cos, sin)
+        k = self.rope(k, cos, sin)
+        cache["k"][i, :, start:end] = k.transpose(1, 0, 2)
+        cache["v"][i, :, start:end] = v.transpose(1, 0, 2)
+        out = np.empty((T, d.heads, d.head_dim), F32)
+        for hq in range(d.heads):
+            kv = hq // group
+            K = cache["k"][i, kv, :end]
+            V = cache["v"][i, kv, :end]
+            s = (q[:, hq, :] @ K.T).astype(F32) * scale
+            s = np.where(visible, s, F32(-np.inf))
+            m = s.max(axis=-1, keepdims=True)
+            e = np.exp(s - m).astype(F32)
+            l = e.sum(axis=-1, keepdims=True, dtype=F32)
+            out[:, hq, :] = ((e @ V).astype(F32) / l).astype(F32)
+        attn = self.r(out).reshape(T, d.heads * d.head_dim)
+        x = self.r(x + self.linear(attn, p + "self_attn.o_proj.weight"))
+        h2 = self.rms_norm(x, self.w[p + "post_attention_layernorm.weight"])
+        g = self.linear(h2, p + "mlp.gate_proj.weight")
+        u = self.linear(h2, p + "mlp.up_proj.weight")
+        m = self.r(self.silu(g) * u)
+        return self.r(x + self.linear(m, p + "mlp.down_proj.weight"))
+
+    def forward(self, ids, cache: dict) -> np.ndarray:
+        """Run ``ids`` at positions ``cache.offset ..``; return final-normed hidden [T, H]."""
+        ids = np.asarray(ids, dtype=np.int64)
+        start = cache["offset"]
+        if start + len(ids) > cache["capacity"]:
+            raise ValueError("KV cache capacity exceeded; generation was not shortened")
+        x = self.w["model.embed_tokens.weight"][ids].copy()
+        for i in range(self.d.layers):
+            x = self.layer(i, x, cache, start)
+        cache["offset"] = start + len(ids)
+        return self.final_norm(x)
+
+    def final_norm(self, x) -> np.ndarray:
         return self.rms_norm(x, self.w["model.norm.weight"])
+
+    def cache_from(self, k_layers, v_layers, length: int, capacity: int) -> dict:
+        """A cache holding given K/V (per layer [kv_heads][length][head_dim] float32 values,
+        e.g. read back from the engine) at positions ``0 .. length``: decode steps from it
+        are teacher-forced on those exact cached values."""
+        cache = self.new_cache(capacity)
+        for i, (k, v) in enumerate(zip(k_layers, v_layers)):
+            cache["k"][i, :, :length] = k
+            cache["v"][i, :, :length] = v
+        cache["offset"] = length
+        return cache
 
     def project(self, hidden, phase: str | None) -> np.ndarray:
         """Phase-local LM head (native/src/ar.cpp:302-323); ``None`` = full vocabulary."""

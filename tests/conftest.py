@@ -64,3 +64,17 @@ def tiny_dir(tmp_path_factory, synth):
     d = str(tmp_path_factory.mktemp("tiny"))
     synth.write_converted(d, synth.TINY, seed=0, norm_std=0.1, workers=1)
     return d
+
+
+@pytest.fixture(scope="session")
+def pinned_dir(tmp_path_factory, synth):
+    """The YuE2-3B dims model in BF16 (seed 0, unit norms): the golden fixtures' model."""
+    d = str(tmp_path_factory.mktemp("pinned"))
+    synth.write_converted(d, synth.PINNED, seed=0)
+    return d
+
+
+@pytest.fixture(scope="session")
+def pinned(pinned_dir):
+    """The pinned model loaded on cuda:0 once for every GPU test module."""
+    return load_package().ARModel(pinned_dir)

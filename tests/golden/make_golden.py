@@ -19,6 +19,13 @@ Fixtures:
   124 ids then 4 teacher-forced decode steps (the capture shape of the reference's
   ``tools/oracle.py ar``); semantic-slice logits (BF16 bits), full-vocab argmax and
   K/V samples of layers 0 and 27.
+* ``config2_bf16.npz`` — BASELINE config-2 shape on the same 3B model: 512-id prompt
+  (seed 2), 16 teacher-forced codec ids; semantic logits of every row, ABC logits (text
+  rows + ABC_END) of rows 0/8/16, K/V samples of layers 0 and 27, and the radius between
+  the numpy oracle and upstream on the same inputs (``meta``).
+* ``cfg_pair_bf16.npz`` — BASELINE config-3 shape: conditional prompt of 1024 ids and
+  unconditional prompt of 64 ids (seed 3), each branch with its own cache, stepped with
+  the same 8 codec ids; semantic logits of both branches and the oracle radius.
 * ``sampler_cases.npz`` — upstream ``distribution`` outputs (phase-local) for crafted
   and random cases, plus upstream BF16 CFG mixing, ``penalty ** count`` and RoPE
   ``inv_freq`` values.
@@ -171,6 +178,125 @@ def make_pinned(out_dir):
                         meta=json.dumps({"seed": 0, "std": 0.02, "norm_std": 0.0, "prefill": 124, "decode": 4}))
 
 
+def _upstream_trace(model, prefix, forced, capacity):
+    """Upstream prefill of ``prefix`` then one teacher-forced step per id of ``forced``:
+    the full-vocabulary logits rows (prefill's last position, then each step) and the
+    StaticKVCache (modeling_yue2.py:357-400)."""
+    from yue2.modeling_yue2 import StaticKVCache
+    c = model.config
+    cache = StaticKVCache(c.num_hidden_layers, 1, c.num_key_value_heads, capacity, c.head_dim, torch.bfloat16,
+                          torch.device("cpu"))
+    rows = []
+    with torch.inference_mode():
+        out = model(torch.tensor([prefix]), past_key_values=cache, use_cache=True, logits_to_keep=1).logits[:, -1]
+        rows.append(out[0].clone())
+        for tok in forced:
+            out = model(torch.tensor([[tok]]), past_key_values=cache, use_cache=True, logits_to_keep=1).logits[:, -1]
+            rows.append(out[0].clone())
+    return torch.stack(rows), cache
+
+
+def _phase_slices(full):
+    from yue2.protocol import ABC_END, CODEC_OFFSET, CODEC_SIZE, EOD, MUSIC_END
+    sem = full[..., MUSIC_END:CODEC_OFFSET + CODEC_SIZE]
+    abc = torch.cat([full[..., :EOD], full[..., ABC_END:ABC_END + 1]], dim=-1)
+    return sem, abc
+
+
+def _radius(ours: np.ndarray, ref: np.ndarray) -> dict:
+    return {"max_abs": float(np.abs(ours - ref).max()),
+            "rel_l2": float(np.linalg.norm(ours - ref) / np.linalg.norm(ref))}
+
+
+def _oracle_trace(bits, prefix, forced, capacity, phases):
+    """The numpy oracle on the same weights and ids: the last prefill row and every step's
+    logits per phase (to record the radius between the two valid BF16 implementations)."""
+    sys.path.insert(0, ROOT)
+    from oracle import ar_oracle as ora
+    oracle = ora.OracleAR(bits, synth.PINNED, bf16=True)
+    out = {ph: [] for ph in phases}
+    cache = oracle.new_cache(capacity)
+    h = None
+    for s0 in range(0, len(prefix), 1024):
+        h = oracle.forward(prefix[s0:s0 + 1024], cache)
+    for ph in phases:
+        out[ph].append(oracle.project(h[-1], ph)[0])
+    for tok in forced:
+        h = oracle.forward([tok], cache)
+        for ph in phases:
+            out[ph].append(oracle.project(h[-1], ph)[0])
+    return {ph: np.stack(v) for ph, v in out.items()}
+
+
+def _pinned_bits():
+    with tempfile.TemporaryDirectory() as tmp:
+        synth.write_converted(tmp, synth.PINNED, seed=0, norm_std=0.0)
+        bits = synth.read_safetensors(os.path.join(tmp, "ar-bf16.safetensors"))
+        return {k: np.array(v) for k, v in bits.items()}
+
+
+ABC_ROWS = (0, 8, 16)  # steps whose ABC-phase logits are kept (151,644 columns each)
+
+
+def make_config2(out_dir, bits=None):
+    """BASELINE config-2 shape on YuE2-3B dims: 512 random prompt ids (full vocabulary),
+    then 16 teacher-forced semantic (codec) ids; semantic logits of all 17 rows and ABC
+    logits (text rows + ABC_END) of rows ABC_ROWS; layer-0 and layer-27 K/V samples."""
+    dims = synth.PINNED
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, dims.vocab, (512,), generator=g).tolist()
+    forced = (151853 + torch.randint(0, 32768, (16,), generator=g)).tolist()
+    bits = bits if bits is not None else _pinned_bits()
+    model = upstream_model(dims, bits, torch.bfloat16)
+    full, cache = _upstream_trace(model, prompt, forced, 544)
+    del model
+    sem, abc = _phase_slices(full)
+    sel = np.r_[0:8, 252:260, 504:528]
+    orc = _oracle_trace(bits, prompt, forced, 544, ("semantic", "abc"))
+    sem_f = sem.float().numpy()
+    abc_f = abc[list(ABC_ROWS)].float().numpy()
+    meta = {"seed": 0, "std": 0.02, "norm_std": 0.0, "prefill": 512, "decode": 16, "prompt_seed": 2,
+            "abc_rows": list(ABC_ROWS),
+            "oracle_vs_upstream": {"semantic": _radius(orc["semantic"], sem_f),
+                                   "abc": _radius(orc["abc"][list(ABC_ROWS)], abc_f)}}
+    print("config2 radius", meta["oracle_vs_upstream"])
+    np.savez_compressed(os.path.join(out_dir, "config2_bf16.npz"), prompt=np.array(prompt, np.int32),
+                        forced=np.array(forced, np.int32), semantic_logits=bf16_bits(sem),
+                        abc_logits=bf16_bits(abc[list(ABC_ROWS)]), kv_positions=sel.astype(np.int32),
+                        k_layer0=bf16_bits(cache.key_cache[0][0][:, sel]),
+                        v_layer0=bf16_bits(cache.value_cache[0][0][:, sel]),
+                        k_layer27=bf16_bits(cache.key_cache[27][0][:, sel]),
+                        v_layer27=bf16_bits(cache.value_cache[27][0][:, sel]), meta=json.dumps(meta))
+
+
+def make_cfg_pair(out_dir, bits=None):
+    """BASELINE config-3 shape on YuE2-3B dims: the conditional branch (1024 random ids) and
+    the unconditional branch (64 random ids) of one CFG request, each with its own cache,
+    stepped with the same 8 teacher-forced codec ids (the loop feeds both branches the one
+    sampled token; native/src/sampling.cpp:185-230). Semantic logits of both branches."""
+    dims = synth.PINNED
+    g = torch.Generator().manual_seed(3)
+    cond = torch.randint(0, dims.vocab, (1024,), generator=g).tolist()
+    uncond = torch.randint(0, dims.vocab, (64,), generator=g).tolist()
+    forced = (151853 + torch.randint(0, 32768, (8,), generator=g)).tolist()
+    bits = bits if bits is not None else _pinned_bits()
+    model = upstream_model(dims, bits, torch.bfloat16)
+    full_c, _ = _upstream_trace(model, cond, forced, 1040)
+    full_u, _ = _upstream_trace(model, uncond, forced, 80)
+    del model
+    sem_c, _ = _phase_slices(full_c)
+    sem_u, _ = _phase_slices(full_u)
+    orc_c = _oracle_trace(bits, cond, forced, 1040, ("semantic",))["semantic"]
+    orc_u = _oracle_trace(bits, uncond, forced, 80, ("semantic",))["semantic"]
+    meta = {"seed": 0, "std": 0.02, "norm_std": 0.0, "cond": 1024, "uncond": 64, "decode": 8, "prompt_seed": 3,
+            "oracle_vs_upstream": {"cond": _radius(orc_c, sem_c.float().numpy()),
+                                   "uncond": _radius(orc_u, sem_u.float().numpy())}}
+    print("cfg radius", meta["oracle_vs_upstream"])
+    np.savez_compressed(os.path.join(out_dir, "cfg_pair_bf16.npz"), cond=np.array(cond, np.int32),
+                        uncond=np.array(uncond, np.int32), forced=np.array(forced, np.int32),
+                        cond_logits=bf16_bits(sem_c), uncond_logits=bf16_bits(sem_u), meta=json.dumps(meta))
+
+
 def make_sampler(out_dir):
     from yue2.protocol import ABC_END, CODEC_OFFSET, CODEC_SIZE, EOD, MUSIC_END, VOCAB_SIZE, Sampling
     from yue2.sampling import distribution, window_penalty
@@ -283,7 +409,7 @@ def make_sampler(out_dir):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", choices=["tiny", "pinned", "sampler"], default=None)
+    ap.add_argument("--only", choices=["tiny", "pinned", "sampler", "config2", "cfg"], default=None)
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "vendor", "yue", "src"))
     torch.set_num_threads(os.cpu_count())
@@ -293,6 +419,12 @@ def main():
         make_tiny(HERE)
     if args.only in (None, "pinned"):
         make_pinned(HERE)
+    if args.only in (None, "config2", "cfg"):
+        bits = _pinned_bits()
+        if args.only in (None, "config2"):
+            make_config2(HERE, bits)
+        if args.only in (None, "cfg"):
+            make_cfg_pair(HERE, bits)
 
 
 if __name__ == "__main__":

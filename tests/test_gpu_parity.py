@@ -273,13 +273,6 @@ def test_generate_validation_and_cancel(yar, tiny):
     assert len(toks) == 32
 
 
-@pytest.fixture(scope="module")
-def pinned(yar, synth, tmp_path_factory):
-    d = str(tmp_path_factory.mktemp("pinned"))
-    synth.write_converted(d, synth.PINNED, seed=0)
-    return yar.ARModel(d)
-
-
 def test_pinned_3b_prefill_decode_vs_upstream(yar, pinned, golden):
     """YuE2-3B dims, 28 layers: GPU vs the upstream PyTorch golden (same weights)."""
     g = golden("pinned_bf16.npz")
@@ -460,4 +453,29 @@ def test_generate_batch_replays_exactly(yar, wide2):
         single = f(s.logits(r, None))
         assert np.abs(single - batched[r]).max() <= 0.0625, r
         assert rel_l2(single, batched[r]) <= 2e-2, r
+    s.close()
+
+
+@pytest.mark.parametrize("slots", [2, 3])
+def test_continuous_batching_matches_requests_run_alone(yar, tiny, slots):
+    """Seven requests with their own lengths and sampling served on 2 or 3 rows: finished
+    rows are refilled from the queue between decode chunks, and every request's tokens
+    equal those of the same request generated alone (per-row arithmetic does not depend on
+    the other rows, and each request keeps its own seed and step count)."""
+    rng = np.random.default_rng(61)
+    n = 7
+    prefixes = [rng.integers(0, 4096, int(rng.integers(8, 60))).tolist() for _ in range(n)]
+    seeds = [int(x) for x in rng.integers(0, 2**62, n)]
+    smps = []
+    for i in range(n):
+        mt = int(rng.integers(5, 40))
+        base = SAMPLERS[i % 3]
+        smps.append(yar.Sampling(**dict(base, min_tokens=0, max_tokens=mt)))
+    s = tiny.session(max_rows=3, max_ctx=128)
+    tokens, timing, truncated = s.generate_requests(prefixes, smps, seeds, phase=None, slots=slots)
+    assert timing["requests"] == n and timing["slots"] == slots and timing["refills"] == n - slots
+    for i in range(n):
+        alone, _, trunc = s.generate(prefixes[i], smps[i], seed=seeds[i], phase=None)
+        assert tokens[i] == alone, i
+        assert truncated[i] == trunc, i
     s.close()

@@ -82,12 +82,16 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                              ctypes.c_size_t]),
         "yar_generate_batch": (I, [P, I, i32p, i32p, ctypes.POINTER(_Sampling), ctypes.POINTER(ctypes.c_uint64), I, I,
                                    i32p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.c_char_p, ctypes.c_size_t]),
+        "yar_generate_requests": (I, [P, I, I, i32p, i32p, ctypes.POINTER(_Sampling), ctypes.POINTER(ctypes.c_uint64),
+                                      I, I, i32p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.c_char_p,
+                                      ctypes.c_size_t]),
         "yar_row_reset": (I, [P, I, I]),
         "yar_row_prefill": (I, [P, I, i32p, I, I, I]),
         "yar_rows_step": (I, [P, ctypes.POINTER(I), i32p, I, I]),
         "yar_row_logits": (I, [P, I, u16p, I]),
         "yar_row_kv": (I, [P, I, I, I, I, u16p, u16p]),
         "yar_row_position": (I, [P, I, ctypes.POINTER(I)]),
+        "yar_row_hidden": (I, [P, I, I, u16p, I]),
         "yar_sample_host": (I, [P, u16p, u16p, I, D, ctypes.POINTER(_Sampling), i32p, I, I, I, U64, I, i32p,
                                 ctypes.POINTER(ctypes.c_float)]),
         "yar_sample_device_noalloc": (I, [P, P, ctypes.c_int64, I, I, D, ctypes.POINTER(_Sampling), i32p, I, I, I,
@@ -252,9 +256,49 @@ class Session:
         """Independent requests decoded together on rows 0..n-1: (token lists, timing, truncated)."""
         return _generate_batch(self, prefixes, sampling, seeds, phase, legacy_off)
 
+    def generate_requests(self, prefixes, samplings, seeds, phase="semantic", slots: int = 0,
+                          legacy_off: bool = False):
+        """Continuous batching: requests served on `slots` rows (0 = as many as fit), finished
+        rows refilled from the queue. Returns (token lists, timing, truncated flags)."""
+        n = len(prefixes)
+        lens = np.array([len(p) for p in prefixes], np.int32)
+        flat = _i32(np.concatenate([np.asarray(p, np.int32) for p in prefixes]))
+        sd = np.ascontiguousarray(np.asarray(seeds, np.uint64))
+        arr = (_Sampling * n)(*[smp._c() for smp in samplings])
+        caps = [max(1, smp.max_tokens) for smp in samplings]
+        offs = np.concatenate([[0], np.cumsum(caps)]).astype(np.int64)
+        out = np.zeros(int(offs[-1]), np.int32)
+        n_out, trunc = np.zeros(n, np.int32), np.zeros(n, np.int32)
+        timing = ctypes.create_string_buffer(4096)
+        _check(lib.yar_generate_requests(self._h, n, slots, _ptr(flat, ctypes.c_int32), _ptr(lens, ctypes.c_int32),
+                                         arr, _ptr(sd, ctypes.c_uint64), PHASES[phase], int(legacy_off),
+                                         _ptr(out, ctypes.c_int32), _ptr(n_out, ctypes.c_int),
+                                         _ptr(trunc, ctypes.c_int), timing, len(timing)))
+        tokens = [out[offs[r]:offs[r] + n_out[r]].tolist() for r in range(n)]
+        return tokens, json.loads(timing.value.decode()), [bool(t) for t in trunc]
+
     def set_prefetch_stages(self, n: int):
         """L2 prefetch distance of the persistent decode kernel, in 32 KB stages per SM."""
         _check(lib.yar_session_set_option(self._h, 3, int(n)))
+
+    def set_max_splits(self, n: int):
+        """Cap the decode attention's splits per (row, kv head); 0 restores the automatic plan."""
+        _check(lib.yar_session_set_option(self._h, 4, int(n)))
+
+    def set_fault_inject(self, op: int):
+        """Failure-path testing: operation 1 + 5 * layer + k of the persistent decode waits for
+        a flag nothing writes (short limit), so the step fails with RuntimeError; 0 = off."""
+        _check(lib.yar_session_set_option(self._h, 6, int(op)))
+
+    def set_layer_dump(self, on: bool):
+        """Record each decode step's residual rows after the embedding and every layer."""
+        _check(lib.yar_session_set_option(self._h, 5, int(bool(on))))
+
+    def hidden(self, row: int, slot: int) -> np.ndarray:
+        """Residual row of the last decode step (BF16 bits): slot 0 embedding, l + 1 after layer l."""
+        out = np.empty(self.model.dims["hidden"], np.uint16)
+        _check(lib.yar_row_hidden(self._h, row, slot, _ptr(out, ctypes.c_uint16), out.size))
+        return out
 
     def set_trace(self, on: bool):
         """Record the persistent decode kernel's per-CTA timeline (see ``trace``)."""
@@ -271,9 +315,17 @@ class Session:
 
     def sampler_trace(self) -> np.ndarray:
         """The last sampler launch's phase stamps (16 uint64, see yar_session_trace)."""
+        return self._trace_tail()[:16]
+
+    def step_log(self) -> np.ndarray:
+        """[64][4] globaltimer ns per decode step (ring indexed by step % 64): sampler start
+        and end (request 0), persistent kernel start and end (CTA 0)."""
+        return self._trace_tail()[16:16 + 256].reshape(64, 4)
+
+    def _trace_tail(self) -> np.ndarray:
         d = self.model.dims
         k = d["sms"] * (5 * d["layers"] + 1) * 8
-        out = np.zeros(k + 16, np.uint64)
+        out = np.zeros(k + 16 + 256, np.uint64)
         n = ctypes.c_size_t()
         _check(lib.yar_session_trace(self._h, _ptr(out, ctypes.c_uint64), out.size, ctypes.byref(n)))
         return out[k:]

@@ -25,6 +25,9 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
 void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, double cfg_scale,
                  const ::yar_sampling &smp, const int32_t *history, int n_history, int step, int phase,
                  uint64_t seed, int legacy_off, int32_t *token, float *scores);
+std::string generate_requests(Session &s, int n_req, int slots, const int32_t *prefixes, const int32_t *prefix_lens,
+                              const ::yar_sampling *smps, const uint64_t *seeds, int phase, int legacy_off,
+                              int32_t *out_tokens, int *n_out, int *truncated);
 std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const int32_t *prefix_lens,
                            const ::yar_sampling &smp, const uint64_t *seeds, int phase, int legacy_off,
                            int32_t *out_tokens, int *n_out, int *truncated);
@@ -191,7 +194,8 @@ int yar_session_set_option(yar_session *session, int option, int value) {
       for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old pointer
       s.graphs.clear();
       if (value) {
-        s.trace_elems = size_t(s.m->sm_count) * (5 * s.m->d.layers + 1) * 8 + 16;  // + sampler phases
+        // + sampler phases, + a 64-step log of kernel start/end times
+        s.trace_elems = size_t(s.m->sm_count) * (5 * s.m->d.layers + 1) * 8 + 16 + 64 * 4;
         YAR_CUDA(cudaMalloc(&s.d_trace, s.trace_elems * sizeof(unsigned long long)));
         YAR_CUDA(cudaMemset(s.d_trace, 0, s.trace_elems * sizeof(unsigned long long)));
       }
@@ -202,6 +206,32 @@ int yar_session_set_option(yar_session *session, int option, int value) {
       for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old value
       s.graphs.clear();
       s.prefetch_stages = value;
+    } else if (option == YAR_OPT_MAX_SPLITS) {
+      need(value >= 0 && value <= s.max_splits, "attention splits must be in [0, 32]");
+      YAR_CUDA(cudaSetDevice(s.m->device));
+      YAR_CUDA(cudaStreamSynchronize(s.stream));
+      for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old split plan
+      s.graphs.clear();
+      s.forced_splits = value;
+    } else if (option == YAR_OPT_FAULT_INJECT) {
+      need(value >= 0 && value <= 5 * s.m->d.layers, "fault-injection operation outside the step");
+      YAR_CUDA(cudaSetDevice(s.m->device));
+      YAR_CUDA(cudaStreamSynchronize(s.stream));
+      for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old value
+      s.graphs.clear();
+      s.inject_op = value;
+    } else if (option == YAR_OPT_LAYER_DUMP) {
+      YAR_CUDA(cudaSetDevice(s.m->device));
+      YAR_CUDA(cudaStreamSynchronize(s.stream));
+      for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old pointer
+      s.graphs.clear();
+      if (s.d_layer_dump) cudaFree(s.d_layer_dump);
+      s.d_layer_dump = nullptr;
+      if (value) {
+        const size_t n = size_t(s.m->d.layers + 1) * s.max_rows * s.m->d.hidden;
+        YAR_CUDA(cudaMalloc(&s.d_layer_dump, n * sizeof(yar::bf16)));
+        YAR_CUDA(cudaMemset(s.d_layer_dump, 0, n * sizeof(yar::bf16)));
+      }
     } else {
       throw yar::Error("ValueError", "unknown session option");
     }
@@ -256,6 +286,24 @@ int yar_generate_batch(yar_session *session, int n_requests, const int32_t *pref
   });
 }
 
+int yar_generate_requests(yar_session *session, int n_requests, int slots, const int32_t *prefixes,
+                          const int32_t *prefix_lens, const yar_sampling *samplings, const uint64_t *seeds, int phase,
+                          int legacy_off, int32_t *out_tokens, int *n_out, int *truncated, char *timing_json,
+                          size_t timing_cap) {
+  return guarded([&] {
+    need(session && prefixes && prefix_lens && samplings && seeds && out_tokens && n_out && truncated,
+         "missing argument");
+    const std::string timing = yar::generate_requests(*session->s, n_requests, slots, prefixes, prefix_lens,
+                                                      samplings, seeds, phase, legacy_off, out_tokens, n_out,
+                                                      truncated);
+    if (timing_json && timing_cap > 0) {
+      const size_t n = timing.size() < timing_cap - 1 ? timing.size() : timing_cap - 1;
+      std::memcpy(timing_json, timing.data(), n);
+      timing_json[n] = '\0';
+    }
+  });
+}
+
 int yar_row_reset(yar_session *session, int row, int capacity) {
   return guarded([&] {
     need(session, "session is required");
@@ -300,15 +348,33 @@ int yar_row_kv(yar_session *session, int row, int layer, int start, int count, u
     std::vector<int> table(s.pages_per_row);
     YAR_CUDA(cudaMemcpy(table.data(), s.d_page_table + size_t(row) * s.pages_per_row,
                         table.size() * sizeof(int), cudaMemcpyDeviceToHost));
+    // One copy per (k|v, head, page): a page holds a contiguous run of positions.
     for (int kv = 0; kv < 2; ++kv)
       for (int h = 0; h < d.kv_heads; ++h)
-        for (int i = 0; i < count; ++i) {
+        for (int i = 0; i < count;) {
           const int pos = start + i, page = table[pos / s.page_tokens], slot = pos % s.page_tokens;
+          const int run = std::min(count - i, s.page_tokens - slot);
           const size_t blk = (size_t(layer) * s.num_pages + page) * 2 + kv;
           const yar::bf16 *src = s.kv + blk * s.kv_page_elems + (size_t(h) * s.page_tokens + slot) * d.head_dim;
           uint16_t *dst = (kv ? v : k) + (size_t(h) * count + i) * d.head_dim;
-          YAR_CUDA(cudaMemcpy(dst, src, size_t(d.head_dim) * 2, cudaMemcpyDeviceToHost));
+          YAR_CUDA(cudaMemcpy(dst, src, size_t(run) * d.head_dim * 2, cudaMemcpyDeviceToHost));
+          i += run;
         }
+  });
+}
+
+int yar_row_hidden(yar_session *session, int row, int slot, uint16_t *out, int n) {
+  return guarded([&] {
+    need(session && out, "session and out are required");
+    auto &s = *session->s;
+    const auto &d = s.m->d;
+    need(s.d_layer_dump != nullptr, "the hidden-state record is off (YAR_OPT_LAYER_DUMP)");
+    need(row >= 0 && row < s.max_rows && slot >= 0 && slot <= d.layers && n == d.hidden,
+         "row, slot or width outside the record");
+    YAR_CUDA(cudaSetDevice(s.m->device));
+    YAR_CUDA(cudaStreamSynchronize(s.stream));
+    YAR_CUDA(cudaMemcpy(out, s.d_layer_dump + (size_t(slot) * s.max_rows + row) * d.hidden, size_t(n) * 2,
+                        cudaMemcpyDeviceToHost));
   });
 }
 

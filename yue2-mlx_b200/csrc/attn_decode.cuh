@@ -7,15 +7,16 @@
 // split) is processed by 256 threads (8 warps):
 //   1. q-norm + RoPE of the group's G q heads; the unit holding the new position also
 //      norms and ropes the new k and appends k, v to the paged cache;
-//   2. per chunk (rows staged in shared memory): FP32 scores with 2-4 threads per (head,
-//      position), the chunk's max and exp-sum, P.V with one output dim per thread (or a
-//      fixed split of the positions when G x D < 256), folded into the running (max, sum,
-//      o) with exp rescaling;
+//   2. per chunk (rows staged in shared memory): each warp takes eight of the 64 positions
+//      — FP32 scores (4 lanes per position), its running max / exp-sum / output rescaled by
+//      exp(m_old - m_new), P.V over its rows — with no barrier among the warps; the warps'
+//      states are combined once at the end of the unit;
 //   3. a partial (max, sum, o[D]) per q head; the last of the row's splits to arrive merges
 //      them into the BF16 head outputs (native/src/ar.cpp:88-96, :276-291;
 //      oracle/port/lyra/ar.py:131-145).
 #pragma once
 #include "common.cuh"
+#include "tma_ring.cuh"
 
 namespace yar {
 
@@ -91,6 +92,16 @@ struct DecodeAttnParams {
   int out_ndst;  // tensor parallelism: also stored at out + out_dst[i] bytes (peer copies)
   const long long *out_dst;
   int *error;  // device error word: expired waits of the standalone kernel (may be null)
+  // Flagged transport (the persistent kernel; null: plain buffers): raw projections read
+  // from flagged words [rows][qkv_ll_stride] once they carry qkv_flag, head outputs
+  // written as flagged words [rows][out_ll_stride] with out_flag.
+  const uint2 *qkv_ll = nullptr;
+  int qkv_ll_stride = 0;
+  uint32_t qkv_flag = 0;
+  uint2 *out_ll = nullptr;
+  int out_ll_stride = 0;
+  uint32_t out_flag = 0;
+  long long ll_limit = 1ll << 22;  // polls of a flagged wait before it gives up
 };
 
 constexpr int kKvChunk = 64;  // positions per KV chunk
@@ -113,9 +124,8 @@ template <int D, int G>
 struct __align__(16) AttnTeamSmem {
   bf16 q_b[G][D];              // normed, roped q (BF16-exact values)
   bf16 knew[D], vnew[D];       // the new position's k (normed, roped) and v, as cached
-  float p_s[G][kKvChunk];      // exp(score - chunk max)
-  float red[2][kAttnThreads / 32];
-  float pvp[kAttnThreads / G / (D / 8)][G * D];  // P.V partials per position phase
+  float wml[kAttnThreads / 32][G][2];  // per-warp (max, exp-sum) at the unit's end
+  float pvp[kAttnThreads / 32][G * D];  // per-warp unnormalized outputs at the unit's end
   int last_flag;
 };
 
@@ -213,22 +223,33 @@ __device__ __forceinline__ void attn_load_norm_w(const bf16 *qn, const bf16 *kn,
 
 // Step 1 of a unit: q heads into sm.q_s; when `holds_new`, the new k/v into sm.knew/vnew
 // and appended to the cache at the row's position.
+// With flagged input (p.qkv_ll) the projections are polled until they carry p.qkv_flag;
+// returns false on every team thread when such a wait gave up (code 64 recorded).
 template <int D, int G>
-__device__ void attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const AttnRow<D> &rs, int row, int kvh,
+__device__ bool attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const AttnRow<D> &rs, int row, int kvh,
                         bool holds_new, const float (&wv)[D / 32], int tid, int bar_id) {
   static_assert(G < kAttnThreads / 32, "one warp per q head plus one for the new k");
   constexpr int NPL = D / 32;
   const AttnGeom &g = p.g;
   const int warp = tid >> 5, lane = tid & 31;
+  bool ok = true;
   if (warp < G || (warp == G && holds_new)) {
     const bool is_k = warp == G;
-    const bf16 *qkv = p.qkv + size_t(row) * (g.qdim + 2 * g.kvdim);
-    const bf16 *src = is_k ? qkv + g.qdim + kvh * D : qkv + (kvh * G + warp) * D;
+    const int rw = g.qdim + 2 * g.kvdim;
+    const int e0 = is_k ? g.qdim + kvh * D : (kvh * G + warp) * D, ev = g.qdim + g.kvdim + kvh * D;
+    // Element e of the row's projections: plain, or half (e & 1) of flagged word e / 2.
+    auto elem = [&](int e) -> float {
+      if (!p.qkv_ll) return bf2f(__ldcg(p.qkv + size_t(row) * rw + e));
+      uint32_t w = 0;
+      if (!ll_wait1(p.qkv_ll + size_t(row) * p.qkv_ll_stride + (e >> 1), p.qkv_flag, w, p.error, p.ll_limit))
+        ok = false;
+      return (e & 1) ? bf_hi(w) : bf_lo(w);
+    };
     float hv[NPL], vv[NPL];
 #pragma unroll
     for (int i = 0; i < NPL; ++i) {
-      hv[i] = bf2f(__ldcg(src + lane + 32 * i));
-      if (is_k) vv[i] = bf2f(__ldcg(qkv + g.qdim + g.kvdim + kvh * D + lane + 32 * i));
+      hv[i] = elem(e0 + lane + 32 * i);
+      if (is_k) vv[i] = elem(ev + lane + 32 * i);
     }
     norm_rope_regs<D>(hv, wv, rs.cosr, rs.sinr, g.eps, lane);
     if (!is_k) {
@@ -247,135 +268,188 @@ __device__ void attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const
       }
     }
   }
-  team_sync(bar_id);
+  if (!p.qkv_ll) {
+    team_sync(bar_id);
+    return true;
+  }
+  int all_ok;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(all_ok)
+      : "r"(int(ok)), "r"(bar_id), "n"(kAttnThreads)
+      : "memory");
+  if (!all_ok && tid == 0 && p.error) atomicOr(p.error, 64);
+  return all_ok != 0;
 }
 
-// Running state of one thread: output tid (q head tid / D, dim tid % D) when tid < G x D.
+// The final state of one unit for thread tid < G x D: output tid (q head tid / D, dim
+// tid % D) as the running max, exp-sum and unnormalized output.
 template <int D>
 struct AttnAcc {
   float m, l, o;
 };
-template <int D>
-__device__ __forceinline__ void attn_acc_init(AttnAcc<D> &a) {
-  a.m = -INFINITY;
-  a.l = 0.f;
-  a.o = 0.f;
+
+// Chunk streaming: warp w owns positions [8w, 8w + 8) of every 64-position chunk and keeps
+// its own online-softmax state, so a chunk needs no barrier among the warps. Lane l works
+// on position p = l / 4 of the warp's eight for scores (part l % 4 of the D dims, reduced
+// by two shuffles), and on dims [l * D/32, +D/32) for P.V; the warps' states are combined
+// once per unit (attn_combine).
+template <int D, int G>
+struct AttnWarpAcc {
+  float m[G], l[G];     // running max and exp-sum of the warp's positions (same on every lane)
+  float o[G][D / 32];   // this lane's output dims, unnormalized
+};
+template <int D, int G>
+__device__ __forceinline__ void attn_warp_init(AttnWarpAcc<D, G> &a) {
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    a.m[h] = -INFINITY;
+    a.l[h] = 0.f;
+#pragma unroll
+    for (int k = 0; k < D / 32; ++k) a.o[h][k] = 0.f;
+  }
 }
 
-// Step 2, one chunk: rows [0, n_main) of Ks/Vs (shared memory, row pitch D) and, when
-// `extra`, the new position (sm.knew/vnew) as row n_main. Ends with a barrier.
-//   Scores: the threads of head hd (256 / G of them) form 4-thread groups; part p of a
-//   group holds its quarter of q in registers (in the rotated order below) and dots it
-//   with that quarter of rows ps, ps + slots, ... (16-byte K loads in an order rotated by
-//   row and part, so a quarter-warp never hits one bank group twice); the 4 parts are
-//   added by shuffles.
-//   P.V: thread (head hd, dim group dg of 8 dims, phase q) sums p_r * V[r][8 dg .. +7]
-//   over the rows r = q (mod phases) with 16-byte V loads; the phases are added in order
-//   through shared memory, one output per thread.
+// 16-byte chunk j of the part (D/4 dims) that lane `lane` reads of a K row, in a rotated
+// order: the eight lanes of one shared-memory phase (two positions x four parts) then hit
+// eight distinct bank groups (rows are D x 2 bytes, a multiple of 128).
+template <int D>
+__device__ __forceinline__ int attn_kchunk(int lane, int j) {
+  constexpr int CPP = D / 32;  // 16-byte chunks per part
+  const int p = lane >> 2, part = lane & 3;
+  const int rot = CPP == 4 ? 2 * (p & 1) + (part >> 1) : (p & 1);
+  return part * CPP + ((j + rot) & (CPP - 1));
+}
+
+// One chunk for this warp: positions [8w, 8w + 8) of rows [0, n_main) of Ks/Vs (shared
+// memory, row pitch D) and, when `extra`, the new position (knew/vnew) as row n_main.
+// FP32 scores (mixed-precision BF16 FMAs), the warp's running max/sum/output rescaled by
+// exp(m_old - m_new); only this warp's rows are read.
+// q comes from shared memory (q_b, after attn_qk) chunk by chunk in the same rotated order
+// as the K loads (conflict-free too), which keeps 32 registers free in the caller.
 template <int D, int G>
-__device__ void attn_chunk(AttnTeamSmem<D, G> &sm, const bf16 *Ks, const bf16 *Vs, int n_main, bool extra, float scale,
-                           AttnAcc<D> &acc, int tid, int bar_id) {
-  constexpr int NC = D / 8;                  // 16-byte chunks per row
-  constexpr int THD = kAttnThreads / G;      // threads per head
-  constexpr int CP = NC / 4;                 // chunks per part
-  constexpr int SLOTS = THD / 4;             // position slots per head
-  constexpr int PPT = kKvChunk / SLOTS;      // positions per thread
-  constexpr int WPH = THD / 32;              // warps per head
-  constexpr int NPH = THD / NC;              // P.V position phases
-  static_assert(CP >= 1 && (CP & (CP - 1)) == 0 && PPT >= 1 && NPH >= 1, "unsupported attention shape");
+__device__ __forceinline__ void attn_chunk(const bf16 (&q_b)[G][D], const bf16 *knew, const bf16 *vnew,
+                                           const bf16 *Ks, const bf16 *Vs, int n_main, bool extra, float scale,
+                                           AttnWarpAcc<D, G> &acc, int tid) {
+  constexpr int CPP = D / 32, DL = D / 32;
   const int lane = tid & 31, warp = tid >> 5;
-  const int hd = tid / THD, u = tid % THD, part = u % 4, ps = u / 4;
   const int n = n_main + (extra ? 1 : 0);
-  // This part's q chunks in the rotated order of the K loads (the rotation depends on the
-  // lane only), BF16 pairs.
-  uint4 qr[CP];
+  const int i = warp * 8 + (lane >> 2);
+  const bool valid = i < n;
+  float sc[G];
+  {
+    float lo[G], hi[G];
 #pragma unroll
-  for (int j = 0; j < CP; ++j) {
-    const int cj = (j + ps * (CP > 1 ? CP / 2 : 1) + (part >> 1)) & (CP - 1);
-    qr[j] = *reinterpret_cast<const uint4 *>(&sm.q_b[hd][(part * CP + cj) * 8]);
-  }
-  float sc[PPT];
+    for (int h = 0; h < G; ++h) lo[h] = hi[h] = 0.f;
+    if (valid) {
+      const bf16 *kr = i < n_main ? Ks + size_t(i) * D : knew;
 #pragma unroll
-  for (int k = 0; k < PPT; ++k) {
-    const int i = ps + k * SLOTS;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    if (i < n) {
-      const bf16 *kr = i < n_main ? Ks + size_t(i) * D : sm.knew;
+      for (int j = 0; j < CPP; ++j) {
+        const int c = attn_kchunk<D>(lane, j);
+        const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + c * 8);
 #pragma unroll
-      for (int j = 0; j < CP; ++j) {
-        const int cj = (j + ps * (CP > 1 ? CP / 2 : 1) + (part >> 1)) & (CP - 1);
-        const uint4 k8 = *reinterpret_cast<const uint4 *>(kr + (part * CP + cj) * 8);
-        const uint4 q8 = qr[j];
-        fma_bf16x2(a0, a1, q8.x, k8.x);
-        fma_bf16x2(a2, a3, q8.y, k8.y);
-        fma_bf16x2(a0, a1, q8.z, k8.z);
-        fma_bf16x2(a2, a3, q8.w, k8.w);
+        for (int h = 0; h < G; ++h) {
+          const uint4 q8 = *reinterpret_cast<const uint4 *>(&q_b[h][c * 8]);
+          fma_bf16x2(lo[h], hi[h], q8.x, k8.x);
+          fma_bf16x2(lo[h], hi[h], q8.y, k8.y);
+          fma_bf16x2(lo[h], hi[h], q8.z, k8.z);
+          fma_bf16x2(lo[h], hi[h], q8.w, k8.w);
+        }
       }
     }
-    float dot = (a0 + a1) + (a2 + a3);
-    dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
-    dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
-    sc[k] = i < n ? dot * scale : -INFINITY;
-  }
-  float mx = sc[0];
 #pragma unroll
-  for (int k = 1; k < PPT; ++k) mx = fmaxf(mx, sc[k]);
-  mx = warp_max(mx);
-  if (lane == 0) sm.red[0][warp] = mx;
-  team_sync(bar_id);
-  float mc = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < WPH; ++w) mc = fmaxf(mc, sm.red[0][hd * WPH + w]);
-  float pt = 0.f;
-#pragma unroll
-  for (int k = 0; k < PPT; ++k) {
-    const int i = ps + k * SLOTS;
-    const float pe = i < n ? expf(sc[k] - mc) : 0.f;
-    if (part == 0) sm.p_s[hd][i] = pe;
-    pt += pe;
-  }
-  const float psum = warp_sum(part == 0 ? pt : 0.f);
-  if (lane == 0) sm.red[1][warp] = psum;
-  team_sync(bar_id);
-  // P.V partials.
-  {
-    const int dg = u % NC, q = u / NC;
-    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int r = q; r < n; r += NPH) {
-      const float pr = sm.p_s[hd][r];
-      const uint4 v8 = *reinterpret_cast<const uint4 *>((r < n_main ? Vs + size_t(r) * D : sm.vnew) + dg * 8);
-      o8[0] = fmaf(pr, bf_lo(v8.x), o8[0]);
-      o8[1] = fmaf(pr, bf_hi(v8.x), o8[1]);
-      o8[2] = fmaf(pr, bf_lo(v8.y), o8[2]);
-      o8[3] = fmaf(pr, bf_hi(v8.y), o8[3]);
-      o8[4] = fmaf(pr, bf_lo(v8.z), o8[4]);
-      o8[5] = fmaf(pr, bf_hi(v8.z), o8[5]);
-      o8[6] = fmaf(pr, bf_lo(v8.w), o8[6]);
-      o8[7] = fmaf(pr, bf_hi(v8.w), o8[7]);
+    for (int h = 0; h < G; ++h) {
+      float d = lo[h] + hi[h];
+      d += __shfl_xor_sync(0xFFFFFFFFu, d, 1);
+      d += __shfl_xor_sync(0xFFFFFFFFu, d, 2);
+      sc[h] = valid ? d * scale : -INFINITY;
     }
-    float *dst = &sm.pvp[q][hd * D + dg * 8];
-    *reinterpret_cast<float4 *>(dst) = make_float4(o8[0], o8[1], o8[2], o8[3]);
-    *reinterpret_cast<float4 *>(dst + 4) = make_float4(o8[4], o8[5], o8[6], o8[7]);
+  }
+  float pv[G], alpha[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float mc = sc[h];
+    mc = fmaxf(mc, __shfl_xor_sync(0xFFFFFFFFu, mc, 4));
+    mc = fmaxf(mc, __shfl_xor_sync(0xFFFFFFFFu, mc, 8));
+    mc = fmaxf(mc, __shfl_xor_sync(0xFFFFFFFFu, mc, 16));
+    const float mn = fmaxf(acc.m[h], mc);
+    // mn is -inf only while the warp has seen no position at all (then nothing changes).
+    alpha[h] = mn == -INFINITY ? 1.f : expf(acc.m[h] - mn);
+    pv[h] = valid ? expf(sc[h] - mn) : 0.f;
+    float ps = pv[h];
+    ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 4);
+    ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 8);
+    ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 16);
+    acc.l[h] = acc.l[h] * alpha[h] + ps;
+    acc.m[h] = mn;
+#pragma unroll
+    for (int k = 0; k < DL; ++k) acc.o[h][k] *= alpha[h];
+  }
+  const int nw = min(8, n - warp * 8);  // the warp's valid rows (uniform across the warp)
+#pragma unroll
+  for (int pp = 0; pp < 8; ++pp) {
+    float w[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) w[h] = __shfl_sync(0xFFFFFFFFu, pv[h], pp * 4);
+    if (pp < nw) {
+      const int r = warp * 8 + pp;
+      const bf16 *vr = (r < n_main ? Vs + size_t(r) * D : vnew) + lane * DL;
+      float v[DL];
+      if constexpr (DL == 4) {
+        const uint2 v4 = *reinterpret_cast<const uint2 *>(vr);
+        v[0] = bf_lo(v4.x), v[1] = bf_hi(v4.x), v[2] = bf_lo(v4.y), v[3] = bf_hi(v4.y);
+      } else {
+        const uint32_t v2 = *reinterpret_cast<const uint32_t *>(vr);
+        v[0] = bf_lo(v2), v[1] = bf_hi(v2);
+      }
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int k = 0; k < DL; ++k) acc.o[h][k] = fmaf(w[h], v[k], acc.o[h][k]);
+    }
+  }
+}
+
+// Combine the eight warps' states (in warp order) into the unit's (max, sum, output) for
+// thread tid < G x D. Ends with a barrier; sm.pvp is the exchange space.
+template <int D, int G>
+__device__ __forceinline__ AttnAcc<D> attn_combine(AttnTeamSmem<D, G> &sm, const AttnWarpAcc<D, G> &acc, int tid,
+                                                   int bar_id) {
+  constexpr int DL = D / 32, NW = kAttnThreads / 32;
+  static_assert(sizeof(sm.pvp) >= sizeof(float) * NW * G * D, "combine space");
+  const int lane = tid & 31, warp = tid >> 5;
+  float *wo = &sm.pvp[0][0];  // [warp][G][D]
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+#pragma unroll
+    for (int k = 0; k < DL; ++k) wo[(warp * G + h) * D + lane * DL + k] = acc.o[h][k];
+    if (lane == 0) {
+      sm.wml[warp][h][0] = acc.m[h];
+      sm.wml[warp][h][1] = acc.l[h];
+    }
   }
   team_sync(bar_id);
+  AttnAcc<D> r{-INFINITY, 0.f, 0.f};
   if (tid < G * D) {
-    const int oh = tid / D;
-    float oc = 0.f;
+    const int h = tid / D, d = tid % D;
+    float M = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < NPH; ++q) oc += sm.pvp[q][tid];
-    float lcv = 0.f, mcv = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wml[w][h][0]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
 #pragma unroll
-    for (int w = 0; w < WPH; ++w) {
-      lcv += sm.red[1][oh * WPH + w];
-      mcv = fmaxf(mcv, sm.red[0][oh * WPH + w]);
+      for (int w = 0; w < NW; ++w) {
+        const float mw = sm.wml[w][h][0];
+        if (mw == -INFINITY) continue;
+        const float c = expf(mw - M);
+        L += sm.wml[w][h][1] * c;
+        O += wo[(w * G + h) * D + d] * c;
+      }
     }
-    const float mn = fmaxf(acc.m, mcv);
-    const float ca = expf(acc.m - mn), cb = expf(mcv - mn);
-    acc.l = acc.l * ca + lcv * cb;
-    acc.o = acc.o * ca + oc * cb;
-    acc.m = mn;
+    r.m = M, r.l = L, r.o = O;
   }
   team_sync(bar_id);
+  return r;
 }
 
 // Merge the n_active split partials of the G heads of (row, kv_head) into the BF16 head
@@ -418,12 +492,30 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
       }
       M = Mb;
     }
-    bf16 *o = p.out + size_t(row) * p.out_stride + (kvh * G + hd) * D + d;
     const bf16 v = f2bf(O * (1.0f / Ls));
-    *o = v;
-    for (int i = 0; i < p.out_ndst; ++i) *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(o) + p.out_dst[i]) = v;
+    if (p.out_ll) {
+      // Adjacent dims pair up in one flagged word (even lane stores; tid < G x D is whole warps).
+      const bf16 v1 = __ushort_as_bfloat16(
+          (unsigned short)__shfl_down_sync(0xFFFFFFFFu, (unsigned)__bfloat16_as_ushort(v), 1));
+      if ((d & 1) == 0)
+        ll_store_all(p.out_ll + size_t(row) * p.out_ll_stride + (((kvh * G + hd) * D + d) >> 1), pack_bf16x2(v, v1),
+                     p.out_flag, p.out_ndst, p.out_dst);
+    } else {
+      bf16 *o = p.out + size_t(row) * p.out_stride + (kvh * G + hd) * D + d;
+      *o = v;
+      for (int i = 0; i < p.out_ndst; ++i) *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(o) + p.out_dst[i]) = v;
+    }
   }
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
+}
+
+// Flagged output of an inactive row: the G heads of kv head `kvh` as zero words with the
+// step's flag, so the consumers of every row's words never wait on a row without work.
+template <int D, int G>
+__device__ void attn_write_inactive(const DecodeAttnParams &p, int row, int kvh, int tid) {
+  for (int w = tid; w < G * D / 2; w += kAttnThreads)
+    ll_store_all(p.out_ll + size_t(row) * p.out_ll_stride + ((kvh * G * D) >> 1) + w, 0u, p.out_flag, p.out_ndst,
+                 p.out_dst);
 }
 
 // Step 3: store this unit's partial, count its arrival, and merge when it is the last of

@@ -83,6 +83,10 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
       const size_t ox = take(size_t(max_rows) * d.hidden * 2), oa = take(size_t(max_rows) * f.qdim() * 2),
                    om = take(size_t(max_rows) * f.ffn * 2), ol = take(size_t(max_rows) * s->logit_stride * 2),
                    oc = take(size_t(s->n_ctr) * 4);
+      // Flagged words: 8 bytes per two values, for the persistent kernel's 1 or 2 rows.
+      const size_t llr = size_t(std::min(max_rows, 2));
+      const size_t oxl = take(llr * d.hidden * 4), oql = take(llr * d.qkv_rows() * 4), oal = take(llr * f.qdim() * 4),
+                   oml = take(llr * f.ffn * 4);
       s->xregion = dmalloc<char>(off);
       s->xregion_bytes = off;
       YAR_CUDA(cudaMemset(s->xregion, 0, off));
@@ -91,6 +95,11 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
       s->mlp = reinterpret_cast<bf16 *>(s->xregion + om);
       s->logits = reinterpret_cast<bf16 *>(s->xregion + ol);
       s->d_ctr = reinterpret_cast<int *>(s->xregion + oc);
+      s->x_ll = reinterpret_cast<uint2 *>(s->xregion + oxl);
+      s->qkv_ll = reinterpret_cast<uint2 *>(s->xregion + oql);
+      s->attn_ll = reinterpret_cast<uint2 *>(s->xregion + oal);
+      s->mlp_ll = reinterpret_cast<uint2 *>(s->xregion + oml);
+      s->ll_bytes = off - oxl;
     }
     s->max_splits = 32;
     s->attn_part = dmalloc<float>(size_t(max_rows) * d.heads * s->max_splits * (d.head_dim + 2));
@@ -144,7 +153,7 @@ void free_session(Session *s) {
                                                s->attn_part, s->attn_count, s->px, s->ph, s->pqkv, s->pq,
                                                s->pattn, s->pmlp, s->pids, s->d_req, s->d_out_tokens,
                                                s->d_scores, s->d_epoch, s->d_trace, s->gemm_ws, s->tp_send,
-                                               s->tp_recv})
+                                               s->tp_recv, s->d_layer_dump})
     if (p) cudaFree(p);
   if (s->h_pinned) cudaFreeHost(s->h_pinned);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -277,6 +286,7 @@ void row_prefill(Session &s, int row, const int32_t *ids, int n, int phase, int 
   const int start0 = s.pos[row];
   if (start0 + n > s.capacity[row]) throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
   cudaStream_t st = s.stream;
+  YAR_CUDA(cudaMemsetAsync(s.d_error, 0, sizeof(int), st));
   const int H = d.hidden, QKV = d.qkv_rows();
   // Linears on the tcgen05 tensor-core GEMM where the shape allows (K % 64, N % 128);
   // otherwise the mma.sync GEMM.
@@ -341,17 +351,30 @@ static bool use_persistent(Session &s, int n_rows) {
 // epoch are never zeroed then (targets grow with the epoch), except every 2^20 steps, when
 // all ranks stop at a barrier, zero them, and meet again before any of them goes on.
 static void reset_step_sync(Session &s) {
+  // The flagged words restart with the epoch: their flags (step, operation) must not match
+  // anything written before the reset.
   if (s.m->tp_world == 1 || !s.tp_mapped) {
     YAR_CUDA(cudaMemsetAsync(s.d_ctr, 0, s.n_ctr * sizeof(int), s.stream));
     YAR_CUDA(cudaMemsetAsync(s.d_epoch, 0, sizeof(int), s.stream));
+    YAR_CUDA(cudaMemsetAsync(s.x_ll, 0, s.ll_bytes, s.stream));
   } else if (s.tp_epoch_steps >= (1ll << 20)) {
     tp_barrier(*s.m, s.tp_send, s.stream);
     YAR_CUDA(cudaMemsetAsync(s.d_ctr, 0, s.n_ctr * sizeof(int), s.stream));
     YAR_CUDA(cudaMemsetAsync(s.d_epoch, 0, sizeof(int), s.stream));
+    YAR_CUDA(cudaMemsetAsync(s.x_ll, 0, s.ll_bytes, s.stream));
     tp_barrier(*s.m, s.tp_send, s.stream);
     s.tp_epoch_steps = 0;
   }
   YAR_CUDA(cudaMemsetAsync(s.attn_count, 0, size_t(s.max_rows) * s.m->d.kv_heads * sizeof(int), s.stream));
+}
+
+// Hidden-state record (session option): the residual rows into slot `slot` of the record
+// (0 = embedding, l + 1 = after layer l).
+static void dump_hidden(Session &s, int slot, int n_rows) {
+  if (!s.d_layer_dump) return;
+  const size_t H = size_t(s.m->d.hidden);
+  YAR_CUDA(cudaMemcpyAsync(s.d_layer_dump + size_t(slot) * s.max_rows * H, s.x, size_t(n_rows) * H * sizeof(bf16),
+                           cudaMemcpyDeviceToDevice, s.stream));
 }
 
 // Batches of at least this many rows run the decode linears as tcgen05 GEMMs: the weights
@@ -379,6 +402,7 @@ static void decode_forward_batched(Session &s, int n_rows, int phase) {
   const int splits = std::max(1, (2 * 5 * m.sm_count + n_rows * kvh - 1) / (n_rows * kvh));
   const LayerShape ls = layer_shape(m);
   launch_embed_rows(m, s, n_rows, st);
+  dump_hidden(s, 0, n_rows);
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
     launch_rmsnorm_rows(s.x, w.ln1, n_rows, H, d.eps, s.ph, st);
@@ -392,6 +416,7 @@ static void decode_forward_batched(Session &s, int n_rows, int phase) {
     tp_gather(m, s, s.mlp, n_rows, ls.Ff, ls.Fl);
     gemm(s.mlp, ls.Ff, w.down, ls.Hs, s.x + ls.h0, H, kEpiResidual);
     tp_gather(m, s, s.x, n_rows, H, ls.Hs);
+    dump_hidden(s, l + 1, n_rows);
   }
   // Head: GEMM over the normalized rows (odd last phase row and ABC extra row as GEMVs).
   launch_rmsnorm_rows(s.x, m.final_norm, n_rows, H, d.eps, s.ph, st);
@@ -413,6 +438,7 @@ static void decode_forward(Session &s, int n_rows, int phase) {
   const LayerShape ls = layer_shape(m);
   const int H = d.hidden;
   launch_embed_rows(m, s, n_rows, st);
+  dump_hidden(s, 0, n_rows);
   for (int l = 0; l < d.layers; ++l) {
     const LayerWeights &w = m.layers[l];
     launch_gemv(w.qkv, d.qkv_rows(), H, s.x, H, w.ln1, d.eps, s.qkv, d.qkv_rows(), kEpiStore, n_rows, s.d_error,
@@ -428,6 +454,7 @@ static void decode_forward(Session &s, int n_rows, int phase) {
     launch_gemv(w.down, ls.Hs, ls.Ff, s.mlp, ls.Ff, nullptr, d.eps, s.x + ls.h0, H, kEpiResidual, n_rows, s.d_error,
                 m.sm_count, st);
     tp_gather(m, s, s.x, n_rows, H, ls.Hs);
+    dump_hidden(s, l + 1, n_rows);
   }
   project(m, s, s.x, H, false, n_rows, phase, s.logits);
 }
@@ -451,13 +478,20 @@ void rows_step(Session &s, const int *rows, const int32_t *tokens, int n, int ph
   cudaStream_t st = s.stream;
   YAR_CUDA(cudaMemcpyAsync(s.d_active, active.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
   YAR_CUDA(cudaMemcpyAsync(s.d_token, tok.data(), hi * sizeof(int), cudaMemcpyHostToDevice, st));
+  YAR_CUDA(cudaMemsetAsync(s.d_error, 0, sizeof(int), st));
   reset_step_sync(s);
   decode_forward(s, hi, phase);
   s.tp_epoch_steps += 1;
   YAR_CUDA(cudaStreamSynchronize(st));
   int err = 0;
   YAR_CUDA(cudaMemcpy(&err, s.d_error, sizeof(int), cudaMemcpyDeviceToHost));
-  if (err) throw Error("RuntimeError", "device error flags " + std::to_string(err));
+  if (err) {
+    // The step is void: the rows keep their positions (the device latch may have advanced)
+    // and the session stays usable for the next call.
+    YAR_CUDA(cudaMemcpyAsync(s.d_pos, s.pos.data(), s.max_rows * sizeof(int), cudaMemcpyHostToDevice, st));
+    YAR_CUDA(cudaStreamSynchronize(st));
+    throw Error("RuntimeError", "device error flags " + std::to_string(err));
+  }
   for (int i = 0; i < n; ++i) s.pos[rows[i]] += 1;
 }
 
@@ -593,12 +627,15 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
   YAR_CUDA(cudaEventCreate(&ev1));
   YAR_CUDA(cudaEventRecord(ev0, st));
   float decode_ms = 0.f;
+  double host_launch_s = 0;  // host time spent enqueuing the graph replays
   while (steps < smp.max_tokens && !done) {
     if (cancel && cancel(cancel_ctx)) throw Error("InterruptedError", std::string("Cancelled during ") +
                                                                           (phase == kPhaseAbc ? "abc" : "semantic"));
     const int k = std::min(kChunk, smp.max_tokens - steps);
     YAR_CUDA(cudaEventRecord(ev0, st));
+    const double h0 = now_s();
     for (int i = 0; i < k; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
+    host_launch_s += now_s() - h0;
     s.tp_epoch_steps += k;
     YAR_CUDA(cudaEventRecord(ev1, st));
     steps += k;
@@ -659,7 +696,8 @@ std::string generate(Session &s, const int32_t *prefix, int n_prefix, const ::ya
                            {"tp_exchange", s.m->tp_world == 1 ? "none" : s.tp_mapped ? "peer_stores" : "nccl"},
                            {"backend", "cuda-sm100a"},
                            {"decode_steps", steps},
-                           {"decode_device_ms", decode_ms}};
+                           {"decode_device_ms", decode_ms},
+                           {"host_launch_ms", 1000 * host_launch_s}};
   return timing.dump();
 }
 
@@ -722,109 +760,147 @@ void sample_host(Model &m, const uint16_t *cond, const uint16_t *uncond, int n, 
 }
 
 
-// Many independent requests decoded in lockstep on rows 0..n-1 (no CFG): each is prefilled
-// on its own row, then every step samples all unfinished requests (one sampler CTA each,
-// own seed) and forwards all rows at once (rows >= 16 use the batched tcgen05 forward).
-// A request stops at its end token or after max_tokens; finished rows are skipped by the
-// sampler, embedding and attention.
-std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const int32_t *prefix_lens,
-                           const ::yar_sampling &smp, const uint64_t *seeds, int phase, int legacy_off,
-                           int32_t *out_tokens, int *n_out, int *truncated) {
+// Many independent requests (no CFG) served from a queue on `slots` rows of the session —
+// continuous batching. Request i is prefilled on a free row when one is available; every
+// step samples all rows' unfinished requests (one sampler CTA each, own seed and sampling)
+// and forwards all rows at once (16+ rows use the batched tcgen05 forward). The step graph
+// reads each row's request record and activity from device memory, so a row whose request
+// ended (end token or its max_tokens) is refilled between decode chunks with the next
+// waiting request (its prefill, a fresh record, the row active again) without a new graph.
+// Request i's native tokens (end token excluded) land at out_tokens[sum of the earlier
+// requests' max_tokens ..].
+std::string generate_requests(Session &s, int n_req, int slots, const int32_t *prefixes, const int32_t *prefix_lens,
+                              const ::yar_sampling *smps, const uint64_t *seeds, int phase, int legacy_off,
+                              int32_t *out_tokens, int *n_out, int *truncated) {
   const Model &m = *s.m;
   phase_rows(m.d, phase);
-  validate_sampling(smp);
-  if (n_req < 1 || n_req > s.max_rows) throw Error("ValueError", "request count must be in [1, session rows]");
-  if (smp.max_tokens > s.out_cap) throw Error("ValueError", "max_tokens exceeds the session output capacity");
-  size_t off = 0;
-  std::vector<size_t> starts(n_req);
+  if (n_req < 1) throw Error("ValueError", "request count must be at least 1");
+  if (slots <= 0) slots = std::min(n_req, s.max_rows);
+  if (slots > s.max_rows || slots > n_req) throw Error("ValueError", "slots must be in [1, min(requests, session rows)]");
+  std::vector<size_t> starts(n_req), outs(n_req);
+  size_t off = 0, out_off = 0;
   for (int r = 0; r < n_req; ++r) {
-    const int n = prefix_lens[r];
+    validate_sampling(smps[r]);
+    const int n = prefix_lens[r], mt = smps[r].max_tokens;
     if (n < 1) throw Error("ValueError", "AR prefix must contain at least one token");
-    if (size_t(n) + size_t(smp.max_tokens) > size_t(m.d.context))
+    if (size_t(n) + size_t(mt) > size_t(m.d.context))
       throw Error("ValueError", "Prefix + requested generation budget exceeds 24576; no implicit truncation");
-    if (n + smp.max_tokens > s.max_ctx)
-      throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
+    if (n + mt > s.max_ctx) throw Error("ValueError", "KV cache capacity exceeded; generation was not shortened");
+    if (mt > s.out_cap) throw Error("ValueError", "max_tokens exceeds the session output capacity");
     if (seeds[r] >= (uint64_t(1) << 63)) throw Error("ValueError", "seed must be an integer in [0, 2**63)");
     starts[r] = off;
     off += size_t(n);
+    outs[r] = out_off;
+    out_off += size_t(mt);
   }
   YAR_CUDA(cudaSetDevice(m.device));
-  YAR_CUDA(cudaStreamSynchronize(s.stream));
-  const double t0 = now_s();
-  for (int r = 0; r < n_req; ++r) {
-    row_reset(s, r, prefix_lens[r] + smp.max_tokens);
-    row_prefill(s, r, prefixes + starts[r], prefix_lens[r], phase, 0, nullptr, nullptr);
-  }
-  const double prefill_seconds = now_s() - t0;
-  std::vector<RequestState> reqs(n_req);
-  for (int r = 0; r < n_req; ++r) reqs[r] = make_request(m, s, r, -1, phase, smp, 1.0, seeds[r], 0, legacy_off != 0);
   cudaStream_t st = s.stream;
-  YAR_CUDA(cudaMemcpyAsync(s.d_req, reqs.data(), n_req * sizeof(RequestState), cudaMemcpyHostToDevice, st));
-  std::vector<int> act(n_req, 1);
-  YAR_CUDA(cudaMemcpyAsync(s.d_active, act.data(), n_req * sizeof(int), cudaMemcpyHostToDevice, st));
+  YAR_CUDA(cudaStreamSynchronize(st));
+  const double t0 = now_s();
+  double prefill_seconds = 0;
+  std::vector<int> slot_req(slots, -1);  // request on each row (-1: none)
+  int next = 0, admitted_late = 0;
+  // Prefill request r on `row` and arm its sampler record.
+  auto admit = [&](int row, int r) {
+    const double p0 = now_s();
+    row_reset(s, row, prefix_lens[r] + smps[r].max_tokens);
+    row_prefill(s, row, prefixes + starts[r], prefix_lens[r], phase, 0, nullptr, nullptr);
+    prefill_seconds += now_s() - p0;
+    const RequestState req = make_request(m, s, row, -1, phase, smps[r], 1.0, seeds[r], 0, legacy_off != 0);
+    YAR_CUDA(cudaMemcpyAsync(s.d_req + row, &req, sizeof(req), cudaMemcpyHostToDevice, st));
+    const int one = 1;
+    YAR_CUDA(cudaMemcpyAsync(s.d_active + row, &one, sizeof(int), cudaMemcpyHostToDevice, st));
+    YAR_CUDA(cudaStreamSynchronize(st));  // the host values above are on the stack
+    slot_req[row] = r;
+  };
+  for (int row = 0; row < slots; ++row) admit(row, next++);
   YAR_CUDA(cudaMemsetAsync(s.d_error, 0, sizeof(int), st));
   reset_step_sync(s);
   YAR_CUDA(cudaStreamSynchronize(st));
-  cudaGraphExec_t exec = step_graph(s, n_req, n_req, phase);
+  cudaGraphExec_t exec = step_graph(s, slots, slots, phase);
 
   const int kChunk = 16;
-  int steps = 0;
+  int steps = 0, finished = 0;
   float decode_ms = 0.f;
   cudaEvent_t ev0, ev1;
   YAR_CUDA(cudaEventCreate(&ev0));
   YAR_CUDA(cudaEventCreate(&ev1));
-  std::vector<int> prog(size_t(n_req) * 4);  // (step, done, n_out, error) per request
-  bool all_done = false;
-  while (steps < smp.max_tokens && !all_done) {
-    const int k = std::min(kChunk, smp.max_tokens - steps);
-    YAR_CUDA(cudaEventRecord(ev0, st));
-    for (int i = 0; i < k; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
-    s.tp_epoch_steps += k;
-    YAR_CUDA(cudaEventRecord(ev1, st));
-    steps += k;
-    YAR_CUDA(cudaMemcpy2DAsync(prog.data(), 4 * sizeof(int), &s.d_req[0].step, sizeof(RequestState), 4 * sizeof(int),
-                               n_req, cudaMemcpyDeviceToHost, st));
-    int derr = 0;
-    YAR_CUDA(cudaMemcpyAsync(&derr, s.d_error, sizeof(int), cudaMemcpyDeviceToHost, st));
-    YAR_CUDA(cudaStreamSynchronize(st));
-    float ms = 0.f;
-    YAR_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
-    decode_ms += ms;
-    all_done = true;
-    for (int r = 0; r < n_req; ++r) {
-      if (prog[4 * r + 3] || derr)
-        throw Error("RuntimeError", "device sampler/forward error " + std::to_string(prog[4 * r + 3]) + "/" +
-                                        std::to_string(derr));
-      if (!prog[4 * r + 1] && prog[4 * r] < smp.max_tokens) all_done = false;
+  std::vector<int> prog(size_t(slots) * 4);  // (step, done, n_out, error) per row's record
+  long long total = 0;
+  try {
+    while (finished < n_req) {
+      YAR_CUDA(cudaEventRecord(ev0, st));
+      for (int i = 0; i < kChunk; ++i) YAR_CUDA(cudaGraphLaunch(exec, st));
+      s.tp_epoch_steps += kChunk;
+      YAR_CUDA(cudaEventRecord(ev1, st));
+      steps += kChunk;
+      YAR_CUDA(cudaMemcpy2DAsync(prog.data(), 4 * sizeof(int), &s.d_req[0].step, sizeof(RequestState),
+                                 4 * sizeof(int), slots, cudaMemcpyDeviceToHost, st));
+      int derr = 0;
+      YAR_CUDA(cudaMemcpyAsync(&derr, s.d_error, sizeof(int), cudaMemcpyDeviceToHost, st));
+      YAR_CUDA(cudaStreamSynchronize(st));
+      float ms = 0.f;
+      YAR_CUDA(cudaEventElapsedTime(&ms, ev0, ev1));
+      decode_ms += ms;
+      for (int row = 0; row < slots; ++row) {
+        const int r = slot_req[row];
+        if (r < 0) continue;
+        const int *pg = &prog[4 * row];
+        if (pg[3] || derr)
+          throw Error("RuntimeError", "device sampler/forward error " + std::to_string(pg[3]) + "/" +
+                                          std::to_string(derr));
+        if (!pg[1] && pg[0] < smps[r].max_tokens) continue;
+        // Request r is finished: collect its tokens, release its pages, refill the row.
+        const int dn = pg[2];
+        YAR_CUDA(cudaMemcpy(out_tokens + outs[r], s.d_out_tokens + size_t(row) * s.out_cap,
+                            size_t(dn) * sizeof(int32_t), cudaMemcpyDeviceToHost));
+        n_out[r] = dn;
+        truncated[r] = pg[0] > dn ? 0 : 1;  // a sampled end token is counted in step, not stored
+        total += dn;
+        ++finished;
+        for (int p : s.row_pages[row]) s.free_pages.push_back(p);
+        s.row_pages[row].clear();
+        s.capacity[row] = 0;
+        slot_req[row] = -1;
+        if (next < n_req) {
+          admit(row, next++);
+          ++admitted_late;
+        }
+      }
     }
+  } catch (...) {
+    cudaEventDestroy(ev0);
+    cudaEventDestroy(ev1);
+    throw;
   }
   YAR_CUDA(cudaEventDestroy(ev0));
   YAR_CUDA(cudaEventDestroy(ev1));
-  long long total = 0;
-  for (int r = 0; r < n_req; ++r) {
-    const int dn = prog[4 * r + 2];
-    YAR_CUDA(cudaMemcpy(out_tokens + size_t(r) * smp.max_tokens, s.d_out_tokens + size_t(r) * s.out_cap,
-                        size_t(dn) * sizeof(int32_t), cudaMemcpyDeviceToHost));
-    n_out[r] = dn;
-    truncated[r] = prog[4 * r] > dn ? 0 : 1;  // a sampled end token is counted in step, not stored
-    total += dn;
-    for (int p : s.row_pages[r]) s.free_pages.push_back(p);
-    s.row_pages[r].clear();
-    s.capacity[r] = 0;
-  }
   const double seconds = now_s() - t0;
   nlohmann::json timing = {{"seconds", seconds},
                            {"prefill_seconds", prefill_seconds},
                            {"requests", n_req},
+                           {"slots", slots},
+                           {"refills", admitted_late},
                            {"content_tokens", total},
                            {"decode_steps", steps},
                            {"decode_device_ms", decode_ms},
                            {"execution", "cuda_graph"},
-                           {"forward", n_req >= kBatchedRows ? "batched_tcgen05" : "per_row"},
+                           {"forward", slots >= kBatchedRows ? "batched_tcgen05" : "per_row"},
                            {"tensor_parallel", s.m->tp_world},
                            {"tp_exchange", s.m->tp_world == 1 ? "none" : s.tp_mapped ? "peer_stores" : "nccl"},
                            {"backend", "cuda-sm100a"}};
   return timing.dump();
+}
+
+// Many independent requests decoded together on rows 0..n-1 (no CFG, one sampling for all):
+// generate_requests with one row per request.
+std::string generate_batch(Session &s, int n_req, const int32_t *prefixes, const int32_t *prefix_lens,
+                           const ::yar_sampling &smp, const uint64_t *seeds, int phase, int legacy_off,
+                           int32_t *out_tokens, int *n_out, int *truncated) {
+  if (n_req < 1 || n_req > s.max_rows) throw Error("ValueError", "request count must be in [1, session rows]");
+  const std::vector<::yar_sampling> smps(n_req, smp);
+  return generate_requests(s, n_req, n_req, prefixes, prefix_lens, smps.data(), seeds, phase, legacy_off, out_tokens,
+                           n_out, truncated);
 }
 
 }  // namespace yar

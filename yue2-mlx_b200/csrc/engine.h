@@ -226,6 +226,11 @@ struct Session {
   float *gemm_ws = nullptr;  // split-K partials of the tcgen05 GEMM
   size_t gemm_ws_floats = 0;
   int prefetch_stages = 6;  // persistent kernel: L2 prefetch distance beyond the ring
+  int forced_splits = 0;    // decode attention splits per (row, kv head); 0 = automatic
+  int inject_op = 0;        // persistent kernel: operation whose wait is made to expire (0 = none)
+  // Hidden-state record of the last decode step (when enabled): [layers + 1][max_rows][hidden]
+  // BF16 — the embedding rows, then the residual rows after each layer.
+  bf16 *d_layer_dump = nullptr;
   unsigned long long *d_trace = nullptr;  // persistent-kernel timeline (when enabled)
   // Tensor parallelism: a rank's block of rows before ([rows][n]) and after
   // ([world][rows][n]) the all-gather.
@@ -236,6 +241,10 @@ struct Session {
   // out), so the persistent kernel stores its outputs straight into the peers' buffers.
   char *xregion = nullptr;
   size_t xregion_bytes = 0;
+  // Flagged-word activations of the persistent kernel (in the exchange region; rows up to
+  // 2): residual rows, raw q/k/v, attention heads, FFN activations; ll_bytes in all.
+  uint2 *x_ll = nullptr, *qkv_ll = nullptr, *attn_ll = nullptr, *mlp_ll = nullptr;
+  size_t ll_bytes = 0;
   bool tp_mapped = false;
   long long tp_dst[7] = {};
   std::vector<void *> tp_peer_regions;
@@ -250,6 +259,7 @@ constexpr int kCandCap = 2048;
 // in one round of longer units instead of two rounds of short ones. Counted with the whole
 // model's KV heads, so tensor-parallel ranks split each head's positions as one GPU does.
 inline int decode_max_splits(const Model &m, const Session &s, int n_rows) {
+  if (s.forced_splits > 0) return s.forced_splits < s.max_splits ? s.forced_splits : s.max_splits;
   const int per = m.sm_count / (m.full.kv_heads * (n_rows > 0 ? n_rows : 1));
   return per < 1 ? 1 : per < s.max_splits ? per : s.max_splits;
 }

@@ -97,17 +97,35 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (c0 < c1) issue(c0, 0);
+  int issued = 0;  // chunks whose copies were issued (uniform across the CTA)
+  if (c0 < c1) {
+    issue(c0, 0);
+    issued = 1;
+  }
   attn_qk<D, G>(p, sm, rs, row, kvh, split == sp.n_splits - 1, wv, tid, 1);
-  AttnAcc<D> acc;
-  attn_acc_init(acc);
+  AttnWarpAcc<D, G> wacc;
+  attn_warp_init(wacc);
+  // A bulk wait that expires is latched CTA-wide (`bad`): no further copies are issued and
+  // no chunk is computed; the unit still arrives (so the arrival count stays consistent)
+  // and, before the CTA exits, waits (bounded) for every copy it issued.
+  bool bad = false;
+  int done = 0;  // chunks whose copies completed
   for (int c = c0; c < c1; ++c) {
     const int slot = (c - c0) & 1, base = c * kKvChunk, n_main = min(kKvChunk, pos - base);
-    // The other buffer was last read by chunk c - 1, whose attn_chunk ended on a team
-    // barrier: it is free for chunk c + 1.
-    if (c + 1 < c1) issue(c + 1, slot ^ 1);
+    // The other buffer was last read by chunk c - 1, which every warp had finished at the
+    // barrier ending that iteration: it is free for chunk c + 1.
+    if (c + 1 < c1 && !bad) {
+      issue(c + 1, slot ^ 1);
+      ++issued;
+    }
     if (bulk) {
-      if (!mbar_wait(&kv_full[slot], unsigned((c - c0) >> 1) & 1u) && tid == 0 && p.error) atomicOr(p.error, 8);
+      const bool failed = !bad && !mbar_wait(&kv_full[slot], unsigned((c - c0) >> 1) & 1u);
+      if (__syncthreads_or(failed)) {
+        if (!bad && tid == 0 && p.error) atomicOr(p.error, 8);
+        bad = true;
+      }
+      if (bad) break;
+      done = c - c0 + 1;
     } else if (c + 1 < c1) {
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
@@ -115,8 +133,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(DecodeAttnParams p
     }
     team_sync(1);
     const bf16 *kb = kvbuf + size_t(slot) * 2 * kKvChunk * D;
-    attn_chunk<D, G>(sm, kb, kb + kKvChunk * D, n_main, pos - base < kKvChunk, p.g.scale, acc, tid, 1);
+    attn_chunk<D, G>(sm.q_b, sm.knew, sm.vnew, kb, kb + kKvChunk * D, n_main, pos - base < kKvChunk, p.g.scale,
+                     wacc, tid);
+    team_sync(1);
   }
+  if (bad)
+    for (int i = done; i < issued; ++i) mbar_wait(&kv_full[i & 1], unsigned(i >> 1) & 1u);
+  const AttnAcc<D> acc = attn_combine<D, G>(sm, wacc, tid, 1);
   attn_finish<D, G>(p, sm, acc, row, kvh, split, sp.n_splits, tid, 1);
 }
 

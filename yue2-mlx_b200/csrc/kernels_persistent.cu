@@ -4,7 +4,7 @@
 // Why: bs1 decode streams 2.95 GB of weights per token through ~143 dependent operations;
 // as separate kernels every boundary costs a ramp and a tail (several us), far more than
 // the bandwidth time of the small projections. Here each CTA's producer lane streams the
-// CTA's weight rows for every task of the step, in order, through a 5-stage (160 KB)
+// CTA's weight rows for every task of the step, in order, through a 6-stage (192 KB)
 // shared-memory ring, waiting only for ring space — never for activations — so HBM keeps
 // streaming while the consumer warps wait at operation boundaries.
 //
@@ -36,7 +36,7 @@
 
 namespace yar {
 
-constexpr int kPersistStages = 5;
+constexpr int kPersistStages = 6;
 constexpr int kPersistThreads = (kRingConsumers + 1) * 32;
 constexpr int kPersistMaxK = 6144;
 constexpr long long kCounterWaitLimit = 1ll << 22;  // polls of ~100 ns: under a second
@@ -53,11 +53,21 @@ struct PersistParams {
   int head_rows, extra_row;  // phase rows [0, head_rows) of `head`, plus one extra row or -1
   bf16 *x, *qkv, *attn, *mlp, *logits;
   int logit_stride;
+  // Flagged-word copies of the activations (two BF16 values + a flag per 8-byte word),
+  // [rows][stride words]: the residual rows, raw q/k/v, attention heads, FFN activations.
+  uint2 *x_ll, *qkv_ll, *attn_ll, *mlp_ll;
+  int x_lls, qkv_lls, attn_lls, mlp_lls;
   DecodeAttnParams ap;
   int *token, *pos, *cur_pos, *capacity, *active, *error;
   int *ctr, *epoch;
   int prefetch_stages;        // L2 prefetch distance beyond the ring, in stages
   unsigned long long *trace;  // optional [cta][op][8] SM-clock stamps (clock64), op = 5*layer + k
+  bf16 *layer_dump;           // optional [n_layers + 1][dump_stride rows][H]: x after embedding / each layer
+  int dump_stride;
+  // Failure-path testing: operation `inject_op` (1 + 5 l + k; 0 = none) waits for a flag
+  // nothing writes, and every flagged wait gives up after `ll_limit` polls.
+  int inject_op;
+  long long ll_limit;
   // Tensor parallelism: ranks, and the byte offsets from this rank's exchange region to
   // each peer's (as mapped here).
   int tp_world, tp_ndst;
@@ -150,24 +160,67 @@ __device__ __forceinline__ UnitInfo step_unit(const StepRows<NB> &r, int kvh_n, 
 
 constexpr int kMaxCtaChunks = 64;  // KV chunks of one CTA in one layer
 
+// Rotation of the group ranges per operation (o: 0 QKV, 2 O, 3 gate/up, 4 down), as
+// fractions of the grid: the CTAs holding one more group than the even share differ from
+// operation to operation, so no CTA carries the most stages of every operation of a layer
+// (on 148 SMs a CTA streams at most 22 stages per layer instead of 23) and every producer
+// gets ahead of its consumers somewhere in the layer.
+__host__ __device__ __forceinline__ int op_rotation(int o, int grid) {
+  const int num = o == 2 ? 125 : o == 3 ? 108 : o == 4 ? 75 : 0;
+  return num * grid / 148;
+}
+
 __device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// The flag of operation `op` of step `epoch` (op 0: the embedding; 1 + 5 l + k: operation
+// k of layer l — 0 QKV, 1 attention, 2 O, 3 gate/up, 4 down): unique per step and
+// operation (the epoch restarts with zeroed words), never zero.
+__device__ __forceinline__ uint32_t ll_flag(int epoch, int op, int n_layers) {
+  return uint32_t(epoch + 1) * uint32_t(5 * n_layers + 2) + uint32_t(op) + 1u;
+}
+
 // `dst`: the peer offsets (tp_ndst of them) the exchanged outputs are also stored at.
-__device__ __forceinline__ GemvTask layer_task(const PersistParams &p, int l, int k, const long long *dst) {
+// Operations read and write the flagged words: the residual rows x carry the flag of
+// their last writer (the embedding, O or down).
+__device__ __forceinline__ GemvTask layer_task(const PersistParams &p, int l, int k, const long long *dst, int epoch) {
   const LayerWeights &w = p.layers[l];
-  const int H = p.H, nd = p.tp_ndst;
+  const int H = p.H, nd = p.tp_ndst, nL = p.n_layers;
+  auto fl = [&](int op) { return ll_flag(epoch, op, nL); };
+  const uint32_t x_in = l == 0 ? fl(0) : fl(1 + 5 * (l - 1) + 4);  // x as the layer receives it
+  GemvTask t;
   switch (k) {
-    case 0: return GemvTask{w.qkv, p.QKV, H, p.x, H, w.ln1, p.eps, p.qkv, p.QKV, kEpiStore, 0, nullptr};
-    case 1: return GemvTask{w.o, p.HS, p.QD, p.attn, p.QD, nullptr, p.eps, p.x + p.h0, H, kEpiResidual, nd, dst};
-    case 2: return GemvTask{w.gu, 2 * p.FL, H, p.x, H, w.ln2, p.eps, p.mlp + p.f0, p.F, kEpiSwiGLU, nd, dst};
-    default: return GemvTask{w.down, p.HS, p.F, p.mlp, p.F, nullptr, p.eps, p.x + p.h0, H, kEpiResidual, nd, dst};
+    case 0:
+      t = GemvTask{w.qkv, p.QKV, H, p.x, H, w.ln1, p.eps, p.qkv, p.QKV, kEpiStore, 0, nullptr};
+      t.in_ll = p.x_ll, t.in_ll_stride = p.x_lls, t.in_flag = x_in;
+      t.out_ll = p.qkv_ll, t.out_ll_stride = p.qkv_lls, t.out_flag = fl(1 + 5 * l);
+      return t;
+    case 1:
+      t = GemvTask{w.o, p.HS, p.QD, p.attn, p.QD, nullptr, p.eps, p.x + p.h0, H, kEpiResidual, nd, dst};
+      t.in_ll = p.attn_ll, t.in_ll_stride = p.attn_lls, t.in_flag = fl(1 + 5 * l + 1);
+      t.out_ll = p.x_ll + p.h0 / 2, t.out_ll_stride = p.x_lls, t.out_flag = fl(1 + 5 * l + 2), t.res_flag = x_in;
+      return t;
+    case 2:
+      t = GemvTask{w.gu, 2 * p.FL, H, p.x, H, w.ln2, p.eps, p.mlp + p.f0, p.F, kEpiSwiGLU, nd, dst};
+      t.in_ll = p.x_ll, t.in_ll_stride = p.x_lls, t.in_flag = fl(1 + 5 * l + 2);
+      t.out_ll = p.mlp_ll + p.f0 / 2, t.out_ll_stride = p.mlp_lls, t.out_flag = fl(1 + 5 * l + 3);
+      return t;
+    default:
+      t = GemvTask{w.down, p.HS, p.F, p.mlp, p.F, nullptr, p.eps, p.x + p.h0, H, kEpiResidual, nd, dst};
+      t.in_ll = p.mlp_ll, t.in_ll_stride = p.mlp_lls, t.in_flag = fl(1 + 5 * l + 3);
+      t.out_ll = p.x_ll + p.h0 / 2, t.out_ll_stride = p.x_lls, t.out_flag = fl(1 + 5 * l + 4),
+      t.res_flag = fl(1 + 5 * l + 2);
+      return t;
   }
 }
-__device__ __forceinline__ GemvTask head_task(const PersistParams &p, const long long *dst) {
-  return GemvTask{p.head,   p.head_rows, p.H, p.x, p.H, p.final_norm, p.eps, p.logits, p.logit_stride, kEpiStore,
-                  p.tp_ndst, dst};
+// The head reads the final residual rows (flagged) and writes plain logits (read by the
+// next kernel).
+__device__ __forceinline__ GemvTask head_task(const PersistParams &p, const long long *dst, int epoch) {
+  GemvTask t{p.head,   p.head_rows, p.H, p.x, p.H, p.final_norm, p.eps, p.logits, p.logit_stride, kEpiStore,
+             p.tp_ndst, dst};
+  t.in_ll = p.x_ll, t.in_ll_stride = p.x_lls, t.in_flag = ll_flag(epoch, 1 + 5 * (p.n_layers - 1) + 4, p.n_layers);
+  return t;
 }
 
 struct KvChunkRef {
@@ -265,7 +318,8 @@ struct Producer {
       }
     }
     const int groups = (c.N + 7) / 8;
-    const int g0 = int(blockIdx.x) * groups / int(gridDim.x), g1 = (int(blockIdx.x) + 1) * groups / int(gridDim.x);
+    const int pos = (int(blockIdx.x) + (c.l == nL ? 0 : op_rotation(c.o, int(gridDim.x)))) % int(gridDim.x);
+    const int g0 = pos * groups / int(gridDim.x), g1 = (pos + 1) * groups / int(gridDim.x);
     c.KS = c.K / kRingPiece;
     c.g = g0;
     c.ks = 0;
@@ -360,8 +414,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nL = p.n_layers, H = p.H;
-  auto task = [&](int l, int k) { return layer_task(p, l, k, s_dst); };
-  const GemvTask head = head_task(p, s_dst);
   const bool tp = p.tp_world > 1;
   const int W = p.tp_world;
   if (threadIdx.x < kMaxTpWorld - 1) s_dst[threadIdx.x] = threadIdx.x < p.tp_ndst ? p.tp_dst[threadIdx.x] : 0;
@@ -378,6 +430,15 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   __syncthreads();
   const int epoch = s_epoch;
   const int all = int(gridDim.x);
+  // The op's task; an injected fault makes its input wait for a flag that is never written.
+  auto task = [&](int l, int k) {
+    GemvTask t = layer_task(p, l, k, s_dst, epoch);
+    t.ll_limit = p.ll_limit;
+    const int op = 1 + 5 * l + (k == 0 ? 0 : k + 1);
+    if (p.inject_op == op) t.in_flag ^= 0x80000000u;
+    return t;
+  };
+  auto fl = [&](int op) { return ll_flag(epoch, op, nL); };
 
   if (warp == kRingConsumers) {
     if (lane == 0) {
@@ -471,18 +532,19 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   const int c_embed = 0, c_head = 1 + 5 * nL;
   auto c_op = [&](int l, int k) { return 1 + 5 * l + k; };  // k: 0 qkv, 1 attn, 2 o, 3 gu, 4 down
 
-  // Embedding of each active row's token and the position latch (CTA 0).
+  // Embedding of each row's token (an inactive row: zeros) as flagged residual words, and
+  // the position latch (CTA 0).
   if (blockIdx.x == 0) {
     for (int b = 0; b < NB; ++b) {
-      if (!__ldcg(p.active + b)) continue;
-      int tok = __ldcg(p.token + b);
+      const bool act_row = __ldcg(p.active + b) != 0;
+      int tok = act_row ? __ldcg(p.token + b) : 0;
       if (tok < 0 || tok >= p.vocab) {
         if (ctid == 0) atomicOr(p.error, 1);
         tok = 0;
       }
-      const uint4 *src = reinterpret_cast<const uint4 *>(p.embed + size_t(tok) * H);
-      uint4 *dst = reinterpret_cast<uint4 *>(p.x + size_t(b) * H);
-      for (int c = ctid; c < H / 8; c += kRingConsumers * 32) dst[c] = src[c];
+      const uint32_t *src = reinterpret_cast<const uint32_t *>(p.embed + size_t(tok) * H);
+      for (int c = ctid; c < H / 2; c += kRingConsumers * 32)
+        ll_store_all(p.x_ll + size_t(b) * p.x_lls + c, act_row ? __ldg(src + c) : 0u, fl(0), 0, nullptr);
     }
     if (ctid == 0)
       for (int b = 0; b < NB; ++b) {
@@ -505,8 +567,28 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 7] = sm_clock();
     }
   };
+  // Hidden-state record (optional): CTA 0 copies the residual rows once they carry the flag
+  // of the operation that completed them (`slot` 0: the embedding, l + 1: after layer l).
+  auto dump_x = [&](int slot) {
+    if (!p.layer_dump || blockIdx.x != 0 || bad) return;
+    const uint32_t want = slot == 0 ? fl(0) : fl(c_op(slot - 1, 4));
+    for (int b = 0; b < NB; ++b) {
+      uint32_t *dst = reinterpret_cast<uint32_t *>(p.layer_dump + (size_t(slot) * p.dump_stride + b) * H);
+      for (int c = ctid; c < H / 2; c += kRingConsumers * 32) {
+        uint32_t w = 0;
+        if (!ll_wait1(p.x_ll + size_t(b) * p.x_lls + c, want, w, p.error)) atomicOr(p.error, 64);
+        dst[c] = w;
+      }
+    }
+  };
   calib(0);
+  // Step log (tracing only): CTA 0's start and end ns of this step (64-step ring after the
+  // per-CTA timeline and the sampler's 16 stamps; slots 2 and 3 of the step's entry).
+  unsigned long long *step_log =
+      p.trace ? p.trace + size_t(gridDim.x) * (5 * nL + 1) * 8 + 16 + size_t(epoch & 63) * 4 : nullptr;
+  if (step_log && blockIdx.x == 0 && ctid == 0) step_log[2] = globaltimer();
   wait_for(c_embed, epoch + 1, false);
+  dump_x(0);
   // This step's row state (activity, position, cos/sin, page table) for the attention units.
   for (int b = 0; b < NB; ++b) attn_row_load<128>(rowst[b], p.ap, b, ctid, kRingConsumers * 32);
   consumer_sync();
@@ -517,33 +599,46 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   }
   const int U = step_units(srows, kvh_n, nsplit);
 
+  // One GEMV operation: stage the flagged input rows (the wait for the producing
+  // operation), consume this CTA's stages, write its flagged outputs.
+  // A CTA without rows of the operation (possible under tensor parallelism) skips it: it
+  // neither waits for nor reads the input words, which a later operation may overwrite.
+  auto gemv_op = [&](const GemvTask &t, int op_slot, const uint4 (*wn)[4], int o) {
+    int g0, g1;
+    task_groups(t.N, blockIdx.x, gridDim.x, g0, g1, op_rotation(o, int(gridDim.x)));
+    if (g0 == g1) return;
+    if (!ring_stage_act<NB>(t, act, red, ctid, wn, p.error)) bad = true;
+    stamp(op_slot, 1);
+    ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+    stamp(op_slot, 2);
+  };
+
   uint4 wn_next[4];  // RMSNorm weight chunks of the next norm-prologue GEMV, loaded before its wait
   ring_norm_w_load(task(0, 0), wn_next, ctid);
   for (int l = 0; l < nL; ++l) {
-    int g0, g1;
     // QKV (RMSNorm of x fused).
-    {
-      stamp(5 * l, 0);
-      const GemvTask t = task(l, 0);
-      task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-      ring_stage_act<NB>(t, act, red, ctid, &wn_next);
-      stamp(5 * l, 1);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
-      stamp(5 * l, 2);
-      signal(c_op(l, 0), false);
-      stamp(5 * l, 3);
-    }
-    // Attention: the CTA's units, one after another on all consumer warps; each unit's KV
-    // chunks are ring stages (every consumer warp releases each once).
+    stamp(5 * l, 0);
+    gemv_op(task(l, 0), 5 * l, &wn_next, 0);
+    stamp(5 * l, 3);
+    // Attention: the CTA's units, one after another on all consumer warps; each unit waits
+    // for its own kv head's projections (flagged words) and streams its KV chunks as ring
+    // stages (every consumer warp releases each once).
     float wv[4];
     if (int(blockIdx.x) < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
-    wait_for(c_op(l, 0), (epoch + 1) * all, false);
     stamp(5 * l + 1, 0);
     {
       DecodeAttnParams ap = p.ap;
       ap.layer = l;
       ap.out_ndst = p.tp_ndst;
       ap.out_dst = s_dst;
+      ap.qkv_ll = p.qkv_ll;
+      ap.qkv_ll_stride = p.qkv_lls;
+      ap.qkv_flag = fl(c_op(l, 0));
+      ap.out_ll = p.attn_ll + (ap.out - p.attn) / 2;  // this rank's heads within the whole width
+      ap.out_ll_stride = p.attn_lls;
+      ap.out_flag = fl(c_op(l, 1));
+      ap.ll_limit = p.ll_limit;
+      if (p.inject_op == c_op(l, 1)) ap.qkv_flag ^= 0x80000000u;
       long long itk = it;
       for (int k = 0, u = blockIdx.x; u < U; ++k, u += gridDim.x) {
         const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
@@ -551,97 +646,71 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
         unsigned long long *st =
             (p.trace && k == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
         const AttnRow<128> &rs = rowst[ui.row];
-        if (ui.active && !bad) attn_qk<128, 2>(ap, *team_sm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ctid, 1);
+        if (ui.active && !bad &&
+            !attn_qk<128, 2>(ap, *team_sm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ctid, 1))
+          bad = true;
         attn_stamp(st, 3, ctid);
-        AttnAcc<128> acc;
-        attn_acc_init(acc);
+        AttnWarpAcc<128, 2> wacc;
+        attn_warp_init(wacc);
+        // Each warp waits for, computes and releases its share of every chunk on its own;
+        // an expired wait is voted once per unit (the barrier below).
+        bool wbad = bad;
         for (int j = 0; j < nch; ++j) {
           const long long ij = itk + j;
           const int sidx = int(ij % NS);
-          bool failed = false;
-          if (!bad) failed = !mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
-          if (team_any(1, failed)) {
-            if (ctid == 0 && !bad) atomicOr(p.error, 8);
-            bad = true;
+          if (!wbad && !mbar_wait(&full[sidx], unsigned(ij / NS) & 1u)) {
+            if (lane == 0) atomicOr(p.error, 8);
+            wbad = true;
           }
-          if (!bad) {
+          wbad = __any_sync(0xFFFFFFFFu, wbad);
+          if (!wbad) {
             const bf16 *ks = ring + size_t(sidx) * 8 * kRingRowPitch;
             const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
-            attn_chunk<128, 2>(*team_sm, ks, ks + kKvChunk * 128, n_main, rs.pos - base < kKvChunk, ap.g.scale, acc,
-                               ctid, 1);
+            attn_chunk<128, 2>(team_sm->q_b, team_sm->knew, team_sm->vnew, ks, ks + kKvChunk * 128, n_main,
+                               rs.pos - base < kKvChunk, ap.g.scale, wacc, ctid);
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[sidx]);
         }
+        if (team_any(1, wbad)) bad = true;
         attn_stamp(st, 4, ctid);
-        bool merged = false;
-        if (ui.active && !bad) merged = attn_finish<128, 2>(ap, *team_sm, acc, ui.row, ui.kvh, ui.split, ui.n_splits, ctid, 1);
-        attn_stamp(st, 5, ctid);
-        // An inactive row (or a failed step) counts each kv head once, from split 0.
-        if (merged || (ui.split == 0 && (bad || !ui.active))) {
-          consumer_sync();
-          if (ctid == 0) publish(c_op(l, 1), true);
+        if (ui.active && !bad) {
+          const AttnAcc<128> acc = attn_combine<128, 2>(*team_sm, wacc, ctid, 1);
+          attn_finish<128, 2>(ap, *team_sm, acc, ui.row, ui.kvh, ui.split, ui.n_splits, ctid, 1);
+        } else if (!ui.active && ui.split == 0) {
+          attn_write_inactive<128, 2>(ap, ui.row, ui.kvh, ctid);  // an inactive row's heads: zero words
         }
+        attn_stamp(st, 5, ctid);
         itk += nch;
       }
       it = itk;
     }
     stamp(5 * l + 1, 2);
     // O (+ residual).
-    stamp(5 * l + 2, 6);  // wait began
-    wait_for(c_op(l, 1), (epoch + 1) * kvh_n * NB * W, true);
-    {
-      stamp(5 * l + 2, 0);
-      const GemvTask t = task(l, 1);
-      task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-      ring_stage_act<NB>(t, act, red, ctid);
-      stamp(5 * l + 2, 1);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
-      stamp(5 * l + 2, 2);
-      signal(c_op(l, 2), true);
-      stamp(5 * l + 2, 3);
-    }
+    stamp(5 * l + 2, 0);
+    gemv_op(task(l, 1), 5 * l + 2, nullptr, 2);
+    stamp(5 * l + 2, 3);
     // gate/up (RMSNorm of x fused, SwiGLU epilogue).
-    stamp(5 * l + 3, 6);  // wait began
     ring_norm_w_load(task(l, 2), wn_next, ctid);
-    wait_for(c_op(l, 2), (epoch + 1) * all * W, true);
-    {
-      stamp(5 * l + 3, 0);
-      const GemvTask t = task(l, 2);
-      task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-      ring_stage_act<NB>(t, act, red, ctid, &wn_next);
-      stamp(5 * l + 3, 1);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
-      stamp(5 * l + 3, 2);
-      signal(c_op(l, 3), true);
-      stamp(5 * l + 3, 3);
-    }
+    stamp(5 * l + 3, 0);
+    gemv_op(task(l, 2), 5 * l + 3, &wn_next, 3);
+    stamp(5 * l + 3, 3);
     // down (+ residual).
-    stamp(5 * l + 4, 6);  // wait began
-    wait_for(c_op(l, 3), (epoch + 1) * all * W, true);
-    {
-      stamp(5 * l + 4, 0);
-      const GemvTask t = task(l, 3);
-      task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
-      ring_stage_act<NB>(t, act, red, ctid);
-      stamp(5 * l + 4, 1);
-      ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
-      stamp(5 * l + 4, 2);
-      signal(c_op(l, 4), true);
-      stamp(5 * l + 4, 3);
-    }
-    if (l + 1 < nL) {
-      stamp(5 * (l + 1), 6);  // the next QKV's wait began
-      ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
-    }
-    wait_for(c_op(l, 4), (epoch + 1) * all * W, true);
+    stamp(5 * l + 4, 0);
+    gemv_op(task(l, 3), 5 * l + 4, nullptr, 4);
+    stamp(5 * l + 4, 3);
+    if (l + 1 < nL) ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
+    dump_x(l + 1);
   }
   // Final RMSNorm + phase rows of the LM head.
   {
+    GemvTask head = head_task(p, s_dst, epoch);
+    head.ll_limit = p.ll_limit;
     int g0, g1;
     stamp(5 * nL, 0);
     task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
-    ring_stage_act<NB>(head, act, red, ctid);
+    const bool extra_cta = p.extra_row >= 0 && blockIdx.x == gridDim.x - 1;  // uses `act` below
+    if ((g0 < g1 || extra_cta) && !ring_stage_act<NB>(head, act, red, ctid, nullptr, p.error)) bad = true;
     stamp(5 * nL, 1);
     ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
     stamp(5 * nL, 2);
@@ -663,16 +732,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       v = warp_sum(v);
       if (lane == 0) store_all(p.logits + size_t(warp) * p.logit_stride + p.head_rows, f2bf(v), p.tp_ndst, s_dst);
     }
-    signal(c_head, true);
+    // Under tensor parallelism the head columns of every rank must be in before the step
+    // ends (the sampler, launched after this kernel, reads the whole logits rows).
+    if (tp) signal(c_head, true);
     calib(5 * nL);
   }
-  // CTA 0 ends the step once every rank's head columns are in (the sampler, launched after
-  // this kernel, reads the whole logits rows).
   if (blockIdx.x == 0) {
-    wait_for(c_head, (epoch + 1) * all * W, true);
+    if (tp) wait_for(c_head, (epoch + 1) * all * W, true);
     if (ctid == 0) {
       __threadfence();
       atomicExch(p.epoch, epoch + 1);
+      if (step_log) step_log[3] = globaltimer();
     }
   }
 }
@@ -738,6 +808,14 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.mlp = s.mlp;
   p.logits = s.logits + c0;
   p.logit_stride = s.logit_stride;
+  p.x_ll = s.x_ll;
+  p.qkv_ll = s.qkv_ll;
+  p.attn_ll = s.attn_ll;
+  p.mlp_ll = s.mlp_ll;
+  p.x_lls = d.hidden / 2;
+  p.qkv_lls = d.qkv_rows() / 2;
+  p.attn_lls = m.full.qdim() / 2;
+  p.mlp_lls = m.full.ffn / 2;
   p.tp_world = m.tp_world;
   p.tp_ndst = m.tp_world > 1 ? m.tp_world - 1 : 0;
   for (int i = 0; i < kMaxTpWorld - 1; ++i) p.tp_dst[i] = i < p.tp_ndst ? s.tp_dst[i] : 0;
@@ -783,6 +861,10 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.ctr = s.d_ctr;
   p.epoch = s.d_epoch;
   p.trace = s.d_trace;
+  p.layer_dump = s.d_layer_dump;
+  p.dump_stride = s.max_rows;
+  p.inject_op = s.inject_op;
+  p.ll_limit = s.inject_op > 0 ? (1ll << 16) : (1ll << 22);
   p.prefetch_stages = s.prefetch_stages;
 
   cudaLaunchConfig_t cfg = {};

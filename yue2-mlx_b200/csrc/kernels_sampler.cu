@@ -73,11 +73,13 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
   auto stamp = [&](int k) {
     if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[k] = (unsigned long long)clock64();
   };
+  unsigned long long t_start = 0;
   auto stamp_ns = [&](int k) {
     if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) {
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       p.trace[k] = t;
+      if (k == 12) t_start = t;
     }
   };
   stamp_ns(12);
@@ -549,6 +551,11 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       if (st.row_u >= 0) p.active[st.row_u] = 0;
     }
     stamp_ns(13);
+    // Step log (tracing only): request 0's start and end ns for step `step` (64-step ring).
+    if (p.trace && blockIdx.x == 0) {
+      p.trace[16 + (step & 63) * 4] = t_start;
+      p.trace[16 + (step & 63) * 4 + 1] = p.trace[13];
+    }
   }
 }
 

@@ -22,6 +22,9 @@
 // stale is read. Two calls whose kernels overlapped on the GPU would race on the array:
 // a process-wide lock, held until the call's step has finished on its stream, keeps this
 // entry point's own calls from overlapping.
+//
+// The call runs with the model's device current and gives the calling thread back the
+// current device it had on entry, on success and on error alike.
 #include <climits>
 #include <cmath>
 #include <cstring>
@@ -55,6 +58,23 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_lock;
 NoAllocScratch *g_scratch_addr[kMaxDevices] = {};
+
+// Makes `device` current for the guard's lifetime and gives the calling thread back its
+// own current device on every exit path (a PyTorch caller keeps its tensors and launches
+// on the device it had selected, whichever device the model lives on).
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int device) {
+    YAR_CUDA(cudaGetDevice(&prev));
+    if (prev != device) YAR_CUDA(cudaSetDevice(device));
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard &) = delete;
+  DeviceGuard &operator=(const DeviceGuard &) = delete;
+};
 
 // Device address of this device's copy of the array; the caller holds the lock and has
 // made `device` current.
@@ -115,7 +135,7 @@ void sample_device_noalloc(Model &m, const uint16_t *logits, long long row_strid
   for (int i = n_history - keep; i < n_history; ++i) r.hist[i % kHistCap] = history[i];
 
   std::lock_guard<std::mutex> lock(g_scratch_lock);
-  YAR_CUDA(cudaSetDevice(m.device));
+  DeviceGuard on_model_device(m.device);
   NoAllocScratch *scr = scratch_for(m.device);
   YAR_CUDA(cudaMemcpyAsync(&scr->req, &r, sizeof(r), cudaMemcpyHostToDevice, st));
   launch_sampler_ex(&scr->req, reinterpret_cast<const bf16 *>(logits), cfg ? int(row_stride) : n, scr->scores,

@@ -33,7 +33,88 @@ struct GemvTask {
   // i < n_dst — the same place in each peer rank's mapped copy of the buffer.
   int n_dst;
   const long long *dst;
+  // Flagged transport (the persistent kernel): activations read from flagged words `in_ll`
+  // (row stride in words) once they carry `in_flag`, outputs written as flagged words to
+  // `out_ll` with `out_flag` (and to the peers' copies); a residual epilogue reads the old
+  // residual words, which carry `res_flag`. Null: plain BF16 buffers (`in`, `out`).
+  const uint2 *in_ll = nullptr;
+  int in_ll_stride = 0;
+  uint32_t in_flag = 0;
+  uint2 *out_ll = nullptr;
+  int out_ll_stride = 0;
+  uint32_t out_flag = 0, res_flag = 0;
+  long long ll_limit = 1ll << 22;  // polls of a flagged wait before it gives up
 };
+
+// ---------------------------------------------------------------------------------------
+// Flagged words: two BF16 values (low half = the even element) and a 32-bit flag in one
+// 8-byte word, written with one 8-byte store. A reader that sees the expected flag in a
+// word sees that word's data (the store is single-copy atomic at 8 bytes), so a consumer
+// waits by polling the data itself: no fence, no counter, no second load. The flag names
+// the step and the operation that wrote the word, so words of earlier steps never match.
+constexpr long long kLlWaitLimit = 1ll << 22;  // polls before giving up (about a second)
+
+__device__ __forceinline__ void ll_store(uint2 *p, uint32_t data, uint32_t flag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(flag) : "memory");
+}
+// Store one flagged word locally and into each peer's mapped copy (byte offsets dst[i]).
+__device__ __forceinline__ void ll_store_all(uint2 *p, uint32_t data, uint32_t flag, int n_dst,
+                                             const long long *dst) {
+  ll_store(p, data, flag);
+  for (int i = 0; i < n_dst; ++i) ll_store(reinterpret_cast<uint2 *>(reinterpret_cast<char *>(p) + dst[i]), data, flag);
+}
+__device__ __forceinline__ uint4 ll_load2(const uint2 *p) {  // words p[0], p[1] (16-byte aligned)
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint2 ll_load1(const uint2 *p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ll_error_word(const int *p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait (bounded) for 2*NQ consecutive words at p (16-byte aligned) to carry `flag` and
+// return their data halves; false when the limit passed or another CTA recorded an error.
+template <int NQ>
+__device__ __forceinline__ bool ll_wait(const uint2 *p, uint32_t flag, uint32_t (&data)[2 * NQ], const int *error,
+                                        long long limit = kLlWaitLimit) {
+  for (long long i = 0;; ++i) {
+    bool ok = true;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const uint4 v = ll_load2(p + 2 * q);
+      data[2 * q] = v.x;
+      data[2 * q + 1] = v.z;
+      ok = ok && v.y == flag && v.w == flag;
+    }
+    if (ok) return true;
+    if (i >= limit) return false;
+    if ((i & 255) == 255 && error && ll_error_word(error) != 0) return false;
+    if (i >= 8) __nanosleep(32);
+  }
+}
+__device__ __forceinline__ bool ll_wait1(const uint2 *p, uint32_t flag, uint32_t &data, const int *error,
+                                         long long limit = kLlWaitLimit) {
+  for (long long i = 0;; ++i) {
+    const uint2 v = ll_load1(p);
+    data = v.x;
+    if (v.y == flag) return true;
+    if (i >= limit) return false;
+    if ((i & 255) == 255 && error && ll_error_word(error) != 0) return false;
+    if (i >= 8) __nanosleep(32);
+  }
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(bf16 lo, bf16 hi) {
+  return uint32_t(__bfloat16_as_ushort(lo)) | (uint32_t(__bfloat16_as_ushort(hi)) << 16);
+}
 
 // Store v at o and at its copies in the peers' mapped buffers.
 __device__ __forceinline__ void store_all(bf16 *o, bf16 v, int n_dst, const long long *dst) {
@@ -99,10 +180,15 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kRingConsumers * 32) : "memory");
 }
 
-__device__ __forceinline__ void task_groups(int N, int cta, int ctas, int &g0, int &g1) {
+// CTA `cta`'s 8-row groups [g0, g1) of an N-row task: contiguous ranges of floor or ceil
+// of groups / ctas, the ceil ranges at the CTAs whose position (cta + rot) % ctas the even
+// split gives them. `rot` lets consecutive operations put their extra groups on different
+// CTAs (which group a CTA computes does not change the group's arithmetic).
+__device__ __forceinline__ void task_groups(int N, int cta, int ctas, int &g0, int &g1, int rot = 0) {
   const int groups = (N + 7) / 8;
-  g0 = int((long long)cta * groups / ctas);
-  g1 = int((long long)(cta + 1) * groups / ctas);
+  const int pos = (cta + rot) % ctas;
+  g0 = int((long long)pos * groups / ctas);
+  g1 = int((long long)(pos + 1) * groups / ctas);
 }
 
 // Producer: issue this CTA's stages of one task, continuing the ring sequence `it`.
@@ -168,10 +254,29 @@ __device__ __forceinline__ void ring_norm_w_load(const GemvTask &t, uint4 (&wn)[
   }
 }
 
+// Flagged staging: the thread's 8-element chunk k of row b, once its four words carry the
+// task's input flag; false (chunk zeroed) when the wait gave up.
+__device__ __forceinline__ bool ll_chunk(const GemvTask &t, int b, int k, uint4 &out, const int *error) {
+  uint32_t d[4];
+  const bool ok = ll_wait<2>(t.in_ll + size_t(b) * t.in_ll_stride + (k >> 1), t.in_flag, d, error, t.ll_limit);
+  out = ok ? make_uint4(d[0], d[1], d[2], d[3]) : make_uint4(0, 0, 0, 0);
+  return ok;
+}
+
+// `error` (flagged input only): the device error word — an expired wait records code 64
+// there and returns false on every consumer thread (the staged rows are then meaningless).
 template <int NB>
-__device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int ctid, const uint4 (*wn_pre)[4] = nullptr) {
+__device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int ctid, const uint4 (*wn_pre)[4] = nullptr,
+                               int *error = nullptr) {
   constexpr int T = kRingConsumers * 32;
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K;
+  bool ok = true;
+  auto load = [&](int b, int k) -> uint4 {
+    if (!t.in_ll) return __ldcg(reinterpret_cast<const uint4 *>(t.in + size_t(b) * t.in_stride + k));
+    uint4 v;
+    if (!ll_chunk(t, b, k, v, error)) ok = false;
+    return v;
+  };
   if (t.norm_w) {
     uint4 wn[4];
     if (wn_pre) {
@@ -182,13 +287,12 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
     }
     uint4 xv[NB][4];
     for (int b = 0; b < NB; ++b) {
-      const bf16 *x = t.in + size_t(b) * t.in_stride;
       float ss = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int k = (ctid + j * T) * 8;
         if (k < K) {
-          xv[b][j] = __ldcg(reinterpret_cast<const uint4 *>(x + k));
+          xv[b][j] = load(b, k);
           const uint32_t w4[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -223,13 +327,22 @@ __device__ void ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
       }
     }
   } else {
-    for (int b = 0; b < NB; ++b) {
-      const bf16 *x = t.in + size_t(b) * t.in_stride;
-      for (int c = ctid; c < K / 8; c += T)
-        act_store_chunk(act + b * K, c * 8, __ldcg(reinterpret_cast<const uint4 *>(x + c * 8)));
-    }
+    for (int b = 0; b < NB; ++b)
+      for (int c = ctid; c < K / 8; c += T) act_store_chunk(act + b * K, c * 8, load(b, c * 8));
   }
-  consumer_sync();
+  if (!t.in_ll) {
+    consumer_sync();
+    return true;
+  }
+  // The barrier also agrees on the outcome of every thread's waits.
+  int all_ok;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(all_ok)
+      : "r"(int(ok)), "n"(kRingConsumers * 32)
+      : "memory");
+  if (!all_ok && ctid == 0 && error) atomicOr(error, 64);
+  return all_ok != 0;
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
@@ -246,7 +359,7 @@ __device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a2, ui
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-constexpr int kRingMaxGroups = 32;  // 8-row groups whose partial sums wait for one epilogue
+constexpr int kRingMaxGroups = 8;  // 8-row groups whose partial sums wait for one epilogue
 
 // Bytes of the group-partials buffer ring_consume needs.
 __host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGroups * kRingConsumers * NB * 8; }
@@ -309,7 +422,59 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
       }
     }
     consumer_sync();
-    if (!bad) {
+    if (!bad && t.out_ll) {
+      // Flagged epilogue: one thread per pair of adjacent outputs, one flagged word each.
+      const bool swiglu = t.epi == kEpiSwiGLU;
+      const int per_group = NB * (swiglu ? 2 : 4);
+      for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {
+        const int gi = u / per_group, rem = u % per_group;
+        const float *src = gred + size_t(gi) * kRingConsumers * NB * 8;
+        const int r0 = (gb + gi) * 8;
+        float v[2];
+        int col;
+        const int b = swiglu ? rem / 2 : rem / 4, j = swiglu ? rem % 2 : rem % 4;
+        if (swiglu) {
+          if (r0 + 4 * j + 3 >= t.N) continue;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {  // outputs 2j + e of the group: rows 2(2j + e) (gate), +1 (up)
+            const int rg = 2 * (2 * j + e);
+            float gs = 0.f, us = 0.f;
+#pragma unroll
+            for (int w = 0; w < kRingConsumers; ++w) {
+              gs += src[w * NB * 8 + b * 8 + rg];
+              us += src[w * NB * 8 + b * 8 + rg + 1];
+            }
+            v[e] = rbf(silu_f32(rbf(gs))) * rbf(us);
+          }
+          col = (r0 >> 1) + 2 * j;
+        } else {
+          if (r0 + 2 * j + 1 >= t.N) continue;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float a = 0.f;
+#pragma unroll
+            for (int w = 0; w < kRingConsumers; ++w) a += src[w * NB * 8 + b * 8 + 2 * j + e];
+            v[e] = a;
+          }
+          col = r0 + 2 * j;
+        }
+        uint2 *o = t.out_ll + size_t(b) * t.out_ll_stride + (col >> 1);
+        bf16 lo, hi;
+        if (t.epi == kEpiResidual) {
+          uint32_t old = 0;
+          if (!ll_wait1(o, t.res_flag, old, error, t.ll_limit)) {
+            atomicOr(error, 64);
+            continue;
+          }
+          lo = f2bf(bf_lo(old) + rbf(v[0]));
+          hi = f2bf(bf_hi(old) + rbf(v[1]));
+        } else {
+          lo = f2bf(v[0]);
+          hi = f2bf(v[1]);
+        }
+        ll_store_all(o, pack_bf16x2(lo, hi), t.out_flag, t.n_dst, t.dst);
+      }
+    } else if (!bad) {
       const bool swiglu = t.epi == kEpiSwiGLU;
       const int per_group = NB * (swiglu ? 4 : 8);
       for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {

@@ -16,8 +16,11 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -28,7 +31,9 @@ namespace yar {
 namespace {
 struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
-  ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char *(*error_string)(ncclResult_t) = nullptr;
@@ -52,7 +57,10 @@ const NcclApi &nccl() {
       return p;
     };
     api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
-    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+    api.comm_init_rank_config =
+        reinterpret_cast<decltype(api.comm_init_rank_config)>(sym("ncclCommInitRankConfig"));
+    api.comm_get_async_error = reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
     api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
@@ -65,6 +73,31 @@ void check(ncclResult_t r, const char *what) {
   if (r == ncclSuccess) return;
   const char *msg = nccl().error_string ? nccl().error_string(r) : "unknown";
   throw Error("RuntimeError", std::string(what) + " failed: " + msg);
+}
+
+// Seconds the ranks get to join a communicator (YAR_TP_JOIN_TIMEOUT_S, default 300), and
+// to finish any later call the non-blocking communicator reports as in progress.
+double join_timeout_s() {
+  const char *v = std::getenv("YAR_TP_JOIN_TIMEOUT_S");
+  const double t = v ? std::atof(v) : 0.0;
+  return t > 0 ? t : 300.0;
+}
+
+// The communicator is non-blocking (so a rank whose peers never arrive can give up): a
+// call may return ncclInProgress, after which its state is polled until it settles or the
+// deadline passes — then the communicator is aborted and the call fails.
+void settle(ncclComm_t comm, ncclResult_t r, const char *what, double timeout_s) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress) {
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+      nccl().comm_abort(comm);
+      throw Error("RuntimeError", std::string(what) + ": tensor-parallel ranks did not join within " +
+                                      std::to_string(int(timeout_s)) + " s (communicator aborted)");
+    }
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    check(nccl().comm_get_async_error(comm, &r) == ncclSuccess ? ncclSuccess : ncclSystemError, what);
+  }
+  check(r, what);
 }
 }  // namespace
 
@@ -80,7 +113,11 @@ void tp_init(Model &m, int rank, int world, const uint8_t *id_bytes) {
   std::memcpy(&id, id_bytes, sizeof(id));
   YAR_CUDA(cudaSetDevice(m.device));
   ncclComm_t comm = nullptr;
-  check(nccl().comm_init_rank(&comm, world, id, rank), "ncclCommInitRank");
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  const ncclResult_t r = nccl().comm_init_rank_config(&comm, world, id, rank, &config);
+  if (r != ncclSuccess && r != ncclInProgress) check(r, "ncclCommInitRankConfig");
+  settle(comm, r, "ncclCommInitRankConfig", join_timeout_s());
   m.tp_comm = comm;
 }
 
@@ -91,7 +128,8 @@ void tp_destroy(Model &m) {
 }
 
 void tp_allgather_bf16(const Model &m, const bf16 *send, bf16 *recv, size_t n, cudaStream_t st) {
-  check(nccl().all_gather(send, recv, n, ncclBfloat16, static_cast<ncclComm_t>(m.tp_comm), st), "ncclAllGather");
+  auto comm = static_cast<ncclComm_t>(m.tp_comm);
+  settle(comm, nccl().all_gather(send, recv, n, ncclBfloat16, comm, st), "ncclAllGather", join_timeout_s());
 }
 
 namespace {
@@ -103,8 +141,8 @@ std::vector<char> allgather_host(const Model &m, const void *mine, size_t bytes,
   std::vector<char> out(bytes * W);
   try {
     YAR_CUDA(cudaMemcpyAsync(d + bytes * W, mine, bytes, cudaMemcpyHostToDevice, st));
-    check(nccl().all_gather(d + bytes * W, d, bytes, ncclInt8, static_cast<ncclComm_t>(m.tp_comm), st),
-          "ncclAllGather");
+    auto comm = static_cast<ncclComm_t>(m.tp_comm);
+    settle(comm, nccl().all_gather(d + bytes * W, d, bytes, ncclInt8, comm, st), "ncclAllGather", join_timeout_s());
     YAR_CUDA(cudaMemcpyAsync(out.data(), d, bytes * W, cudaMemcpyDeviceToHost, st));
     YAR_CUDA(cudaStreamSynchronize(st));
   } catch (...) {
