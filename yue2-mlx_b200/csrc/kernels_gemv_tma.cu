@@ -63,8 +63,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) k_gemv_tma(TmaGemvParams p) {
   pdl_wait();
   ring_stage_act<NB>(p.t, act, red, threadIdx.x);
   long long it = 0;
-  bool bad = false;
-  ring_consume<NB, kTmaStages>(p.t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, threadIdx.x);
+  bool bad = false, dead = false;
+  ring_consume<NB, kTmaStages>(p.t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, threadIdx.x);
 }
 
 size_t gemv_tma_smem(int NB, int K) {

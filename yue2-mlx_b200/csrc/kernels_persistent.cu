@@ -478,7 +478,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
 
   // ------------------------------------------------------------------ consumers
   const int ctid = threadIdx.x;
-  bool bad = false;
+  bool bad = false, dead = false;  // dead: a ring wait expired (the producer is presumed stuck)
   long long it = 0;
   auto stamp = [&](int o, int k) {
     if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
@@ -609,7 +609,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     if (g0 == g1) return;
     if (!ring_stage_act<NB>(t, act, red, ctid, wn, p.error)) bad = true;
     stamp(op_slot, 1);
-    ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+    ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, ctid);
     stamp(op_slot, 2);
   };
 
@@ -652,15 +652,20 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
         attn_stamp(st, 3, ctid);
         AttnWarpAcc<128, 2> wacc;
         attn_warp_init(wacc);
-        // Each warp waits for, computes and releases its share of every chunk on its own;
-        // an expired wait is voted once per unit (the barrier below).
+        // Each warp waits for, computes and releases its share of every chunk on its own; a
+        // failure is voted once per unit (the barrier below). After a failure elsewhere the
+        // chunks are still waited for and released; an expired ring wait stops both.
         bool wbad = bad;
         for (int j = 0; j < nch; ++j) {
           const long long ij = itk + j;
           const int sidx = int(ij % NS);
-          if (!wbad && !mbar_wait(&full[sidx], unsigned(ij / NS) & 1u)) {
-            if (lane == 0) atomicOr(p.error, 8);
-            wbad = true;
+          bool landed = false;
+          if (!dead) {
+            landed = mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
+            if (!landed) {
+              if (lane == 0) atomicOr(p.error, 8);
+              dead = wbad = true;
+            }
           }
           wbad = __any_sync(0xFFFFFFFFu, wbad);
           if (!wbad) {
@@ -670,7 +675,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
                                rs.pos - base < kKvChunk, ap.g.scale, wacc, ctid);
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[sidx]);
+          if (lane == 0 && landed) mbar_arrive(&empty[sidx]);
         }
         if (team_any(1, wbad)) bad = true;
         attn_stamp(st, 4, ctid);
@@ -712,7 +717,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     const bool extra_cta = p.extra_row >= 0 && blockIdx.x == gridDim.x - 1;  // uses `act` below
     if ((g0 < g1 || extra_cta) && !ring_stage_act<NB>(head, act, red, ctid, nullptr, p.error)) bad = true;
     stamp(5 * nL, 1);
-    ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad, ctid);
+    ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, ctid);
     stamp(5 * nL, 2);
     if (p.extra_row >= 0 && blockIdx.x == gridDim.x - 1 && warp < NB && !bad) {
       // The ABC phase's extra row (ABC_END), from the normalized activations in `act`.

@@ -370,11 +370,14 @@ __host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGrou
 // ldmatrix straight from the ring) and the activation rows as rows 0..NB-1 of A,
 // accumulating in FP32 across the stages of a group. Warps park their per-group partial
 // sums in `gred`; one barrier per up to kRingMaxGroups groups, then the 8 partials of
-// each output are added in warp order and the epilogue is applied. After a wait expires
-// (`bad`), stages are still released and barriers still taken, without computing.
+// each output are added in warp order and the epilogue is applied. After a failure
+// elsewhere (`bad`) stages are still waited for and released and barriers still taken,
+// without computing; once a ring wait itself expired (`dead`: the producer is presumed
+// stuck, a copy may still be landing) no stage is waited for or released any more.
 template <int NB, int NS>
 __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring, const bf16 *act, uint64_t *full,
-                             uint64_t *empty, long long &it, float *gred, int *error, bool &bad, int ctid) {
+                             uint64_t *empty, long long &it, float *gred, int *error, bool &bad, bool &dead,
+                             int ctid) {
   static_assert(NB >= 1 && NB <= 8, "activation rows must fit the MMA's first 8 rows");
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K, KS = K / kRingPiece;
   const int grow = lane >> 2, gcol = (lane & 3) * 2;  // fragment row / column pair of this lane
@@ -388,9 +391,13 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
       float c2[2][4] = {};
       for (int ks = 0; ks < KS; ++ks, ++it) {
         const int s = int(it % NS);
-        if (!bad && !mbar_wait(&full[s], unsigned(it / NS) & 1u)) {
-          if (lane == 0) atomicOr(error, 8);
-          bad = true;
+        bool landed = false;
+        if (!dead) {
+          landed = mbar_wait(&full[s], unsigned(it / NS) & 1u);
+          if (!landed) {
+            if (lane == 0) atomicOr(error, 8);
+            dead = bad = true;
+          }
         }
         if (!bad) {
           const bf16 *wst = ring + size_t(s) * 8 * kRingRowPitch;
@@ -408,7 +415,7 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0 && landed) mbar_arrive(&empty[s]);
       }
       float c[4];
 #pragma unroll
