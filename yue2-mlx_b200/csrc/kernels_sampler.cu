@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     s[i] = v;
   };
   const bool vec = (reinterpret_cast<uintptr_t>(lc) & 15) == 0 && (!lu || (reinterpret_cast<uintptr_t>(lu) & 15) == 0);
+  const bool s_vec = (reinterpret_cast<uintptr_t>(s) & 15) == 0;
   if (vec) {
     // 16-byte loads: 8 logits per load, every load of a thread in flight at once.
     const int nv = n / 8;
@@ -115,6 +116,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       const uint4 cq = *reinterpret_cast<const uint4 *>(lc + size_t(c) * 8);
       const uint4 uq = lu ? *reinterpret_cast<const uint4 *>(lu + size_t(c) * 8) : cq;
       const uint32_t cw[4] = {cq.x, cq.y, cq.z, cq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
+      float v8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float v = (e & 1) ? bf_hi(cw[e >> 1]) : bf_lo(cw[e >> 1]);
@@ -124,7 +126,16 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
           const float scaled = round_bf16(f_mul(delta, scale));
           v = round_bf16(f_add(u, scaled));
         }
-        s[c * 8 + e] = v;
+        v8[e] = v;
+      }
+      // Two 16-byte stores when the score row allows them (eight 4-byte stores 32 bytes
+      // apart per lane conflict 8 ways in shared memory).
+      if (s_vec) {
+        *reinterpret_cast<float4 *>(s + c * 8) = make_float4(v8[0], v8[1], v8[2], v8[3]);
+        *reinterpret_cast<float4 *>(s + c * 8 + 4) = make_float4(v8[4], v8[5], v8[6], v8[7]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s[c * 8 + e] = v8[e];
       }
     }
     for (int i = nv * 8 + tid; i < n; i += kSampThreads) mix(i);
@@ -231,8 +242,8 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
     }
     stamp(3);
     // k-th largest value: radix select on order-preserving keys, four 8-bit digits from
-    // the top. Each warp counts into its own 256-bin histogram (lanes with the same bin add
-    // once), so warps never contend when the logits crowd a few bins; the 32 histograms are
+    // the top. Each warp counts into its own 256-bin histogram with shared-memory atomics,
+    // so warps never contend when the logits crowd a few bins; the 32 histograms are
     // summed per bin and warp 0 finds the bin holding the k-th key by a scan from the top.
     const int k = min(st.top_k, n);
     uint32_t pre = 0;
@@ -259,9 +270,7 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
           const uint32_t key = f32_order_key(s[listed ? list[j] : j]);
           if ((key & hmask) == (pre & hmask)) bin = (key >> shift) & 255u;
         }
-        const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
-        if (bin != 0xFFFFFFFFu && lane == __ffs(peers) - 1) wh[bin] += __popc(peers);
-        __syncwarp();
+        if (bin != 0xFFFFFFFFu) atomicAdd(&wh[bin], 1);
       }
       __syncthreads();
       if (tid < 256) {
@@ -305,8 +314,18 @@ __global__ void __launch_bounds__(kSampThreads) k_sampler(SamplerParams p) {
       if (!listed && pass < 3 && kth_cnt <= kListCap) {
         if (tid == 0) list_n = 0;
         __syncthreads();
-        for (int i = tid; i < n; i += kSampThreads)
-          if ((f32_order_key(s[i]) >> shift) == (pre >> shift)) list[atomicAdd(&list_n, 1)] = i;
+        // One shared-memory atomic per warp and round (the matching lanes' slots follow from
+        // the ballot), not one per row: the list only feeds the later passes' counts, so
+        // the order of its entries does not matter.
+        for (int base = 0; base < n; base += kSampThreads) {
+          const int i = base + tid;
+          const bool hit = i < n && (f32_order_key(s[i]) >> shift) == (pre >> shift);
+          const unsigned m = __ballot_sync(0xFFFFFFFFu, hit);
+          int first = 0;
+          if (lane == 0 && m) first = atomicAdd(&list_n, __popc(m));
+          first = __shfl_sync(0xFFFFFFFFu, first, 0);
+          if (hit) list[first + __popc(m & ((1u << lane) - 1u))] = i;
+        }
         __syncthreads();
         listed = true;
         m = list_n;

@@ -49,7 +49,7 @@ struct NoAllocScratch {
   RequestState req;
   int token[2];   // per-row sampled token (the decode loop's feedback slot; unused here)
   int active[2];  // per-row active flag (likewise)
-  float scores[kNoAllocMaxColumns];
+  alignas(16) float scores[kNoAllocMaxColumns];
 };
 
 static __device__ __align__(256) NoAllocScratch g_sampler_scratch[1];
