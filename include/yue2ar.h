@@ -116,7 +116,8 @@ int yar_session_free(yar_session *session);
  * stamps: wait done, activations staged, stages consumed, signalled, producer first/last
  * issue; slots 6/7 of operation 0 and of the head hold globaltimer ns and the SM clock
  * at the step's start and end, for converting cycles to time), overwritten by every
- * step; read it with yar_session_trace. YAR_OPT_PREFETCH_STAGES (default 6, 0..64): how many
+ * step that has an active row (so it keeps the last step that did work, not the final
+ * launch after a request's last token); read it with yar_session_trace. YAR_OPT_PREFETCH_STAGES (default 6, 0..64): how many
  * 32 KB stages per SM the persistent kernel pulls into L2 ahead of its shared-memory ring
  * (its lookahead while the step waits at operation boundaries). */
 enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3, YAR_OPT_MAX_SPLITS = 4,
@@ -135,10 +136,11 @@ enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3, Y
  * the call returns YAR_FAILURE ("RuntimeError"). No fault, trap or hang is involved; the
  * session stays usable (the next call starts from cleared state). */
 int yar_session_set_option(yar_session *session, int option, int value);
-/* Copy the last step's timeline ([sm][5 * layers + 1][8] uint64, then 16 sampler stamps:
- * SM clocks at its phase ends, and globaltimer ns at its start and end in slots 12/13,
- * then a [64][4] step log indexed by decode step % 64: globaltimer ns of the sampler's
- * start and end (request 0) and of the persistent kernel's start and end (CTA 0)) to host. */
+/* Copy the timeline of the last step with an active row ([sm][5 * layers + 1][8] uint64,
+ * then 16 sampler stamps: SM clocks at its phase ends, and globaltimer ns at its start and
+ * end in slots 12/13, then a [64][4] step log indexed by the session's decode step count
+ * % 64, written on every step: globaltimer ns of the sampler's start and end (request 0)
+ * and of the persistent kernel's start and end (CTA 0)) to host. */
 int yar_session_trace(yar_session *session, uint64_t *out, size_t n, size_t *n_written);
 
 /* generate_tokens — native/src/sampling.cpp:185-288 (upstream sampling.py:57-154): prefill

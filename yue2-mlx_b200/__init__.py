@@ -305,7 +305,9 @@ class Session:
         _check(lib.yar_session_set_option(self._h, 2, int(bool(on))))
 
     def trace(self) -> np.ndarray:
-        """Last step's timeline: [sm][5 * layers + 1][8] globaltimer stamps in ns."""
+        """Timeline of the last step with an active row: [sm][5 * layers + 1][8] SM-clock
+        stamps per CTA and operation (slots 6/7 of the first operation and of the head:
+        globaltimer ns and SM clock at the step's start and end)."""
         d = self.model.dims
         k = d["sms"] * (5 * d["layers"] + 1) * 8
         out = np.zeros(k + 16, np.uint64)

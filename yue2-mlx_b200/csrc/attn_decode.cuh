@@ -225,6 +225,38 @@ __device__ __forceinline__ void attn_load_norm_w(const bf16 *qn, const bf16 *kn,
 // and appended to the cache at the row's position.
 // With flagged input (p.qkv_ll) the projections are polled until they carry p.qkv_flag;
 // returns false on every team thread when such a wait gave up (code 64 recorded).
+// Bounded poll of the flagged words holding elements a + 32 i and, when b >= 0, b + 32 i
+// (i < N) until all carry `flag`: every pass issues all 2N loads before checking any.
+template <int N>
+__device__ __forceinline__ bool ll_wait_lane_words(const uint2 *words, int a, int b, uint32_t flag,
+                                                   uint32_t (&da)[N], uint32_t (&db)[N], const int *error,
+                                                   long long limit) {
+  for (long long it = 0;; ++it) {
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const uint2 w = ll_load1(words + ((a + 32 * i) >> 1));
+      da[i] = w.x;
+      ok = ok && w.y == flag;
+    }
+    if (b >= 0) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const uint2 w = ll_load1(words + ((b + 32 * i) >> 1));
+        db[i] = w.x;
+        ok = ok && w.y == flag;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) db[i] = 0u;
+    }
+    if (ok) return true;
+    if (it >= limit) return false;
+    if ((it & 255) == 255 && error && ll_error_word(error) != 0) return false;
+    if (it >= 8) __nanosleep(32);
+  }
+}
+
 template <int D, int G>
 __device__ bool attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const AttnRow<D> &rs, int row, int kvh,
                         bool holds_new, const float (&wv)[D / 32], int tid, int bar_id) {
@@ -237,19 +269,27 @@ __device__ bool attn_qk(const DecodeAttnParams &p, AttnTeamSmem<D, G> &sm, const
     const bool is_k = warp == G;
     const int rw = g.qdim + 2 * g.kvdim;
     const int e0 = is_k ? g.qdim + kvh * D : (kvh * G + warp) * D, ev = g.qdim + g.kvdim + kvh * D;
-    // Element e of the row's projections: plain, or half (e & 1) of flagged word e / 2.
-    auto elem = [&](int e) -> float {
-      if (!p.qkv_ll) return bf2f(__ldcg(p.qkv + size_t(row) * rw + e));
-      uint32_t w = 0;
-      if (!ll_wait1(p.qkv_ll + size_t(row) * p.qkv_ll_stride + (e >> 1), p.qkv_flag, w, p.error, p.ll_limit))
-        ok = false;
-      return (e & 1) ? bf_hi(w) : bf_lo(w);
-    };
+    // Elements e0 + lane + 32 i (and, for the k warp, the v elements ev + lane + 32 i) of the
+    // row's projections: plain, or half (e & 1) of flagged word e / 2, all of a lane's
+    // words polled together (one round trip once they are written).
     float hv[NPL], vv[NPL];
+    if (!p.qkv_ll) {
 #pragma unroll
-    for (int i = 0; i < NPL; ++i) {
-      hv[i] = elem(e0 + lane + 32 * i);
-      if (is_k) vv[i] = elem(ev + lane + 32 * i);
+      for (int i = 0; i < NPL; ++i) {
+        hv[i] = bf2f(__ldcg(p.qkv + size_t(row) * rw + e0 + lane + 32 * i));
+        vv[i] = is_k ? bf2f(__ldcg(p.qkv + size_t(row) * rw + ev + lane + 32 * i)) : 0.f;
+      }
+    } else {
+      const uint2 *words = p.qkv_ll + size_t(row) * p.qkv_ll_stride;
+      uint32_t wq[NPL], wv2[NPL];
+      ok = ll_wait_lane_words<NPL>(words, e0 + lane, is_k ? ev + lane : -1, p.qkv_flag, wq, wv2, p.error,
+                                   p.ll_limit);
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) {
+        const int e = e0 + lane + 32 * i;  // 32 i is even: every element of a lane has e's parity
+        hv[i] = (e & 1) ? bf_hi(wq[i]) : bf_lo(wq[i]);
+        vv[i] = (e & 1) ? bf_hi(wv2[i]) : bf_lo(wv2[i]);
+      }
     }
     norm_rope_regs<D>(hv, wv, rs.cosr, rs.sinr, g.eps, lane);
     if (!is_k) {
@@ -454,12 +494,12 @@ __device__ __forceinline__ AttnAcc<D> attn_combine(AttnTeamSmem<D, G> &sm, const
 
 // Merge the n_active split partials of the G heads of (row, kv_head) into the BF16 head
 // outputs. Thread t < G x D owns output t (head t / D, dim t % D) and reads that dim plus
-// (m, l) of up to 8 splits in one round trip; batches fold into the running (M, L, O)
+// (m, l) of up to 16 splits in one round trip; batches fold into the running (M, L, O)
 // with exp rescaling, in split order. The merging unit resets the arrival counter.
 template <int D, int G>
 __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, int kvh, int row, int n_active,
                            int tid) {
-  constexpr int MB = 8;
+  constexpr int MB = 16;
   if (tid < G * D) {
     const int hd = tid / D, d = tid % D;
     const float *pr0 = part_base + size_t(kvh * G + hd) * p.max_splits * (D + 2);

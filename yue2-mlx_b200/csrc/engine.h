@@ -57,6 +57,9 @@ struct Model {
   const bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
   std::vector<LayerWeights> layers;
   LayerWeights *d_layers = nullptr;  // device copy of `layers` (persistent decode kernel)
+  // Device array [layer][4] of the stage maps (128-byte TMA descriptors) of qkv, o, gu and
+  // down for the persistent decode kernel; null when the shapes do not fit its ring.
+  void *d_wmaps = nullptr;
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
   // Tensor parallelism: this rank's share of the heads, KV heads and FFN columns is in `d`
   // (the whole model's dims in `full`, the rank's rows in `tp`); `tp_comm` is the NCCL
@@ -169,6 +172,9 @@ void configure_gemv_tma_kernels();
 void configure_persistent_kernels();
 void configure_sampler_kernels();
 bool persistent_supported(const Model &m, int n_rows);
+// Encodes m.d_wmaps (after the weights are uploaded); leaves it null when a K is not a
+// multiple of 2048.
+void build_stage_maps(Model &m);
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
 
 enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };

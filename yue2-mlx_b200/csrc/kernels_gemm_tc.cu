@@ -331,6 +331,25 @@ CUtensorMap kmajor_map(const bf16 *ptr, int rows, int K, int box_rows) {
 }
 }  // namespace
 
+// The decode GEMVs' stage map (tma_ring.cuh): W [N][K] row-major BF16 viewed as {64
+// columns, N rows, K/64 column blocks} with byte strides {2K, 128}; a {64, 8, 32} box is
+// one 32 KB stage (8 rows x 2048 columns), written to shared memory with the 128-byte
+// swizzle; rows past N are zero-filled.
+void encode_stage_map(CUtensorMap *map, const bf16 *W, int N, int K) {
+  if (N < 1 || K < 2048 || K % 2048 != 0 || (reinterpret_cast<uintptr_t>(W) & 15) != 0)
+    throw Error("RuntimeError", "stage map: W must be 16-byte aligned with K a multiple of 2048");
+  const EncodeTiled fn = encode_fn();
+  if (!fn) throw Error("RuntimeError", "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {64, cuuint64_t(N), cuuint64_t(K / 64)};
+  const cuuint64_t strides[2] = {cuuint64_t(K) * 2, 128};
+  const cuuint32_t box[3] = {64, 8, 32};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16 *>(W), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error("RuntimeError", "cuTensorMapEncodeTiled failed for a stage map");
+}
+
 void configure_gemm_tc_kernels() {
   YAR_CUDA(cudaFuncSetAttribute(k_gemm_tc<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
   YAR_CUDA(cudaFuncSetAttribute(k_gemm_tc<kEpiResidual>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));

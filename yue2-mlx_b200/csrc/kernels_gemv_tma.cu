@@ -1,17 +1,16 @@
 // kernels_gemv_tma.cu — decode GEMV with the weight stream staged through shared memory
-// by bulk asynchronous copies (cp.async.bulk, the TMA engine's linear mode) and mbarriers.
+// by TMA tensor copies (one 32 KB stage per copy, tma_ring.cuh) and mbarriers.
 //
 // Same operator and fusions as kernels_gemv.cu (RMSNorm prologue; store / residual /
 // SwiGLU epilogue; reference ops native/src/ar.cpp:20-51, :266-298), for K a multiple of
 // 2048 and one or two activation rows (bs1 and a CFG pair).
 //
 // One CTA per SM: 8 consumer warps + 1 producer warp. The CTA owns a contiguous range of
-// 8-row groups; a group is streamed as K/2048 stages, each 8 row pieces of 2048 BF16
-// (4 KB, contiguous in the row-major matrix) = 32 KB. A 3-stage ring keeps 96 KB per SM in
-// flight without holding registers. The producer starts copying before
-// griddepcontrol.wait (weights do not depend on the previous kernel), so a kernel's first
-// 96 KB per SM arrive while its predecessor finishes; 96 KB of stages + the activations
-// leave room for the next kernel's CTA on the same SM.
+// 8-row groups; a group is streamed as K/2048 stages of 8 rows x 2048 BF16 = 32 KB. A
+// 3-stage ring keeps 96 KB per SM in flight without holding registers. The producer starts
+// copying before griddepcontrol.wait (weights do not depend on the previous kernel), so a
+// kernel's first 96 KB per SM arrive while its predecessor finishes; 96 KB of stages + the
+// activations leave room for the next kernel's CTA on the same SM.
 //
 // Every mbarrier wait is bounded; on expiry the kernel records an error code and stops
 // issuing work, and the producer drains the copies it issued before exiting.
@@ -23,21 +22,29 @@ constexpr int kTmaThreads = (kRingConsumers + 1) * 32;
 constexpr int kTmaStages = 3;
 
 struct TmaGemvParams {
+  CUtensorMap wmap;  // the weight's stage map (encode_stage_map)
   GemvTask t;
   int *error;
 };
 
 template <int NB, int EPI>
-__global__ void __launch_bounds__(kTmaThreads, 1) k_gemv_tma(TmaGemvParams p) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  bf16 *ring = reinterpret_cast<bf16 *>(smem_raw);                                  // [S][8][2048]
+__global__ void __launch_bounds__(kTmaThreads, 1) k_gemv_tma(const __grid_constant__ TmaGemvParams p) {
+  // 1024-byte alignment: the stages are 128-byte-swizzled tensor copies.
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  bf16 *ring = reinterpret_cast<bf16 *>(smem_raw);                                  // [S][8 x 2048]
   bf16 *act = reinterpret_cast<bf16 *>(smem_raw + kTmaStages * kRingStageBytes);  // [NB][K]
   __shared__ __align__(8) uint64_t full[kTmaStages], empty[kTmaStages];
   __shared__ float red[NB * kRingConsumers];
-  float *gred = reinterpret_cast<float *>(smem_raw + kTmaStages * kRingStageBytes + size_t(NB) * p.t.K * 2);
+  GemvTask t = p.t;
+  t.wmap = &p.wmap;
+  float *gred = reinterpret_cast<float *>(smem_raw + kTmaStages * kRingStageBytes + size_t(NB) * t.K * 2);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if ((smem_u32(ring) & 1023) != 0) {  // never copy into a misaligned ring
+    if (threadIdx.x == 0) atomicOr(p.error, 1);
+    return;
+  }
   int g0, g1;
-  task_groups(p.t.N, blockIdx.x, gridDim.x, g0, g1);
+  task_groups(t.N, blockIdx.x, gridDim.x, g0, g1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTmaStages; ++s) {
@@ -54,17 +61,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1) k_gemv_tma(TmaGemvParams p) {
     // before the wait.
     if (lane == 0) {
       long long it = 0;
-      ring_produce<kTmaStages>(p.t, g0, g1, ring, full, empty, it, p.error);
+      ring_produce<kTmaStages>(t, g0, g1, ring, full, empty, it, p.error);
       ring_drain<kTmaStages>(full, it);
     }
     pdl_wait();
     return;
   }
   pdl_wait();
-  ring_stage_act<NB>(p.t, act, red, threadIdx.x);
+  ring_stage_act<NB>(t, act, red, threadIdx.x);
   long long it = 0;
   bool bad = false, dead = false;
-  ring_consume<NB, kTmaStages>(p.t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, threadIdx.x);
+  ring_consume<NB, kTmaStages>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, threadIdx.x);
 }
 
 size_t gemv_tma_smem(int NB, int K) {
@@ -100,10 +107,13 @@ void configure_gemv_tma_kernels() {
 bool launch_gemv_tma(const bf16 *W, int N, int K, const bf16 *in, int in_stride, const bf16 *norm_w, float eps,
                      bf16 *out, int out_stride, int epilogue, int n_rows, int *error, int sm_count,
                      cudaStream_t st) {
-  if (K % kRingPiece != 0 || n_rows < 1 || n_rows > 2) return false;
+  if (K % kRingPiece != 0 || K > kStageMaxK || n_rows < 1 || n_rows > 2) return false;
   if ((reinterpret_cast<uintptr_t>(W) & 15) != 0) return false;
   if (epilogue == kEpiSwiGLU && (N % 2) != 0) return false;
-  TmaGemvParams p{GemvTask{W, N, K, in, in_stride, norm_w, eps, out, out_stride, epilogue}, error};
+  TmaGemvParams p{};
+  p.t = GemvTask{W, N, K, in, in_stride, norm_w, eps, out, out_stride, epilogue};
+  p.error = error;
+  encode_stage_map(&p.wmap, W, N, K);
   if (n_rows == 1) {
     if (epilogue == kEpiSwiGLU) tma_launch<1, kEpiSwiGLU>(p, sm_count, st);
     else if (epilogue == kEpiResidual) tma_launch<1, kEpiResidual>(p, sm_count, st);

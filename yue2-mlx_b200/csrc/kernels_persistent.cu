@@ -8,12 +8,13 @@
 // shared-memory ring, waiting only for ring space — never for activations — so HBM keeps
 // streaming while the consumer warps wait at operation boundaries.
 //
-// Grid: one CTA per SM, co-resident by cooperative launch. Block: 8 consumer warps + 1
-// producer warp. Operation boundaries are global counters: a CTA finishing its share
-// fences its writes and adds 1; consumers of the next operation wait (bounded) until
-// the counter reaches (epoch + 1) x contributions, where `epoch` counts completed steps
-// (the last action of a step is CTA 0 advancing it), so counters never need a reset
-// between steps. Inter-CTA data is read through L2 (ld.cg).
+// Grid: one CTA per SM, co-resident by cooperative launch. Block: 8 consumer warps + a
+// producer warpgroup (one lane issues the copies; see kPersistThreads). Operation boundaries are flagged words: every output is stored as an
+// 8-byte word of two BF16 values and a flag naming the step and the operation, and the
+// next operation polls (bounded) the words it reads until they carry the expected flag.
+// Global counters remain for the position latch at the step's start and, under tensor
+// parallelism, for the head; `epoch` counts completed steps (the last action of a step is
+// CTA 0 advancing it), so neither flags nor counters need a reset between steps.
 //
 // The GEMV and attention code is the same device code as the standalone kernels
 // (tma_ring.cuh, attn_decode.cuh): both paths produce identical logits.
@@ -26,24 +27,41 @@
 // Tensor parallelism (tp_world ranks, one GPU each, every rank running this kernel for the
 // same step): each rank's operations compute its rows (its heads' attention, its hidden
 // rows of O and down, its FFN rows of gate/up, its columns of the head) and the epilogues
-// store every value both locally and into each peer's mapped copy of the buffer (x, attn,
-// mlp, logits: one exchange region per session, mapped by CUDA IPC). The counters of
-// attention, O, gate/up, down and the head are then released to every rank at system
-// scope, and their waits count all ranks' contributions — the all-gather is the
-// epilogue's stores, and the wait is the only synchronization. QKV stays rank-local.
+// store every flagged word both locally and into each peer's mapped copy of the buffer
+// (x, attn, mlp, logits: one exchange region per session, mapped by CUDA IPC); a reader
+// polls its local copy for the flag. The all-gather is the epilogue's stores, and the
+// flag wait is the only synchronization. The head's counter is released to every rank at
+// system scope and counts all ranks' contributions. QKV stays rank-local.
 #include "attn_decode.cuh"
 #include "tma_ring.cuh"
 
 namespace yar {
 
 constexpr int kPersistStages = 6;
-constexpr int kPersistThreads = (kRingConsumers + 1) * 32;
+// Block: two consumer warpgroups (warps 0..7) and a producer warpgroup (warps 8..11; lane
+// 0 of warp 8 issues the copies). The launch gives every thread 168 registers (65536 / 384,
+// rounded down to 8); the producer warpgroup then returns registers (setmaxnreg.dec to
+// 40) and the consumer warpgroups take them (setmaxnreg.inc to 232): 4 x 32 x 40 +
+// 8 x 32 x 232 = 64,512, the launch's total, and per scheduler partition (warps k, k+4,
+// k+8) 40 + 2 x 232 = 504 x 32 <= 16,384. With 168 the one-row kernel spilled; with 232 it
+// does not. The host launches only a build whose kernels use exactly kPersistLaunchRegs
+// (an increase beyond the launch's total would never be granted).
+constexpr int kPersistProducerWarps = 4;
+constexpr int kPersistThreads = (kRingConsumers + kPersistProducerWarps) * 32;
+constexpr int kPersistLaunchRegs = 168, kPersistProducerRegs = 40, kPersistConsumerRegs = 232;
+static_assert(kPersistProducerWarps * 32 * kPersistProducerRegs + kRingConsumers * 32 * kPersistConsumerRegs <=
+                  kPersistThreads * kPersistLaunchRegs,
+              "register split exceeds the launch's registers");
+static_assert(kPersistProducerRegs + 2 * kPersistConsumerRegs <= 512, "register split exceeds a scheduler partition");
 constexpr int kPersistMaxK = 6144;
 constexpr long long kCounterWaitLimit = 1ll << 22;  // polls of ~100 ns: under a second
 
 constexpr int kMaxTpWorld = 8;
+constexpr int kMaxPersistGrid = 256;
 
 struct PersistParams {
+  CUtensorMap head_map;        // stage map of this rank's phase rows of the head (`head`, `head_rows`)
+  const CUtensorMap *wmaps;    // device array [layer][4]: stage maps of qkv, o, gu, down
   const LayerWeights *layers;  // device array, one entry per layer
   // QKV: this rank's q/k/v rows; QD, F: the model's query and FFN widths (the K of O and
   // down); HS, h0: this rank's hidden rows of O and down; FL, f0: its FFN rows.
@@ -72,7 +90,11 @@ struct PersistParams {
   // each peer's (as mapped here).
   int tp_world, tp_ndst;
   long long tp_dst[kMaxTpWorld - 1];
+  // CTA c runs attention units attn_rank[c], + grid, ...: rank 0 is the CTA with the
+  // fewest GEMV stages per layer (attention_ranks below).
+  unsigned char attn_rank[kMaxPersistGrid];
 };
+static_assert(sizeof(PersistParams) <= 4096, "kernel parameters must fit the 4 KB launch limit");
 
 __device__ __forceinline__ unsigned long long sm_clock() { return (unsigned long long)clock64(); }
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -119,7 +141,8 @@ __device__ __forceinline__ bool team_any(int bar_id, bool v) {
 
 // The attention units of one step: rows in order; an active row has kv_heads x n_splits
 // units (kv head major), an inactive row kv_heads units without work, each standing in for
-// its kv head's arrival. Unit u runs on CTA u % grid, on all its consumer warps.
+// its kv head's arrival. Unit u runs on the CTA of attention rank u % grid, on all its
+// consumer warps.
 // Its chunks travel through the CTA's weight ring as stages (K rows, then V rows),
 // issued right after the layer's QKV stages.
 template <int NB>
@@ -163,11 +186,35 @@ constexpr int kMaxCtaChunks = 64;  // KV chunks of one CTA in one layer
 // Rotation of the group ranges per operation (o: 0 QKV, 2 O, 3 gate/up, 4 down), as
 // fractions of the grid: the CTAs holding one more group than the even share differ from
 // operation to operation, so no CTA carries the most stages of every operation of a layer
-// (on 148 SMs a CTA streams at most 22 stages per layer instead of 23) and every producer
-// gets ahead of its consumers somewhere in the layer.
+// (on 148 SMs a CTA streams at most 22 GEMV stages per layer instead of 23) and every
+// producer gets ahead of its consumers somewhere in the layer.
 __host__ __device__ __forceinline__ int op_rotation(int o, int grid) {
   const int num = o == 2 ? 125 : o == 3 ? 108 : o == 4 ? 75 : 0;
   return num * grid / 148;
+}
+
+// Stages CTA `cta` streams of an N x K operation o (the split task_groups and the
+// producer use).
+__host__ __device__ __forceinline__ int op_cta_stages(int N, int K, int o, int cta, int grid) {
+  const int groups = (N + 7) / 8, pos = (cta + op_rotation(o, grid)) % grid;
+  return ((pos + 1) * groups / grid - pos * groups / grid) * (K / kRingPiece);
+}
+
+// Attention ranks: CTAs ordered by the GEMV stages they stream per layer (fewest first,
+// then by index). A KV chunk is one more stage in its CTA's ring, and every operation
+// waits for the CTA that finishes it last, so the units go to the CTAs with the fewest
+// stages: at 96 one-chunk units on 148 SMs no CTA streams more than 22 stages per layer
+// (23 with units on CTAs 0..95).
+inline void attention_ranks(PersistParams &p, int grid) {
+  int order[kMaxPersistGrid], total[kMaxPersistGrid];
+  for (int c = 0; c < grid; ++c) {
+    total[c] = op_cta_stages(p.QKV, p.H, 0, c, grid) + op_cta_stages(p.HS, p.QD, 2, c, grid) +
+               op_cta_stages(2 * p.FL, p.H, 3, c, grid) + op_cta_stages(p.HS, p.F, 4, c, grid);
+    int i = c;  // insertion sort by (total, index)
+    for (; i > 0 && total[order[i - 1]] > total[c]; --i) order[i] = order[i - 1];
+    order[i] = c;
+  }
+  for (int i = 0; i < grid; ++i) p.attn_rank[order[i]] = static_cast<unsigned char>(i);
 }
 
 __device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
@@ -231,7 +278,7 @@ struct KvChunkRef {
 // operation's constants are loaded once on entering it.
 struct ProdCursor {
   int l, o, i, len;
-  const bf16 *W;  // GEMV operations: weight, K, this CTA's first group, stages per group
+  const CUtensorMap *map;  // GEMV operations: weight stage map, K, this CTA's first group, stages per group
   int K, N, g, ks, KS;
 };
 
@@ -242,22 +289,22 @@ struct ProdCursor {
 template <int NB>
 struct Producer {
   const LayerWeights *layers;
-  const bf16 *head;
+  const CUtensorMap *wmaps, *head_map;
   int head_rows, H, QKV, QD, F, HS, FL, nL, epoch;
   bf16 *pool;
   AttnGeom g;
   int max_splits;
   const int *page_table, *ctr, *active, *cur_pos;
   int *error;
-  int nkv;
+  int nkv, arank;
   bool planned, failed;
   KvChunkRef *kv;  // this CTA's chunk list (shared memory, kMaxCtaChunks entries)
 
   __device__ Producer(const PersistParams &p, int ep, KvChunkRef *kv_smem)
-      : layers(p.layers), head(p.head), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F), HS(p.HS),
+      : layers(p.layers), wmaps(p.wmaps), head_map(&p.head_map), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F), HS(p.HS),
         FL(p.FL), nL(p.n_layers), epoch(ep), pool(p.ap.pool), g(p.ap.g), max_splits(p.ap.max_splits),
         page_table(p.ap.page_table), ctr(p.ctr), active(p.active), cur_pos(p.cur_pos), error(p.error), nkv(0),
-        planned(false), failed(false), kv(kv_smem) {}
+        arank(p.attn_rank[blockIdx.x]), planned(false), failed(false), kv(kv_smem) {}
 
   // This CTA's KV chunks, once CTA 0 has latched the step's positions (bounded wait).
   __device__ bool plan() {
@@ -280,7 +327,7 @@ struct Producer {
       rows.pos[b] = __ldcg(cur_pos + b);
     }
     const int U = step_units(rows, g.kv_heads, max_splits);
-    for (int u = blockIdx.x; u < U; u += gridDim.x) {
+    for (int u = arank; u < U; u += gridDim.x) {
       const UnitInfo ui = step_unit(rows, g.kv_heads, max_splits, u);
       for (int c = ui.c0; c < ui.c1; ++c) {
         if (nkv == kMaxCtaChunks) {
@@ -307,14 +354,14 @@ struct Producer {
       return;
     }
     if (c.l == nL) {
-      c.W = head, c.N = head_rows, c.K = H;
+      c.map = head_map, c.N = head_rows, c.K = H;
     } else {
-      const LayerWeights &w = layers[c.l];
+      const CUtensorMap *m = wmaps + 4 * c.l;
       switch (c.o) {
-        case 0: c.W = w.qkv, c.N = QKV, c.K = H; break;
-        case 2: c.W = w.o, c.N = HS, c.K = QD; break;
-        case 3: c.W = w.gu, c.N = 2 * FL, c.K = H; break;
-        default: c.W = w.down, c.N = HS, c.K = F; break;
+        case 0: c.map = m, c.N = QKV, c.K = H; break;
+        case 2: c.map = m + 1, c.N = HS, c.K = QD; break;
+        case 3: c.map = m + 2, c.N = 2 * FL, c.K = H; break;
+        default: c.map = m + 3, c.N = HS, c.K = F; break;
       }
     }
     const int groups = (c.N + 7) / 8;
@@ -369,11 +416,8 @@ struct Producer {
       }
       return;
     }
-    const int r0 = c.g * 8, nrows = min(8, c.N - r0);
-    const bf16 *src = c.W + size_t(r0) * c.K + size_t(c.ks) * kRingPiece;
-    mbar_arrive_expect_tx(bar, unsigned(nrows) * kRingPiece * 2);
-    for (int r = 0; r < nrows; ++r)
-      bulk_g2s_hint(dst + r * kRingRowPitch, src + size_t(r) * c.K, kRingPiece * 2, bar, pol);
+    mbar_arrive_expect_tx(bar, unsigned(kRingStageBytes));
+    stage_load(dst, c.map, c.g * 8, c.ks, bar, pol);
   }
   // Pull the stage's bytes into L2.
   __device__ void prefetch(const ProdCursor &c) const {
@@ -386,15 +430,14 @@ struct Producer {
       prefetch_l2(pool + (blk + 1) * g.page_elems + off, unsigned(r.n_main) * 256);
       return;
     }
-    const int r0 = c.g * 8, nrows = min(8, c.N - r0);
-    const bf16 *src = c.W + size_t(r0) * c.K + size_t(c.ks) * kRingPiece;
-    for (int r = 0; r < nrows; ++r) prefetch_l2(src + size_t(r) * c.K, kRingPiece * 2);
+    stage_prefetch(c.map, c.g * 8, c.ks);
   }
 };
 
 template <int NB>
-__global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(PersistParams p) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+__global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const __grid_constant__ PersistParams p) {
+  // 1024-byte alignment: the weight stages are 128-byte-swizzled tensor copies.
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   constexpr int NS = kPersistStages;
   using ASm = AttnTeamSmem<128, 2>;
   // Layout: ring | act (GEMV activations) aliased with the attention teams' scratch (the
@@ -408,8 +451,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
   __shared__ float red[NB * kRingConsumers];
   __shared__ AttnRow<128> rowst[NB];
-  __shared__ int s_epoch, s_bad;
+  __shared__ int s_epoch, s_bad, s_trace;
   __shared__ KvChunkRef kv_chunks[kMaxCtaChunks];
+  __shared__ uint4 s_keep[2][NB * kResKeepCols / 8];  // kept residual columns for O and down
   __shared__ long long s_dst[kMaxTpWorld - 1];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -417,6 +461,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   const bool tp = p.tp_world > 1;
   const int W = p.tp_world;
   if (threadIdx.x < kMaxTpWorld - 1) s_dst[threadIdx.x] = threadIdx.x < p.tp_ndst ? p.tp_dst[threadIdx.x] : 0;
+  if ((smem_u32(ring) & 1023) != 0) {  // never copy into a misaligned ring (every CTA alike)
+    if (threadIdx.x == 0) atomicOr(p.error, 1);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -426,9 +474,15 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_epoch = ld_acquire(p.epoch);
     s_bad = 0;
+    // The timeline records steps with an active row only (the sampler that ran before this
+    // kernel has set this step's activity), so it keeps the last step that did work.
+    int any_active = 0;
+    for (int b = 0; b < NB; ++b) any_active |= __ldcg(p.active + b);
+    s_trace = p.trace != nullptr && any_active != 0;
   }
   __syncthreads();
   const int epoch = s_epoch;
+  unsigned long long *const trace = s_trace ? p.trace : nullptr;
   const int all = int(gridDim.x);
   // The op's task; an injected fault makes its input wait for a flag that is never written.
   auto task = [&](int l, int k) {
@@ -440,10 +494,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   };
   auto fl = [&](int op) { return ll_flag(epoch, op, nL); };
 
-  if (warp == kRingConsumers) {
-    if (lane == 0) {
+  if (warp >= kRingConsumers) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPersistProducerRegs));
+    if (warp == kRingConsumers && lane == 0) {
       auto pstamp = [&](int o, int k) {
-        if (p.trace) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
+        if (trace) trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
       };
       Producer<NB> pr(p, epoch, kv_chunks);
       ProdCursor ic, pc;
@@ -466,7 +521,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
         }
         const int op = 5 * ic.l + ic.o, so = ic.o == 1 ? 6 : 4;  // attention op slots 4/5 hold unit stamps
         if (ic.i == 0) pstamp(op, so);
-        pr.issue(ic, ring + size_t(s) * 8 * kRingRowPitch, &full[s], pol);
+        pr.issue(ic, ring + size_t(s) * kRingStageElems, &full[s], pol);
         ++it;
         iv = pr.next(ic);
         if (!iv || 5 * ic.l + ic.o != op) pstamp(op, so + 1);
@@ -477,11 +532,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   }
 
   // ------------------------------------------------------------------ consumers
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPersistConsumerRegs));
   const int ctid = threadIdx.x;
   bool bad = false, dead = false;  // dead: a ring wait expired (the producer is presumed stuck)
   long long it = 0;
   auto stamp = [&](int o, int k) {
-    if (p.trace && ctid == 0) p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
+    if (trace && ctid == 0) trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
   };
   // Thread 0 publishes one share of counter idx: to this rank only (GPU scope), or
   // (exchanged operations under tensor parallelism) to every rank at system scope.
@@ -562,9 +618,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   }
   // Trace calibration: globaltimer (ns) and the SM clock at the step's start and end.
   auto calib = [&](int o) {
-    if (p.trace && ctid == 0) {
-      p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 6] = globaltimer();
-      p.trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 7] = sm_clock();
+    if (trace && ctid == 0) {
+      trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 6] = globaltimer();
+      trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + 7] = sm_clock();
     }
   };
   // Hidden-state record (optional): CTA 0 copies the residual rows once they carry the flag
@@ -597,20 +653,42 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     srows.active[b] = rowst[b].active;
     srows.pos[b] = rowst[b].pos;
   }
-  const int U = step_units(srows, kvh_n, nsplit);
+  const int U = step_units(srows, kvh_n, nsplit), arank = p.attn_rank[blockIdx.x];
 
   // One GEMV operation: stage the flagged input rows (the wait for the producing
   // operation), consume this CTA's stages, write its flagged outputs.
   // A CTA without rows of the operation (possible under tensor parallelism) skips it: it
   // neither waits for nor reads the input words, which a later operation may overwrite.
-  auto gemv_op = [&](const GemvTask &t, int op_slot, const uint4 (*wn)[4], int o) {
+  // `keep`, [keep_lo, keep_hi): raw input columns the staging keeps (RMSNorm operations).
+  // Returns whether the CTA took part.
+  auto gemv_op = [&](const GemvTask &t, int op_slot, const uint4 (*wn)[4], int o, uint4 *keep = nullptr,
+                     int keep_lo = 0, int keep_hi = 0) {
     int g0, g1;
     task_groups(t.N, blockIdx.x, gridDim.x, g0, g1, op_rotation(o, int(gridDim.x)));
-    if (g0 == g1) return;
-    if (!ring_stage_act<NB>(t, act, red, ctid, wn, p.error)) bad = true;
+    if (g0 == g1) return false;
+    if (!ring_stage_act<NB, kPersistMaxK / kRingPiece>(t, act, red, ctid, wn, p.error, keep, keep_lo, keep_hi)) bad = true;
     stamp(op_slot, 1);
     ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, ctid);
     stamp(op_slot, 2);
+    return true;
+  };
+  // The residual operations (O, down) add this CTA's output columns [8 g0, 8 g1) of x (from
+  // h0): the RMSNorm staging before each (QKV, gate/up) reads all of x and keeps those
+  // columns in s_keep[0] (for O) and s_keep[1] (for down), so their epilogues read the old
+  // residual from shared memory instead of polling it through L2.
+  int keep_lo[2], keep_hi[2];
+  for (int i = 0; i < 2; ++i) {
+    int g0, g1;
+    task_groups(p.HS, blockIdx.x, gridDim.x, g0, g1, op_rotation(i == 0 ? 2 : 4, int(gridDim.x)));
+    keep_lo[i] = 8 * g0;
+    keep_hi[i] = (g1 - g0) * 8 <= kResKeepCols ? 8 * g1 : 8 * g0;  // too wide: poll instead
+  }
+  auto with_kept = [&](GemvTask t, bool kept, int i) {
+    if (kept && keep_hi[i] > keep_lo[i]) {
+      t.res_smem = reinterpret_cast<const uint32_t *>(s_keep[i]);
+      t.res_lo = keep_lo[i];
+    }
+    return t;
   };
 
   uint4 wn_next[4];  // RMSNorm weight chunks of the next norm-prologue GEMV, loaded before its wait
@@ -618,13 +696,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
   for (int l = 0; l < nL; ++l) {
     // QKV (RMSNorm of x fused).
     stamp(5 * l, 0);
-    gemv_op(task(l, 0), 5 * l, &wn_next, 0);
+    const bool kept_o = gemv_op(task(l, 0), 5 * l, &wn_next, 0, s_keep[0], p.h0 + keep_lo[0], p.h0 + keep_hi[0]);
     stamp(5 * l, 3);
     // Attention: the CTA's units, one after another on all consumer warps; each unit waits
     // for its own kv head's projections (flagged words) and streams its KV chunks as ring
     // stages (every consumer warp releases each once).
     float wv[4];
-    if (int(blockIdx.x) < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
+    if (arank < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
     stamp(5 * l + 1, 0);
     {
       DecodeAttnParams ap = p.ap;
@@ -640,11 +718,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
       ap.ll_limit = p.ll_limit;
       if (p.inject_op == c_op(l, 1)) ap.qkv_flag ^= 0x80000000u;
       long long itk = it;
-      for (int k = 0, u = blockIdx.x; u < U; ++k, u += gridDim.x) {
+      for (int k = 0, u = arank; u < U; ++k, u += gridDim.x) {
         const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
         const int nch = ui.c1 - ui.c0;
         unsigned long long *st =
-            (p.trace && k == 0) ? p.trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
+            (trace && k == 0) ? trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
         const AttnRow<128> &rs = rowst[ui.row];
         if (ui.active && !bad &&
             !attn_qk<128, 2>(ap, *team_sm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ctid, 1))
@@ -668,8 +746,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
             }
           }
           wbad = __any_sync(0xFFFFFFFFu, wbad);
+          if (j == 0) attn_stamp(st, 1, ctid);  // the unit's first chunk has landed
           if (!wbad) {
-            const bf16 *ks = ring + size_t(sidx) * 8 * kRingRowPitch;
+            const bf16 *ks = ring + size_t(sidx) * kRingStageElems;
             const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
             attn_chunk<128, 2>(team_sm->q_b, team_sm->knew, team_sm->vnew, ks, ks + kKvChunk * 128, n_main,
                                rs.pos - base < kKvChunk, ap.g.scale, wacc, ctid);
@@ -693,16 +772,16 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     stamp(5 * l + 1, 2);
     // O (+ residual).
     stamp(5 * l + 2, 0);
-    gemv_op(task(l, 1), 5 * l + 2, nullptr, 2);
+    gemv_op(with_kept(task(l, 1), kept_o, 0), 5 * l + 2, nullptr, 2);
     stamp(5 * l + 2, 3);
     // gate/up (RMSNorm of x fused, SwiGLU epilogue).
     ring_norm_w_load(task(l, 2), wn_next, ctid);
     stamp(5 * l + 3, 0);
-    gemv_op(task(l, 2), 5 * l + 3, &wn_next, 3);
+    const bool kept_d = gemv_op(task(l, 2), 5 * l + 3, &wn_next, 3, s_keep[1], p.h0 + keep_lo[1], p.h0 + keep_hi[1]);
     stamp(5 * l + 3, 3);
     // down (+ residual).
     stamp(5 * l + 4, 0);
-    gemv_op(task(l, 3), 5 * l + 4, nullptr, 4);
+    gemv_op(with_kept(task(l, 3), kept_d, 1), 5 * l + 4, nullptr, 4);
     stamp(5 * l + 4, 3);
     if (l + 1 < nL) ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
     dump_x(l + 1);
@@ -715,7 +794,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(Persis
     stamp(5 * nL, 0);
     task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
     const bool extra_cta = p.extra_row >= 0 && blockIdx.x == gridDim.x - 1;  // uses `act` below
-    if ((g0 < g1 || extra_cta) && !ring_stage_act<NB>(head, act, red, ctid, nullptr, p.error)) bad = true;
+    if ((g0 < g1 || extra_cta) && !ring_stage_act<NB, kPersistMaxK / kRingPiece>(head, act, red, ctid, nullptr, p.error))
+      bad = true;
     stamp(5 * nL, 1);
     ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, ctid);
     stamp(5 * nL, 2);
@@ -765,14 +845,37 @@ void configure_persistent_kernels() {
 }
 
 // True when the persistent kernel handles this model and row count.
+void build_stage_maps(Model &m) {
+  const Dims &d = m.d, &f = m.full;
+  if (d.hidden % kRingPiece || f.qdim() % kRingPiece || f.ffn % kRingPiece) return;
+  // The shapes launch_persistent gives the kernel (this rank's rows).
+  const int QKV = d.qkv_rows(), HS = m.tp.h_rows, FL = d.ffn;
+  std::vector<CUtensorMap> maps(size_t(d.layers) * 4);
+  for (int l = 0; l < d.layers; ++l) {
+    const LayerWeights &w = m.layers[l];
+    encode_stage_map(&maps[4 * l + 0], w.qkv, QKV, d.hidden);
+    encode_stage_map(&maps[4 * l + 1], w.o, HS, f.qdim());
+    encode_stage_map(&maps[4 * l + 2], w.gu, 2 * FL, d.hidden);
+    encode_stage_map(&maps[4 * l + 3], w.down, HS, f.ffn);
+  }
+  YAR_CUDA(cudaMalloc(&m.d_wmaps, maps.size() * sizeof(CUtensorMap)));
+  YAR_CUDA(cudaMemcpy(m.d_wmaps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+}
+
 bool persistent_supported(const Model &m, int n_rows) {
   // The ring GEMVs need every K (hidden, and the model's query and FFN widths: O and down
-  // keep their whole input width under tensor parallelism) a multiple of 2048.
+  // keep their whole input width under tensor parallelism) a multiple of 2048, and the
+  // stage maps of the layers' weights.
   const Dims &d = m.d, &f = m.full;
-  if (n_rows < 1 || n_rows > 2 || m.tp_world > kMaxTpWorld) return false;
+  if (n_rows < 1 || n_rows > 2 || m.tp_world > kMaxTpWorld || !m.d_wmaps) return false;
   if (d.head_dim != 128 || d.heads != 2 * d.kv_heads) return false;
   if (d.hidden % kRingPiece || f.qdim() % kRingPiece || f.ffn % kRingPiece || f.ffn > kPersistMaxK ||
       d.hidden > kPersistMaxK || f.qdim() > kPersistMaxK)
+    return false;
+  // The register split (setmaxnreg) assumes the launch's per-thread registers.
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, n_rows == 1 ? k_decode_persistent<1> : k_decode_persistent<2>) != cudaSuccess ||
+      fa.numRegs != kPersistLaunchRegs)
     return false;
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, n_rows == 1 ? k_decode_persistent<1> : k_decode_persistent<2>,
@@ -787,6 +890,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   if (m.tp_world > 1 && !s.tp_mapped) throw Error("RuntimeError", "persistent tensor-parallel decode needs mapped peers");
   PersistParams p;
   p.layers = m.d_layers;
+  p.wmaps = static_cast<const CUtensorMap *>(m.d_wmaps);
   p.n_layers = d.layers;
   p.H = d.hidden;
   p.QKV = d.qkv_rows();
@@ -806,6 +910,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   const int c0 = std::min(width, m.tp_rank * slice), c1 = std::min(width, c0 + slice);
   p.head = m.lm_head + size_t(pr.row0 + c0) * d.hidden;
   p.head_rows = std::max(0, std::min(c1, pr.n_main) - c0);
+  if (p.head_rows > 0) encode_stage_map(&p.head_map, p.head, p.head_rows, d.hidden);
   p.extra_row = pr.extra >= 0 && c0 <= pr.n_main && pr.n_main < c1 ? pr.extra - pr.row0 - c0 : -1;
   p.x = s.x;
   p.qkv = s.qkv;
@@ -871,6 +976,8 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.inject_op = s.inject_op;
   p.ll_limit = s.inject_op > 0 ? (1ll << 16) : (1ll << 22);
   p.prefetch_stages = s.prefetch_stages;
+  if (m.sm_count > kMaxPersistGrid) throw Error("RuntimeError", "persistent decode takes at most 256 SMs");
+  attention_ranks(p, m.sm_count);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.sm_count);

@@ -379,6 +379,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     }
     YAR_CUDA(cudaMalloc(&m->d_layers, sizeof(LayerWeights) * d.layers));
     YAR_CUDA(cudaMemcpy(m->d_layers, m->layers.data(), sizeof(LayerWeights) * d.layers, cudaMemcpyHostToDevice));
+    build_stage_maps(*m);
     m->embed = at(o_embed);
     m->lm_head = at(o_head);
     m->final_norm = at(o_norm);
@@ -416,6 +417,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     tp_destroy(*m);
     if (m->arena) cudaFree(m->arena);
     if (m->d_layers) cudaFree(m->d_layers);
+    if (m->d_wmaps) cudaFree(m->d_wmaps);
     delete m;
     throw;
   }
@@ -428,6 +430,7 @@ void free_model(Model *m) {
   tp_destroy(*m);
   if (m->arena) cudaFree(m->arena);
   if (m->d_layers) cudaFree(m->d_layers);
+  if (m->d_wmaps) cudaFree(m->d_wmaps);
   delete m;
 }
 

@@ -1,22 +1,29 @@
-// tma_ring.cuh — the shared-memory weight ring of the decode GEMVs: bulk asynchronous
-// copies (cp.async.bulk, the TMA engine's linear mode) into 32 KB stages tracked by
-// mbarriers, one producer lane and eight consumer warps. Used by the standalone GEMV
-// kernel and by the persistent decode kernel, which therefore compute identical bits.
+// tma_ring.cuh — the shared-memory weight ring of the decode GEMVs: one TMA tensor copy
+// (cp.async.bulk.tensor) per 32 KB stage, tracked by mbarriers, one producer lane and eight
+// consumer warps. Used by the standalone GEMV kernel and by the persistent decode kernel,
+// which therefore compute identical bits.
 //
 // A GEMV task y = W x (W row-major [N][K], K a multiple of 2048) is cut into 8-row groups;
-// a CTA owns groups [g0, g1) and streams each group as K/2048 stages of 8 row pieces of
-// 2048 BF16 (4 KB each, contiguous). Consumer warp w computes row 8g + w; lanes read the
-// piece lane-contiguously (16-byte chunks c = lane + 32t), so shared-memory reads are
-// conflict-free. Every wait is bounded.
+// a CTA owns groups [g0, g1) and streams each group as K/2048 stages of 8 rows x 2048
+// columns. A stage arrives through the matrix's stage map: a 3-D view of W as {64 columns,
+// N rows, K/64 column blocks} with strides {2K, 128} bytes and a {64, 8, 32} box under the
+// 128-byte swizzle, so one copy moves the whole 32 KB and shared memory receives 32 blocks
+// of 8 rows x 128 bytes in which row r's 16-byte chunk c sits at chunk c ^ r. The eight
+// rows of an ldmatrix 8x8 matrix (one chunk of rows 0..7) then fall in eight different
+// bank groups, and rows past N arrive zero-filled. (Eight 4 KB linear copies into padded
+// rows take about 1.45x the time per stage: the copy engine works per request.)
+// Every wait is bounded.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace yar {
 
 constexpr int kRingConsumers = 8;
-constexpr int kRingPiece = 2048;                      // BF16 elements per row piece
-constexpr int kRingRowPitch = kRingPiece + 8;         // +16 bytes: ldmatrix rows hit distinct banks
-constexpr int kRingStageBytes = 8 * kRingRowPitch * 2;  // 32,896 bytes
+constexpr int kRingPiece = 2048;                       // columns of a stage
+constexpr int kRingStageElems = 8 * kRingPiece;        // 8 rows x 2048 BF16
+constexpr int kRingStageBytes = kRingStageElems * 2;   // 32 KB (the tensor copy's transaction bytes)
 constexpr long long kRingWaitLimit = 1ll << 22;      // try_wait polls before giving up (seconds)
 
 struct GemvTask {
@@ -44,7 +51,19 @@ struct GemvTask {
   int out_ll_stride = 0;
   uint32_t out_flag = 0, res_flag = 0;
   long long ll_limit = 1ll << 22;  // polls of a flagged wait before it gives up
+  // Flagged residual epilogue: the old residual words of this CTA's output columns
+  // [res_lo, res_lo + kResKeepCols) in shared memory (row b at word b * kResKeepCols / 2),
+  // read instead of polling the residual words in global memory. Null: poll.
+  const uint32_t *res_smem = nullptr;
+  int res_lo = 0;
+  // The stage map of W (encode_stage_map), for producers that copy through it
+  // (ring_produce); a kernel-parameter or global-memory address.
+  const CUtensorMap *wmap = nullptr;
 };
+
+// Host: W's stage map ({64, N, K/64} view, {64, 8, 32} box, 128-byte swizzle) into `map`.
+void encode_stage_map(CUtensorMap *map, const bf16 *W, int N, int K);
+constexpr int kResKeepCols = 64;  // residual columns per row a CTA can keep in shared memory
 
 // ---------------------------------------------------------------------------------------
 // Flagged words: two BF16 values (low half = the even element) and a 32-bit flag in one
@@ -168,6 +187,24 @@ __device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsign
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Stage (rows [row0, row0 + 8), columns [2048 ks, 2048 ks + 2048)) of a matrix through its
+// stage map into `dst` (1024-byte aligned), completing kRingStageBytes on `bar`.
+__device__ __forceinline__ void stage_load(bf16 *dst, const CUtensorMap *map, int row0, int ks, uint64_t *bar,
+                                           uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(0), "r"(row0), "r"(ks * (kRingPiece / 64)), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+// The same stage pulled into L2 only.
+__device__ __forceinline__ void stage_prefetch(const CUtensorMap *map, int row0, int ks) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(0), "r"(row0),
+               "r"(ks * (kRingPiece / 64))
+               : "memory");
+}
+// Offset (elements) in a swizzled stage of the 16-byte chunk C (columns 8C..8C+7) of row r.
+__device__ __forceinline__ int stage_chunk(int C, int r) { return (C >> 3) * 512 + r * 64 + (((C & 7) ^ r) << 3); }
 // Weights are read once per token and 3 GB pass through L2 between two reads of the same
 // row, so they are marked evict-first: L2 keeps the KV cache and the activations instead.
 __device__ __forceinline__ uint64_t weight_stream_policy() {
@@ -191,8 +228,8 @@ __device__ __forceinline__ void task_groups(int N, int cta, int ctas, int &g0, i
   g1 = int((long long)(pos + 1) * groups / ctas);
 }
 
-// Producer: issue this CTA's stages of one task, continuing the ring sequence `it`.
-// Returns false (and stops) when a wait for a free stage expires.
+// Producer: issue this CTA's stages of one task (one stage-map copy each), continuing the
+// ring sequence `it`. Returns false (and stops) when a wait for a free stage expires.
 template <int NS>
 __device__ bool ring_produce(const GemvTask &t, int g0, int g1, bf16 *ring, uint64_t *full, uint64_t *empty,
                              long long &it, int *error) {
@@ -205,11 +242,8 @@ __device__ bool ring_produce(const GemvTask &t, int g0, int g1, bf16 *ring, uint
         atomicOr(error, 4);
         return false;
       }
-      const int r0 = g * 8, nrows = min(8, t.N - r0);
-      mbar_arrive_expect_tx(&full[s], unsigned(nrows) * kRingPiece * 2);
-      for (int r = 0; r < nrows; ++r)
-        bulk_g2s_hint(ring + (size_t(s) * 8 + r) * kRingRowPitch,
-                      t.W + size_t(r0 + r) * t.K + size_t(ks) * kRingPiece, kRingPiece * 2, &full[s], pol);
+      mbar_arrive_expect_tx(&full[s], unsigned(kRingStageBytes));
+      stage_load(ring + size_t(s) * kRingStageElems, t.wmap, g * 8, ks, &full[s], pol);
     }
   return true;
 }
@@ -221,9 +255,7 @@ __device__ void ring_drain(uint64_t *full, long long issued) {
   for (long long i = issued > NS ? issued - NS : 0; i < issued; ++i) mbar_wait(&full[i % NS], unsigned(i / NS) & 1u);
 }
 
-// Consumers: the task's activation rows into `act` ([NB][K] BF16), RMSNorm applied when the
-// task has a norm weight (modeling_yue2.py:131-132): x is read once into registers (up to
-// 4 chunks of 8 per thread, K <= 8192), reduced, normalized. `red` holds NB x 8 floats.
+// `red` (ring_stage_act) holds NB x 8 floats.
 // Activation rows are kept in shared memory in MMA-fragment order: within every block of
 // 32 elements (16 two-element words), word w sits at position (w % 4) * 4 + w / 4, so the
 // four words a lane needs for two k-tiles (w = q, q + 4, q + 8, q + 12) are one 16-byte
@@ -254,55 +286,87 @@ __device__ __forceinline__ void ring_norm_w_load(const GemvTask &t, uint4 (&wn)[
   }
 }
 
-// Flagged staging: the thread's 8-element chunk k of row b, once its four words carry the
-// task's input flag; false (chunk zeroed) when the wait gave up.
-__device__ __forceinline__ bool ll_chunk(const GemvTask &t, int b, int k, uint4 &out, const int *error) {
-  uint32_t d[4];
-  const bool ok = ll_wait<2>(t.in_ll + size_t(b) * t.in_ll_stride + (k >> 1), t.in_flag, d, error, t.ll_limit);
-  out = ok ? make_uint4(d[0], d[1], d[2], d[3]) : make_uint4(0, 0, 0, 0);
-  return ok;
-}
+// Chunks of 8 activations a consumer thread stages per row: chunk ctid + j x 256 for
+// j < MC (the kernel's bound, at most kStageChunks), so K <= MC x 2048.
+constexpr int kStageChunks = 4;
+constexpr int kStageMaxK = kStageChunks * kRingConsumers * 32 * 8;
 
+// Consumers: the task's activation rows into `act` ([NB][K] BF16, fragment order), RMSNorm
+// applied when the task has a norm weight (modeling_yue2.py:131-132). Flagged input is
+// polled in passes: every pass issues the loads of all of this thread's chunks of every row
+// (before checking any, so the wait costs one round trip once the words are written), then
+// stores them raw to `act` and checks their flags; the pass that sees every flag holds the
+// data. RMSNorm then reduces the sum of squares of that pass and rescales `act` in place.
 // `error` (flagged input only): the device error word — an expired wait records code 64
 // there and returns false on every consumer thread (the staged rows are then meaningless).
-template <int NB>
+// `keep` (optional): the raw input chunks of columns [keep_lo, keep_hi) (multiples of 8,
+// at most kResKeepCols apart) are also stored there, row b at keep + b * kResKeepCols / 8:
+// the residual a later epilogue of this CTA adds. K <= MC x 2048.
+template <int NB, int MC = kStageChunks>
 __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int ctid, const uint4 (*wn_pre)[4] = nullptr,
-                               int *error = nullptr) {
+                               int *error = nullptr, uint4 *keep = nullptr, int keep_lo = 0, int keep_hi = 0) {
+  static_assert(MC >= 1 && MC <= kStageChunks, "chunks per thread");
   constexpr int T = kRingConsumers * 32;
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K;
+  float ss[NB];
   bool ok = true;
-  auto load = [&](int b, int k) -> uint4 {
-    if (!t.in_ll) return __ldcg(reinterpret_cast<const uint4 *>(t.in + size_t(b) * t.in_stride + k));
-    uint4 v;
-    if (!ll_chunk(t, b, k, v, error)) ok = false;
-    return v;
-  };
+  for (long long it = 0;; ++it) {
+    uint4 v[NB][MC];
+    uint32_t flags_ok = 1u;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int j = 0; j < MC; ++j) {
+        const int k = (ctid + j * T) * 8;
+        if (k >= K) continue;
+        if (t.in_ll) {
+          const uint2 *p = t.in_ll + size_t(b) * t.in_ll_stride + (k >> 1);
+          const uint4 a = ll_load2(p), c = ll_load2(p + 2);
+          v[b][j] = make_uint4(a.x, a.z, c.x, c.z);
+          flags_ok &= uint32_t(a.y == t.in_flag) & uint32_t(a.w == t.in_flag) & uint32_t(c.y == t.in_flag) &
+                      uint32_t(c.w == t.in_flag);
+        } else {
+          v[b][j] = __ldcg(reinterpret_cast<const uint4 *>(t.in + size_t(b) * t.in_stride + k));
+        }
+      }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      ss[b] = 0.f;
+#pragma unroll
+      for (int j = 0; j < MC; ++j) {
+        const int k = (ctid + j * T) * 8;
+        if (k >= K) continue;
+        act_store_chunk(act + b * K, k, v[b][j]);
+        if (keep && k >= keep_lo && k < keep_hi) keep[b * (kResKeepCols / 8) + ((k - keep_lo) >> 3)] = v[b][j];
+        if (t.norm_w) {
+          const uint32_t w4[4] = {v[b][j].x, v[b][j].y, v[b][j].z, v[b][j].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a = bf_lo(w4[q]), c = bf_hi(w4[q]);
+            ss[b] += a * a + c * c;
+          }
+        }
+      }
+    }
+    if (!t.in_ll || flags_ok) break;
+    if (it >= t.ll_limit || ((it & 255) == 255 && error && ll_error_word(error) != 0)) {
+      ok = false;
+      break;
+    }
+    if (it >= 8) __nanosleep(32);
+  }
   if (t.norm_w) {
     uint4 wn[4];
     if (wn_pre) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) wn[j] = (*wn_pre)[j];
     } else {
-      ring_norm_w_load(t, wn, ctid);  // with x below: one round trip
+      ring_norm_w_load(t, wn, ctid);
     }
-    uint4 xv[NB][4];
+#pragma unroll
     for (int b = 0; b < NB; ++b) {
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int k = (ctid + j * T) * 8;
-        if (k < K) {
-          xv[b][j] = load(b, k);
-          const uint32_t w4[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float a = bf_lo(w4[q]), c = bf_hi(w4[q]);
-            ss += a * a + c * c;
-          }
-        }
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) red[b * kRingConsumers + warp] = ss;
+      const float s = warp_sum(ss[b]);
+      if (lane == 0) red[b * kRingConsumers + warp] = s;
     }
     consumer_sync();
     for (int b = 0; b < NB; ++b) {
@@ -311,10 +375,11 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
       for (int i = 0; i < kRingConsumers; ++i) tot += red[b * kRingConsumers + i];
       const float scale = rms_scale_bf16(tot, K, t.eps);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < MC; ++j) {
         const int k = (ctid + j * T) * 8;
         if (k >= K) continue;
-        const uint32_t xq[4] = {xv[b][j].x, xv[b][j].y, xv[b][j].z, xv[b][j].w};
+        const uint4 x = act_load_chunk(act + b * K, k);  // this thread's own raw chunk
+        const uint32_t xq[4] = {x.x, x.y, x.z, x.w};
         const uint32_t wq[4] = {wn[j].x, wn[j].y, wn[j].z, wn[j].w};
         uint32_t o[4];
 #pragma unroll
@@ -326,9 +391,6 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
         act_store_chunk(act + b * K, k, make_uint4(o[0], o[1], o[2], o[3]));
       }
     }
-  } else {
-    for (int b = 0; b < NB; ++b)
-      for (int c = ctid; c < K / 8; c += T) act_store_chunk(act + b * K, c * 8, load(b, c * 8));
   }
   if (!t.in_ll) {
     consumer_sync();
@@ -365,9 +427,10 @@ constexpr int kRingMaxGroups = 8;  // 8-row groups whose partial sums wait for o
 __host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGroups * kRingConsumers * NB * 8; }
 
 // Consumers: consume the task's stages (continuing `it`) and apply the epilogue. Each
-// stage is 8 weight rows x 2048; warp w owns the k range [256w, 256w+256) of every stage
-// and runs tensor-core MMAs with the 8 weight rows as the B operand (n = 8, read by
-// ldmatrix straight from the ring) and the activation rows as rows 0..NB-1 of A,
+// stage is 8 weight rows x 2048 (swizzled, see the top of this file); warp w owns the k
+// range [256w, 256w+256) of every stage and runs tensor-core MMAs with the 8 weight rows
+// as the B operand (n = 8, read by ldmatrix straight from the ring) and the activation rows
+// as rows 0..NB-1 of A,
 // accumulating in FP32 across the stages of a group. Warps park their per-group partial
 // sums in `gred`; one barrier per up to kRingMaxGroups groups, then the 8 partials of
 // each output are added in warp order and the epilogue is applied. After a failure
@@ -381,32 +444,35 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
   static_assert(NB >= 1 && NB <= 8, "activation rows must fit the MMA's first 8 rows");
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K, KS = K / kRingPiece;
   const int grow = lane >> 2, gcol = (lane & 3) * 2;  // fragment row / column pair of this lane
-  // ldmatrix x4 addresses: matrices (k, k+8, k+16, k+24) of rows 0..7.
-  const int lrow = lane & 7, lk = (lane >> 3) * 8;
+  // ldmatrix x4 addresses: lane l gives row l & 7 of matrix l >> 3, the 16-byte chunk
+  // k0 / 8 + (l >> 3) of the stage (matrices k, k+8, k+16, k+24 of rows 0..7).
+  const int lrow = lane & 7, lmat = lane >> 3;
+  // Ring position of `it`, kept incrementally.
+  int s = int(it % NS);
+  unsigned phase = unsigned(it / NS) & 1u;
   for (int gb = g0; gb < g1; gb += kRingMaxGroups) {
     const int ge = min(g1, gb + kRingMaxGroups);
     for (int g = gb; g < ge; ++g) {
       // Two independent accumulator chains (even / odd k-tile pairs) halve the MMAs that
       // serialize on one accumulator; they are added at the end.
       float c2[2][4] = {};
-      for (int ks = 0; ks < KS; ++ks, ++it) {
-        const int s = int(it % NS);
+      for (int ks = 0; ks < KS; ++ks) {
         bool landed = false;
         if (!dead) {
-          landed = mbar_wait(&full[s], unsigned(it / NS) & 1u);
+          landed = mbar_wait(&full[s], phase);
           if (!landed) {
             if (lane == 0) atomicOr(error, 8);
             dead = bad = true;
           }
         }
         if (!bad) {
-          const bf16 *wst = ring + size_t(s) * 8 * kRingRowPitch;
+          const bf16 *wst = ring + size_t(s) * kRingStageElems;
           const bf16 *ar = act + size_t(ks) * kRingPiece;
 #pragma unroll
           for (int kt = 0; kt < 16; kt += 2) {
             const int k0 = warp * 256 + kt * 16;  // two k-tiles of 16: [k0, k0 + 32)
             uint32_t b0, b1, b2, b3;
-            ldsm_x4(b0, b1, b2, b3, wst + lrow * kRingRowPitch + k0 + lk);
+            ldsm_x4(b0, b1, b2, b3, wst + stage_chunk((k0 >> 3) + lmat, lrow));
             uint4 a4 = make_uint4(0, 0, 0, 0);  // (a0, a2) of k-tile kt, then of kt + 1
             if (grow < NB) a4 = *reinterpret_cast<const uint4 *>(ar + size_t(grow) * K + k0 + gcol * 4);
             const uint32_t a0 = a4.x, a2 = a4.y, a0n = a4.z, a2n = a4.w;
@@ -416,6 +482,11 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
         }
         __syncwarp();
         if (lane == 0 && landed) mbar_arrive(&empty[s]);
+        ++it;
+        if (++s == NS) {
+          s = 0;
+          phase ^= 1u;
+        }
       }
       float c[4];
 #pragma unroll
@@ -469,7 +540,9 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
         bf16 lo, hi;
         if (t.epi == kEpiResidual) {
           uint32_t old = 0;
-          if (!ll_wait1(o, t.res_flag, old, error, t.ll_limit)) {
+          if (t.res_smem) {
+            old = t.res_smem[b * (kResKeepCols / 2) + ((col - t.res_lo) >> 1)];
+          } else if (!ll_wait1(o, t.res_flag, old, error, t.ll_limit)) {
             atomicOr(error, 64);
             continue;
           }
