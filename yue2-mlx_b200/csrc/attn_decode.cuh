@@ -102,6 +102,11 @@ struct DecodeAttnParams {
   int out_ll_stride = 0;
   uint32_t out_flag = 0;
   long long ll_limit = 1ll << 22;  // polls of a flagged wait before it gives up
+  // Split partials as flagged words (FP32 value + flag), [rows][heads][max_splits][D + 2]
+  // (m, l, o[D]), merged by a dedicated merge job (attn_merge_ll) instead of the last
+  // split to arrive; null: plain partials in `part` and arrival counters.
+  uint2 *part_ll = nullptr;
+  uint32_t part_flag = 0;
 };
 
 constexpr int kKvChunk = 64;  // positions per KV chunk
@@ -232,23 +237,23 @@ __device__ __forceinline__ bool ll_wait_lane_words(const uint2 *words, int a, in
                                                    uint32_t (&da)[N], uint32_t (&db)[N], const int *error,
                                                    long long limit) {
   for (long long it = 0;; ++it) {
-    bool ok = true;
+    // Every load of the pass is issued before any flag is compared.
+    uint2 wa[N], wb[N];
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      const uint2 w = ll_load1(words + ((a + 32 * i) >> 1));
-      da[i] = w.x;
-      ok = ok && w.y == flag;
-    }
+    for (int i = 0; i < N; ++i) wa[i] = ll_load1(words + ((a + 32 * i) >> 1));
     if (b >= 0) {
 #pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const uint2 w = ll_load1(words + ((b + 32 * i) >> 1));
-        db[i] = w.x;
-        ok = ok && w.y == flag;
-      }
+      for (int i = 0; i < N; ++i) wb[i] = ll_load1(words + ((b + 32 * i) >> 1));
     } else {
 #pragma unroll
-      for (int i = 0; i < N; ++i) db[i] = 0u;
+      for (int i = 0; i < N; ++i) wb[i] = make_uint2(0u, flag);
+    }
+    uint32_t ok = 1u;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      da[i] = wa[i].x;
+      db[i] = wb[i].x;
+      ok &= uint32_t(wa[i].y == flag) & uint32_t(wb[i].y == flag);
     }
     if (ok) return true;
     if (it >= limit) return false;
@@ -492,14 +497,56 @@ __device__ __forceinline__ AttnAcc<D> attn_combine(AttnTeamSmem<D, G> &sm, const
   return r;
 }
 
+constexpr int kMergeBatch = 16;  // splits whose partials one merge round trip reads
+
+// Fold a batch of split partials (m, l, o; m = -inf: absent) into the running (M, L, O) of
+// one output, in split order: rescale the running state to the batch's max, then add each
+// split's exp-weighted l and o. Every merge path uses this, so their bits agree.
+template <int MB>
+__device__ __forceinline__ void merge_fold(float &M, float &Ls, float &O, const float (&mv)[MB], const float (&lv)[MB],
+                                           const float (&ov)[MB]) {
+  float Mb = M;
+#pragma unroll
+  for (int j = 0; j < MB; ++j) Mb = fmaxf(Mb, mv[j]);
+  if (Mb == -INFINITY) return;
+  const float r = M == -INFINITY ? 0.f : expf(M - Mb);
+  Ls *= r;
+  O *= r;
+#pragma unroll
+  for (int j = 0; j < MB; ++j) {
+    if (mv[j] == -INFINITY) continue;
+    const float c = expf(mv[j] - Mb);
+    Ls += lv[j] * c;
+    O += ov[j] * c;
+  }
+  M = Mb;
+}
+
+// Store the BF16 output v of head (kvh * G + hd), dim d of `row` (thread t < G x D owns
+// t = hd * D + d; whole warps take part: adjacent dims pair up in one flagged word).
+template <int D, int G>
+__device__ __forceinline__ void attn_out_store(const DecodeAttnParams &p, int row, int kvh, int hd, int d, bf16 v) {
+  if (p.out_ll) {
+    const bf16 v1 =
+        __ushort_as_bfloat16((unsigned short)__shfl_down_sync(0xFFFFFFFFu, (unsigned)__bfloat16_as_ushort(v), 1));
+    if ((d & 1) == 0)
+      ll_store_all(p.out_ll + size_t(row) * p.out_ll_stride + (((kvh * G + hd) * D + d) >> 1), pack_bf16x2(v, v1),
+                   p.out_flag, p.out_ndst, p.out_dst);
+  } else {
+    bf16 *o = p.out + size_t(row) * p.out_stride + (kvh * G + hd) * D + d;
+    *o = v;
+    for (int i = 0; i < p.out_ndst; ++i) *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(o) + p.out_dst[i]) = v;
+  }
+}
+
 // Merge the n_active split partials of the G heads of (row, kv_head) into the BF16 head
 // outputs. Thread t < G x D owns output t (head t / D, dim t % D) and reads that dim plus
-// (m, l) of up to 16 splits in one round trip; batches fold into the running (M, L, O)
-// with exp rescaling, in split order. The merging unit resets the arrival counter.
+// (m, l) of up to kMergeBatch splits in one round trip; batches fold into the running
+// (M, L, O) in split order (merge_fold). The merging unit resets the arrival counter.
 template <int D, int G>
 __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, int kvh, int row, int n_active,
                            int tid) {
-  constexpr int MB = 16;
+  constexpr int MB = kMergeBatch;
   if (tid < G * D) {
     const int hd = tid / D, d = tid % D;
     const float *pr0 = part_base + size_t(kvh * G + hd) * p.max_splits * (D + 2);
@@ -509,6 +556,7 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
 #pragma unroll
       for (int j = 0; j < MB; ++j) {
         mv[j] = -INFINITY;
+        lv[j] = ov[j] = 0.f;
         if (s0 + j < n_active) {
           const float *pr = pr0 + size_t(s0 + j) * (D + 2);
           mv[j] = __ldcg(pr);
@@ -516,37 +564,97 @@ __device__ void attn_merge(const DecodeAttnParams &p, const float *part_base, in
           ov[j] = __ldcg(pr + 2 + d);
         }
       }
-      float Mb = M;
-#pragma unroll
-      for (int j = 0; j < MB; ++j) Mb = fmaxf(Mb, mv[j]);
-      if (Mb == -INFINITY) continue;
-      const float r = M == -INFINITY ? 0.f : expf(M - Mb);
-      Ls *= r;
-      O *= r;
-#pragma unroll
-      for (int j = 0; j < MB; ++j) {
-        if (mv[j] == -INFINITY) continue;
-        const float c = expf(mv[j] - Mb);
-        Ls += lv[j] * c;
-        O += ov[j] * c;
-      }
-      M = Mb;
+      merge_fold<MB>(M, Ls, O, mv, lv, ov);
     }
-    const bf16 v = f2bf(O * (1.0f / Ls));
-    if (p.out_ll) {
-      // Adjacent dims pair up in one flagged word (even lane stores; tid < G x D is whole warps).
-      const bf16 v1 = __ushort_as_bfloat16(
-          (unsigned short)__shfl_down_sync(0xFFFFFFFFu, (unsigned)__bfloat16_as_ushort(v), 1));
-      if ((d & 1) == 0)
-        ll_store_all(p.out_ll + size_t(row) * p.out_ll_stride + (((kvh * G + hd) * D + d) >> 1), pack_bf16x2(v, v1),
-                     p.out_flag, p.out_ndst, p.out_dst);
-    } else {
-      bf16 *o = p.out + size_t(row) * p.out_stride + (kvh * G + hd) * D + d;
-      *o = v;
-      for (int i = 0; i < p.out_ndst; ++i) *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(o) + p.out_dst[i]) = v;
-    }
+    attn_out_store<D, G>(p, row, kvh, hd, d, f2bf(O * (1.0f / Ls)));
   }
   if (tid == 0) p.count[row * p.g.kv_heads + kvh] = 0;
+}
+
+// Flagged partials (p.part_ll): this unit's combined state as words of its split's slot.
+template <int D, int G>
+__device__ __forceinline__ void attn_partial_ll(const DecodeAttnParams &p, const AttnAcc<D> &acc, int row, int kvh,
+                                                int split, int tid) {
+  if (tid < G * D) {
+    const int hd = tid / D, d = tid % D;
+    uint2 *pr = p.part_ll + ((size_t(row) * p.g.heads + kvh * G + hd) * p.max_splits + split) * (D + 2);
+    ll_store(pr + 2 + d, __float_as_uint(acc.o), p.part_flag);
+    if (d == 0) {
+      ll_store(pr, __float_as_uint(acc.m), p.part_flag);
+      ll_store(pr + 1, __float_as_uint(acc.l), p.part_flag);
+    }
+  }
+}
+
+// A row whose context is one split: its unit's state is the head output (the merge of a
+// single partial computes the same bits: exp(0) = 1).
+template <int D, int G>
+__device__ __forceinline__ void attn_single_out(const DecodeAttnParams &p, const AttnAcc<D> &acc, int row, int kvh,
+                                                int tid) {
+  if (tid < G * D) {
+    float M = -INFINITY, Ls = 0.f, O = 0.f;
+    const float mv[1] = {acc.m}, lv[1] = {acc.l}, ov[1] = {acc.o};
+    merge_fold<1>(M, Ls, O, mv, lv, ov);
+    attn_out_store<D, G>(p, row, kvh, tid / D, tid % D, f2bf(O * (1.0f / Ls)));
+  }
+}
+
+// Merge job of (row, kv_head) over flagged partials: every batch of kMergeBatch splits is
+// polled (bounded; each pass issues all its loads first, and a warp leaves the poll when
+// all its lanes' words carry p.part_flag), then folded as attn_merge does. Lane L loads
+// (m, l) of split s0 + L % kMergeBatch and every lane the o of its own dim for each split;
+// (m, l) reach the other lanes by shuffles. False (nothing stored, error 64 recorded)
+// when a wait gave up. `st` (tracing, optional): SM clocks when each of the first two
+// batches was complete (slots 3, 4) and when the outputs were stored (slot 5).
+template <int D, int G>
+__device__ bool attn_merge_ll(const DecodeAttnParams &p, int row, int kvh, int n_splits, int tid,
+                              unsigned long long *st = nullptr) {
+  constexpr int MB = kMergeBatch;
+  static_assert(MB <= 32 && G * D % 32 == 0, "one (m, l) per lane; whole warps");
+  bool ok = true;
+  if (tid < G * D) {
+    const int hd = tid / D, d = tid % D, lane = tid & 31;
+    const uint2 *pr0 = p.part_ll + (size_t(row) * p.g.heads + kvh * G + hd) * p.max_splits * (D + 2);
+    float M = -INFINITY, Ls = 0.f, O = 0.f;
+    for (int s0 = 0; s0 < n_splits && ok; s0 += MB) {
+      uint2 wm, wl, wo[MB];
+      for (long long it = 0;; ++it) {
+        const uint2 *prm = pr0 + size_t(min(s0 + lane % MB, n_splits - 1)) * (D + 2);  // past the end: a repeat
+        wm = ll_load1(prm);
+        wl = ll_load1(prm + 1);
+#pragma unroll
+        for (int j = 0; j < MB; ++j) wo[j] = ll_load1(pr0 + size_t(min(s0 + j, n_splits - 1)) * (D + 2) + 2 + d);
+        uint32_t mine = uint32_t(wm.y == p.part_flag) & uint32_t(wl.y == p.part_flag);
+#pragma unroll
+        for (int j = 0; j < MB; ++j) mine &= uint32_t(wo[j].y == p.part_flag);
+        if (__all_sync(0xFFFFFFFFu, mine != 0u)) break;
+        if (it >= p.ll_limit ||
+            ((it & 255) == 255 && p.error && __any_sync(0xFFFFFFFFu, ll_error_word(p.error) != 0))) {
+          ok = false;
+          break;
+        }
+        if (it >= 8) __nanosleep(32);
+      }
+      if (s0 < 2 * MB) attn_stamp(st, 3 + s0 / MB, tid);
+      if (!ok) break;
+      float mv[MB], lv[MB], ov[MB];
+#pragma unroll
+      for (int j = 0; j < MB; ++j) {
+        const bool in = s0 + j < n_splits;
+        const float m = __shfl_sync(0xFFFFFFFFu, __uint_as_float(wm.x), j);
+        const float l = __shfl_sync(0xFFFFFFFFu, __uint_as_float(wl.x), j);
+        mv[j] = in ? m : -INFINITY;
+        lv[j] = in ? l : 0.f;
+        ov[j] = in ? __uint_as_float(wo[j].x) : 0.f;
+      }
+      merge_fold<MB>(M, Ls, O, mv, lv, ov);
+    }
+    // The pairing store needs the whole warp (ok is warp-uniform here).
+    if (ok) attn_out_store<D, G>(p, row, kvh, hd, d, f2bf(O * (1.0f / Ls)));
+    attn_stamp(st, 5, tid);
+  }
+  if (!ok && tid % 32 == 0 && p.error) atomicOr(p.error, 64);
+  return ok;
 }
 
 // Flagged output of an inactive row: the G heads of kv head `kvh` as zero words with the

@@ -86,7 +86,8 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
       // Flagged words: 8 bytes per two values, for the persistent kernel's 1 or 2 rows.
       const size_t llr = size_t(std::min(max_rows, 2));
       const size_t oxl = take(llr * d.hidden * 4), oql = take(llr * d.qkv_rows() * 4), oal = take(llr * f.qdim() * 4),
-                   oml = take(llr * f.ffn * 4);
+                   oml = take(llr * f.ffn * 4),
+                   opl = take(llr * d.heads * kSessionMaxSplits * (d.head_dim + 2) * sizeof(uint2));
       s->xregion = dmalloc<char>(off);
       s->xregion_bytes = off;
       YAR_CUDA(cudaMemset(s->xregion, 0, off));
@@ -99,9 +100,10 @@ Session *create_session(Model *m, int max_rows, int max_ctx, int page_tokens) {
       s->qkv_ll = reinterpret_cast<uint2 *>(s->xregion + oql);
       s->attn_ll = reinterpret_cast<uint2 *>(s->xregion + oal);
       s->mlp_ll = reinterpret_cast<uint2 *>(s->xregion + oml);
+      s->part_ll = reinterpret_cast<uint2 *>(s->xregion + opl);
       s->ll_bytes = off - oxl;
     }
-    s->max_splits = 32;
+    s->max_splits = kSessionMaxSplits;
     s->attn_part = dmalloc<float>(size_t(max_rows) * d.heads * s->max_splits * (d.head_dim + 2));
     s->attn_count = dmalloc<int>(size_t(max_rows) * d.kv_heads);
     YAR_CUDA(cudaMemset(s->attn_count, 0, size_t(max_rows) * d.kv_heads * sizeof(int)));

@@ -49,6 +49,9 @@ struct LayerWeights {
   const bf16 *ln1, *ln2, *qn, *kn;
 };
 
+// Splits per (row, kv head) the decode attention's partial buffers hold.
+constexpr int kSessionMaxSplits = 32;
+
 struct Model {
   Dims d;
   int device = 0, sm_count = 148;
@@ -205,7 +208,7 @@ struct Session {
   // Split-KV attention scratch.
   float *attn_part = nullptr;  // [max_rows][heads][max_splits][head_dim + 2]
   int *attn_count = nullptr;   // [max_rows][kv_heads]
-  int max_splits = 0;
+  int max_splits = 0;  // kSessionMaxSplits
   // Prefill activations (prefill_chunk rows).
   bf16 *px = nullptr, *ph = nullptr, *pqkv = nullptr, *pq = nullptr, *pattn = nullptr, *pmlp = nullptr;
   int *pids = nullptr;
@@ -250,6 +253,9 @@ struct Session {
   // Flagged-word activations of the persistent kernel (in the exchange region; rows up to
   // 2): residual rows, raw q/k/v, attention heads, FFN activations; ll_bytes in all.
   uint2 *x_ll = nullptr, *qkv_ll = nullptr, *attn_ll = nullptr, *mlp_ll = nullptr;
+  // The decode attention's split partials as flagged words ([rows][heads][max_splits]
+  // [head_dim + 2]; rank-local, after the exchanged buffers in the same region).
+  uint2 *part_ll = nullptr;
   size_t ll_bytes = 0;
   bool tp_mapped = false;
   long long tp_dst[7] = {};

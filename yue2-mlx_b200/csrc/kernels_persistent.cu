@@ -654,6 +654,14 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     srows.pos[b] = rowst[b].pos;
   }
   const int U = step_units(srows, kvh_n, nsplit), arank = p.attn_rank[blockIdx.x];
+  // Merge jobs of this step: rows that are active and split their context.
+  bool merge_row[NB];
+  int merge_splits[NB], n_merges = 0;
+  for (int b = 0; b < NB; ++b) {
+    merge_splits[b] = srows.active[b] ? split_plan(srows.pos[b] + 1, nsplit).n_splits : 1;
+    merge_row[b] = srows.active[b] && merge_splits[b] > 1;
+    if (merge_row[b]) n_merges += kvh_n;
+  }
 
   // One GEMV operation: stage the flagged input rows (the wait for the producing
   // operation), consume this CTA's stages, write its flagged outputs.
@@ -715,6 +723,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
       ap.out_ll = p.attn_ll + (ap.out - p.attn) / 2;  // this rank's heads within the whole width
       ap.out_ll_stride = p.attn_lls;
       ap.out_flag = fl(c_op(l, 1));
+      ap.part_flag = ap.out_flag;  // another buffer: the same step and operation
       ap.ll_limit = p.ll_limit;
       if (p.inject_op == c_op(l, 1)) ap.qkv_flag ^= 0x80000000u;
       long long itk = it;
@@ -760,7 +769,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
         attn_stamp(st, 4, ctid);
         if (ui.active && !bad) {
           const AttnAcc<128> acc = attn_combine<128, 2>(*team_sm, wacc, ctid, 1);
-          attn_finish<128, 2>(ap, *team_sm, acc, ui.row, ui.kvh, ui.split, ui.n_splits, ctid, 1);
+          if (ui.n_splits == 1)
+            attn_single_out<128, 2>(ap, acc, ui.row, ui.kvh, ctid);
+          else
+            attn_partial_ll<128, 2>(ap, acc, ui.row, ui.kvh, ui.split, ctid);
         } else if (!ui.active && ui.split == 0) {
           attn_write_inactive<128, 2>(ap, ui.row, ui.kvh, ctid);  // an inactive row's heads: zero words
         }
@@ -768,6 +780,25 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
         itk += nch;
       }
       it = itk;
+      // Merge jobs: one per (active row with more than one split, kv head), on the CTAs of
+      // attention ranks U, U + 1, ... (those without units while the grid has room): each
+      // polls its splits' flagged partials and writes the head outputs. No split waits for
+      // another, and no arrival counter is taken.
+      if (!bad) {
+        const int G = int(gridDim.x);
+        for (int j = ((arank - U) % G + G) % G; j < n_merges; j += G) {
+          int b = 0, jj = j;
+          for (; b < NB; ++b) {
+            if (!merge_row[b]) continue;
+            if (jj < kvh_n) break;
+            jj -= kvh_n;
+          }
+          if (b == NB) break;
+          unsigned long long *st = (trace && arank >= U && j < G) ? trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8
+                                                                : nullptr;  // a CTA without units: free slots
+          if (!attn_merge_ll<128, 2>(ap, b, jj, merge_splits[b], ctid, st)) bad = true;
+        }
+      }
     }
     stamp(5 * l + 1, 2);
     // O (+ residual).
@@ -956,6 +987,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   a.cos_tab = m.rope_cos;
   a.sin_tab = m.rope_sin;
   a.part = s.attn_part;
+  a.part_ll = s.part_ll;
   a.count = s.attn_count;
   a.out = s.attn + m.tp.q_row0;
   a.out_stride = m.full.qdim();

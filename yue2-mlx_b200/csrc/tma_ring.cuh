@@ -106,13 +106,15 @@ template <int NQ>
 __device__ __forceinline__ bool ll_wait(const uint2 *p, uint32_t flag, uint32_t (&data)[2 * NQ], const int *error,
                                         long long limit = kLlWaitLimit) {
   for (long long i = 0;; ++i) {
-    bool ok = true;
+    uint4 v[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) v[q] = ll_load2(p + 2 * q);  // every load issued before any check
+    uint32_t ok = 1u;
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
-      const uint4 v = ll_load2(p + 2 * q);
-      data[2 * q] = v.x;
-      data[2 * q + 1] = v.z;
-      ok = ok && v.y == flag && v.w == flag;
+      data[2 * q] = v[q].x;
+      data[2 * q + 1] = v[q].z;
+      ok &= uint32_t(v[q].y == flag) & uint32_t(v[q].w == flag);
     }
     if (ok) return true;
     if (i >= limit) return false;
@@ -310,40 +312,54 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K;
   float ss[NB];
   bool ok = true;
-  for (long long it = 0;; ++it) {
-    uint4 v[NB][MC];
-    uint32_t flags_ok = 1u;
+  // Rows polled per pass: all of them while their chunks fit 4 per thread (the words in
+  // flight stay in registers), else one row after another (their words are written by the
+  // same epilogues, so the later rows cost about one more round trip).
+  constexpr int RP = NB * MC <= 4 ? NB : 1;
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
+  for (int b0 = 0; b0 < NB && ok; b0 += RP) {
+  for (long long it = 0;; ++it) {
+    // Every load of the pass is issued before any flag is compared (a comparison between
+    // two loads would make the second wait for the first's round trip); then each chunk is
+    // stored raw to `act` (and `keep`), and its squares are summed.
+    uint4 wa[RP][MC], wc[RP][MC];
+#pragma unroll
+    for (int r = 0; r < RP; ++r)
 #pragma unroll
       for (int j = 0; j < MC; ++j) {
-        const int k = (ctid + j * T) * 8;
+        const int b = b0 + r, k = (ctid + j * T) * 8;
         if (k >= K) continue;
         if (t.in_ll) {
           const uint2 *p = t.in_ll + size_t(b) * t.in_ll_stride + (k >> 1);
-          const uint4 a = ll_load2(p), c = ll_load2(p + 2);
-          v[b][j] = make_uint4(a.x, a.z, c.x, c.z);
-          flags_ok &= uint32_t(a.y == t.in_flag) & uint32_t(a.w == t.in_flag) & uint32_t(c.y == t.in_flag) &
-                      uint32_t(c.w == t.in_flag);
+          wa[r][j] = ll_load2(p);
+          wc[r][j] = ll_load2(p + 2);
         } else {
-          v[b][j] = __ldcg(reinterpret_cast<const uint4 *>(t.in + size_t(b) * t.in_stride + k));
+          const uint4 x = __ldcg(reinterpret_cast<const uint4 *>(t.in + size_t(b) * t.in_stride + k));
+          wa[r][j] = make_uint4(x.x, 0u, x.y, 0u);
+          wc[r][j] = make_uint4(x.z, 0u, x.w, 0u);
         }
       }
+    uint32_t flags_ok = 1u;
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
+    for (int r = 0; r < RP; ++r) {
+      const int b = b0 + r;
       ss[b] = 0.f;
 #pragma unroll
       for (int j = 0; j < MC; ++j) {
         const int k = (ctid + j * T) * 8;
         if (k >= K) continue;
-        act_store_chunk(act + b * K, k, v[b][j]);
-        if (keep && k >= keep_lo && k < keep_hi) keep[b * (kResKeepCols / 8) + ((k - keep_lo) >> 3)] = v[b][j];
+        const uint4 a = wa[r][j], c = wc[r][j];
+        flags_ok &= uint32_t(a.y == t.in_flag) & uint32_t(a.w == t.in_flag) & uint32_t(c.y == t.in_flag) &
+                    uint32_t(c.w == t.in_flag);
+        const uint4 x = make_uint4(a.x, a.z, c.x, c.z);
+        act_store_chunk(act + b * K, k, x);
+        if (keep && k >= keep_lo && k < keep_hi) keep[b * (kResKeepCols / 8) + ((k - keep_lo) >> 3)] = x;
         if (t.norm_w) {
-          const uint32_t w4[4] = {v[b][j].x, v[b][j].y, v[b][j].z, v[b][j].w};
+          const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const float a = bf_lo(w4[q]), c = bf_hi(w4[q]);
-            ss[b] += a * a + c * c;
+            const float lo = bf_lo(w4[q]), hi = bf_hi(w4[q]);
+            ss[b] += lo * lo + hi * hi;
           }
         }
       }
@@ -354,6 +370,7 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
       break;
     }
     if (it >= 8) __nanosleep(32);
+  }
   }
   if (t.norm_w) {
     uint4 wn[4];
