@@ -146,11 +146,12 @@ struct AttnRow {
 
 // Fill `rs` for `row` with `nthreads` threads starting at thread `tid`; the caller
 // synchronizes afterwards. Tables longer than kMaxPages stay in global memory.
+// `active` and `pos` as the caller computed them for this step.
 template <int D>
-__device__ void attn_row_load(AttnRow<D> &rs, const DecodeAttnParams &p, int row, int tid, int nthreads) {
-  const int pos = __ldcg(p.cur_pos + row);
+__device__ void attn_row_load_at(AttnRow<D> &rs, const DecodeAttnParams &p, int row, int active, int pos, int tid,
+                                 int nthreads) {
   if (tid == 0) {
-    rs.active = __ldcg(p.active + row);
+    rs.active = active;
     rs.pos = pos;
   }
   for (int i = tid; i < D / 2; i += nthreads) {
@@ -159,6 +160,11 @@ __device__ void attn_row_load(AttnRow<D> &rs, const DecodeAttnParams &p, int row
   }
   const int n = p.g.pages_per_row < AttnRow<D>::kMaxPages ? p.g.pages_per_row : AttnRow<D>::kMaxPages;
   for (int i = tid; i < n; i += nthreads) rs.ptab[i] = p.page_table[size_t(row) * p.g.pages_per_row + i];
+}
+// The row's activity and latched position from p.active / p.cur_pos.
+template <int D>
+__device__ void attn_row_load(AttnRow<D> &rs, const DecodeAttnParams &p, int row, int tid, int nthreads) {
+  attn_row_load_at<D>(rs, p, row, __ldcg(p.active + row), __ldcg(p.cur_pos + row), tid, nthreads);
 }
 
 template <int D>

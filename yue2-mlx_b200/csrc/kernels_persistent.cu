@@ -294,7 +294,7 @@ struct Producer {
   bf16 *pool;
   AttnGeom g;
   int max_splits;
-  const int *page_table, *ctr, *active, *cur_pos;
+  const int *page_table, *ctr, *active, *pos, *capacity;
   int *error;
   int nkv, arank;
   bool planned, failed;
@@ -303,28 +303,17 @@ struct Producer {
   __device__ Producer(const PersistParams &p, int ep, KvChunkRef *kv_smem)
       : layers(p.layers), wmaps(p.wmaps), head_map(&p.head_map), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F), HS(p.HS),
         FL(p.FL), nL(p.n_layers), epoch(ep), pool(p.ap.pool), g(p.ap.g), max_splits(p.ap.max_splits),
-        page_table(p.ap.page_table), ctr(p.ctr), active(p.active), cur_pos(p.cur_pos), error(p.error), nkv(0),
+        page_table(p.ap.page_table), ctr(p.ctr), active(p.active), pos(p.pos), capacity(p.capacity), error(p.error), nkv(0),
         arank(p.attn_rank[blockIdx.x]), planned(false), failed(false), kv(kv_smem) {}
 
-  // This CTA's KV chunks, once CTA 0 has latched the step's positions (bounded wait).
+  // This CTA's KV chunks. The step's rows are computed here as every CTA computes them
+  // (step_row): no CTA waits for another to latch them.
   __device__ bool plan() {
-    long long i = 0;
-    for (; i < kCounterWaitLimit; ++i) {
-      if (ld_acquire(ctr) >= epoch + 1) break;
-      if (ld_acquire(error) != 0) {
-        i = kCounterWaitLimit;
-        break;
-      }
-      __nanosleep(64);
-    }
-    if (i >= kCounterWaitLimit) {
-      atomicOr(error, 16);
-      return false;
-    }
     StepRows<NB> rows;
     for (int b = 0; b < NB; ++b) {
-      rows.active[b] = __ldcg(active + b);
-      rows.pos[b] = __ldcg(cur_pos + b);
+      const int a = __ldcg(active + b), q = __ldcg(pos + b);
+      rows.active[b] = a && q < __ldcg(capacity + b);
+      rows.pos[b] = q;
     }
     const int U = step_units(rows, g.kv_heads, max_splits);
     for (int u = arank; u < U; u += gridDim.x) {
@@ -452,6 +441,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   __shared__ float red[NB * kRingConsumers];
   __shared__ AttnRow<128> rowst[NB];
   __shared__ int s_epoch, s_bad, s_trace;
+  __shared__ int s_row[NB][4];  // this step's rows: active, position, token, active before the room check
   __shared__ KvChunkRef kv_chunks[kMaxCtaChunks];
   __shared__ uint4 s_keep[2][NB * kResKeepCols / 8];  // kept residual columns for O and down
   __shared__ long long s_dst[kMaxTpWorld - 1];
@@ -490,6 +480,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     t.ll_limit = p.ll_limit;
     const int op = 1 + 5 * l + (k == 0 ? 0 : k + 1);
     if (p.inject_op == op) t.in_flag ^= 0x80000000u;
+    if (l == 0 && k == 0 && p.inject_op != op) {
+      // The first QKV reads each row's token embedding itself (an inactive row: zeros).
+      t.in_ll = nullptr;
+      t.in_gather = true;
+      for (int b = 0; b < NB; ++b) t.in_row[b] = s_row[b][0] ? p.embed + size_t(s_row[b][2]) * H : nullptr;
+    }
     return t;
   };
   auto fl = [&](int op) { return ll_flag(epoch, op, nL); };
@@ -585,37 +581,38 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     bad = s_bad != 0;
   };
   const int kvh_n = p.ap.g.kv_heads, nsplit = p.ap.max_splits;
-  const int c_embed = 0, c_head = 1 + 5 * nL;
+  const int c_head = 1 + 5 * nL;  // counter 0 (the old position latch) is unused
   auto c_op = [&](int l, int k) { return 1 + 5 * l + k; };  // k: 0 qkv, 1 attn, 2 o, 3 gu, 4 down
 
-  // Embedding of each row's token (an inactive row: zeros) as flagged residual words, and
-  // the position latch (CTA 0).
-  if (blockIdx.x == 0) {
+  // The step's rows, computed alike by every CTA from what the sampler and the previous
+  // step left (no latch between CTAs): a row is active when the sampler left it active and
+  // it has room for one more position; it forwards position pos[b] and token token[b]. CTA
+  // 0 advances the positions at the step's end, when every CTA has read them (each CTA's
+  // layer-0 outputs, which CTA 0 waits for, come after its reads). CTA 0 also records the
+  // errors (a full row, a token out of range: token 0 is used) and writes each row's
+  // embedding as flagged residual words (an inactive row: zeros) for the readers that poll
+  // x after the embedding (the hidden-state record, residual epilogues without kept
+  // columns); the first QKV reads the embedding rows directly.
+  if (ctid == 0)
     for (int b = 0; b < NB; ++b) {
-      const bool act_row = __ldcg(p.active + b) != 0;
-      int tok = act_row ? __ldcg(p.token + b) : 0;
-      if (tok < 0 || tok >= p.vocab) {
-        if (ctid == 0) atomicOr(p.error, 1);
-        tok = 0;
-      }
-      const uint32_t *src = reinterpret_cast<const uint32_t *>(p.embed + size_t(tok) * H);
-      for (int c = ctid; c < H / 2; c += kRingConsumers * 32)
-        ll_store_all(p.x_ll + size_t(b) * p.x_lls + c, act_row ? __ldg(src + c) : 0u, fl(0), 0, nullptr);
+      const int a = __ldcg(p.active + b), q = __ldcg(p.pos + b);
+      const bool full = a && q >= __ldcg(p.capacity + b);
+      int tok = a && !full ? __ldcg(p.token + b) : 0;
+      const bool bad_tok = tok < 0 || tok >= p.vocab;
+      if (bad_tok) tok = 0;
+      s_row[b][0] = a && !full;
+      s_row[b][1] = q;
+      s_row[b][2] = tok;
+      s_row[b][3] = a;
+      if (blockIdx.x == 0 && (full || bad_tok)) atomicOr(p.error, full ? 2 : 1);
     }
-    if (ctid == 0)
-      for (int b = 0; b < NB; ++b) {
-        if (!__ldcg(p.active + b)) continue;
-        const int q = __ldcg(p.pos + b);
-        p.cur_pos[b] = q;
-        if (q >= __ldcg(p.capacity + b)) {
-          atomicOr(p.error, 2);
-          p.active[b] = 0;
-        } else {
-          p.pos[b] = q + 1;
-        }
-      }
-    signal(c_embed, false);
-  }
+  consumer_sync();
+  if (blockIdx.x == 0)
+    for (int b = 0; b < NB; ++b) {
+      const uint32_t *src = reinterpret_cast<const uint32_t *>(p.embed + size_t(s_row[b][2]) * H);
+      for (int c = ctid; c < H / 2; c += kRingConsumers * 32)
+        ll_store_all(p.x_ll + size_t(b) * p.x_lls + c, s_row[b][0] ? __ldg(src + c) : 0u, fl(0), 0, nullptr);
+    }
   // Trace calibration: globaltimer (ns) and the SM clock at the step's start and end.
   auto calib = [&](int o) {
     if (trace && ctid == 0) {
@@ -643,10 +640,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   unsigned long long *step_log =
       p.trace ? p.trace + size_t(gridDim.x) * (5 * nL + 1) * 8 + 16 + size_t(epoch & 63) * 4 : nullptr;
   if (step_log && blockIdx.x == 0 && ctid == 0) step_log[2] = globaltimer();
-  wait_for(c_embed, epoch + 1, false);
   dump_x(0);
   // This step's row state (activity, position, cos/sin, page table) for the attention units.
-  for (int b = 0; b < NB; ++b) attn_row_load<128>(rowst[b], p.ap, b, ctid, kRingConsumers * 32);
+  for (int b = 0; b < NB; ++b)
+    attn_row_load_at<128>(rowst[b], p.ap, b, s_row[b][0], s_row[b][1], ctid, kRingConsumers * 32);
   consumer_sync();
   StepRows<NB> srows;
   for (int b = 0; b < NB; ++b) {
@@ -856,6 +853,16 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   if (blockIdx.x == 0) {
     if (tp) wait_for(c_head, (epoch + 1) * all * W, true);
     if (ctid == 0) {
+      // The positions advance (a full row is deactivated instead); the host reads them after
+      // the step, and the next step's CTAs after this kernel.
+      for (int b = 0; b < NB; ++b) {
+        if (!s_row[b][3]) continue;
+        p.cur_pos[b] = s_row[b][1];
+        if (s_row[b][0])
+          p.pos[b] = s_row[b][1] + 1;
+        else
+          p.active[b] = 0;
+      }
       __threadfence();
       atomicExch(p.epoch, epoch + 1);
       if (step_log) step_log[3] = globaltimer();

@@ -59,6 +59,11 @@ struct GemvTask {
   // The stage map of W (encode_stage_map), for producers that copy through it
   // (ring_produce); a kernel-parameter or global-memory address.
   const CUtensorMap *wmap = nullptr;
+  // Gathered input (plain loads, when in_ll is null): row b read from in_row[b] (null:
+  // zeros) instead of in + b * in_stride; the persistent kernel's first QKV reads each
+  // row's token embedding this way.
+  bool in_gather = false;
+  const bf16 *in_row[2] = {nullptr, nullptr};
 };
 
 // Host: W's stage map ({64, N, K/64} view, {64, 8, 32} box, 128-byte swizzle) into `map`.
@@ -334,7 +339,8 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
           wa[r][j] = ll_load2(p);
           wc[r][j] = ll_load2(p + 2);
         } else {
-          const uint4 x = __ldcg(reinterpret_cast<const uint4 *>(t.in + size_t(b) * t.in_stride + k));
+          const bf16 *row = t.in_gather ? t.in_row[b] : t.in + size_t(b) * t.in_stride;
+          const uint4 x = row ? __ldcg(reinterpret_cast<const uint4 *>(row + k)) : make_uint4(0u, 0u, 0u, 0u);
           wa[r][j] = make_uint4(x.x, 0u, x.y, 0u);
           wc[r][j] = make_uint4(x.z, 0u, x.w, 0u);
         }
