@@ -480,6 +480,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     t.ll_limit = p.ll_limit;
     const int op = 1 + 5 * l + (k == 0 ? 0 : k + 1);
     if (p.inject_op == op) t.in_flag ^= 0x80000000u;
+    // O and down (no RMSNorm): each consumer warp stages its own k-range, so a warp starts
+    // as soon as its inputs (for O: its kv head's outputs) are written.
+    if (k == 1 || k == 3) t.stage_per_warp = true;
     if (l == 0 && k == 0 && p.inject_op != op) {
       // The first QKV reads each row's token embedding itself (an inactive row: zeros).
       t.in_ll = nullptr;
@@ -671,9 +674,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     int g0, g1;
     task_groups(t.N, blockIdx.x, gridDim.x, g0, g1, op_rotation(o, int(gridDim.x)));
     if (g0 == g1) return false;
-    if (!ring_stage_act<NB, kPersistMaxK / kRingPiece>(t, act, red, ctid, wn, p.error, keep, keep_lo, keep_hi)) bad = true;
+    if (!t.stage_per_warp &&
+        !ring_stage_act<NB, kPersistMaxK / kRingPiece>(t, act, red, ctid, wn, p.error, keep, keep_lo, keep_hi))
+      bad = true;
     stamp(op_slot, 1);
-    ring_consume<NB, NS>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, ctid);
+    ring_consume<NB, NS, kPersistMaxK / kRingPiece>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead,
+                                                    ctid);
     stamp(op_slot, 2);
     return true;
   };
@@ -825,7 +831,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     if ((g0 < g1 || extra_cta) && !ring_stage_act<NB, kPersistMaxK / kRingPiece>(head, act, red, ctid, nullptr, p.error))
       bad = true;
     stamp(5 * nL, 1);
-    ring_consume<NB, NS>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead, ctid);
+    ring_consume<NB, NS, kPersistMaxK / kRingPiece>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad,
+                                                    dead, ctid);
     stamp(5 * nL, 2);
     if (p.extra_row >= 0 && blockIdx.x == gridDim.x - 1 && warp < NB && !bad) {
       // The ABC phase's extra row (ABC_END), from the normalized activations in `act`.

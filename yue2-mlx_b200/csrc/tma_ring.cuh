@@ -64,6 +64,10 @@ struct GemvTask {
   // row's token embedding this way.
   bool in_gather = false;
   const bf16 *in_row[2] = {nullptr, nullptr};
+  // Per-warp staging (flagged input, no RMSNorm): ring_consume itself makes each consumer
+  // warp poll and stage only its own k-range of every row, so a warp starts as soon as its
+  // inputs are written (no staging barrier across the CTA); no ring_stage_act call.
+  bool stage_per_warp = false;
 };
 
 // Host: W's stage map ({64, N, K/64} view, {64, 8, 32} box, 128-byte swizzle) into `map`.
@@ -430,6 +434,63 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
   return all_ok != 0;
 }
 
+// Per-warp flagged staging (a task without RMSNorm): warp `warp` polls only its own
+// k-range of every row — chunk (ks, lane) = columns ks * 2048 + 256 warp + 8 lane, +8 for
+// ks < K / 2048 <= MC — issuing every load of a pass before comparing any, and stores it
+// to `act` in fragment order (ring_consume reads exactly this range). Rows are polled
+// together while their chunks fit 4 per lane, else one after another. The warp leaves a
+// poll together (its lanes vote); false when the wait gave up.
+template <int NB, int MC>
+__device__ bool ll_stage_warp(const GemvTask &t, bf16 *act, int lane, int warp, const int *error) {
+  constexpr int RP = NB * MC <= 4 ? NB : 1;
+  const int KS = t.K / kRingPiece;
+#pragma unroll
+  for (int b0 = 0; b0 < NB; b0 += RP) {
+    for (long long it = 0;; ++it) {
+      uint4 wa[RP][MC], wc[RP][MC];
+#pragma unroll
+      for (int r = 0; r < RP; ++r)
+#pragma unroll
+        for (int ks = 0; ks < MC; ++ks) {
+          if (ks >= KS) continue;
+          const int k = ks * kRingPiece + warp * 256 + lane * 8;
+          const uint2 *p = t.in_ll + size_t(b0 + r) * t.in_ll_stride + (k >> 1);
+          wa[r][ks] = ll_load2(p);
+          wc[r][ks] = ll_load2(p + 2);
+        }
+      uint32_t ok = 1u;
+#pragma unroll
+      for (int r = 0; r < RP; ++r)
+#pragma unroll
+        for (int ks = 0; ks < MC; ++ks) {
+          if (ks >= KS) continue;
+          const int k = ks * kRingPiece + warp * 256 + lane * 8;
+          const uint4 a = wa[r][ks], c = wc[r][ks];
+          ok &= uint32_t(a.y == t.in_flag) & uint32_t(a.w == t.in_flag) & uint32_t(c.y == t.in_flag) &
+                uint32_t(c.w == t.in_flag);
+          act_store_chunk(act + size_t(b0 + r) * t.K, k, make_uint4(a.x, a.z, c.x, c.z));
+        }
+      if (__all_sync(0xFFFFFFFFu, ok != 0u)) break;
+      if (it >= t.ll_limit ||
+          ((it & 255) == 255 && error && __any_sync(0xFFFFFFFFu, ll_error_word(error) != 0)))
+        return false;
+      if (it >= 8) __nanosleep(32);
+    }
+  }
+  return true;
+}
+
+// True on every consumer thread when `v` is true on any (barrier 1, the 256 consumers).
+__device__ __forceinline__ bool consumer_any(bool v) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(int(v)), "n"(kRingConsumers * 32)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -460,12 +521,19 @@ __host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGrou
 // elsewhere (`bad`) stages are still waited for and released and barriers still taken,
 // without computing; once a ring wait itself expired (`dead`: the producer is presumed
 // stuck, a copy may still be landing) no stage is waited for or released any more.
-template <int NB, int NS>
-__device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring, const bf16 *act, uint64_t *full,
+// A task with `stage_per_warp` is staged here, warp by warp (ll_stage_warp, K <= MC x 2048);
+// the batch barrier then also agrees on `bad`.
+template <int NB, int NS, int MC = kStageChunks>
+__device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring, bf16 *act, uint64_t *full,
                              uint64_t *empty, long long &it, float *gred, int *error, bool &bad, bool &dead,
                              int ctid) {
   static_assert(NB >= 1 && NB <= 8, "activation rows must fit the MMA's first 8 rows");
   const int lane = ctid & 31, warp = ctid >> 5, K = t.K, KS = K / kRingPiece;
+  if (t.stage_per_warp && !bad && !ll_stage_warp<NB, MC>(t, act, lane, warp, error)) {
+    if (lane == 0 && error) atomicOr(error, 64);
+    bad = true;
+  }
+  __syncwarp();
   const int grow = lane >> 2, gcol = (lane & 3) * 2;  // fragment row / column pair of this lane
   // ldmatrix x4 addresses: lane l gives row l & 7 of matrix l >> 3, the 16-byte chunk
   // k0 / 8 + (l >> 3) of the stage (matrices k, k+8, k+16, k+24 of rows 0..7).
@@ -522,7 +590,7 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
         dst[1] = c[1];
       }
     }
-    consumer_sync();
+    bad = consumer_any(bad);  // the batch barrier; a warp's own staging may have failed
     if (!bad && t.out_ll) {
       // Flagged epilogue: one thread per pair of adjacent outputs, one flagged word each.
       const bool swiglu = t.epi == kEpiSwiGLU;
