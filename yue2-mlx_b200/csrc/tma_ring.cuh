@@ -505,7 +505,7 @@ __device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a2, ui
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-constexpr int kRingMaxGroups = 8;  // 8-row groups whose partial sums wait for one epilogue
+constexpr int kRingMaxGroups = 12;  // 8-row groups whose partial sums wait for one epilogue (gate/up: 10-11 per CTA)
 
 // Bytes of the group-partials buffer ring_consume needs.
 __host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGroups * kRingConsumers * NB * 8; }
