@@ -610,8 +610,8 @@ __device__ __forceinline__ void attn_single_out(const DecodeAttnParams &p, const
 // all its lanes' words carry p.part_flag), then folded as attn_merge does. Lane L loads
 // (m, l) of split s0 + L % kMergeBatch and every lane the o of its own dim for each split;
 // (m, l) reach the other lanes by shuffles. False (nothing stored, error 64 recorded)
-// when a wait gave up. `st` (tracing, optional): SM clocks when each of the first two
-// batches was complete (slots 3, 4) and when the outputs were stored (slot 5).
+// when a wait gave up. `st` (tracing, optional): SM clocks when the first batch was
+// complete (slot 3), when all were folded (slot 4) and when the outputs were stored (slot 5).
 template <int D, int G>
 __device__ bool attn_merge_ll(const DecodeAttnParams &p, int row, int kvh, int n_splits, int tid,
                               unsigned long long *st = nullptr) {
@@ -641,20 +641,34 @@ __device__ bool attn_merge_ll(const DecodeAttnParams &p, int row, int kvh, int n
         }
         if (it >= 8) __nanosleep(32);
       }
-      if (s0 < 2 * MB) attn_stamp(st, 3 + s0 / MB, tid);
+      if (s0 == 0) attn_stamp(st, 3, tid);
       if (!ok) break;
-      float mv[MB], lv[MB], ov[MB];
+      // merge_fold's arithmetic with each split's weight computed once, on its lane, and
+      // shuffled (the same expf of the same operands, folded in the same order, so the
+      // bits equal merge_fold's): the batch max by a butterfly (max is exact in any order),
+      // the rescale of the running state, then split by split in order.
+      const int jl = lane % MB;
+      const float m_l = s0 + jl < n_splits ? __uint_as_float(wm.x) : -INFINITY;
+      float Mb = fmaxf(M, m_l);
 #pragma unroll
-      for (int j = 0; j < MB; ++j) {
-        const bool in = s0 + j < n_splits;
-        const float m = __shfl_sync(0xFFFFFFFFu, __uint_as_float(wm.x), j);
-        const float l = __shfl_sync(0xFFFFFFFFu, __uint_as_float(wl.x), j);
-        mv[j] = in ? m : -INFINITY;
-        lv[j] = in ? l : 0.f;
-        ov[j] = in ? __uint_as_float(wo[j].x) : 0.f;
+      for (int off = 1; off < MB; off <<= 1) Mb = fmaxf(Mb, __shfl_xor_sync(0xFFFFFFFFu, Mb, off));
+      if (Mb != -INFINITY) {
+        const float r = M == -INFINITY ? 0.f : expf(M - Mb);
+        Ls *= r;
+        O *= r;
+        const float c_l = m_l == -INFINITY ? -1.f : expf(m_l - Mb);  // -1: no split (skipped)
+        const float l_l = __uint_as_float(wl.x);
+#pragma unroll
+        for (int j = 0; j < MB; ++j) {
+          const float c = __shfl_sync(0xFFFFFFFFu, c_l, j), l = __shfl_sync(0xFFFFFFFFu, l_l, j);
+          if (c < 0.f) continue;
+          Ls += l * c;
+          O += __uint_as_float(wo[j].x) * c;
+        }
+        M = Mb;
       }
-      merge_fold<MB>(M, Ls, O, mv, lv, ov);
     }
+    attn_stamp(st, 4, tid);
     // The pairing store needs the whole warp (ok is warp-uniform here).
     if (ok) attn_out_store<D, G>(p, row, kvh, hd, d, f2bf(O * (1.0f / Ls)));
     attn_stamp(st, 5, tid);
