@@ -130,6 +130,7 @@ struct __align__(16) AttnTeamSmem {
   bf16 q_b[G][D];              // normed, roped q (BF16-exact values)
   bf16 knew[D], vnew[D];       // the new position's k (normed, roped) and v, as cached
   float wml[kAttnThreads / 32][G][2];  // per-warp (max, exp-sum) at the unit's end
+  float wc[kAttnThreads / 32][G];      // per-warp weight exp(m_w - M) in the combine (-1: no positions)
   float pvp[kAttnThreads / 32][G * D];  // per-warp unnormalized outputs at the unit's end
   int last_flag;
 };
@@ -480,6 +481,17 @@ __device__ __forceinline__ AttnAcc<D> attn_combine(AttnTeamSmem<D, G> &sm, const
     }
   }
   team_sync(bar_id);
+  // The weight exp(m_w - M) of warp w's state for head h, computed once (thread h x NW + w)
+  // instead of by each of the head's D threads.
+  if (tid < G * NW) {
+    const int h = tid / NW, w = tid % NW;
+    float M = -INFINITY;
+#pragma unroll
+    for (int v = 0; v < NW; ++v) M = fmaxf(M, sm.wml[v][h][0]);
+    const float mw = sm.wml[w][h][0];
+    sm.wc[w][h] = (M == -INFINITY || mw == -INFINITY) ? -1.f : expf(mw - M);
+  }
+  team_sync(bar_id);
   AttnAcc<D> r{-INFINITY, 0.f, 0.f};
   if (tid < G * D) {
     const int h = tid / D, d = tid % D;
@@ -490,9 +502,8 @@ __device__ __forceinline__ AttnAcc<D> attn_combine(AttnTeamSmem<D, G> &sm, const
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < NW; ++w) {
-        const float mw = sm.wml[w][h][0];
-        if (mw == -INFINITY) continue;
-        const float c = expf(mw - M);
+        const float c = sm.wc[w][h];
+        if (c < 0.f) continue;
         L += sm.wml[w][h][1] * c;
         O += wo[(w * G + h) * D + d] * c;
       }
