@@ -705,119 +705,126 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   uint4 wn_next[4];  // RMSNorm weight chunks of the next norm-prologue GEMV, loaded before its wait
   ring_norm_w_load(task(0, 0), wn_next, ctid);
   for (int l = 0; l < nL; ++l) {
-    // QKV (RMSNorm of x fused).
-    stamp(5 * l, 0);
-    const bool kept_o = gemv_op(task(l, 0), 5 * l, &wn_next, 0, s_keep[0], p.h0 + keep_lo[0], p.h0 + keep_hi[0]);
-    stamp(5 * l, 3);
-    // Attention: the CTA's units, one after another on all consumer warps; each unit waits
-    // for its own kv head's projections (flagged words) and streams its KV chunks as ring
-    // stages (every consumer warp releases each once).
-    float wv[4];
-    if (arank < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
-    stamp(5 * l + 1, 0);
-    {
-      DecodeAttnParams ap = p.ap;
-      ap.layer = l;
-      ap.out_ndst = p.tp_ndst;
-      ap.out_dst = s_dst;
-      ap.qkv_ll = p.qkv_ll;
-      ap.qkv_ll_stride = p.qkv_lls;
-      ap.qkv_flag = fl(c_op(l, 0));
-      ap.out_ll = p.attn_ll + (ap.out - p.attn) / 2;  // this rank's heads within the whole width
-      ap.out_ll_stride = p.attn_lls;
-      ap.out_flag = fl(c_op(l, 1));
-      ap.part_flag = ap.out_flag;  // another buffer: the same step and operation
-      ap.ll_limit = p.ll_limit;
-      if (p.inject_op == c_op(l, 1)) ap.qkv_flag ^= 0x80000000u;
-      long long itk = it;
-      for (int k = 0, u = arank; u < U; ++k, u += gridDim.x) {
-        const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
-        const int nch = ui.c1 - ui.c0;
-        unsigned long long *st =
-            (trace && k == 0) ? trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
-        const AttnRow<128> &rs = rowst[ui.row];
-        if (ui.active && !bad &&
-            !attn_qk<128, 2>(ap, *team_sm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ctid, 1))
-          bad = true;
-        attn_stamp(st, 3, ctid);
-        AttnWarpAcc<128, 2> wacc;
-        attn_warp_init(wacc);
-        // Each warp waits for, computes and releases its share of every chunk on its own; a
-        // failure is voted once per unit (the barrier below). After a failure elsewhere the
-        // chunks are still waited for and released; an expired ring wait stops both.
-        bool wbad = bad;
-        for (int j = 0; j < nch; ++j) {
-          const long long ij = itk + j;
-          const int sidx = int(ij % NS);
-          bool landed = false;
-          if (!dead) {
-            landed = mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
-            if (!landed) {
-              if (lane == 0) atomicOr(p.error, 8);
-              dead = wbad = true;
+    // The layer's five operations in one rolled loop: the four GEMVs share one instance of
+    // the GEMV code (the copies of an unrolled loop each ran cold once per launch, and the
+    // first layer paid for every one of them).
+    bool kept_o = false, kept_d = false;
+#pragma unroll 1
+    for (int k = 0; k < 5; ++k) {
+      stamp(5 * l + k, 0);
+      if (k == 1) {
+        // Attention: the CTA's units, one after another on all consumer warps; each unit waits
+        // for its own kv head's projections (flagged words) and streams its KV chunks as ring
+        // stages (every consumer warp releases each once).
+        float wv[4];
+        if (arank < U) attn_load_norm_w<128, 2>(p.layers[l].qn, p.layers[l].kn, wv, ctid);
+        stamp(5 * l + 1, 0);
+        {
+          DecodeAttnParams ap = p.ap;
+          ap.layer = l;
+          ap.out_ndst = p.tp_ndst;
+          ap.out_dst = s_dst;
+          ap.qkv_ll = p.qkv_ll;
+          ap.qkv_ll_stride = p.qkv_lls;
+          ap.qkv_flag = fl(c_op(l, 0));
+          ap.out_ll = p.attn_ll + (ap.out - p.attn) / 2;  // this rank's heads within the whole width
+          ap.out_ll_stride = p.attn_lls;
+          ap.out_flag = fl(c_op(l, 1));
+          ap.part_flag = ap.out_flag;  // another buffer: the same step and operation
+          ap.ll_limit = p.ll_limit;
+          if (p.inject_op == c_op(l, 1)) ap.qkv_flag ^= 0x80000000u;
+          long long itk = it;
+          for (int ku = 0, u = arank; u < U; ++ku, u += gridDim.x) {
+            const UnitInfo ui = step_unit(srows, kvh_n, nsplit, u);
+            const int nch = ui.c1 - ui.c0;
+            unsigned long long *st =
+                (trace && ku == 0) ? trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8 : nullptr;
+            const AttnRow<128> &rs = rowst[ui.row];
+            if (ui.active && !bad &&
+                !attn_qk<128, 2>(ap, *team_sm, rs, ui.row, ui.kvh, ui.split == ui.n_splits - 1, wv, ctid, 1))
+              bad = true;
+            attn_stamp(st, 3, ctid);
+            AttnWarpAcc<128, 2> wacc;
+            attn_warp_init(wacc);
+            // Each warp waits for, computes and releases its share of every chunk on its own; a
+            // failure is voted once per unit (the barrier below). After a failure elsewhere the
+            // chunks are still waited for and released; an expired ring wait stops both.
+            bool wbad = bad;
+            for (int j = 0; j < nch; ++j) {
+              const long long ij = itk + j;
+              const int sidx = int(ij % NS);
+              bool landed = false;
+              if (!dead) {
+                landed = mbar_wait(&full[sidx], unsigned(ij / NS) & 1u);
+                if (!landed) {
+                  if (lane == 0) atomicOr(p.error, 8);
+                  dead = wbad = true;
+                }
+              }
+              wbad = __any_sync(0xFFFFFFFFu, wbad);
+              if (j == 0) attn_stamp(st, 1, ctid);  // the unit's first chunk has landed
+              if (!wbad) {
+                const bf16 *ks = ring + size_t(sidx) * kRingStageElems;
+                const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
+                attn_chunk<128, 2>(team_sm->q_b, team_sm->knew, team_sm->vnew, ks, ks + kKvChunk * 128, n_main,
+                                   rs.pos - base < kKvChunk, ap.g.scale, wacc, ctid);
+              }
+              __syncwarp();
+              if (lane == 0 && landed) mbar_arrive(&empty[sidx]);
+            }
+            if (team_any(1, wbad)) bad = true;
+            attn_stamp(st, 4, ctid);
+            if (ui.active && !bad) {
+              const AttnAcc<128> acc = attn_combine<128, 2>(*team_sm, wacc, ctid, 1);
+              if (ui.n_splits == 1)
+                attn_single_out<128, 2>(ap, acc, ui.row, ui.kvh, ctid);
+              else
+                attn_partial_ll<128, 2>(ap, acc, ui.row, ui.kvh, ui.split, ctid);
+            } else if (!ui.active && ui.split == 0) {
+              attn_write_inactive<128, 2>(ap, ui.row, ui.kvh, ctid);  // an inactive row's heads: zero words
+            }
+            attn_stamp(st, 5, ctid);
+            itk += nch;
+          }
+          it = itk;
+          // Merge jobs: one per (active row with more than one split, kv head), on the CTAs of
+          // attention ranks U, U + 1, ... (those without units while the grid has room): each
+          // polls its splits' flagged partials and writes the head outputs. No split waits for
+          // another, and no arrival counter is taken.
+          if (!bad) {
+            const int G = int(gridDim.x);
+            for (int j = ((arank - U) % G + G) % G; j < n_merges; j += G) {
+              int b = 0, jj = j;
+              for (; b < NB; ++b) {
+                if (!merge_row[b]) continue;
+                if (jj < kvh_n) break;
+                jj -= kvh_n;
+              }
+              if (b == NB) break;
+              unsigned long long *st = (trace && arank >= U && j < G) ? trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8
+                                                                    : nullptr;  // a CTA without units: free slots
+              if (!attn_merge_ll<128, 2>(ap, b, jj, merge_splits[b], ctid, st)) bad = true;
             }
           }
-          wbad = __any_sync(0xFFFFFFFFu, wbad);
-          if (j == 0) attn_stamp(st, 1, ctid);  // the unit's first chunk has landed
-          if (!wbad) {
-            const bf16 *ks = ring + size_t(sidx) * kRingStageElems;
-            const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
-            attn_chunk<128, 2>(team_sm->q_b, team_sm->knew, team_sm->vnew, ks, ks + kKvChunk * 128, n_main,
-                               rs.pos - base < kKvChunk, ap.g.scale, wacc, ctid);
-          }
-          __syncwarp();
-          if (lane == 0 && landed) mbar_arrive(&empty[sidx]);
         }
-        if (team_any(1, wbad)) bad = true;
-        attn_stamp(st, 4, ctid);
-        if (ui.active && !bad) {
-          const AttnAcc<128> acc = attn_combine<128, 2>(*team_sm, wacc, ctid, 1);
-          if (ui.n_splits == 1)
-            attn_single_out<128, 2>(ap, acc, ui.row, ui.kvh, ctid);
-          else
-            attn_partial_ll<128, 2>(ap, acc, ui.row, ui.kvh, ui.split, ctid);
-        } else if (!ui.active && ui.split == 0) {
-          attn_write_inactive<128, 2>(ap, ui.row, ui.kvh, ctid);  // an inactive row's heads: zero words
-        }
-        attn_stamp(st, 5, ctid);
-        itk += nch;
+        stamp(5 * l + 1, 2);
+        continue;
       }
-      it = itk;
-      // Merge jobs: one per (active row with more than one split, kv head), on the CTAs of
-      // attention ranks U, U + 1, ... (those without units while the grid has room): each
-      // polls its splits' flagged partials and writes the head outputs. No split waits for
-      // another, and no arrival counter is taken.
-      if (!bad) {
-        const int G = int(gridDim.x);
-        for (int j = ((arank - U) % G + G) % G; j < n_merges; j += G) {
-          int b = 0, jj = j;
-          for (; b < NB; ++b) {
-            if (!merge_row[b]) continue;
-            if (jj < kvh_n) break;
-            jj -= kvh_n;
-          }
-          if (b == NB) break;
-          unsigned long long *st = (trace && arank >= U && j < G) ? trace + (size_t(blockIdx.x) * (5 * nL + 1) + 5 * l + 1) * 8
-                                                                : nullptr;  // a CTA without units: free slots
-          if (!attn_merge_ll<128, 2>(ap, b, jj, merge_splits[b], ctid, st)) bad = true;
-        }
-      }
+      // k: 0 QKV (RMSNorm of x fused), 2 O (+ residual), 3 gate/up (RMSNorm, SwiGLU),
+      // 4 down (+ residual); the GEMV task index is k, or k - 1 after attention.
+      const int tk = k == 0 ? 0 : k - 1;
+      const bool norm_op = k == 0 || k == 3, res_op = k == 2 || k == 4;
+      const int ki = k <= 2 ? 0 : 1;  // kept residual columns: for O (0) or down (1)
+      GemvTask t = task(l, tk);
+      if (res_op) t = with_kept(t, ki == 0 ? kept_o : kept_d, ki);
+      const bool took = gemv_op(t, 5 * l + k, norm_op ? &wn_next : nullptr, k, norm_op ? s_keep[ki] : nullptr,
+                                p.h0 + keep_lo[ki], p.h0 + keep_hi[ki]);
+      if (k == 0) kept_o = took;
+      if (k == 3) kept_d = took;
+      stamp(5 * l + k, 3);
+      if (k == 2) ring_norm_w_load(task(l, 2), wn_next, ctid);  // gate/up's norm weights
+      if (k == 4 && l + 1 < nL) ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
     }
-    stamp(5 * l + 1, 2);
-    // O (+ residual).
-    stamp(5 * l + 2, 0);
-    gemv_op(with_kept(task(l, 1), kept_o, 0), 5 * l + 2, nullptr, 2);
-    stamp(5 * l + 2, 3);
-    // gate/up (RMSNorm of x fused, SwiGLU epilogue).
-    ring_norm_w_load(task(l, 2), wn_next, ctid);
-    stamp(5 * l + 3, 0);
-    const bool kept_d = gemv_op(task(l, 2), 5 * l + 3, &wn_next, 3, s_keep[1], p.h0 + keep_lo[1], p.h0 + keep_hi[1]);
-    stamp(5 * l + 3, 3);
-    // down (+ residual).
-    stamp(5 * l + 4, 0);
-    gemv_op(with_kept(task(l, 3), kept_d, 1), 5 * l + 4, nullptr, 4);
-    stamp(5 * l + 4, 3);
-    if (l + 1 < nL) ring_norm_w_load(task(l + 1, 0), wn_next, ctid);
     dump_x(l + 1);
   }
   // Final RMSNorm + phase rows of the LM head.
