@@ -117,7 +117,7 @@ int yar_session_free(yar_session *session);
  * issue; slots 6/7 of operation 0 and of the head hold globaltimer ns and the SM clock
  * at the step's start and end, for converting cycles to time), overwritten by every
  * step that has an active row (so it keeps the last step that did work, not the final
- * launch after a request's last token); read it with yar_session_trace. YAR_OPT_PREFETCH_STAGES (default 6, 0..64): how many
+ * launch after a request's last token); read it with yar_session_trace. YAR_OPT_PREFETCH_STAGES (default 2, 0..64): how many
  * 32 KB stages per SM the persistent kernel pulls into L2 ahead of its shared-memory ring
  * (its lookahead while the step waits at operation boundaries). */
 enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3, YAR_OPT_MAX_SPLITS = 4,

@@ -234,7 +234,7 @@ struct Session {
   int n_ctr = 0;
   float *gemm_ws = nullptr;  // split-K partials of the tcgen05 GEMM
   size_t gemm_ws_floats = 0;
-  int prefetch_stages = 6;  // persistent kernel: L2 prefetch distance beyond the ring
+  int prefetch_stages = 2;  // persistent kernel: L2 prefetch distance beyond the ring
   int forced_splits = 0;    // decode attention splits per (row, kv head); 0 = automatic
   int inject_op = 0;        // persistent kernel: operation whose wait is made to expire (0 = none)
   // Hidden-state record of the last decode step (when enabled): [layers + 1][max_rows][hidden]
