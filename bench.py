@@ -52,6 +52,22 @@ def step_bytes(L: int) -> int:
     return 28 * LAYER_BYTES + NORM_BYTES + HEAD_BYTES + EMBED_BYTES + KV_BYTES_PER_POS * (L + 1)
 
 
+def q8_matrix_bytes(rows: int, cols: int) -> int:
+    """Bytes of one matrix in 8-bit form: a byte per weight plus a BF16 scale and bias per
+    64 weights (rows padded to the 16-row stage unit the kernel streams)."""
+    return (rows + 15) // 16 * 16 * cols * (1 + 4 / 64)
+
+
+Q8_LAYER_BYTES = int(q8_matrix_bytes(4096, 2048) + q8_matrix_bytes(2048, 2048) + q8_matrix_bytes(12288, 2048)
+                     + q8_matrix_bytes(2048, 6144))
+Q8_HEAD_BYTES = int(q8_matrix_bytes(32769, 2048))
+
+
+def q8_step_bytes(L: int) -> int:
+    """Algorithmic HBM bytes of one 8-bit decode step at L visible positions (B = 1)."""
+    return 28 * Q8_LAYER_BYTES + NORM_BYTES + Q8_HEAD_BYTES + EMBED_BYTES + KV_BYTES_PER_POS * (L + 1)
+
+
 def load_module(name, path, pkg=None):
     import importlib.util
     if name in sys.modules:
@@ -249,15 +265,62 @@ def measured_traffic(avg_L: float):
         return None
 
 
-def ensure_weights(rank: int, world: int, barrier) -> str:
+def ensure_weights(rank: int, world: int, barrier, q8: bool = False) -> str:
     synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
     d = os.environ.get("YAR_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "yar_bench_3b_seed0"))
     marker = os.path.join(d, ".complete")
     if rank == 0 and not os.path.exists(marker):
         synth.write_converted(d, synth.PINNED, seed=0)
         open(marker, "w").write("ok")
+    marker8 = os.path.join(d, ".complete_8bit")
+    if q8 and rank == 0 and not os.path.exists(marker8):
+        # The 8-bit artifact of the same weights (conversion.py:651-735 quantizes the BF16 file).
+        synth.write_quantized(d, synth.PINNED)
+        import json as _json
+        man = _json.load(open(os.path.join(d, "conversion.json")))
+        man["precisions"]["8bit"] = {"ar": "ar-8bit.safetensors", "bits": 8, "group_size": 64, "mode": "affine",
+                                     "linear_only": True, "embedding_dtype": "bfloat16"}
+        _json.dump(man, open(os.path.join(d, "conversion.json"), "w"), indent=1)
+        open(marker8, "w").write("ok")
     barrier()
     return d
+
+
+def q8_song(yar, weights, rank, barrier, maxall, steps: int, local: int, peak: float):
+    """Config 2 on the `8bit` precision of the same weights (affine 8-bit group-64 linears,
+    ar-8bit.safetensors): the same prompts, sampling and timing as the headline, decode
+    through the 8-bit persistent kernel."""
+    import torch
+    model = yar.ARModel(weights, device=local, precision="8bit")
+    session = model.session(max_rows=1, max_ctx=PROMPT + DECODE)
+    smp = yar.Sampling(**SAMPLING)
+    rng = np.random.default_rng(3000 + rank)
+    prompts = [rng.integers(0, 184704, PROMPT).astype(np.int32) for _ in range(2 + steps)]
+    for i in range(2):
+        session.generate(prompts[i], smp, seed=i, phase="semantic")
+    barrier()
+    decode_ms, wall, tokens = 0.0, 0.0, 0
+    for i in range(steps):
+        t0 = time.perf_counter()
+        toks, timing, _ = session.generate(prompts[2 + i], smp, seed=2 + i, phase="semantic")
+        wall += time.perf_counter() - t0
+        decode_ms += timing["decode_device_ms"]
+        tokens += len(toks)
+    torch.cuda.synchronize()
+    barrier()
+    decode_s, wall_s = maxall(decode_ms / 1000.0), maxall(wall)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    per_token_s = decode_s / tokens
+    bytes_per_step = q8_step_bytes(int(PROMPT + DECODE / 2))
+    achieved = bytes_per_step / per_token_s / 1e9
+    session.close()
+    model.close()
+    return {"workload": "config2 on the 8bit precision of the bench weights (affine 8-bit group-64 linears, "
+                        "BF16 embedding and norms), same prompts/sampling/timing as the headline",
+            "value": tokens * world / decode_s, "unit": "tok/s", "ms_per_token": 1000 * per_token_s,
+            "e2e": {"value": tokens * world / wall_s, "unit": "tok/s"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "bytes_per_step": bytes_per_step}}
 
 
 class CpuDecoder:
@@ -350,6 +413,7 @@ def main():
     ap.add_argument("--no-bs64", action="store_true", help="skip the config-5 batched throughput measurement")
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context tensor-parallel song")
     ap.add_argument("--no-cfg", action="store_true", help="skip the config-3 classifier-free-guidance song")
+    ap.add_argument("--no-q8", action="store_true", help="skip the config-2 song on 8-bit weights")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -458,6 +522,13 @@ def main():
                                        "config5 continuous batching: 96 requests per GPU on 64 rows, prompts "
                                        "U[256,2048], U[512,1536] tokens each, top-k 50", rows=64,
                                        n_requests=96, lengths=(512, 1536))
+    q8 = None
+    if not args.no_q8:
+        try:
+            ensure_weights(rank, world, barrier, q8=True)
+            q8 = q8_song(yar, weights, rank, barrier, maxall, args.steps, local, peak)
+        except Exception as e:
+            q8 = {"error": f"{type(e).__name__}: {e}"[:300]}
     long = None
     if not args.no_long:
         # Every rank takes the same path, so a failure here is raised on every rank alike:
@@ -495,6 +566,7 @@ def main():
             "bs64_per_gpu": bs64_weak,
             "bs64_continuous": bs64_cont,
             "long_context": long,
+            "q8": q8,
         }
         print(json.dumps(out))
     session.close()

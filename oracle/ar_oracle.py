@@ -20,6 +20,13 @@ float32:
 * ``MLP``       modeling_yue2.py:223-224 — ``down(bf16(bf16(silu_f32(gate)) * up))``
 * ``DecoderLayer`` AR-only branch modeling_yue2.py:296-303 — BF16 residual adds
 * ``project``   native/src/ar.cpp:302-323 — phase-local LM-head rows
+* affine 8-bit linears (the ``8bit`` precision, ar.cpp:20-29 and :305-311 call
+  ``mx::quantized_matmul(x, w, scales, biases, transpose=true, 64, 8, "affine")``; MLX
+  0.32.2, pinned by conversion.py:31, is not in the reference tree): the published
+  semantics — element 4i + j of a row in bits 8j..8j+7 of U32 word i, and per 64-column
+  group ``w = scale * q + bias`` with BF16 scale and bias — restated by dequantizing to
+  float32 (``dequantize_affine8``) and contracting in float32 like every other linear.
+  Parity of this restatement with MLX itself is unpinned (MLX runs only on Apple GPUs).
 
 In ``bf16=False`` mode no rounding is applied (BASELINE config 1 runs the tiny model in
 FP32). Parity of this restatement with the upstream code is pinned by the golden vectors
@@ -79,6 +86,26 @@ def rope_cos_sin(positions, head_dim: int, theta: float):
     return np.cos(angles.astype(np.float64)).astype(F32), np.sin(angles.astype(np.float64)).astype(F32)
 
 
+def dequantize_affine8(packed, scales_bits, biases_bits) -> np.ndarray:
+    """Float32 ``scale * q + bias`` of an affine 8-bit group-64 matrix: ``packed`` U32
+    ``[rows, cols / 4]`` (element 4i + j in bits 8j..8j+7 of word i), BF16 bits of the
+    scales and biases ``[rows, cols / 64]``."""
+    words = np.ascontiguousarray(packed, dtype=np.uint32)
+    rows = words.shape[0]
+    shifts = np.arange(4, dtype=np.uint32) * np.uint32(8)
+    q = ((words[:, :, None] >> shifts[None, None, :]) & np.uint32(0xFF)).reshape(rows, -1).astype(F32)
+    s = bf16_from_bits(scales_bits)
+    b = bf16_from_bits(biases_bits)
+    groups = s.shape[1]
+    out = q.reshape(rows, groups, -1) * s[:, :, None] + b[:, :, None]
+    return out.reshape(rows, -1).astype(F32)
+
+
+def _quantized_groups(tensors) -> set:
+    """Names of the ``.weight`` entries that have ``.scales`` beside them."""
+    return {k[: -len("scales")] + "weight" for k in tensors if k.endswith(".scales")}
+
+
 class LazyBf16Weights:
     """BF16 bit arrays (e.g. memory-mapped safetensors) whose float32 values are formed on
     each access and not kept: a 3B-parameter model then costs no resident float32 copy,
@@ -86,8 +113,12 @@ class LazyBf16Weights:
 
     def __init__(self, bits: dict):
         self.bits = bits
+        self.quantized = _quantized_groups(bits)
 
     def __getitem__(self, name):
+        if name in self.quantized:
+            p = name[: -len("weight")]
+            return dequantize_affine8(self.bits[name], self.bits[p + "scales"], self.bits[p + "biases"])
         return bf16_from_bits(self.bits[name])
 
 
@@ -101,7 +132,14 @@ class OracleAR:
             self.w = LazyBf16Weights(tensors)
             return
         self.w = {}
+        quantized = _quantized_groups(tensors)
         for name, value in tensors.items():
+            if name.endswith(".scales") or name.endswith(".biases"):
+                continue
+            if name in quantized:  # affine 8-bit: float32 scale * q + bias, not rounded
+                p = name[: -len("weight")]
+                self.w[name] = dequantize_affine8(value, tensors[p + "scales"], tensors[p + "biases"])
+                continue
             if prerounded:  # float32 arrays (or row-indexable views) already holding BF16 values, kept as given
                 self.w[name] = value
                 continue

@@ -30,6 +30,8 @@ LIB_PATH = os.path.join(HERE, "libyue2ar_cuda.so")
 OK, FAILURE, INVALID_INPUT, CANCELLED = 0, 1, 2, 130
 PHASES = {"abc": 0, "semantic": 1, None: 2, "full": 2}
 LOAD_ANY_DIMS = 1
+LOAD_8BIT = 2
+PRECISIONS = ("bf16", "8bit")
 
 EOD, ABC_END, MUSIC_END = 151643, 151848, 151852
 CODEC_OFFSET, CODEC_SIZE, CONTEXT = 151853, 32768, 24576
@@ -67,6 +69,8 @@ def _load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "yar_version": (ctypes.c_char_p, []),
         "yar_model_load": (I, [ctypes.c_char_p, I, ctypes.POINTER(P)]),
         "yar_model_load_ex": (I, [ctypes.c_char_p, I, ctypes.c_uint32, ctypes.POINTER(P)]),
+        "yar_model_load_precision": (I, [ctypes.c_char_p, ctypes.c_char_p, I, ctypes.c_uint32, ctypes.POINTER(P)]),
+        "yar_model_precision_bits": (I, [P, ctypes.POINTER(I)]),
         "yar_tp_unique_id": (I, [ctypes.c_char_p]),
         "yar_tp_plan": (I, [I, I, I, I, I, I, I, ctypes.POINTER(ctypes.c_int64)]),
         "yar_tp_head_slice": (I, [I, I, I, ctypes.POINTER(I), ctypes.POINTER(I)]),
@@ -164,20 +168,27 @@ def tp_head_slice(width: int, rank: int, world: int) -> tuple[int, int]:
 
 
 class ARModel:
-    """Converted BF16 AR weights resident on one GPU (ARModel, ar.cpp:133-238).
+    """Converted AR weights resident on one GPU (ARModel, ar.cpp:133-238).
 
-    ``tp=(rank, world, nccl_id)`` loads this rank's tensor-parallel share instead: its
-    KV-head groups and FFN column block, with NCCL exchanges inside every forward. All
-    ranks must then make the same calls with the same arguments."""
+    ``precision`` is the reference's: "bf16" (ar-bf16.safetensors) or "8bit" (affine 8-bit
+    group-64 linears, ar-8bit.safetensors); "4bit" is rejected (not built).
+    ``tp=(rank, world, nccl_id)`` loads this rank's tensor-parallel share instead (BF16
+    only): its KV-head groups and FFN column block, with NCCL exchanges inside every
+    forward. All ranks must then make the same calls with the same arguments."""
 
-    def __init__(self, path: str, device: int = 0, any_dims: bool = False, tp=None):
+    def __init__(self, path: str, device: int = 0, any_dims: bool = False, tp=None, precision: str = "bf16"):
         h = ctypes.c_void_p()
         flags = LOAD_ANY_DIMS if any_dims else 0
         if tp is None:
-            _check(lib.yar_model_load_ex(os.fsencode(path), device, flags, ctypes.byref(h)))
+            _check(lib.yar_model_load_precision(os.fsencode(path), precision.encode(), device, flags,
+                                                ctypes.byref(h)))
             self.tp_rank, self.tp_world = 0, 1
         else:
             rank, world, nccl_id = tp
+            if precision not in PRECISIONS:
+                raise ValueError("precision must be 'bf16' or '8bit'")
+            if precision == "8bit":
+                flags |= LOAD_8BIT
             if len(nccl_id) != 128:
                 raise ValueError("nccl_id must be the 128 bytes of tp_unique_id()")
             _check(lib.yar_model_load_tp(os.fsencode(path), device, rank, world, bytes(nccl_id), flags,
@@ -189,6 +200,9 @@ class ARModel:
         keys = ("hidden", "layers", "heads", "kv_heads", "head_dim", "ffn", "vocab", "context", "weights_mib", "sms")
         self.dims = dict(zip(keys, [int(v) for v in dims]))
         self.device = device
+        b = ctypes.c_int()
+        _check(lib.yar_model_precision_bits(h, ctypes.byref(b)))
+        self.precision = "8bit" if b.value == 8 else "bf16"
 
     def session(self, max_rows: int = 2, max_ctx: int = 4096, page_tokens: int = 256) -> "Session":
         return Session(self, max_rows, max_ctx, page_tokens)

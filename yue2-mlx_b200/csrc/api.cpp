@@ -102,6 +102,28 @@ int yar_model_load_ex(const char *dir, int device, uint32_t flags, yar_model **o
 
 int yar_model_load(const char *dir, int device, yar_model **out) { return yar_model_load_ex(dir, device, 0, out); }
 
+int yar_model_load_precision(const char *dir, const char *precision, int device, uint32_t flags, yar_model **out) {
+  return guarded([&] {
+    need(dir && precision && out, "dir, precision and out are required");
+    *out = nullptr;
+    const std::string p = precision;
+    if (p != "bf16" && p != "8bit" && p != "4bit")
+      throw yar::Error("ValueError", "precision must be 'bf16', '8bit', or '4bit'");
+    if (p == "4bit") throw yar::Error("ValueError", "4-bit AR weights are not built in this engine");
+    flags &= ~uint32_t(YAR_LOAD_8BIT);
+    if (p == "8bit") flags |= YAR_LOAD_8BIT;
+    auto *h = new yar_model{yar::load_model(dir, device, flags)};
+    *out = h;
+  });
+}
+
+int yar_model_precision_bits(const yar_model *model, int *bits) {
+  return guarded([&] {
+    need(model && bits, "model and bits are required");
+    *bits = model->m->bits;
+  });
+}
+
 int yar_tp_unique_id(uint8_t *out) {
   return guarded([&] {
     need(out, "out is required");

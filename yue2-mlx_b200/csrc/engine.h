@@ -49,6 +49,13 @@ struct LayerWeights {
   const bf16 *ln1, *ln2, *qn, *kn;
 };
 
+// Stage images of one layer's 8-bit weights (the `8bit` precision), in the fused row
+// order of LayerWeights: the layout the 8-bit ring consumer reads (16-row units of
+// K / 2048 stages of 34,816 bytes, written by q8_stage_image).
+struct QLayer {
+  const unsigned char *qkv, *o, *gu, *down;
+};
+
 // Splits per (row, kv head) the decode attention's partial buffers hold.
 constexpr int kSessionMaxSplits = 32;
 
@@ -64,6 +71,17 @@ struct Model {
   // down for the persistent decode kernel; null when the shapes do not fit its ring.
   void *d_wmaps = nullptr;
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
+  // Precision: 0 (BF16 weights) or 8 (affine 8-bit, group 64). With 8 the arena holds the
+  // weights dequantized to BF16 (prefill, batched and per-operation decode read them) and
+  // `qarena` the stage images the persistent decode kernel streams: per layer (d_qlayers)
+  // and per phase of the head (this rank's phase rows; null for a phase the vocabulary
+  // does not have).
+  int bits = 0;
+  void *qarena = nullptr;
+  size_t qarena_bytes = 0;
+  std::vector<QLayer> qlayers;
+  QLayer *d_qlayers = nullptr;
+  const unsigned char *qhead[3] = {nullptr, nullptr, nullptr};
   // Tensor parallelism: this rank's share of the heads, KV heads and FFN columns is in `d`
   // (the whole model's dims in `full`, the rank's rows in `tp`); `tp_comm` is the NCCL
   // communicator (null: one GPU).
@@ -179,6 +197,13 @@ bool persistent_supported(const Model &m, int n_rows);
 // multiple of 2048.
 void build_stage_maps(Model &m);
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
+// 8-bit weights at load time (kernels_quant.cu): raw q bytes [rows][K] and BF16 scale /
+// bias bits [rows][K / 64] into BF16 weights, or into a stage image of q8_image_bytes.
+size_t q8_image_bytes(int rows, int K);
+void launch_q8_dequant(const uint8_t *q, const uint16_t *s, const uint16_t *b, long long rows, int K, bf16 *out,
+                       cudaStream_t st);
+void launch_q8_image(const uint8_t *q, const uint16_t *s, const uint16_t *b, int rows, int K, unsigned char *img,
+                     cudaStream_t st);
 
 enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
 

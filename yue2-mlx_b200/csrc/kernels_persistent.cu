@@ -38,6 +38,9 @@
 namespace yar {
 
 constexpr int kPersistStages = 6;
+// 8-bit weights: 34,816-byte stages (16 rows x 2048 columns and their scale/bias words); a
+// KV chunk (32 KB) fits one. Five of them leave the shared memory the 8-bit kernel needs.
+constexpr int kPersistStagesQ8 = 5;
 // Block: two consumer warpgroups (warps 0..7) and a producer warpgroup (warps 8..11; lane
 // 0 of warp 8 issues the copies). The launch gives every thread 168 registers (65536 / 384,
 // rounded down to 8); the producer warpgroup then returns registers (setmaxnreg.dec to
@@ -62,6 +65,10 @@ constexpr int kMaxPersistGrid = 256;
 struct PersistParams {
   CUtensorMap head_map;        // stage map of this rank's phase rows of the head (`head`, `head_rows`)
   const CUtensorMap *wmaps;    // device array [layer][4]: stage maps of qkv, o, gu, down
+  // 8-bit weights (the kernel's QB = 8): stage images per layer and of this rank's phase
+  // rows of the head (rows [0, head_rows) as `head`).
+  const QLayer *qlayers;
+  const unsigned char *qhead;
   const LayerWeights *layers;  // device array, one entry per layer
   // QKV: this rank's q/k/v rows; QD, F: the model's query and FFN widths (the K of O and
   // down); HS, h0: this rank's hidden rows of O and down; FL, f0: its FFN rows.
@@ -194,9 +201,9 @@ __host__ __device__ __forceinline__ int op_rotation(int o, int grid) {
 }
 
 // Stages CTA `cta` streams of an N x K operation o (the split task_groups and the
-// producer use).
-__host__ __device__ __forceinline__ int op_cta_stages(int N, int K, int o, int cta, int grid) {
-  const int groups = (N + 7) / 8, pos = (cta + op_rotation(o, grid)) % grid;
+// producer use; units of `urows` rows: 8 for BF16 stages, 16 for 8-bit ones).
+__host__ __device__ __forceinline__ int op_cta_stages(int N, int K, int o, int cta, int grid, int urows = 8) {
+  const int groups = (N + urows - 1) / urows, pos = (cta + op_rotation(o, grid)) % grid;
   return ((pos + 1) * groups / grid - pos * groups / grid) * (K / kRingPiece);
 }
 
@@ -205,11 +212,11 @@ __host__ __device__ __forceinline__ int op_cta_stages(int N, int K, int o, int c
 // waits for the CTA that finishes it last, so the units go to the CTAs with the fewest
 // stages: at 96 one-chunk units on 148 SMs no CTA streams more than 22 stages per layer
 // (23 with units on CTAs 0..95).
-inline void attention_ranks(PersistParams &p, int grid) {
+inline void attention_ranks(PersistParams &p, int grid, int urows) {
   int order[kMaxPersistGrid], total[kMaxPersistGrid];
   for (int c = 0; c < grid; ++c) {
-    total[c] = op_cta_stages(p.QKV, p.H, 0, c, grid) + op_cta_stages(p.HS, p.QD, 2, c, grid) +
-               op_cta_stages(2 * p.FL, p.H, 3, c, grid) + op_cta_stages(p.HS, p.F, 4, c, grid);
+    total[c] = op_cta_stages(p.QKV, p.H, 0, c, grid, urows) + op_cta_stages(p.HS, p.QD, 2, c, grid, urows) +
+               op_cta_stages(2 * p.FL, p.H, 3, c, grid, urows) + op_cta_stages(p.HS, p.F, 4, c, grid, urows);
     int i = c;  // insertion sort by (total, index)
     for (; i > 0 && total[order[i - 1]] > total[c]; --i) order[i] = order[i - 1];
     order[i] = c;
@@ -278,7 +285,8 @@ struct KvChunkRef {
 // operation's constants are loaded once on entering it.
 struct ProdCursor {
   int l, o, i, len;
-  const CUtensorMap *map;  // GEMV operations: weight stage map, K, this CTA's first group, stages per group
+  const CUtensorMap *map;    // GEMV operations: weight stage map (BF16) or stage image (8-bit),
+  const unsigned char *img;  // K, this CTA's first group (unit), stages per group
   int K, N, g, ks, KS;
 };
 
@@ -286,10 +294,13 @@ struct ProdCursor {
 // stages into the ring, and `prefetch_stages` stages ahead of that to pull the same
 // bytes into L2 (cp.async.bulk.prefetch), so HBM keeps streaming while the consumers wait
 // at operation boundaries and the ring copies of those stages then hit L2.
-template <int NB>
+template <int NB, int QB>
 struct Producer {
+  static constexpr bool kQ8 = QB == 8;
   const LayerWeights *layers;
   const CUtensorMap *wmaps, *head_map;
+  const QLayer *qlayers;
+  const unsigned char *qhead;
   int head_rows, H, QKV, QD, F, HS, FL, nL, epoch;
   bf16 *pool;
   AttnGeom g;
@@ -301,7 +312,7 @@ struct Producer {
   KvChunkRef *kv;  // this CTA's chunk list (shared memory, kMaxCtaChunks entries)
 
   __device__ Producer(const PersistParams &p, int ep, KvChunkRef *kv_smem)
-      : layers(p.layers), wmaps(p.wmaps), head_map(&p.head_map), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F), HS(p.HS),
+      : layers(p.layers), wmaps(p.wmaps), head_map(&p.head_map), qlayers(p.qlayers), qhead(p.qhead), head_rows(p.head_rows), H(p.H), QKV(p.QKV), QD(p.QD), F(p.F), HS(p.HS),
         FL(p.FL), nL(p.n_layers), epoch(ep), pool(p.ap.pool), g(p.ap.g), max_splits(p.ap.max_splits),
         page_table(p.ap.page_table), ctr(p.ctr), active(p.active), pos(p.pos), capacity(p.capacity), error(p.error), nkv(0),
         arank(p.attn_rank[blockIdx.x]), planned(false), failed(false), kv(kv_smem) {}
@@ -343,17 +354,18 @@ struct Producer {
       return;
     }
     if (c.l == nL) {
-      c.map = head_map, c.N = head_rows, c.K = H;
+      c.map = head_map, c.img = qhead, c.N = head_rows, c.K = H;
     } else {
       const CUtensorMap *m = wmaps + 4 * c.l;
+      const QLayer q = kQ8 ? qlayers[c.l] : QLayer{};
       switch (c.o) {
-        case 0: c.map = m, c.N = QKV, c.K = H; break;
-        case 2: c.map = m + 1, c.N = HS, c.K = QD; break;
-        case 3: c.map = m + 2, c.N = 2 * FL, c.K = H; break;
-        default: c.map = m + 3, c.N = HS, c.K = F; break;
+        case 0: c.map = m, c.img = q.qkv, c.N = QKV, c.K = H; break;
+        case 2: c.map = m + 1, c.img = q.o, c.N = HS, c.K = QD; break;
+        case 3: c.map = m + 2, c.img = q.gu, c.N = 2 * FL, c.K = H; break;
+        default: c.map = m + 3, c.img = q.down, c.N = HS, c.K = F; break;
       }
     }
-    const int groups = (c.N + 7) / 8;
+    const int groups = kQ8 ? (c.N + kQ8Rows - 1) / kQ8Rows : (c.N + 7) / 8;
     const int pos = (int(blockIdx.x) + (c.l == nL ? 0 : op_rotation(c.o, int(gridDim.x)))) % int(gridDim.x);
     const int g0 = pos * groups / int(gridDim.x), g1 = (pos + 1) * groups / int(gridDim.x);
     c.KS = c.K / kRingPiece;
@@ -405,6 +417,11 @@ struct Producer {
       }
       return;
     }
+    if (kQ8) {
+      mbar_arrive_expect_tx(bar, unsigned(kQ8StageBytes));
+      bulk_g2s_hint(dst, c.img + (size_t(c.g) * c.KS + c.ks) * kQ8StageBytes, unsigned(kQ8StageBytes), bar, pol);
+      return;
+    }
     mbar_arrive_expect_tx(bar, unsigned(kRingStageBytes));
     stage_load(dst, c.map, c.g * 8, c.ks, bar, pol);
   }
@@ -419,24 +436,36 @@ struct Producer {
       prefetch_l2(pool + (blk + 1) * g.page_elems + off, unsigned(r.n_main) * 256);
       return;
     }
-    stage_prefetch(c.map, c.g * 8, c.ks);
+    if (kQ8)
+      prefetch_l2(c.img + (size_t(c.g) * c.KS + c.ks) * kQ8StageBytes, unsigned(kQ8StageBytes));
+    else
+      stage_prefetch(c.map, c.g * 8, c.ks);
   }
 };
 
-template <int NB>
+// QB: the weights' precision — 0 (BF16, stage-map copies) or 8 (affine 8-bit stage images,
+// ring_consume_q8); everything else is shared.
+template <int NB, int QB>
 __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const __grid_constant__ PersistParams p) {
   // 1024-byte alignment: the weight stages are 128-byte-swizzled tensor copies.
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  constexpr int NS = kPersistStages;
+  constexpr bool kQ8 = QB == 8;
+  constexpr int NS = kQ8 ? kPersistStagesQ8 : kPersistStages;
+  constexpr int kSlot = kQ8 ? kQ8StageBytes : kRingStageBytes;  // bytes of a ring slot
+  constexpr int kUrows = kQ8 ? kQ8Rows : 8;                       // weight rows of a stage
   using ASm = AttnTeamSmem<128, 2>;
   // Layout: ring | act (GEMV activations) aliased with the attention teams' scratch (the
   // two are never live at once) | group partials.
   constexpr size_t kActBytes = size_t(NB) * kPersistMaxK * 2;
   constexpr size_t kUnion = kActBytes > sizeof(ASm) ? kActBytes : sizeof(ASm);
+  unsigned char *ringb = smem_raw;
   bf16 *ring = reinterpret_cast<bf16 *>(smem_raw);
-  bf16 *act = reinterpret_cast<bf16 *>(smem_raw + NS * kRingStageBytes);
-  ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kRingStageBytes);  // attention scratch
-  float *gred = reinterpret_cast<float *>(smem_raw + NS * kRingStageBytes + kUnion);
+  bf16 *act = reinterpret_cast<bf16 *>(smem_raw + NS * kSlot);
+  ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kSlot);  // attention scratch
+  float *gred = reinterpret_cast<float *>(smem_raw + NS * kSlot + kUnion);
+  // 8-bit: the group sums and FP16 factors of the staged rows (q8_stage_chunk).
+  __shared__ __align__(16) float s_sumx[kQ8 ? NB * (kPersistMaxK / 64) : 4];
+  __shared__ __align__(16) float s_qfac[kQ8 ? NB * (kPersistMaxK / 64) : 4];
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
   __shared__ float red[NB * kRingConsumers];
   __shared__ AttnRow<128> rowst[NB];
@@ -483,6 +512,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
     // O and down (no RMSNorm): each consumer warp stages its own k-range, so a warp starts
     // as soon as its inputs (for O: its kv head's outputs) are written.
     if (k == 1 || k == 3) t.stage_per_warp = true;
+    if (kQ8) {
+      const QLayer &q = p.qlayers[l];
+      t.qimg = k == 0 ? q.qkv : k == 1 ? q.o : k == 2 ? q.gu : q.down;
+      t.sumx = s_sumx;
+      t.qfac = s_qfac;
+    }
     if (l == 0 && k == 0 && p.inject_op != op) {
       // The first QKV reads each row's token embedding itself (an inactive row: zeros).
       t.in_ll = nullptr;
@@ -499,7 +534,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
       auto pstamp = [&](int o, int k) {
         if (trace) trace[(size_t(blockIdx.x) * (5 * nL + 1) + o) * 8 + k] = sm_clock();
       };
-      Producer<NB> pr(p, epoch, kv_chunks);
+      Producer<NB, QB> pr(p, epoch, kv_chunks);
       ProdCursor ic, pc;
       pr.begin(ic);
       pc = ic;
@@ -520,7 +555,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
         }
         const int op = 5 * ic.l + ic.o, so = ic.o == 1 ? 6 : 4;  // attention op slots 4/5 hold unit stamps
         if (ic.i == 0) pstamp(op, so);
-        pr.issue(ic, ring + size_t(s) * kRingStageElems, &full[s], pol);
+        pr.issue(ic, reinterpret_cast<bf16 *>(ringb + size_t(s) * kSlot), &full[s], pol);
         ++it;
         iv = pr.next(ic);
         if (!iv || 5 * ic.l + ic.o != op) pstamp(op, so + 1);
@@ -672,14 +707,18 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   auto gemv_op = [&](const GemvTask &t, int op_slot, const uint4 (*wn)[4], int o, uint4 *keep = nullptr,
                      int keep_lo = 0, int keep_hi = 0) {
     int g0, g1;
-    task_groups(t.N, blockIdx.x, gridDim.x, g0, g1, op_rotation(o, int(gridDim.x)));
+    task_groups(t.N, blockIdx.x, gridDim.x, g0, g1, op_rotation(o, int(gridDim.x)), kUrows);
     if (g0 == g1) return false;
     if (!t.stage_per_warp &&
         !ring_stage_act<NB, kPersistMaxK / kRingPiece>(t, act, red, ctid, wn, p.error, keep, keep_lo, keep_hi))
       bad = true;
     stamp(op_slot, 1);
-    ring_consume<NB, NS, kPersistMaxK / kRingPiece>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead,
-                                                    ctid);
+    if constexpr (kQ8)
+      ring_consume_q8<NB, NS, kPersistMaxK / kRingPiece>(t, g0, g1, ringb, act, full, empty, it, gred, p.error, bad,
+                                                         dead, ctid);
+    else
+      ring_consume<NB, NS, kPersistMaxK / kRingPiece>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead,
+                                                      ctid);
     stamp(op_slot, 2);
     return true;
   };
@@ -690,9 +729,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   int keep_lo[2], keep_hi[2];
   for (int i = 0; i < 2; ++i) {
     int g0, g1;
-    task_groups(p.HS, blockIdx.x, gridDim.x, g0, g1, op_rotation(i == 0 ? 2 : 4, int(gridDim.x)));
-    keep_lo[i] = 8 * g0;
-    keep_hi[i] = (g1 - g0) * 8 <= kResKeepCols ? 8 * g1 : 8 * g0;  // too wide: poll instead
+    task_groups(p.HS, blockIdx.x, gridDim.x, g0, g1, op_rotation(i == 0 ? 2 : 4, int(gridDim.x)), kUrows);
+    keep_lo[i] = kUrows * g0;
+    keep_hi[i] = (g1 - g0) * kUrows <= kResKeepCols ? kUrows * g1 : kUrows * g0;  // too wide: poll instead
   }
   auto with_kept = [&](GemvTask t, bool kept, int i) {
     if (kept && keep_hi[i] > keep_lo[i]) {
@@ -764,7 +803,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
               wbad = __any_sync(0xFFFFFFFFu, wbad);
               if (j == 0) attn_stamp(st, 1, ctid);  // the unit's first chunk has landed
               if (!wbad) {
-                const bf16 *ks = ring + size_t(sidx) * kRingStageElems;
+                const bf16 *ks = reinterpret_cast<const bf16 *>(ringb + size_t(sidx) * kSlot);
                 const int base = (ui.c0 + j) * kKvChunk, n_main = min(kKvChunk, rs.pos - base);
                 attn_chunk<128, 2>(team_sm->q_b, team_sm->knew, team_sm->vnew, ks, ks + kKvChunk * 128, n_main,
                                    rs.pos - base < kKvChunk, ap.g.scale, wacc, ctid);
@@ -831,22 +870,43 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   {
     GemvTask head = head_task(p, s_dst, epoch);
     head.ll_limit = p.ll_limit;
+    if (kQ8) {
+      head.qimg = p.qhead;
+      head.sumx = s_sumx;
+      head.qfac = s_qfac;
+    }
     int g0, g1;
     stamp(5 * nL, 0);
-    task_groups(head.N, blockIdx.x, gridDim.x, g0, g1);
+    task_groups(head.N, blockIdx.x, gridDim.x, g0, g1, 0, kUrows);
     const bool extra_cta = p.extra_row >= 0 && blockIdx.x == gridDim.x - 1;  // uses `act` below
     if ((g0 < g1 || extra_cta) && !ring_stage_act<NB, kPersistMaxK / kRingPiece>(head, act, red, ctid, nullptr, p.error))
       bad = true;
     stamp(5 * nL, 1);
-    ring_consume<NB, NS, kPersistMaxK / kRingPiece>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad,
-                                                    dead, ctid);
+    if constexpr (kQ8)
+      ring_consume_q8<NB, NS, kPersistMaxK / kRingPiece>(head, g0, g1, ringb, act, full, empty, it, gred, p.error,
+                                                         bad, dead, ctid);
+    else
+      ring_consume<NB, NS, kPersistMaxK / kRingPiece>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad,
+                                                      dead, ctid);
     stamp(5 * nL, 2);
     if (p.extra_row >= 0 && blockIdx.x == gridDim.x - 1 && warp < NB && !bad) {
-      // The ABC phase's extra row (ABC_END), from the normalized activations in `act`.
+      // The ABC phase's extra row (ABC_END), from the normalized activations in `act` (8-bit
+      // weights: the row's BF16 dequantized copy, and `act` holds FP16 values times the
+      // group's factor, exactly the BF16 values).
       const bf16 *wr = p.head + size_t(p.extra_row - 0) * H;
       float v = 0.f;
       for (int c = lane; c < H / 8; c += 32) {
-        const uint4 wq = ldg16(wr + c * 8), av = act_load_chunk(act + warp * H, c * 8);
+        uint4 av = act_load_chunk(act + warp * H, c * 8);
+        if constexpr (kQ8) {
+          const float f = s_qfac[warp * (H / 64) + c / 8];
+          uint32_t *w4 = reinterpret_cast<uint32_t *>(&av);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 h = __half22float2(*reinterpret_cast<const __half2 *>(&w4[q]));
+            w4[q] = pack_bf16x2(__float2bfloat16_rn(h.x * f), __float2bfloat16_rn(h.y * f));
+          }
+        }
+        const uint4 wq = ldg16(wr + c * 8);
         v = fmaf(bf_lo(wq.x), bf_lo(av.x), v);
         v = fmaf(bf_hi(wq.x), bf_hi(av.x), v);
         v = fmaf(bf_lo(wq.y), bf_lo(av.y), v);
@@ -884,16 +944,23 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   }
 }
 
-size_t persistent_smem(int NB) {
+size_t persistent_smem(int NB, int QB) {
   const size_t act = size_t(NB) * kPersistMaxK * 2, teams = sizeof(AttnTeamSmem<128, 2>);
-  return size_t(kPersistStages) * kRingStageBytes + (act > teams ? act : teams) + size_t(ring_gred_floats(NB)) * 4;
+  const size_t ring = QB == 8 ? size_t(kPersistStagesQ8) * kQ8StageBytes : size_t(kPersistStages) * kRingStageBytes;
+  return ring + (act > teams ? act : teams) + size_t(ring_gred_floats(NB)) * 4;
+}
+
+// The kernel instance for a row count and precision.
+static const void *persistent_kernel(int n_rows, int bits) {
+  if (bits == 8) return n_rows == 1 ? (const void *)k_decode_persistent<1, 8> : (const void *)k_decode_persistent<2, 8>;
+  return n_rows == 1 ? (const void *)k_decode_persistent<1, 0> : (const void *)k_decode_persistent<2, 0>;
 }
 
 void configure_persistent_kernels() {
-  YAR_CUDA(cudaFuncSetAttribute(k_decode_persistent<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(persistent_smem(1))));
-  YAR_CUDA(cudaFuncSetAttribute(k_decode_persistent<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(persistent_smem(2))));
+  for (int bits : {0, 8})
+    for (int rows = 1; rows <= 2; ++rows)
+      YAR_CUDA(cudaFuncSetAttribute(persistent_kernel(rows, bits), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(persistent_smem(rows, bits))));
 }
 
 // True when the persistent kernel handles this model and row count.
@@ -926,12 +993,13 @@ bool persistent_supported(const Model &m, int n_rows) {
     return false;
   // The register split (setmaxnreg) assumes the launch's per-thread registers.
   cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, n_rows == 1 ? k_decode_persistent<1> : k_decode_persistent<2>) != cudaSuccess ||
+  if (m.bits == 8 && (!m.d_qlayers || m.tp_world > 1)) return false;
+  if (cudaFuncGetAttributes(&fa, persistent_kernel(n_rows, m.bits)) != cudaSuccess ||
       fa.numRegs != kPersistLaunchRegs)
     return false;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, n_rows == 1 ? k_decode_persistent<1> : k_decode_persistent<2>,
-                                                    kPersistThreads, persistent_smem(n_rows)) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, persistent_kernel(n_rows, m.bits), kPersistThreads,
+                                                    persistent_smem(n_rows, m.bits)) != cudaSuccess)
     return false;
   return per_sm >= 1;
 }
@@ -943,6 +1011,9 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   PersistParams p;
   p.layers = m.d_layers;
   p.wmaps = static_cast<const CUtensorMap *>(m.d_wmaps);
+  p.qlayers = m.d_qlayers;
+  p.qhead = m.bits == 8 ? m.qhead[phase] : nullptr;
+  if (m.bits == 8 && !p.qhead) throw Error("RuntimeError", "no 8-bit head image for this phase");
   p.n_layers = d.layers;
   p.H = d.hidden;
   p.QKV = d.qkv_rows();
@@ -1030,22 +1101,24 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.ll_limit = s.inject_op > 0 ? (1ll << 16) : (1ll << 22);
   p.prefetch_stages = s.prefetch_stages;
   if (m.sm_count > kMaxPersistGrid) throw Error("RuntimeError", "persistent decode takes at most 256 SMs");
-  attention_ranks(p, m.sm_count);
+  attention_ranks(p, m.sm_count, m.bits == 8 ? kQ8Rows : 8);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.sm_count);
   cfg.blockDim = dim3(kPersistThreads);
-  cfg.dynamicSmemBytes = persistent_smem(n_rows);
+  cfg.dynamicSmemBytes = persistent_smem(n_rows, m.bits);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (n_rows == 1)
-    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_decode_persistent<1>, p));
+  if (m.bits == 8)
+    YAR_CUDA(n_rows == 1 ? cudaLaunchKernelEx(&cfg, k_decode_persistent<1, 8>, p)
+                         : cudaLaunchKernelEx(&cfg, k_decode_persistent<2, 8>, p));
   else
-    YAR_CUDA(cudaLaunchKernelEx(&cfg, k_decode_persistent<2>, p));
+    YAR_CUDA(n_rows == 1 ? cudaLaunchKernelEx(&cfg, k_decode_persistent<1, 0>, p)
+                         : cudaLaunchKernelEx(&cfg, k_decode_persistent<2, 0>, p));
 }
 
 }  // namespace yar

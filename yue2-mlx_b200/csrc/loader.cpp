@@ -3,11 +3,16 @@
 // native/src/pipeline.cpp:131-176).
 //
 // Checks, in the reference's order and with its error types:
-//   1. conversion.json is a schema-1 manifest with a precisions.bf16 record naming
-//      ar-bf16.safetensors and dtype bfloat16                      (ar.cpp:137-154)
+//   1. conversion.json is a schema-1 manifest with a record for the precision: bf16 names
+//      ar-bf16.safetensors and dtype bfloat16; 8bit names ar-8bit.safetensors with bits 8,
+//      group_size 64, mode affine, linear_only                   (ar.cpp:137-160)
 //   2. config.json matches the pinned generator config             (ar.cpp:161-192)
-//   3. ar-bf16.safetensors holds exactly the AR tensor set, BF16, with the pinned shapes
-//                                                                   (ar.cpp:193-236)
+//   3. the AR file holds exactly the AR tensor set with the pinned shapes: BF16, or for
+//      8bit every linear as a U32 [out, in / 4] weight with BF16 [out, in / 64] scales
+//      and biases                                                  (ar.cpp:193-236)
+// 8-bit weights are dequantized on the GPU into the BF16 layout below (prefill and the
+// batched and per-operation decode paths read it) and also written as the stage images
+// the persistent decode kernel streams (Model::qarena).
 // Device layout (one allocation): per layer the q/k/v rows stacked into one [q+2kv][H]
 // matrix, gate/up rows interleaved (row 2j gate j, row 2j+1 up j) so a SwiGLU output
 // comes from one row pair, and everything else as stored (row-major [out][in]).
@@ -15,7 +20,9 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -116,11 +123,12 @@ static Dims config_dims(const Json &config, bool any_dims) {
 struct TensorRec {
   std::vector<int64_t> shape;
   uint64_t begin, end;
+  std::string dtype;  // "BF16" or "U32"
 };
 
 static std::map<std::string, TensorRec> read_safetensors_header(const std::string &path, uint64_t &data_start) {
   std::ifstream in(path, std::ios::binary);
-  if (!in) throw Error("FileNotFoundError", "Converted artifact does not contain bf16 AR weights: " + path);
+  if (!in) throw Error("FileNotFoundError", "Converted artifact does not contain its AR weights file: " + path);
   in.seekg(0, std::ios::end);
   const uint64_t size = uint64_t(in.tellg());
   in.seekg(0);
@@ -146,12 +154,14 @@ static std::map<std::string, TensorRec> read_safetensors_header(const std::strin
     const Json &r = it.value();
     if (!r.is_object() || !r.contains("dtype") || !r.contains("shape") || !r.contains("data_offsets"))
       throw Error("ValueError", "Invalid safetensors entry: " + it.key());
-    if (r["dtype"] != "BF16") throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + it.key());
+    if (r["dtype"] != "BF16" && r["dtype"] != "U32")
+      throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + it.key());
     TensorRec t;
+    t.dtype = r["dtype"].get<std::string>();
     for (const auto &v : r["shape"]) t.shape.push_back(v.get<int64_t>());
     t.begin = r["data_offsets"][0].get<uint64_t>();
     t.end = r["data_offsets"][1].get<uint64_t>();
-    uint64_t n = 2;
+    uint64_t n = t.dtype == "U32" ? 4 : 2;
     for (auto v : t.shape) n *= uint64_t(v);
     if (t.end < t.begin || t.end - t.begin != n || data_start + t.end > size)
       throw Error("ValueError", "Truncated or inconsistent safetensors tensor: " + it.key());
@@ -181,49 +191,71 @@ TpPlan tp_plan(const Dims &d, int rank, int world) {
 Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_rank, int tp_world,
                   const uint8_t *nccl_id) {
   const bool any_dims = flags & 1u;
+  const int bits = (flags & 2u) ? 8 : 0;  // YAR_LOAD_8BIT: the `8bit` precision
+  const std::string precision = bits ? "8bit" : "bf16";
   if (tp_world > 1 && !nccl_id) throw Error("ValueError", "tensor parallelism needs an NCCL unique id");
+  if (tp_world > 1 && bits) throw Error("ValueError", "8-bit AR weights are not built for tensor parallelism");
   // 1. Manifest.
   Json manifest = read_json(dir + "/conversion.json");
   if (!manifest.is_object() || manifest.value("schema", 0) != 1)
     throw Error("ValueError", "conversion.json must be a schema-1 manifest");
   if (!manifest.contains("precisions") || !manifest["precisions"].is_object() ||
-      !manifest["precisions"].contains("bf16") || !manifest["precisions"]["bf16"].is_object())
-    throw Error("FileNotFoundError", "Converted artifact does not contain bf16 AR weights");
-  const Json &entry = manifest["precisions"]["bf16"];
-  if (entry.value("ar", std::string()) != "ar-bf16.safetensors")
+      !manifest["precisions"].contains(precision) || !manifest["precisions"][precision].is_object())
+    throw Error("FileNotFoundError", "Converted artifact does not contain " + precision + " AR weights");
+  const Json &entry = manifest["precisions"][precision];
+  const std::string filename = "ar-" + precision + ".safetensors";
+  if (entry.value("ar", std::string()) != filename)
     throw Error("ValueError", "Manifest AR filename does not match precision");
-  if (entry.value("dtype", std::string()) != "bfloat16")
-    throw Error("ValueError", "BF16 manifest entry must declare dtype='bfloat16'");
+  if (!bits) {
+    if (entry.value("dtype", std::string()) != "bfloat16")
+      throw Error("ValueError", "BF16 manifest entry must declare dtype='bfloat16'");
+  } else if (entry.value("bits", 0) != bits || entry.value("group_size", 0) != 64 ||
+             entry.value("mode", std::string()) != "affine" || entry.value("linear_only", false) != true) {
+    throw Error("ValueError", "Invalid affine quantization settings in AR manifest");
+  }
   // 2. Config.
   const Dims d = config_dims(read_json(dir + "/config.json"), any_dims);
+  if (bits && (d.hidden % 64 || d.ffn % 64 || d.qdim() % 64))
+    throw Error("ValueError", "8-bit AR weights need every linear's input width to be a multiple of 64");
   // 3. Tensors.
-  const std::string path = dir + "/ar-bf16.safetensors";
+  const std::string path = dir + "/" + filename;
   uint64_t data_start = 0;
   auto recs = read_safetensors_header(path, data_start);
   std::set<std::string> expected;
-  auto require = [&](const std::string &name, std::vector<int64_t> shape) {
+  auto require = [&](const std::string &name, std::vector<int64_t> shape, const char *dtype = "BF16") {
     expected.insert(name);
     auto it = recs.find(name);
     if (it == recs.end()) throw Error("ValueError", "Missing AR tensor: " + name);
-    if (it->second.shape != shape) throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + name);
+    if (it->second.shape != shape || it->second.dtype != dtype)
+      throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + name);
+  };
+  // A linear layer's tensors (ar.cpp:208-214): the BF16 weight, or the packed 8-bit form.
+  auto require_linear = [&](const std::string &n, int64_t out, int64_t in) {
+    if (!bits) {
+      require(n + ".weight", {out, in});
+      return;
+    }
+    require(n + ".weight", {out, in * bits / 32}, "U32");
+    require(n + ".scales", {out, in / 64});
+    require(n + ".biases", {out, in / 64});
   };
   const int H = d.hidden, Q = d.qdim(), KV = d.kvdim(), F = d.ffn, V = d.vocab, D = d.head_dim;
   require("model.embed_tokens.weight", {V, H});
   require("model.norm.weight", {H});
-  require("lm_head.weight", {V, H});
+  require_linear("lm_head", V, H);
   for (int i = 0; i < d.layers; ++i) {
     const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
     require(n + ".input_layernorm.weight", {H});
     require(n + ".post_attention_layernorm.weight", {H});
     require(a + ".q_norm.weight", {D});
     require(a + ".k_norm.weight", {D});
-    require(a + ".q_proj.weight", {Q, H});
-    require(a + ".k_proj.weight", {KV, H});
-    require(a + ".v_proj.weight", {KV, H});
-    require(a + ".o_proj.weight", {H, Q});
-    require(n + ".mlp.gate_proj.weight", {F, H});
-    require(n + ".mlp.up_proj.weight", {F, H});
-    require(n + ".mlp.down_proj.weight", {H, F});
+    require_linear(a + ".q_proj", Q, H);
+    require_linear(a + ".k_proj", KV, H);
+    require_linear(a + ".v_proj", KV, H);
+    require_linear(a + ".o_proj", H, Q);
+    require_linear(n + ".mlp.gate_proj", F, H);
+    require_linear(n + ".mlp.up_proj", F, H);
+    require_linear(n + ".mlp.down_proj", H, F);
   }
   for (const auto &[name, rec] : recs)
     if (!expected.count(name)) throw Error("ValueError", "Unexpected AR tensor: " + name);
@@ -278,6 +310,56 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     YAR_CUDA(cudaMalloc(&m->arena, off));
     char *base = static_cast<char *>(m->arena);
     auto at = [&](size_t o) { return reinterpret_cast<bf16 *>(base + o); };
+
+    // 8-bit: the stage images (m->qarena; only when every K is a multiple of 2048, the
+    // persistent kernel's stage width) and the raw buffers of one fused matrix (freed when
+    // the load ends).
+    struct DevBuf {
+      void *p = nullptr;
+      ~DevBuf() {
+        if (p) cudaFree(p);
+      }
+    } raw_qb, raw_sb, raw_bb;
+    struct QLO { size_t qkv, o, gu, down; };
+    std::vector<QLO> qlo(d.layers);
+    size_t qh_off[3] = {SIZE_MAX, SIZE_MAX, SIZE_MAX};
+    unsigned char *qbase = nullptr;
+    char *raw_q = nullptr;
+    uint16_t *raw_s = nullptr, *raw_b = nullptr;
+    if (bits) {
+      m->bits = bits;
+      if (H % 2048 == 0 && Q % 2048 == 0 && F % 2048 == 0) {
+        size_t qoff = 0;
+        auto qtake = [&](size_t bytes) {
+          const size_t o = qoff;
+          qoff = (qoff + bytes + 1023) & ~size_t(1023);
+          return o;
+        };
+        for (int i = 0; i < d.layers; ++i) {
+          qlo[i].qkv = qtake(q8_image_bytes(Q + 2 * KV, H));
+          qlo[i].o = qtake(q8_image_bytes(H, Q));
+          qlo[i].gu = qtake(q8_image_bytes(2 * F, H));
+          qlo[i].down = qtake(q8_image_bytes(H, F));
+        }
+        const bool pinned_vocab = V == 184704;  // the protocol phases; otherwise the whole vocabulary
+        for (int ph : {kPhaseAbc, kPhaseSemantic, kPhaseFull}) {
+          if ((ph == kPhaseFull) == pinned_vocab) continue;
+          qh_off[ph] = qtake(q8_image_bytes(phase_rows(d, ph).n_main, H));
+        }
+        m->qarena_bytes = qoff;
+        YAR_CUDA(cudaMalloc(&m->qarena, qoff));
+        qbase = static_cast<unsigned char *>(m->qarena);
+        m->qlayers.resize(d.layers);
+      }
+      const size_t max_nk = std::max({size_t(Q + 2 * KV) * H, size_t(H) * Q, size_t(2 * F) * H, size_t(H) * F,
+                                      size_t(V) * H});
+      YAR_CUDA(cudaMalloc(&raw_qb.p, max_nk));
+      YAR_CUDA(cudaMalloc(&raw_sb.p, max_nk / 64 * 2));
+      YAR_CUDA(cudaMalloc(&raw_bb.p, max_nk / 64 * 2));
+      raw_q = static_cast<char *>(raw_qb.p);
+      raw_s = static_cast<uint16_t *>(raw_sb.p);
+      raw_b = static_cast<uint16_t *>(raw_bb.p);
+    }
 
     // Stream the file through a pinned staging buffer.
     const int fd = ::open(path.c_str(), O_RDONLY);
@@ -356,12 +438,75 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
         buf ^= 1;
       }
     };
+    // 8-bit: whole rows of a tensor into device memory with a destination row pitch (the
+    // rows of one fused matrix: q/k/v stacked, gate/up interleaved).
+    auto upload_rows = [&](const std::string &name, int64_t row0, int64_t nrows, char *dst, size_t dst_pitch) {
+      const TensorRec &r = recs.at(name);
+      const size_t row_bytes = size_t(r.shape[1]) * (r.dtype == "U32" ? 4 : 2);
+      const int64_t rows_per = int64_t(stage_bytes / row_bytes);
+      for (int64_t r0 = 0; r0 < nrows; r0 += rows_per) {
+        const int64_t nr = std::min(rows_per, nrows - r0);
+        if (pending[buf]) YAR_CUDA(cudaEventSynchronize(done[buf]));
+        char *sb = static_cast<char *>(stage) + buf * stage_bytes;
+        pread_all(sb, data_start + r.begin + uint64_t(row0 + r0) * row_bytes, size_t(nr) * row_bytes);
+        YAR_CUDA(cudaMemcpy2DAsync(dst + size_t(r0) * dst_pitch, dst_pitch, sb, row_bytes, row_bytes, size_t(nr),
+                                   cudaMemcpyHostToDevice, st));
+        YAR_CUDA(cudaEventRecord(done[buf], st));
+        pending[buf] = true;
+        buf ^= 1;
+      }
+    };
+    // A linear's q bytes, scales and biases (rows [row0, row0 + nrows)) into the raw
+    // buffers at fused row `dst_row`, every `stride`-th row.
+    auto upload_q8 = [&](const std::string &lin, int64_t row0, int64_t nrows, int K, int64_t dst_row, int stride) {
+      const size_t qrow = size_t(K), srow = size_t(K / 64) * 2;
+      upload_rows(lin + ".weight", row0, nrows, raw_q + size_t(dst_row) * qrow, stride * qrow);
+      upload_rows(lin + ".scales", row0, nrows, reinterpret_cast<char *>(raw_s) + size_t(dst_row) * srow, stride * srow);
+      upload_rows(lin + ".biases", row0, nrows, reinterpret_cast<char *>(raw_b) + size_t(dst_row) * srow, stride * srow);
+    };
+    // The raw fused matrix (N x K) into BF16 weights at `dst` and a stage image at `img`.
+    auto finish_q8 = [&](int N, int K, char *dst, unsigned char *img) {
+      launch_q8_dequant(reinterpret_cast<const uint8_t *>(raw_q), raw_s, raw_b, N, K, reinterpret_cast<bf16 *>(dst), st);
+      if (img) launch_q8_image(reinterpret_cast<const uint8_t *>(raw_q), raw_s, raw_b, N, K, img, st);
+      // The raw buffers are refilled next: wait for these kernels (and the copies before).
+      YAR_CUDA(cudaStreamSynchronize(st));
+      pending[0] = pending[1] = false;
+    };
     upload("model.embed_tokens.weight", base + o_embed);
-    upload("lm_head.weight", base + o_head);
+    if (!bits) {
+      upload("lm_head.weight", base + o_head);
+    } else {
+      upload_q8("lm_head", 0, V, H, 0, 1);
+      finish_q8(V, H, base + o_head, nullptr);
+      // Stage images of each phase's rows of the head (the persistent kernel's head rows).
+      for (int ph = 0; ph < 3; ++ph) {
+        if (!qbase || qh_off[ph] == SIZE_MAX) continue;
+        const PhaseRows pr = phase_rows(d, ph);
+        launch_q8_image(reinterpret_cast<const uint8_t *>(raw_q) + size_t(pr.row0) * H, raw_s + size_t(pr.row0) * (H / 64),
+                        raw_b + size_t(pr.row0) * (H / 64), pr.n_main, H, qbase + qh_off[ph], st);
+        m->qhead[ph] = qbase + qh_off[ph];
+      }
+      YAR_CUDA(cudaStreamSynchronize(st));
+    }
     upload("model.norm.weight", base + o_norm);
     m->layers.resize(d.layers);
     for (int i = 0; i < d.layers; ++i) {
       const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
+      if (bits) {  // one GPU (8-bit weights are not built for tensor parallelism)
+        upload_q8(a + ".q_proj", 0, Q, H, 0, 1);
+        upload_q8(a + ".k_proj", 0, KV, H, Q, 1);
+        upload_q8(a + ".v_proj", 0, KV, H, Q + KV, 1);
+        auto img = [&](size_t o) { return qbase ? qbase + o : nullptr; };
+        finish_q8(Q + 2 * KV, H, base + lo[i].qkv, img(qlo[i].qkv));
+        upload_q8(a + ".o_proj", 0, H, Q, 0, 1);
+        finish_q8(H, Q, base + lo[i].o, img(qlo[i].o));
+        upload_q8(n + ".mlp.gate_proj", 0, F, H, 0, 2);
+        upload_q8(n + ".mlp.up_proj", 0, F, H, 1, 2);
+        finish_q8(2 * F, H, base + lo[i].gu, img(qlo[i].gu));
+        upload_q8(n + ".mlp.down_proj", 0, H, F, 0, 1);
+        finish_q8(H, F, base + lo[i].down, img(qlo[i].down));
+        if (qbase) m->qlayers[i] = QLayer{img(qlo[i].qkv), img(qlo[i].o), img(qlo[i].gu), img(qlo[i].down)};
+      } else {
       // Rank r: q rows of its heads, k/v rows of its KV heads, its FFN block of gate/up rows,
       // its hidden rows of O and down (all of them when tp_world == 1).
       upload_block(a + ".q_proj.weight", base + lo[i].qkv, plan.q_row0, Ql, 0, H);
@@ -370,6 +515,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
       upload_block(a + ".o_proj.weight", base + lo[i].o, plan.h_row0, Hs, 0, Q);
       upload_gate_up(n + ".mlp.gate_proj.weight", n + ".mlp.up_proj.weight", base + lo[i].gu, plan.ffn_row0, Fl);
       upload_block(n + ".mlp.down_proj.weight", base + lo[i].down, plan.h_row0, Hs, 0, F);
+      }
       upload(n + ".input_layernorm.weight", base + lo[i].ln1);
       upload(n + ".post_attention_layernorm.weight", base + lo[i].ln2);
       upload(a + ".q_norm.weight", base + lo[i].qn);
@@ -379,6 +525,10 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     }
     YAR_CUDA(cudaMalloc(&m->d_layers, sizeof(LayerWeights) * d.layers));
     YAR_CUDA(cudaMemcpy(m->d_layers, m->layers.data(), sizeof(LayerWeights) * d.layers, cudaMemcpyHostToDevice));
+    if (!m->qlayers.empty()) {
+      YAR_CUDA(cudaMalloc(&m->d_qlayers, sizeof(QLayer) * d.layers));
+      YAR_CUDA(cudaMemcpy(m->d_qlayers, m->qlayers.data(), sizeof(QLayer) * d.layers, cudaMemcpyHostToDevice));
+    }
     build_stage_maps(*m);
     m->embed = at(o_embed);
     m->lm_head = at(o_head);
@@ -418,6 +568,8 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     if (m->arena) cudaFree(m->arena);
     if (m->d_layers) cudaFree(m->d_layers);
     if (m->d_wmaps) cudaFree(m->d_wmaps);
+    if (m->qarena) cudaFree(m->qarena);
+    if (m->d_qlayers) cudaFree(m->d_qlayers);
     delete m;
     throw;
   }
@@ -431,6 +583,8 @@ void free_model(Model *m) {
   if (m->arena) cudaFree(m->arena);
   if (m->d_layers) cudaFree(m->d_layers);
   if (m->d_wmaps) cudaFree(m->d_wmaps);
+  if (m->qarena) cudaFree(m->qarena);
+  if (m->d_qlayers) cudaFree(m->d_qlayers);
   delete m;
 }
 

@@ -15,6 +15,7 @@
 // Every wait is bounded.
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 
@@ -68,6 +69,12 @@ struct GemvTask {
   // warp poll and stage only its own k-range of every row, so a warp starts as soon as its
   // inputs are written (no staging barrier across the CTA); no ring_stage_act call.
   bool stage_per_warp = false;
+  // Affine 8-bit weights (ring_consume_q8): W's stage image (q8_stage_image), and shared
+  // memory for each 64-column group of the staged rows ([rows][K / 64]): the FP32 sum of
+  // its values and the power-of-two factor of its FP16 copy. With `sumx` set the staging
+  // fills both and leaves the rows in `act` as FP16 (q8_stage_chunk).
+  const unsigned char *qimg = nullptr;
+  float *sumx = nullptr, *qfac = nullptr;
 };
 
 // Host: W's stage map ({64, N, K/64} view, {64, 8, 32} box, 128-byte swizzle) into `map`.
@@ -228,12 +235,13 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kRingConsumers * 32) : "memory");
 }
 
-// CTA `cta`'s 8-row groups [g0, g1) of an N-row task: contiguous ranges of floor or ceil
-// of groups / ctas, the ceil ranges at the CTAs whose position (cta + rot) % ctas the even
-// split gives them. `rot` lets consecutive operations put their extra groups on different
-// CTAs (which group a CTA computes does not change the group's arithmetic).
-__device__ __forceinline__ void task_groups(int N, int cta, int ctas, int &g0, int &g1, int rot = 0) {
-  const int groups = (N + 7) / 8;
+// CTA `cta`'s groups [g0, g1) of an N-row task (groups of `urows` rows: 8 for BF16 stages,
+// 16 for 8-bit ones): contiguous ranges of floor or ceil of groups / ctas, the ceil ranges
+// at the CTAs whose position (cta + rot) % ctas the even split gives them. `rot` lets
+// consecutive operations put their extra groups on different CTAs (which group a CTA
+// computes does not change the group's arithmetic).
+__device__ __forceinline__ void task_groups(int N, int cta, int ctas, int &g0, int &g1, int rot = 0, int urows = 8) {
+  const int groups = (N + urows - 1) / urows;
   const int pos = (cta + rot) % ctas;
   g0 = int((long long)pos * groups / ctas);
   g1 = int((long long)(pos + 1) * groups / ctas);
@@ -294,6 +302,45 @@ __device__ __forceinline__ void ring_norm_w_load(const GemvTask &t, uint4 (&wn)[
   for (int j = 0; j < 4; ++j) {
     const int k = (ctid + j * T) * 8;
     if (t.norm_w && k < t.K) wn[j] = ldg16(t.norm_w + k);
+  }
+}
+
+// 8-bit tasks: the statistics of a staged 16-byte chunk of row `row` (columns k..k+7) and
+// its rewrite to FP16. A 64-column group's 8 chunks sit at 8 consecutive lanes (lanes
+// 8m..8m+7, k = 64 G + 8 (lane & 7)); every lane of the warp takes part. The lanes add the
+// chunk's BF16 values in FP32 (sum(x): the bias term) and take their largest magnitude m;
+// lane 8m stores the sum at sums[G] and the group's factor f = 2^e at facs[G], e >= 0 the
+// least with m / f < 2^15. Each lane then rewrites its chunk as the FP16 values x / f:
+// exact (a power-of-two scale of a BF16 value, whose 8-bit significand FP16's 11 bits
+// hold), except below 2^-14 f where FP16 is subnormal and rounds to a multiple of 2^-24 f.
+__device__ __forceinline__ void q8_stage_chunk(bf16 *row, float *sums, float *facs, int k, int lane) {
+  const uint4 x = act_load_chunk(row, k);
+  const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+  float s = 0.f, m = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float lo = bf_lo(w4[q]), hi = bf_hi(w4[q]);
+    s = (s + lo) + hi;
+    m = fmaxf(m, fmaxf(fabsf(lo), fabsf(hi)));
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  }
+  // m < 2^(ex - 126) for biased exponent ex: e = ex - 141 puts m / 2^e below 2^15.
+  const int e = max(0, ((__float_as_int(m) >> 23) & 0xFF) - 141);
+  const float inv = __int_as_float((127 - e) << 23);
+  uint32_t h[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const __half2 v = __floats2half2_rn(bf_lo(w4[q]) * inv, bf_hi(w4[q]) * inv);
+    h[q] = *reinterpret_cast<const uint32_t *>(&v);
+  }
+  act_store_chunk(row, k, make_uint4(h[0], h[1], h[2], h[3]));
+  if ((lane & 7) == 0) {
+    sums[k >> 6] = s;
+    facs[k >> 6] = __int_as_float((127 + e) << 23);
   }
 }
 
@@ -419,6 +466,17 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
       }
     }
   }
+  if (t.sumx) {
+    const int KG = K / 64;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int j = 0; j < MC; ++j) {
+        const int k = (ctid + j * T) * 8;
+        if (k >= K) continue;  // warp-uniform: K is a multiple of 2048
+        q8_stage_chunk(act + b * K, t.sumx + b * KG, t.qfac + b * KG, k, lane);
+      }
+  }
   if (!t.in_ll) {
     consumer_sync();
     return true;
@@ -477,6 +535,17 @@ __device__ bool ll_stage_warp(const GemvTask &t, bf16 *act, int lane, int warp, 
       if (it >= 8) __nanosleep(32);
     }
   }
+  if (t.sumx) {  // this warp's groups only: the warp's own consumer reads them
+    const int KG = t.K / 64;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int ks = 0; ks < MC; ++ks) {
+        if (ks >= KS) continue;
+        const int k = ks * kRingPiece + warp * 256 + lane * 8;
+        q8_stage_chunk(act + size_t(b) * t.K, t.sumx + b * KG, t.qfac + b * KG, k, lane);
+      }
+  }
   return true;
 }
 
@@ -509,6 +578,100 @@ constexpr int kRingMaxGroups = 12;  // 8-row groups whose partial sums wait for 
 
 // Bytes of the group-partials buffer ring_consume needs.
 __host__ __device__ constexpr int ring_gred_floats(int NB) { return kRingMaxGroups * kRingConsumers * NB * 8; }
+
+// The epilogue of 8-row groups [gb, ge) of a task: the 8 warps' partial sums of each output
+// (gred, group gb first) are added in warp order and stored (flagged words or plain BF16),
+// with the task's epilogue applied. Every consumer thread takes part.
+template <int NB>
+__device__ __forceinline__ void ring_epilogue(const GemvTask &t, int gb, int ge, const float *gred, int *error,
+                                              int ctid) {
+  if (t.out_ll) {
+    // Flagged epilogue: one thread per pair of adjacent outputs, one flagged word each.
+    const bool swiglu = t.epi == kEpiSwiGLU;
+    const int per_group = NB * (swiglu ? 2 : 4);
+    for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {
+      const int gi = u / per_group, rem = u % per_group;
+      const float *src = gred + size_t(gi) * kRingConsumers * NB * 8;
+      const int r0 = (gb + gi) * 8;
+      float v[2];
+      int col;
+      const int b = swiglu ? rem / 2 : rem / 4, j = swiglu ? rem % 2 : rem % 4;
+      if (swiglu) {
+        if (r0 + 4 * j + 3 >= t.N) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {  // outputs 2j + e of the group: rows 2(2j + e) (gate), +1 (up)
+          const int rg = 2 * (2 * j + e);
+          float gs = 0.f, us = 0.f;
+#pragma unroll
+          for (int w = 0; w < kRingConsumers; ++w) {
+            gs += src[w * NB * 8 + b * 8 + rg];
+            us += src[w * NB * 8 + b * 8 + rg + 1];
+          }
+          v[e] = rbf(silu_f32(rbf(gs))) * rbf(us);
+        }
+        col = (r0 >> 1) + 2 * j;
+      } else {
+        if (r0 + 2 * j + 1 >= t.N) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float a = 0.f;
+#pragma unroll
+          for (int w = 0; w < kRingConsumers; ++w) a += src[w * NB * 8 + b * 8 + 2 * j + e];
+          v[e] = a;
+        }
+        col = r0 + 2 * j;
+      }
+      uint2 *o = t.out_ll + size_t(b) * t.out_ll_stride + (col >> 1);
+      bf16 lo, hi;
+      if (t.epi == kEpiResidual) {
+        uint32_t old = 0;
+        if (t.res_smem) {
+          old = t.res_smem[b * (kResKeepCols / 2) + ((col - t.res_lo) >> 1)];
+        } else if (!ll_wait1(o, t.res_flag, old, error, t.ll_limit)) {
+          atomicOr(error, 64);
+          continue;
+        }
+        lo = f2bf(bf_lo(old) + rbf(v[0]));
+        hi = f2bf(bf_hi(old) + rbf(v[1]));
+      } else {
+        lo = f2bf(v[0]);
+        hi = f2bf(v[1]);
+      }
+      ll_store_all(o, pack_bf16x2(lo, hi), t.out_flag, t.n_dst, t.dst);
+    }
+  } else {
+    const bool swiglu = t.epi == kEpiSwiGLU;
+    const int per_group = NB * (swiglu ? 4 : 8);
+    for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {
+      const int gi = u / per_group, rem = u % per_group;
+      const float *src = gred + size_t(gi) * kRingConsumers * NB * 8;
+      const int r0 = (gb + gi) * 8;
+      if (swiglu) {
+        const int b = rem / 4, j = rem % 4;  // pair j of the group: rows 2j (gate), 2j+1 (up)
+        if (r0 + 2 * j + 1 >= t.N) continue;
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int w = 0; w < kRingConsumers; ++w) {
+          gs += src[w * NB * 8 + b * 8 + 2 * j];
+          us += src[w * NB * 8 + b * 8 + 2 * j + 1];
+        }
+        const float gate = rbf(gs), up = rbf(us);
+        store_all(t.out + size_t(b) * t.out_stride + (r0 >> 1) + j, f2bf(rbf(silu_f32(gate)) * up), t.n_dst, t.dst);
+      } else {
+        const int b = rem / 8, r = rem % 8;
+        if (r0 + r >= t.N) continue;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kRingConsumers; ++w) v += src[w * NB * 8 + b * 8 + r];
+        bf16 *o = t.out + size_t(b) * t.out_stride + r0 + r;
+        if (t.epi == kEpiResidual)
+          store_all(o, f2bf(bf2f(__ldcg(o)) + rbf(v)), t.n_dst, t.dst);
+        else
+          store_all(o, f2bf(v), t.n_dst, t.dst);
+      }
+    }
+  }
+}
 
 // Consumers: consume the task's stages (continuing `it`) and apply the epilogue. Each
 // stage is 8 weight rows x 2048 (swizzled, see the top of this file); warp w owns the k
@@ -591,93 +754,151 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
       }
     }
     bad = consumer_any(bad);  // the batch barrier; a warp's own staging may have failed
-    if (!bad && t.out_ll) {
-      // Flagged epilogue: one thread per pair of adjacent outputs, one flagged word each.
-      const bool swiglu = t.epi == kEpiSwiGLU;
-      const int per_group = NB * (swiglu ? 2 : 4);
-      for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {
-        const int gi = u / per_group, rem = u % per_group;
-        const float *src = gred + size_t(gi) * kRingConsumers * NB * 8;
-        const int r0 = (gb + gi) * 8;
-        float v[2];
-        int col;
-        const int b = swiglu ? rem / 2 : rem / 4, j = swiglu ? rem % 2 : rem % 4;
-        if (swiglu) {
-          if (r0 + 4 * j + 3 >= t.N) continue;
+    if (!bad) ring_epilogue<NB>(t, gb, ge, gred, error, ctid);
+    if (ge < g1) consumer_sync();  // the next batch reuses gred
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Affine 8-bit weights (the `8bit` precision: per 64-column group w = scale * q + bias,
+// q in [0, 255], BF16 scale and bias; mlx quantized_matmul as ar.cpp:20-29 calls it).
+// A stage is 16 weight rows x 2048 columns of one matrix's image (q8_stage_image writes
+// it): kQ8QBytes of weights followed by 512 scale/bias words, one bulk copy. The weights
+// are laid out for the MMA's A operand (16 rows: the whole stage in one m16n8k16 per
+// k-tile, the weights as exact FP16 integers; the activation rows, staged as FP16, are the
+// B operand's columns): warp w's 64-column group j
+// is 2 x 32 lanes x 16 bytes at ((w * 4 + j) * 2 + h) * 512 + lane * 16, lane (g = lane / 4,
+// t = lane % 4) holding, for k-tiles kt = 2h and 2h + 1, the words (row g, kt), (row g + 8,
+// kt) of bytes at columns 16 kt + {2t, 2t + 1, 2t + 8, 2t + 9} of the group. Scale/bias
+// word (G, i) — BF16 scale low, BF16 bias high — of the stage's group G = 4w + j sits at
+// kQ8QBytes + (16 G + 2 (r % 8) + r / 8) x 4 for unit row r. Rows past N are zero.
+constexpr int kQ8Rows = 16;
+constexpr int kQ8QBytes = kQ8Rows * kRingPiece;                         // 32 KB of 8-bit weights
+constexpr int kQ8StageBytes = kQ8QBytes + kQ8Rows * (kRingPiece / 64) * 4;  // + scale/bias words: 34,816
+
+// Two 8-bit weights (the bytes of w that selector `sel` picks) as an FP16 pair: each byte
+// q placed under the exponent byte 0x64 is the FP16 value 1024 + q (ulp 1 in [1024,
+// 2048)), and one packed subtraction of 1024 leaves q exactly.
+__device__ __forceinline__ uint32_t q8_f16x2(uint32_t w, uint32_t sel) {
+  const uint32_t v = __byte_perm(w, 0x64646464u, sel);
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(0x64006400u));
+  return r;
+}
+// m16n8k16, FP16 operands, FP32 accumulators (no side effects: the compiler may schedule
+// it among independent work).
+__device__ __forceinline__ void mma_f16_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// One k-tile of a stage: the words (row g, kt) = wg and (row g + 8, kt) = wg8 hold bytes of
+// columns {2t, 2t + 1, 2t + 8, 2t + 9}: A fragments a0 / a2 from wg, a1 / a3 from wg8.
+__device__ __forceinline__ void q8_mma_tile(float *c, uint32_t wg, uint32_t wg8, uint32_t b0, uint32_t b1) {
+  mma_f16_16816(c, q8_f16x2(wg, 0x4140u), q8_f16x2(wg8, 0x4140u), q8_f16x2(wg, 0x4342u), q8_f16x2(wg8, 0x4342u), b0,
+                b1);
+}
+
+// Consumers of an 8-bit task: 16-row units [u0, u1), each K / 2048 stages (continuing
+// `it`). The staging left the activation rows as FP16 with a power-of-two factor f per
+// 64-column group (q8_stage_chunk). Warp w runs its 256 columns of every stage: per
+// 64-column group, four MMAs (16 weight rows as exact FP16 integers x the activation rows)
+// in two independent chains give sum(x q) / f per row, and the group adds
+// (scale f) * that + bias * sum(x) in FP32 — the affine dequantization of every weight
+// folded into two FMAs per output. Partial sums go to gred as ring_consume's, two 8-row
+// groups per unit, and the same epilogue follows (ring_epilogue). Failure handling is
+// ring_consume's.
+template <int NB, int NS, int MC = kStageChunks>
+__device__ void ring_consume_q8(const GemvTask &t, int u0, int u1, const unsigned char *ring, bf16 *act,
+                                uint64_t *full, uint64_t *empty, long long &it, float *gred, int *error, bool &bad,
+                                bool &dead, int ctid) {
+  static_assert(NB >= 1 && NB <= 2, "8-bit stages take one or two activation rows");
+  const int lane = ctid & 31, warp = ctid >> 5, K = t.K, KS = K / kRingPiece, KG = K / 64;
+  if (t.stage_per_warp && !bad && !ll_stage_warp<NB, MC>(t, act, lane, warp, error)) {
+    if (lane == 0 && error) atomicOr(error, 64);
+    bad = true;
+  }
+  __syncwarp();
+  const int g = lane >> 2, tq = lane & 3;  // A row g (and g + 8); B/C column pair 2 tq, 2 tq + 1
+  int s = int(it % NS);
+  unsigned phase = unsigned(it / NS) & 1u;
+  constexpr int kUnits = kRingMaxGroups / 2;  // units whose partial sums wait for one epilogue
+  const int G8 = (t.N + 7) / 8;
+  for (int ub = u0; ub < u1; ub += kUnits) {
+    const int ue = min(u1, ub + kUnits);
+    for (int u = ub; u < ue; ++u) {
+      // acc: (row g, activation row 2 tq), (g, 2 tq + 1), (g + 8, 2 tq), (g + 8, 2 tq + 1)
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ks = 0; ks < KS; ++ks) {
+        bool landed = false;
+        if (!dead) {
+          landed = mbar_wait(&full[s], phase);
+          if (!landed) {
+            if (lane == 0) atomicOr(error, 8);
+            dead = bad = true;
+          }
+        }
+        if (!bad) {
+          const unsigned char *st = ring + size_t(s) * kQ8StageBytes;
+          const bf16 *ar = act + size_t(ks) * kRingPiece;
+          // Group sums and factors of activation rows 2 tq, 2 tq + 1 for the warp's 4 groups.
+          float4 sx[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+          float4 fx[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {  // outputs 2j + e of the group: rows 2(2j + e) (gate), +1 (up)
-            const int rg = 2 * (2 * j + e);
-            float gs = 0.f, us = 0.f;
-#pragma unroll
-            for (int w = 0; w < kRingConsumers; ++w) {
-              gs += src[w * NB * 8 + b * 8 + rg];
-              us += src[w * NB * 8 + b * 8 + rg + 1];
+          for (int e = 0; e < 2; ++e)
+            if (2 * tq + e < NB) {
+              const int o = (2 * tq + e) * KG + ks * 32 + warp * 4;
+              sx[e] = *reinterpret_cast<const float4 *>(t.sumx + o);
+              fx[e] = *reinterpret_cast<const float4 *>(t.qfac + o);
             }
-            v[e] = rbf(silu_f32(rbf(gs))) * rbf(us);
-          }
-          col = (r0 >> 1) + 2 * j;
-        } else {
-          if (r0 + 2 * j + 1 >= t.N) continue;
+          const float sx0[4] = {sx[0].x, sx[0].y, sx[0].z, sx[0].w}, sx1[4] = {sx[1].x, sx[1].y, sx[1].z, sx[1].w};
+          const float fx0[4] = {fx[0].x, fx[0].y, fx[0].z, fx[0].w}, fx1[4] = {fx[1].x, fx[1].y, fx[1].z, fx[1].w};
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float a = 0.f;
-#pragma unroll
-            for (int w = 0; w < kRingConsumers; ++w) a += src[w * NB * 8 + b * 8 + 2 * j + e];
-            v[e] = a;
+          for (int j = 0; j < 4; ++j) {
+            const int k0 = warp * 256 + j * 64;
+            uint4 x01 = make_uint4(0, 0, 0, 0), x23 = make_uint4(0, 0, 0, 0);  // B: k-tiles 0, 1 / 2, 3
+            if (g < NB) {
+              x01 = *reinterpret_cast<const uint4 *>(ar + size_t(g) * K + k0 + tq * 8);
+              x23 = *reinterpret_cast<const uint4 *>(ar + size_t(g) * K + k0 + 32 + tq * 8);
+            }
+            const uint4 *qp = reinterpret_cast<const uint4 *>(st + ((warp * 4 + j) * 64 + lane) * 16);
+            const uint4 q01 = qp[0], q23 = qp[32];
+            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+            q8_mma_tile(c0, q01.x, q01.y, x01.x, x01.y);
+            q8_mma_tile(c1, q23.x, q23.y, x23.x, x23.y);
+            q8_mma_tile(c0, q01.z, q01.w, x01.z, x01.w);
+            q8_mma_tile(c1, q23.z, q23.w, x23.z, x23.w);
+            const uint2 sb = *reinterpret_cast<const uint2 *>(st + kQ8QBytes + ((warp * 4 + j) * 16 + 2 * g) * 4);
+            const float s_g = bf_lo(sb.x), b_g = bf_hi(sb.x), s_g8 = bf_lo(sb.y), b_g8 = bf_hi(sb.y);
+            acc[0] = fmaf(s_g * fx0[j], c0[0] + c1[0], fmaf(b_g, sx0[j], acc[0]));
+            acc[1] = fmaf(s_g * fx1[j], c0[1] + c1[1], fmaf(b_g, sx1[j], acc[1]));
+            acc[2] = fmaf(s_g8 * fx0[j], c0[2] + c1[2], fmaf(b_g8, sx0[j], acc[2]));
+            acc[3] = fmaf(s_g8 * fx1[j], c0[3] + c1[3], fmaf(b_g8, sx1[j], acc[3]));
           }
-          col = r0 + 2 * j;
         }
-        uint2 *o = t.out_ll + size_t(b) * t.out_ll_stride + (col >> 1);
-        bf16 lo, hi;
-        if (t.epi == kEpiResidual) {
-          uint32_t old = 0;
-          if (t.res_smem) {
-            old = t.res_smem[b * (kResKeepCols / 2) + ((col - t.res_lo) >> 1)];
-          } else if (!ll_wait1(o, t.res_flag, old, error, t.ll_limit)) {
-            atomicOr(error, 64);
-            continue;
-          }
-          lo = f2bf(bf_lo(old) + rbf(v[0]));
-          hi = f2bf(bf_hi(old) + rbf(v[1]));
-        } else {
-          lo = f2bf(v[0]);
-          hi = f2bf(v[1]);
+        __syncwarp();
+        if (lane == 0 && landed) mbar_arrive(&empty[s]);
+        ++it;
+        if (++s == NS) {
+          s = 0;
+          phase ^= 1u;
         }
-        ll_store_all(o, pack_bf16x2(lo, hi), t.out_flag, t.n_dst, t.dst);
       }
-    } else if (!bad) {
-      const bool swiglu = t.epi == kEpiSwiGLU;
-      const int per_group = NB * (swiglu ? 4 : 8);
-      for (int u = ctid; u < (ge - gb) * per_group; u += kRingConsumers * 32) {
-        const int gi = u / per_group, rem = u % per_group;
-        const float *src = gred + size_t(gi) * kRingConsumers * NB * 8;
-        const int r0 = (gb + gi) * 8;
-        if (swiglu) {
-          const int b = rem / 4, j = rem % 4;  // pair j of the group: rows 2j (gate), 2j+1 (up)
-          if (r0 + 2 * j + 1 >= t.N) continue;
-          float gs = 0.f, us = 0.f;
+      if (tq == 0) {  // columns 0, 1: the activation rows
+        float *d0 = gred + (size_t(2 * (u - ub)) * kRingConsumers + warp) * NB * 8;
+        float *d1 = d0 + size_t(kRingConsumers) * NB * 8;
 #pragma unroll
-          for (int w = 0; w < kRingConsumers; ++w) {
-            gs += src[w * NB * 8 + b * 8 + 2 * j];
-            us += src[w * NB * 8 + b * 8 + 2 * j + 1];
-          }
-          const float gate = rbf(gs), up = rbf(us);
-          store_all(t.out + size_t(b) * t.out_stride + (r0 >> 1) + j, f2bf(rbf(silu_f32(gate)) * up), t.n_dst, t.dst);
-        } else {
-          const int b = rem / 8, r = rem % 8;
-          if (r0 + r >= t.N) continue;
-          float v = 0.f;
-#pragma unroll
-          for (int w = 0; w < kRingConsumers; ++w) v += src[w * NB * 8 + b * 8 + r];
-          bf16 *o = t.out + size_t(b) * t.out_stride + r0 + r;
-          if (t.epi == kEpiResidual)
-            store_all(o, f2bf(bf2f(__ldcg(o)) + rbf(v)), t.n_dst, t.dst);
-          else
-            store_all(o, f2bf(v), t.n_dst, t.dst);
+        for (int b = 0; b < NB; ++b) {
+          d0[b * 8 + g] = acc[b];
+          d1[b * 8 + g] = acc[2 + b];
         }
       }
     }
-    if (ge < g1) consumer_sync();  // the next batch reuses gred
+    bad = consumer_any(bad);  // the batch barrier; a warp's own staging may have failed
+    if (!bad) ring_epilogue<NB>(t, 2 * ub, min(2 * ue, G8), gred, error, ctid);
+    if (ue < u1) consumer_sync();  // the next batch reuses gred
   }
 }
 

@@ -7,7 +7,13 @@ the layout ``lyra prepare`` produces for the AR partition and which ``ARModel`` 
 
 * ``config.json``      — the generator config (conversion.cpp:203-221);
 * ``conversion.json``  — schema-1 manifest with a ``precisions.bf16`` record;
-* ``ar-bf16.safetensors`` — the AR tensors only, BF16, row-major ``[out, in]``.
+* ``ar-bf16.safetensors`` — the AR tensors only, BF16, row-major ``[out, in]``;
+* ``ar-8bit.safetensors`` (``precisions=("bf16", "8bit")``) — the same tensors with every
+  linear weight (q/k/v/o, gate/up/down, LM head; not the embedding) in affine 8-bit
+  group-64 form, as ``lyra prepare`` writes it (conversion.py:596-620, :651-735): the
+  packed ``.weight`` as U32 ``[out, in / 4]`` (element 4i + j in bits 8j..8j+7 of word
+  i, so the words' little-endian bytes are the elements in order) and BF16 ``.scales`` /
+  ``.biases`` ``[out, in / 64]``; ``w ~= scale * q + bias`` per 64-column group.
 
 Weights: every matrix (embedding and LM head included) is N(0, std) with std 0.02,
 drawn with numpy's PCG64 ``standard_normal`` in float32, multiplied by float32(std) and
@@ -167,9 +173,118 @@ def _fill_job(args):
     return bits.size
 
 
+QUANT_GROUP = 64
+
+
+def linear_names(dims: Dims) -> list[str]:
+    """The weights the 8-bit artifact quantizes: every linear layer's (linear_only), not
+    the embedding table (ar.cpp:204-222 lists them)."""
+    return [name for name, shape in tensor_specs(dims) if len(shape) == 2 and name != "model.embed_tokens.weight"]
+
+
+def quantize_affine8(w: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Affine 8-bit group-64 quantization of a float32 ``[rows, cols]`` matrix, after the
+    published scheme of ``mlx.core.quantize`` (mode "affine"; MLX 0.32.2 is the version
+    conversion.py:31 pins): per 64-column group, scale = (max - min) / 255 (at least 1e-7)
+    and bias = min, each stored as BF16, and q = round((w - bias) / scale) in [0, 255],
+    formed with the stored values. Returns (q uint8, scale bits, bias bits)."""
+    rows, cols = w.shape
+    g = np.asarray(w, dtype=np.float32).reshape(rows, cols // QUANT_GROUP, QUANT_GROUP)
+    lo, hi = g.min(axis=2), g.max(axis=2)
+    scale = np.maximum((hi - lo) / np.float32(255.0), np.float32(1e-7)).astype(np.float32)
+    s_bits, b_bits = f32_to_bf16_bits(scale), f32_to_bf16_bits(lo)
+    s = bf16_bits_to_f32(s_bits)[:, :, None]
+    b = bf16_bits_to_f32(b_bits)[:, :, None]
+    q = np.clip(np.rint((g - b) / s), 0, 255).astype(np.uint8).reshape(rows, cols)
+    return q, s_bits, b_bits
+
+
+def _q8_layout(d: Dims):
+    """Header of ar-8bit.safetensors: the BF16 file's tensors in the same order, every
+    linear as ``.weight`` (U32), ``.scales`` and ``.biases`` (BF16)."""
+    linear = set(linear_names(d))
+    header, off, parts = {}, 0, []
+    for name, shape in tensor_specs(d):
+        if name in linear:
+            out, inp = shape
+            if inp % QUANT_GROUP:  # conversion.py:610-611
+                raise ValueError(f"Linear weight cannot use group-64 quantization: {name}")
+            prefix = name[: -len("weight")]
+            items = [(name, "U32", [out, inp // 4], out * inp),
+                     (prefix + "scales", "BF16", [out, inp // QUANT_GROUP], out * inp // QUANT_GROUP * 2),
+                     (prefix + "biases", "BF16", [out, inp // QUANT_GROUP], out * inp // QUANT_GROUP * 2)]
+        else:
+            items = [(name, "BF16", list(shape), int(np.prod(shape)) * 2)]
+        for key, dtype, shp, n in items:
+            header[key] = {"dtype": dtype, "shape": shp, "data_offsets": [off, off + n]}
+            off += n
+        parts.append((name, shape, name in linear))
+    header["__metadata__"] = {"format": "mlx", "partition": "ar", "precision": "8bit"}
+    raw = json.dumps(header, separators=(",", ":")).encode()
+    raw += b" " * ((8 - (len(raw) % 8)) % 8)
+    return parts, header, raw
+
+
+def _q8_job(args):
+    src, dst, data_start, header, name, shape, is_linear, r0, r1 = args
+    bits = read_safetensors(src)[name]
+    mm = np.memmap(dst, dtype=np.uint8, mode="r+")
+    if not is_linear:
+        b, _ = header[name]["data_offsets"]
+        view = np.ascontiguousarray(bits).view(np.uint8).reshape(-1)
+        mm[data_start + b:data_start + b + view.size] = view
+    else:
+        q, sb, bb = quantize_affine8(bf16_bits_to_f32(bits[r0:r1]))
+        cols = shape[1]
+        prefix = name[: -len("weight")]
+        b = header[name]["data_offsets"][0] + r0 * cols
+        mm[data_start + b:data_start + b + q.size] = q.reshape(-1)
+        for key, arr in ((prefix + "scales", sb), (prefix + "biases", bb)):
+            b = header[key]["data_offsets"][0] + r0 * (cols // QUANT_GROUP) * 2
+            v = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
+            mm[data_start + b:data_start + b + v.size] = v
+    mm.flush()
+    del mm
+
+
+def write_quantized(directory: str, dims: Dims, workers: int | None = None) -> str:
+    """ar-8bit.safetensors from the directory's ar-bf16.safetensors (the BF16 weights are
+    the source, as in conversion.py:651-735)."""
+    parts, header, raw = _q8_layout(dims)
+    src = os.path.join(directory, "ar-bf16.safetensors")
+    dst = os.path.join(directory, "ar-8bit.safetensors")
+    data_start = 8 + len(raw)
+    total = data_start + max(v["data_offsets"][1] for k, v in header.items() if k != "__metadata__")
+    with open(dst, "wb") as f:
+        f.write(np.uint64(len(raw)).tobytes())
+        f.write(raw)
+        f.truncate(total)
+    jobs = []
+    for name, shape, is_linear in parts:
+        if not is_linear:
+            jobs.append((src, dst, data_start, header, name, shape, False, 0, 0))
+            continue
+        step = max(16, (1 << 23) // shape[1])
+        for r0 in range(0, shape[0], step):
+            jobs.append((src, dst, data_start, header, name, shape, True, r0, min(shape[0], r0 + step)))
+    workers = workers or min(32, os.cpu_count() or 1)
+    if workers > 1 and len(jobs) > 1:
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            for _ in pool.map(_q8_job, jobs):
+                pass
+    else:
+        for j in jobs:
+            _q8_job(j)
+    return dst
+
+
 def write_converted(directory: str, dims: Dims = PINNED, seed: int = 0, std: float = 0.02,
-                    norm_std: float = 0.0, workers: int | None = None) -> str:
-    """Write config.json, conversion.json and ar-bf16.safetensors under ``directory``."""
+                    norm_std: float = 0.0, workers: int | None = None,
+                    precisions: tuple[str, ...] = ("bf16",)) -> str:
+    """Write config.json, conversion.json and ar-bf16.safetensors under ``directory``
+    (and ar-8bit.safetensors when ``precisions`` names "8bit")."""
+    if any(p not in ("bf16", "8bit") for p in precisions) or "bf16" not in precisions:
+        raise ValueError("precisions: 'bf16', optionally with '8bit'")
     os.makedirs(directory, exist_ok=True)
     specs, header, raw = _layout(dims)
     path = os.path.join(directory, "ar-bf16.safetensors")
@@ -209,13 +324,19 @@ def write_converted(directory: str, dims: Dims = PINNED, seed: int = 0, std: flo
                 "precisions": {"bf16": {"ar": "ar-bf16.safetensors", "nar": "nar-bf16.safetensors",
                                         "dtype": "bfloat16"}},
                 "files": {}}
+    if "8bit" in precisions:
+        write_quantized(directory, dims, workers)
+        # The record conversion.py:754-761 writes for a quantized precision.
+        manifest["precisions"]["8bit"] = {"ar": "ar-8bit.safetensors", "bits": 8, "group_size": QUANT_GROUP,
+                                          "mode": "affine", "linear_only": True, "embedding_dtype": "bfloat16"}
     with open(os.path.join(directory, "conversion.json"), "w") as f:
         json.dump(manifest, f, indent=1)
     return directory
 
 
 def read_safetensors(path: str) -> dict[str, np.ndarray]:
-    """Read a BF16 safetensors file into {name: uint16 array} (memory-mapped)."""
+    """Read a safetensors file into {name: array} (memory-mapped): BF16 tensors as uint16
+    bits, U32 tensors as uint32."""
     with open(path, "rb") as f:
         n = int(np.frombuffer(f.read(8), dtype=np.uint64)[0])
         header = json.loads(f.read(n))
@@ -225,5 +346,6 @@ def read_safetensors(path: str) -> dict[str, np.ndarray]:
         if name == "__metadata__":
             continue
         b, e = rec["data_offsets"]
-        out[name] = mm[8 + n + b:8 + n + e].view(np.uint16).reshape(rec["shape"])
+        dt = {"BF16": np.uint16, "U32": np.uint32}[rec["dtype"]]
+        out[name] = mm[8 + n + b:8 + n + e].view(dt).reshape(rec["shape"])
     return out
