@@ -253,11 +253,11 @@ def long_context(yar, model_one, weights, rank, world, local, barrier, maxall):
             "tensor_parallel": timing["tensor_parallel"], "tp_exchange": timing["tp_exchange"]}
 
 
-def measured_traffic(avg_L: float):
+def measured_traffic(avg_L: float, profile: str = "decode_persistent_config2.txt"):
     """DRAM bytes (read + write) of one persistent decode launch from the committed ncu
     capture, moved from the captured position to `avg_L` by the KV bytes per position
     (weights and head rows are position-independent)."""
-    path = os.path.join(ROOT, "profiles", "decode_persistent_config2.txt")
+    path = os.path.join(ROOT, "profiles", profile)
     try:
         kv = dict(line.split(":", 1) for line in open(path) if line.startswith("traffic_"))
         return int(int(kv["traffic_bytes_per_launch"]) + KV_BYTES_PER_POS * (avg_L - int(kv["traffic_position"])))
@@ -414,6 +414,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context tensor-parallel song")
     ap.add_argument("--no-cfg", action="store_true", help="skip the config-3 classifier-free-guidance song")
     ap.add_argument("--no-q8", action="store_true", help="skip the config-2 song on 8-bit weights")
+    ap.add_argument("--precision", choices=["bf16", "8bit"], default="bf16",
+                    help="weights of the headline song (8bit: the q8 line is the headline itself)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -461,10 +463,14 @@ def main():
         barrier = lambda: torch.cuda.synchronize()
         maxall = lambda v: v
 
-    weights = ensure_weights(rank, world, barrier)
+    q8_head = args.precision == "8bit"
+    weights = ensure_weights(rank, world, barrier, q8=q8_head)
     yar = load_module("yue2_mlx_b200", os.path.join(ROOT, "yue2-mlx_b200", "__init__.py"),
                       os.path.join(ROOT, "yue2-mlx_b200"))
-    model = yar.ARModel(weights, device=local)
+    model = yar.ARModel(weights, device=local, precision=args.precision)
+    if q8_head:
+        config = dict(config, workload=config["workload"] + ", 8bit precision (affine 8-bit group-64 linears)",
+                      l2="inputs larger than L2 (1.65 GB of weights per step)")
     session = model.session(max_rows=1, max_ctx=PROMPT + DECODE)
     smp = yar.Sampling(**SAMPLING)
     rng = np.random.default_rng(1000 + rank)
@@ -493,7 +499,7 @@ def main():
     e2e = total_tokens / wall_s
     per_token_s = decode_s / (tokens)
     avg_L = PROMPT + DECODE / 2
-    bytes_per_step = step_bytes(int(avg_L))
+    bytes_per_step = q8_step_bytes(int(avg_L)) if q8_head else step_bytes(int(avg_L))
     peak, peak_kind = peaks()
     achieved = bytes_per_step / per_token_s / 1e9
     layers = 28
@@ -503,7 +509,7 @@ def main():
     # Prefill of 512 tokens per layer: RMSNorm, QKV GEMM, q/k post, attention, O GEMM and
     # its split-K reduction, RMSNorm, gate/up GEMM, down GEMM and its reduction.
     prefill_launches = 1 + 10 * layers + 1
-    traffic = measured_traffic(avg_L)
+    traffic = measured_traffic(avg_L, "decode_q8_config2.txt" if q8_head else "decode_persistent_config2.txt")
     cfg = None if args.no_cfg else cfg_song(yar, model, rank, barrier, maxall)
     bs64 = bs64_weak = bs64_cont = None
     if not args.no_bs64:
@@ -523,7 +529,7 @@ def main():
                                        "U[256,2048], U[512,1536] tokens each, top-k 50", rows=64,
                                        n_requests=96, lengths=(512, 1536))
     q8 = None
-    if not args.no_q8:
+    if not args.no_q8 and not q8_head:
         try:
             ensure_weights(rank, world, barrier, q8=True)
             q8 = q8_song(yar, weights, rank, barrier, maxall, args.steps, local, peak)
@@ -548,7 +554,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * decode_s / args.steps, "ms_per_token": 1000 * per_token_s,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8 weights, bf16 activations" if q8_head else "bf16",
             "data": "synthetic (seeded N(0,0.02) weights, random prompt ids)", "config": config,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                     "d2h_bytes_per_step": DECODE * 4 + 20 * ((DECODE + 15) // 16),

@@ -39,7 +39,8 @@ namespace yar {
 
 constexpr int kPersistStages = 6;
 // 8-bit weights: 34,816-byte stages (16 rows x 2048 columns and their scale/bias words); a
-// KV chunk (32 KB) fits one. Five of them leave the shared memory the 8-bit kernel needs.
+// KV chunk (32 KB) fits one. Five of them leave the shared memory the two-row kernel needs
+// (a sixth for one row measured no faster: 0.833 vs 0.827 ms per token at config 2).
 constexpr int kPersistStagesQ8 = 5;
 // Block: two consumer warpgroups (warps 0..7) and a producer warpgroup (warps 8..11; lane
 // 0 of warp 8 issues the copies). The launch gives every thread 168 registers (65536 / 384,
