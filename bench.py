@@ -52,20 +52,20 @@ def step_bytes(L: int) -> int:
     return 28 * LAYER_BYTES + NORM_BYTES + HEAD_BYTES + EMBED_BYTES + KV_BYTES_PER_POS * (L + 1)
 
 
-def q8_matrix_bytes(rows: int, cols: int) -> int:
-    """Bytes of one matrix in 8-bit form: a byte per weight plus a BF16 scale and bias per
-    64 weights (rows padded to the 16-row stage unit the kernel streams)."""
-    return (rows + 15) // 16 * 16 * cols * (1 + 4 / 64)
+def q_matrix_bytes(rows: int, cols: int, bits: int = 8) -> int:
+    """Bytes of one matrix in quantized form: bits / 8 bytes per weight plus a BF16 scale and
+    bias per 64 weights (rows padded to the 16-row stage unit the kernel streams)."""
+    return int((rows + 15) // 16 * 16 * cols * (bits / 8 + 4 / 64))
 
 
-Q8_LAYER_BYTES = int(q8_matrix_bytes(4096, 2048) + q8_matrix_bytes(2048, 2048) + q8_matrix_bytes(12288, 2048)
-                     + q8_matrix_bytes(2048, 6144))
-Q8_HEAD_BYTES = int(q8_matrix_bytes(32769, 2048))
+def q_step_bytes(L: int, bits: int = 8) -> int:
+    """Algorithmic HBM bytes of one quantized decode step at L visible positions (B = 1)."""
+    layer = sum(q_matrix_bytes(r, c, bits) for r, c in ((4096, 2048), (2048, 2048), (12288, 2048), (2048, 6144)))
+    return 28 * layer + NORM_BYTES + q_matrix_bytes(32769, 2048, bits) + EMBED_BYTES + KV_BYTES_PER_POS * (L + 1)
 
 
 def q8_step_bytes(L: int) -> int:
-    """Algorithmic HBM bytes of one 8-bit decode step at L visible positions (B = 1)."""
-    return 28 * Q8_LAYER_BYTES + NORM_BYTES + Q8_HEAD_BYTES + EMBED_BYTES + KV_BYTES_PER_POS * (L + 1)
+    return q_step_bytes(L, 8)
 
 
 def load_module(name, path, pkg=None):
@@ -265,33 +265,33 @@ def measured_traffic(avg_L: float, profile: str = "decode_persistent_config2.txt
         return None
 
 
-def ensure_weights(rank: int, world: int, barrier, q8: bool = False) -> str:
+def ensure_weights(rank: int, world: int, barrier, q8: bool = False, q4: bool = False) -> str:
     synth = load_module("yue2_mlx_b200_synth", os.path.join(ROOT, "yue2-mlx_b200", "synth.py"))
     d = os.environ.get("YAR_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "yar_bench_3b_seed0"))
     marker = os.path.join(d, ".complete")
     if rank == 0 and not os.path.exists(marker):
         synth.write_converted(d, synth.PINNED, seed=0)
         open(marker, "w").write("ok")
-    marker8 = os.path.join(d, ".complete_8bit")
-    if q8 and rank == 0 and not os.path.exists(marker8):
-        # The 8-bit artifact of the same weights (conversion.py:651-735 quantizes the BF16 file).
-        synth.write_quantized(d, synth.PINNED)
-        import json as _json
-        man = _json.load(open(os.path.join(d, "conversion.json")))
-        man["precisions"]["8bit"] = {"ar": "ar-8bit.safetensors", "bits": 8, "group_size": 64, "mode": "affine",
-                                     "linear_only": True, "embedding_dtype": "bfloat16"}
-        _json.dump(man, open(os.path.join(d, "conversion.json"), "w"), indent=1)
-        open(marker8, "w").write("ok")
+    for bits, want in ((8, q8), (4, q4)):
+        marker_q = os.path.join(d, f".complete_{bits}bit")
+        if want and rank == 0 and not os.path.exists(marker_q):
+            # The quantized artifact of the same weights (conversion.py:651-735 quantizes the
+            # BF16 file).
+            synth.write_quantized(d, synth.PINNED, bits=bits)
+            man = json.load(open(os.path.join(d, "conversion.json")))
+            man["precisions"][f"{bits}bit"] = synth.quantized_record(bits)
+            json.dump(man, open(os.path.join(d, "conversion.json"), "w"), indent=1)
+            open(marker_q, "w").write("ok")
     barrier()
     return d
 
 
-def q8_song(yar, weights, rank, barrier, maxall, steps: int, local: int, peak: float):
-    """Config 2 on the `8bit` precision of the same weights (affine 8-bit group-64 linears,
-    ar-8bit.safetensors): the same prompts, sampling and timing as the headline, decode
-    through the 8-bit persistent kernel."""
+def q8_song(yar, weights, rank, barrier, maxall, steps: int, local: int, peak: float, bits: int = 8):
+    """Config 2 on the `8bit` (or `4bit`) precision of the same weights (affine group-64
+    linears, ar-<bits>bit.safetensors): the same prompts, sampling and timing as the
+    headline, decode through the quantized persistent kernel."""
     import torch
-    model = yar.ARModel(weights, device=local, precision="8bit")
+    model = yar.ARModel(weights, device=local, precision=f"{bits}bit")
     session = model.session(max_rows=1, max_ctx=PROMPT + DECODE)
     smp = yar.Sampling(**SAMPLING)
     rng = np.random.default_rng(3000 + rank)
@@ -311,12 +311,12 @@ def q8_song(yar, weights, rank, barrier, maxall, steps: int, local: int, peak: f
     decode_s, wall_s = maxall(decode_ms / 1000.0), maxall(wall)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     per_token_s = decode_s / tokens
-    bytes_per_step = q8_step_bytes(int(PROMPT + DECODE / 2))
+    bytes_per_step = q_step_bytes(int(PROMPT + DECODE / 2), bits)
     achieved = bytes_per_step / per_token_s / 1e9
     session.close()
     model.close()
-    return {"workload": "config2 on the 8bit precision of the bench weights (affine 8-bit group-64 linears, "
-                        "BF16 embedding and norms), same prompts/sampling/timing as the headline",
+    return {"workload": f"config2 on the {bits}bit precision of the bench weights (affine {bits}-bit group-64 "
+                        "linears, BF16 embedding and norms), same prompts/sampling/timing as the headline",
             "value": tokens * world / decode_s, "unit": "tok/s", "ms_per_token": 1000 * per_token_s,
             "e2e": {"value": tokens * world / wall_s, "unit": "tok/s"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -414,8 +414,9 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-context tensor-parallel song")
     ap.add_argument("--no-cfg", action="store_true", help="skip the config-3 classifier-free-guidance song")
     ap.add_argument("--no-q8", action="store_true", help="skip the config-2 song on 8-bit weights")
-    ap.add_argument("--precision", choices=["bf16", "8bit"], default="bf16",
-                    help="weights of the headline song (8bit: the q8 line is the headline itself)")
+    ap.add_argument("--no-q4", action="store_true", help="skip the config-2 song on 4-bit weights")
+    ap.add_argument("--precision", choices=["bf16", "8bit", "4bit"], default="bf16",
+                    help="weights of the headline song (quantized: that precision's line is the headline)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -463,14 +464,16 @@ def main():
         barrier = lambda: torch.cuda.synchronize()
         maxall = lambda v: v
 
-    q8_head = args.precision == "8bit"
-    weights = ensure_weights(rank, world, barrier, q8=q8_head)
+    q8_head = args.precision != "bf16"
+    head_bits = {"bf16": 0, "8bit": 8, "4bit": 4}[args.precision]
+    weights = ensure_weights(rank, world, barrier, q8=head_bits == 8, q4=head_bits == 4)
     yar = load_module("yue2_mlx_b200", os.path.join(ROOT, "yue2-mlx_b200", "__init__.py"),
                       os.path.join(ROOT, "yue2-mlx_b200"))
     model = yar.ARModel(weights, device=local, precision=args.precision)
     if q8_head:
-        config = dict(config, workload=config["workload"] + ", 8bit precision (affine 8-bit group-64 linears)",
-                      l2="inputs larger than L2 (1.65 GB of weights per step)")
+        config = dict(config, workload=config["workload"] + f", {args.precision} precision (affine {head_bits}-bit "
+                                                            "group-64 linears)",
+                      l2=f"inputs larger than L2 ({q_step_bytes(0, head_bits) / 1e9:.2f} GB of weights per step)")
     session = model.session(max_rows=1, max_ctx=PROMPT + DECODE)
     smp = yar.Sampling(**SAMPLING)
     rng = np.random.default_rng(1000 + rank)
@@ -499,7 +502,7 @@ def main():
     e2e = total_tokens / wall_s
     per_token_s = decode_s / (tokens)
     avg_L = PROMPT + DECODE / 2
-    bytes_per_step = q8_step_bytes(int(avg_L)) if q8_head else step_bytes(int(avg_L))
+    bytes_per_step = q_step_bytes(int(avg_L), head_bits) if q8_head else step_bytes(int(avg_L))
     peak, peak_kind = peaks()
     achieved = bytes_per_step / per_token_s / 1e9
     layers = 28
@@ -509,7 +512,7 @@ def main():
     # Prefill of 512 tokens per layer: RMSNorm, QKV GEMM, q/k post, attention, O GEMM and
     # its split-K reduction, RMSNorm, gate/up GEMM, down GEMM and its reduction.
     prefill_launches = 1 + 10 * layers + 1
-    traffic = measured_traffic(avg_L, "decode_q8_config2.txt" if q8_head else "decode_persistent_config2.txt")
+    traffic = measured_traffic(avg_L, f"decode_q{head_bits}_config2.txt" if q8_head else "decode_persistent_config2.txt")
     cfg = None if args.no_cfg else cfg_song(yar, model, rank, barrier, maxall)
     bs64 = bs64_weak = bs64_cont = None
     if not args.no_bs64:
@@ -528,13 +531,16 @@ def main():
                                        "config5 continuous batching: 96 requests per GPU on 64 rows, prompts "
                                        "U[256,2048], U[512,1536] tokens each, top-k 50", rows=64,
                                        n_requests=96, lengths=(512, 1536))
-    q8 = None
-    if not args.no_q8 and not q8_head:
+    quant = {}
+    for bits, skip in ((8, args.no_q8), (4, args.no_q4)):
+        if skip or q8_head:
+            quant[bits] = None
+            continue
         try:
-            ensure_weights(rank, world, barrier, q8=True)
-            q8 = q8_song(yar, weights, rank, barrier, maxall, args.steps, local, peak)
+            ensure_weights(rank, world, barrier, q8=bits == 8, q4=bits == 4)
+            quant[bits] = q8_song(yar, weights, rank, barrier, maxall, args.steps, local, peak, bits)
         except Exception as e:
-            q8 = {"error": f"{type(e).__name__}: {e}"[:300]}
+            quant[bits] = {"error": f"{type(e).__name__}: {e}"[:300]}
     long = None
     if not args.no_long:
         # Every rank takes the same path, so a failure here is raised on every rank alike:
@@ -555,7 +561,7 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * decode_s / args.steps, "ms_per_token": 1000 * per_token_s,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "u8 weights, bf16 activations" if q8_head else "bf16",
+            "dtype": f"u{head_bits} weights, bf16 activations" if q8_head else "bf16",
             "data": "synthetic (seeded N(0,0.02) weights, random prompt ids)", "config": config,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                     "d2h_bytes_per_step": DECODE * 4 + 20 * ((DECODE + 15) // 16),
@@ -573,7 +579,8 @@ def main():
             "bs64_per_gpu": bs64_weak,
             "bs64_continuous": bs64_cont,
             "long_context": long,
-            "q8": q8,
+            "q8": quant[8],
+            "q4": quant[4],
         }
         print(json.dumps(out))
     session.close()

@@ -43,7 +43,9 @@ enum {
   YAR_LOAD_ANY_DIMS = 1u << 0,
   /* Load the `8bit` precision (ar-8bit.safetensors: affine 8-bit group-64 linears) instead
    * of bf16, as ARModel(dir, "8bit") (native/src/ar.cpp:150-160, :208-214). One GPU only. */
-  YAR_LOAD_8BIT = 1u << 1
+  YAR_LOAD_8BIT = 1u << 1,
+  /* The `4bit` precision (ar-4bit.safetensors: affine 4-bit group-64 linears). One GPU only. */
+  YAR_LOAD_4BIT = 1u << 2
 };
 
 /* lyra::Sampling (native/include/lyra/types.hpp:78-87), same field meaning and the same
@@ -78,13 +80,14 @@ const char *yar_version(void);
 int yar_model_load(const char *dir, int device, yar_model **out);
 int yar_model_load_ex(const char *dir, int device, uint32_t flags, yar_model **out);
 /* ARModel::ARModel(dir, precision) — native/src/ar.cpp:133-238 with its precision argument:
- * "bf16" or "8bit" (the manifest's precisions.<precision> record, ar-<precision>.safetensors;
- * for 8bit the record must say bits 8, group_size 64, mode affine, linear_only, and every
- * linear is a U32 [out, in/4] weight with BF16 [out, in/64] scales and biases). "4bit" is
- * rejected (not built). 8-bit weights are streamed as such by the persistent decode kernel
- * (one and two rows); prefill and the batched decode read them dequantized to BF16. */
+ * "bf16", "8bit" or "4bit" (the manifest's precisions.<precision> record,
+ * ar-<precision>.safetensors; quantized, the record must say bits 8 / 4, group_size 64, mode
+ * affine, linear_only, and every linear is a U32 [out, in*bits/32] weight with BF16
+ * [out, in/64] scales and biases). Quantized weights are streamed as such by the persistent
+ * decode kernel (one and two rows); prefill and the batched decode read them dequantized to
+ * BF16. */
 int yar_model_load_precision(const char *dir, const char *precision, int device, uint32_t flags, yar_model **out);
-/* The loaded precision's bits: 0 (bf16) or 8. */
+/* The loaded precision's bits: 0 (bf16), 8 or 4. */
 int yar_model_precision_bits(const yar_model *model, int *bits);
 int yar_model_free(yar_model *model);
 /* Tensor parallelism over `world` GPUs, one process per GPU (no reference counterpart:

@@ -20,12 +20,13 @@ float32:
 * ``MLP``       modeling_yue2.py:223-224 — ``down(bf16(bf16(silu_f32(gate)) * up))``
 * ``DecoderLayer`` AR-only branch modeling_yue2.py:296-303 — BF16 residual adds
 * ``project``   native/src/ar.cpp:302-323 — phase-local LM-head rows
-* affine 8-bit linears (the ``8bit`` precision, ar.cpp:20-29 and :305-311 call
-  ``mx::quantized_matmul(x, w, scales, biases, transpose=true, 64, 8, "affine")``; MLX
-  0.32.2, pinned by conversion.py:31, is not in the reference tree): the published
-  semantics — element 4i + j of a row in bits 8j..8j+7 of U32 word i, and per 64-column
-  group ``w = scale * q + bias`` with BF16 scale and bias — restated by dequantizing to
-  float32 (``dequantize_affine8``) and contracting in float32 like every other linear.
+* affine 8- and 4-bit linears (the ``8bit`` / ``4bit`` precisions, ar.cpp:20-29 and
+  :305-311 call ``mx::quantized_matmul(x, w, scales, biases, transpose=true, 64, bits,
+  "affine")``; MLX 0.32.2, pinned by conversion.py:31, is not in the reference tree): the
+  published semantics — element (32 / bits) i + j of a row in bits (bits j).. of U32 word
+  i, and per 64-column group ``w = scale * q + bias`` with BF16 scale and bias — restated
+  by dequantizing to float32 (``dequantize_affine``) and contracting in float32 like
+  every other linear.
   Parity of this restatement with MLX itself is unpinned (MLX runs only on Apple GPUs).
 
 In ``bf16=False`` mode no rounding is applied (BASELINE config 1 runs the tiny model in
@@ -86,19 +87,27 @@ def rope_cos_sin(positions, head_dim: int, theta: float):
     return np.cos(angles.astype(np.float64)).astype(F32), np.sin(angles.astype(np.float64)).astype(F32)
 
 
-def dequantize_affine8(packed, scales_bits, biases_bits) -> np.ndarray:
-    """Float32 ``scale * q + bias`` of an affine 8-bit group-64 matrix: ``packed`` U32
-    ``[rows, cols / 4]`` (element 4i + j in bits 8j..8j+7 of word i), BF16 bits of the
-    scales and biases ``[rows, cols / 64]``."""
+def dequantize_affine(packed, scales_bits, biases_bits) -> np.ndarray:
+    """Float32 ``scale * q + bias`` of an affine group-64 matrix: ``packed`` U32
+    ``[rows, cols * bits / 32]`` (element (32 / bits) i + j in bits (bits j).. of word i;
+    bits 8 or 4, known from the shapes), BF16 bits of the scales and biases
+    ``[rows, cols / 64]``."""
     words = np.ascontiguousarray(packed, dtype=np.uint32)
-    rows = words.shape[0]
-    shifts = np.arange(4, dtype=np.uint32) * np.uint32(8)
-    q = ((words[:, :, None] >> shifts[None, None, :]) & np.uint32(0xFF)).reshape(rows, -1).astype(F32)
+    rows, groups = words.shape[0], np.asarray(scales_bits).shape[1]
+    bits = words.shape[1] * 32 // (groups * 64)
+    if bits not in (8, 4):
+        raise ValueError("packed width does not match 8 or 4 bits per weight")
+    per = 32 // bits
+    shifts = np.arange(per, dtype=np.uint32) * np.uint32(bits)
+    q = ((words[:, :, None] >> shifts[None, None, :]) & np.uint32((1 << bits) - 1)).reshape(rows, -1).astype(F32)
     s = bf16_from_bits(scales_bits)
     b = bf16_from_bits(biases_bits)
-    groups = s.shape[1]
     out = q.reshape(rows, groups, -1) * s[:, :, None] + b[:, :, None]
     return out.reshape(rows, -1).astype(F32)
+
+
+def dequantize_affine8(packed, scales_bits, biases_bits) -> np.ndarray:
+    return dequantize_affine(packed, scales_bits, biases_bits)
 
 
 def _quantized_groups(tensors) -> set:
@@ -118,7 +127,7 @@ class LazyBf16Weights:
     def __getitem__(self, name):
         if name in self.quantized:
             p = name[: -len("weight")]
-            return dequantize_affine8(self.bits[name], self.bits[p + "scales"], self.bits[p + "biases"])
+            return dequantize_affine(self.bits[name], self.bits[p + "scales"], self.bits[p + "biases"])
         return bf16_from_bits(self.bits[name])
 
 
@@ -136,9 +145,9 @@ class OracleAR:
         for name, value in tensors.items():
             if name.endswith(".scales") or name.endswith(".biases"):
                 continue
-            if name in quantized:  # affine 8-bit: float32 scale * q + bias, not rounded
+            if name in quantized:  # affine 8- or 4-bit: float32 scale * q + bias, not rounded
                 p = name[: -len("weight")]
-                self.w[name] = dequantize_affine8(value, tensors[p + "scales"], tensors[p + "biases"])
+                self.w[name] = dequantize_affine(value, tensors[p + "scales"], tensors[p + "biases"])
                 continue
             if prerounded:  # float32 arrays (or row-indexable views) already holding BF16 values, kept as given
                 self.w[name] = value

@@ -1,4 +1,4 @@
-"""8-bit weights on the GPU (the `8bit` precision: affine, group 64), against the oracle's
+"""Quantized weights on the GPU (the `8bit` and `4bit` precisions: affine, group 64), against the oracle's
 float32 dequantization (``dequantize_affine8``; MLX itself runs only on Apple GPUs, so
 this restatement is the anchor).
 
@@ -35,16 +35,31 @@ def yar():
 
 
 @pytest.fixture(scope="module")
-def q8wide(yar, synth, tmp_path_factory):
-    """Pinned widths, 2 layers, 4096-row vocabulary, in 8-bit: the persistent kernel runs
-    at its production shapes and the oracle stays fast."""
+def qwide_dir(synth, tmp_path_factory):
+    """Pinned widths, 2 layers, 4096-row vocabulary, in 8 and 4 bits: the persistent kernel
+    runs at its production shapes and the oracle stays fast."""
     dims = dataclasses.replace(synth.PINNED, layers=2, vocab=4096, context=4096)
-    d = str(tmp_path_factory.mktemp("q8wide"))
-    synth.write_converted(d, dims, seed=3, norm_std=0.1, precisions=("bf16", "8bit"))
-    oracle = ora.OracleAR(synth.read_safetensors(os.path.join(d, "ar-8bit.safetensors")), dims, bf16=True)
-    model = yar.ARModel(d, any_dims=True, precision="8bit")
-    assert model.precision == "8bit"
+    d = str(tmp_path_factory.mktemp("qwide"))
+    synth.write_converted(d, dims, seed=3, norm_std=0.1, precisions=("bf16", "8bit", "4bit"))
+    return d, dims
+
+
+def _qmodel(yar, synth, qwide_dir, precision):
+    d, dims = qwide_dir
+    oracle = ora.OracleAR(synth.read_safetensors(os.path.join(d, f"ar-{precision}.safetensors")), dims, bf16=True)
+    model = yar.ARModel(d, any_dims=True, precision=precision)
+    assert model.precision == precision
     return model, oracle
+
+
+@pytest.fixture(scope="module")
+def q8wide(yar, synth, qwide_dir):
+    return _qmodel(yar, synth, qwide_dir, "8bit")
+
+
+@pytest.fixture(scope="module")
+def q4wide(yar, synth, qwide_dir):
+    return _qmodel(yar, synth, qwide_dir, "4bit")
 
 
 def _decode(model, rows, prompts, forced, persistent, ctx=400):
@@ -136,3 +151,36 @@ def test_q8_generate_replays_with_the_cpu_sampler(yar, q8wide):
     assert len(tokens) == 24 and truncated and timing["execution"] == "cuda_graph"
     s.close()
     replay_generation(yar, model, prefix, tokens, smp, 7, None)
+
+
+@pytest.mark.parametrize("rows", [1, 2])
+def test_q4_persistent_decode_vs_oracle(q4wide, rows):
+    """4-bit stage images (18,432-byte stages, nibbles unpacked to FP16 integers) on the same
+    bounds as the 8-bit prefill-inheriting case (max-abs 0.09, rel-L2 0.025)."""
+    model, oracle = q4wide
+    rng = np.random.default_rng(4)
+    prompt, forced = rng.integers(0, 4096, 300).tolist(), rng.integers(0, 4096, 8).tolist()
+    gpu, ran = _decode(model, rows, [prompt, prompt], forced, persistent=True)
+    assert ran, "the 4-bit persistent decode kernel did not run"
+    if rows == 2:
+        np.testing.assert_array_equal(gpu[0], gpu[1])
+    orc = _oracle(oracle, prompt, forced)
+    err = (float(np.abs(gpu[0] - orc).max()), rel_l2(gpu[0], orc))
+    assert err[0] <= 0.09 and err[1] <= 0.025, err
+    top2 = np.sort(orc, axis=1)[:, -2:]
+    clear = top2[:, 1] - top2[:, 0] > 0.05
+    assert np.array_equal(gpu[0].argmax(1)[clear], orc.argmax(1)[clear])
+
+
+def test_q4_generate_replays_with_the_cpu_sampler(yar, q4wide):
+    from tests.test_gpu_parity import replay_generation
+    model, _ = q4wide
+    rng = np.random.default_rng(22)
+    prefix = rng.integers(0, 4096, 64).tolist()
+    smp = dict(temperature=1.0, top_p=0.93, top_k=50, repetition_penalty=1.2, penalty_window=50, min_tokens=24,
+               max_tokens=24)
+    s = model.session(max_rows=2, max_ctx=128)
+    tokens, timing, truncated = s.generate(prefix, yar.Sampling(**smp), seed=9, phase=None)
+    assert len(tokens) == 24 and truncated and timing["execution"] == "cuda_graph"
+    s.close()
+    replay_generation(yar, model, prefix, tokens, smp, 9, None)

@@ -1,4 +1,4 @@
-"""The `8bit` precision without a GPU: the synthetic artifact has the reference's layout
+"""The `8bit` and `4bit` precisions without a GPU: the synthetic artifacts have the reference's layout
 (conversion.py:596-620, :754-761), the oracle's dequantization follows the published
 affine group-64 semantics, and the loader rejects bad 8-bit checkpoints with the
 reference's messages (native/src/ar.cpp:137-160, :193-236) before touching the device."""
@@ -30,7 +30,7 @@ def q8_dims(synth):
 @pytest.fixture(scope="module")
 def q8_dir(tmp_path_factory, synth, q8_dims):
     d = str(tmp_path_factory.mktemp("q8small"))
-    synth.write_converted(d, q8_dims, seed=5, norm_std=0.1, workers=2, precisions=("bf16", "8bit"))
+    synth.write_converted(d, q8_dims, seed=5, norm_std=0.1, workers=2, precisions=("bf16", "8bit", "4bit"))
     return d
 
 
@@ -103,7 +103,7 @@ def _copy(src, dst):
 
 
 def test_precision_argument(yar, q8_dir):
-    for bad, needle in (("fp8", "precision must be"), ("4bit", "not built")):
+    for bad, needle in (("fp8", "precision must be"), ("int4", "precision must be")):
         with pytest.raises(yar.YarError) as e:
             yar.ARModel(q8_dir, any_dims=True, precision=bad)
         assert e.value.kind == "ValueError" and needle in e.value.message
@@ -155,3 +155,42 @@ def test_q8_tensor_set_checks(yar, q8_dir, tmp_path, mutate, needle):
     with pytest.raises(yar.YarError) as e:
         yar.ARModel(str(d), any_dims=True, precision="8bit")
     assert e.value.status == yar.INVALID_INPUT and needle in e.value.message
+
+
+def test_4bit_artifact_and_packing(synth, q8_dir, q8_dims):
+    man = json.load(open(os.path.join(q8_dir, "conversion.json")))
+    assert man["precisions"]["4bit"] == {"ar": "ar-4bit.safetensors", "bits": 4, "group_size": 64,
+                                         "mode": "affine", "linear_only": True, "embedding_dtype": "bfloat16"}
+    q4 = synth.read_safetensors(os.path.join(q8_dir, "ar-4bit.safetensors"))
+    b = synth.read_safetensors(os.path.join(q8_dir, "ar-bf16.safetensors"))
+    name = "model.layers.0.mlp.down_proj"
+    w = q4[name + ".weight"]
+    assert w.dtype == np.uint32 and w.shape == (q8_dims.hidden, q8_dims.ffn // 8)
+    # Element 8i + j in bits 4j..4j+3 of word i.
+    q, _, _ = synth.quantize_affine(synth.bf16_bits_to_f32(b[name + ".weight"]), 4)
+    assert q.max() <= 15
+    word = int(w[3, 5])
+    assert [(word >> (4 * j)) & 15 for j in range(8)] == [int(v) for v in q[3, 40:48]]
+    deq = ora.dequantize_affine(w, q4[name + ".scales"], q4[name + ".biases"])
+    s = synth.bf16_bits_to_f32(q4[name + ".scales"])
+    ref = synth.bf16_bits_to_f32(b[name + ".weight"]).reshape(deq.shape[0], -1, 64)
+    err = np.abs(deq.reshape(ref.shape) - ref)
+    assert np.all(err <= s[:, :, None] * 0.75 + np.abs(synth.bf16_bits_to_f32(q4[name + ".biases"]))[:, :, None] / 128)
+    o = ora.OracleAR(q4, q8_dims, bf16=True)
+    np.testing.assert_array_equal(o.w[name + ".weight"], deq)
+
+
+def test_4bit_manifest_and_tensor_checks(yar, q8_dir, tmp_path):
+    d = _copy(q8_dir, tmp_path / "m")
+    man = json.load(open(d / "conversion.json"))
+    man["precisions"]["4bit"]["bits"] = 8
+    json.dump(man, open(d / "conversion.json", "w"))
+    with pytest.raises(yar.YarError, match="Invalid affine quantization"):
+        yar.ARModel(str(d), any_dims=True, precision="4bit")
+    d2 = _copy(q8_dir, tmp_path / "m2")
+    # An 8-bit-shaped weight where the 4-bit file must hold [out, in / 8].
+    _rewrite_header(str(d2 / "ar-4bit.safetensors"),
+                    lambda h: h["lm_head.weight"].update(shape=[h["lm_head.weight"]["shape"][0] // 2,
+                                                              2 * h["lm_head.weight"]["shape"][1]]))
+    with pytest.raises(yar.YarError, match="shape/dtype: lm_head.weight"):
+        yar.ARModel(str(d2), any_dims=True, precision="4bit")

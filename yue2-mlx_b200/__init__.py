@@ -31,7 +31,8 @@ OK, FAILURE, INVALID_INPUT, CANCELLED = 0, 1, 2, 130
 PHASES = {"abc": 0, "semantic": 1, None: 2, "full": 2}
 LOAD_ANY_DIMS = 1
 LOAD_8BIT = 2
-PRECISIONS = ("bf16", "8bit")
+LOAD_4BIT = 4
+PRECISIONS = ("bf16", "8bit", "4bit")
 
 EOD, ABC_END, MUSIC_END = 151643, 151848, 151852
 CODEC_OFFSET, CODEC_SIZE, CONTEXT = 151853, 32768, 24576
@@ -170,8 +171,8 @@ def tp_head_slice(width: int, rank: int, world: int) -> tuple[int, int]:
 class ARModel:
     """Converted AR weights resident on one GPU (ARModel, ar.cpp:133-238).
 
-    ``precision`` is the reference's: "bf16" (ar-bf16.safetensors) or "8bit" (affine 8-bit
-    group-64 linears, ar-8bit.safetensors); "4bit" is rejected (not built).
+    ``precision`` is the reference's: "bf16" (ar-bf16.safetensors), "8bit" or "4bit" (affine
+    8- / 4-bit group-64 linears, ar-8bit / ar-4bit.safetensors).
     ``tp=(rank, world, nccl_id)`` loads this rank's tensor-parallel share instead (BF16
     only): its KV-head groups and FFN column block, with NCCL exchanges inside every
     forward. All ranks must then make the same calls with the same arguments."""
@@ -186,9 +187,8 @@ class ARModel:
         else:
             rank, world, nccl_id = tp
             if precision not in PRECISIONS:
-                raise ValueError("precision must be 'bf16' or '8bit'")
-            if precision == "8bit":
-                flags |= LOAD_8BIT
+                raise ValueError("precision must be 'bf16', '8bit', or '4bit'")
+            flags |= {"bf16": 0, "8bit": LOAD_8BIT, "4bit": LOAD_4BIT}[precision]
             if len(nccl_id) != 128:
                 raise ValueError("nccl_id must be the 128 bytes of tp_unique_id()")
             _check(lib.yar_model_load_tp(os.fsencode(path), device, rank, world, bytes(nccl_id), flags,
@@ -202,7 +202,7 @@ class ARModel:
         self.device = device
         b = ctypes.c_int()
         _check(lib.yar_model_precision_bits(h, ctypes.byref(b)))
-        self.precision = "8bit" if b.value == 8 else "bf16"
+        self.precision = {8: "8bit", 4: "4bit"}.get(b.value, "bf16")
 
     def session(self, max_rows: int = 2, max_ctx: int = 4096, page_tokens: int = 256) -> "Session":
         return Session(self, max_rows, max_ctx, page_tokens)

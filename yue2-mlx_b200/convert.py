@@ -11,8 +11,9 @@ holding the AR decoder and the NAR acoustic model together — into the director
 * ``ar-bf16.safetensors``: the AR tensors (embedding, final norm, LM head, and every
   ``model.layers.*`` tensor without ``.nar_``), bytes copied unchanged;
 * ``nar-bf16.safetensors``: every other tensor (the NAR stage's; not used by this engine);
-* ``ar-8bit.safetensors`` when ``precisions`` names "8bit": the linears in affine 8-bit
-  group-64 form (``synth.write_quantized``: the published affine scheme; MLX's own
+* ``ar-8bit.safetensors`` / ``ar-4bit.safetensors`` when ``precisions`` names "8bit" /
+  "4bit": the linears in affine group-64 form (``synth.write_quantized``: the published
+  affine scheme; MLX's own
   quantizer, which the reference calls, is not on this machine, so the 8-bit bytes are
   this build's quantization of the same weights, not the reference's);
 * ``conversion.json``: the schema-1 manifest with one record per precision and the size
@@ -163,8 +164,8 @@ def file_record(path: str) -> dict:
 def prepare_ar(src: str, out_dir: str, precisions=("bf16",), config: dict | None = None,
                any_dims: bool = False) -> str:
     """Write the converted AR directory (see the module docstring); returns ``out_dir``."""
-    if "bf16" not in precisions or any(p not in ("bf16", "8bit") for p in precisions):
-        raise ValueError("precisions: 'bf16', optionally with '8bit'")
+    if "bf16" not in precisions or any(p not in ("bf16", "8bit", "4bit") for p in precisions):
+        raise ValueError("precisions: 'bf16', optionally with '8bit' and '4bit'")
     recs, base = _sources(src)
     if config is None:
         cpath = os.path.join(base, "config.json")
@@ -201,11 +202,11 @@ def prepare_ar(src: str, out_dir: str, precisions=("bf16",), config: dict | None
                                                {"format": "mlx", "partition": "nar", "precision": "bfloat16"})
     manifest_precisions = {"bf16": {"ar": "ar-bf16.safetensors", "nar": "nar-bf16.safetensors",
                                     "dtype": "bfloat16"}}
-    if "8bit" in precisions:
-        synth.write_quantized(out_dir, dims)
-        files["ar-8bit.safetensors"] = file_record(os.path.join(out_dir, "ar-8bit.safetensors"))
-        manifest_precisions["8bit"] = {"ar": "ar-8bit.safetensors", "bits": 8, "group_size": synth.QUANT_GROUP,
-                                       "mode": "affine", "linear_only": True, "embedding_dtype": "bfloat16"}
+    for bits in (8, 4):
+        if f"{bits}bit" in precisions:
+            synth.write_quantized(out_dir, dims, bits=bits)
+            files[f"ar-{bits}bit.safetensors"] = file_record(os.path.join(out_dir, f"ar-{bits}bit.safetensors"))
+            manifest_precisions[f"{bits}bit"] = synth.quantized_record(bits)
     with open(os.path.join(out_dir, "config.json"), "w") as f:
         json.dump(config, f, indent=1)
     files["config.json"] = file_record(os.path.join(out_dir, "config.json"))

@@ -109,9 +109,9 @@ int yar_model_load_precision(const char *dir, const char *precision, int device,
     const std::string p = precision;
     if (p != "bf16" && p != "8bit" && p != "4bit")
       throw yar::Error("ValueError", "precision must be 'bf16', '8bit', or '4bit'");
-    if (p == "4bit") throw yar::Error("ValueError", "4-bit AR weights are not built in this engine");
-    flags &= ~uint32_t(YAR_LOAD_8BIT);
+    flags &= ~uint32_t(YAR_LOAD_8BIT | YAR_LOAD_4BIT);
     if (p == "8bit") flags |= YAR_LOAD_8BIT;
+    if (p == "4bit") flags |= YAR_LOAD_4BIT;
     auto *h = new yar_model{yar::load_model(dir, device, flags)};
     *out = h;
   });

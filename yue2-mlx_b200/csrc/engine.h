@@ -71,7 +71,7 @@ struct Model {
   // down for the persistent decode kernel; null when the shapes do not fit its ring.
   void *d_wmaps = nullptr;
   const float *rope_cos = nullptr, *rope_sin = nullptr;  // [context][head_dim/2], BF16-rounded values
-  // Precision: 0 (BF16 weights) or 8 (affine 8-bit, group 64). With 8 the arena holds the
+  // Precision: 0 (BF16 weights), 8 or 4 (affine, group 64). Quantized, the arena holds the
   // weights dequantized to BF16 (prefill, batched and per-operation decode read them) and
   // `qarena` the stage images the persistent decode kernel streams: per layer (d_qlayers)
   // and per phase of the head (this rank's phase rows; null for a phase the vocabulary
@@ -197,13 +197,14 @@ bool persistent_supported(const Model &m, int n_rows);
 // multiple of 2048.
 void build_stage_maps(Model &m);
 void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase, cudaStream_t st);
-// 8-bit weights at load time (kernels_quant.cu): raw q bytes [rows][K] and BF16 scale /
-// bias bits [rows][K / 64] into BF16 weights, or into a stage image of q8_image_bytes.
-size_t q8_image_bytes(int rows, int K);
-void launch_q8_dequant(const uint8_t *q, const uint16_t *s, const uint16_t *b, long long rows, int K, bf16 *out,
-                       cudaStream_t st);
-void launch_q8_image(const uint8_t *q, const uint16_t *s, const uint16_t *b, int rows, int K, unsigned char *img,
-                     cudaStream_t st);
+// Quantized weights at load time (kernels_quant.cu): raw packed rows [rows][K * bits / 8]
+// (bits 8 or 4) and BF16 scale / bias bits [rows][K / 64] into BF16 weights, or into a
+// stage image of q_image_bytes.
+size_t q_image_bytes(int rows, int K, int bits);
+void launch_q_dequant(const uint8_t *q, const uint16_t *s, const uint16_t *b, long long rows, int K, int bits,
+                      bf16 *out, cudaStream_t st);
+void launch_q_image(const uint8_t *q, const uint16_t *s, const uint16_t *b, int rows, int K, int bits,
+                    unsigned char *img, cudaStream_t st);
 
 enum Epilogue { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2 };
 

@@ -66,7 +66,7 @@ constexpr int kMaxPersistGrid = 256;
 struct PersistParams {
   CUtensorMap head_map;        // stage map of this rank's phase rows of the head (`head`, `head_rows`)
   const CUtensorMap *wmaps;    // device array [layer][4]: stage maps of qkv, o, gu, down
-  // 8-bit weights (the kernel's QB = 8): stage images per layer and of this rank's phase
+  // Quantized weights (the kernel's QB = 8 or 4): stage images per layer and of this rank's phase
   // rows of the head (rows [0, head_rows) as `head`).
   const QLayer *qlayers;
   const unsigned char *qhead;
@@ -297,7 +297,8 @@ struct ProdCursor {
 // at operation boundaries and the ring copies of those stages then hit L2.
 template <int NB, int QB>
 struct Producer {
-  static constexpr bool kQ8 = QB == 8;
+  static constexpr bool kQ8 = QB != 0;  // quantized weights (8 or 4 bits)
+  static constexpr int kQStage = kQ8 ? q_stage_bytes<(QB ? QB : 8)>() : 0;
   const LayerWeights *layers;
   const CUtensorMap *wmaps, *head_map;
   const QLayer *qlayers;
@@ -419,8 +420,8 @@ struct Producer {
       return;
     }
     if (kQ8) {
-      mbar_arrive_expect_tx(bar, unsigned(kQ8StageBytes));
-      bulk_g2s_hint(dst, c.img + (size_t(c.g) * c.KS + c.ks) * kQ8StageBytes, unsigned(kQ8StageBytes), bar, pol);
+      mbar_arrive_expect_tx(bar, unsigned(kQStage));
+      bulk_g2s_hint(dst, c.img + (size_t(c.g) * c.KS + c.ks) * kQStage, unsigned(kQStage), bar, pol);
       return;
     }
     mbar_arrive_expect_tx(bar, unsigned(kRingStageBytes));
@@ -438,21 +439,22 @@ struct Producer {
       return;
     }
     if (kQ8)
-      prefetch_l2(c.img + (size_t(c.g) * c.KS + c.ks) * kQ8StageBytes, unsigned(kQ8StageBytes));
+      prefetch_l2(c.img + (size_t(c.g) * c.KS + c.ks) * kQStage, unsigned(kQStage));
     else
       stage_prefetch(c.map, c.g * 8, c.ks);
   }
 };
 
-// QB: the weights' precision — 0 (BF16, stage-map copies) or 8 (affine 8-bit stage images,
-// ring_consume_q8); everything else is shared.
+// QB: the weights' precision — 0 (BF16, stage-map copies), 8 or 4 (affine 8- or 4-bit stage
+// images, ring_consume_q8); everything else is shared.
 template <int NB, int QB>
 __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const __grid_constant__ PersistParams p) {
   // 1024-byte alignment: the weight stages are 128-byte-swizzled tensor copies.
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  constexpr bool kQ8 = QB == 8;
+  constexpr bool kQ8 = QB != 0;  // quantized weights (8 or 4 bits)
+  constexpr int kBits = QB ? QB : 8;
   constexpr int NS = kQ8 ? kPersistStagesQ8 : kPersistStages;
-  constexpr int kSlot = kQ8 ? kQ8StageBytes : kRingStageBytes;  // bytes of a ring slot
+  constexpr int kSlot = kQ8 ? kQ8StageBytes : kRingStageBytes;  // bytes of a ring slot (a 4-bit stage uses 18,432)
   constexpr int kUrows = kQ8 ? kQ8Rows : 8;                       // weight rows of a stage
   using ASm = AttnTeamSmem<128, 2>;
   // Layout: ring | act (GEMV activations) aliased with the attention teams' scratch (the
@@ -464,9 +466,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
   bf16 *act = reinterpret_cast<bf16 *>(smem_raw + NS * kSlot);
   ASm *team_sm = reinterpret_cast<ASm *>(smem_raw + NS * kSlot);  // attention scratch
   float *gred = reinterpret_cast<float *>(smem_raw + NS * kSlot + kUnion);
-  // 8-bit: the group sums and FP16 factors of the staged rows (q8_stage_chunk).
+  // Quantized: the group sums, FP16 factors and offset shares of the staged rows (q8_stage_chunk).
   __shared__ __align__(16) float s_sumx[kQ8 ? NB * (kPersistMaxK / 64) : 4];
   __shared__ __align__(16) float s_qfac[kQ8 ? NB * (kPersistMaxK / 64) : 4];
+  __shared__ __align__(16) float s_qneg[kQ8 ? NB * (kPersistMaxK / 64) : 4];
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
   __shared__ float red[NB * kRingConsumers];
   __shared__ AttnRow<128> rowst[NB];
@@ -518,6 +521,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
       t.qimg = k == 0 ? q.qkv : k == 1 ? q.o : k == 2 ? q.gu : q.down;
       t.sumx = s_sumx;
       t.qfac = s_qfac;
+      t.qneg = s_qneg;
     }
     if (l == 0 && k == 0 && p.inject_op != op) {
       // The first QKV reads each row's token embedding itself (an inactive row: zeros).
@@ -715,8 +719,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
       bad = true;
     stamp(op_slot, 1);
     if constexpr (kQ8)
-      ring_consume_q8<NB, NS, kPersistMaxK / kRingPiece>(t, g0, g1, ringb, act, full, empty, it, gred, p.error, bad,
-                                                         dead, ctid);
+      ring_consume_q8<NB, NS, kPersistMaxK / kRingPiece, kBits>(t, g0, g1, ringb, act, full, empty, it, gred,
+                                                                p.error, bad, dead, ctid);
     else
       ring_consume<NB, NS, kPersistMaxK / kRingPiece>(t, g0, g1, ring, act, full, empty, it, gred, p.error, bad, dead,
                                                       ctid);
@@ -875,6 +879,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
       head.qimg = p.qhead;
       head.sumx = s_sumx;
       head.qfac = s_qfac;
+      head.qneg = s_qneg;
     }
     int g0, g1;
     stamp(5 * nL, 0);
@@ -884,8 +889,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
       bad = true;
     stamp(5 * nL, 1);
     if constexpr (kQ8)
-      ring_consume_q8<NB, NS, kPersistMaxK / kRingPiece>(head, g0, g1, ringb, act, full, empty, it, gred, p.error,
-                                                         bad, dead, ctid);
+      ring_consume_q8<NB, NS, kPersistMaxK / kRingPiece, kBits>(head, g0, g1, ringb, act, full, empty, it, gred,
+                                                                p.error, bad, dead, ctid);
     else
       ring_consume<NB, NS, kPersistMaxK / kRingPiece>(head, g0, g1, ring, act, full, empty, it, gred, p.error, bad,
                                                       dead, ctid);
@@ -947,18 +952,19 @@ __global__ void __launch_bounds__(kPersistThreads, 1) k_decode_persistent(const 
 
 size_t persistent_smem(int NB, int QB) {
   const size_t act = size_t(NB) * kPersistMaxK * 2, teams = sizeof(AttnTeamSmem<128, 2>);
-  const size_t ring = QB == 8 ? size_t(kPersistStagesQ8) * kQ8StageBytes : size_t(kPersistStages) * kRingStageBytes;
+  const size_t ring = QB ? size_t(kPersistStagesQ8) * kQ8StageBytes : size_t(kPersistStages) * kRingStageBytes;
   return ring + (act > teams ? act : teams) + size_t(ring_gred_floats(NB)) * 4;
 }
 
 // The kernel instance for a row count and precision.
 static const void *persistent_kernel(int n_rows, int bits) {
   if (bits == 8) return n_rows == 1 ? (const void *)k_decode_persistent<1, 8> : (const void *)k_decode_persistent<2, 8>;
+  if (bits == 4) return n_rows == 1 ? (const void *)k_decode_persistent<1, 4> : (const void *)k_decode_persistent<2, 4>;
   return n_rows == 1 ? (const void *)k_decode_persistent<1, 0> : (const void *)k_decode_persistent<2, 0>;
 }
 
 void configure_persistent_kernels() {
-  for (int bits : {0, 8})
+  for (int bits : {0, 8, 4})
     for (int rows = 1; rows <= 2; ++rows)
       YAR_CUDA(cudaFuncSetAttribute(persistent_kernel(rows, bits), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(persistent_smem(rows, bits))));
@@ -994,7 +1000,7 @@ bool persistent_supported(const Model &m, int n_rows) {
     return false;
   // The register split (setmaxnreg) assumes the launch's per-thread registers.
   cudaFuncAttributes fa{};
-  if (m.bits == 8 && (!m.d_qlayers || m.tp_world > 1)) return false;
+  if (m.bits && (!m.d_qlayers || m.tp_world > 1)) return false;
   if (cudaFuncGetAttributes(&fa, persistent_kernel(n_rows, m.bits)) != cudaSuccess ||
       fa.numRegs != kPersistLaunchRegs)
     return false;
@@ -1013,8 +1019,8 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.layers = m.d_layers;
   p.wmaps = static_cast<const CUtensorMap *>(m.d_wmaps);
   p.qlayers = m.d_qlayers;
-  p.qhead = m.bits == 8 ? m.qhead[phase] : nullptr;
-  if (m.bits == 8 && !p.qhead) throw Error("RuntimeError", "no 8-bit head image for this phase");
+  p.qhead = m.bits ? m.qhead[phase] : nullptr;
+  if (m.bits && !p.qhead) throw Error("RuntimeError", "no quantized head image for this phase");
   p.n_layers = d.layers;
   p.H = d.hidden;
   p.QKV = d.qkv_rows();
@@ -1102,7 +1108,7 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   p.ll_limit = s.inject_op > 0 ? (1ll << 16) : (1ll << 22);
   p.prefetch_stages = s.prefetch_stages;
   if (m.sm_count > kMaxPersistGrid) throw Error("RuntimeError", "persistent decode takes at most 256 SMs");
-  attention_ranks(p, m.sm_count, m.bits == 8 ? kQ8Rows : 8);
+  attention_ranks(p, m.sm_count, m.bits ? kQ8Rows : 8);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m.sm_count);
@@ -1117,6 +1123,9 @@ void launch_decode_persistent(const Model &m, Session &s, int n_rows, int phase,
   if (m.bits == 8)
     YAR_CUDA(n_rows == 1 ? cudaLaunchKernelEx(&cfg, k_decode_persistent<1, 8>, p)
                          : cudaLaunchKernelEx(&cfg, k_decode_persistent<2, 8>, p));
+  else if (m.bits == 4)
+    YAR_CUDA(n_rows == 1 ? cudaLaunchKernelEx(&cfg, k_decode_persistent<1, 4>, p)
+                         : cudaLaunchKernelEx(&cfg, k_decode_persistent<2, 4>, p));
   else
     YAR_CUDA(n_rows == 1 ? cudaLaunchKernelEx(&cfg, k_decode_persistent<1, 0>, p)
                          : cudaLaunchKernelEx(&cfg, k_decode_persistent<2, 0>, p));

@@ -4,13 +4,13 @@
 //
 // Checks, in the reference's order and with its error types:
 //   1. conversion.json is a schema-1 manifest with a record for the precision: bf16 names
-//      ar-bf16.safetensors and dtype bfloat16; 8bit names ar-8bit.safetensors with bits 8,
-//      group_size 64, mode affine, linear_only                   (ar.cpp:137-160)
+//      ar-bf16.safetensors and dtype bfloat16; 8bit / 4bit name ar-8bit / ar-4bit
+//      .safetensors with bits 8 / 4, group_size 64, mode affine, linear_only (ar.cpp:137-160)
 //   2. config.json matches the pinned generator config             (ar.cpp:161-192)
 //   3. the AR file holds exactly the AR tensor set with the pinned shapes: BF16, or for
-//      8bit every linear as a U32 [out, in / 4] weight with BF16 [out, in / 64] scales
+//      8bit / 4bit every linear as a U32 [out, in * bits / 32] weight with BF16 [out, in / 64] scales
 //      and biases                                                  (ar.cpp:193-236)
-// 8-bit weights are dequantized on the GPU into the BF16 layout below (prefill and the
+// Quantized weights are dequantized on the GPU into the BF16 layout below (prefill and the
 // batched and per-operation decode paths read it) and also written as the stage images
 // the persistent decode kernel streams (Model::qarena).
 // Device layout (one allocation): per layer the q/k/v rows stacked into one [q+2kv][H]
@@ -191,10 +191,12 @@ TpPlan tp_plan(const Dims &d, int rank, int world) {
 Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_rank, int tp_world,
                   const uint8_t *nccl_id) {
   const bool any_dims = flags & 1u;
-  const int bits = (flags & 2u) ? 8 : 0;  // YAR_LOAD_8BIT: the `8bit` precision
-  const std::string precision = bits ? "8bit" : "bf16";
+  if ((flags & 2u) && (flags & 4u)) throw Error("ValueError", "choose one of 8-bit and 4-bit weights");
+  // YAR_LOAD_8BIT / YAR_LOAD_4BIT: the `8bit` / `4bit` precision.
+  const int bits = (flags & 2u) ? 8 : (flags & 4u) ? 4 : 0;
+  const std::string precision = bits ? std::to_string(bits) + "bit" : "bf16";
   if (tp_world > 1 && !nccl_id) throw Error("ValueError", "tensor parallelism needs an NCCL unique id");
-  if (tp_world > 1 && bits) throw Error("ValueError", "8-bit AR weights are not built for tensor parallelism");
+  if (tp_world > 1 && bits) throw Error("ValueError", "quantized AR weights are not built for tensor parallelism");
   // 1. Manifest.
   Json manifest = read_json(dir + "/conversion.json");
   if (!manifest.is_object() || manifest.value("schema", 0) != 1)
@@ -216,7 +218,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
   // 2. Config.
   const Dims d = config_dims(read_json(dir + "/config.json"), any_dims);
   if (bits && (d.hidden % 64 || d.ffn % 64 || d.qdim() % 64))
-    throw Error("ValueError", "8-bit AR weights need every linear's input width to be a multiple of 64");
+    throw Error("ValueError", "quantized AR weights need every linear's input width to be a multiple of 64");
   // 3. Tensors.
   const std::string path = dir + "/" + filename;
   uint64_t data_start = 0;
@@ -229,7 +231,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     if (it->second.shape != shape || it->second.dtype != dtype)
       throw Error("ValueError", "Incompatible AR tensor shape/dtype: " + name);
   };
-  // A linear layer's tensors (ar.cpp:208-214): the BF16 weight, or the packed 8-bit form.
+  // A linear layer's tensors (ar.cpp:208-214): the BF16 weight, or the packed quantized form.
   auto require_linear = [&](const std::string &n, int64_t out, int64_t in) {
     if (!bits) {
       require(n + ".weight", {out, in});
@@ -311,7 +313,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     char *base = static_cast<char *>(m->arena);
     auto at = [&](size_t o) { return reinterpret_cast<bf16 *>(base + o); };
 
-    // 8-bit: the stage images (m->qarena; only when every K is a multiple of 2048, the
+    // Quantized: the stage images (m->qarena; only when every K is a multiple of 2048, the
     // persistent kernel's stage width) and the raw buffers of one fused matrix (freed when
     // the load ends).
     struct DevBuf {
@@ -336,15 +338,15 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
           return o;
         };
         for (int i = 0; i < d.layers; ++i) {
-          qlo[i].qkv = qtake(q8_image_bytes(Q + 2 * KV, H));
-          qlo[i].o = qtake(q8_image_bytes(H, Q));
-          qlo[i].gu = qtake(q8_image_bytes(2 * F, H));
-          qlo[i].down = qtake(q8_image_bytes(H, F));
+          qlo[i].qkv = qtake(q_image_bytes(Q + 2 * KV, H, bits));
+          qlo[i].o = qtake(q_image_bytes(H, Q, bits));
+          qlo[i].gu = qtake(q_image_bytes(2 * F, H, bits));
+          qlo[i].down = qtake(q_image_bytes(H, F, bits));
         }
         const bool pinned_vocab = V == 184704;  // the protocol phases; otherwise the whole vocabulary
         for (int ph : {kPhaseAbc, kPhaseSemantic, kPhaseFull}) {
           if ((ph == kPhaseFull) == pinned_vocab) continue;
-          qh_off[ph] = qtake(q8_image_bytes(phase_rows(d, ph).n_main, H));
+          qh_off[ph] = qtake(q_image_bytes(phase_rows(d, ph).n_main, H, bits));
         }
         m->qarena_bytes = qoff;
         YAR_CUDA(cudaMalloc(&m->qarena, qoff));
@@ -438,7 +440,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
         buf ^= 1;
       }
     };
-    // 8-bit: whole rows of a tensor into device memory with a destination row pitch (the
+    // Quantized: whole rows of a tensor into device memory with a destination row pitch (the
     // rows of one fused matrix: q/k/v stacked, gate/up interleaved).
     auto upload_rows = [&](const std::string &name, int64_t row0, int64_t nrows, char *dst, size_t dst_pitch) {
       const TensorRec &r = recs.at(name);
@@ -459,15 +461,16 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     // A linear's q bytes, scales and biases (rows [row0, row0 + nrows)) into the raw
     // buffers at fused row `dst_row`, every `stride`-th row.
     auto upload_q8 = [&](const std::string &lin, int64_t row0, int64_t nrows, int K, int64_t dst_row, int stride) {
-      const size_t qrow = size_t(K), srow = size_t(K / 64) * 2;
+      const size_t qrow = size_t(K) * bits / 8, srow = size_t(K / 64) * 2;
       upload_rows(lin + ".weight", row0, nrows, raw_q + size_t(dst_row) * qrow, stride * qrow);
       upload_rows(lin + ".scales", row0, nrows, reinterpret_cast<char *>(raw_s) + size_t(dst_row) * srow, stride * srow);
       upload_rows(lin + ".biases", row0, nrows, reinterpret_cast<char *>(raw_b) + size_t(dst_row) * srow, stride * srow);
     };
     // The raw fused matrix (N x K) into BF16 weights at `dst` and a stage image at `img`.
     auto finish_q8 = [&](int N, int K, char *dst, unsigned char *img) {
-      launch_q8_dequant(reinterpret_cast<const uint8_t *>(raw_q), raw_s, raw_b, N, K, reinterpret_cast<bf16 *>(dst), st);
-      if (img) launch_q8_image(reinterpret_cast<const uint8_t *>(raw_q), raw_s, raw_b, N, K, img, st);
+      launch_q_dequant(reinterpret_cast<const uint8_t *>(raw_q), raw_s, raw_b, N, K, bits, reinterpret_cast<bf16 *>(dst),
+                       st);
+      if (img) launch_q_image(reinterpret_cast<const uint8_t *>(raw_q), raw_s, raw_b, N, K, bits, img, st);
       // The raw buffers are refilled next: wait for these kernels (and the copies before).
       YAR_CUDA(cudaStreamSynchronize(st));
       pending[0] = pending[1] = false;
@@ -482,8 +485,9 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
       for (int ph = 0; ph < 3; ++ph) {
         if (!qbase || qh_off[ph] == SIZE_MAX) continue;
         const PhaseRows pr = phase_rows(d, ph);
-        launch_q8_image(reinterpret_cast<const uint8_t *>(raw_q) + size_t(pr.row0) * H, raw_s + size_t(pr.row0) * (H / 64),
-                        raw_b + size_t(pr.row0) * (H / 64), pr.n_main, H, qbase + qh_off[ph], st);
+        launch_q_image(reinterpret_cast<const uint8_t *>(raw_q) + size_t(pr.row0) * H * bits / 8,
+                       raw_s + size_t(pr.row0) * (H / 64), raw_b + size_t(pr.row0) * (H / 64), pr.n_main, H, bits,
+                       qbase + qh_off[ph], st);
         m->qhead[ph] = qbase + qh_off[ph];
       }
       YAR_CUDA(cudaStreamSynchronize(st));
@@ -492,7 +496,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     m->layers.resize(d.layers);
     for (int i = 0; i < d.layers; ++i) {
       const std::string n = "model.layers." + std::to_string(i), a = n + ".self_attn";
-      if (bits) {  // one GPU (8-bit weights are not built for tensor parallelism)
+      if (bits) {  // one GPU (quantized weights are not built for tensor parallelism)
         upload_q8(a + ".q_proj", 0, Q, H, 0, 1);
         upload_q8(a + ".k_proj", 0, KV, H, Q, 1);
         upload_q8(a + ".v_proj", 0, KV, H, Q + KV, 1);

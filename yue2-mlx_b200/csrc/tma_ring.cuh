@@ -74,7 +74,7 @@ struct GemvTask {
   // its values and the power-of-two factor of its FP16 copy. With `sumx` set the staging
   // fills both and leaves the rows in `act` as FP16 (q8_stage_chunk).
   const unsigned char *qimg = nullptr;
-  float *sumx = nullptr, *qfac = nullptr;
+  float *sumx = nullptr, *qfac = nullptr, *qneg = nullptr;
 };
 
 // Host: W's stage map ({64, N, K/64} view, {64, 8, 32} box, 128-byte swizzle) into `map`.
@@ -309,11 +309,13 @@ __device__ __forceinline__ void ring_norm_w_load(const GemvTask &t, uint4 (&wn)[
 // its rewrite to FP16. A 64-column group's 8 chunks sit at 8 consecutive lanes (lanes
 // 8m..8m+7, k = 64 G + 8 (lane & 7)); every lane of the warp takes part. The lanes add the
 // chunk's BF16 values in FP32 (sum(x): the bias term) and take their largest magnitude m;
-// lane 8m stores the sum at sums[G] and the group's factor f = 2^e at facs[G], e >= 0 the
-// least with m / f < 2^15. Each lane then rewrites its chunk as the FP16 values x / f:
+// lane 8m stores the sum at sums[G], the group's factor f = 2^e at facs[G] (e >= 0 the least
+// with m / f < 2^15) and -1024 sum / f at negs[G] (the weights enter the MMAs offset by 1024:
+// this starts a group's accumulator at minus that offset's share). Each lane then rewrites
+// its chunk as the FP16 values x / f:
 // exact (a power-of-two scale of a BF16 value, whose 8-bit significand FP16's 11 bits
 // hold), except below 2^-14 f where FP16 is subnormal and rounds to a multiple of 2^-24 f.
-__device__ __forceinline__ void q8_stage_chunk(bf16 *row, float *sums, float *facs, int k, int lane) {
+__device__ __forceinline__ void q8_stage_chunk(bf16 *row, float *sums, float *facs, float *negs, int k, int lane) {
   const uint4 x = act_load_chunk(row, k);
   const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
   float s = 0.f, m = 0.f;
@@ -341,6 +343,7 @@ __device__ __forceinline__ void q8_stage_chunk(bf16 *row, float *sums, float *fa
   if ((lane & 7) == 0) {
     sums[k >> 6] = s;
     facs[k >> 6] = __int_as_float((127 + e) << 23);
+    negs[k >> 6] = -1024.f * s * inv;  // exact scalings of s by powers of two
   }
 }
 
@@ -474,7 +477,7 @@ __device__ bool ring_stage_act(const GemvTask &t, bf16 *act, float *red, int cti
       for (int j = 0; j < MC; ++j) {
         const int k = (ctid + j * T) * 8;
         if (k >= K) continue;  // warp-uniform: K is a multiple of 2048
-        q8_stage_chunk(act + b * K, t.sumx + b * KG, t.qfac + b * KG, k, lane);
+        q8_stage_chunk(act + b * K, t.sumx + b * KG, t.qfac + b * KG, t.qneg + b * KG, k, lane);
       }
   }
   if (!t.in_ll) {
@@ -543,7 +546,7 @@ __device__ bool ll_stage_warp(const GemvTask &t, bf16 *act, int lane, int warp, 
       for (int ks = 0; ks < MC; ++ks) {
         if (ks >= KS) continue;
         const int k = ks * kRingPiece + warp * 256 + lane * 8;
-        q8_stage_chunk(act + size_t(b) * t.K, t.sumx + b * KG, t.qfac + b * KG, k, lane);
+        q8_stage_chunk(act + size_t(b) * t.K, t.sumx + b * KG, t.qfac + b * KG, t.qneg + b * KG, k, lane);
       }
   }
   return true;
@@ -775,16 +778,28 @@ __device__ void ring_consume(const GemvTask &t, int g0, int g1, const bf16 *ring
 constexpr int kQ8Rows = 16;
 constexpr int kQ8QBytes = kQ8Rows * kRingPiece;                         // 32 KB of 8-bit weights
 constexpr int kQ8StageBytes = kQ8QBytes + kQ8Rows * (kRingPiece / 64) * 4;  // + scale/bias words: 34,816
-
-// Two 8-bit weights (the bytes of w that selector `sel` picks) as an FP16 pair: each byte
-// q placed under the exponent byte 0x64 is the FP16 value 1024 + q (ulp 1 in [1024,
-// 2048)), and one packed subtraction of 1024 leaves q exactly.
-__device__ __forceinline__ uint32_t q8_f16x2(uint32_t w, uint32_t sel) {
-  const uint32_t v = __byte_perm(w, 0x64646464u, sel);
-  uint32_t r;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(0x64006400u));
-  return r;
+// 4-bit weights (the `4bit` precision) use the same units and scale/bias words with half
+// the weight bytes: lane (g, t)'s 16 bytes of warp w's group j sit at ((w * 4 + j) * 32 +
+// lane) * 16, one word per k-tile kt holding the eight nibbles of its A fragments — a0
+// (row g, columns 2t, 2t + 1), a1 (row g + 8, same columns), a2 (row g, 2t + 8, 2t + 9),
+// a3 (row g + 8, same) — fragment s's even column in bits 4s..4s+3 and its odd column in
+// bits 16 + 4s..16 + 4s + 3.
+constexpr int kQ4QBytes = kQ8Rows * kRingPiece / 2;                     // 16 KB of 4-bit weights
+constexpr int kQ4StageBytes = kQ4QBytes + kQ8Rows * (kRingPiece / 64) * 4;  // 18,432
+template <int BITS>
+__host__ __device__ constexpr int q_stage_bytes() {
+  return BITS == 8 ? kQ8StageBytes : kQ4StageBytes;
 }
+
+// Two 8-bit weights (the bytes of w that selector `sel` picks) as an FP16 pair offset by
+// 1024: each byte q placed under the exponent byte 0x64 is the FP16 value 1024 + q (ulp 1 in
+// [1024, 2048)). The offset is not subtracted per weight: a group's accumulator starts at
+// -1024 sum(x) instead (q8_stage_chunk's negs).
+__device__ __forceinline__ uint32_t q8_f16x2(uint32_t w, uint32_t sel) { return __byte_perm(w, 0x64646464u, sel); }
+// Two 4-bit weights as an FP16 pair offset by 1024: the nibbles at bits 0..3 and 16..19 of
+// w under exponent 0x64 are 1024 + n; with mask 0x00F000F0 (bits 4..7, 20..23) they are
+// 1024 + 16 n, exact as well (ulp 1 below 2048), so two fragments per word need no shift.
+__device__ __forceinline__ uint32_t q4_f16x2(uint32_t w, uint32_t mask) { return (w & mask) | 0x64006400u; }
 // m16n8k16, FP16 operands, FP32 accumulators (no side effects: the compiler may schedule
 // it among independent work).
 __device__ __forceinline__ void mma_f16_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -800,17 +815,26 @@ __device__ __forceinline__ void q8_mma_tile(float *c, uint32_t wg, uint32_t wg8,
   mma_f16_16816(c, q8_f16x2(wg, 0x4140u), q8_f16x2(wg8, 0x4140u), q8_f16x2(wg, 0x4342u), q8_f16x2(wg8, 0x4342u), b0,
                 b1);
 }
+// The same k-tile from one 4-bit word (fragments a0..a3 at nibble offsets 0, 4, 8, 12). Rows
+// g + 8 (a1, a3: the upper nibble of each byte pair) enter as 1024 + 16 q, so their sums
+// come out as 16 sum(x q) on top of the offset: the caller scales them by 1/16.
+__device__ __forceinline__ void q4_mma_tile(float *c, uint32_t w, uint32_t b0, uint32_t b1) {
+  const uint32_t w8 = w >> 8;
+  mma_f16_16816(c, q4_f16x2(w, 0x000F000Fu), q4_f16x2(w, 0x00F000F0u), q4_f16x2(w8, 0x000F000Fu),
+                q4_f16x2(w8, 0x00F000F0u), b0, b1);
+}
 
-// Consumers of an 8-bit task: 16-row units [u0, u1), each K / 2048 stages (continuing
-// `it`). The staging left the activation rows as FP16 with a power-of-two factor f per
-// 64-column group (q8_stage_chunk). Warp w runs its 256 columns of every stage: per
-// 64-column group, four MMAs (16 weight rows as exact FP16 integers x the activation rows)
-// in two independent chains give sum(x q) / f per row, and the group adds
-// (scale f) * that + bias * sum(x) in FP32 — the affine dequantization of every weight
-// folded into two FMAs per output. Partial sums go to gred as ring_consume's, two 8-row
-// groups per unit, and the same epilogue follows (ring_epilogue). Failure handling is
-// ring_consume's.
-template <int NB, int NS, int MC = kStageChunks>
+// Consumers of a quantized task (BITS 8 or 4): 16-row units [u0, u1), each K / 2048 stages
+// (continuing `it`; 8-bit stages fill a kQ8StageBytes slot, 4-bit ones kQ4StageBytes of it).
+// The staging left the activation rows as FP16 with a power-of-two factor f per 64-column
+// group (q8_stage_chunk). Warp w runs its 256 columns of every stage: per 64-column group,
+// four MMAs (16 weight rows as FP16 integers offset by 1024 x the activation rows) in two
+// independent chains, the first started at -1024 sum(x / f), give sum(x q) / f per row, and
+// the group adds (scale f) * that + bias * sum(x) in FP32 — the affine dequantization of
+// every weight folded into two FMAs per output. Partial sums go to gred as ring_consume's,
+// two 8-row groups per unit, and the same epilogue follows (ring_epilogue). Failure
+// handling is ring_consume's.
+template <int NB, int NS, int MC = kStageChunks, int BITS = 8>
 __device__ void ring_consume_q8(const GemvTask &t, int u0, int u1, const unsigned char *ring, bf16 *act,
                                 uint64_t *full, uint64_t *empty, long long &it, float *gred, int *error, bool &bad,
                                 bool &dead, int ctid) {
@@ -841,20 +865,24 @@ __device__ void ring_consume_q8(const GemvTask &t, int u0, int u1, const unsigne
           }
         }
         if (!bad) {
-          const unsigned char *st = ring + size_t(s) * kQ8StageBytes;
+          const unsigned char *st = ring + size_t(s) * kQ8StageBytes;  // slots of kQ8StageBytes
+          constexpr int kQB = BITS == 8 ? kQ8QBytes : kQ4QBytes;
           const bf16 *ar = act + size_t(ks) * kRingPiece;
           // Group sums and factors of activation rows 2 tq, 2 tq + 1 for the warp's 4 groups.
           float4 sx[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
           float4 fx[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+          float4 nx[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
 #pragma unroll
           for (int e = 0; e < 2; ++e)
             if (2 * tq + e < NB) {
               const int o = (2 * tq + e) * KG + ks * 32 + warp * 4;
               sx[e] = *reinterpret_cast<const float4 *>(t.sumx + o);
               fx[e] = *reinterpret_cast<const float4 *>(t.qfac + o);
+              nx[e] = *reinterpret_cast<const float4 *>(t.qneg + o);
             }
           const float sx0[4] = {sx[0].x, sx[0].y, sx[0].z, sx[0].w}, sx1[4] = {sx[1].x, sx[1].y, sx[1].z, sx[1].w};
           const float fx0[4] = {fx[0].x, fx[0].y, fx[0].z, fx[0].w}, fx1[4] = {fx[1].x, fx[1].y, fx[1].z, fx[1].w};
+          const float nx0[4] = {nx[0].x, nx[0].y, nx[0].z, nx[0].w}, nx1[4] = {nx[1].x, nx[1].y, nx[1].z, nx[1].w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int k0 = warp * 256 + j * 64;
@@ -863,15 +891,26 @@ __device__ void ring_consume_q8(const GemvTask &t, int u0, int u1, const unsigne
               x01 = *reinterpret_cast<const uint4 *>(ar + size_t(g) * K + k0 + tq * 8);
               x23 = *reinterpret_cast<const uint4 *>(ar + size_t(g) * K + k0 + 32 + tq * 8);
             }
-            const uint4 *qp = reinterpret_cast<const uint4 *>(st + ((warp * 4 + j) * 64 + lane) * 16);
-            const uint4 q01 = qp[0], q23 = qp[32];
-            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-            q8_mma_tile(c0, q01.x, q01.y, x01.x, x01.y);
-            q8_mma_tile(c1, q23.x, q23.y, x23.x, x23.y);
-            q8_mma_tile(c0, q01.z, q01.w, x01.z, x01.w);
-            q8_mma_tile(c1, q23.z, q23.w, x23.z, x23.w);
-            const uint2 sb = *reinterpret_cast<const uint2 *>(st + kQ8QBytes + ((warp * 4 + j) * 16 + 2 * g) * 4);
-            const float s_g = bf_lo(sb.x), b_g = bf_hi(sb.x), s_g8 = bf_lo(sb.y), b_g8 = bf_hi(sb.y);
+            // c0 starts at the offset's share (-1024 sum(x / f) per activation row), c1 at 0.
+            float c0[4] = {nx0[j], nx1[j], nx0[j], nx1[j]}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (BITS == 8) {
+              const uint4 *qp = reinterpret_cast<const uint4 *>(st + ((warp * 4 + j) * 64 + lane) * 16);
+              const uint4 q01 = qp[0], q23 = qp[32];
+              q8_mma_tile(c0, q01.x, q01.y, x01.x, x01.y);
+              q8_mma_tile(c1, q23.x, q23.y, x23.x, x23.y);
+              q8_mma_tile(c0, q01.z, q01.w, x01.z, x01.w);
+              q8_mma_tile(c1, q23.z, q23.w, x23.z, x23.w);
+            } else {
+              const uint4 qv = *reinterpret_cast<const uint4 *>(st + ((warp * 4 + j) * 32 + lane) * 16);
+              q4_mma_tile(c0, qv.x, x01.x, x01.y);
+              q4_mma_tile(c1, qv.z, x23.x, x23.y);
+              q4_mma_tile(c0, qv.y, x01.z, x01.w);
+              q4_mma_tile(c1, qv.w, x23.z, x23.w);
+            }
+            const uint2 sb = *reinterpret_cast<const uint2 *>(st + kQB + ((warp * 4 + j) * 16 + 2 * g) * 4);
+            // 4 bits: rows g + 8 came out as 16 sum(x q) (q4_mma_tile); 1/16 is exact.
+            const float s_g = bf_lo(sb.x), b_g = bf_hi(sb.x), b_g8 = bf_hi(sb.y);
+            const float s_g8 = BITS == 8 ? bf_lo(sb.y) : bf_lo(sb.y) * 0.0625f;
             acc[0] = fmaf(s_g * fx0[j], c0[0] + c1[0], fmaf(b_g, sx0[j], acc[0]));
             acc[1] = fmaf(s_g * fx1[j], c0[1] + c1[1], fmaf(b_g, sx1[j], acc[1]));
             acc[2] = fmaf(s_g8 * fx0[j], c0[2] + c1[2], fmaf(b_g8, sx0[j], acc[2]));

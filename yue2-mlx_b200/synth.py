@@ -8,12 +8,13 @@ the layout ``lyra prepare`` produces for the AR partition and which ``ARModel`` 
 * ``config.json``      — the generator config (conversion.cpp:203-221);
 * ``conversion.json``  — schema-1 manifest with a ``precisions.bf16`` record;
 * ``ar-bf16.safetensors`` — the AR tensors only, BF16, row-major ``[out, in]``;
-* ``ar-8bit.safetensors`` (``precisions=("bf16", "8bit")``) — the same tensors with every
-  linear weight (q/k/v/o, gate/up/down, LM head; not the embedding) in affine 8-bit
-  group-64 form, as ``lyra prepare`` writes it (conversion.py:596-620, :651-735): the
-  packed ``.weight`` as U32 ``[out, in / 4]`` (element 4i + j in bits 8j..8j+7 of word
-  i, so the words' little-endian bytes are the elements in order) and BF16 ``.scales`` /
-  ``.biases`` ``[out, in / 64]``; ``w ~= scale * q + bias`` per 64-column group.
+* ``ar-8bit.safetensors`` / ``ar-4bit.safetensors`` (``precisions`` naming "8bit" /
+  "4bit") — the same tensors with every linear weight (q/k/v/o, gate/up/down, LM head;
+  not the embedding) in affine group-64 form, as ``lyra prepare`` writes it
+  (conversion.py:596-620, :651-735): the packed ``.weight`` as U32 ``[out, in * bits / 32]``
+  (element (32 / bits) i + j in bits (bits j).. of word i; at 8 bits the words'
+  little-endian bytes are the elements in order) and BF16 ``.scales`` / ``.biases``
+  ``[out, in / 64]``; ``w ~= scale * q + bias`` per 64-column group.
 
 Weights: every matrix (embedding and LM head included) is N(0, std) with std 0.02,
 drawn with numpy's PCG64 ``standard_normal`` in float32, multiplied by float32(std) and
@@ -182,25 +183,41 @@ def linear_names(dims: Dims) -> list[str]:
     return [name for name, shape in tensor_specs(dims) if len(shape) == 2 and name != "model.embed_tokens.weight"]
 
 
-def quantize_affine8(w: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
-    """Affine 8-bit group-64 quantization of a float32 ``[rows, cols]`` matrix, after the
-    published scheme of ``mlx.core.quantize`` (mode "affine"; MLX 0.32.2 is the version
-    conversion.py:31 pins): per 64-column group, scale = (max - min) / 255 (at least 1e-7)
-    and bias = min, each stored as BF16, and q = round((w - bias) / scale) in [0, 255],
-    formed with the stored values. Returns (q uint8, scale bits, bias bits)."""
+def quantize_affine(w: np.ndarray, bits: int = 8) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Affine group-64 quantization of a float32 ``[rows, cols]`` matrix to ``bits`` (8 or
+    4), after the published scheme of ``mlx.core.quantize`` (mode "affine"; MLX 0.32.2 is
+    the version conversion.py:31 pins): per 64-column group, scale = (max - min) / (2^bits
+    - 1) (at least 1e-7) and bias = min, each stored as BF16, and q = round((w - bias) /
+    scale) in [0, 2^bits - 1], formed with the stored values. Returns (q uint8 [rows, cols],
+    scale bits, bias bits)."""
+    top = (1 << bits) - 1
     rows, cols = w.shape
     g = np.asarray(w, dtype=np.float32).reshape(rows, cols // QUANT_GROUP, QUANT_GROUP)
     lo, hi = g.min(axis=2), g.max(axis=2)
-    scale = np.maximum((hi - lo) / np.float32(255.0), np.float32(1e-7)).astype(np.float32)
+    scale = np.maximum((hi - lo) / np.float32(top), np.float32(1e-7)).astype(np.float32)
     s_bits, b_bits = f32_to_bf16_bits(scale), f32_to_bf16_bits(lo)
     s = bf16_bits_to_f32(s_bits)[:, :, None]
     b = bf16_bits_to_f32(b_bits)[:, :, None]
-    q = np.clip(np.rint((g - b) / s), 0, 255).astype(np.uint8).reshape(rows, cols)
+    q = np.clip(np.rint((g - b) / s), 0, top).astype(np.uint8).reshape(rows, cols)
     return q, s_bits, b_bits
 
 
-def _q8_layout(d: Dims):
-    """Header of ar-8bit.safetensors: the BF16 file's tensors in the same order, every
+def quantize_affine8(w: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    return quantize_affine(w, 8)
+
+
+def pack_words(q: np.ndarray, bits: int) -> np.ndarray:
+    """The U32 words of ``q`` [rows, cols] at ``bits`` per element: element (32 / bits) i + j
+    in bits (bits j)..(bits j + bits - 1) of word i; as little-endian bytes."""
+    rows, cols = q.shape
+    if bits == 8:
+        return np.ascontiguousarray(q, dtype=np.uint8).view(np.uint32)
+    n = q.astype(np.uint32).reshape(rows, cols // 8, 8)
+    return (n << (np.arange(8, dtype=np.uint32) * np.uint32(4))).sum(axis=2, dtype=np.uint32)
+
+
+def _q_layout(d: Dims, bits: int):
+    """Header of ar-<bits>bit.safetensors: the BF16 file's tensors in the same order, every
     linear as ``.weight`` (U32), ``.scales`` and ``.biases`` (BF16)."""
     linear = set(linear_names(d))
     header, off, parts = {}, 0, []
@@ -210,7 +227,7 @@ def _q8_layout(d: Dims):
             if inp % QUANT_GROUP:  # conversion.py:610-611
                 raise ValueError(f"Linear weight cannot use group-64 quantization: {name}")
             prefix = name[: -len("weight")]
-            items = [(name, "U32", [out, inp // 4], out * inp),
+            items = [(name, "U32", [out, inp * bits // 32], out * inp * bits // 8),
                      (prefix + "scales", "BF16", [out, inp // QUANT_GROUP], out * inp // QUANT_GROUP * 2),
                      (prefix + "biases", "BF16", [out, inp // QUANT_GROUP], out * inp // QUANT_GROUP * 2)]
         else:
@@ -219,14 +236,14 @@ def _q8_layout(d: Dims):
             header[key] = {"dtype": dtype, "shape": shp, "data_offsets": [off, off + n]}
             off += n
         parts.append((name, shape, name in linear))
-    header["__metadata__"] = {"format": "mlx", "partition": "ar", "precision": "8bit"}
+    header["__metadata__"] = {"format": "mlx", "partition": "ar", "precision": f"{bits}bit"}
     raw = json.dumps(header, separators=(",", ":")).encode()
     raw += b" " * ((8 - (len(raw) % 8)) % 8)
     return parts, header, raw
 
 
-def _q8_job(args):
-    src, dst, data_start, header, name, shape, is_linear, r0, r1 = args
+def _q_job(args):
+    src, dst, data_start, header, name, shape, is_linear, r0, r1, qbits = args
     bits = read_safetensors(src)[name]
     mm = np.memmap(dst, dtype=np.uint8, mode="r+")
     if not is_linear:
@@ -234,11 +251,12 @@ def _q8_job(args):
         view = np.ascontiguousarray(bits).view(np.uint8).reshape(-1)
         mm[data_start + b:data_start + b + view.size] = view
     else:
-        q, sb, bb = quantize_affine8(bf16_bits_to_f32(bits[r0:r1]))
+        q, sb, bb = quantize_affine(bf16_bits_to_f32(bits[r0:r1]), qbits)
+        words = pack_words(q, qbits).view(np.uint8).reshape(-1)
         cols = shape[1]
         prefix = name[: -len("weight")]
-        b = header[name]["data_offsets"][0] + r0 * cols
-        mm[data_start + b:data_start + b + q.size] = q.reshape(-1)
+        b = header[name]["data_offsets"][0] + r0 * cols * qbits // 8
+        mm[data_start + b:data_start + b + words.size] = words
         for key, arr in ((prefix + "scales", sb), (prefix + "biases", bb)):
             b = header[key]["data_offsets"][0] + r0 * (cols // QUANT_GROUP) * 2
             v = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
@@ -247,12 +265,20 @@ def _q8_job(args):
     del mm
 
 
-def write_quantized(directory: str, dims: Dims, workers: int | None = None) -> str:
-    """ar-8bit.safetensors from the directory's ar-bf16.safetensors (the BF16 weights are
-    the source, as in conversion.py:651-735)."""
-    parts, header, raw = _q8_layout(dims)
+def quantized_record(bits: int) -> dict:
+    """The manifest record conversion.py:754-761 writes for a quantized precision."""
+    return {"ar": f"ar-{bits}bit.safetensors", "bits": bits, "group_size": QUANT_GROUP, "mode": "affine",
+            "linear_only": True, "embedding_dtype": "bfloat16"}
+
+
+def write_quantized(directory: str, dims: Dims, workers: int | None = None, bits: int = 8) -> str:
+    """ar-<bits>bit.safetensors (bits 8 or 4) from the directory's ar-bf16.safetensors (the
+    BF16 weights are the source, as in conversion.py:651-735)."""
+    if bits not in (8, 4):
+        raise ValueError("bits must be 8 or 4")
+    parts, header, raw = _q_layout(dims, bits)
     src = os.path.join(directory, "ar-bf16.safetensors")
-    dst = os.path.join(directory, "ar-8bit.safetensors")
+    dst = os.path.join(directory, f"ar-{bits}bit.safetensors")
     data_start = 8 + len(raw)
     total = data_start + max(v["data_offsets"][1] for k, v in header.items() if k != "__metadata__")
     with open(dst, "wb") as f:
@@ -262,19 +288,19 @@ def write_quantized(directory: str, dims: Dims, workers: int | None = None) -> s
     jobs = []
     for name, shape, is_linear in parts:
         if not is_linear:
-            jobs.append((src, dst, data_start, header, name, shape, False, 0, 0))
+            jobs.append((src, dst, data_start, header, name, shape, False, 0, 0, bits))
             continue
         step = max(16, (1 << 23) // shape[1])
         for r0 in range(0, shape[0], step):
-            jobs.append((src, dst, data_start, header, name, shape, True, r0, min(shape[0], r0 + step)))
+            jobs.append((src, dst, data_start, header, name, shape, True, r0, min(shape[0], r0 + step), bits))
     workers = workers or min(32, os.cpu_count() or 1)
     if workers > 1 and len(jobs) > 1:
         with ThreadPoolExecutor(max_workers=workers) as pool:
-            for _ in pool.map(_q8_job, jobs):
+            for _ in pool.map(_q_job, jobs):
                 pass
     else:
         for j in jobs:
-            _q8_job(j)
+            _q_job(j)
     return dst
 
 
@@ -282,9 +308,9 @@ def write_converted(directory: str, dims: Dims = PINNED, seed: int = 0, std: flo
                     norm_std: float = 0.0, workers: int | None = None,
                     precisions: tuple[str, ...] = ("bf16",)) -> str:
     """Write config.json, conversion.json and ar-bf16.safetensors under ``directory``
-    (and ar-8bit.safetensors when ``precisions`` names "8bit")."""
-    if any(p not in ("bf16", "8bit") for p in precisions) or "bf16" not in precisions:
-        raise ValueError("precisions: 'bf16', optionally with '8bit'")
+    (and ar-8bit / ar-4bit.safetensors when ``precisions`` names "8bit" / "4bit")."""
+    if any(p not in ("bf16", "8bit", "4bit") for p in precisions) or "bf16" not in precisions:
+        raise ValueError("precisions: 'bf16', optionally with '8bit' and '4bit'")
     os.makedirs(directory, exist_ok=True)
     specs, header, raw = _layout(dims)
     path = os.path.join(directory, "ar-bf16.safetensors")
@@ -324,11 +350,10 @@ def write_converted(directory: str, dims: Dims = PINNED, seed: int = 0, std: flo
                 "precisions": {"bf16": {"ar": "ar-bf16.safetensors", "nar": "nar-bf16.safetensors",
                                         "dtype": "bfloat16"}},
                 "files": {}}
-    if "8bit" in precisions:
-        write_quantized(directory, dims, workers)
-        # The record conversion.py:754-761 writes for a quantized precision.
-        manifest["precisions"]["8bit"] = {"ar": "ar-8bit.safetensors", "bits": 8, "group_size": QUANT_GROUP,
-                                          "mode": "affine", "linear_only": True, "embedding_dtype": "bfloat16"}
+    for bits in (8, 4):
+        if f"{bits}bit" in precisions:
+            write_quantized(directory, dims, workers, bits)
+            manifest["precisions"][f"{bits}bit"] = quantized_record(bits)
     with open(os.path.join(directory, "conversion.json"), "w") as f:
         json.dump(manifest, f, indent=1)
     return directory
