@@ -136,7 +136,11 @@ int yar_session_free(yar_session *session);
  * 32 KB stages per SM the persistent kernel pulls into L2 ahead of its shared-memory ring
  * (its lookahead while the step waits at operation boundaries). */
 enum { YAR_OPT_PERSISTENT = 1, YAR_OPT_TRACE = 2, YAR_OPT_PREFETCH_STAGES = 3, YAR_OPT_MAX_SPLITS = 4,
-       YAR_OPT_LAYER_DUMP = 5, YAR_OPT_FAULT_INJECT = 6 };
+       YAR_OPT_LAYER_DUMP = 5, YAR_OPT_FAULT_INJECT = 6, YAR_OPT_PREFILL_ATTN_TC = 7 };
+/* YAR_OPT_PREFILL_ATTN_TC (default 1): prefill attention for head_dim 128 on tcgen05 tensor
+ * cores with TMEM accumulators and TMA-fed K/V; 0 selects the mma.sync kernel (the same
+ * quotient; the two differ by rounding: summation order, exp2 of log2-scaled scores and a
+ * running maximum raised in steps on the tcgen05 side). */
 /* YAR_OPT_MAX_SPLITS (default 0 = automatic, else 1..32): the number of splits each (row,
  * kv head) of the decode attention is cut into at most — 1 puts a row's whole context in
  * one unit (the longest chain of chunks), for parity tests of the split-KV rescaling.

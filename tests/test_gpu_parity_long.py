@@ -221,8 +221,13 @@ def test_pinned_3b_config2_capture_vs_upstream(yar, pinned, golden):
         max_abs, rel = _bound(meta["oracle_vs_upstream"][phase], (0.0625, 0.01))
         assert np.abs(ours - ref).max() <= max_abs, phase
         assert rel_l2(ours, ref) <= rel, phase
+        # Greedy choices must agree where upstream's top-1/top-2 margin exceeds twice the
+        # measured radius between two valid implementations: below that either order is
+        # within the logit bound (row 0 of the ABC rows has margin 0.078 against a 0.19
+        # radius, and the mma.sync and tcgen05 prefill attentions pick differently there).
         srt = np.sort(ref, axis=1)
-        sure = srt[:, -1] - srt[:, -2] > 0.05
+        sure = srt[:, -1] - srt[:, -2] > 2 * meta["oracle_vs_upstream"][phase]["max_abs"]
+        assert sure.any(), phase
         assert (np.argmax(ours, 1)[sure] == np.argmax(ref, 1)[sure]).all(), phase
         if phase == "semantic":
             sel = g["kv_positions"]

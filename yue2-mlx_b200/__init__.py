@@ -295,6 +295,10 @@ class Session:
         """L2 prefetch distance of the persistent decode kernel, in 32 KB stages per SM."""
         _check(lib.yar_session_set_option(self._h, 3, int(n)))
 
+    def set_prefill_attention_tc(self, on: bool):
+        """Prefill attention (head_dim 128) on tcgen05 tensor cores (default) or, off, the mma.sync kernel."""
+        _check(lib.yar_session_set_option(self._h, 7, int(bool(on))))
+
     def set_max_splits(self, n: int):
         """Cap the decode attention's splits per (row, kv head); 0 restores the automatic plan."""
         _check(lib.yar_session_set_option(self._h, 4, int(n)))

@@ -242,6 +242,8 @@ int yar_session_set_option(yar_session *session, int option, int value) {
       for (auto &g : s.graphs) cudaGraphExecDestroy(g.exec);  // graphs captured the old value
       s.graphs.clear();
       s.inject_op = value;
+    } else if (option == YAR_OPT_PREFILL_ATTN_TC) {
+      s.prefill_attn_tc = value != 0;
     } else if (option == YAR_OPT_LAYER_DUMP) {
       YAR_CUDA(cudaSetDevice(s.m->device));
       YAR_CUDA(cudaStreamSynchronize(s.stream));

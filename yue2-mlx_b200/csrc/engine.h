@@ -1,5 +1,6 @@
 // engine.h — internal types of the YuE2 AR engine (host C++20 + CUDA sm_100a).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -178,6 +179,9 @@ bool gemm_tc_supported(const bf16 *A, int M, int K, const bf16 *W, int N, const 
 void launch_gemm_tc(const bf16 *A, int M, int K, const bf16 *W, int N, bf16 *C, int ldc, int epilogue, int *error,
                     float *ws, size_t ws_floats, cudaStream_t st, int split_n = 0);
 void configure_gemm_tc_kernels();
+// A 2-D TMA map of `rows` rows of 128 BF16 at `base` (256-byte pitch), {64, 64} boxes,
+// 128-byte swizzle; false when the driver's encoder is unavailable or refuses it.
+bool encode_rows128_map(CUtensorMap *map, const bf16 *base, uint64_t rows);
 void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
                              cudaStream_t st);
 void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
@@ -189,6 +193,7 @@ void fill_penalty_alpha(RequestState &r, double penalty, bool legacy);
 void configure_gemv_kernels();
 void configure_gemm_kernels();
 void configure_attn_kernels();
+void configure_attn_tc_kernels();
 void configure_gemv_tma_kernels();
 void configure_persistent_kernels();
 void configure_sampler_kernels();
@@ -254,6 +259,7 @@ struct Session {
   int *h_pinned = nullptr;  // pinned staging for small D2H reads
   // Persistent decode kernel: operation counters and the completed-step epoch.
   bool use_persistent = true;
+  bool prefill_attn_tc = true;  // head_dim 128 prefill attention on tcgen05 (else mma.sync)
   int persistent_ok[3] = {-1, -1, -1};  // per row count: unknown / no / yes
   int *d_ctr = nullptr;
   int *d_epoch = nullptr;

@@ -255,7 +255,8 @@ void launch_qkv_post_prefill(const Model &m, Session &s, int layer, int row, int
 }
 
 // Causal prefill attention over the row's cache positions [0, start + T) for head_dim 64
-// (head_dim 128 runs k_attn_prefill_mma below): grid (ceil(T/64), heads), 256 threads,
+// (head_dim 128 runs k_attn_prefill_tc in kernels_attn_tc.cu, or k_attn_prefill_mma below
+// with session option 7 off): grid (ceil(T/64), heads), 256 threads,
 // FP32 tiles of 64 queries x 64 keys in shared memory.
 // Thread t owns queries 4*(t/16) .. +3 and, for scores, keys 4*(t%16) .. +3; for the
 // output, dims (D/16)*(t%16) .. +D/16-1.
@@ -611,6 +612,10 @@ void configure_attn_kernels() {
                                 int(prefill_attn_smem(64))));
 }
 
+// kernels_attn_tc.cu: the tcgen05 kernel for head_dim 128; false when it does not apply.
+bool launch_attn_prefill_tc(const Model &m, Session &s, const AttnGeom &g, int layer, int row, int start, int T,
+                            cudaStream_t st);
+
 void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int start, int T,
                          cudaStream_t st) {
   PrefillAttnParams p;
@@ -624,6 +629,7 @@ void launch_attn_prefill(const Model &m, Session &s, int layer, int row, int sta
   p.out = s.pattn + m.tp.q_row0;
   p.out_stride = m.full.qdim();
   const int D = m.d.head_dim;
+  if (D == 128 && s.prefill_attn_tc && launch_attn_prefill_tc(m, s, p.g, layer, row, start, T, st)) return;
   dim3 grid((T + 63) / 64, m.d.heads);
   if (D == 128)
     k_attn_prefill_mma<<<grid, 128, kPfSmem, st>>>(p);

@@ -350,6 +350,18 @@ void encode_stage_map(CUtensorMap *map, const bf16 *W, int N, int K) {
   if (r != CUDA_SUCCESS) throw Error("RuntimeError", "cuTensorMapEncodeTiled failed for a stage map");
 }
 
+bool encode_rows128_map(CUtensorMap *map, const bf16 *base, uint64_t rows) {
+  const EncodeTiled fn = encode_fn();
+  if (!fn || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  const cuuint64_t dims[2] = {128, cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {256};
+  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<bf16 *>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 void configure_gemm_tc_kernels() {
   YAR_CUDA(cudaFuncSetAttribute(k_gemm_tc<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
   YAR_CUDA(cudaFuncSetAttribute(k_gemm_tc<kEpiResidual>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));

@@ -283,6 +283,7 @@ Model *load_model(const std::string &dir, int device, uint32_t flags, int tp_ran
     configure_gemv_kernels();
     configure_gemm_kernels();
     configure_attn_kernels();
+    configure_attn_tc_kernels();
     configure_gemv_tma_kernels();
     configure_persistent_kernels();
     configure_sampler_kernels();
