@@ -13,8 +13,8 @@
 //   * it issues S_j = Q K_j^T (M = 128 queries, N = 64 keys, K = 128 dims: 8 tcgen05.mma
 //     kind::f16, BF16 in, FP32 out) into one of two 64-column TMEM buffers, two tiles ahead
 //     of the softmax, and commits it;
-//   * thread t reads its 64 scores (tcgen05.ld), scales them into log2 units, masks them,
-//     and writes P = 2^(s - m) as BF16 high and low parts (P keeps ~16 significant bits)
+//   * thread t reads its 64 scores (tcgen05.ld), masks them (tiles on the diagonal only),
+//     scales them into log2 units, and writes P = 2^(s - m) as BF16 high and low parts (P keeps ~16 significant bits)
 //     into one of two pairs of swizzled 128 x 64 operand tiles. m is the row's running
 //     maximum, raised only when a tile's maximum exceeds it by more than 8 (so P <= 256);
 //     when it is raised the thread rescales its sum l and, once the previous P.V has
@@ -82,6 +82,12 @@ __device__ __forceinline__ uint64_t at_desc(const void *tile) {
 __device__ __forceinline__ uint64_t at_desc_mn(const void *tile) {
   return (uint64_t(at_smem(tile) >> 4) & 0x3FFFull) | (uint64_t(kAtKV >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
          (1ull << 46) | (2ull << 61);
+}
+// 2^x by the PTX approximate base-2 exponential (relative error below 2^-22; 2^-inf = 0).
+__device__ __forceinline__ float at_ex2(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 // Byte offset of 16-byte chunk c (elements 8c..8c+7) of row r in that layout.
 __device__ __forceinline__ int at_sw(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -311,12 +317,21 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       float s[kAtBK];
       at_ld64(lanes + uint32_t(j & 1) * kAtBK, s);
-      float mx = -INFINITY;
+      // The causal mask, on tiles reaching past the CTA's first query only (CTA-uniform).
+      if ((j + 1) * kAtBK - 1 > p.start + q0) {
 #pragma unroll
-      for (int k = 0; k < kAtBK; ++k) {
-        s[k] = j * kAtBK + k <= qpos ? s[k] * sl2 : -INFINITY;
-        mx = fmaxf(mx, s[k]);
+        for (int k = 0; k < kAtBK; ++k) s[k] = j * kAtBK + k <= qpos ? s[k] : -INFINITY;
       }
+      // Row maximum of the raw scores in eight independent chains; the scale is positive,
+      // so max(s) * sl2 is the maximum of the rounded scaled scores.
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+      for (int k = 8; k < kAtBK; ++k) mx8[k & 7] = fmaxf(mx8[k & 7], s[k]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                       sl2;
       const bool raise = mx > m + kAtRescale;  // false while both are -inf
       if (__any_sync(0xFFFFFFFFu, raise)) {
         const float mn = raise ? mx : m;
@@ -340,14 +355,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
           }
         }
       }
-      const float mm = m == -INFINITY ? 0.f : m;
-      float ps = 0.f;
+      // P = 2^(s * sl2 - m) (one rounding before the exponential), summed in eight chains.
+      const float nm = m == -INFINITY ? 0.f : -m;
+      float ps8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ps8[i] = 0.f;
 #pragma unroll
       for (int k = 0; k < kAtBK; ++k) {
-        s[k] = exp2f(s[k] - mm);  // masked: 2^-inf = 0
-        ps += s[k];
+        s[k] = at_ex2(fmaf(s[k], sl2, nm));  // masked: 2^-inf = 0
+        ps8[k & 7] += s[k];
       }
-      l += ps;
+      l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       // P buffer j & 1 was last read by P.V_{j-2}.
       if (j >= 2) {
         ok = at_wait(&o_done[j & 1], unsigned((j - 2) >> 1) & 1u);
