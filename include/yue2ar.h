@@ -202,7 +202,10 @@ int yar_generate_requests(yar_session *session, int n_requests, int slots, const
                           char *timing_json, size_t timing_cap);
 
 /* Row-level API (ARModel::hidden/project + KVCache, ar.cpp:246-323), used by batched
- * serving and by parity tests. A row owns a page table and a position. */
+ * serving and by parity tests. A row owns a page table and a position. yar_row_prefill and
+ * yar_rows_step are the library's prefill and decode-step entries; a sampled step is
+ * yar_generate (the whole loop on the device) or, token at a time, yar_rows_step followed
+ * by yar_sample_host (or yar_sample_device_noalloc on device-resident logits). */
 int yar_row_reset(yar_session *session, int row, int capacity);
 /* Prefill `n` ids into `row` at its current position (chunks of `chunk` tokens, 1024 if
  * 0; native/src/sampling.cpp:152-183) and project the last hidden state onto `phase`. */
